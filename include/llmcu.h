@@ -1,0 +1,243 @@
+/*
+ * llmcu.h -- C ABI of the B200-native Qwen3 LoRA training step (libllmcu.so).
+ *
+ * The reference (visheshnarayan/llm.cu) has no library API: its trainer calls
+ * C++-linkage functions whose signatures are re-declared by hand in each file
+ * (src/train.cu:27-39, include/lora.h:66-90) and exits on any CUDA error
+ * (include/utils.h:10-27).  This header is the drop-in boundary that replaces
+ * that call surface.  Each entry point names the reference function(s) it
+ * stands in for.
+ *
+ * Conventions
+ *   - Plain C: pointers, sizes, PODs.  No torch or C++ types.
+ *   - Every call returns an llmcu_status and never calls exit(); the text of
+ *     the last failure on a context is llmcu_last_error(ctx).
+ *   - The library owns all device memory.  llmcu_ctx_create() allocates one
+ *     arena sized for (max_batch, max_seq); no call made during a training
+ *     step allocates device memory.
+ *   - One context per device per host thread.  Work runs on context-owned
+ *     streams (one compute stream, one communication stream).
+ *   - "host" pointers are ordinary CPU memory (pinned or not); "device"
+ *     pointers are CUDA device addresses on the context's device.
+ *   - Token ids are int32 [batch, seq] row-major; targets are the inputs
+ *     shifted by one (src/train.cu:253-258).
+ */
+#ifndef LLMCU_H
+#define LLMCU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LLMCU_ABI_VERSION 1
+
+typedef enum {
+    LLMCU_OK = 0,
+    LLMCU_ERR_INVALID_ARG = 1,   /* bad size, id, pointer or state           */
+    LLMCU_ERR_CUDA = 2,          /* a CUDA runtime call failed               */
+    LLMCU_ERR_OOM = 3,           /* device arena could not be allocated      */
+    LLMCU_ERR_IO = 4,            /* file missing, short read or short write  */
+    LLMCU_ERR_NCCL = 5,          /* a NCCL call failed or a peer aborted     */
+    LLMCU_ERR_TIMEOUT = 6,       /* a host-side deadline expired             */
+    LLMCU_ERR_DEVICE_CHECK = 7,  /* a kernel's own check failed (bounded wait
+                                    expired, id out of range); the context
+                                    stays usable                             */
+    LLMCU_ERR_UNSUPPORTED = 8    /* shape/config this build does not handle */
+} llmcu_status;
+
+/* Model dimensions: the runtime form of the reference's compile-time macros
+ * (include/config.h:5-21, include/lora.h:6-8). */
+typedef struct {
+    int32_t hidden;        /* HIDDEN_SIZE            2048  */
+    int32_t n_layers;      /* NUM_LAYERS             28    */
+    int32_t n_heads;       /* NUM_HEADS              16    */
+    int32_t n_kv_heads;    /* NUM_KV_HEADS           8     */
+    int32_t head_dim;      /* HEAD_DIM               128 (64 and 128 supported) */
+    int32_t ffn;           /* INTERMEDIATE_SIZE      6144  */
+    int32_t vocab;         /* VOCAB_SIZE             151936 */
+    float   rope_theta;    /* ROPE_THETA             1e6   */
+    float   rms_eps;       /* RMS_NORM_EPS           1e-6  */
+} llmcu_model_cfg;
+
+typedef struct {
+    int32_t rank;          /* LORA_RANK   16 (1..16 supported) */
+    float   alpha;         /* LORA_ALPHA  32 -> scale alpha/rank */
+} llmcu_lora_cfg;
+
+typedef enum { LLMCU_BASE_FP16 = 0, LLMCU_BASE_INT8 = 1 } llmcu_base_dtype;
+
+typedef struct {
+    int32_t max_batch;          /* sequences per step on this device            */
+    int32_t max_seq;            /* tokens per sequence                          */
+    int32_t base_dtype;         /* llmcu_base_dtype                             */
+    int32_t loss_all_positions; /* 0 = reference convention: positions 0..S-2
+                                   of each sequence (src/kernels/loss.cu:18-21);
+                                   1 = every position                           */
+} llmcu_run_cfg;
+
+typedef struct {
+    float lr, beta1, beta2, eps, weight_decay;   /* src/train.cu:174-183 */
+} llmcu_adamw_cfg;
+
+/* Base tensor ids for llmcu_set_base_tensor (file names of
+ * src/train.cu:56-89 / python/export_weights.py:19-25). */
+typedef enum {
+    LLMCU_T_EMBED = 0,       /* model.embed_tokens.weight   [V, H] (lm_head tied) */
+    LLMCU_T_FINAL_NORM = 1,  /* model.norm.weight           [H]                   */
+    LLMCU_T_ATTN_NORM = 2,   /* layers.l.input_layernorm    [H]                   */
+    LLMCU_T_FFN_NORM = 3,    /* layers.l.post_attention_layernorm [H]             */
+    LLMCU_T_WQ = 4,          /* self_attn.q_proj   [nh*hd, H]  */
+    LLMCU_T_WK = 5,          /* self_attn.k_proj   [nkv*hd, H] */
+    LLMCU_T_WV = 6,          /* self_attn.v_proj   [nkv*hd, H] */
+    LLMCU_T_WO = 7,          /* self_attn.o_proj   [H, nh*hd]  */
+    LLMCU_T_Q_NORM = 8,      /* self_attn.q_norm   [hd]        */
+    LLMCU_T_K_NORM = 9,      /* self_attn.k_norm   [hd]        */
+    LLMCU_T_W_GATE = 10,     /* mlp.gate_proj      [I, H]      */
+    LLMCU_T_W_UP = 11,       /* mlp.up_proj        [I, H]      */
+    LLMCU_T_W_DOWN = 12,     /* mlp.down_proj      [H, I]      */
+    LLMCU_T_COUNT = 13
+} llmcu_tensor_id;
+
+/* LoRA projection ids, in the order of include/lora.h:22-27. */
+typedef enum { LLMCU_P_Q = 0, LLMCU_P_K = 1, LLMCU_P_V = 2, LLMCU_P_O = 3 } llmcu_proj;
+
+typedef struct llmcu_ctx llmcu_ctx;
+
+/* ---------------------------------------------------------------- context */
+
+/* Replaces load-time setup of src/train.cu:217-242 (lora_weights_init,
+ * lora_grads_alloc, lora_acts_alloc, alloc_train_ws): validates the config and
+ * allocates the whole arena on `device`.  LoRA adapters start as A = 0, B = 0. */
+llmcu_status llmcu_ctx_create(const llmcu_model_cfg* model, const llmcu_lora_cfg* lora,
+                              const llmcu_run_cfg* run, int device, llmcu_ctx** out);
+/* Replaces lora_weights_free / lora_grads_free / lora_acts_free. */
+void llmcu_ctx_destroy(llmcu_ctx* ctx);
+/* Text of the last failure on ctx (never NULL; "" if none). */
+const char* llmcu_last_error(const llmcu_ctx* ctx);
+/* Library version string, e.g. "llmcu 1 sm_100a". */
+const char* llmcu_version(void);
+/* Bytes of device memory the context holds. */
+size_t llmcu_device_bytes(const llmcu_ctx* ctx);
+/* The compute stream (a cudaStream_t) -- for callers that order their own
+ * device work after a step. */
+void* llmcu_stream(const llmcu_ctx* ctx);
+llmcu_status llmcu_synchronize(llmcu_ctx* ctx);
+
+/* ------------------------------------------------------------ base weights */
+
+/* Replaces load_weight() for one tensor (src/train.cu:42-54): `host` holds
+ * fp32 data with the tensor's reference shape; it is converted to the base
+ * dtype (fp16, or INT8 + per-row fp32 scales) on the device.  `layer` is
+ * ignored for EMBED / FINAL_NORM. */
+llmcu_status llmcu_set_base_tensor(llmcu_ctx* ctx, int tensor_id, int layer, const float* host);
+/* Replaces load_model() (src/train.cu:56-89): reads the reference's fp32
+ * weight files from `dir` (model.embed_tokens.weight.bin, ...); the separate
+ * lm_head.weight.bin is not read because the head is tied to the embedding. */
+llmcu_status llmcu_load_base_fp32_files(llmcu_ctx* ctx, const char* dir);
+/* Synthetic base for benchmarks: every linear ~ N(0, std) drawn on the device
+ * from a counter-based generator keyed by `seed`, norm gains 1. */
+llmcu_status llmcu_init_base_synthetic(llmcu_ctx* ctx, uint64_t seed, float std);
+
+/* ------------------------------------------------------------------ LoRA */
+
+/* A is [rank, d_in] and B is [d_out, rank], fp32 row-major, host memory --
+ * the layout of include/lora.h:13-20 and of the lora_step files. */
+llmcu_status llmcu_set_lora(llmcu_ctx* ctx, int layer, int proj, const float* A, const float* B);
+llmcu_status llmcu_get_lora(llmcu_ctx* ctx, int layer, int proj, float* A, float* B);
+/* Gradients of the last llmcu_forward_backward / llmcu_train_step. */
+llmcu_status llmcu_get_lora_grads(llmcu_ctx* ctx, int layer, int proj, float* dA, float* dB);
+/* Synthetic adapters on the device: A ~ U(+-1/sqrt(d_in)), B ~ N(0, b_std). */
+llmcu_status llmcu_init_lora_synthetic(llmcu_ctx* ctx, uint64_t seed, float b_std);
+/* Zero the AdamW moments (m, v). */
+llmcu_status llmcu_reset_optimizer(llmcu_ctx* ctx);
+/* Total LoRA parameter count (A and B of every adapter). */
+int64_t llmcu_lora_param_count(const llmcu_ctx* ctx);
+
+/* ------------------------------------------------------------------ steps */
+
+/* One full step: lora_grads_zero + transformer_forward_lora +
+ * cross_entropy_forward + transformer_backward_lora + adamw_step_lora
+ * (src/train.cu:251-291).  tokens/targets are HOST int32 [batch, seq];
+ * *loss_out receives the mean NLL (over all ranks when data parallel). */
+llmcu_status llmcu_train_step(llmcu_ctx* ctx, const int32_t* tokens, const int32_t* targets,
+                              int batch, int seq, const llmcu_adamw_cfg* opt, int step,
+                              float* loss_out);
+/* The same step with DEVICE token buffers; the loss stays on the device
+ * (read it with llmcu_read_loss).  Nothing is copied to or from the host. */
+llmcu_status llmcu_train_step_device(llmcu_ctx* ctx, const int32_t* d_tokens,
+                                     const int32_t* d_targets, int batch, int seq,
+                                     const llmcu_adamw_cfg* opt, int step);
+/* Mean loss of the last step (synchronises the compute stream). */
+llmcu_status llmcu_read_loss(llmcu_ctx* ctx, float* loss_out);
+/* Forward + loss + backward only (gradients left in place, no optimizer);
+ * the split form of the step used by the parity tests. */
+llmcu_status llmcu_forward_backward(llmcu_ctx* ctx, const int32_t* tokens, const int32_t* targets,
+                                    int batch, int seq, float* loss_out);
+/* AdamW over all adapters with the gradients in place (adamw_step_lora,
+ * src/kernels/lora.cu:235-246); bias corrections use `step` (1-based). */
+llmcu_status llmcu_adamw(llmcu_ctx* ctx, const llmcu_adamw_cfg* opt, int step);
+
+/* --------------------------------------------------------- checkpointing */
+
+/* Replaces save_lora (src/train.cu:146-170): writes
+ * dir/lora_step{step}_layer{l}_{wq,wk,wv,wo}_{A,B}.bin, raw fp32, A [r, d_in],
+ * B [d_out, r], no header -- the files python/save_lora.py reads. */
+llmcu_status llmcu_save_lora(llmcu_ctx* ctx, const char* dir, int step);
+/* Reads the same files back (e.g. those written by save_lora.py --from-hf). */
+llmcu_status llmcu_load_lora(llmcu_ctx* ctx, const char* dir, int step);
+
+/* --------------------------------------------------------------- INT8 */
+
+/* Per-row symmetric quantiser, bit-exact with quantize_kernel
+ * (src/kernels/quantize.cu:8-50): scale = absmax/127, q = rint(clamp(w/scale)).
+ * DEVICE pointers: w fp32 [rows, cols], q int8 [rows, cols], scale fp32 [rows];
+ * `stream` is a cudaStream_t (NULL = legacy default stream). */
+llmcu_status llmcu_quantize_int8_rows(const float* w, int rows, int cols, int8_t* q,
+                                      float* scale, void* stream);
+
+/* -------------------------------------------------------- data parallel */
+
+/* NCCL unique id of 128 bytes for rank 0 to broadcast out of band. */
+llmcu_status llmcu_dp_get_unique_id(void* id128);
+/* Joins a data-parallel group of `world` ranks (one per GPU).  After this
+ * call every step allreduces the LoRA gradients (sum, fp32) per layer on the
+ * communication stream, overlapped with the rest of the backward pass, and
+ * the loss is averaged over ranks.  The reference is single-GPU only. */
+llmcu_status llmcu_dp_init(llmcu_ctx* ctx, const void* id128, int rank, int world);
+/* Host deadline for each NCCL wait; on expiry the communicator is aborted and
+ * LLMCU_ERR_TIMEOUT is returned (default 60000 ms). */
+llmcu_status llmcu_dp_set_timeout_ms(llmcu_ctx* ctx, int ms);
+
+/* ------------------------------------------------------------ kernel test
+ * Single-kernel entry points on DEVICE pointers, used by the kernel-level
+ * parity tests.  `stream` is a cudaStream_t; results are asynchronous. */
+
+/* C[M,N] (fp32) = A[M,K] . B[N,K]^T, fp16 inputs, K-major rows with leading
+ * dims lda/ldb/ldc in elements -- the NT product of matmul_kernel
+ * (src/kernels/matmul.cu:8-51) on the tcgen05 path. */
+llmcu_status llmcu_gemm_nt_f16(const void* A, const void* B, float* C, int M, int N, int K,
+                               int lda, int ldb, int ldc, void* stream);
+/* Causal GQA attention forward: q [B*S, nh*hd], k/v [B*S, nkv*hd] fp16 with
+ * row strides ldq/ldk/ldv; o [B*S, nh*hd] fp16, lse [B, nh, S] fp32
+ * (replaces naive_attn_kernel, src/kernels/lora_forward.cu:48-135). */
+llmcu_status llmcu_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                                 int batch, int seq, int n_heads, int n_kv_heads, int head_dim,
+                                 int ldq, int ldk, int ldv, void* stream);
+/* Its backward (replaces attn_backward_kernel + expand/contract,
+ * src/kernels/lora_backward.cu:104-208): dq [B*S, nh*hd] fp32, dk [B*S,
+ * nkv*hd] fp32, dv written fp16 with row stride lddv.  `scratch_delta` is
+ * fp32 [B, nh, S]. */
+llmcu_status llmcu_attention_bwd(const void* q, const void* k, const void* v, const void* o,
+                                 const void* dout, const float* lse, float* scratch_delta,
+                                 float* dq, float* dk, void* dv, int batch, int seq,
+                                 int n_heads, int n_kv_heads, int head_dim, int ldq, int ldk,
+                                 int ldv, int lddv, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLMCU_H */

@@ -1,0 +1,103 @@
+// common.cuh -- declarations shared by the kernel translation units.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "sm100.cuh"
+
+namespace llmcu {
+
+// ---- attention.cu
+cudaError_t attention_forward(const __half* q, const __half* k, const __half* v, __half* o, float* lse, int B, int S,
+                              int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, cudaStream_t st);
+cudaError_t attention_backward(const __half* q, const __half* k, const __half* v, const __half* o,
+                               const __half* dout, const float* lse, float* delta, float* dq, float* dk, __half* dv,
+                               int B, int S, int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int lddq,
+                               int lddk, int lddv, cudaStream_t st);
+
+// ---- gemm.cu
+// Tensor operand for the GEMM: fp16, K-major rows (K contiguous), `ld`
+// elements between rows; `rows` x `k` valid extent.
+struct Operand {
+  const __half* ptr;
+  int rows;
+  int k;
+  int ld;
+};
+
+enum class Epi : int {
+  kStoreF16 = 0,
+  kStoreF32 = 1,
+  kResidF32 = 2,
+  kSwiGLU = 3,
+  kSwiGLUBwd = 4,
+  kCEStats = 5,
+  kCEGrad = 6,
+};
+
+struct EpiArgs {
+  // generic outputs
+  void* out = nullptr;
+  int ld_out = 0;
+  int accumulate = 0;
+  const float* resid = nullptr;
+  // SwiGLU
+  __half* gu = nullptr;       // interleaved [M, 2I]
+  const __half* gu_in = nullptr;
+  int ld_gu = 0;
+  __half* act = nullptr;      // [M, I]
+  int ld_act = 0;
+  // cross-entropy
+  const int* targets = nullptr;
+  float* part_max = nullptr;
+  float* part_sum = nullptr;
+  float* tgt_logit = nullptr;
+  const float* lse = nullptr;
+  const uint8_t* valid = nullptr;
+  int col_base = 0;
+  float gscale = 1.f;
+};
+
+// C[M,N] = A0 . B0^T (+ A1 . B1^T) with the given epilogue.  A*.rows = M,
+// B*.rows = N; A0.k == B0.k == K0; A1/B1 may have k == 0 (absent).
+cudaError_t gemm(const Operand& A0, const Operand& B0, const Operand& A1, const Operand& B1, int M, int N, Epi epi,
+                 const EpiArgs& ea, int* err, cudaStream_t st, int bn_hint = 0);
+int gemm_num_sms();
+
+// ---- kernels.cu
+cudaError_t embed_forward(const int* tokens, const __half* E, float* out, int M, int H, int V, int* err,
+                          cudaStream_t st);
+cudaError_t rmsnorm_forward(const float* x, const float* w, __half* out, int M, int H, float eps, cudaStream_t st);
+// dres (+)= rmsnorm_bwd(dy, x, w); dres16 = fp16(dres)
+cudaError_t rmsnorm_backward(const float* dy, const float* x, const float* w, float* dres, __half* dres16, int M,
+                             int H, float eps, int accumulate, cudaStream_t st);
+cudaError_t qknorm_rope_forward(const __half* qkv, int ld_qkv, const float* qn_w, const float* kn_w,
+                                const float* cos_t, const float* sin_t, __half* q_out, __half* k_out, int B, int S,
+                                int nh, int nkv, int hd, float eps, cudaStream_t st);
+cudaError_t qknorm_rope_backward(const float* dq, const float* dk, const __half* qkv, int ld_qkv, const float* qn_w,
+                                 const float* kn_w, const float* cos_t, const float* sin_t, __half* dqkv, int B,
+                                 int S, int nh, int nkv, int hd, float eps, cudaStream_t st);
+cudaError_t rope_tables(float* cos_t, float* sin_t, int S, int hd, float theta, cudaStream_t st);
+// row_loss_and_sum: [M] per-row losses followed by their sum at [M]
+cudaError_t ce_reduce(const float* part_max, const float* part_sum, const float* tgt_logit, const uint8_t* valid,
+                      float* lse, float* row_loss_and_sum, int M, int tiles_n, cudaStream_t st);
+cudaError_t ce_valid_rows(uint8_t* valid, const int* targets, int B, int S, int all_positions, int V, int* err,
+                          cudaStream_t st);
+cudaError_t adamw_flat(float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1, float b2,
+                       float eps, float wd, float bc1, float bc2, float gscale, cudaStream_t st);
+cudaError_t fill_f32(float* p, int64_t n, float v, cudaStream_t st);
+cudaError_t fill_normal_f16(__half* p, int64_t n, uint64_t seed, float stddev, cudaStream_t st);
+cudaError_t fill_normal_f32(float* p, int64_t n, uint64_t seed, float stddev, cudaStream_t st);
+cudaError_t fill_uniform_f32(float* p, int64_t n, uint64_t seed, float lo, float hi, cudaStream_t st);
+// dst[r, c] (fp16) = src[r, c] with dst row = row_map(r), optionally transposed
+cudaError_t convert_weight(const float* src, int rows, int cols, __half* dst, int ld_dst, int row_off,
+                           int interleave, __half* dst_t, int ld_t, int col_off_t, cudaStream_t st);
+cudaError_t transpose_f16(const __half* src, int rows, int cols, int ld_src, __half* dst, int ld_dst,
+                          cudaStream_t st);
+cudaError_t quantize_rows_int8(const float* w, int rows, int cols, int8_t* q, float* scale, cudaStream_t st);
+cudaError_t dequant_rows_f16(const int8_t* q, const float* scale, int rows, int cols, __half* out, cudaStream_t st);
+
+}  // namespace llmcu

@@ -1,0 +1,554 @@
+// kernels.cu -- bandwidth-bound kernels of the step: embedding gather,
+// RMSNorm fwd/bwd, QK-norm + RoPE fwd/bwd, cross-entropy reduction, AdamW,
+// weight conversion / synthetic init and the per-row INT8 quantiser.
+//
+// All row kernels put one warp on one row and move 16 bytes per lane per
+// access; reductions are warp shuffles (no shared-memory trees).
+#include <cmath>
+
+#include "common.cuh"
+
+namespace llmcu {
+
+namespace {
+
+constexpr int kRowWarps = 8;  // warps per CTA for row kernels
+
+__device__ __forceinline__ void load8h(const __half* p, float (&f)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+// ------------------------------------------------------------ embedding
+// out[m, :] = E[tok[m], :]   (src/kernels/embed.cu:6-14), fp16 table -> fp32
+__global__ void embed_kernel(const int* __restrict__ tok, const __half* __restrict__ E, float* __restrict__ out,
+                             int M, int H, int V, int* err) {
+  const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (m >= M) return;
+  int t = tok[m];
+  if (t < 0 || t >= V) {
+    if (lane == 0) atomicOr(err, kErrTokenRange);
+    t = 0;
+  }
+  const __half* src = E + static_cast<size_t>(t) * H;
+  float* dst = out + static_cast<size_t>(m) * H;
+  for (int c = lane * 8; c < H; c += 256) {
+    float f[8];
+    load8h(src + c, f);
+    *reinterpret_cast<float4*>(dst + c) = make_float4(f[0], f[1], f[2], f[3]);
+    *reinterpret_cast<float4*>(dst + c + 4) = make_float4(f[4], f[5], f[6], f[7]);
+  }
+}
+
+// ------------------------------------------------------------ RMSNorm
+// y = x * rsqrt(mean(x^2) + eps) * w   (src/kernels/rmsnorm.cu:6-34)
+__global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                   __half* __restrict__ out, int M, int H, float eps) {
+  const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (m >= M) return;
+  const float* xr = x + static_cast<size_t>(m) * H;
+  float ss = 0.f;
+  for (int c = lane * 4; c < H; c += 128) {
+    float4 v = *reinterpret_cast<const float4*>(xr + c);
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / static_cast<float>(H) + eps);
+  __half* orow = out + static_cast<size_t>(m) * H;
+  for (int c = lane * 4; c < H; c += 128) {
+    float4 v = *reinterpret_cast<const float4*>(xr + c);
+    float4 g = *reinterpret_cast<const float4*>(w + c);
+    uint2 u;
+    u.x = pack_half2(v.x * r * g.x, v.y * r * g.y);
+    u.y = pack_half2(v.z * r * g.z, v.w * r * g.w);
+    *reinterpret_cast<uint2*>(orow + c) = u;
+  }
+}
+
+// dx = r * (dy*w - c*x), c = r^2/H * sum(dy*w*x)   (src/kernels/rmsnorm.cu:53-90)
+// dres = (accumulate ? dres : 0) + dx ; dres16 = fp16(dres)
+__global__ void rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                   const float* __restrict__ w, float* __restrict__ dres,
+                                   __half* __restrict__ dres16, int M, int H, float eps, int accumulate) {
+  const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (m >= M) return;
+  const size_t base = static_cast<size_t>(m) * H;
+  float ss = 0.f, dot = 0.f;
+  for (int c = lane * 4; c < H; c += 128) {
+    float4 xv = *reinterpret_cast<const float4*>(x + base + c);
+    float4 dv = *reinterpret_cast<const float4*>(dy + base + c);
+    float4 g = *reinterpret_cast<const float4*>(w + c);
+    ss += xv.x * xv.x + xv.y * xv.y + xv.z * xv.z + xv.w * xv.w;
+    dot += dv.x * g.x * xv.x + dv.y * g.y * xv.y + dv.z * g.z * xv.z + dv.w * g.w * xv.w;
+  }
+  ss = warp_sum(ss);
+  dot = warp_sum(dot);
+  const float r = rsqrtf(ss / static_cast<float>(H) + eps);
+  const float cc = r * r / static_cast<float>(H) * dot;
+  for (int c = lane * 4; c < H; c += 128) {
+    float4 xv = *reinterpret_cast<const float4*>(x + base + c);
+    float4 dv = *reinterpret_cast<const float4*>(dy + base + c);
+    float4 g = *reinterpret_cast<const float4*>(w + c);
+    float4 o = make_float4(r * (dv.x * g.x - cc * xv.x), r * (dv.y * g.y - cc * xv.y), r * (dv.z * g.z - cc * xv.z),
+                           r * (dv.w * g.w - cc * xv.w));
+    if (accumulate) {
+      float4 p = *reinterpret_cast<const float4*>(dres + base + c);
+      o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+    }
+    *reinterpret_cast<float4*>(dres + base + c) = o;
+    uint2 u;
+    u.x = pack_half2(o.x, o.y);
+    u.y = pack_half2(o.z, o.w);
+    *reinterpret_cast<uint2*>(dres16 + base + c) = u;
+  }
+}
+
+// ------------------------------------------------------- QK-norm + RoPE
+// cos/sin tables with the reference's fp32 arithmetic (src/kernels/rope.cu:15-20):
+// freq = 1 / powf(theta, 2d/hd), angle = pos * freq.
+__global__ void rope_table_kernel(float* cos_t, float* sin_t, int S, int hd, float theta) {
+  const int half = hd / 2;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= S * half) return;
+  const int pos = i / half, d = i % half;
+  const float freq = 1.0f / powf(theta, (2.0f * d) / static_cast<float>(hd));
+  const float ang = static_cast<float>(pos) * freq;
+  cos_t[i] = cosf(ang);
+  sin_t[i] = sinf(ang);
+}
+
+// One warp per (token, head).  q heads then k heads.  Per-head RMSNorm with
+// the q_norm / k_norm gain, then the half-split rotation of pairs (d, d+hd/2)
+// (src/kernels/lora_forward.cu:233-237, src/kernels/rope.cu:26-35).
+template <int HD>
+__global__ void qknorm_rope_fwd_kernel(const __half* __restrict__ qkv, int ld, const float* __restrict__ qn_w,
+                                       const float* __restrict__ kn_w, const float* __restrict__ cos_t,
+                                       const float* __restrict__ sin_t, __half* __restrict__ q_out,
+                                       __half* __restrict__ k_out, int M, int S, int nh, int nkv, float eps) {
+  constexpr int kHalf = HD / 2;
+  constexpr int kPer = kHalf / 32;  // pairs per lane
+  const int w = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int nhead = nh + nkv;
+  if (w >= M * nhead) return;
+  const int m = w / nhead, hh = w % nhead;
+  const bool isq = hh < nh;
+  const __half* src = qkv + static_cast<size_t>(m) * ld + (isq ? hh * HD : nh * HD + (hh - nh) * HD);
+  const float* gw = isq ? qn_w : kn_w;
+  float x0[kPer], x1[kPer];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int d = lane + 32 * i;
+    x0[i] = __half2float(src[d]);
+    x1[i] = __half2float(src[d + kHalf]);
+    ss += x0[i] * x0[i] + x1[i] * x1[i];
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / static_cast<float>(HD) + eps);
+  const int pos = m % S;
+  __half* dst = isq ? q_out + static_cast<size_t>(m) * nh * HD + hh * HD
+                    : k_out + static_cast<size_t>(m) * nkv * HD + (hh - nh) * HD;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int d = lane + 32 * i;
+    const float a = x0[i] * r * gw[d];
+    const float b = x1[i] * r * gw[d + kHalf];
+    const float c = cos_t[pos * kHalf + d], s = sin_t[pos * kHalf + d];
+    dst[d] = __float2half_rn(a * c - b * s);
+    dst[d + kHalf] = __float2half_rn(b * c + a * s);
+  }
+}
+
+// Inverse rotation (src/kernels/rope.cu:57-83) then the per-head RMSNorm
+// backward at the raw q / k (src/kernels/rmsnorm.cu:53-90); writes fp16 into
+// the q / k columns of dqkv.
+template <int HD>
+__global__ void qknorm_rope_bwd_kernel(const float* __restrict__ dq, const float* __restrict__ dk,
+                                       const __half* __restrict__ qkv, int ld, const float* __restrict__ qn_w,
+                                       const float* __restrict__ kn_w, const float* __restrict__ cos_t,
+                                       const float* __restrict__ sin_t, __half* __restrict__ dqkv, int M, int S,
+                                       int nh, int nkv, float eps) {
+  constexpr int kHalf = HD / 2;
+  constexpr int kPer = kHalf / 32;
+  const int w = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int nhead = nh + nkv;
+  if (w >= M * nhead) return;
+  const int m = w / nhead, hh = w % nhead;
+  const bool isq = hh < nh;
+  const int col = isq ? hh * HD : nh * HD + (hh - nh) * HD;
+  const __half* xs = qkv + static_cast<size_t>(m) * ld + col;
+  const float* g = isq ? dq + static_cast<size_t>(m) * nh * HD + hh * HD
+                       : dk + static_cast<size_t>(m) * nkv * HD + (hh - nh) * HD;
+  const float* gw = isq ? qn_w : kn_w;
+  const int pos = m % S;
+  float x0[kPer], x1[kPer], d0[kPer], d1[kPer];
+  float ss = 0.f, dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int d = lane + 32 * i;
+    x0[i] = __half2float(xs[d]);
+    x1[i] = __half2float(xs[d + kHalf]);
+    const float g0 = g[d], g1 = g[d + kHalf];
+    const float c = cos_t[pos * kHalf + d], s = sin_t[pos * kHalf + d];
+    d0[i] = (g0 * c + g1 * s) * gw[d];          // d(normed) * w
+    d1[i] = (g1 * c - g0 * s) * gw[d + kHalf];
+    ss += x0[i] * x0[i] + x1[i] * x1[i];
+    dot += d0[i] * x0[i] + d1[i] * x1[i];
+  }
+  ss = warp_sum(ss);
+  dot = warp_sum(dot);
+  const float r = rsqrtf(ss / static_cast<float>(HD) + eps);
+  const float cc = r * r / static_cast<float>(HD) * dot;
+  __half* dst = dqkv + static_cast<size_t>(m) * ld + col;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int d = lane + 32 * i;
+    dst[d] = __float2half_rn(r * (d0[i] - cc * x0[i]));
+    dst[d + kHalf] = __float2half_rn(r * (d1[i] - cc * x1[i]));
+  }
+}
+
+// ------------------------------------------------------- cross-entropy
+// valid[m] = 1 if row m contributes to the loss; checks target ids.
+__global__ void ce_valid_kernel(uint8_t* valid, const int* targets, int B, int S, int all_positions, int V,
+                                int* err) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= B * S) return;
+  const int s = m % S;
+  const int t = targets[m];
+  const bool in_range = t >= 0 && t < V;
+  if (!in_range) atomicOr(err, kErrTokenRange);
+  valid[m] = (in_range && (all_positions || s < S - 1)) ? 1 : 0;
+}
+
+// lse[m] = log(sum_j exp(logit)) from per-tile (max, sumexp); row loss =
+// lse - logit[target] (src/kernels/loss.cu:66-67).  One warp per row.
+__global__ void ce_lse_kernel(const float* __restrict__ pmax, const float* __restrict__ psum,
+                              const float* __restrict__ tgt, const uint8_t* __restrict__ valid,
+                              float* __restrict__ lse, float* __restrict__ row_loss, int M, int T) {
+  const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (m >= M) return;
+  const float* pm = pmax + static_cast<size_t>(m) * T;
+  const float* ps = psum + static_cast<size_t>(m) * T;
+  float mx = -INFINITY;
+  for (int i = lane; i < T; i += 32) mx = fmaxf(mx, pm[i]);
+  mx = warp_max(mx);
+  float s = 0.f;
+  for (int i = lane; i < T; i += 32) s += ps[i] * exp2f((pm[i] - mx) * kLog2e);
+  s = warp_sum(s);
+  const float l = mx + logf(s);
+  if (lane == 0) {
+    lse[m] = l;
+    row_loss[m] = valid[m] ? (l - tgt[m]) : 0.f;
+  }
+}
+
+// Deterministic single-CTA sum of the row losses.
+__global__ void sum_kernel(const float* __restrict__ x, int n, float* __restrict__ out) {
+  __shared__ float red[32];
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) *out = t;
+  }
+}
+
+// ---------------------------------------------------------------- AdamW
+// One launch over the flat adapter buffer (src/kernels/lora.cu:206-220, same
+// operations in the same order).  g is scaled by gscale first (the gradient
+// unscale / data-parallel mean).
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, int64_t n, float lr, float b1, float b2, float eps, float wd,
+                             float bc1, float bc2, float gscale) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float gi = g[i] * gscale;
+    const float mi = b1 * m[i] + (1.0f - b1) * gi;
+    const float vi = b2 * v[i] + (1.0f - b2) * gi * gi;
+    m[i] = mi;
+    v[i] = vi;
+    const float mh = mi / bc1;
+    const float vh = vi / bc2;
+    p[i] = p[i] * (1.0f - lr * wd) - lr * mh / (sqrtf(vh) + eps);
+  }
+}
+
+// ------------------------------------------------------------ init / fill
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ float u01(uint64_t h) {  // (0, 1]
+  return (static_cast<float>(h >> 40) + 1.0f) * (1.0f / 16777216.0f);
+}
+__device__ __forceinline__ float normal_at(uint64_t seed, int64_t i) {
+  const uint64_t h1 = mix64(seed ^ mix64(static_cast<uint64_t>(i) * 2 + 1));
+  const uint64_t h2 = mix64(h1 ^ 0x5851F42D4C957F2Dull);
+  const float r = sqrtf(-2.0f * logf(u01(h1)));
+  return r * cospif(2.0f * u01(h2));
+}
+
+__global__ void fill_f32_kernel(float* p, int64_t n, float v) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p[i] = v;
+}
+__global__ void fill_normal_f16_kernel(__half* p, int64_t n, uint64_t seed, float sd) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p[i] = __float2half_rn(normal_at(seed, i) * sd);
+}
+__global__ void fill_normal_f32_kernel(float* p, int64_t n, uint64_t seed, float sd) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p[i] = normal_at(seed, i) * sd;
+}
+__global__ void fill_uniform_f32_kernel(float* p, int64_t n, uint64_t seed, float lo, float hi) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p[i] = lo + (hi - lo) * (u01(mix64(seed ^ mix64(static_cast<uint64_t>(i)))) - 0.5f / 16777216.0f);
+}
+
+// fp32 [rows, cols] -> fp16 rows of dst (row r goes to row_map(r)) and, if
+// dst_t != null, the transposed copy dst_t[c, col_off_t + row_map(r)].
+// interleave != 0 maps row r to (r/128)*256 + r%128 + (interleave==2 ? 128 : 0)
+// (the gate/up block interleave of the fused W_gu).
+__device__ __forceinline__ int map_row(int r, int row_off, int interleave) {
+  if (!interleave) return row_off + r;
+  return (r >> 7) * 256 + (r & 127) + (interleave == 2 ? 128 : 0);
+}
+__global__ void convert_weight_kernel(const float* __restrict__ src, int rows, int cols, __half* __restrict__ dst,
+                                      int ld_dst, int row_off, int interleave, __half* __restrict__ dst_t, int ld_t,
+                                      int col_off_t) {
+  __shared__ float tile[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  for (int i = ty; i < 32; i += 8) {
+    const int r = r0 + i, c = c0 + tx;
+    float v = 0.f;
+    if (r < rows && c < cols) {
+      v = src[static_cast<size_t>(r) * cols + c];
+      dst[static_cast<size_t>(map_row(r, row_off, interleave)) * ld_dst + c] = __float2half_rn(v);
+    }
+    tile[i][tx] = v;
+  }
+  if (!dst_t) return;
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int c = c0 + i, r = r0 + tx;
+    if (r < rows && c < cols)
+      dst_t[static_cast<size_t>(c) * ld_t + col_off_t + map_row(r, 0, interleave)] = __float2half_rn(tile[tx][i]);
+  }
+}
+
+__global__ void transpose_f16_kernel(const __half* __restrict__ src, int rows, int cols, int ld_src,
+                                     __half* __restrict__ dst, int ld_dst) {
+  __shared__ __half tile[32][34];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int i = ty; i < 32; i += 8) {
+    const int r = r0 + i, c = c0 + tx;
+    tile[i][tx] = (r < rows && c < cols) ? src[static_cast<size_t>(r) * ld_src + c] : __float2half_rn(0.f);
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int c = c0 + i, r = r0 + tx;
+    if (r < rows && c < cols) dst[static_cast<size_t>(c) * ld_dst + r] = tile[tx][i];
+  }
+}
+
+// ------------------------------------------------------------------ INT8
+// Bit-exact with quantize_kernel (src/kernels/quantize.cu:8-44): every step is
+// one IEEE-rounded fp32 operation in the reference's order.
+__global__ void quantize_rows_kernel(const float* __restrict__ w, int cols, int8_t* __restrict__ q,
+                                     float* __restrict__ scale) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const float* wr = w + static_cast<size_t>(row) * cols;
+  float mx = 0.f;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) mx = fmaxf(mx, fabsf(wr[c]));
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_max(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float s = __fdiv_rn(red[0], 127.0f);
+  if (threadIdx.x == 0) scale[row] = s;
+  const float inv = (s > 0.0f) ? __fdiv_rn(1.0f, s) : 0.0f;
+  int8_t* qr = q + static_cast<size_t>(row) * cols;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    float v = __fmul_rn(wr[c], inv);
+    v = fminf(fmaxf(v, -127.0f), 127.0f);
+    qr[c] = static_cast<int8_t>(__float2int_rn(v));
+  }
+}
+
+__global__ void dequant_rows_kernel(const int8_t* __restrict__ q, const float* __restrict__ scale, int rows,
+                                    int cols, __half* __restrict__ out) {
+  const int64_t n = static_cast<int64_t>(rows) * cols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = __float2half_rn(static_cast<float>(q[i]) * scale[i / cols]);
+}
+
+int grid_for(int64_t n, int threads) {
+  int64_t g = (n + threads - 1) / threads;
+  if (g > 148 * 32) g = 148 * 32;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+}  // namespace
+
+cudaError_t embed_forward(const int* tokens, const __half* E, float* out, int M, int H, int V, int* err,
+                          cudaStream_t st) {
+  if (H % 8) return cudaErrorInvalidValue;
+  embed_kernel<<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(tokens, E, out, M, H, V, err);
+  return cudaGetLastError();
+}
+
+cudaError_t rmsnorm_forward(const float* x, const float* w, __half* out, int M, int H, float eps, cudaStream_t st) {
+  if (H % 4) return cudaErrorInvalidValue;
+  rmsnorm_fwd_kernel<<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(x, w, out, M, H, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t rmsnorm_backward(const float* dy, const float* x, const float* w, float* dres, __half* dres16, int M,
+                             int H, float eps, int accumulate, cudaStream_t st) {
+  if (H % 4) return cudaErrorInvalidValue;
+  rmsnorm_bwd_kernel<<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(dy, x, w, dres, dres16, M, H, eps,
+                                                                                  accumulate);
+  return cudaGetLastError();
+}
+
+cudaError_t rope_tables(float* cos_t, float* sin_t, int S, int hd, float theta, cudaStream_t st) {
+  const int n = S * (hd / 2);
+  rope_table_kernel<<<(n + 255) / 256, 256, 0, st>>>(cos_t, sin_t, S, hd, theta);
+  return cudaGetLastError();
+}
+
+cudaError_t qknorm_rope_forward(const __half* qkv, int ld_qkv, const float* qn_w, const float* kn_w,
+                                const float* cos_t, const float* sin_t, __half* q_out, __half* k_out, int B, int S,
+                                int nh, int nkv, int hd, float eps, cudaStream_t st) {
+  const int M = B * S;
+  const int warps = M * (nh + nkv);
+  const int grid = (warps + kRowWarps - 1) / kRowWarps;
+  if (hd == 128)
+    qknorm_rope_fwd_kernel<128><<<grid, kRowWarps * 32, 0, st>>>(qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, q_out, k_out,
+                                                                  M, S, nh, nkv, eps);
+  else if (hd == 64)
+    qknorm_rope_fwd_kernel<64><<<grid, kRowWarps * 32, 0, st>>>(qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, q_out, k_out,
+                                                                 M, S, nh, nkv, eps);
+  else
+    return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+cudaError_t qknorm_rope_backward(const float* dq, const float* dk, const __half* qkv, int ld_qkv, const float* qn_w,
+                                 const float* kn_w, const float* cos_t, const float* sin_t, __half* dqkv, int B,
+                                 int S, int nh, int nkv, int hd, float eps, cudaStream_t st) {
+  const int M = B * S;
+  const int warps = M * (nh + nkv);
+  const int grid = (warps + kRowWarps - 1) / kRowWarps;
+  if (hd == 128)
+    qknorm_rope_bwd_kernel<128><<<grid, kRowWarps * 32, 0, st>>>(dq, dk, qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, dqkv,
+                                                                  M, S, nh, nkv, eps);
+  else if (hd == 64)
+    qknorm_rope_bwd_kernel<64><<<grid, kRowWarps * 32, 0, st>>>(dq, dk, qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, dqkv,
+                                                                 M, S, nh, nkv, eps);
+  else
+    return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+cudaError_t ce_valid_rows(uint8_t* valid, const int* targets, int B, int S, int all_positions, int V, int* err,
+                          cudaStream_t st) {
+  const int M = B * S;
+  ce_valid_kernel<<<(M + 255) / 256, 256, 0, st>>>(valid, targets, B, S, all_positions, V, err);
+  return cudaGetLastError();
+}
+
+cudaError_t ce_reduce(const float* part_max, const float* part_sum, const float* tgt_logit, const uint8_t* valid,
+                      float* lse, float* row_loss_and_sum, int M, int tiles_n, cudaStream_t st) {
+  float* row_loss = row_loss_and_sum;
+  float* total = row_loss_and_sum + M;
+  ce_lse_kernel<<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(part_max, part_sum, tgt_logit, valid,
+                                                                             lse, row_loss, M, tiles_n);
+  sum_kernel<<<1, 1024, 0, st>>>(row_loss, M, total);
+  return cudaGetLastError();
+}
+
+cudaError_t adamw_flat(float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1, float b2,
+                       float eps, float wd, float bc1, float bc2, float gscale, cudaStream_t st) {
+  adamw_kernel<<<grid_for(n, 256), 256, 0, st>>>(p, g, m, v, n, lr, b1, b2, eps, wd, bc1, bc2, gscale);
+  return cudaGetLastError();
+}
+
+cudaError_t fill_f32(float* p, int64_t n, float v, cudaStream_t st) {
+  fill_f32_kernel<<<grid_for(n, 256), 256, 0, st>>>(p, n, v);
+  return cudaGetLastError();
+}
+cudaError_t fill_normal_f16(__half* p, int64_t n, uint64_t seed, float sd, cudaStream_t st) {
+  fill_normal_f16_kernel<<<grid_for(n, 256), 256, 0, st>>>(p, n, seed, sd);
+  return cudaGetLastError();
+}
+cudaError_t fill_normal_f32(float* p, int64_t n, uint64_t seed, float sd, cudaStream_t st) {
+  fill_normal_f32_kernel<<<grid_for(n, 256), 256, 0, st>>>(p, n, seed, sd);
+  return cudaGetLastError();
+}
+cudaError_t fill_uniform_f32(float* p, int64_t n, uint64_t seed, float lo, float hi, cudaStream_t st) {
+  fill_uniform_f32_kernel<<<grid_for(n, 256), 256, 0, st>>>(p, n, seed, lo, hi);
+  return cudaGetLastError();
+}
+
+cudaError_t convert_weight(const float* src, int rows, int cols, __half* dst, int ld_dst, int row_off,
+                           int interleave, __half* dst_t, int ld_t, int col_off_t, cudaStream_t st) {
+  dim3 grid((cols + 31) / 32, (rows + 31) / 32);
+  convert_weight_kernel<<<grid, 256, 0, st>>>(src, rows, cols, dst, ld_dst, row_off, interleave, dst_t, ld_t,
+                                              col_off_t);
+  return cudaGetLastError();
+}
+
+cudaError_t transpose_f16(const __half* src, int rows, int cols, int ld_src, __half* dst, int ld_dst,
+                          cudaStream_t st) {
+  dim3 grid((cols + 31) / 32, (rows + 31) / 32);
+  transpose_f16_kernel<<<grid, 256, 0, st>>>(src, rows, cols, ld_src, dst, ld_dst);
+  return cudaGetLastError();
+}
+
+cudaError_t quantize_rows_int8(const float* w, int rows, int cols, int8_t* q, float* scale, cudaStream_t st) {
+  if (rows <= 0 || cols <= 0) return cudaErrorInvalidValue;
+  quantize_rows_kernel<<<rows, 256, 0, st>>>(w, cols, q, scale);
+  return cudaGetLastError();
+}
+
+cudaError_t dequant_rows_f16(const int8_t* q, const float* scale, int rows, int cols, __half* out, cudaStream_t st) {
+  const int64_t n = static_cast<int64_t>(rows) * cols;
+  dequant_rows_kernel<<<grid_for(n, 256), 256, 0, st>>>(q, scale, rows, cols, out);
+  return cudaGetLastError();
+}
+
+}  // namespace llmcu

@@ -1,0 +1,1221 @@
+// llmcu.cu -- the C ABI (include/llmcu.h): context, device arena, weight and
+// adapter I/O, the training step schedule and data-parallel plumbing.
+//
+// Step schedule on the compute stream (reference order, src/train.cu:251-291,
+// restated for fused kernels; M = batch * seq rows):
+//   lora_prep                          fp16 operands from the fp32 adapters
+//   embed -> for each layer:
+//     rmsnorm(attn) -> h = xn A_cat^T -> qkv = [xn|h][W_qkv|2B]^T
+//     -> QK-norm+RoPE -> flash attention -> h_o = o A_o^T
+//     -> resid_mid = resid + [o|h_o][W_o|2B_o]^T
+//     -> rmsnorm(ffn) -> gate/up GEMM with SwiGLU -> resid_out = resid_mid + act W_d^T
+//   final rmsnorm -> lm_head pass 1 (per-tile max / sum-exp) -> LSE + loss
+//   -> per vocab chunk: lm_head pass 2 (dlogits chunk) + d_xf += dl E_chunk
+//   -> final-norm backward -> for each layer, reversed:
+//     down dX + SwiGLU bwd -> gate/up dX -> ffn-norm bwd -> dh_o -> o dX (+LoRA)
+//     -> LoRA grads (o) -> attention bwd -> RoPE/QK-norm bwd -> dh_qkv
+//     -> qkv dX (+LoRA) -> LoRA grads (q,k,v) -> attn-norm bwd
+//     [data parallel: allreduce of this layer's adapter gradients on the
+//      communication stream, overlapping the layers still to run]
+//   AdamW over the flat adapter buffer.
+#include <nccl.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/llmcu.h"
+#include "common.cuh"
+#include "lora.cuh"
+
+using namespace llmcu;
+
+namespace {
+
+constexpr float kGradScale = 64.0f;   // dlogits are scaled by this power of two (fp16 range)
+constexpr int kVocabChunk = 8192;     // lm_head backward processes the vocabulary in chunks
+
+struct LayerW {
+  __half *wqkv, *wqkvT, *wo, *woT, *wgu, *wguT, *wd, *wdT;
+  float *attn_norm, *ffn_norm, *q_norm, *k_norm;
+  // INT8 base: q [out, in] per fused weight + per-row scales; transposed copies
+  int8_t *q_qkv, *q_o, *q_gu, *q_d;
+  int8_t *qT_qkv, *qT_o, *qT_gu, *qT_d;
+  float *s_qkv, *s_o, *s_gu, *s_d;
+};
+
+struct LayerA {  // forward stash
+  float *resid_mid;
+  __half *xn, *hq, *qkv, *qrope, *krope, *attn, *ho, *xn2, *gu, *act;
+  float* lse;
+};
+
+}  // namespace
+
+struct llmcu_ctx {
+  llmcu_model_cfg m;
+  llmcu_lora_cfg lc;
+  llmcu_run_cfg rc;
+  int device = 0;
+  int H = 0, Q = 0, KV = 0, QKV = 0, I = 0, V = 0, L = 0, hd = 0, nh = 0, nkv = 0, Mmax = 0;
+  LoraDims ld;
+  int64_t n_lora = 0;
+  std::string err;
+  cudaStream_t st = nullptr, comm = nullptr;
+  char* arena = nullptr;
+  size_t arena_bytes = 0;
+
+  // base
+  __half *E = nullptr, *ET = nullptr;
+  float* final_norm = nullptr;
+  int8_t *qE = nullptr;
+  float* sE = nullptr;
+  std::vector<LayerW> lw;
+  // int8 dequant scratch (one layer's fp16 weights, forward and transposed)
+  __half *dq_w = nullptr, *dq_wT = nullptr;
+
+  // lora
+  float *lp = nullptr, *lg = nullptr, *lm = nullptr, *lv = nullptr;
+  __half* lderived = nullptr;
+  float* lpart = nullptr;
+  int lpart_amax = 0;
+
+  // activations
+  std::vector<float*> resid;  // L + 1 buffers
+  std::vector<LayerA> la;
+  __half* xf = nullptr;
+  float *part_max = nullptr, *part_sum = nullptr, *tgt_logit = nullptr, *lse_ce = nullptr, *row_loss = nullptr;
+  uint8_t* valid = nullptr;
+  __half* dl = nullptr;
+  float* d_xf = nullptr;
+  int ce_tiles = 0;
+  // backward scratch
+  float *dres = nullptr, *dxn = nullptr, *dq = nullptr, *dk = nullptr, *delta = nullptr;
+  __half *dres16 = nullptr, *dgu = nullptr, *dho = nullptr, *dattn = nullptr, *dqkv = nullptr, *dhq = nullptr;
+  // io
+  int *tok = nullptr, *tgt = nullptr, *derr = nullptr;
+  float* loss_dev = nullptr;   // [0] = mean loss of the last step
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  float* stage = nullptr;      // fp32 staging for host uploads
+  size_t stage_elems = 0;
+  int last_n_valid = 0;
+
+  // data parallel
+  ncclComm_t nccl = nullptr;
+  int rank = 0, world = 1;
+  int timeout_ms = 60000;
+  std::vector<cudaEvent_t> ev_layer;
+  cudaEvent_t ev_comm_done = nullptr, ev_step_done = nullptr;
+};
+
+namespace {
+
+llmcu_status fail(llmcu_ctx* c, llmcu_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (c) c->err = buf;
+  return s;
+}
+
+#define CK(expr)                                                                                   \
+  do {                                                                                             \
+    cudaError_t e_ = (expr);                                                                       \
+    if (e_ != cudaSuccess)                                                                         \
+      return fail(ctx, LLMCU_ERR_CUDA, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, \
+                  __LINE__);                                                                       \
+  } while (0)
+
+#define CKS(expr)                                  \
+  do {                                             \
+    llmcu_status s_ = (expr);                      \
+    if (s_ != LLMCU_OK) return s_;                 \
+  } while (0)
+
+Operand op(const __half* p, int rows, int k, int ld) { return Operand{p, rows, k, ld}; }
+const Operand kNone{nullptr, 0, 0, 0};
+
+// ------------------------------------------------------------------ arena
+struct Carver {
+  size_t off = 0;
+  char* base = nullptr;
+  template <class T>
+  T* take(size_t n) {
+    off = (off + 255) / 256 * 256;
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += n * sizeof(T);
+    return p;
+  }
+};
+
+void carve(llmcu_ctx* c, Carver& cv) {
+  const size_t H = c->H, Q = c->Q, KV = c->KV, QKV = c->QKV, I = c->I, V = c->V, M = c->Mmax, L = c->L;
+  const bool int8 = c->rc.base_dtype == LLMCU_BASE_INT8;
+  c->lw.assign(L, LayerW{});
+  c->la.assign(L, LayerA{});
+  c->resid.assign(L + 1, nullptr);
+  // base weights
+  if (!int8) {
+    c->E = cv.take<__half>(V * H);
+    c->ET = cv.take<__half>(H * V);
+  } else {
+    c->qE = cv.take<int8_t>(V * H);
+    c->sE = cv.take<float>(V);
+    c->E = cv.take<__half>(V * H);   // dequantised copies of the tied head (gather + lm_head)
+    c->ET = cv.take<__half>(H * V);
+  }
+  c->final_norm = cv.take<float>(H);
+  for (size_t l = 0; l < L; ++l) {
+    LayerW& w = c->lw[l];
+    if (!int8) {
+      w.wqkv = cv.take<__half>(QKV * H);
+      w.wqkvT = cv.take<__half>(H * QKV);
+      w.wo = cv.take<__half>(H * Q);
+      w.woT = cv.take<__half>(Q * H);
+      w.wgu = cv.take<__half>(2 * I * H);
+      w.wguT = cv.take<__half>(H * 2 * I);
+      w.wd = cv.take<__half>(H * I);
+      w.wdT = cv.take<__half>(I * H);
+    } else {
+      w.q_qkv = cv.take<int8_t>(QKV * H);
+      w.qT_qkv = cv.take<int8_t>(H * QKV);
+      w.s_qkv = cv.take<float>(QKV);
+      w.q_o = cv.take<int8_t>(H * Q);
+      w.qT_o = cv.take<int8_t>(Q * H);
+      w.s_o = cv.take<float>(H);
+      w.q_gu = cv.take<int8_t>(2 * I * H);
+      w.qT_gu = cv.take<int8_t>(H * 2 * I);
+      w.s_gu = cv.take<float>(2 * I);
+      w.q_d = cv.take<int8_t>(H * I);
+      w.qT_d = cv.take<int8_t>(I * H);
+      w.s_d = cv.take<float>(H);
+    }
+    w.attn_norm = cv.take<float>(H);
+    w.ffn_norm = cv.take<float>(H);
+    w.q_norm = cv.take<float>(c->hd);
+    w.k_norm = cv.take<float>(c->hd);
+  }
+  if (int8) {
+    const size_t wmax = std::max({QKV * H, H * Q, 2 * I * H, H * I});
+    c->dq_w = cv.take<__half>(wmax);
+    c->dq_wT = cv.take<__half>(wmax);
+  }
+  // lora
+  const size_t n = static_cast<size_t>(c->n_lora);
+  c->lp = cv.take<float>(n);
+  c->lg = cv.take<float>(n);
+  c->lm = cv.take<float>(n);
+  c->lv = cv.take<float>(n);
+  c->lderived = cv.take<__half>(static_cast<size_t>(c->ld.derived_per_layer) * L);
+  c->lpart_amax = static_cast<int>((std::max({H, Q, KV}) + 63) / 64 * 64);
+  c->lpart = cv.take<float>(static_cast<size_t>(kLoraMaxSplits) * kLoraMaxProbs * c->lpart_amax * 16);
+  // activations
+  for (size_t l = 0; l <= L; ++l) c->resid[l] = cv.take<float>(M * H);
+  const size_t lse_n = static_cast<size_t>(c->rc.max_batch) * c->nh * c->rc.max_seq;
+  for (size_t l = 0; l < L; ++l) {
+    LayerA& a = c->la[l];
+    a.resid_mid = cv.take<float>(M * H);
+    a.xn = cv.take<__half>(M * H);
+    a.hq = cv.take<__half>(M * 64);
+    a.qkv = cv.take<__half>(M * QKV);
+    a.qrope = cv.take<__half>(M * Q);
+    a.krope = cv.take<__half>(M * KV);
+    a.attn = cv.take<__half>(M * Q);
+    a.ho = cv.take<__half>(M * 64);
+    a.xn2 = cv.take<__half>(M * H);
+    a.gu = cv.take<__half>(M * 2 * I);
+    a.act = cv.take<__half>(M * I);
+    a.lse = cv.take<float>(lse_n);
+  }
+  c->xf = cv.take<__half>(M * H);
+  c->ce_tiles = static_cast<int>((V + 255) / 256);
+  c->part_max = cv.take<float>(M * c->ce_tiles);
+  c->part_sum = cv.take<float>(M * c->ce_tiles);
+  c->tgt_logit = cv.take<float>(M);
+  c->lse_ce = cv.take<float>(M);
+  c->row_loss = cv.take<float>(M + 1);
+  c->valid = cv.take<uint8_t>(M);
+  const size_t vc = std::min<size_t>(V, kVocabChunk);
+  c->dl = cv.take<__half>(M * vc);
+  c->d_xf = cv.take<float>(M * H);
+  c->dres = cv.take<float>(M * H);
+  c->dres16 = cv.take<__half>(M * H);
+  c->dxn = cv.take<float>(M * H);
+  c->dgu = cv.take<__half>(M * 2 * I);
+  c->dho = cv.take<__half>(M * 64);
+  c->dattn = cv.take<__half>(M * Q);
+  c->dq = cv.take<float>(M * Q);
+  c->dk = cv.take<float>(M * KV);
+  c->delta = cv.take<float>(lse_n);
+  c->dqkv = cv.take<__half>(M * QKV);
+  c->dhq = cv.take<__half>(M * 64);
+  c->tok = cv.take<int>(M);
+  c->tgt = cv.take<int>(M);
+  c->derr = cv.take<int>(4);
+  c->loss_dev = cv.take<float>(4);
+  c->rope_cos = cv.take<float>(static_cast<size_t>(c->rc.max_seq) * (c->hd / 2));
+  c->rope_sin = cv.take<float>(static_cast<size_t>(c->rc.max_seq) * (c->hd / 2));
+  c->stage_elems = std::max({V * H, 2 * I * H, QKV * H});
+  c->stage = cv.take<float>(c->stage_elems);
+}
+
+llmcu_status check_dev_err(llmcu_ctx* ctx) {
+  int e = 0;
+  CK(cudaMemcpyAsync(&e, ctx->derr, sizeof(int), cudaMemcpyDeviceToHost, ctx->st));
+  CK(cudaStreamSynchronize(ctx->st));
+  if (e) {
+    CK(cudaMemsetAsync(ctx->derr, 0, sizeof(int), ctx->st));
+    if (e & kErrTokenRange) return fail(ctx, LLMCU_ERR_INVALID_ARG, "token or target id outside [0, vocab)");
+    return fail(ctx, LLMCU_ERR_DEVICE_CHECK, "device-side check failed (error bits 0x%x)", e);
+  }
+  return LLMCU_OK;
+}
+
+// ---------------------------------------------------------- nccl helpers
+llmcu_status nccl_wait(llmcu_ctx* ctx, ncclResult_t r, const char* what) {
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    if (r == ncclSuccess) return LLMCU_OK;
+    if (r != ncclInProgress) {
+      return fail(ctx, LLMCU_ERR_NCCL, "%s: %s", what, ncclGetErrorString(r));
+    }
+    ncclResult_t ar = ncclSuccess;
+    ncclCommGetAsyncError(ctx->nccl, &ar);
+    r = ar;
+    if (r == ncclInProgress) {
+      const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+      if (ms > ctx->timeout_ms) {
+        ncclCommAbort(ctx->nccl);
+        ctx->nccl = nullptr;
+        ctx->world = 1;
+        return fail(ctx, LLMCU_ERR_TIMEOUT, "%s: NCCL did not complete within %d ms; communicator aborted", what,
+                    ctx->timeout_ms);
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+  }
+}
+
+// Wait on the host for `ev` with the context deadline; on expiry abort NCCL.
+llmcu_status wait_event(llmcu_ctx* ctx, cudaEvent_t ev) {
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    cudaError_t q = cudaEventQuery(ev);
+    if (q == cudaSuccess) return LLMCU_OK;
+    if (q != cudaErrorNotReady) return fail(ctx, LLMCU_ERR_CUDA, "step failed: %s", cudaGetErrorString(q));
+    if (ctx->nccl) {
+      ncclResult_t ar = ncclSuccess;
+      ncclCommGetAsyncError(ctx->nccl, &ar);
+      if (ar != ncclSuccess && ar != ncclInProgress) {
+        ncclCommAbort(ctx->nccl);
+        ctx->nccl = nullptr;
+        ctx->world = 1;
+        return fail(ctx, LLMCU_ERR_NCCL, "NCCL error during step: %s", ncclGetErrorString(ar));
+      }
+    }
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+    if (ms > ctx->timeout_ms) {
+      if (ctx->nccl) {
+        ncclCommAbort(ctx->nccl);
+        ctx->nccl = nullptr;
+        ctx->world = 1;
+      }
+      return fail(ctx, LLMCU_ERR_TIMEOUT, "step did not complete within %d ms", ctx->timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  }
+}
+
+// ------------------------------------------------------------- INT8 base
+// Dequantise one layer's weight (or its transposed copy) into fp16 scratch.
+// Forward copy: W[o, i] = q[o, i] * s[o].  Transposed copy: WT[i, o] = qT[i, o] * s[o].
+__global__ void dequant_cols_kernel(const int8_t* __restrict__ q, const float* __restrict__ s, int rows, int cols,
+                                    __half* __restrict__ out) {
+  const int64_t n = static_cast<int64_t>(rows) * cols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = __float2half_rn(static_cast<float>(q[i]) * s[i % cols]);
+}
+
+__global__ void transpose_i8_kernel(const int8_t* __restrict__ src, int rows, int cols, int8_t* __restrict__ dst) {
+  __shared__ int8_t tile[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int i = ty; i < 32; i += 8) {
+    const int r = r0 + i, c = c0 + tx;
+    tile[i][tx] = (r < rows && c < cols) ? src[static_cast<size_t>(r) * cols + c] : 0;
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int c = c0 + i, r = r0 + tx;
+    if (r < rows && c < cols) dst[static_cast<size_t>(c) * rows + r] = tile[tx][i];
+  }
+}
+
+__global__ void scale_loss_kernel(const float* total, float inv_n, float* out) { out[0] = total[0] * inv_n; }
+
+int grid_n(int64_t n) {
+  int64_t g = (n + 255) / 256;
+  return static_cast<int>(std::min<int64_t>(std::max<int64_t>(g, 1), 148 * 16));
+}
+
+const __half* fwd_weight(llmcu_ctx* c, const __half* w16, const int8_t* q, const float* s, int rows, int cols,
+                         cudaError_t* e) {
+  if (c->rc.base_dtype != LLMCU_BASE_INT8) return w16;
+  *e = dequant_rows_f16(q, s, rows, cols, c->dq_w, c->st);
+  return c->dq_w;
+}
+const __half* bwd_weight(llmcu_ctx* c, const __half* wT16, const int8_t* qT, const float* s, int rows_t, int cols_t,
+                         cudaError_t* e) {
+  if (c->rc.base_dtype != LLMCU_BASE_INT8) return wT16;
+  dequant_cols_kernel<<<grid_n(static_cast<int64_t>(rows_t) * cols_t), 256, 0, c->st>>>(qT, s, rows_t, cols_t,
+                                                                                        c->dq_wT);
+  *e = cudaGetLastError();
+  return c->dq_wT;
+}
+
+// ----------------------------------------------------------------- step
+llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
+  const int M = B * S;
+  const int H = ctx->H, Q = ctx->Q, KV = ctx->KV, QKV = ctx->QKV, I = ctx->I, V = ctx->V;
+  const float eps = ctx->m.rms_eps;
+  cudaStream_t st = ctx->st;
+  int* err = ctx->derr;
+  const LoraDims& d = ctx->ld;
+  const int r = ctx->lc.rank;
+  const int n_valid_local = ctx->rc.loss_all_positions ? M : B * (S - 1);
+  const double n_valid_total = static_cast<double>(n_valid_local) * ctx->world;
+  ctx->last_n_valid = n_valid_local;
+  const float unscale = static_cast<float>(1.0 / (kGradScale * n_valid_total));
+  cudaError_t e = cudaSuccess;
+
+  CK(lora_prep(ctx->lp, d, ctx->L, ctx->lderived, st));
+  CK(ce_valid_rows(ctx->valid, ctx->tgt, B, S, ctx->rc.loss_all_positions, V, err, st));
+  const __half* E = ctx->E;
+  CK(embed_forward(ctx->tok, E, ctx->resid[0], M, H, V, err, st));
+
+  // ------------------------------------------------------------ forward
+  for (int l = 0; l < ctx->L; ++l) {
+    LayerW& w = ctx->lw[l];
+    LayerA& a = ctx->la[l];
+    const __half* D = ctx->lderived + d.derived_per_layer * l;
+    const float* x = ctx->resid[l];
+    CK(rmsnorm_forward(x, w.attn_norm, a.xn, M, H, eps, st));
+    CK(gemm(op(a.xn, M, H, H), op(D + d.d_acat, 64, H, H), kNone, kNone, M, 64, Epi::kStoreF16,
+            EpiArgs{a.hq, 64}, err, st));
+    const __half* wqkv = fwd_weight(ctx, w.wqkv, w.q_qkv, w.s_qkv, QKV, H, &e);
+    CK(e);
+    CK(gemm(op(a.xn, M, H, H), op(wqkv, QKV, H, H), op(a.hq, M, 64, 64), op(D + d.d_bblk, QKV, 64, 64), M, QKV,
+            Epi::kStoreF16, EpiArgs{a.qkv, QKV}, err, st));
+    CK(qknorm_rope_forward(a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, a.qrope, a.krope, B, S,
+                           ctx->nh, ctx->nkv, ctx->hd, eps, st));
+    CK(attention_forward(a.qrope, a.krope, a.qkv + Q + KV, a.attn, a.lse, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV,
+                         QKV, Q, st));
+    CK(gemm(op(a.attn, M, Q, Q), op(D + d.d_ao, 64, Q, Q), kNone, kNone, M, 64, Epi::kStoreF16, EpiArgs{a.ho, 64},
+            err, st));
+    const __half* wo = fwd_weight(ctx, w.wo, w.q_o, w.s_o, H, Q, &e);
+    CK(e);
+    {
+      EpiArgs ea;
+      ea.out = a.resid_mid;
+      ea.ld_out = H;
+      ea.resid = x;
+      CK(gemm(op(a.attn, M, Q, Q), op(wo, H, Q, Q), op(a.ho, M, 64, 64), op(D + d.d_bo, H, 64, 64), M, H,
+              Epi::kResidF32, ea, err, st));
+    }
+    CK(rmsnorm_forward(a.resid_mid, w.ffn_norm, a.xn2, M, H, eps, st));
+    const __half* wgu = fwd_weight(ctx, w.wgu, w.q_gu, w.s_gu, 2 * I, H, &e);
+    CK(e);
+    {
+      EpiArgs ea;
+      ea.gu = a.gu;
+      ea.ld_gu = 2 * I;
+      ea.act = a.act;
+      ea.ld_act = I;
+      CK(gemm(op(a.xn2, M, H, H), op(wgu, 2 * I, H, H), kNone, kNone, M, 2 * I, Epi::kSwiGLU, ea, err, st, 256));
+    }
+    const __half* wd = fwd_weight(ctx, w.wd, w.q_d, w.s_d, H, I, &e);
+    CK(e);
+    {
+      EpiArgs ea;
+      ea.out = ctx->resid[l + 1];
+      ea.ld_out = H;
+      ea.resid = a.resid_mid;
+      CK(gemm(op(a.act, M, I, I), op(wd, H, I, I), kNone, kNone, M, H, Epi::kResidF32, ea, err, st));
+    }
+  }
+
+  // ------------------------------------------------------- lm_head + CE
+  float* xfinal = ctx->resid[ctx->L];
+  CK(rmsnorm_forward(xfinal, ctx->final_norm, ctx->xf, M, H, eps, st));
+  {
+    EpiArgs ea;
+    ea.targets = ctx->tgt;
+    ea.part_max = ctx->part_max;
+    ea.part_sum = ctx->part_sum;
+    ea.tgt_logit = ctx->tgt_logit;
+    CK(gemm(op(ctx->xf, M, H, H), op(E, V, H, H), kNone, kNone, M, V, Epi::kCEStats, ea, err, st, 256));
+  }
+  CK(ce_reduce(ctx->part_max, ctx->part_sum, ctx->tgt_logit, ctx->valid, ctx->lse_ce, ctx->row_loss, M,
+               ctx->ce_tiles, st));
+  const int vc = std::min(V, kVocabChunk);
+  for (int c0 = 0, ci = 0; c0 < V; c0 += vc, ++ci) {
+    const int n = std::min(vc, V - c0);
+    EpiArgs ea;
+    ea.targets = ctx->tgt;
+    ea.lse = ctx->lse_ce;
+    ea.valid = ctx->valid;
+    ea.out = ctx->dl;
+    ea.ld_out = vc;
+    ea.col_base = c0;
+    ea.gscale = kGradScale;
+    CK(gemm(op(ctx->xf, M, H, H), op(E + static_cast<size_t>(c0) * H, n, H, H), kNone, kNone, M, n, Epi::kCEGrad, ea,
+            err, st));
+    EpiArgs eb;
+    eb.out = ctx->d_xf;
+    eb.ld_out = H;
+    eb.accumulate = ci > 0;
+    CK(gemm(op(ctx->dl, M, n, vc), op(ctx->ET + c0, H, n, V), kNone, kNone, M, H, Epi::kStoreF32, eb, err, st));
+  }
+  CK(rmsnorm_backward(ctx->d_xf, xfinal, ctx->final_norm, ctx->dres, ctx->dres16, M, H, eps, 0, st));
+
+  // ----------------------------------------------------------- backward
+  for (int l = ctx->L - 1; l >= 0; --l) {
+    LayerW& w = ctx->lw[l];
+    LayerA& a = ctx->la[l];
+    const __half* D = ctx->lderived + d.derived_per_layer * l;
+    float* G = ctx->lg + d.per_layer * l;
+    // MLP
+    const __half* wdT = bwd_weight(ctx, w.wdT, w.qT_d, w.s_d, I, H, &e);
+    CK(e);
+    {
+      EpiArgs ea;
+      ea.gu_in = a.gu;
+      ea.gu = ctx->dgu;
+      ea.ld_gu = 2 * I;
+      CK(gemm(op(ctx->dres16, M, H, H), op(wdT, I, H, H), kNone, kNone, M, I, Epi::kSwiGLUBwd, ea, err, st, 256));
+    }
+    const __half* wguT = bwd_weight(ctx, w.wguT, w.qT_gu, w.s_gu, H, 2 * I, &e);
+    CK(e);
+    CK(gemm(op(ctx->dgu, M, 2 * I, 2 * I), op(wguT, H, 2 * I, 2 * I), kNone, kNone, M, H, Epi::kStoreF32,
+            EpiArgs{ctx->dxn, H}, err, st));
+    CK(rmsnorm_backward(ctx->dxn, a.resid_mid, w.ffn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
+    // O projection
+    CK(gemm(op(ctx->dres16, M, H, H), op(D + d.d_boT, 64, H, H), kNone, kNone, M, 64, Epi::kStoreF16,
+            EpiArgs{ctx->dho, 64}, err, st));
+    const __half* woT = bwd_weight(ctx, w.woT, w.qT_o, w.s_o, Q, H, &e);
+    CK(e);
+    CK(gemm(op(ctx->dres16, M, H, H), op(woT, Q, H, H), op(ctx->dho, M, 64, 64), op(D + d.d_aoT, Q, 64, 64), M, Q,
+            Epi::kStoreF16, EpiArgs{ctx->dattn, Q}, err, st));
+    {
+      LoraGradBatch gb{};
+      gb.n = 2;
+      gb.a_max = ctx->lpart_amax;
+      // dBo[h, j] = s * sum_m dres[m, h] ho[m, j]
+      gb.p[0] = LoraGradProb{ctx->dres16, H, a.ho, 64, G + d.oBo, r, 1, H, r, d.scale * unscale};
+      // dAo[j, q] = sum_m dho[m, j] attn[m, q]
+      gb.p[1] = LoraGradProb{a.attn, Q, ctx->dho, 64, G + d.oAo, 1, Q, Q, r, unscale};
+      CK(lora_grad(gb, M, ctx->lpart, st));
+    }
+    // attention
+    CK(attention_backward(a.qrope, a.krope, a.qkv + Q + KV, a.attn, ctx->dattn, a.lse, ctx->delta, ctx->dq, ctx->dk,
+                          ctx->dqkv + Q + KV, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV, QKV, Q, Q, KV, QKV, st));
+    CK(qknorm_rope_backward(ctx->dq, ctx->dk, a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, ctx->dqkv,
+                            B, S, ctx->nh, ctx->nkv, ctx->hd, eps, st));
+    // QKV projection
+    CK(gemm(op(ctx->dqkv, M, QKV, QKV), op(D + d.d_bblkT, 64, QKV, QKV), kNone, kNone, M, 64, Epi::kStoreF16,
+            EpiArgs{ctx->dhq, 64}, err, st));
+    const __half* wqkvT = bwd_weight(ctx, w.wqkvT, w.qT_qkv, w.s_qkv, H, QKV, &e);
+    CK(e);
+    CK(gemm(op(ctx->dqkv, M, QKV, QKV), op(wqkvT, H, QKV, QKV), op(ctx->dhq, M, 64, 64), op(D + d.d_acatT, H, 64, 64),
+            M, H, Epi::kStoreF32, EpiArgs{ctx->dxn, H}, err, st));
+    {
+      LoraGradBatch gb{};
+      gb.n = 6;
+      gb.a_max = ctx->lpart_amax;
+      const float sb = d.scale * unscale;
+      gb.p[0] = LoraGradProb{ctx->dqkv, QKV, a.hq, 64, G + d.oBq, r, 1, Q, r, sb};
+      gb.p[1] = LoraGradProb{ctx->dqkv + Q, QKV, a.hq + kSegK, 64, G + d.oBk, r, 1, KV, r, sb};
+      gb.p[2] = LoraGradProb{ctx->dqkv + Q + KV, QKV, a.hq + kSegV, 64, G + d.oBv, r, 1, KV, r, sb};
+      gb.p[3] = LoraGradProb{a.xn, H, ctx->dhq, 64, G + d.oAq, 1, H, H, r, unscale};
+      gb.p[4] = LoraGradProb{a.xn, H, ctx->dhq + kSegK, 64, G + d.oAk, 1, H, H, r, unscale};
+      gb.p[5] = LoraGradProb{a.xn, H, ctx->dhq + kSegV, 64, G + d.oAv, 1, H, H, r, unscale};
+      CK(lora_grad(gb, M, ctx->lpart, st));
+    }
+    CK(rmsnorm_backward(ctx->dxn, ctx->resid[l], w.attn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
+    if (ctx->nccl) {
+      CK(cudaEventRecord(ctx->ev_layer[l], st));
+      CK(cudaStreamWaitEvent(ctx->comm, ctx->ev_layer[l], 0));
+      CKS(nccl_wait(ctx, ncclAllReduce(G, G, static_cast<size_t>(d.per_layer), ncclFloat, ncclSum, ctx->nccl,
+                                       ctx->comm),
+                    "allreduce of layer gradients"));
+    }
+  }
+  // loss: sum over valid rows (over all ranks) / number of valid rows
+  float* total = ctx->row_loss + M;
+  if (ctx->nccl) {
+    CK(cudaEventRecord(ctx->ev_layer[0], st));
+    CK(cudaStreamWaitEvent(ctx->comm, ctx->ev_layer[0], 0));
+    CKS(nccl_wait(ctx, ncclAllReduce(total, total, 1, ncclFloat, ncclSum, ctx->nccl, ctx->comm), "loss allreduce"));
+    CK(cudaEventRecord(ctx->ev_comm_done, ctx->comm));
+    CK(cudaStreamWaitEvent(st, ctx->ev_comm_done, 0));
+  }
+  scale_loss_kernel<<<1, 1, 0, st>>>(total, static_cast<float>(1.0 / n_valid_total), ctx->loss_dev);
+  CK(cudaGetLastError());
+  return LLMCU_OK;
+}
+
+llmcu_status validate_step(llmcu_ctx* ctx, int B, int S) {
+  if (B <= 0 || S <= 1 || B > ctx->rc.max_batch || S > ctx->rc.max_seq)
+    return fail(ctx, LLMCU_ERR_INVALID_ARG, "batch %d / seq %d outside [1, %d] x [2, %d]", B, S, ctx->rc.max_batch,
+                ctx->rc.max_seq);
+  return LLMCU_OK;
+}
+
+llmcu_status do_adamw(llmcu_ctx* ctx, const llmcu_adamw_cfg* o, int step) {
+  if (!o || step < 1) return fail(ctx, LLMCU_ERR_INVALID_ARG, "adamw: null config or step < 1");
+  const float bc1 = 1.0f - powf(o->beta1, static_cast<float>(step));
+  const float bc2 = 1.0f - powf(o->beta2, static_cast<float>(step));
+  CK(adamw_flat(ctx->lp, ctx->lg, ctx->lm, ctx->lv, ctx->n_lora, o->lr, o->beta1, o->beta2, o->eps, o->weight_decay,
+                bc1, bc2, 1.0f, ctx->st));
+  return LLMCU_OK;
+}
+
+llmcu_status upload_tokens(llmcu_ctx* ctx, const int32_t* tokens, const int32_t* targets, int M) {
+  if (!tokens || !targets) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null token pointer");
+  CK(cudaMemcpyAsync(ctx->tok, tokens, sizeof(int) * M, cudaMemcpyHostToDevice, ctx->st));
+  CK(cudaMemcpyAsync(ctx->tgt, targets, sizeof(int) * M, cudaMemcpyHostToDevice, ctx->st));
+  return LLMCU_OK;
+}
+
+llmcu_status read_loss(llmcu_ctx* ctx, float* loss_out) {
+  float h = 0.f;
+  CK(cudaMemcpyAsync(&h, ctx->loss_dev, sizeof(float), cudaMemcpyDeviceToHost, ctx->st));
+  CK(cudaEventRecord(ctx->ev_step_done, ctx->st));
+  CKS(wait_event(ctx, ctx->ev_step_done));
+  CKS(check_dev_err(ctx));
+  if (loss_out) *loss_out = h;
+  return LLMCU_OK;
+}
+
+}  // namespace
+
+// ====================================================================== ABI
+
+extern "C" {
+
+const char* llmcu_version(void) { return "llmcu 1 sm_100a"; }
+
+const char* llmcu_last_error(const llmcu_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+size_t llmcu_device_bytes(const llmcu_ctx* ctx) { return ctx ? ctx->arena_bytes : 0; }
+
+void* llmcu_stream(const llmcu_ctx* ctx) { return ctx ? static_cast<void*>(ctx->st) : nullptr; }
+
+int64_t llmcu_lora_param_count(const llmcu_ctx* ctx) { return ctx ? ctx->n_lora : 0; }
+
+llmcu_status llmcu_ctx_create(const llmcu_model_cfg* model, const llmcu_lora_cfg* lora, const llmcu_run_cfg* run,
+                              int device, llmcu_ctx** out) {
+  if (!model || !lora || !run || !out) return LLMCU_ERR_INVALID_ARG;
+  *out = nullptr;
+  const llmcu_model_cfg& m = *model;
+  if (m.hidden <= 0 || m.n_layers <= 0 || m.n_heads <= 0 || m.n_kv_heads <= 0 || m.vocab <= 0 || m.ffn <= 0)
+    return LLMCU_ERR_INVALID_ARG;
+  if (m.head_dim != 64 && m.head_dim != 128) return LLMCU_ERR_UNSUPPORTED;
+  if (m.n_heads % m.n_kv_heads) return LLMCU_ERR_INVALID_ARG;
+  if (m.hidden % 64 || m.ffn % 128 || m.vocab % 8) return LLMCU_ERR_UNSUPPORTED;
+  if (lora->rank < 1 || lora->rank > 16) return LLMCU_ERR_UNSUPPORTED;
+  if (run->max_batch < 1 || run->max_seq < 2) return LLMCU_ERR_INVALID_ARG;
+  if (run->base_dtype != LLMCU_BASE_FP16 && run->base_dtype != LLMCU_BASE_INT8) return LLMCU_ERR_INVALID_ARG;
+
+  llmcu_ctx* ctx = new llmcu_ctx();
+  ctx->m = m;
+  ctx->lc = *lora;
+  ctx->rc = *run;
+  ctx->device = device;
+  ctx->H = m.hidden;
+  ctx->L = m.n_layers;
+  ctx->nh = m.n_heads;
+  ctx->nkv = m.n_kv_heads;
+  ctx->hd = m.head_dim;
+  ctx->Q = m.n_heads * m.head_dim;
+  ctx->KV = m.n_kv_heads * m.head_dim;
+  ctx->QKV = ctx->Q + 2 * ctx->KV;
+  ctx->I = m.ffn;
+  ctx->V = m.vocab;
+  ctx->Mmax = run->max_batch * run->max_seq;
+  ctx->ld = LoraDims::make(lora->rank, ctx->H, ctx->Q, ctx->KV, lora->alpha / static_cast<float>(lora->rank));
+  ctx->n_lora = ctx->ld.per_layer * ctx->L;
+
+  auto bail = [&](llmcu_status s) {
+    llmcu_ctx_destroy(ctx);
+    return s;
+  };
+  if (cudaSetDevice(device) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
+  if (cudaStreamCreateWithFlags(&ctx->st, cudaStreamNonBlocking) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
+  if (cudaStreamCreateWithFlags(&ctx->comm, cudaStreamNonBlocking) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
+  Carver probe;
+  carve(ctx, probe);
+  ctx->arena_bytes = probe.off + 256;
+  if (cudaMalloc(&ctx->arena, ctx->arena_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    ctx->arena = nullptr;
+    return bail(LLMCU_ERR_OOM);
+  }
+  Carver cv;
+  cv.base = ctx->arena;
+  carve(ctx, cv);
+  ctx->ev_layer.assign(ctx->L, nullptr);
+  for (auto& ev : ctx->ev_layer)
+    if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
+  if (cudaEventCreateWithFlags(&ctx->ev_comm_done, cudaEventDisableTiming) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
+  if (cudaEventCreateWithFlags(&ctx->ev_step_done, cudaEventDisableTiming) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
+  // zero everything once (adapters A = B = 0, moments 0), norms = 1
+  if (cudaMemsetAsync(ctx->arena, 0, ctx->arena_bytes, ctx->st) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
+  fill_f32(ctx->final_norm, ctx->H, 1.0f, ctx->st);
+  for (auto& w : ctx->lw) {
+    fill_f32(w.attn_norm, ctx->H, 1.0f, ctx->st);
+    fill_f32(w.ffn_norm, ctx->H, 1.0f, ctx->st);
+    fill_f32(w.q_norm, ctx->hd, 1.0f, ctx->st);
+    fill_f32(w.k_norm, ctx->hd, 1.0f, ctx->st);
+  }
+  if (rope_tables(ctx->rope_cos, ctx->rope_sin, run->max_seq, ctx->hd, m.rope_theta, ctx->st) != cudaSuccess)
+    return bail(LLMCU_ERR_CUDA);
+  if (cudaStreamSynchronize(ctx->st) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
+  *out = ctx;
+  return LLMCU_OK;
+}
+
+void llmcu_ctx_destroy(llmcu_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  if (ctx->st) cudaStreamSynchronize(ctx->st);
+  if (ctx->comm) cudaStreamSynchronize(ctx->comm);
+  if (ctx->nccl) ncclCommDestroy(ctx->nccl);
+  for (auto ev : ctx->ev_layer)
+    if (ev) cudaEventDestroy(ev);
+  if (ctx->ev_comm_done) cudaEventDestroy(ctx->ev_comm_done);
+  if (ctx->ev_step_done) cudaEventDestroy(ctx->ev_step_done);
+  if (ctx->arena) cudaFree(ctx->arena);
+  if (ctx->st) cudaStreamDestroy(ctx->st);
+  if (ctx->comm) cudaStreamDestroy(ctx->comm);
+  delete ctx;
+}
+
+llmcu_status llmcu_synchronize(llmcu_ctx* ctx) {
+  if (!ctx) return LLMCU_ERR_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  CK(cudaStreamSynchronize(ctx->st));
+  CK(cudaStreamSynchronize(ctx->comm));
+  return LLMCU_OK;
+}
+
+// ---------------------------------------------------------------- weights
+
+static llmcu_status upload_stage(llmcu_ctx* ctx, const float* host, size_t n) {
+  if (n > ctx->stage_elems) return fail(ctx, LLMCU_ERR_INVALID_ARG, "tensor larger than the staging buffer");
+  CK(cudaMemcpyAsync(ctx->stage, host, n * sizeof(float), cudaMemcpyHostToDevice, ctx->st));
+  return LLMCU_OK;
+}
+
+// Places one fp32 [rows, cols] weight (already in ctx->stage) into the fused
+// fp16 layout (row offset / gate-up interleave) and its transposed copy, or
+// into the INT8 layout (per-row quantiser + transposed int8 copy).
+static llmcu_status place_linear(llmcu_ctx* ctx, int rows, int cols, __half* w, __half* wT, int ld_t, int row_off,
+                                 int interleave, int8_t* q, int8_t* qT, float* s) {
+  if (ctx->rc.base_dtype != LLMCU_BASE_INT8) {
+    CK(convert_weight(ctx->stage, rows, cols, w, cols, row_off, interleave, wT, ld_t, 0, ctx->st));
+    return LLMCU_OK;
+  }
+  // INT8: quantise rows of this tensor in place of the fused block
+  const int fused_row = interleave ? 0 : row_off;
+  if (interleave) {
+    // quantise into a temporary block then scatter rows to the interleaved slots
+    int8_t* tmp = reinterpret_cast<int8_t*>(ctx->dq_w);
+    float* stmp = reinterpret_cast<float*>(ctx->dq_wT);
+    CK(quantize_rows_int8(ctx->stage, rows, cols, tmp, stmp, ctx->st));
+    for (int r0 = 0; r0 < rows; r0 += 128) {
+      const int dst_row = (r0 >> 7) * 256 + (interleave == 2 ? 128 : 0);
+      const int n = std::min(128, rows - r0);
+      CK(cudaMemcpyAsync(q + static_cast<size_t>(dst_row) * cols, tmp + static_cast<size_t>(r0) * cols,
+                         static_cast<size_t>(n) * cols, cudaMemcpyDeviceToDevice, ctx->st));
+      CK(cudaMemcpyAsync(s + dst_row, stmp + r0, n * sizeof(float), cudaMemcpyDeviceToDevice, ctx->st));
+    }
+  } else {
+    CK(quantize_rows_int8(ctx->stage, rows, cols, q + static_cast<size_t>(fused_row) * cols, s + fused_row, ctx->st));
+  }
+  (void)qT;
+  (void)wT;
+  (void)ld_t;
+  return LLMCU_OK;
+}
+
+static llmcu_status finish_int8_transposes(llmcu_ctx* ctx, int layer) {
+  LayerW& w = ctx->lw[layer];
+  const int H = ctx->H, Q = ctx->Q, QKV = ctx->QKV, I = ctx->I;
+  struct T { const int8_t* q; int8_t* qT; int rows, cols; } ts[4] = {
+      {w.q_qkv, w.qT_qkv, QKV, H}, {w.q_o, w.qT_o, H, Q}, {w.q_gu, w.qT_gu, 2 * I, H}, {w.q_d, w.qT_d, H, I}};
+  for (auto& t : ts) {
+    dim3 grid((t.cols + 31) / 32, (t.rows + 31) / 32);
+    transpose_i8_kernel<<<grid, 256, 0, ctx->st>>>(t.q, t.rows, t.cols, t.qT);
+    CK(cudaGetLastError());
+  }
+  return LLMCU_OK;
+}
+
+llmcu_status llmcu_set_base_tensor(llmcu_ctx* ctx, int id, int layer, const float* host) {
+  if (!ctx || !host) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null argument");
+  CK(cudaSetDevice(ctx->device));
+  const int H = ctx->H, Q = ctx->Q, KV = ctx->KV, QKV = ctx->QKV, I = ctx->I, V = ctx->V, hd = ctx->hd;
+  const bool per_layer = id >= LLMCU_T_ATTN_NORM && id < LLMCU_T_COUNT;
+  if (per_layer && (layer < 0 || layer >= ctx->L)) return fail(ctx, LLMCU_ERR_INVALID_ARG, "layer %d out of range", layer);
+  const bool int8 = ctx->rc.base_dtype == LLMCU_BASE_INT8;
+  switch (id) {
+    case LLMCU_T_EMBED: {
+      CKS(upload_stage(ctx, host, static_cast<size_t>(V) * H));
+      if (!int8) {
+        CK(convert_weight(ctx->stage, V, H, ctx->E, H, 0, 0, ctx->ET, V, 0, ctx->st));
+      } else {
+        CK(quantize_rows_int8(ctx->stage, V, H, ctx->qE, ctx->sE, ctx->st));
+        CK(dequant_rows_f16(ctx->qE, ctx->sE, V, H, ctx->E, ctx->st));
+        CK(transpose_f16(ctx->E, V, H, H, ctx->ET, V, ctx->st));
+      }
+      break;
+    }
+    case LLMCU_T_FINAL_NORM:
+      CK(cudaMemcpyAsync(ctx->final_norm, host, H * sizeof(float), cudaMemcpyHostToDevice, ctx->st));
+      break;
+    case LLMCU_T_ATTN_NORM:
+      CK(cudaMemcpyAsync(ctx->lw[layer].attn_norm, host, H * sizeof(float), cudaMemcpyHostToDevice, ctx->st));
+      break;
+    case LLMCU_T_FFN_NORM:
+      CK(cudaMemcpyAsync(ctx->lw[layer].ffn_norm, host, H * sizeof(float), cudaMemcpyHostToDevice, ctx->st));
+      break;
+    case LLMCU_T_Q_NORM:
+      CK(cudaMemcpyAsync(ctx->lw[layer].q_norm, host, hd * sizeof(float), cudaMemcpyHostToDevice, ctx->st));
+      break;
+    case LLMCU_T_K_NORM:
+      CK(cudaMemcpyAsync(ctx->lw[layer].k_norm, host, hd * sizeof(float), cudaMemcpyHostToDevice, ctx->st));
+      break;
+    case LLMCU_T_WQ:
+    case LLMCU_T_WK:
+    case LLMCU_T_WV: {
+      LayerW& w = ctx->lw[layer];
+      const int rows = id == LLMCU_T_WQ ? Q : KV;
+      const int off = id == LLMCU_T_WQ ? 0 : (id == LLMCU_T_WK ? Q : Q + KV);
+      CKS(upload_stage(ctx, host, static_cast<size_t>(rows) * H));
+      if (!int8) {
+        CK(convert_weight(ctx->stage, rows, H, w.wqkv, H, off, 0, w.wqkvT, QKV, off, ctx->st));
+      } else {
+        CKS(place_linear(ctx, rows, H, nullptr, nullptr, 0, off, 0, w.q_qkv, w.qT_qkv, w.s_qkv));
+        CKS(finish_int8_transposes(ctx, layer));
+      }
+      break;
+    }
+    case LLMCU_T_WO: {
+      LayerW& w = ctx->lw[layer];
+      CKS(upload_stage(ctx, host, static_cast<size_t>(H) * Q));
+      if (!int8) {
+        CK(convert_weight(ctx->stage, H, Q, w.wo, Q, 0, 0, w.woT, H, 0, ctx->st));
+      } else {
+        CKS(place_linear(ctx, H, Q, nullptr, nullptr, 0, 0, 0, w.q_o, w.qT_o, w.s_o));
+        CKS(finish_int8_transposes(ctx, layer));
+      }
+      break;
+    }
+    case LLMCU_T_W_GATE:
+    case LLMCU_T_W_UP: {
+      LayerW& w = ctx->lw[layer];
+      const int il = id == LLMCU_T_W_GATE ? 1 : 2;
+      CKS(upload_stage(ctx, host, static_cast<size_t>(I) * H));
+      if (!int8) {
+        CK(convert_weight(ctx->stage, I, H, w.wgu, H, 0, il, w.wguT, 2 * I, 0, ctx->st));
+      } else {
+        CKS(place_linear(ctx, I, H, nullptr, nullptr, 0, 0, il, w.q_gu, w.qT_gu, w.s_gu));
+        CKS(finish_int8_transposes(ctx, layer));
+      }
+      break;
+    }
+    case LLMCU_T_W_DOWN: {
+      LayerW& w = ctx->lw[layer];
+      CKS(upload_stage(ctx, host, static_cast<size_t>(H) * I));
+      if (!int8) {
+        CK(convert_weight(ctx->stage, H, I, w.wd, I, 0, 0, w.wdT, H, 0, ctx->st));
+      } else {
+        CKS(place_linear(ctx, H, I, nullptr, nullptr, 0, 0, 0, w.q_d, w.qT_d, w.s_d));
+        CKS(finish_int8_transposes(ctx, layer));
+      }
+      break;
+    }
+    default:
+      return fail(ctx, LLMCU_ERR_INVALID_ARG, "unknown tensor id %d", id);
+  }
+  CK(cudaStreamSynchronize(ctx->st));
+  return LLMCU_OK;
+}
+
+llmcu_status llmcu_load_base_fp32_files(llmcu_ctx* ctx, const char* dir) {
+  if (!ctx || !dir) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null argument");
+  const int H = ctx->H, Q = ctx->Q, KV = ctx->KV, I = ctx->I, V = ctx->V, hd = ctx->hd;
+  std::vector<float> buf;
+  auto load = [&](const std::string& name, size_t n) -> llmcu_status {
+    const std::string path = std::string(dir) + "/" + name;
+    FILE* f = fopen(path.c_str(), "rb");
+    if (!f) return fail(ctx, LLMCU_ERR_IO, "cannot open %s", path.c_str());
+    buf.resize(n);
+    const size_t got = fread(buf.data(), sizeof(float), n, f);
+    fclose(f);
+    if (got != n) return fail(ctx, LLMCU_ERR_IO, "short read %s (%zu of %zu floats)", path.c_str(), got, n);
+    return LLMCU_OK;
+  };
+  CKS(load("model.embed_tokens.weight.bin", static_cast<size_t>(V) * H));
+  CKS(llmcu_set_base_tensor(ctx, LLMCU_T_EMBED, 0, buf.data()));
+  CKS(load("model.norm.weight.bin", H));
+  CKS(llmcu_set_base_tensor(ctx, LLMCU_T_FINAL_NORM, 0, buf.data()));
+  struct F { const char* n; int id; size_t sz; };
+  for (int l = 0; l < ctx->L; ++l) {
+    const F fs[] = {
+        {"input_layernorm.weight", LLMCU_T_ATTN_NORM, static_cast<size_t>(H)},
+        {"post_attention_layernorm.weight", LLMCU_T_FFN_NORM, static_cast<size_t>(H)},
+        {"self_attn.q_proj.weight", LLMCU_T_WQ, static_cast<size_t>(Q) * H},
+        {"self_attn.k_proj.weight", LLMCU_T_WK, static_cast<size_t>(KV) * H},
+        {"self_attn.v_proj.weight", LLMCU_T_WV, static_cast<size_t>(KV) * H},
+        {"self_attn.o_proj.weight", LLMCU_T_WO, static_cast<size_t>(H) * Q},
+        {"self_attn.q_norm.weight", LLMCU_T_Q_NORM, static_cast<size_t>(hd)},
+        {"self_attn.k_norm.weight", LLMCU_T_K_NORM, static_cast<size_t>(hd)},
+        {"mlp.gate_proj.weight", LLMCU_T_W_GATE, static_cast<size_t>(I) * H},
+        {"mlp.up_proj.weight", LLMCU_T_W_UP, static_cast<size_t>(I) * H},
+        {"mlp.down_proj.weight", LLMCU_T_W_DOWN, static_cast<size_t>(H) * I},
+    };
+    for (const F& f : fs) {
+      char name[256];
+      snprintf(name, sizeof(name), "model.layers.%d.%s.bin", l, f.n);
+      CKS(load(name, f.sz));
+      CKS(llmcu_set_base_tensor(ctx, f.id, l, buf.data()));
+    }
+  }
+  return LLMCU_OK;
+}
+
+llmcu_status llmcu_init_base_synthetic(llmcu_ctx* ctx, uint64_t seed, float stddev) {
+  if (!ctx) return LLMCU_ERR_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  const int64_t H = ctx->H, Q = ctx->Q, QKV = ctx->QKV, I = ctx->I, V = ctx->V;
+  cudaStream_t st = ctx->st;
+  uint64_t k = seed * 1000003ull + 17;
+  auto lin = [&](int rows, int cols, __half* w, __half* wT, int8_t* q, int8_t* qT, float* s) -> llmcu_status {
+    const int64_t n = static_cast<int64_t>(rows) * cols;
+    if (ctx->rc.base_dtype != LLMCU_BASE_INT8) {
+      CK(fill_normal_f16(w, n, k++, stddev, st));
+      CK(transpose_f16(w, rows, cols, cols, wT, rows, st));
+    } else {
+      CK(fill_normal_f32(ctx->stage, n, k++, stddev, st));
+      CK(quantize_rows_int8(ctx->stage, rows, cols, q, s, st));
+      dim3 grid((cols + 31) / 32, (rows + 31) / 32);
+      transpose_i8_kernel<<<grid, 256, 0, st>>>(q, rows, cols, qT);
+      CK(cudaGetLastError());
+    }
+    return LLMCU_OK;
+  };
+  if (ctx->rc.base_dtype != LLMCU_BASE_INT8) {
+    CK(fill_normal_f16(ctx->E, V * H, k++, stddev, st));
+    CK(transpose_f16(ctx->E, static_cast<int>(V), static_cast<int>(H), static_cast<int>(H), ctx->ET,
+                     static_cast<int>(V), st));
+  } else {
+    CK(fill_normal_f32(ctx->stage, V * H, k++, stddev, st));
+    CK(quantize_rows_int8(ctx->stage, static_cast<int>(V), static_cast<int>(H), ctx->qE, ctx->sE, st));
+    CK(dequant_rows_f16(ctx->qE, ctx->sE, static_cast<int>(V), static_cast<int>(H), ctx->E, st));
+    CK(transpose_f16(ctx->E, static_cast<int>(V), static_cast<int>(H), static_cast<int>(H), ctx->ET,
+                     static_cast<int>(V), st));
+  }
+  for (auto& w : ctx->lw) {
+    CKS(lin(static_cast<int>(QKV), static_cast<int>(H), w.wqkv, w.wqkvT, w.q_qkv, w.qT_qkv, w.s_qkv));
+    CKS(lin(static_cast<int>(H), static_cast<int>(Q), w.wo, w.woT, w.q_o, w.qT_o, w.s_o));
+    CKS(lin(static_cast<int>(2 * I), static_cast<int>(H), w.wgu, w.wguT, w.q_gu, w.qT_gu, w.s_gu));
+    CKS(lin(static_cast<int>(H), static_cast<int>(I), w.wd, w.wdT, w.q_d, w.qT_d, w.s_d));
+  }
+  CK(cudaStreamSynchronize(st));
+  return LLMCU_OK;
+}
+
+// ------------------------------------------------------------------- LoRA
+
+static llmcu_status check_proj(llmcu_ctx* ctx, int layer, int proj) {
+  if (layer < 0 || layer >= ctx->L || proj < 0 || proj > 3)
+    return fail(ctx, LLMCU_ERR_INVALID_ARG, "layer %d / proj %d out of range", layer, proj);
+  return LLMCU_OK;
+}
+
+llmcu_status llmcu_set_lora(llmcu_ctx* ctx, int layer, int proj, const float* A, const float* B) {
+  if (!ctx || !A || !B) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null argument");
+  CKS(check_proj(ctx, layer, proj));
+  CK(cudaSetDevice(ctx->device));
+  const LoraDims& d = ctx->ld;
+  float* base = ctx->lp + d.per_layer * layer;
+  const size_t nA = static_cast<size_t>(d.r) * d.d_in(proj), nB = static_cast<size_t>(d.d_out(proj)) * d.r;
+  CK(cudaMemcpyAsync(base + d.offA(proj), A, nA * sizeof(float), cudaMemcpyHostToDevice, ctx->st));
+  CK(cudaMemcpyAsync(base + d.offB(proj), B, nB * sizeof(float), cudaMemcpyHostToDevice, ctx->st));
+  CK(cudaStreamSynchronize(ctx->st));
+  return LLMCU_OK;
+}
+
+static llmcu_status get_pair(llmcu_ctx* ctx, const float* flat, int layer, int proj, float* A, float* B) {
+  if (!ctx || !A || !B) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null argument");
+  CKS(check_proj(ctx, layer, proj));
+  CK(cudaSetDevice(ctx->device));
+  const LoraDims& d = ctx->ld;
+  const float* base = flat + d.per_layer * layer;
+  const size_t nA = static_cast<size_t>(d.r) * d.d_in(proj), nB = static_cast<size_t>(d.d_out(proj)) * d.r;
+  CK(cudaStreamSynchronize(ctx->comm));
+  CK(cudaMemcpyAsync(A, base + d.offA(proj), nA * sizeof(float), cudaMemcpyDeviceToHost, ctx->st));
+  CK(cudaMemcpyAsync(B, base + d.offB(proj), nB * sizeof(float), cudaMemcpyDeviceToHost, ctx->st));
+  CK(cudaStreamSynchronize(ctx->st));
+  return LLMCU_OK;
+}
+
+llmcu_status llmcu_get_lora(llmcu_ctx* ctx, int layer, int proj, float* A, float* B) {
+  return get_pair(ctx, ctx ? ctx->lp : nullptr, layer, proj, A, B);
+}
+
+llmcu_status llmcu_get_lora_grads(llmcu_ctx* ctx, int layer, int proj, float* dA, float* dB) {
+  return get_pair(ctx, ctx ? ctx->lg : nullptr, layer, proj, dA, dB);
+}
+
+llmcu_status llmcu_init_lora_synthetic(llmcu_ctx* ctx, uint64_t seed, float b_std) {
+  if (!ctx) return LLMCU_ERR_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  const LoraDims& d = ctx->ld;
+  uint64_t k = seed * 7919ull + 3;
+  for (int l = 0; l < ctx->L; ++l) {
+    float* base = ctx->lp + d.per_layer * l;
+    for (int p = 0; p < 4; ++p) {
+      const float bound = 1.0f / sqrtf(static_cast<float>(d.d_in(p)));
+      CK(fill_uniform_f32(base + d.offA(p), static_cast<int64_t>(d.r) * d.d_in(p), k++, -bound, bound, ctx->st));
+      CK(fill_normal_f32(base + d.offB(p), static_cast<int64_t>(d.d_out(p)) * d.r, k++, b_std, ctx->st));
+    }
+  }
+  CK(cudaStreamSynchronize(ctx->st));
+  return LLMCU_OK;
+}
+
+llmcu_status llmcu_reset_optimizer(llmcu_ctx* ctx) {
+  if (!ctx) return LLMCU_ERR_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  CK(cudaMemsetAsync(ctx->lm, 0, ctx->n_lora * sizeof(float), ctx->st));
+  CK(cudaMemsetAsync(ctx->lv, 0, ctx->n_lora * sizeof(float), ctx->st));
+  CK(cudaStreamSynchronize(ctx->st));
+  return LLMCU_OK;
+}
+
+// ------------------------------------------------------------------ steps
+
+llmcu_status llmcu_forward_backward(llmcu_ctx* ctx, const int32_t* tokens, const int32_t* targets, int batch, int seq,
+                                    float* loss_out) {
+  if (!ctx) return LLMCU_ERR_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  CKS(validate_step(ctx, batch, seq));
+  CKS(upload_tokens(ctx, tokens, targets, batch * seq));
+  CKS(run_forward_backward(ctx, batch, seq));
+  return read_loss(ctx, loss_out);
+}
+
+llmcu_status llmcu_adamw(llmcu_ctx* ctx, const llmcu_adamw_cfg* opt, int step) {
+  if (!ctx) return LLMCU_ERR_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  CKS(do_adamw(ctx, opt, step));
+  CK(cudaStreamSynchronize(ctx->st));
+  return LLMCU_OK;
+}
+
+llmcu_status llmcu_train_step(llmcu_ctx* ctx, const int32_t* tokens, const int32_t* targets, int batch, int seq,
+                              const llmcu_adamw_cfg* opt, int step, float* loss_out) {
+  if (!ctx) return LLMCU_ERR_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  CKS(validate_step(ctx, batch, seq));
+  if (!opt || step < 1) return fail(ctx, LLMCU_ERR_INVALID_ARG, "adamw: null config or step < 1");
+  CKS(upload_tokens(ctx, tokens, targets, batch * seq));
+  CKS(run_forward_backward(ctx, batch, seq));
+  CKS(do_adamw(ctx, opt, step));
+  return read_loss(ctx, loss_out);
+}
+
+llmcu_status llmcu_train_step_device(llmcu_ctx* ctx, const int32_t* d_tokens, const int32_t* d_targets, int batch,
+                                     int seq, const llmcu_adamw_cfg* opt, int step) {
+  if (!ctx || !d_tokens || !d_targets) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null argument");
+  CK(cudaSetDevice(ctx->device));
+  CKS(validate_step(ctx, batch, seq));
+  if (!opt || step < 1) return fail(ctx, LLMCU_ERR_INVALID_ARG, "adamw: null config or step < 1");
+  const int M = batch * seq;
+  CK(cudaMemcpyAsync(ctx->tok, d_tokens, sizeof(int) * M, cudaMemcpyDeviceToDevice, ctx->st));
+  CK(cudaMemcpyAsync(ctx->tgt, d_targets, sizeof(int) * M, cudaMemcpyDeviceToDevice, ctx->st));
+  CKS(run_forward_backward(ctx, batch, seq));
+  CKS(do_adamw(ctx, opt, step));
+  return LLMCU_OK;
+}
+
+llmcu_status llmcu_read_loss(llmcu_ctx* ctx, float* loss_out) {
+  if (!ctx) return LLMCU_ERR_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  return read_loss(ctx, loss_out);
+}
+
+// ---------------------------------------------------------- checkpointing
+
+static const char* kProjNames[4] = {"wq", "wk", "wv", "wo"};
+
+llmcu_status llmcu_save_lora(llmcu_ctx* ctx, const char* dir, int step) {
+  if (!ctx || !dir) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null argument");
+  const LoraDims& d = ctx->ld;
+  std::vector<float> A, B;
+  for (int l = 0; l < ctx->L; ++l) {
+    for (int p = 0; p < 4; ++p) {
+      A.resize(static_cast<size_t>(d.r) * d.d_in(p));
+      B.resize(static_cast<size_t>(d.d_out(p)) * d.r);
+      CKS(llmcu_get_lora(ctx, l, p, A.data(), B.data()));
+      const std::vector<float>* parts[2] = {&A, &B};
+      const char* ab[2] = {"A", "B"};
+      for (int i = 0; i < 2; ++i) {
+        char path[1024];
+        snprintf(path, sizeof(path), "%s/lora_step%d_layer%d_%s_%s.bin", dir, step, l, kProjNames[p], ab[i]);
+        FILE* f = fopen(path, "wb");
+        if (!f) return fail(ctx, LLMCU_ERR_IO, "cannot write %s", path);
+        const size_t n = fwrite(parts[i]->data(), sizeof(float), parts[i]->size(), f);
+        fclose(f);
+        if (n != parts[i]->size()) return fail(ctx, LLMCU_ERR_IO, "short write %s", path);
+      }
+    }
+  }
+  return LLMCU_OK;
+}
+
+llmcu_status llmcu_load_lora(llmcu_ctx* ctx, const char* dir, int step) {
+  if (!ctx || !dir) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null argument");
+  const LoraDims& d = ctx->ld;
+  std::vector<float> A, B;
+  for (int l = 0; l < ctx->L; ++l) {
+    for (int p = 0; p < 4; ++p) {
+      A.resize(static_cast<size_t>(d.r) * d.d_in(p));
+      B.resize(static_cast<size_t>(d.d_out(p)) * d.r);
+      std::vector<float>* parts[2] = {&A, &B};
+      const char* ab[2] = {"A", "B"};
+      for (int i = 0; i < 2; ++i) {
+        char path[1024];
+        snprintf(path, sizeof(path), "%s/lora_step%d_layer%d_%s_%s.bin", dir, step, l, kProjNames[p], ab[i]);
+        FILE* f = fopen(path, "rb");
+        if (!f) return fail(ctx, LLMCU_ERR_IO, "cannot open %s", path);
+        const size_t n = fread(parts[i]->data(), sizeof(float), parts[i]->size(), f);
+        fclose(f);
+        if (n != parts[i]->size()) return fail(ctx, LLMCU_ERR_IO, "short read %s", path);
+      }
+      CKS(llmcu_set_lora(ctx, l, p, A.data(), B.data()));
+    }
+  }
+  return LLMCU_OK;
+}
+
+// ------------------------------------------------------------------- INT8
+
+llmcu_status llmcu_quantize_int8_rows(const float* w, int rows, int cols, int8_t* q, float* scale, void* stream) {
+  if (!w || !q || !scale || rows <= 0 || cols <= 0) return LLMCU_ERR_INVALID_ARG;
+  if (quantize_rows_int8(w, rows, cols, q, scale, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return LLMCU_ERR_CUDA;
+  return LLMCU_OK;
+}
+
+// ---------------------------------------------------------- data parallel
+
+llmcu_status llmcu_dp_get_unique_id(void* id128) {
+  if (!id128) return LLMCU_ERR_INVALID_ARG;
+  static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id size");
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) return LLMCU_ERR_NCCL;
+  memcpy(id128, &id, sizeof(id));
+  return LLMCU_OK;
+}
+
+llmcu_status llmcu_dp_set_timeout_ms(llmcu_ctx* ctx, int ms) {
+  if (!ctx || ms <= 0) return LLMCU_ERR_INVALID_ARG;
+  ctx->timeout_ms = ms;
+  return LLMCU_OK;
+}
+
+llmcu_status llmcu_dp_init(llmcu_ctx* ctx, const void* id128, int rank, int world) {
+  if (!ctx || !id128 || world < 1 || rank < 0 || rank >= world) return fail(ctx, LLMCU_ERR_INVALID_ARG, "bad dp args");
+  CK(cudaSetDevice(ctx->device));
+  if (ctx->nccl) return fail(ctx, LLMCU_ERR_INVALID_ARG, "data parallel group already initialised");
+  if (world == 1) return LLMCU_OK;
+  ncclUniqueId id;
+  memcpy(&id, id128, sizeof(id));
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  ncclComm_t comm = nullptr;
+  ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &cfg);
+  ctx->nccl = comm;
+  llmcu_status s = nccl_wait(ctx, r, "ncclCommInitRankConfig");
+  if (s != LLMCU_OK) {
+    if (ctx->nccl) {
+      ncclCommAbort(ctx->nccl);
+      ctx->nccl = nullptr;
+    }
+    return s;
+  }
+  ctx->rank = rank;
+  ctx->world = world;
+  return LLMCU_OK;
+}
+
+// ------------------------------------------------------------ kernel test
+
+llmcu_status llmcu_gemm_nt_f16(const void* A, const void* B, float* C, int M, int N, int K, int lda, int ldb, int ldc,
+                               void* stream) {
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0) return LLMCU_ERR_INVALID_ARG;
+  static int* d_err = nullptr;
+  if (!d_err) {
+    if (cudaMalloc(&d_err, sizeof(int)) != cudaSuccess) return LLMCU_ERR_CUDA;
+    cudaMemset(d_err, 0, sizeof(int));
+  }
+  EpiArgs ea;
+  ea.out = C;
+  ea.ld_out = ldc;
+  cudaError_t e = gemm(op(static_cast<const __half*>(A), M, K, lda), op(static_cast<const __half*>(B), N, K, ldb), kNone,
+                       kNone, M, N, Epi::kStoreF32, ea, d_err, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LLMCU_OK : LLMCU_ERR_CUDA;
+}
+
+llmcu_status llmcu_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int batch, int seq,
+                                 int n_heads, int n_kv_heads, int head_dim, int ldq, int ldk, int ldv, void* stream) {
+  if (!q || !k || !v || !o || !lse || batch <= 0 || seq <= 0 || n_heads <= 0 || n_kv_heads <= 0 ||
+      n_heads % n_kv_heads)
+    return LLMCU_ERR_INVALID_ARG;
+  cudaError_t e = attention_forward(static_cast<const __half*>(q), static_cast<const __half*>(k),
+                                    static_cast<const __half*>(v), static_cast<__half*>(o), lse, batch, seq, n_heads,
+                                    n_kv_heads, head_dim, ldq, ldk, ldv, n_heads * head_dim,
+                                    static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LLMCU_OK : (e == cudaErrorInvalidValue ? LLMCU_ERR_UNSUPPORTED : LLMCU_ERR_CUDA);
+}
+
+llmcu_status llmcu_attention_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                                 const float* lse, float* scratch_delta, float* dq, float* dk, void* dv, int batch,
+                                 int seq, int n_heads, int n_kv_heads, int head_dim, int ldq, int ldk, int ldv,
+                                 int lddv, void* stream) {
+  if (!q || !k || !v || !o || !dout || !lse || !scratch_delta || !dq || !dk || !dv || batch <= 0 || seq <= 0 ||
+      n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads)
+    return LLMCU_ERR_INVALID_ARG;
+  const int ldo = n_heads * head_dim;
+  cudaError_t e = attention_backward(
+      static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v),
+      static_cast<const __half*>(o), static_cast<const __half*>(dout), lse, scratch_delta, dq, dk,
+      static_cast<__half*>(dv), batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk, ldv, ldo, ldo,
+      n_kv_heads * head_dim, lddv, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LLMCU_OK : (e == cudaErrorInvalidValue ? LLMCU_ERR_UNSUPPORTED : LLMCU_ERR_CUDA);
+}
+
+}  // extern "C"

@@ -1,0 +1,81 @@
+// lora.cuh -- flat adapter layout and the LoRA kernel interfaces.
+#pragma once
+
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace llmcu {
+
+// Offsets (in floats) of each adapter inside one layer of the flat fp32
+// buffer, and of each derived fp16 operand inside one layer of the derived
+// buffer.  A [r, d_in], B [d_out, r] row-major.
+struct LoraDims {
+  int r, H, Q, KV;
+  float scale;  // alpha / r
+  int64_t oAq, oBq, oAk, oBk, oAv, oBv, oAo, oBo, per_layer;
+  int64_t d_acat, d_acatT, d_bblk, d_bblkT, d_ao, d_aoT, d_bo, d_boT, derived_per_layer;
+
+  static LoraDims make(int r, int H, int Q, int KV, float scale) {
+    LoraDims d{};
+    d.r = r; d.H = H; d.Q = Q; d.KV = KV; d.scale = scale;
+    int64_t o = 0;
+    d.oAq = o; o += static_cast<int64_t>(r) * H;
+    d.oBq = o; o += static_cast<int64_t>(Q) * r;
+    d.oAk = o; o += static_cast<int64_t>(r) * H;
+    d.oBk = o; o += static_cast<int64_t>(KV) * r;
+    d.oAv = o; o += static_cast<int64_t>(r) * H;
+    d.oBv = o; o += static_cast<int64_t>(KV) * r;
+    d.oAo = o; o += static_cast<int64_t>(r) * Q;
+    d.oBo = o; o += static_cast<int64_t>(H) * r;
+    d.per_layer = o;
+    const int64_t QKV = Q + 2 * KV;
+    int64_t e = 0;
+    auto al = [](int64_t x) { return (x + 127) / 128 * 128; };  // keep every operand 256-byte aligned
+    d.d_acat = e; e = al(e + 64LL * H);
+    d.d_acatT = e; e = al(e + 64LL * H);
+    d.d_bblk = e; e = al(e + 64LL * QKV);
+    d.d_bblkT = e; e = al(e + 64LL * QKV);
+    d.d_ao = e; e = al(e + 64LL * Q);
+    d.d_aoT = e; e = al(e + 64LL * Q);
+    d.d_bo = e; e = al(e + 64LL * H);
+    d.d_boT = e; e = al(e + 64LL * H);
+    d.derived_per_layer = e;
+    return d;
+  }
+  // adapter (proj 0..3 = q, k, v, o) offsets and dims
+  int64_t offA(int proj) const { return proj == 0 ? oAq : proj == 1 ? oAk : proj == 2 ? oAv : oAo; }
+  int64_t offB(int proj) const { return proj == 0 ? oBq : proj == 1 ? oBk : proj == 2 ? oBv : oBo; }
+  int d_in(int proj) const { return proj == 3 ? Q : H; }
+  int d_out(int proj) const { return proj == 0 ? Q : proj == 3 ? H : KV; }
+};
+
+constexpr int kLoraMaxProbs = 8;
+// first column of the k and v rank segments in the 64-wide LoRA operands
+constexpr int kSegK = 16;
+constexpr int kSegV = 32;
+constexpr int kLoraMaxSplits = 16;
+
+// C[a, b] = scale * sum_m U[m, a] * W[m, b]  for a < A, b < Bn (<= 16);
+// stored at out[a * sa + b * sb].
+struct LoraGradProb {
+  const __half* U;
+  int ldu;
+  const __half* W;
+  int ldw;
+  float* out;
+  int sa, sb;
+  int A, Bn;
+  float scale;
+};
+struct LoraGradBatch {
+  LoraGradProb p[kLoraMaxProbs];
+  int n;
+  int a_max;  // multiple of 64, >= every A
+};
+
+cudaError_t lora_prep(const float* flat, const LoraDims& d, int n_layers, __half* derived, cudaStream_t st);
+cudaError_t lora_grad(const LoraGradBatch& batch, int M, float* part, cudaStream_t st);
+int lora_grad_splits(int M, int a_max, int n);
+
+}  // namespace llmcu

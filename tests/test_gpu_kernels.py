@@ -1,0 +1,101 @@
+"""Kernel-level parity on the GPU: each CUDA kernel, called through the C ABI
+(libllmcu.so), against a plain PyTorch fp32 reference of the same op on the
+same fp16 inputs.
+
+Tolerances: GEMM outputs to 1e-3 relative L2 (fp32 accumulation of exact fp16
+products; only summation order differs).  Attention to 1e-2 relative L2
+(probabilities are rounded to fp16 before the P.V and dS.K products)."""
+import math
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_l2(a, b):
+    a = a.double().flatten()
+    b = b.double().flatten()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 2048), (32, 64, 256), (200, 300, 200), (128, 151936 // 8, 2048),
+                                   (1000, 2048, 6144)])
+def test_gemm_nt_matches_torch(llmcu, cuda_device, M, N, K):
+    g = torch.Generator(device="cpu").manual_seed(M * 7 + N)
+    A = torch.randn(M, K, generator=g).half().to(cuda_device)
+    B = torch.randn(N, K, generator=g).half().to(cuda_device)
+    C = torch.full((M, N), float("nan"), device=cuda_device, dtype=torch.float32)
+    llmcu.gemm_nt_f16(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, K, K, N,
+                      torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ref = A.float() @ B.float().t()
+    assert torch.isfinite(C).all()
+    assert rel_l2(C, ref) < 1e-3
+
+
+def _attn_ref(q, k, v, B, S, nh, nkv, hd):
+    qh = q.view(B, S, nh, hd).transpose(1, 2)
+    kh = k.view(B, S, nkv, hd).repeat_interleave(nh // nkv, dim=2).transpose(1, 2)
+    vh = v.view(B, S, nkv, hd).repeat_interleave(nh // nkv, dim=2).transpose(1, 2)
+    s = (qh @ kh.transpose(-1, -2)) / math.sqrt(hd)
+    mask = torch.ones(S, S, dtype=torch.bool, device=q.device).triu(1)
+    s = s.masked_fill(mask, float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    o = torch.softmax(s, dim=-1) @ vh
+    return o.transpose(1, 2).reshape(B * S, nh * hd), lse
+
+
+@pytest.mark.parametrize("B,S,nh,nkv,hd", [(2, 128, 4, 2, 64), (1, 32, 4, 2, 64), (2, 512, 16, 8, 128),
+                                           (1, 200, 16, 8, 128), (1, 1000, 4, 2, 128)])
+def test_attention_fwd_bwd_matches_torch(llmcu, cuda_device, B, S, nh, nkv, hd):
+    g = torch.Generator(device="cpu").manual_seed(S + nh)
+    M = B * S
+    q = torch.randn(M, nh * hd, generator=g).half().to(cuda_device)
+    k = torch.randn(M, nkv * hd, generator=g).half().to(cuda_device)
+    v = torch.randn(M, nkv * hd, generator=g).half().to(cuda_device)
+    do = torch.randn(M, nh * hd, generator=g).half().to(cuda_device)
+    o = torch.empty(M, nh * hd, device=cuda_device, dtype=torch.float16)
+    lse = torch.empty(B, nh, S, device=cuda_device, dtype=torch.float32)
+    st = torch.cuda.current_stream().cuda_stream
+    llmcu.attention_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), B, S, nh, nkv,
+                        hd, nh * hd, nkv * hd, nkv * hd, st)
+    torch.cuda.synchronize()
+    qf, kf, vf = (t.float().requires_grad_(True) for t in (q, k, v))
+    o_ref, lse_ref = _attn_ref(qf, kf, vf, B, S, nh, nkv, hd)
+    assert rel_l2(o.float(), o_ref) < 1e-2
+    assert torch.allclose(lse, lse_ref, atol=2e-3, rtol=1e-4)
+
+    o_ref.backward(do.float())
+    delta = torch.empty(B, nh, S, device=cuda_device, dtype=torch.float32)
+    dq = torch.empty(M, nh * hd, device=cuda_device, dtype=torch.float32)
+    dk = torch.empty(M, nkv * hd, device=cuda_device, dtype=torch.float32)
+    dv = torch.empty(M, nkv * hd, device=cuda_device, dtype=torch.float16)
+    llmcu.attention_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(),
+                        delta.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, S, nh, nkv, hd,
+                        nh * hd, nkv * hd, nkv * hd, nkv * hd, st)
+    torch.cuda.synchronize()
+    assert rel_l2(dq, qf.grad) < 1e-2
+    assert rel_l2(dk, kf.grad) < 1e-2
+    assert rel_l2(dv.float(), vf.grad) < 1e-2
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 2048), (7, 13), (2048, 6144), (3, 1)])
+def test_int8_quantiser_bit_exact(llmcu, cuda_device, rows, cols):
+    from oracle.quant import quantize_rows
+    rng = np.random.Generator(np.random.PCG64(rows * 1000 + cols))
+    w = (rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02)).astype(np.float16).astype(np.float32)
+    if rows >= 3:
+        w[1] = 0.0                                     # all-zero row -> scale 0, q 0
+        w[2, 0] = 0.5                                  # ties in w*inv around .5 are exercised by the draw
+    q_ref, s_ref = quantize_rows(w)
+    wd = torch.from_numpy(w).to(cuda_device)
+    qd = torch.empty(rows, cols, dtype=torch.int8, device=cuda_device)
+    sd = torch.empty(rows, dtype=torch.float32, device=cuda_device)
+    llmcu.quantize_int8_rows(wd.data_ptr(), rows, cols, qd.data_ptr(), sd.data_ptr(),
+                             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(qd.cpu().numpy(), q_ref)
+    assert np.array_equal(sd.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
