@@ -211,6 +211,19 @@ llmcu_status llmcu_dp_init(llmcu_ctx* ctx, const void* id128, int rank, int worl
  * LLMCU_ERR_TIMEOUT is returned (default 60000 ms). */
 llmcu_status llmcu_dp_set_timeout_ms(llmcu_ctx* ctx, int ms);
 
+/* ------------------------------------------------------------- profiling */
+
+/* Per-kernel-class timing.  While enabled, every step records CUDA events on
+ * the compute stream around each kernel launch (classes: gemm_tc,
+ * attention_fwd, attention_bwd, norm_rope, lora_grad, lora_prep, ce_reduce,
+ * embed, adamw, int8_dequant).  The reference has no counterpart (its
+ * per-component timers exist only in the inference bench,
+ * src/kernels/forward.cu:207-335). */
+llmcu_status llmcu_profile_enable(llmcu_ctx* ctx, int on);
+/* Writes {"class": {"ms": total, "launches": n}, ...} accumulated since the
+ * last reset into buf (NUL-terminated); reset != 0 clears the totals. */
+llmcu_status llmcu_profile_read(llmcu_ctx* ctx, char* buf, size_t len, int reset);
+
 /* ------------------------------------------------------------ kernel test
  * Single-kernel entry points on DEVICE pointers, used by the kernel-level
  * parity tests.  `stream` is a cudaStream_t; results are asynchronous. */

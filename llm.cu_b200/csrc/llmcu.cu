@@ -106,6 +106,14 @@ struct llmcu_ctx {
   size_t stage_elems = 0;
   int last_n_valid = 0;
 
+  // per-kernel-class timing (llmcu_profile_enable)
+  bool prof_on = false;
+  std::vector<cudaEvent_t> prof_ev;
+  std::vector<int> prof_cls;  // class of each recorded (begin, end) event pair
+  int prof_n = 0;             // events used
+  double prof_ms[16] = {0};
+  int64_t prof_cnt[16] = {0};
+
   // data parallel
   ncclComm_t nccl = nullptr;
   int rank = 0, world = 1;
@@ -134,10 +142,31 @@ llmcu_status fail(llmcu_ctx* c, llmcu_status s, const char* fmt, ...) {
                   __LINE__);                                                                       \
   } while (0)
 
+enum ProfClass : int {
+  P_GEMM = 0, P_ATTN_FWD, P_ATTN_BWD, P_NORM, P_LORA_GRAD, P_LORA_PREP, P_CE, P_EMBED, P_ADAMW, P_DEQUANT, P_COUNT
+};
+const char* kProfNames[P_COUNT] = {"gemm_tc", "attention_fwd", "attention_bwd", "norm_rope", "lora_grad",
+                                   "lora_prep", "ce_reduce", "embed", "adamw", "int8_dequant"};
+const int kProfLaunches[P_COUNT] = {1, 1, 3, 1, 2, 1, 2, 1, 1, 1};  // kernels per call
+
+void prof_mark(llmcu_ctx* c, int cls) {
+  if (!c->prof_on || c->prof_n + 1 > static_cast<int>(c->prof_ev.size())) return;
+  cudaEventRecord(c->prof_ev[c->prof_n], c->st);
+  if ((c->prof_n & 1) == 0) c->prof_cls.push_back(cls);
+  ++c->prof_n;
+}
+
 #define CKS(expr)                                  \
   do {                                             \
     llmcu_status s_ = (expr);                      \
     if (s_ != LLMCU_OK) return s_;                 \
+  } while (0)
+
+#define TIMED(cls, expr)        \
+  do {                          \
+    prof_mark(ctx, cls);        \
+    CK(expr);                   \
+    prof_mark(ctx, cls);        \
   } while (0)
 
 Operand op(const __half* p, int rows, int k, int ld) { return Operand{p, rows, k, ld}; }
@@ -370,14 +399,18 @@ int grid_n(int64_t n) {
 const __half* fwd_weight(llmcu_ctx* c, const __half* w16, const int8_t* q, const float* s, int rows, int cols,
                          cudaError_t* e) {
   if (c->rc.base_dtype != LLMCU_BASE_INT8) return w16;
+  prof_mark(c, P_DEQUANT);
   *e = dequant_rows_f16(q, s, rows, cols, c->dq_w, c->st);
+  prof_mark(c, P_DEQUANT);
   return c->dq_w;
 }
 const __half* bwd_weight(llmcu_ctx* c, const __half* wT16, const int8_t* qT, const float* s, int rows_t, int cols_t,
                          cudaError_t* e) {
   if (c->rc.base_dtype != LLMCU_BASE_INT8) return wT16;
+  prof_mark(c, P_DEQUANT);
   dequant_cols_kernel<<<grid_n(static_cast<int64_t>(rows_t) * cols_t), 256, 0, c->st>>>(qT, s, rows_t, cols_t,
                                                                                         c->dq_wT);
+  prof_mark(c, P_DEQUANT);
   *e = cudaGetLastError();
   return c->dq_wT;
 }
@@ -397,10 +430,10 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   const float unscale = static_cast<float>(1.0 / (kGradScale * n_valid_total));
   cudaError_t e = cudaSuccess;
 
-  CK(lora_prep(ctx->lp, d, ctx->L, ctx->lderived, st));
-  CK(ce_valid_rows(ctx->valid, ctx->tgt, B, S, ctx->rc.loss_all_positions, V, err, st));
+  TIMED(P_LORA_PREP, lora_prep(ctx->lp, d, ctx->L, ctx->lderived, st));
+  TIMED(P_CE, ce_valid_rows(ctx->valid, ctx->tgt, B, S, ctx->rc.loss_all_positions, V, err, st));
   const __half* E = ctx->E;
-  CK(embed_forward(ctx->tok, E, ctx->resid[0], M, H, V, err, st));
+  TIMED(P_EMBED, embed_forward(ctx->tok, E, ctx->resid[0], M, H, V, err, st));
 
   // ------------------------------------------------------------ forward
   for (int l = 0; l < ctx->L; ++l) {
@@ -408,18 +441,18 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     LayerA& a = ctx->la[l];
     const __half* D = ctx->lderived + d.derived_per_layer * l;
     const float* x = ctx->resid[l];
-    CK(rmsnorm_forward(x, w.attn_norm, a.xn, M, H, eps, st));
-    CK(gemm(op(a.xn, M, H, H), op(D + d.d_acat, 64, H, H), kNone, kNone, M, 64, Epi::kStoreF16,
+    TIMED(P_NORM, rmsnorm_forward(x, w.attn_norm, a.xn, M, H, eps, st));
+    TIMED(P_GEMM, gemm(op(a.xn, M, H, H), op(D + d.d_acat, 64, H, H), kNone, kNone, M, 64, Epi::kStoreF16,
             EpiArgs{a.hq, 64}, err, st));
     const __half* wqkv = fwd_weight(ctx, w.wqkv, w.q_qkv, w.s_qkv, QKV, H, &e);
     CK(e);
-    CK(gemm(op(a.xn, M, H, H), op(wqkv, QKV, H, H), op(a.hq, M, 64, 64), op(D + d.d_bblk, QKV, 64, 64), M, QKV,
+    TIMED(P_GEMM, gemm(op(a.xn, M, H, H), op(wqkv, QKV, H, H), op(a.hq, M, 64, 64), op(D + d.d_bblk, QKV, 64, 64), M, QKV,
             Epi::kStoreF16, EpiArgs{a.qkv, QKV}, err, st));
-    CK(qknorm_rope_forward(a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, a.qrope, a.krope, B, S,
+    TIMED(P_NORM, qknorm_rope_forward(a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, a.qrope, a.krope, B, S,
                            ctx->nh, ctx->nkv, ctx->hd, eps, st));
-    CK(attention_forward(a.qrope, a.krope, a.qkv + Q + KV, a.attn, a.lse, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV,
+    TIMED(P_ATTN_FWD, attention_forward(a.qrope, a.krope, a.qkv + Q + KV, a.attn, a.lse, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV,
                          QKV, Q, st));
-    CK(gemm(op(a.attn, M, Q, Q), op(D + d.d_ao, 64, Q, Q), kNone, kNone, M, 64, Epi::kStoreF16, EpiArgs{a.ho, 64},
+    TIMED(P_GEMM, gemm(op(a.attn, M, Q, Q), op(D + d.d_ao, 64, Q, Q), kNone, kNone, M, 64, Epi::kStoreF16, EpiArgs{a.ho, 64},
             err, st));
     const __half* wo = fwd_weight(ctx, w.wo, w.q_o, w.s_o, H, Q, &e);
     CK(e);
@@ -428,10 +461,10 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       ea.out = a.resid_mid;
       ea.ld_out = H;
       ea.resid = x;
-      CK(gemm(op(a.attn, M, Q, Q), op(wo, H, Q, Q), op(a.ho, M, 64, 64), op(D + d.d_bo, H, 64, 64), M, H,
+      TIMED(P_GEMM, gemm(op(a.attn, M, Q, Q), op(wo, H, Q, Q), op(a.ho, M, 64, 64), op(D + d.d_bo, H, 64, 64), M, H,
               Epi::kResidF32, ea, err, st));
     }
-    CK(rmsnorm_forward(a.resid_mid, w.ffn_norm, a.xn2, M, H, eps, st));
+    TIMED(P_NORM, rmsnorm_forward(a.resid_mid, w.ffn_norm, a.xn2, M, H, eps, st));
     const __half* wgu = fwd_weight(ctx, w.wgu, w.q_gu, w.s_gu, 2 * I, H, &e);
     CK(e);
     {
@@ -440,7 +473,7 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       ea.ld_gu = 2 * I;
       ea.act = a.act;
       ea.ld_act = I;
-      CK(gemm(op(a.xn2, M, H, H), op(wgu, 2 * I, H, H), kNone, kNone, M, 2 * I, Epi::kSwiGLU, ea, err, st, 256));
+      TIMED(P_GEMM, gemm(op(a.xn2, M, H, H), op(wgu, 2 * I, H, H), kNone, kNone, M, 2 * I, Epi::kSwiGLU, ea, err, st, 256));
     }
     const __half* wd = fwd_weight(ctx, w.wd, w.q_d, w.s_d, H, I, &e);
     CK(e);
@@ -449,22 +482,22 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       ea.out = ctx->resid[l + 1];
       ea.ld_out = H;
       ea.resid = a.resid_mid;
-      CK(gemm(op(a.act, M, I, I), op(wd, H, I, I), kNone, kNone, M, H, Epi::kResidF32, ea, err, st));
+      TIMED(P_GEMM, gemm(op(a.act, M, I, I), op(wd, H, I, I), kNone, kNone, M, H, Epi::kResidF32, ea, err, st));
     }
   }
 
   // ------------------------------------------------------- lm_head + CE
   float* xfinal = ctx->resid[ctx->L];
-  CK(rmsnorm_forward(xfinal, ctx->final_norm, ctx->xf, M, H, eps, st));
+  TIMED(P_NORM, rmsnorm_forward(xfinal, ctx->final_norm, ctx->xf, M, H, eps, st));
   {
     EpiArgs ea;
     ea.targets = ctx->tgt;
     ea.part_max = ctx->part_max;
     ea.part_sum = ctx->part_sum;
     ea.tgt_logit = ctx->tgt_logit;
-    CK(gemm(op(ctx->xf, M, H, H), op(E, V, H, H), kNone, kNone, M, V, Epi::kCEStats, ea, err, st, 256));
+    TIMED(P_GEMM, gemm(op(ctx->xf, M, H, H), op(E, V, H, H), kNone, kNone, M, V, Epi::kCEStats, ea, err, st, 256));
   }
-  CK(ce_reduce(ctx->part_max, ctx->part_sum, ctx->tgt_logit, ctx->valid, ctx->lse_ce, ctx->row_loss, M,
+  TIMED(P_CE, ce_reduce(ctx->part_max, ctx->part_sum, ctx->tgt_logit, ctx->valid, ctx->lse_ce, ctx->row_loss, M,
                ctx->ce_tiles, st));
   const int vc = std::min(V, kVocabChunk);
   for (int c0 = 0, ci = 0; c0 < V; c0 += vc, ++ci) {
@@ -477,15 +510,15 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     ea.ld_out = vc;
     ea.col_base = c0;
     ea.gscale = kGradScale;
-    CK(gemm(op(ctx->xf, M, H, H), op(E + static_cast<size_t>(c0) * H, n, H, H), kNone, kNone, M, n, Epi::kCEGrad, ea,
+    TIMED(P_GEMM, gemm(op(ctx->xf, M, H, H), op(E + static_cast<size_t>(c0) * H, n, H, H), kNone, kNone, M, n, Epi::kCEGrad, ea,
             err, st));
     EpiArgs eb;
     eb.out = ctx->d_xf;
     eb.ld_out = H;
     eb.accumulate = ci > 0;
-    CK(gemm(op(ctx->dl, M, n, vc), op(ctx->ET + c0, H, n, V), kNone, kNone, M, H, Epi::kStoreF32, eb, err, st));
+    TIMED(P_GEMM, gemm(op(ctx->dl, M, n, vc), op(ctx->ET + c0, H, n, V), kNone, kNone, M, H, Epi::kStoreF32, eb, err, st));
   }
-  CK(rmsnorm_backward(ctx->d_xf, xfinal, ctx->final_norm, ctx->dres, ctx->dres16, M, H, eps, 0, st));
+  TIMED(P_NORM, rmsnorm_backward(ctx->d_xf, xfinal, ctx->final_norm, ctx->dres, ctx->dres16, M, H, eps, 0, st));
 
   // ----------------------------------------------------------- backward
   for (int l = ctx->L - 1; l >= 0; --l) {
@@ -501,19 +534,19 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       ea.gu_in = a.gu;
       ea.gu = ctx->dgu;
       ea.ld_gu = 2 * I;
-      CK(gemm(op(ctx->dres16, M, H, H), op(wdT, I, H, H), kNone, kNone, M, I, Epi::kSwiGLUBwd, ea, err, st, 256));
+      TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op(wdT, I, H, H), kNone, kNone, M, I, Epi::kSwiGLUBwd, ea, err, st, 256));
     }
     const __half* wguT = bwd_weight(ctx, w.wguT, w.qT_gu, w.s_gu, H, 2 * I, &e);
     CK(e);
-    CK(gemm(op(ctx->dgu, M, 2 * I, 2 * I), op(wguT, H, 2 * I, 2 * I), kNone, kNone, M, H, Epi::kStoreF32,
+    TIMED(P_GEMM, gemm(op(ctx->dgu, M, 2 * I, 2 * I), op(wguT, H, 2 * I, 2 * I), kNone, kNone, M, H, Epi::kStoreF32,
             EpiArgs{ctx->dxn, H}, err, st));
-    CK(rmsnorm_backward(ctx->dxn, a.resid_mid, w.ffn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
+    TIMED(P_NORM, rmsnorm_backward(ctx->dxn, a.resid_mid, w.ffn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
     // O projection
-    CK(gemm(op(ctx->dres16, M, H, H), op(D + d.d_boT, 64, H, H), kNone, kNone, M, 64, Epi::kStoreF16,
+    TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op(D + d.d_boT, 64, H, H), kNone, kNone, M, 64, Epi::kStoreF16,
             EpiArgs{ctx->dho, 64}, err, st));
     const __half* woT = bwd_weight(ctx, w.woT, w.qT_o, w.s_o, Q, H, &e);
     CK(e);
-    CK(gemm(op(ctx->dres16, M, H, H), op(woT, Q, H, H), op(ctx->dho, M, 64, 64), op(D + d.d_aoT, Q, 64, 64), M, Q,
+    TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op(woT, Q, H, H), op(ctx->dho, M, 64, 64), op(D + d.d_aoT, Q, 64, 64), M, Q,
             Epi::kStoreF16, EpiArgs{ctx->dattn, Q}, err, st));
     {
       LoraGradBatch gb{};
@@ -523,19 +556,19 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       gb.p[0] = LoraGradProb{ctx->dres16, H, a.ho, 64, G + d.oBo, r, 1, H, r, d.scale * unscale};
       // dAo[j, q] = sum_m dho[m, j] attn[m, q]
       gb.p[1] = LoraGradProb{a.attn, Q, ctx->dho, 64, G + d.oAo, 1, Q, Q, r, unscale};
-      CK(lora_grad(gb, M, ctx->lpart, st));
+      TIMED(P_LORA_GRAD, lora_grad(gb, M, ctx->lpart, st));
     }
     // attention
-    CK(attention_backward(a.qrope, a.krope, a.qkv + Q + KV, a.attn, ctx->dattn, a.lse, ctx->delta, ctx->dq, ctx->dk,
+    TIMED(P_ATTN_BWD, attention_backward(a.qrope, a.krope, a.qkv + Q + KV, a.attn, ctx->dattn, a.lse, ctx->delta, ctx->dq, ctx->dk,
                           ctx->dqkv + Q + KV, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV, QKV, Q, Q, KV, QKV, st));
-    CK(qknorm_rope_backward(ctx->dq, ctx->dk, a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, ctx->dqkv,
+    TIMED(P_NORM, qknorm_rope_backward(ctx->dq, ctx->dk, a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, ctx->dqkv,
                             B, S, ctx->nh, ctx->nkv, ctx->hd, eps, st));
     // QKV projection
-    CK(gemm(op(ctx->dqkv, M, QKV, QKV), op(D + d.d_bblkT, 64, QKV, QKV), kNone, kNone, M, 64, Epi::kStoreF16,
+    TIMED(P_GEMM, gemm(op(ctx->dqkv, M, QKV, QKV), op(D + d.d_bblkT, 64, QKV, QKV), kNone, kNone, M, 64, Epi::kStoreF16,
             EpiArgs{ctx->dhq, 64}, err, st));
     const __half* wqkvT = bwd_weight(ctx, w.wqkvT, w.qT_qkv, w.s_qkv, H, QKV, &e);
     CK(e);
-    CK(gemm(op(ctx->dqkv, M, QKV, QKV), op(wqkvT, H, QKV, QKV), op(ctx->dhq, M, 64, 64), op(D + d.d_acatT, H, 64, 64),
+    TIMED(P_GEMM, gemm(op(ctx->dqkv, M, QKV, QKV), op(wqkvT, H, QKV, QKV), op(ctx->dhq, M, 64, 64), op(D + d.d_acatT, H, 64, 64),
             M, H, Epi::kStoreF32, EpiArgs{ctx->dxn, H}, err, st));
     {
       LoraGradBatch gb{};
@@ -548,9 +581,9 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       gb.p[3] = LoraGradProb{a.xn, H, ctx->dhq, 64, G + d.oAq, 1, H, H, r, unscale};
       gb.p[4] = LoraGradProb{a.xn, H, ctx->dhq + kSegK, 64, G + d.oAk, 1, H, H, r, unscale};
       gb.p[5] = LoraGradProb{a.xn, H, ctx->dhq + kSegV, 64, G + d.oAv, 1, H, H, r, unscale};
-      CK(lora_grad(gb, M, ctx->lpart, st));
+      TIMED(P_LORA_GRAD, lora_grad(gb, M, ctx->lpart, st));
     }
-    CK(rmsnorm_backward(ctx->dxn, ctx->resid[l], w.attn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
+    TIMED(P_NORM, rmsnorm_backward(ctx->dxn, ctx->resid[l], w.attn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
     if (ctx->nccl) {
       CK(cudaEventRecord(ctx->ev_layer[l], st));
       CK(cudaStreamWaitEvent(ctx->comm, ctx->ev_layer[l], 0));
@@ -584,7 +617,7 @@ llmcu_status do_adamw(llmcu_ctx* ctx, const llmcu_adamw_cfg* o, int step) {
   if (!o || step < 1) return fail(ctx, LLMCU_ERR_INVALID_ARG, "adamw: null config or step < 1");
   const float bc1 = 1.0f - powf(o->beta1, static_cast<float>(step));
   const float bc2 = 1.0f - powf(o->beta2, static_cast<float>(step));
-  CK(adamw_flat(ctx->lp, ctx->lg, ctx->lm, ctx->lv, ctx->n_lora, o->lr, o->beta1, o->beta2, o->eps, o->weight_decay,
+  TIMED(P_ADAMW, adamw_flat(ctx->lp, ctx->lg, ctx->lm, ctx->lv, ctx->n_lora, o->lr, o->beta1, o->beta2, o->eps, o->weight_decay,
                 bc1, bc2, 1.0f, ctx->st));
   return LLMCU_OK;
 }
@@ -701,6 +734,8 @@ void llmcu_ctx_destroy(llmcu_ctx* ctx) {
   if (ctx->comm) cudaStreamSynchronize(ctx->comm);
   if (ctx->nccl) ncclCommDestroy(ctx->nccl);
   for (auto ev : ctx->ev_layer)
+    if (ev) cudaEventDestroy(ev);
+  for (auto ev : ctx->prof_ev)
     if (ev) cudaEventDestroy(ev);
   if (ctx->ev_comm_done) cudaEventDestroy(ctx->ev_comm_done);
   if (ctx->ev_step_done) cudaEventDestroy(ctx->ev_step_done);
@@ -1169,6 +1204,58 @@ llmcu_status llmcu_dp_init(llmcu_ctx* ctx, const void* id128, int rank, int worl
   }
   ctx->rank = rank;
   ctx->world = world;
+  return LLMCU_OK;
+}
+
+// -------------------------------------------------------------- profiling
+
+static void prof_collect(llmcu_ctx* ctx) {
+  if (ctx->prof_n == 0) return;
+  cudaEventSynchronize(ctx->prof_ev[ctx->prof_n - 1]);
+  for (int i = 0; i + 1 < ctx->prof_n; i += 2) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, ctx->prof_ev[i], ctx->prof_ev[i + 1]) == cudaSuccess) {
+      const int c = ctx->prof_cls[i / 2];
+      ctx->prof_ms[c] += ms;
+      ctx->prof_cnt[c] += kProfLaunches[c];
+    }
+  }
+  ctx->prof_n = 0;
+  ctx->prof_cls.clear();
+}
+
+llmcu_status llmcu_profile_enable(llmcu_ctx* ctx, int on) {
+  if (!ctx) return LLMCU_ERR_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  if (on && ctx->prof_ev.empty()) {
+    ctx->prof_ev.resize(8192);
+    for (auto& ev : ctx->prof_ev) CK(cudaEventCreate(&ev));
+  }
+  if (!on) prof_collect(ctx);
+  ctx->prof_on = on != 0;
+  return LLMCU_OK;
+}
+
+llmcu_status llmcu_profile_read(llmcu_ctx* ctx, char* buf, size_t len, int reset) {
+  if (!ctx || !buf || len == 0) return LLMCU_ERR_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  prof_collect(ctx);
+  std::string out = "{";
+  for (int c = 0; c < P_COUNT; ++c) {
+    char item[160];
+    snprintf(item, sizeof(item), "%s\"%s\": {\"ms\": %.6f, \"launches\": %lld}", c ? ", " : "", kProfNames[c],
+             ctx->prof_ms[c], static_cast<long long>(ctx->prof_cnt[c]));
+    out += item;
+  }
+  out += "}";
+  if (out.size() + 1 > len) return fail(ctx, LLMCU_ERR_INVALID_ARG, "profile buffer too small");
+  memcpy(buf, out.c_str(), out.size() + 1);
+  if (reset) {
+    for (int c = 0; c < P_COUNT; ++c) {
+      ctx->prof_ms[c] = 0;
+      ctx->prof_cnt[c] = 0;
+    }
+  }
   return LLMCU_OK;
 }
 

@@ -136,6 +136,8 @@ _SIGS = {
     "llmcu_dp_get_unique_id": (C.c_int, [C.c_void_p]),
     "llmcu_dp_init": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
     "llmcu_dp_set_timeout_ms": (C.c_int, [C.c_void_p, C.c_int]),
+    "llmcu_profile_enable": (C.c_int, [C.c_void_p, C.c_int]),
+    "llmcu_profile_read": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.c_int]),
     "llmcu_gemm_nt_f16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                     C.c_int, C.c_int, C.c_void_p]),
     "llmcu_attention_fwd": (C.c_int, [C.c_void_p] * 5 + [C.c_int] * 8 + [C.c_void_p]),
@@ -340,6 +342,16 @@ class Context:
 
     def load_lora(self, directory: str, step: int):
         self._check(lib().llmcu_load_lora(self._h, directory.encode(), step), "load_lora")
+
+    # -- profiling
+    def profile_enable(self, on: bool = True):
+        self._check(lib().llmcu_profile_enable(self._h, int(on)), "profile_enable")
+
+    def profile_read(self, reset: bool = True) -> dict:
+        import json
+        buf = C.create_string_buffer(4096)
+        self._check(lib().llmcu_profile_read(self._h, buf, 4096, int(reset)), "profile_read")
+        return json.loads(buf.value.decode())
 
     # -- data parallel
     @staticmethod
