@@ -21,7 +21,7 @@ It restates, in torch fp32 autograd on the CPU, the step that llm.cu's
 * AdamW (decoupled weight decay) .......... src/kernels/lora.cu:212-219
 
 Autograd gives the true gradient.  ``ref_bugs=True`` instead reproduces the
-three places where the reference's hand-written backward departs from it, so
+four places where the reference's hand-written backward departs from it, so
 that the golden can be pinned against the reference's own CUDA build
 (oracle/ref_harness):
 
@@ -32,9 +32,18 @@ that the golden can be pinned against the reference's own CUDA build
 * A11 the last position gets no dlogits row (its gradient is zero; the
   reference leaves the row uninitialised, the harness zeroes it)
   ........................................ src/kernels/loss.cu:18-21
+* A14 SwiGLU backward runs in place with d_swiglu aliased to d_gate
+  (src/kernels/lora_backward.cu:287 calls silu_backward(d_gate, .., d_gate,
+  d_up)), so d_up is formed from the already-overwritten d_gate:
+  d_up = (dy * u * silu'(g)) * silu(g) instead of dy * silu(g)
+  ........................................ src/kernels/activation.cu:35-36
 
-Parity of the training path is pinned by fixtures generated with the
-reference's own CUDA code (``tests/golden/``); see ``pin_status()``.
+Pinning: with ``ref_bugs=True`` this golden reproduces the reference
+trainer's own CUDA build (oracle/ref_harness, compiled from the reference
+sources) on seeded inputs -- loss, every LoRA gradient and the post-AdamW
+adapters agree to ~2e-6 relative (fixtures tests/golden/ref_tiny_*.npz,
+checked by tests/test_oracle.py).  The CUDA product is checked against the
+default (true-gradient) mode.
 """
 from __future__ import annotations
 
@@ -213,6 +222,24 @@ class _FinalNormRefBug(torch.autograd.Function):
         return rmsnorm_backward_at(dy, x_bwd, w, ctx.eps), None, None, None
 
 
+class _SwiGLURefBug(torch.autograd.Function):
+    """silu(g) * u whose backward reproduces the in-place aliasing of A14."""
+
+    @staticmethod
+    def forward(ctx, g, u):
+        ctx.save_for_backward(g, u)
+        return torch.nn.functional.silu(g) * u
+
+    @staticmethod
+    def backward(ctx, dy):
+        g, u = ctx.saved_tensors
+        sig = torch.sigmoid(g)
+        silu = g * sig
+        dg = dy * u * (sig * (1.0 + g * (1.0 - sig)))
+        du = dg * silu                              # reads the overwritten d_gate
+        return dg, du
+
+
 class _LoraDownRefBug(torch.autograd.Function):
     """h = x A^T whose dX reads A [r, d_in] with a [d_in, r] layout (A18)."""
 
@@ -322,7 +349,8 @@ def forward_backward(cfg: ModelCfg, base: Dict[str, np.ndarray], lora: Dict[str,
             xn2 = rmsnorm(x, W[p + "ffn_norm"], eps)
             g = xn2 @ W[p + "w_gate"].t()
             u = xn2 @ W[p + "w_up"].t()
-            x = x + (torch.nn.functional.silu(g) * u) @ W[p + "w_down"].t()
+            act = _SwiGLURefBug.apply(g, u) if ref_bugs else torch.nn.functional.silu(g) * u
+            x = x + act @ W[p + "w_down"].t()
         if ref_bugs:
             xf = _FinalNormRefBug.apply(x, post_attn_last.detach(), W["final_norm"], eps)
         else:
