@@ -323,7 +323,7 @@ def main():
     per_launch_s = gemm_ms_step / gemm_launches_step / 1e3
     achieved = per_launch_flops / per_launch_s / 1e12
     traffic = None
-    prof_path = os.path.join(ROOT, "profiles", "gemm_traffic.json")
+    prof_path = os.path.join(ROOT, "profiles", "gemm_traffic_c2.txt")
     if os.path.exists(prof_path):
         with open(prof_path) as f:
             tr = json.load(f).get(args.workload)
