@@ -249,6 +249,30 @@ llmcu_status llmcu_attention_bwd(const void* q, const void* k, const void* v, co
                                  int n_heads, int n_kv_heads, int head_dim, int ldq, int ldk,
                                  int ldv, int lddv, void* stream);
 
+/* The attention backward above with no scratch argument and no allocation.
+ * No counterpart in the reference (its backward cudaMallocs and frees
+ * temporaries on every call, src/kernels/lora_backward.cu:330-346).
+ * For callers that must not allocate device memory themselves: code running
+ * under a caching allocator that owns the device's memory (a cudaMalloc beside
+ * it fragments memory and escapes its accounting), or a latency-critical loop
+ * where cudaMalloc's implicit device synchronisation would stall other streams.
+ * The row sums it needs live in a 4 MiB array inside this library, which every
+ * GPU that loads the library holds until the process exits:
+ *   - batch * n_heads * seq must be <= 1,048,576, else LLMCU_ERR_UNSUPPORTED
+ *     and nothing is launched;
+ *   - the first call on a device looks up that device's copy of the array
+ *     (make it with the intended device current);
+ *   - all calls share the one array: calls that overlap on the GPU (different
+ *     streams, or several host threads) race and give wrong results; calls on
+ *     one stream are ordered and safe.  Every entry the kernels read is written
+ *     earlier in the same call, so stale contents from a previous call are
+ *     never used.
+ * Same arguments, layouts and results as llmcu_attention_bwd otherwise. */
+llmcu_status llmcu_attention_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
+                                         const void* dout, const float* lse, float* dq, float* dk, void* dv,
+                                         int batch, int seq, int n_heads, int n_kv_heads, int head_dim,
+                                         int ldq, int ldk, int ldv, int lddv, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -16,6 +16,9 @@
 // Tiles: 64 query rows x 64 key rows, 4 warps x 16 rows, fp16 operands in
 // XOR-swizzled shared memory fed by cp.async, mma.sync m16n8k16 with fp32
 // accumulation.  head_dim 64 and 128.
+#include <mutex>
+
+#include "../../include/llmcu.h"
 #include "common.cuh"
 
 namespace llmcu {
@@ -590,3 +593,58 @@ cudaError_t attention_backward(const __half* q, const __half* k, const __half* v
 }
 
 }  // namespace llmcu
+
+namespace llmcu {
+
+// ------------------------------------------- allocation-free backward variant
+// File-scope scratch for the row-wise dO.O sums of llmcu_attention_bwd_noalloc.
+// Every device that loads this library holds it (4 MiB) until the process
+// exits.  In host code the name is only a stand-in; the device address comes
+// from cudaGetSymbolAddress, looked up once per device with that device current.
+namespace {
+constexpr int64_t kNoAllocDeltaFloats = 1 << 20;  // batch * n_heads * seq <= 1,048,576
+__device__ __align__(256) float g_noalloc_delta[kNoAllocDeltaFloats];
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kMaxDevices] = {};
+
+cudaError_t noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_delta);
+    if (e != cudaSuccess) return e;
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+}  // namespace
+
+}  // namespace llmcu
+
+extern "C" llmcu_status llmcu_attention_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
+                                                    const void* dout, const float* lse, float* dq, float* dk,
+                                                    void* dv, int batch, int seq, int n_heads, int n_kv_heads,
+                                                    int head_dim, int ldq, int ldk, int ldv, int lddv,
+                                                    void* stream) {
+  using namespace llmcu;
+  if (!q || !k || !v || !o || !dout || !lse || !dq || !dk || !dv || batch <= 0 || seq <= 0 || n_heads <= 0 ||
+      n_kv_heads <= 0 || n_heads % n_kv_heads)
+    return LLMCU_ERR_INVALID_ARG;
+  if (static_cast<int64_t>(batch) * n_heads * seq > kNoAllocDeltaFloats) return LLMCU_ERR_UNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128) return LLMCU_ERR_UNSUPPORTED;
+  float* delta = nullptr;
+  if (noalloc_scratch(&delta) != cudaSuccess) return LLMCU_ERR_CUDA;
+  const int ldo = n_heads * head_dim;
+  const cudaError_t e = attention_backward(
+      static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v),
+      static_cast<const __half*>(o), static_cast<const __half*>(dout), lse, delta, dq, dk, static_cast<__half*>(dv),
+      batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk, ldv, ldo, ldo, n_kv_heads * head_dim, lddv,
+      static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LLMCU_OK : LLMCU_ERR_CUDA;
+}

@@ -142,6 +142,7 @@ _SIGS = {
                                     C.c_int, C.c_int, C.c_void_p]),
     "llmcu_attention_fwd": (C.c_int, [C.c_void_p] * 5 + [C.c_int] * 8 + [C.c_void_p]),
     "llmcu_attention_bwd": (C.c_int, [C.c_void_p] * 10 + [C.c_int] * 9 + [C.c_void_p]),
+    "llmcu_attention_bwd_noalloc": (C.c_int, [C.c_void_p] * 9 + [C.c_int] * 9 + [C.c_void_p]),
 }
 
 
@@ -389,6 +390,14 @@ def attention_bwd(q, k, v, o, do, lse, delta, dq, dk, dv, batch, seq, nh, nkv, h
                   stream=0):
     _chk(lib().llmcu_attention_bwd(q, k, v, o, do, lse, delta, dq, dk, dv, batch, seq, nh, nkv, hd, ldq, ldk,
                                    ldv, lddv, stream), "attention_bwd")
+
+
+def attention_bwd_noalloc(q, k, v, o, do, lse, dq, dk, dv, batch, seq, nh, nkv, hd, ldq, ldk, ldv, lddv,
+                          stream=0) -> int:
+    """Allocation-free attention backward; returns the raw status (callers
+    check LLMCU_ERR_UNSUPPORTED for sizes above the library's fixed scratch)."""
+    return lib().llmcu_attention_bwd_noalloc(q, k, v, o, do, lse, dq, dk, dv, batch, seq, nh, nkv, hd, ldq,
+                                             ldk, ldv, lddv, stream)
 
 
 def quantize_int8_rows(w_ptr, rows, cols, q_ptr, scale_ptr, stream=0):
