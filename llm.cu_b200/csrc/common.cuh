@@ -19,6 +19,9 @@ cudaError_t attention_backward(const __half* q, const __half* k, const __half* v
                                int lddk, int lddv, cudaStream_t st);
 
 // ---- gemm.cu
+// Column slices per GEMM tile (epilogue warps per TMEM lane quadrant); the
+// lm_head statistics epilogue writes one (max, sum-exp) partial per slice.
+constexpr int kGemmEpiGroups = 2;
 // Tensor operand for the GEMM: fp16, K-major rows (K contiguous), `ld`
 // elements between rows; `rows` x `k` valid extent.
 struct Operand {
@@ -66,6 +69,13 @@ struct EpiArgs {
 cudaError_t gemm(const Operand& A0, const Operand& B0, const Operand& A1, const Operand& B1, int M, int N, Epi epi,
                  const EpiArgs& ea, int* err, cudaStream_t st, int bn_hint = 0);
 int gemm_num_sms();
+// Skinny GEMM (N <= 64, e.g. the LoRA h = x A^T products): split over K into
+// (tile, split) units spread across the SMs, fp32 partials in `ws`, then a
+// fixed-order reduction to fp16 `out` -- deterministic.
+constexpr int kSkinnyMaxSplits = 16;
+size_t gemm_skinny_ws_floats(int M, int N);
+cudaError_t gemm_skinny(const Operand& A, const Operand& B, int M, int N, __half* out, int ld_out, float* ws,
+                        int* err, cudaStream_t st);
 
 // ---- kernels.cu
 cudaError_t embed_forward(const int* tokens, const __half* E, float* out, int M, int H, int V, int* err,
@@ -73,6 +83,8 @@ cudaError_t embed_forward(const int* tokens, const __half* E, float* out, int M,
 cudaError_t rmsnorm_forward(const float* x, const float* w, __half* out, int M, int H, float eps, cudaStream_t st);
 // dres (+)= rmsnorm_bwd(dy, x, w); dres16 = fp16(dres)
 cudaError_t rmsnorm_backward(const float* dy, const float* x, const float* w, float* dres, __half* dres16, int M,
+                             int H, float eps, int accumulate, cudaStream_t st);
+cudaError_t rmsnorm_backward(const __half* dy, const float* x, const float* w, float* dres, __half* dres16, int M,
                              int H, float eps, int accumulate, cudaStream_t st);
 cudaError_t qknorm_rope_forward(const __half* qkv, int ld_qkv, const float* qn_w, const float* kn_w,
                                 const float* cos_t, const float* sin_t, __half* q_out, __half* k_out, int B, int S,

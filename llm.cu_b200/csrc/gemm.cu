@@ -2,6 +2,7 @@
 // shape choice and the launch of the instantiated kernels.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -41,61 +42,81 @@ bool make_map(CUtensorMap* map, const Operand& op, int box_rows) {
   return r == CUDA_SUCCESS;
 }
 
-template <int BN>
+// Output / epilogue-input map: rows x cols of fp16 or fp32, box = 128 bytes of
+// columns x 32 rows (one epilogue warp's slab), 128-byte swizzle.
+bool make_io_map(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, bool f32) {
+  if (!g_encode || !ptr) return false;
+  const int es = f32 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0 || (static_cast<int64_t>(ld) * es) % 16 != 0) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * es};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / es), 32u};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = g_encode(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                        const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// As many pipeline stages as fit beside the epilogue slabs (at most 8).
+template <int BN, int EW, int SLAB>
 constexpr int stages_for() {
-  return BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  constexpr int stage = kBlockM * kBlockK * 2 + BN * kBlockK * 2;
+  constexpr int s = (232448 - 1536 - EW * SLAB) / stage;
+  return s > 8 ? 8 : s;
+}
+
+// 8 epilogue warps (two per TMEM lane quadrant) for 128/256-wide tiles, 4 for 64.
+template <int BN>
+constexpr int epi_warps() {
+  return BN >= 128 ? 4 * kGemmEpiGroups : 4;
 }
 
 template <int BN, class E>
-cudaError_t launch(const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
-                   const GemmShape& sh, const typename E::Params& p, int* err, cudaStream_t st) {
-  constexpr int S = stages_for<BN>();
-  using L = GemmSmem<BN, S>;
-  auto kern = gemm_tc_kernel<BN, S, E>;
+cudaError_t launch(const CUtensorMap* maps, const GemmShape& sh, const typename E::Params& p, int* err,
+                   cudaStream_t st) {
+  constexpr int kEpiWarps = epi_warps<BN>();
+  constexpr int S = stages_for<BN, kEpiWarps, E::kSlab>();
+  using L = GemmSmem<BN, S, kEpiWarps, E::kSlab>;
+  static_assert(L::kBytes <= 232448, "shared memory budget");
+  auto kern = gemm_tc_kernel<BN, S, kEpiWarps, E>;
   static bool attr_done = false;  // set once per instantiation
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  int grid = sh.num_tiles < g_num_sms ? sh.num_tiles : g_num_sms;
-  kern<<<grid, kGemmThreads, L::kBytes, st>>>(a0, b0, a1, b1, sh, p, err);
+  const int units = sh.num_tiles * sh.splits;
+  int grid = units < g_num_sms ? units : g_num_sms;
+  kern<<<grid, 64 + 32 * kEpiWarps, L::kBytes, st>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], sh, p,
+                                                     err);
   return cudaGetLastError();
 }
 
 template <int BN>
-cudaError_t dispatch(Epi epi, const EpiArgs& ea, const CUtensorMap& a0, const CUtensorMap& b0,
-                     const CUtensorMap& a1, const CUtensorMap& b1, const GemmShape& sh, int* err, cudaStream_t st) {
+cudaError_t dispatch(Epi epi, const EpiArgs& ea, const CUtensorMap* maps, const GemmShape& sh, int* err,
+                     cudaStream_t st) {
   switch (epi) {
-    case Epi::kStoreF16: {
-      EpiStoreF16::Params p{static_cast<__half*>(ea.out), ea.ld_out};
-      return launch<BN, EpiStoreF16>(a0, b0, a1, b1, sh, p, err, st);
-    }
-    case Epi::kStoreF32: {
-      EpiStoreF32::Params p{static_cast<float*>(ea.out), ea.ld_out, ea.accumulate};
-      return launch<BN, EpiStoreF32>(a0, b0, a1, b1, sh, p, err, st);
-    }
-    case Epi::kResidF32: {
-      EpiResidF32::Params p{static_cast<float*>(ea.out), ea.resid, ea.ld_out};
-      return launch<BN, EpiResidF32>(a0, b0, a1, b1, sh, p, err, st);
-    }
-    case Epi::kSwiGLUBwd: {
-      EpiSwiGLUBwd::Params p{ea.gu_in, ea.gu, ea.ld_gu};
-      return launch<BN, EpiSwiGLUBwd>(a0, b0, a1, b1, sh, p, err, st);
-    }
+    case Epi::kStoreF16:
+      return launch<BN, EpiStoreF16>(maps, sh, EpiStoreF16::Params{}, err, st);
+    case Epi::kStoreF32:
+      return launch<BN, EpiStoreF32>(maps, sh, EpiStoreF32::Params{ea.accumulate}, err, st);
+    case Epi::kResidF32:
+      return launch<BN, EpiResidF32>(maps, sh, EpiResidF32::Params{}, err, st);
+    case Epi::kSwiGLUBwd:
+      return launch<BN, EpiSwiGLUBwd>(maps, sh, EpiSwiGLUBwd::Params{}, err, st);
     case Epi::kCEStats: {
-      EpiCEStats::Params p{ea.targets, ea.part_max, ea.part_sum, ea.tgt_logit, sh.tiles_n};
-      return launch<BN, EpiCEStats>(a0, b0, a1, b1, sh, p, err, st);
+      EpiCEStats::Params p{ea.targets, ea.part_max, ea.part_sum, ea.tgt_logit, sh.tiles_n * (epi_warps<BN>() / 4)};
+      return launch<BN, EpiCEStats>(maps, sh, p, err, st);
     }
     case Epi::kCEGrad: {
-      EpiCEGrad::Params p{ea.targets, ea.lse, ea.valid, static_cast<__half*>(ea.out), ea.ld_out, ea.col_base,
-                          ea.gscale};
-      return launch<BN, EpiCEGrad>(a0, b0, a1, b1, sh, p, err, st);
+      EpiCEGrad::Params p{ea.targets, ea.lse, ea.valid, ea.col_base, ea.gscale};
+      return launch<BN, EpiCEGrad>(maps, sh, p, err, st);
     }
     case Epi::kSwiGLU: {
       if constexpr (BN == 256) {
-        EpiSwiGLU::Params p{ea.gu, ea.ld_gu, ea.act, ea.ld_act};
-        return launch<BN, EpiSwiGLU>(a0, b0, a1, b1, sh, p, err, st);
+        return launch<BN, EpiSwiGLU>(maps, sh, EpiSwiGLU::Params{}, err, st);
       } else {
         return cudaErrorInvalidValue;
       }
@@ -119,14 +140,44 @@ cudaError_t gemm(const Operand& A0, const Operand& B0, const Operand& A1, const 
   int BN = bn_hint;
   if (BN == 0) BN = (epi == Epi::kSwiGLU) ? 256 : (N <= 64 ? 64 : (N <= 128 ? 128 : 256));
   if (epi == Epi::kSwiGLU && BN != 256) return cudaErrorInvalidValue;
-  CUtensorMap a0, b0, a1, b1;
-  if (!make_map(&a0, A0, kBlockM) || !make_map(&b0, B0, BN)) return cudaErrorInvalidValue;
+  if (epi == Epi::kCEStats && BN != 256) return cudaErrorInvalidValue;  // partial slots assume 256-wide tiles
+  CUtensorMap maps[6];  // A0, B0, A1, B1, C, D
+  if (!make_map(&maps[0], A0, kBlockM) || !make_map(&maps[1], B0, BN)) return cudaErrorInvalidValue;
   if (A1.k > 0) {
-    if (!make_map(&a1, A1, kBlockM) || !make_map(&b1, B1, BN)) return cudaErrorInvalidValue;
+    if (!make_map(&maps[2], A1, kBlockM) || !make_map(&maps[3], B1, BN)) return cudaErrorInvalidValue;
   } else {
-    a1 = a0;
-    b1 = b0;
+    maps[2] = maps[0];
+    maps[3] = maps[1];
   }
+  bool okc = true;
+  switch (epi) {
+    case Epi::kStoreF16:
+    case Epi::kCEGrad:
+      okc = make_io_map(&maps[4], ea.out, M, N, ea.ld_out, false);
+      maps[5] = maps[4];
+      break;
+    case Epi::kStoreF32:
+      okc = make_io_map(&maps[4], ea.out, M, N, ea.ld_out, true);
+      maps[5] = maps[4];
+      break;
+    case Epi::kResidF32:
+      okc = make_io_map(&maps[4], ea.out, M, N, ea.ld_out, true) &&
+            make_io_map(&maps[5], ea.resid, M, N, ea.ld_out, true);
+      break;
+    case Epi::kSwiGLU:  // C = gate/up pre-activations [M, N], D = act [M, N/2]
+      okc = make_io_map(&maps[4], ea.gu, M, N, ea.ld_gu, false) &&
+            make_io_map(&maps[5], ea.act, M, N / 2, ea.ld_act, false);
+      break;
+    case Epi::kSwiGLUBwd:  // C = dgu [M, 2N] out, D = gu [M, 2N] in
+      okc = make_io_map(&maps[4], ea.gu, M, 2 * N, ea.ld_gu, false) &&
+            make_io_map(&maps[5], ea.gu_in, M, 2 * N, ea.ld_gu, false);
+      break;
+    case Epi::kCEStats:
+      maps[4] = maps[0];
+      maps[5] = maps[0];
+      break;
+  }
+  if (!okc) return cudaErrorInvalidValue;
   GemmShape sh;
   sh.M = M;
   sh.N = N;
@@ -135,12 +186,74 @@ cudaError_t gemm(const Operand& A0, const Operand& B0, const Operand& A1, const 
   sh.tiles_m = (M + kBlockM - 1) / kBlockM;
   sh.tiles_n = (N + BN - 1) / BN;
   sh.num_tiles = sh.tiles_m * sh.tiles_n;
+  sh.splits = 1;
+  sh.kb_per_split = (A0.k + kBlockK - 1) / kBlockK + (A1.k + kBlockK - 1) / kBlockK;
   switch (BN) {
-    case 64: return dispatch<64>(epi, ea, a0, b0, a1, b1, sh, err, st);
-    case 128: return dispatch<128>(epi, ea, a0, b0, a1, b1, sh, err, st);
-    case 256: return dispatch<256>(epi, ea, a0, b0, a1, b1, sh, err, st);
+    case 64: return dispatch<64>(epi, ea, maps, sh, err, st);
+    case 128: return dispatch<128>(epi, ea, maps, sh, err, st);
+    case 256: return dispatch<256>(epi, ea, maps, sh, err, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+namespace {
+
+// out16[m, n] = sum over splits of part[(s * Mp + m) * N + n]
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int Mp, int M, int N,
+                                     __half* __restrict__ out, int ld_out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // over M * N / 2 pairs
+  if (i >= M * (N / 2)) return;
+  const int m = i / (N / 2), n = 2 * (i % (N / 2));
+  float a = 0.f, b = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float2 v = *reinterpret_cast<const float2*>(part + (static_cast<size_t>(s) * Mp + m) * N + n);
+    a += v.x;
+    b += v.y;
+  }
+  *reinterpret_cast<__half2*>(out + static_cast<size_t>(m) * ld_out + n) = __floats2half2_rn(a, b);
+}
+
+}  // namespace
+
+size_t gemm_skinny_ws_floats(int M, int N) {
+  return static_cast<size_t>(kSkinnyMaxSplits) * ((M + kBlockM - 1) / kBlockM) * kBlockM * N;
+}
+
+cudaError_t gemm_skinny(const Operand& A, const Operand& B, int M, int N, __half* out, int ld_out, float* ws,
+                        int* err, cudaStream_t st) {
+  std::call_once(g_once, init_once);
+  if (!g_encode) return cudaErrorNotSupported;
+  if (M <= 0 || N <= 0 || N > 64 || N % 2 || A.k <= 0 || A.k != B.k) return cudaErrorInvalidValue;
+  const int tiles_m = (M + kBlockM - 1) / kBlockM;
+  const int nk = (A.k + kBlockK - 1) / kBlockK;
+  // enough (tile, split) units to cover the SMs, each with >= 4 k-blocks
+  int splits = (g_num_sms + tiles_m - 1) / tiles_m;
+  splits = std::min(splits, std::max(1, nk / 4));
+  splits = std::min(splits, kSkinnyMaxSplits);
+  const int kbps = (nk + splits - 1) / splits;
+  splits = (nk + kbps - 1) / kbps;
+  const int Mp = tiles_m * kBlockM;
+  CUtensorMap maps[6];
+  if (!make_map(&maps[0], A, kBlockM) || !make_map(&maps[1], B, 64)) return cudaErrorInvalidValue;
+  maps[2] = maps[0];
+  maps[3] = maps[1];
+  if (!make_io_map(&maps[4], ws, splits * Mp, N, N, true)) return cudaErrorInvalidValue;
+  maps[5] = maps[4];
+  GemmShape sh;
+  sh.M = M;
+  sh.N = N;
+  sh.K0 = A.k;
+  sh.K1 = 0;
+  sh.tiles_m = tiles_m;
+  sh.tiles_n = 1;
+  sh.num_tiles = tiles_m;
+  sh.splits = splits;
+  sh.kb_per_split = kbps;
+  cudaError_t e = launch<64, EpiStoreF32>(maps, sh, EpiStoreF32::Params{0}, err, st);
+  if (e != cudaSuccess) return e;
+  const int pairs = M * (N / 2);
+  splitk_reduce_kernel<<<(pairs + 255) / 256, 256, 0, st>>>(ws, splits, Mp, M, N, out, ld_out);
+  return cudaGetLastError();
 }
 
 }  // namespace llmcu

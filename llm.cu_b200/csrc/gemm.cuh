@@ -8,11 +8,19 @@
 // y = xW^T + 2(xA^T)B^T into one accumulation, so the adapter update costs one
 // extra 64-wide K block instead of a separate GEMM and an add pass.
 //
-// Roles (192 threads, one CTA per SM):
-//   warp 0      TMA producer  -- fills a STAGES-deep ring of (A, B) smem tiles
-//   warp 1      MMA issuer    -- tcgen05.mma into one of two TMEM accumulators
-//                               (allocates / frees TMEM for the CTA)
-//   warps 2..5  epilogue      -- tcgen05.ld -> registers -> fused op -> global
+// Roles (64 + 32*EW threads, one CTA per SM):
+//   warp 0        TMA producer -- fills a STAGES-deep ring of (A, B) smem tiles
+//   warp 1        MMA issuer   -- tcgen05.mma into one of two TMEM accumulators
+//                                (allocates / frees TMEM for the CTA)
+//   warps 2..EW+1 epilogue     -- tcgen05.ld -> registers -> fused op; warp w
+//                                reads TMEM lanes 32*(w%4).. (the lane quadrant
+//                                it may access); with EW = 8 two warps share a
+//                                quadrant and split the tile's columns.
+// Epilogue I/O goes through a 4 KB shared-memory slab per warp (32 rows x
+// 128 bytes, 128-byte swizzle): the warp writes its rows there and one lane
+// issues a TMA store (or reduce-add) of the whole slab, so global writes leave
+// the SM as full lines; inputs the epilogue needs (residual, SwiGLU
+// pre-activations) arrive the same way through TMA loads.
 // Tiles: BLOCK_M = 128 rows, BLOCK_N = BN (64/128/256), BLOCK_K = 64 (one
 // 128-byte swizzle row of fp16).  Tile t -> (t % tiles_m, t / tiles_m), so
 // CTAs that run together share the weight (B) tile and stream it once.
@@ -26,210 +34,346 @@ struct GemmShape {
   int M, N;
   int K0, K1;      // K of segment 0 and of the optional segment 1 (0 = none)
   int tiles_m, tiles_n, num_tiles;
+  int splits;      // K splits (1 = none); split s writes rows [s * tiles_m * 128, ...)
+  int kb_per_split;
 };
 
-constexpr int kGemmThreads = 192;
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 64;
+constexpr int kSlabBytes = 32 * 128;  // one 32-row x 128-byte box
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EW, int SLAB = kSlabBytes>
 struct GemmSmem {
   static constexpr int kABytes = kBlockM * kBlockK * 2;       // 16 KB
   static constexpr int kBBytes = BN * kBlockK * 2;            // 8/16/32 KB
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;  // two accumulators
-  static constexpr int kBarOffset = STAGES * kStageBytes;
-  static constexpr int kBytes = kBarOffset + 256 + 1024;       // + barriers + alignment slack
+  static constexpr int kSlabOffset = STAGES * kStageBytes;
+  static constexpr int kBarOffset = kSlabOffset + EW * SLAB;
+  static constexpr int kBytes = kBarOffset + 512 + 1024;       // + barriers + alignment slack
 };
+
+// ------------------------------------------------------ epilogue plumbing
+
+// One epilogue warp's view: its 32-row slab of the tile and its staging slab.
+struct EpiCtx {
+  int lane;
+  int row0;                 // first tile row of this warp (global row index)
+  int row;                  // this thread's row = row0 + lane
+  int M, N;
+  uint32_t slab;            // shared address of the 4 KB staging slab
+  uint64_t* bar;            // mbarrier for TMA loads into the slab
+  uint32_t phase;           // its parity
+  volatile int* abort_flag;
+  int* err;
+  const CUtensorMap* mapC;  // primary output
+  const CUtensorMap* mapD;  // secondary input or output (epilogue specific)
+};
+
+// byte offset of 16-byte chunk j (0..7) of the thread's 128-byte slab row,
+// 128-byte swizzle (chunk ^ row % 8), as TMA lays the box out
+// (box b of the slab: b * 4 KB; boxes are 1024-byte aligned)
+__device__ __forceinline__ uint32_t slab_addr(const EpiCtx& c, int j, int b = 0) {
+  return c.slab + static_cast<uint32_t>(b * kSlabBytes + c.lane * 128 + ((j ^ (c.lane & 7)) << 4));
+}
+__device__ __forceinline__ void slab_st(const EpiCtx& c, int j, uint4 v, int b = 0) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(slab_addr(c, j, b)), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 slab_ld(const EpiCtx& c, int j, int b = 0) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(slab_addr(c, j, b))
+               : "memory");
+  return v;
+}
+// Until the TMA engine has read the slab (previous store from this warp).
+__device__ __forceinline__ void slab_wait_read(const EpiCtx& c) {
+  if (c.lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+  __syncwarp();
+}
+// Publish the slab to the async proxy and store box b of it to map at (x, y).
+__device__ __forceinline__ void slab_store(const EpiCtx& c, const CUtensorMap* map, int x, int y, int b = 0) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (c.lane == 0) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c.slab + b * kSlabBytes), "r"(x), "r"(y)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  }
+}
+// Same, adding the slab (fp32) into global memory.
+__device__ __forceinline__ void slab_reduce_add(const EpiCtx& c, const CUtensorMap* map, int x, int y) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (c.lane == 0) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c.slab), "r"(x), "r"(y)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  }
+}
+// TMA-load the box at (x, y) of map into the slab and wait for it.
+__device__ __forceinline__ bool slab_load(EpiCtx& c, const CUtensorMap* map, int x, int y) {
+  if (c.lane == 0) {
+    mbar_arrive_expect_tx(c.bar, kSlabBytes);
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(c.slab),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(c.bar)), "r"(x), "r"(y)
+        : "memory");
+  }
+  __syncwarp();
+  const bool ok = mbar_wait(c.bar, c.phase, c.abort_flag, c.err, kErrWaitAccum);
+  c.phase ^= 1u;
+  return ok;
+}
+// TMA-load two boxes, (x0, y) into box 0 and (x1, y) into box 1, and wait for both.
+__device__ __forceinline__ bool slab_load2(EpiCtx& c, const CUtensorMap* map, int x0, int x1, int y) {
+  if (c.lane == 0) {
+    mbar_arrive_expect_tx(c.bar, 2 * kSlabBytes);
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(c.slab),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(c.bar)), "r"(x0), "r"(y)
+        : "memory");
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(c.slab + kSlabBytes),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(c.bar)), "r"(x1), "r"(y)
+        : "memory");
+  }
+  __syncwarp();
+  const bool ok = mbar_wait(c.bar, c.phase, c.abort_flag, c.err, kErrWaitAccum);
+  c.phase ^= 1u;
+  return ok;
+}
+
+__device__ __forceinline__ uint4 pack8(const float* v) {
+  uint4 w;
+  w.x = pack_half2(v[0], v[1]);
+  w.y = pack_half2(v[2], v[3]);
+  w.z = pack_half2(v[4], v[5]);
+  w.w = pack_half2(v[6], v[7]);
+  return w;
+}
+__device__ __forceinline__ void unpack8(uint4 w, float* v) {
+  const __half2* h = reinterpret_cast<const __half2*>(&w);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g * (1.0f / (1.0f + __expf(-g))); }
 
 // ----------------------------------------------------------------- epilogues
-// An epilogue sees one row (`row`, < M guaranteed only via the check below)
-// and 32 consecutive accumulator columns starting at `col0`.
+// Interface: kChunk accumulator columns per call (one 128-byte slab row per
+// thread); chunk(col0) sees columns [col0, col0 + kChunk) of row c.row.
+// Returning false aborts the epilogue (a bounded wait expired).
 
+// C (fp16) = acc
 struct EpiStoreF16 {
-  struct Params { __half* C; int ldc; };
+  struct Params {};
   struct State {};
+  static constexpr int kChunk = 64;
+  static constexpr int kSlab = kSlabBytes;
   static constexpr bool kPaired = false;
-  __device__ static void begin(State&, const Params&, int, int) {}
-  __device__ static void chunk(State&, const Params& p, int row, int col0, int M, int N, const float* v) {
-    if (row >= M) return;
-    __half* dst = p.C + static_cast<size_t>(row) * p.ldc + col0;
-    if (col0 + 32 <= N) {
+  static constexpr bool kStores = true;
+  __device__ static void begin(State&, const Params&, const EpiCtx&, int) {}
+  __device__ static bool chunk(State&, const Params&, EpiCtx& c, int col0, const float* v) {
+    if (col0 >= c.N) return true;
+    slab_wait_read(c);
 #pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint4 w;
-        w.x = pack_half2(v[j + 0], v[j + 1]);
-        w.y = pack_half2(v[j + 2], v[j + 3]);
-        w.z = pack_half2(v[j + 4], v[j + 5]);
-        w.w = pack_half2(v[j + 6], v[j + 7]);
-        *reinterpret_cast<uint4*>(dst + j) = w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < N) dst[j] = __float2half_rn(v[j]);
-    }
+    for (int j = 0; j < 8; ++j) slab_st(c, j, pack8(v + 8 * j));
+    slab_store(c, c.mapC, col0, c.row0);
+    return true;
   }
-  __device__ static void end(State&, const Params&, int, int, int) {}
+  __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
 };
 
-// C = acc (fp32), or C += acc when accumulate != 0.
+// C (fp32) = acc, or C += acc (TMA reduce-add) when accumulate != 0.
 struct EpiStoreF32 {
-  struct Params { float* C; int ldc; int accumulate; };
+  struct Params { int accumulate; };
   struct State {};
+  static constexpr int kChunk = 32;
+  static constexpr int kSlab = kSlabBytes;
   static constexpr bool kPaired = false;
-  __device__ static void begin(State&, const Params&, int, int) {}
-  __device__ static void chunk(State&, const Params& p, int row, int col0, int M, int N, const float* v) {
-    if (row >= M) return;
-    float* dst = p.C + static_cast<size_t>(row) * p.ldc + col0;
-    if (col0 + 32 <= N) {
+  static constexpr bool kStores = true;
+  __device__ static void begin(State&, const Params&, const EpiCtx&, int) {}
+  __device__ static bool chunk(State&, const Params& p, EpiCtx& c, int col0, const float* v) {
+    if (col0 >= c.N) return true;
+    slab_wait_read(c);
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        float4 w = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        if (p.accumulate) {
-          float4 o = *reinterpret_cast<const float4*>(dst + j);
-          w.x += o.x; w.y += o.y; w.z += o.z; w.w += o.w;
-        }
-        *reinterpret_cast<float4*>(dst + j) = w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < N) dst[j] = p.accumulate ? dst[j] + v[j] : v[j];
+    for (int j = 0; j < 8; ++j) {
+      uint4 w;
+      w.x = __float_as_uint(v[4 * j]);
+      w.y = __float_as_uint(v[4 * j + 1]);
+      w.z = __float_as_uint(v[4 * j + 2]);
+      w.w = __float_as_uint(v[4 * j + 3]);
+      slab_st(c, j, w);
     }
+    if (p.accumulate)
+      slab_reduce_add(c, c.mapC, col0, c.row0);
+    else
+      slab_store(c, c.mapC, col0, c.row0);
+    return true;
   }
-  __device__ static void end(State&, const Params&, int, int, int) {}
+  __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
 };
 
-// out = acc + resid (fp32): the residual adds of the O and down projections
-// (src/kernels/lora_forward.cu:265,297).
+// out (fp32) = acc + resid: the residual adds of the O and down projections
+// (src/kernels/lora_forward.cu:265,297).  mapD = resid (input), mapC = out.
 struct EpiResidF32 {
-  struct Params { float* out; const float* resid; int ld; };
+  struct Params {};
   struct State {};
+  static constexpr int kChunk = 32;
+  static constexpr int kSlab = kSlabBytes;
   static constexpr bool kPaired = false;
-  __device__ static void begin(State&, const Params&, int, int) {}
-  __device__ static void chunk(State&, const Params& p, int row, int col0, int M, int N, const float* v) {
-    if (row >= M) return;
-    const size_t base = static_cast<size_t>(row) * p.ld + col0;
-    if (col0 + 32 <= N) {
+  static constexpr bool kStores = true;
+  __device__ static void begin(State&, const Params&, const EpiCtx&, int) {}
+  __device__ static bool chunk(State&, const Params&, EpiCtx& c, int col0, const float* v) {
+    if (col0 >= c.N) return true;
+    slab_wait_read(c);
+    if (!slab_load(c, c.mapD, col0, c.row0)) return false;
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        float4 r = *reinterpret_cast<const float4*>(p.resid + base + j);
-        *reinterpret_cast<float4*>(p.out + base + j) =
-            make_float4(v[j] + r.x, v[j + 1] + r.y, v[j + 2] + r.z, v[j + 3] + r.w);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < N) p.out[base + j] = v[j] + p.resid[base + j];
+    for (int j = 0; j < 8; ++j) {
+      uint4 r = slab_ld(c, j);
+      r.x = __float_as_uint(__uint_as_float(r.x) + v[4 * j]);
+      r.y = __float_as_uint(__uint_as_float(r.y) + v[4 * j + 1]);
+      r.z = __float_as_uint(__uint_as_float(r.z) + v[4 * j + 2]);
+      r.w = __float_as_uint(__uint_as_float(r.w) + v[4 * j + 3]);
+      slab_st(c, j, r);
     }
+    slab_store(c, c.mapC, col0, c.row0);
+    return true;
   }
-  __device__ static void end(State&, const Params&, int, int, int) {}
+  __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
 };
-
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
 
 // Gate/up GEMM with SwiGLU (src/kernels/activation.cu:5-11).  The fused
 // weight interleaves 128-row blocks of W_gate and W_up, so a 256-wide tile
 // holds gate columns [0,128) and the matching up columns [128,256).  Writes
 // the pre-activations (kept for the backward) and act = silu(g) * u.
+// mapC = gu [M, 2I] (fp16), mapD = act [M, I] (fp16).
 struct EpiSwiGLU {
-  struct Params { __half* gu; int ld_gu; __half* act; int ld_act; };
+  struct Params {};
   struct State {};
+  static constexpr int kChunk = 64;
+  static constexpr int kSlab = kSlabBytes;
   static constexpr bool kPaired = true;  // requires BN == 256
-  __device__ static void begin(State&, const Params&, int, int) {}
-  // g: columns [col0, col0+32) of the gate half, u: the matching up columns.
-  __device__ static void pair(State&, const Params& p, int row, int tile_n, int c, int M, const float* g,
-                              const float* u) {
-    if (row >= M) return;
-    __half* gdst = p.gu + static_cast<size_t>(row) * p.ld_gu + tile_n * 256 + c;
-    __half* udst = gdst + 128;
-    __half* adst = p.act + static_cast<size_t>(row) * p.ld_act + tile_n * 128 + c;
+  static constexpr bool kStores = true;
+  __device__ static void begin(State&, const Params&, const EpiCtx&, int) {}
+  // g: gate columns [cc, cc+64) of tile tn, u: the matching up columns
+  __device__ static bool pair(State&, const Params&, EpiCtx& c, int tile_n, int cc, const float* g, const float* u) {
+    slab_wait_read(c);
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      uint4 wg, wu, wa;
-      wg.x = pack_half2(g[j], g[j + 1]); wg.y = pack_half2(g[j + 2], g[j + 3]);
-      wg.z = pack_half2(g[j + 4], g[j + 5]); wg.w = pack_half2(g[j + 6], g[j + 7]);
-      wu.x = pack_half2(u[j], u[j + 1]); wu.y = pack_half2(u[j + 2], u[j + 3]);
-      wu.z = pack_half2(u[j + 4], u[j + 5]); wu.w = pack_half2(u[j + 6], u[j + 7]);
+    for (int j = 0; j < 8; ++j) slab_st(c, j, pack8(g + 8 * j));
+    slab_store(c, c.mapC, tile_n * 256 + cc, c.row0);
+    slab_wait_read(c);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) slab_st(c, j, pack8(u + 8 * j));
+    slab_store(c, c.mapC, tile_n * 256 + 128 + cc, c.row0);
+    slab_wait_read(c);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
       float a[8];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) a[t] = silu_f(g[j + t]) * u[j + t];
-      wa.x = pack_half2(a[0], a[1]); wa.y = pack_half2(a[2], a[3]);
-      wa.z = pack_half2(a[4], a[5]); wa.w = pack_half2(a[6], a[7]);
-      *reinterpret_cast<uint4*>(gdst + j) = wg;
-      *reinterpret_cast<uint4*>(udst + j) = wu;
-      *reinterpret_cast<uint4*>(adst + j) = wa;
+      for (int t = 0; t < 8; ++t) a[t] = silu_f(g[8 * j + t]) * u[8 * j + t];
+      slab_st(c, j, pack8(a));
     }
+    slab_store(c, c.mapD, tile_n * 128 + cc, c.row0);
+    return true;
   }
-  __device__ static void end(State&, const Params&, int, int, int) {}
+  __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
 };
 
 // Down-projection dX with the SwiGLU backward fused (src/kernels/activation.cu:26-38):
-// acc = d_act[row, i]; reads g, u from the interleaved stash and writes
-// dg, du into the same interleaved layout (the A operand of the gate/up dX GEMM).
+// acc = d_act[row, i]; reads g, u from the interleaved stash (mapD) and writes
+// dg, du into the same interleaved layout of dgu (mapC), the A operand of the
+// gate/up dX GEMM.
 struct EpiSwiGLUBwd {
-  struct Params { const __half* gu; __half* dgu; int ld; };
+  struct Params {};
   struct State {};
+  static constexpr int kChunk = 64;
+  static constexpr int kSlab = 2 * kSlabBytes;  // g and u boxes side by side
   static constexpr bool kPaired = false;
-  __device__ static void begin(State&, const Params&, int, int) {}
-  __device__ static void chunk(State&, const Params& p, int row, int col0, int M, int N, const float* v) {
-    if (row >= M || col0 >= N) return;
-    // col0 is a multiple of 32, so the 32 columns share one 128-block.
+  static constexpr bool kStores = true;
+  __device__ static void begin(State&, const Params&, const EpiCtx&, int) {}
+  __device__ static bool chunk(State&, const Params&, EpiCtx& c, int col0, const float* v) {
+    if (col0 >= c.N) return true;
+    // col0 is a multiple of 64: the 64 columns share one 128-column block
     const int gcol = (col0 >> 7) * 256 + (col0 & 127);
-    const size_t base = static_cast<size_t>(row) * p.ld + gcol;
+    uint32_t gp[32], up[32];  // g and u as packed half2, later dg and du
+    slab_wait_read(c);
+    if (!slab_load2(c, c.mapD, gcol, gcol + 128, c.row0)) return false;
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      uint4 gr = *reinterpret_cast<const uint4*>(p.gu + base + j);
-      uint4 ur = *reinterpret_cast<const uint4*>(p.gu + base + 128 + j);
-      const __half* gh = reinterpret_cast<const __half*>(&gr);
-      const __half* uh = reinterpret_cast<const __half*>(&ur);
-      float dg[8], du[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        const float g = __half2float(gh[t]);
-        const float u = __half2float(uh[t]);
-        const float sig = 1.0f / (1.0f + __expf(-g));
-        const float dy = v[j + t];
-        dg[t] = dy * u * sig * (1.0f + g * (1.0f - sig));
-        du[t] = dy * g * sig;
-      }
-      uint4 wg, wu;
-      wg.x = pack_half2(dg[0], dg[1]); wg.y = pack_half2(dg[2], dg[3]);
-      wg.z = pack_half2(dg[4], dg[5]); wg.w = pack_half2(dg[6], dg[7]);
-      wu.x = pack_half2(du[0], du[1]); wu.y = pack_half2(du[2], du[3]);
-      wu.z = pack_half2(du[4], du[5]); wu.w = pack_half2(du[6], du[7]);
-      *reinterpret_cast<uint4*>(p.dgu + base + j) = wg;
-      *reinterpret_cast<uint4*>(p.dgu + base + 128 + j) = wu;
+    for (int j = 0; j < 8; ++j) {
+      const uint4 w = slab_ld(c, j, 0);
+      gp[4 * j] = w.x; gp[4 * j + 1] = w.y; gp[4 * j + 2] = w.z; gp[4 * j + 3] = w.w;
+      const uint4 x = slab_ld(c, j, 1);
+      up[4 * j] = x.x; up[4 * j + 1] = x.y; up[4 * j + 2] = x.z; up[4 * j + 3] = x.w;
     }
+#pragma unroll
+    for (int t = 0; t < 32; ++t) {
+      const float2 g2 = __half22float2(*reinterpret_cast<const __half2*>(&gp[t]));
+      const float2 u2 = __half22float2(*reinterpret_cast<const __half2*>(&up[t]));
+      const float s0 = 1.0f / (1.0f + __expf(-g2.x)), s1 = 1.0f / (1.0f + __expf(-g2.y));
+      const float d0 = v[2 * t], d1 = v[2 * t + 1];
+      gp[t] = pack_half2(d0 * u2.x * s0 * (1.0f + g2.x * (1.0f - s0)), d1 * u2.y * s1 * (1.0f + g2.y * (1.0f - s1)));
+      up[t] = pack_half2(d0 * g2.x * s0, d1 * g2.y * s1);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      slab_st(c, j, make_uint4(gp[4 * j], gp[4 * j + 1], gp[4 * j + 2], gp[4 * j + 3]), 0);
+      slab_st(c, j, make_uint4(up[4 * j], up[4 * j + 1], up[4 * j + 2], up[4 * j + 3]), 1);
+    }
+    slab_store(c, c.mapC, gcol, c.row0, 0);
+    if (c.lane == 0) {
+      asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                       reinterpret_cast<uint64_t>(c.mapC)),
+                   "r"(c.slab + kSlabBytes), "r"(gcol + 128), "r"(c.row0)
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+    return true;
   }
-  __device__ static void end(State&, const Params&, int, int, int) {}
+  __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
 };
 
 // lm_head pass 1 (src/kernels/loss.cu:24-61 without the [M,V] logits tensor):
-// per row and vocab tile, the running max and sum of exp of the logits, plus
-// the target logit when the target falls in this tile.
+// per row and (vocab tile, column slice), the running max and sum of exp of
+// the logits, plus the target logit when the target falls in this slice.
 struct EpiCEStats {
   struct Params {
     const int* targets;   // [M]
-    float* part_max;      // [M, tiles_n]
-    float* part_sum;      // [M, tiles_n]
+    float* part_max;      // [M, slots]
+    float* part_sum;      // [M, slots]
     float* tgt_logit;     // [M]
-    int tiles_n;
+    int slots;            // vocab tiles x column slices
   };
   struct State { float m, s; int t; };
+  static constexpr int kChunk = 32;
+  static constexpr int kSlab = kSlabBytes;
   static constexpr bool kPaired = false;
-  __device__ static void begin(State& st, const Params& p, int row, int) {
+  static constexpr bool kStores = false;
+  __device__ static void begin(State& st, const Params&, const EpiCtx&, int) {
     st.m = -INFINITY;
     st.s = 0.0f;
     st.t = -1;
-    (void)p;
-    (void)row;
   }
-  __device__ static void chunk(State& st, const Params& p, int row, int col0, int M, int N, const float* v) {
-    if (row >= M || col0 >= N) return;
-    if (st.t < 0) st.t = __ldg(p.targets + row);
-    const int nv = min(32, N - col0);
+  __device__ static bool chunk(State& st, const Params& p, EpiCtx& c, int col0, const float* v) {
+    if (c.row >= c.M || col0 >= c.N) return true;
+    if (st.t < 0) st.t = __ldg(p.targets + c.row);
+    const int nv = min(32, c.N - col0);
     float cm = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 32; ++j)
@@ -245,78 +389,73 @@ struct EpiCEStats {
     if (tj >= 0 && tj < nv) {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (j == tj) p.tgt_logit[row] = v[j];
+        if (j == tj) p.tgt_logit[c.row] = v[j];
     }
+    return true;
   }
-  __device__ static void end(State& st, const Params& p, int row, int tile_n, int M) {
-    if (row >= M) return;
-    p.part_max[static_cast<size_t>(row) * p.tiles_n + tile_n] = st.m;
-    p.part_sum[static_cast<size_t>(row) * p.tiles_n + tile_n] = st.s;
+  __device__ static void end(State& st, const Params& p, const EpiCtx& c, int slot) {
+    if (c.row >= c.M) return;
+    p.part_max[static_cast<size_t>(c.row) * p.slots + slot] = st.m;
+    p.part_sum[static_cast<size_t>(c.row) * p.slots + slot] = st.s;
   }
 };
 
-// lm_head pass 2: dlogits tile = gscale * (softmax - onehot) for rows that
-// count in the loss, 0 for the others; written fp16 into a vocab chunk buffer
-// (columns relative to the chunk start).
+// lm_head pass 2: dlogits chunk = gscale * (softmax - onehot) for rows that
+// count in the loss, 0 for the others; fp16, columns relative to the vocab
+// chunk (mapC covers the chunk buffer).
 struct EpiCEGrad {
   struct Params {
     const int* targets;    // [M]
     const float* lse;      // [M] natural-log LSE
     const uint8_t* valid;  // [M] 1 if the row counts in the loss
-    __half* dl;            // [M, ld] chunk buffer, columns relative to the chunk
-    int ld;
     int col_base;          // vocab id of the chunk's first column
     float gscale;
   };
   struct State { float lse2; int t; int ok; };
+  static constexpr int kChunk = 64;
+  static constexpr int kSlab = kSlabBytes;
   static constexpr bool kPaired = false;
-  __device__ static void begin(State& st, const Params& p, int row, int) {
-    st.ok = 0;
-    (void)p;
-    (void)row;
+  static constexpr bool kStores = true;
+  __device__ static void begin(State& st, const Params& p, const EpiCtx& c, int) {
+    st.ok = 2;
+    st.t = -1;
+    st.lse2 = 0.f;
+    if (c.row < c.M) {
+      st.ok = p.valid[c.row] ? 1 : 2;
+      st.t = __ldg(p.targets + c.row);
+      st.lse2 = p.lse[c.row] * kLog2e;
+    }
   }
-  __device__ static void chunk(State& st, const Params& p, int row, int col0, int M, int N, const float* v) {
-    if (row >= M || col0 >= N) return;
-    if (!st.ok) {
-      st.ok = p.valid[row] ? 1 : 2;
-      st.t = __ldg(p.targets + row);
-      st.lse2 = p.lse[row] * kLog2e;
-    }
-    __half* dst = p.dl + static_cast<size_t>(row) * p.ld + col0;
-    const int nv = min(32, N - col0);
-    const int tl = st.t - p.col_base - col0;  // target column relative to this chunk of 32
-    float d[32];
+  __device__ static bool chunk(State& st, const Params& p, EpiCtx& c, int col0, const float* v) {
+    if (col0 >= c.N) return true;
+    const int tl = st.t - p.col_base - col0;  // target column relative to this chunk
+    slab_wait_read(c);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      float pr = fast_exp2(v[j] * kLog2e - st.lse2);
-      if (j == tl) pr -= 1.0f;
-      d[j] = (st.ok == 1) ? pr * p.gscale : 0.0f;
-    }
-    if (nv == 32) {
+    for (int j = 0; j < 8; ++j) {
+      float d[8];
 #pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint4 w;
-        w.x = pack_half2(d[j], d[j + 1]); w.y = pack_half2(d[j + 2], d[j + 3]);
-        w.z = pack_half2(d[j + 4], d[j + 5]); w.w = pack_half2(d[j + 6], d[j + 7]);
-        *reinterpret_cast<uint4*>(dst + j) = w;
+      for (int t = 0; t < 8; ++t) {
+        float pr = fast_exp2(v[8 * j + t] * kLog2e - st.lse2);
+        if (8 * j + t == tl) pr -= 1.0f;
+        d[t] = (st.ok == 1) ? pr * p.gscale : 0.0f;
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (j < nv) dst[j] = __float2half_rn(d[j]);
+      slab_st(c, j, pack8(d));
     }
+    slab_store(c, c.mapC, col0, c.row0);
+    return true;
   }
-  __device__ static void end(State&, const Params&, int, int, int) {}
+  __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
 };
 
 // ---------------------------------------------------------------- the kernel
 
-template <int BN, int STAGES, class Epi>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+template <int BN, int STAGES, int EW, class Epi>
+__global__ void __launch_bounds__(64 + 32 * EW, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmB0,
                    const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
                    const GemmShape sh, const typename Epi::Params ep, int* err) {
-  using L = GemmSmem<BN, STAGES>;
+  using L = GemmSmem<BN, STAGES, EW, Epi::kSlab>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
@@ -324,7 +463,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* empty = bars + STAGES;          // [STAGES]
   uint64_t* acc_full = bars + 2 * STAGES;   // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* slab_bar = acc_empty + 2;       // [EW]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(slab_bar + EW);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -337,8 +477,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 128);
+      mbar_init(&acc_empty[a], 32 * EW);
     }
+    for (int w = 0; w < EW; ++w) mbar_init(&slab_bar[w], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -362,16 +503,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int nk0 = (sh.K0 + kBlockK - 1) / kBlockK;
   const int nk1 = (sh.K1 + kBlockK - 1) / kBlockK;
   const int nk = nk0 + nk1;
+  const int num_units = sh.num_tiles * sh.splits;  // (tile, K split) work units
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ producer
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < sh.num_tiles && ok; tile += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int tile = u % sh.num_tiles;
+        const int sp = u / sh.num_tiles;
         const int tm = tile % sh.tiles_m;
         const int tn = tile / sh.tiles_m;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int kb_end = min(nk, (sp + 1) * sh.kb_per_split);
+        for (int kb = sp * sh.kb_per_split; kb < kb_end; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t par = ((it / STAGES) & 1) ^ 1;
           if (!mbar_wait(&empty[s], par, abort_flag, err, kErrWaitConsumer)) { ok = false; break; }
@@ -407,12 +552,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int it = 0;
       int i = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < sh.num_tiles && ok; tile += gridDim.x, ++i) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++i) {
         const int acc = i & 1;
         if (!mbar_wait(&acc_empty[acc], ((i >> 1) & 1) ^ 1, abort_flag, err, kErrWaitEpilogue)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int sp = u / sh.num_tiles;
+        const int kb_begin = sp * sh.kb_per_split;
+        const int kb_end = min(nk, kb_begin + sh.kb_per_split);
+        for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
           const int s = it % STAGES;
           if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag, err, kErrWaitProducer)) { ok = false; break; }
           tc_fence_after();
@@ -423,7 +571,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int k = 0; k < kBlockK / 16; ++k) {
             // +32 bytes per 16-element K step inside the 128-byte swizzle row
-            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb != kb_begin || k != 0) ? 1u : 0u);
           }
           umma_commit(&empty[s]);
         }
@@ -432,43 +580,72 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // -------------------------------------------------------------- epilogue
-    const int ew = warp & 3;  // TMEM lane quadrant this warp may access
+    static_assert(EW == 4 || EW == 8, "4 or 8 epilogue warps");
+    constexpr int kGroups = EW / 4;           // warps sharing one lane quadrant
+    constexpr int kCols = BN / kGroups;       // accumulator columns per warp
+    constexpr int kChunk = Epi::kChunk;
+    static_assert(kCols % kChunk == 0 || Epi::kPaired, "column slice must hold whole chunks");
+    const int ew = warp & 3;                  // TMEM lane quadrant this warp may access
+    const int cgrp = (warp - 2) / 4;          // which column slice of the tile
     const uint32_t lane_off = static_cast<uint32_t>(ew * 32) << 16;
+    EpiCtx c;
+    c.lane = lane;
+    c.M = sh.M;
+    c.N = sh.N;
+    c.slab = smem_u32(smem + L::kSlabOffset + (warp - 2) * Epi::kSlab);
+    c.bar = &slab_bar[warp - 2];
+    c.phase = 0;
+    c.abort_flag = abort_flag;
+    c.err = err;
+    c.mapC = &tmC;
+    c.mapD = &tmD;
     int i = 0;
-    for (int tile = blockIdx.x; tile < sh.num_tiles; tile += gridDim.x, ++i) {
+    bool ok = true;
+    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++i) {
       const int acc = i & 1;
       if (!mbar_wait(&acc_full[acc], (i >> 1) & 1, abort_flag, err, kErrWaitAccum)) break;
       tc_fence_after();
+      const int tile = u % sh.num_tiles;
+      const int sp = u / sh.num_tiles;
       const int tm = tile % sh.tiles_m;
       const int tn = tile / sh.tiles_m;
-      const int row = tm * kBlockM + ew * 32 + lane;
+      c.row0 = (sp * sh.tiles_m + tm) * kBlockM + ew * 32;  // split s -> its own row block of partials
+      c.row = c.row0 + lane;
       const uint32_t tbase = tmem_base + lane_off + acc * BN;
       typename Epi::State st;
-      Epi::begin(st, ep, row, tn);
+      const int slot = tn * kGroups + cgrp;  // per-(tile, column slice) id for row-state epilogues
+      Epi::begin(st, ep, c, slot);
       if constexpr (!Epi::kPaired) {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase + c, r);
+        for (int cc = cgrp * kCols; cc < (cgrp + 1) * kCols && ok; cc += kChunk) {
+          float v[kChunk];
+#pragma unroll
+          for (int q = 0; q < kChunk / 32; ++q)
+            tmem_ld_32x32b_x32(tbase + cc + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * q));
           tmem_ld_wait();
-          Epi::chunk(st, ep, row, tn * BN + c, sh.M, sh.N, reinterpret_cast<const float*>(r));
+          ok = Epi::chunk(st, ep, c, tn * BN + cc, v);
         }
       } else {
         static_assert(BN == 256, "paired epilogue needs 256-wide tiles");
+        constexpr int kPairCols = 128 / kGroups;
 #pragma unroll 1
-        for (int c = 0; c < 128; c += 32) {
-          uint32_t rg[32], ru[32];
-          tmem_ld_32x32b_x32(tbase + c, rg);
-          tmem_ld_32x32b_x32(tbase + 128 + c, ru);
+        for (int cc = cgrp * kPairCols; cc < (cgrp + 1) * kPairCols && ok; cc += kChunk) {
+          float g[kChunk], u[kChunk];
+#pragma unroll
+          for (int q = 0; q < kChunk / 32; ++q) {
+            tmem_ld_32x32b_x32(tbase + cc + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(g + 32 * q));
+            tmem_ld_32x32b_x32(tbase + 128 + cc + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(u + 32 * q));
+          }
           tmem_ld_wait();
-          Epi::pair(st, ep, row, tn, c, sh.M, reinterpret_cast<const float*>(rg),
-                    reinterpret_cast<const float*>(ru));
+          ok = Epi::pair(st, ep, c, tn, cc, g, u);
         }
       }
-      Epi::end(st, ep, row, tn, sh.M);
+      Epi::end(st, ep, c, slot);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
     }
+    if (Epi::kStores && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
   }
 
   tc_fence_before();

@@ -74,8 +74,17 @@ __global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __r
 }
 
 // dx = r * (dy*w - c*x), c = r^2/H * sum(dy*w*x)   (src/kernels/rmsnorm.cu:53-90)
-// dres = (accumulate ? dres : 0) + dx ; dres16 = fp16(dres)
-__global__ void rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+// dres = (accumulate ? dres : 0) + dx ; dres16 = fp16(dres).  dy is fp32 or fp16.
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ld4(const __half* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+template <class DY>
+__global__ void rmsnorm_bwd_kernel(const DY* __restrict__ dy, const float* __restrict__ x,
                                    const float* __restrict__ w, float* __restrict__ dres,
                                    __half* __restrict__ dres16, int M, int H, float eps, int accumulate) {
   const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
@@ -84,9 +93,9 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __
   const size_t base = static_cast<size_t>(m) * H;
   float ss = 0.f, dot = 0.f;
   for (int c = lane * 4; c < H; c += 128) {
-    float4 xv = *reinterpret_cast<const float4*>(x + base + c);
-    float4 dv = *reinterpret_cast<const float4*>(dy + base + c);
-    float4 g = *reinterpret_cast<const float4*>(w + c);
+    float4 xv = ld4(x + base + c);
+    float4 dv = ld4(dy + base + c);
+    float4 g = ld4(w + c);
     ss += xv.x * xv.x + xv.y * xv.y + xv.z * xv.z + xv.w * xv.w;
     dot += dv.x * g.x * xv.x + dv.y * g.y * xv.y + dv.z * g.z * xv.z + dv.w * g.w * xv.w;
   }
@@ -95,9 +104,9 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __
   const float r = rsqrtf(ss / static_cast<float>(H) + eps);
   const float cc = r * r / static_cast<float>(H) * dot;
   for (int c = lane * 4; c < H; c += 128) {
-    float4 xv = *reinterpret_cast<const float4*>(x + base + c);
-    float4 dv = *reinterpret_cast<const float4*>(dy + base + c);
-    float4 g = *reinterpret_cast<const float4*>(w + c);
+    float4 xv = ld4(x + base + c);
+    float4 dv = ld4(dy + base + c);
+    float4 g = ld4(w + c);
     float4 o = make_float4(r * (dv.x * g.x - cc * xv.x), r * (dv.y * g.y - cc * xv.y), r * (dv.z * g.z - cc * xv.z),
                            r * (dv.w * g.w - cc * xv.w));
     if (accumulate) {
@@ -128,14 +137,49 @@ __global__ void rope_table_kernel(float* cos_t, float* sin_t, int S, int hd, flo
 
 // One warp per (token, head).  q heads then k heads.  Per-head RMSNorm with
 // the q_norm / k_norm gain, then the half-split rotation of pairs (d, d+hd/2)
-// (src/kernels/lora_forward.cu:233-237, src/kernels/rope.cu:26-35).
+// (src/kernels/lora_forward.cu:233-237, src/kernels/rope.cu:26-35).  Lane l
+// owns the kV consecutive elements d = kV*l .. of each half (kV = hd/64).
+template <int HD>
+struct QkVec {
+  static constexpr int kHalf = HD / 2;
+  static constexpr int kV = HD / 64;  // consecutive elements per lane per half
+};
+
+template <int HD>
+__device__ __forceinline__ void ld_h(const __half* p, float (&x)[HD / 64]) {
+  if constexpr (HD / 64 == 2) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(p));
+    x[0] = f.x;
+    x[1] = f.y;
+  } else {
+    x[0] = __half2float(*p);
+  }
+}
+template <int HD>
+__device__ __forceinline__ void st_h(__half* p, const float (&x)[HD / 64]) {
+  if constexpr (HD / 64 == 2) {
+    *reinterpret_cast<__half2*>(p) = __floats2half2_rn(x[0], x[1]);
+  } else {
+    *p = __float2half_rn(x[0]);
+  }
+}
+template <int HD>
+__device__ __forceinline__ void ld_f(const float* p, float (&x)[HD / 64]) {
+  if constexpr (HD / 64 == 2) {
+    const float2 f = *reinterpret_cast<const float2*>(p);
+    x[0] = f.x;
+    x[1] = f.y;
+  } else {
+    x[0] = *p;
+  }
+}
+
 template <int HD>
 __global__ void qknorm_rope_fwd_kernel(const __half* __restrict__ qkv, int ld, const float* __restrict__ qn_w,
                                        const float* __restrict__ kn_w, const float* __restrict__ cos_t,
                                        const float* __restrict__ sin_t, __half* __restrict__ q_out,
                                        __half* __restrict__ k_out, int M, int S, int nh, int nkv, float eps) {
-  constexpr int kHalf = HD / 2;
-  constexpr int kPer = kHalf / 32;  // pairs per lane
+  constexpr int kHalf = QkVec<HD>::kHalf, kV = QkVec<HD>::kV;
   const int w = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int nhead = nh + nkv;
@@ -144,29 +188,32 @@ __global__ void qknorm_rope_fwd_kernel(const __half* __restrict__ qkv, int ld, c
   const bool isq = hh < nh;
   const __half* src = qkv + static_cast<size_t>(m) * ld + (isq ? hh * HD : nh * HD + (hh - nh) * HD);
   const float* gw = isq ? qn_w : kn_w;
-  float x0[kPer], x1[kPer];
+  const int d = lane * kV;
+  float x0[kV], x1[kV];
+  ld_h<HD>(src + d, x0);
+  ld_h<HD>(src + d + kHalf, x1);
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    const int d = lane + 32 * i;
-    x0[i] = __half2float(src[d]);
-    x1[i] = __half2float(src[d + kHalf]);
-    ss += x0[i] * x0[i] + x1[i] * x1[i];
-  }
+  for (int i = 0; i < kV; ++i) ss += x0[i] * x0[i] + x1[i] * x1[i];
   ss = warp_sum(ss);
   const float r = rsqrtf(ss / static_cast<float>(HD) + eps);
   const int pos = m % S;
+  float c[kV], s[kV], w0[kV], w1[kV], y0[kV], y1[kV];
+  ld_f<HD>(cos_t + pos * kHalf + d, c);
+  ld_f<HD>(sin_t + pos * kHalf + d, s);
+  ld_f<HD>(gw + d, w0);
+  ld_f<HD>(gw + d + kHalf, w1);
+#pragma unroll
+  for (int i = 0; i < kV; ++i) {
+    const float a = x0[i] * r * w0[i];
+    const float b = x1[i] * r * w1[i];
+    y0[i] = a * c[i] - b * s[i];
+    y1[i] = b * c[i] + a * s[i];
+  }
   __half* dst = isq ? q_out + static_cast<size_t>(m) * nh * HD + hh * HD
                     : k_out + static_cast<size_t>(m) * nkv * HD + (hh - nh) * HD;
-#pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    const int d = lane + 32 * i;
-    const float a = x0[i] * r * gw[d];
-    const float b = x1[i] * r * gw[d + kHalf];
-    const float c = cos_t[pos * kHalf + d], s = sin_t[pos * kHalf + d];
-    dst[d] = __float2half_rn(a * c - b * s);
-    dst[d + kHalf] = __float2half_rn(b * c + a * s);
-  }
+  st_h<HD>(dst + d, y0);
+  st_h<HD>(dst + d + kHalf, y1);
 }
 
 // Inverse rotation (src/kernels/rope.cu:57-83) then the per-head RMSNorm
@@ -178,8 +225,7 @@ __global__ void qknorm_rope_bwd_kernel(const float* __restrict__ dq, const float
                                        const float* __restrict__ kn_w, const float* __restrict__ cos_t,
                                        const float* __restrict__ sin_t, __half* __restrict__ dqkv, int M, int S,
                                        int nh, int nkv, float eps) {
-  constexpr int kHalf = HD / 2;
-  constexpr int kPer = kHalf / 32;
+  constexpr int kHalf = QkVec<HD>::kHalf, kV = QkVec<HD>::kV;
   const int w = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int nhead = nh + nkv;
@@ -192,17 +238,21 @@ __global__ void qknorm_rope_bwd_kernel(const float* __restrict__ dq, const float
                        : dk + static_cast<size_t>(m) * nkv * HD + (hh - nh) * HD;
   const float* gw = isq ? qn_w : kn_w;
   const int pos = m % S;
-  float x0[kPer], x1[kPer], d0[kPer], d1[kPer];
+  const int d = lane * kV;
+  float x0[kV], x1[kV], g0[kV], g1[kV], c[kV], s[kV], w0[kV], w1[kV], d0[kV], d1[kV];
+  ld_h<HD>(xs + d, x0);
+  ld_h<HD>(xs + d + kHalf, x1);
+  ld_f<HD>(g + d, g0);
+  ld_f<HD>(g + d + kHalf, g1);
+  ld_f<HD>(cos_t + pos * kHalf + d, c);
+  ld_f<HD>(sin_t + pos * kHalf + d, s);
+  ld_f<HD>(gw + d, w0);
+  ld_f<HD>(gw + d + kHalf, w1);
   float ss = 0.f, dot = 0.f;
 #pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    const int d = lane + 32 * i;
-    x0[i] = __half2float(xs[d]);
-    x1[i] = __half2float(xs[d + kHalf]);
-    const float g0 = g[d], g1 = g[d + kHalf];
-    const float c = cos_t[pos * kHalf + d], s = sin_t[pos * kHalf + d];
-    d0[i] = (g0 * c + g1 * s) * gw[d];          // d(normed) * w
-    d1[i] = (g1 * c - g0 * s) * gw[d + kHalf];
+  for (int i = 0; i < kV; ++i) {
+    d0[i] = (g0[i] * c[i] + g1[i] * s[i]) * w0[i];  // d(normed) * w
+    d1[i] = (g1[i] * c[i] - g0[i] * s[i]) * w1[i];
     ss += x0[i] * x0[i] + x1[i] * x1[i];
     dot += d0[i] * x0[i] + d1[i] * x1[i];
   }
@@ -210,13 +260,15 @@ __global__ void qknorm_rope_bwd_kernel(const float* __restrict__ dq, const float
   dot = warp_sum(dot);
   const float r = rsqrtf(ss / static_cast<float>(HD) + eps);
   const float cc = r * r / static_cast<float>(HD) * dot;
-  __half* dst = dqkv + static_cast<size_t>(m) * ld + col;
+  float y0[kV], y1[kV];
 #pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    const int d = lane + 32 * i;
-    dst[d] = __float2half_rn(r * (d0[i] - cc * x0[i]));
-    dst[d + kHalf] = __float2half_rn(r * (d1[i] - cc * x1[i]));
+  for (int i = 0; i < kV; ++i) {
+    y0[i] = r * (d0[i] - cc * x0[i]);
+    y1[i] = r * (d1[i] - cc * x1[i]);
   }
+  __half* dst = dqkv + static_cast<size_t>(m) * ld + col;
+  st_h<HD>(dst + d, y0);
+  st_h<HD>(dst + d + kHalf, y1);
 }
 
 // ------------------------------------------------------- cross-entropy
@@ -439,8 +491,16 @@ cudaError_t rmsnorm_forward(const float* x, const float* w, __half* out, int M, 
 cudaError_t rmsnorm_backward(const float* dy, const float* x, const float* w, float* dres, __half* dres16, int M,
                              int H, float eps, int accumulate, cudaStream_t st) {
   if (H % 4) return cudaErrorInvalidValue;
-  rmsnorm_bwd_kernel<<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(dy, x, w, dres, dres16, M, H, eps,
-                                                                                  accumulate);
+  rmsnorm_bwd_kernel<float><<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(dy, x, w, dres, dres16, M, H,
+                                                                                         eps, accumulate);
+  return cudaGetLastError();
+}
+
+cudaError_t rmsnorm_backward(const __half* dy, const float* x, const float* w, float* dres, __half* dres16, int M,
+                             int H, float eps, int accumulate, cudaStream_t st) {
+  if (H % 4) return cudaErrorInvalidValue;
+  rmsnorm_bwd_kernel<__half><<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(dy, x, w, dres, dres16, M,
+                                                                                          H, eps, accumulate);
   return cudaGetLastError();
 }
 

@@ -85,6 +85,7 @@ struct llmcu_ctx {
   __half* lderived = nullptr;
   float* lpart = nullptr;
   int lpart_amax = 0;
+  float* skinny_ws = nullptr;  // split-K partials of the N = 64 LoRA GEMMs
 
   // activations
   std::vector<float*> resid;  // L + 1 buffers
@@ -96,7 +97,8 @@ struct llmcu_ctx {
   float* d_xf = nullptr;
   int ce_tiles = 0;
   // backward scratch
-  float *dres = nullptr, *dxn = nullptr, *dq = nullptr, *dk = nullptr, *delta = nullptr;
+  float *dres = nullptr, *dq = nullptr, *dk = nullptr, *delta = nullptr;
+  __half* dxn = nullptr;  // dX of the normed inputs (fp16, feeds the RMSNorm backward)
   __half *dres16 = nullptr, *dgu = nullptr, *dho = nullptr, *dattn = nullptr, *dqkv = nullptr, *dhq = nullptr;
   // io
   int *tok = nullptr, *tgt = nullptr, *derr = nullptr;
@@ -245,7 +247,8 @@ void carve(llmcu_ctx* c, Carver& cv) {
   c->lv = cv.take<float>(n);
   c->lderived = cv.take<__half>(static_cast<size_t>(c->ld.derived_per_layer) * L);
   c->lpart_amax = static_cast<int>((std::max({H, Q, KV}) + 63) / 64 * 64);
-  c->lpart = cv.take<float>(static_cast<size_t>(kLoraMaxSplits) * kLoraMaxProbs * c->lpart_amax * 16);
+  c->lpart = cv.take<float>(static_cast<size_t>(kLoraMaxSplits) * kLoraMaxProbs * c->lpart_amax * 64);
+  c->skinny_ws = cv.take<float>(gemm_skinny_ws_floats(static_cast<int>(M), 64));
   // activations
   for (size_t l = 0; l <= L; ++l) c->resid[l] = cv.take<float>(M * H);
   const size_t lse_n = static_cast<size_t>(c->rc.max_batch) * c->nh * c->rc.max_seq;
@@ -265,7 +268,7 @@ void carve(llmcu_ctx* c, Carver& cv) {
     a.lse = cv.take<float>(lse_n);
   }
   c->xf = cv.take<__half>(M * H);
-  c->ce_tiles = static_cast<int>((V + 255) / 256);
+  c->ce_tiles = static_cast<int>((V + 255) / 256) * kGemmEpiGroups;
   c->part_max = cv.take<float>(M * c->ce_tiles);
   c->part_sum = cv.take<float>(M * c->ce_tiles);
   c->tgt_logit = cv.take<float>(M);
@@ -277,7 +280,7 @@ void carve(llmcu_ctx* c, Carver& cv) {
   c->d_xf = cv.take<float>(M * H);
   c->dres = cv.take<float>(M * H);
   c->dres16 = cv.take<__half>(M * H);
-  c->dxn = cv.take<float>(M * H);
+  c->dxn = cv.take<__half>(M * H);
   c->dgu = cv.take<__half>(M * 2 * I);
   c->dho = cv.take<__half>(M * 64);
   c->dattn = cv.take<__half>(M * Q);
@@ -442,8 +445,7 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     const __half* D = ctx->lderived + d.derived_per_layer * l;
     const float* x = ctx->resid[l];
     TIMED(P_NORM, rmsnorm_forward(x, w.attn_norm, a.xn, M, H, eps, st));
-    TIMED(P_GEMM, gemm(op(a.xn, M, H, H), op(D + d.d_acat, 64, H, H), kNone, kNone, M, 64, Epi::kStoreF16,
-            EpiArgs{a.hq, 64}, err, st));
+    TIMED(P_GEMM, gemm_skinny(op(a.xn, M, H, H), op(D + d.d_acat, 64, H, H), M, 64, a.hq, 64, ctx->skinny_ws, err, st));
     const __half* wqkv = fwd_weight(ctx, w.wqkv, w.q_qkv, w.s_qkv, QKV, H, &e);
     CK(e);
     TIMED(P_GEMM, gemm(op(a.xn, M, H, H), op(wqkv, QKV, H, H), op(a.hq, M, 64, 64), op(D + d.d_bblk, QKV, 64, 64), M, QKV,
@@ -452,8 +454,7 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
                            ctx->nh, ctx->nkv, ctx->hd, eps, st));
     TIMED(P_ATTN_FWD, attention_forward(a.qrope, a.krope, a.qkv + Q + KV, a.attn, a.lse, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV,
                          QKV, Q, st));
-    TIMED(P_GEMM, gemm(op(a.attn, M, Q, Q), op(D + d.d_ao, 64, Q, Q), kNone, kNone, M, 64, Epi::kStoreF16, EpiArgs{a.ho, 64},
-            err, st));
+    TIMED(P_GEMM, gemm_skinny(op(a.attn, M, Q, Q), op(D + d.d_ao, 64, Q, Q), M, 64, a.ho, 64, ctx->skinny_ws, err, st));
     const __half* wo = fwd_weight(ctx, w.wo, w.q_o, w.s_o, H, Q, &e);
     CK(e);
     {
@@ -538,12 +539,11 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     }
     const __half* wguT = bwd_weight(ctx, w.wguT, w.qT_gu, w.s_gu, H, 2 * I, &e);
     CK(e);
-    TIMED(P_GEMM, gemm(op(ctx->dgu, M, 2 * I, 2 * I), op(wguT, H, 2 * I, 2 * I), kNone, kNone, M, H, Epi::kStoreF32,
+    TIMED(P_GEMM, gemm(op(ctx->dgu, M, 2 * I, 2 * I), op(wguT, H, 2 * I, 2 * I), kNone, kNone, M, H, Epi::kStoreF16,
             EpiArgs{ctx->dxn, H}, err, st));
     TIMED(P_NORM, rmsnorm_backward(ctx->dxn, a.resid_mid, w.ffn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
     // O projection
-    TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op(D + d.d_boT, 64, H, H), kNone, kNone, M, 64, Epi::kStoreF16,
-            EpiArgs{ctx->dho, 64}, err, st));
+    TIMED(P_GEMM, gemm_skinny(op(ctx->dres16, M, H, H), op(D + d.d_boT, 64, H, H), M, 64, ctx->dho, 64, ctx->skinny_ws, err, st));
     const __half* woT = bwd_weight(ctx, w.woT, w.qT_o, w.s_o, Q, H, &e);
     CK(e);
     TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op(woT, Q, H, H), op(ctx->dho, M, 64, 64), op(D + d.d_aoT, Q, 64, 64), M, Q,
@@ -553,9 +553,9 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       gb.n = 2;
       gb.a_max = ctx->lpart_amax;
       // dBo[h, j] = s * sum_m dres[m, h] ho[m, j]
-      gb.p[0] = LoraGradProb{ctx->dres16, H, a.ho, 64, G + d.oBo, r, 1, H, r, d.scale * unscale};
+      gb.p[0] = LoraGradProb{ctx->dres16, H, a.ho, 64, {G + d.oBo}, 1, r, 1, H, r, d.scale * unscale};
       // dAo[j, q] = sum_m dho[m, j] attn[m, q]
-      gb.p[1] = LoraGradProb{a.attn, Q, ctx->dho, 64, G + d.oAo, 1, Q, Q, r, unscale};
+      gb.p[1] = LoraGradProb{a.attn, Q, ctx->dho, 64, {G + d.oAo}, 1, 1, Q, Q, r, unscale};
       TIMED(P_LORA_GRAD, lora_grad(gb, M, ctx->lpart, st));
     }
     // attention
@@ -564,23 +564,21 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     TIMED(P_NORM, qknorm_rope_backward(ctx->dq, ctx->dk, a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, ctx->dqkv,
                             B, S, ctx->nh, ctx->nkv, ctx->hd, eps, st));
     // QKV projection
-    TIMED(P_GEMM, gemm(op(ctx->dqkv, M, QKV, QKV), op(D + d.d_bblkT, 64, QKV, QKV), kNone, kNone, M, 64, Epi::kStoreF16,
-            EpiArgs{ctx->dhq, 64}, err, st));
+    TIMED(P_GEMM, gemm_skinny(op(ctx->dqkv, M, QKV, QKV), op(D + d.d_bblkT, 64, QKV, QKV), M, 64, ctx->dhq, 64, ctx->skinny_ws, err, st));
     const __half* wqkvT = bwd_weight(ctx, w.wqkvT, w.qT_qkv, w.s_qkv, H, QKV, &e);
     CK(e);
     TIMED(P_GEMM, gemm(op(ctx->dqkv, M, QKV, QKV), op(wqkvT, H, QKV, QKV), op(ctx->dhq, M, 64, 64), op(D + d.d_acatT, H, 64, 64),
-            M, H, Epi::kStoreF32, EpiArgs{ctx->dxn, H}, err, st));
+            M, H, Epi::kStoreF16, EpiArgs{ctx->dxn, H}, err, st));
     {
       LoraGradBatch gb{};
-      gb.n = 6;
+      gb.n = 4;
       gb.a_max = ctx->lpart_amax;
       const float sb = d.scale * unscale;
-      gb.p[0] = LoraGradProb{ctx->dqkv, QKV, a.hq, 64, G + d.oBq, r, 1, Q, r, sb};
-      gb.p[1] = LoraGradProb{ctx->dqkv + Q, QKV, a.hq + kSegK, 64, G + d.oBk, r, 1, KV, r, sb};
-      gb.p[2] = LoraGradProb{ctx->dqkv + Q + KV, QKV, a.hq + kSegV, 64, G + d.oBv, r, 1, KV, r, sb};
-      gb.p[3] = LoraGradProb{a.xn, H, ctx->dhq, 64, G + d.oAq, 1, H, H, r, unscale};
-      gb.p[4] = LoraGradProb{a.xn, H, ctx->dhq + kSegK, 64, G + d.oAk, 1, H, H, r, unscale};
-      gb.p[5] = LoraGradProb{a.xn, H, ctx->dhq + kSegV, 64, G + d.oAv, 1, H, H, r, unscale};
+      gb.p[0] = LoraGradProb{ctx->dqkv, QKV, a.hq, 64, {G + d.oBq}, 1, r, 1, Q, r, sb};
+      gb.p[1] = LoraGradProb{ctx->dqkv + Q, QKV, a.hq + kSegK, 64, {G + d.oBk}, 1, r, 1, KV, r, sb};
+      gb.p[2] = LoraGradProb{ctx->dqkv + Q + KV, QKV, a.hq + kSegV, 64, {G + d.oBv}, 1, r, 1, KV, r, sb};
+      // dA_q, dA_k, dA_v in one pass over the normed input (column groups 0 / 16 / 32 of dh)
+      gb.p[3] = LoraGradProb{a.xn, H, ctx->dhq, 64, {G + d.oAq, G + d.oAk, G + d.oAv}, 3, 1, H, H, r, unscale};
       TIMED(P_LORA_GRAD, lora_grad(gb, M, ctx->lpart, st));
     }
     TIMED(P_NORM, rmsnorm_backward(ctx->dxn, ctx->resid[l], w.attn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));

@@ -89,14 +89,14 @@ constexpr int kLgThreads = 128;
 constexpr int kLgA = 64;   // a-rows per CTA (4 warps x 16)
 constexpr int kLgM = 64;   // m per smem stage
 
-__device__ __forceinline__ uint32_t uoff(int m, int c) {  // [64 m][64 a] tile, 8 chunks per row
+__device__ __forceinline__ uint32_t uoff(int m, int c) {  // [64 m][64 cols] tile, 8 chunks per row
   return static_cast<uint32_t>((m * 8 + (c ^ (m & 7))) * 16);
 }
 
 __global__ void __launch_bounds__(kLgThreads) lora_grad_kernel(const LoraGradBatch batch, int M, int splits,
                                                               float* __restrict__ part) {
   __shared__ __align__(128) uint8_t su[2][kLgM * kLgA * 2];
-  __shared__ __align__(128) uint8_t sw[2][kLgM * 16 * 2];
+  __shared__ __align__(128) uint8_t sw[2][kLgM * 64 * 2];
   const LoraGradProb& pb = batch.p[blockIdx.y];
   const int a0 = blockIdx.x * kLgA;
   if (a0 >= pb.A) return;
@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(kLgThreads) lora_grad_kernel(const LoraGradBat
   const int m_begin = split * m_per;
   const int m_end = min(M, m_begin + m_per);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ng = pb.groups;
 
   auto load = [&](int buf, int m0) {
     const uint32_t su_b = smem_u32(su[buf]);
@@ -115,17 +116,15 @@ __global__ void __launch_bounds__(kLgThreads) lora_grad_kernel(const LoraGradBat
       const bool ok = m < m_end && (a0 + c * 8) < pb.A;
       const __half* src = pb.U + static_cast<size_t>(ok ? m : m_begin) * pb.ldu + (ok ? a0 + c * 8 : 0);
       cp_async_16(su_b + uoff(mm, c), src, ok ? 16 : 0);
-    }
-    for (int i = threadIdx.x; i < kLgM * 2; i += kLgThreads) {
-      const int mm = i >> 1, c = i & 1;
-      const int m = m0 + mm;
-      const bool ok = m < m_end;
-      const __half* src = pb.W + static_cast<size_t>(ok ? m : m_begin) * pb.ldw + c * 8;
-      cp_async_16(sw_b + mm * 32 + c * 16, src, ok ? 16 : 0);
+      const bool okw = m < m_end && c < 2 * ng;
+      const __half* srcw = pb.W + static_cast<size_t>(okw ? m : m_begin) * pb.ldw + (okw ? c * 8 : 0);
+      cp_async_16(sw_b + uoff(mm, c), srcw, okw ? 16 : 0);
     }
   };
 
-  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  float acc[8][4];
+#pragma unroll
+  for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
   const int nsteps = m_end > m_begin ? (m_end - m_begin + kLgM - 1) / kLgM : 0;
   if (nsteps > 0) load(0, m_begin);
   cp_async_commit();
@@ -143,38 +142,45 @@ __global__ void __launch_bounds__(kLgThreads) lora_grad_kernel(const LoraGradBat
       uint32_t a[4];
       ldmatrix_x4_trans(su_b + uoff(kk * 16 + (mi >> 1) * 8 + (lane & 7), warp * 2 + (mi & 1)), a[0], a[1], a[2],
                         a[3]);
-      uint32_t b0, b1, b2, b3;
-      ldmatrix_x4_trans(sw_b + (kk * 16 + (mi & 1) * 8 + (lane & 7)) * 32 + (mi >> 1) * 16, b0, b1, b2, b3);
-      mma_16816(acc[0], a, b0, b1);
-      mma_16816(acc[1], a, b2, b3);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        if (g < ng) {
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4_trans(sw_b + uoff(kk * 16 + (mi & 1) * 8 + (lane & 7), 2 * g + (mi >> 1)), b0, b1, b2, b3);
+          mma_16816(acc[2 * g], a, b0, b1);
+          mma_16816(acc[2 * g + 1], a, b2, b3);
+        }
+      }
     }
     __syncthreads();
   }
   cp_async_wait<0>();
 
-  // partial tile [64 a][16 b] for (split, problem, a-block)
-  const int g = lane >> 2, t = lane & 3;
-  float* pp = part + ((static_cast<size_t>(split) * batch.n + blockIdx.y) * batch.a_max + a0) * 16;
+  // partial tile [64 a][64 b] for (split, problem, a-block)
+  const int gq = lane >> 2, t = lane & 3;
+  float* pp = part + ((static_cast<size_t>(split) * batch.n + blockIdx.y) * batch.a_max + a0) * 64;
 #pragma unroll
-  for (int n = 0; n < 2; ++n) {
+  for (int n = 0; n < 8; ++n) {
+    if (n < 2 * ng) {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int a = warp * 16 + g + (e >> 1) * 8;
-      const int b = n * 8 + 2 * t + (e & 1);
-      pp[a * 16 + b] = acc[n][e];
+      for (int e = 0; e < 4; ++e) {
+        const int a = warp * 16 + gq + (e >> 1) * 8;
+        const int b = n * 8 + 2 * t + (e & 1);
+        pp[a * 64 + b] = acc[n][e];
+      }
     }
   }
 }
 
 __global__ void lora_grad_reduce_kernel(const LoraGradBatch batch, int splits, const float* __restrict__ part) {
   const LoraGradProb& pb = batch.p[blockIdx.y];
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;  // a * 16 + b
-  const int a = idx >> 4, b = idx & 15;
-  if (a >= pb.A || b >= pb.Bn) return;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;  // a * 64 + (16 g + b)
+  const int a = idx >> 6, gb = idx & 63, g = gb >> 4, b = gb & 15;
+  if (a >= pb.A || g >= pb.groups || b >= pb.Bn) return;
   float s = 0.f;
   for (int sp = 0; sp < splits; ++sp)
-    s += part[((static_cast<size_t>(sp) * batch.n + blockIdx.y) * batch.a_max + a) * 16 + b];
-  pb.out[static_cast<size_t>(a) * pb.sa + static_cast<size_t>(b) * pb.sb] = s * pb.scale;
+    s += part[((static_cast<size_t>(sp) * batch.n + blockIdx.y) * batch.a_max + a) * 64 + gb];
+  pb.out[g][static_cast<size_t>(a) * pb.sa + static_cast<size_t>(b) * pb.sb] = s * pb.scale;
 }
 
 }  // namespace
@@ -203,7 +209,7 @@ cudaError_t lora_grad(const LoraGradBatch& batch, int M, float* part, cudaStream
   const int splits = lora_grad_splits(M, batch.a_max, batch.n);
   dim3 grid((batch.a_max + kLgA - 1) / kLgA, batch.n, splits);
   lora_grad_kernel<<<grid, kLgThreads, 0, st>>>(batch, M, splits, part);
-  dim3 g2((batch.a_max * 16 + 255) / 256, batch.n);
+  dim3 g2((batch.a_max * 64 + 255) / 256, batch.n);
   lora_grad_reduce_kernel<<<g2, 256, 0, st>>>(batch, splits, part);
   return cudaGetLastError();
 }

@@ -56,14 +56,17 @@ constexpr int kSegK = 16;
 constexpr int kSegV = 32;
 constexpr int kLoraMaxSplits = 16;
 
-// C[a, b] = scale * sum_m U[m, a] * W[m, b]  for a < A, b < Bn (<= 16);
-// stored at out[a * sa + b * sb].
+// C[a, 16*g + b] = scale * sum_m U[m, a] * W[m, 16*g + b]  for a < A,
+// g < groups (<= 4), b < Bn (<= 16); group g is stored at
+// out[g][a * sa + b * sb].  One pass over U serves every group, so the three
+// dA of q/k/v (which share the normed input) read it once.
 struct LoraGradProb {
   const __half* U;
   int ldu;
-  const __half* W;
+  const __half* W;  // 64 columns are read from here on (the padded LoRA width)
   int ldw;
-  float* out;
+  float* out[4];
+  int groups;
   int sa, sb;
   int A, Bn;
   float scale;
