@@ -573,10 +573,8 @@ cudaError_t attn_bwd_launch(const __half* q, const __half* k, const __half* v, c
 }  // namespace
 
 cudaError_t attention_forward(const __half* q, const __half* k, const __half* v, __half* o, float* lse, int B, int S,
-                              int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, cudaStream_t st) {
-  if (hd == 128) return attn_fwd_launch<128>(q, k, v, o, lse, B, S, nh, nkv, ldq, ldk, ldv, ldo, st);
-  if (hd == 64) return attn_fwd_launch<64>(q, k, v, o, lse, B, S, nh, nkv, ldq, ldk, ldv, ldo, st);
-  return cudaErrorInvalidValue;
+                              int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int* err, cudaStream_t st) {
+  return attention_forward_tc(q, k, v, o, lse, B, S, nh, nkv, hd, ldq, ldk, ldv, ldo, err, st);
 }
 
 cudaError_t attention_backward(const __half* q, const __half* k, const __half* v, const __half* o,

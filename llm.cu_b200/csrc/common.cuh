@@ -12,7 +12,11 @@ namespace llmcu {
 
 // ---- attention.cu
 cudaError_t attention_forward(const __half* q, const __half* k, const __half* v, __half* o, float* lse, int B, int S,
-                              int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, cudaStream_t st);
+                              int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int* err, cudaStream_t st);
+// ---- attention_tc.cu
+cudaError_t attention_forward_tc(const __half* q, const __half* k, const __half* v, __half* o, float* lse, int B,
+                                 int S, int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int* err,
+                                 cudaStream_t st);
 cudaError_t attention_backward(const __half* q, const __half* k, const __half* v, const __half* o,
                                const __half* dout, const float* lse, float* delta, float* dq, float* dk, __half* dv,
                                int B, int S, int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int lddq,

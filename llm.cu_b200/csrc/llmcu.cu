@@ -453,7 +453,7 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     TIMED(P_NORM, qknorm_rope_forward(a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, a.qrope, a.krope, B, S,
                            ctx->nh, ctx->nkv, ctx->hd, eps, st));
     TIMED(P_ATTN_FWD, attention_forward(a.qrope, a.krope, a.qkv + Q + KV, a.attn, a.lse, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV,
-                         QKV, Q, st));
+                         QKV, Q, err, st));
     TIMED(P_GEMM, gemm_skinny(op(a.attn, M, Q, Q), op(D + d.d_ao, 64, Q, Q), M, 64, a.ho, 64, ctx->skinny_ws, err, st));
     const __half* wo = fwd_weight(ctx, w.wo, w.q_o, w.s_o, H, Q, &e);
     CK(e);
@@ -1282,7 +1282,7 @@ llmcu_status llmcu_attention_fwd(const void* q, const void* k, const void* v, vo
     return LLMCU_ERR_INVALID_ARG;
   cudaError_t e = attention_forward(static_cast<const __half*>(q), static_cast<const __half*>(k),
                                     static_cast<const __half*>(v), static_cast<__half*>(o), lse, batch, seq, n_heads,
-                                    n_kv_heads, head_dim, ldq, ldk, ldv, n_heads * head_dim,
+                                    n_kv_heads, head_dim, ldq, ldk, ldv, n_heads * head_dim, nullptr,
                                     static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LLMCU_OK : (e == cudaErrorInvalidValue ? LLMCU_ERR_UNSUPPORTED : LLMCU_ERR_CUDA);
 }
