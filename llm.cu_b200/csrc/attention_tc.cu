@@ -1,4 +1,4 @@
-// attention_tc.cu -- causal GQA flash attention forward on tcgen05 / TMEM.
+// attention_tc.cu -- causal GQA flash attention on tcgen05 / TMEM (forward and backward).
 //
 // One CTA per (128-row query tile, query head, sequence), 192 threads:
 //   warp 0     TMA producer: Q once, then (K_j, V_j) 128-row tiles in a 2-deep ring
@@ -286,6 +286,299 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ------------------------------------------------------------- backward
+// One CTA per (128-row key tile, KV head, sequence), 192 threads:
+//   warp 0     TMA producer: K, V once; then per iteration one (Q, dO) tile
+//   warp 1     MMA issuer:   S^T = K Q^T and dP^T = V dO^T; then dV += P^T dO,
+//                            dK += dS^T Q and dQ_part = dS K (dS read from the
+//                            dS^T tile as an MN-major operand)
+//   warps 2-5  softmax:      thread r owns key row r: P^T = exp(S^T - LSE),
+//                            dS^T = P^T (dP^T - delta) into shared memory;
+//                            then, as query row r, drains dQ_part into the
+//                            global fp32 dQ with TMA reduce-add
+// Iterations run over the query heads of the KV group and the query tiles at
+// or after the key tile (causal).  TMEM: S^T / dQ_part [0,128), dP^T
+// [128,256), dV [256, 256+hd), dK [256+hd, 256+2hd).
+template <int HD>
+struct BwdLayout {
+  static constexpr int kT = 128 * HD * 2;       // K, V, Q or dO tile
+  static constexpr int kP = 128 * 128 * 2;      // P^T or dS^T tile
+  static constexpr int kKOff = 0;
+  static constexpr int kVOff = kKOff + kT;
+  static constexpr int kQOff = kVOff + kT;
+  static constexpr int kOOff = kQOff + kT;      // dO
+  static constexpr int kPOff = kOOff + kT;      // P^T (later the dQ drain slabs)
+  static constexpr int kSOff = kPOff + kP;      // dS^T
+  static constexpr int kLOff = kSOff + kP;      // lse*log2e [128], delta [128]
+  static constexpr int kBarOff = kLOff + 2 * 128 * 4;
+  static constexpr int kBytes = kBarOff + 256 + 1024;
+};
+
+__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int HD>
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                       const __grid_constant__ CUtensorMap tmDQ, const float* __restrict__ lse,
+                       const float* __restrict__ delta, float* __restrict__ dk, __half* __restrict__ dv, int S,
+                       int nh, int nkv, int lddk, int lddv, float scale, float scale_log2, int* err) {
+  using L = BwdLayout<HD>;
+  constexpr int kDBoxes = HD / 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* kv_full = bars;
+  uint64_t* q_full = bars + 1;
+  uint64_t* q_free = bars + 2;
+  uint64_t* s_full = bars + 3;
+  uint64_t* p_full = bars + 4;
+  uint64_t* dq_full = bars + 5;
+  uint64_t* dq_free = bars + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* sL = reinterpret_cast<float*>(smem + L::kLOff);
+  float* sD = sL + 128;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkt = gridDim.x;
+  const int kt = blockIdx.x;  // heavy (early) key tiles launch first
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int G = nh / nkv;
+  const int nqt = (S + 127) / 128;
+  const int per_head = nqt - kt;
+  const int n_it = G * per_head;
+  const int row_base = b * S;
+  (void)nkt;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(q_full, 1);
+    mbar_init(q_free, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 128);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s = tmem, t_dp = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 256 + HD;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmO);
+      mbar_arrive_expect_tx(kv_full, 2 * L::kT);
+      for (int i = 0; i < kDBoxes; ++i) {
+        tma_load_2d(smem + L::kKOff + i * kBox, &tmK, kv_full, kvh * HD + 64 * i, row_base + kt * 128);
+        tma_load_2d(smem + L::kVOff + i * kBox, &tmV, kv_full, kvh * HD + 64 * i, row_base + kt * 128);
+      }
+      for (int it = 0; it < n_it; ++it) {
+        const int hq = kvh * G + it / per_head;
+        const int qt = kt + it % per_head;
+        if (it >= 1 && !mbar_wait(q_free, (it - 1) & 1, abort_flag, err, kErrWaitConsumer)) break;
+        mbar_arrive_expect_tx(q_full, 2 * L::kT);
+        for (int i = 0; i < kDBoxes; ++i) {
+          tma_load_2d(smem + L::kQOff + i * kBox, &tmQ, q_full, hq * HD + 64 * i, row_base + qt * 128);
+          tma_load_2d(smem + L::kOOff + i * kBox, &tmO, q_full, hq * HD + 64 * i, row_base + qt * 128);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      constexpr uint32_t idesc_s = idesc_f16_f32(128, 128);                       // K-major x K-major
+      constexpr uint32_t idesc_acc = idesc_f16_f32(128, HD) | (1u << 16);          // B MN-major
+      constexpr uint32_t idesc_dq = idesc_f16_f32(128, HD) | (1u << 15) | (1u << 16);  // A, B MN-major
+      const uint32_t sk = smem_u32(smem + L::kKOff), sv = smem_u32(smem + L::kVOff);
+      const uint32_t sq = smem_u32(smem + L::kQOff), so = smem_u32(smem + L::kOOff);
+      const uint32_t sp = smem_u32(smem + L::kPOff), ss = smem_u32(smem + L::kSOff);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, err, kErrWaitProducer);
+      for (int it = 0; it < n_it && ok; ++it) {
+        if (!mbar_wait(q_full, it & 1, abort_flag, err, kErrWaitProducer)) { ok = false; break; }
+        if (it >= 1 && !mbar_wait(dq_free, (it - 1) & 1, abort_flag, err, kErrWaitEpilogue)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint32_t off = (k >> 2) * kBox + (k & 3) * 32;
+          umma_f16(t_s, sw128_kmajor_desc(sk + off), sw128_kmajor_desc(sq + off), idesc_s, k > 0 ? 1u : 0u);
+          umma_f16(t_dp, sw128_kmajor_desc(sv + off), sw128_kmajor_desc(so + off), idesc_s, k > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, it & 1, abort_flag, err, kErrWaitProducer)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 128 / 16; ++k) {
+          const uint32_t offp = (k >> 2) * kBox + (k & 3) * 32;  // K-major over the 128 query columns
+          umma_f16(t_dv, sw128_kmajor_desc(sp + offp), sw128_mnmajor_desc(so + k * 2048), idesc_acc,
+                   (it > 0 || k > 0) ? 1u : 0u);
+          umma_f16(t_dk, sw128_kmajor_desc(ss + offp), sw128_mnmajor_desc(sq + k * 2048), idesc_acc,
+                   (it > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(q_free);
+#pragma unroll
+        for (int k = 0; k < 128 / 16; ++k)
+          umma_f16(t_s, sw128_mnmajor_desc(ss + k * 2048), sw128_mnmajor_desc(sk + k * 2048), idesc_dq,
+                   k > 0 ? 1u : 0u);
+        umma_commit(dq_full);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- softmax
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;             // key row (phase 1) / query row (drain)
+    const int kr = kt * 128 + r;              // key position
+    const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
+    uint8_t* sP = smem + L::kPOff;
+    uint8_t* sS = smem + L::kSOff;
+    bool ok = true;
+    for (int it = 0; it < n_it && ok; ++it) {
+      const int hq = kvh * G + it / per_head;
+      const int qt = kt + it % per_head;
+      const int q0 = qt * 128;
+      {  // this query tile's lse * log2(e) and delta, shared by all key rows
+        const int qq = q0 + r;
+        const size_t idx = (static_cast<size_t>(b) * nh + hq) * S + qq;
+        sL[r] = qq < S ? lse[idx] * kLog2e : INFINITY;
+        sD[r] = qq < S ? delta[idx] : 0.f;
+      }
+      named_sync_softmax();
+      if (!mbar_wait(s_full, it & 1, abort_flag, err, kErrWaitAccum)) { ok = false; break; }
+      tc_fence_after();
+      // the previous drain's TMA reduce must have read the slabs before P^T is rewritten
+      if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      __syncwarp();
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {  // 32 query columns at a time
+        uint32_t sv[32], dv32[32];
+        tmem_ld_32x32b_x32(t_s + lane_off + 32 * c, sv);
+        tmem_ld_32x32b_x32(t_dp + lane_off + 32 * c, dv32);
+        tmem_ld_wait();
+        uint32_t pp[16], dsp[16];
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int qc = 32 * c + t + e;
+            const int qq = q0 + qc;
+            float p = fast_exp2(__uint_as_float(sv[t + e]) * scale_log2 - sL[qc]);
+            if (qq < kr || qq >= S || kr >= S) p = 0.f;
+            pv[e] = p;
+            dsv[e] = p * (__uint_as_float(dv32[t + e]) - sD[qc]);
+          }
+          pp[t / 2] = pack_half2(pv[0], pv[1]);
+          dsp[t / 2] = pack_half2(dsv[0], dsv[1]);
+        }
+        // row r of P^T / dS^T: query columns 32c.. -> box c/2, 16-byte chunks 4(c%2)..
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int ch = 4 * (c & 1) + u;
+          const uint32_t off = (c >> 1) * kBox + r * 128 + ((ch ^ (r & 7)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(sP + off)), "r"(pp[4 * u]),
+                       "r"(pp[4 * u + 1]), "r"(pp[4 * u + 2]), "r"(pp[4 * u + 3])
+                       : "memory");
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(sS + off)), "r"(dsp[4 * u]),
+                       "r"(dsp[4 * u + 1]), "r"(dsp[4 * u + 2]), "r"(dsp[4 * u + 3])
+                       : "memory");
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(p_full);
+      // ---- drain dQ_part (query row r of this tile) into the global dQ
+      if (!mbar_wait(dq_full, it & 1, abort_flag, err, kErrWaitAccum)) { ok = false; break; }
+      tc_fence_after();
+      const bool valid = q0 + r < S;
+      const uint32_t slab = smem_u32(sP + qd * 4096);  // 32 rows x 32 fp32, inside this warp's P^T rows
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t dqv[32];
+        tmem_ld_32x32b_x32(t_s + lane_off + 32 * c, dqv);
+        tmem_ld_wait();
+        if (c > 0) {
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          __syncwarp();
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float f0 = valid ? __uint_as_float(dqv[4 * j]) * scale : 0.f;
+          const float f1 = valid ? __uint_as_float(dqv[4 * j + 1]) * scale : 0.f;
+          const float f2 = valid ? __uint_as_float(dqv[4 * j + 2]) * scale : 0.f;
+          const float f3 = valid ? __uint_as_float(dqv[4 * j + 3]) * scale : 0.f;
+          const uint32_t a = slab + lane * 128 + ((j ^ (lane & 7)) << 4);
+          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(f0), "f"(f1), "f"(f2), "f"(f3)
+                       : "memory");
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          asm volatile(
+              "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                  reinterpret_cast<uint64_t>(&tmDQ)),
+              "r"(slab), "r"(hq * HD + 32 * c), "r"(row_base + q0 + qd * 32)
+              : "memory");
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);
+      named_sync_softmax();  // every row done with sL / sD before the next tile overwrites them
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
+    // ---- dK (scaled) and dV of key row r
+    if (ok && n_it > 0) {
+      tc_fence_after();
+      const bool valid = kr < S;
+      float* dkrow = dk + static_cast<size_t>(row_base + kr) * lddk + kvh * HD;
+      __half* dvrow = dv + static_cast<size_t>(row_base + kr) * lddv + kvh * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t a[32], bvv[32];
+        tmem_ld_32x32b_x32(t_dk + lane_off + 32 * c, a);
+        tmem_ld_32x32b_x32(t_dv + lane_off + 32 * c, bvv);
+        tmem_ld_wait();
+        if (valid) {
+#pragma unroll
+          for (int t = 0; t < 32; t += 4)
+            *reinterpret_cast<float4*>(dkrow + 32 * c + t) =
+                make_float4(__uint_as_float(a[t]) * scale, __uint_as_float(a[t + 1]) * scale,
+                            __uint_as_float(a[t + 2]) * scale, __uint_as_float(a[t + 3]) * scale);
+#pragma unroll
+          for (int t = 0; t < 32; t += 8) {
+            uint4 w;
+            w.x = pack_half2(__uint_as_float(bvv[t]), __uint_as_float(bvv[t + 1]));
+            w.y = pack_half2(__uint_as_float(bvv[t + 2]), __uint_as_float(bvv[t + 3]));
+            w.z = pack_half2(__uint_as_float(bvv[t + 4]), __uint_as_float(bvv[t + 5]));
+            w.w = pack_half2(__uint_as_float(bvv[t + 6]), __uint_as_float(bvv[t + 7]));
+            *reinterpret_cast<uint4*>(dvrow + 32 * c + t) = w;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -311,6 +604,48 @@ bool tile_map(CUtensorMap* m, const __half* p, int rows, int cols, int ld) {
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// [rows, cols] fp32, box 32 columns x 32 rows (one drain slab), 128-B swizzle.
+bool f32_slab_map(CUtensorMap* m, const float* p, int rows, int cols, int ld) {
+  auto enc = encoder();
+  if (!enc || reinterpret_cast<uintptr_t>(p) % 16 || (ld * 4) % 16) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
+  cuuint32_t box[2] = {32u, 32u};
+  cuuint32_t es[2] = {1u, 1u};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int HD>
+cudaError_t bwd_tc_launch(const __half* q, const __half* k, const __half* v, const __half* dout, const float* lse,
+                          const float* delta, float* dq, float* dk, __half* dv, int B, int S, int nh, int nkv,
+                          int ldq, int ldk, int ldv, int ldo, int lddq, int lddk, int lddv, int* err,
+                          cudaStream_t st) {
+  using L = BwdLayout<HD>;
+  CUtensorMap mq, mk, mv, mo, mdq;
+  if (!tile_map(&mq, q, B * S, nh * HD, ldq) || !tile_map(&mk, k, B * S, nkv * HD, ldk) ||
+      !tile_map(&mv, v, B * S, nkv * HD, ldv) || !tile_map(&mo, dout, B * S, nh * HD, ldo) ||
+      !f32_slab_map(&mdq, dq, B * S, nh * HD, lddq))
+    return cudaErrorInvalidValue;
+  auto kern = attn_bwd_tc_kernel<HD>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  // dQ accumulates partial products of every key tile
+  cudaError_t e = cudaMemset2DAsync(dq, static_cast<size_t>(lddq) * 4, 0, static_cast<size_t>(nh) * HD * 4,
+                                    static_cast<size_t>(B) * S, st);
+  if (e != cudaSuccess) return e;
+  dim3 grid((S + 127) / 128, nkv, B);
+  const float scale = 1.0f / sqrtf(static_cast<float>(HD));
+  kern<<<grid, 192, L::kBytes, st>>>(mq, mk, mv, mo, mdq, lse, delta, dk, dv, S, nh, nkv, lddk, lddv, scale,
+                                     scale * kLog2e, err);
+  return cudaGetLastError();
+}
+
 template <int HD>
 cudaError_t fwd_tc_launch(const __half* q, const __half* k, const __half* v, __half* o, float* lse, int B, int S,
                           int nh, int nkv, int ldq, int ldk, int ldv, int ldo, int* err, cudaStream_t st) {
@@ -333,6 +668,19 @@ cudaError_t fwd_tc_launch(const __half* q, const __half* k, const __half* v, __h
 }
 
 }  // namespace
+
+cudaError_t attention_backward_tc(const __half* q, const __half* k, const __half* v, const __half* dout,
+                                  const float* lse, const float* delta, float* dq, float* dk, __half* dv, int B, int S,
+                                  int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int lddq, int lddk,
+                                  int lddv, int* err, cudaStream_t st) {
+  if (hd == 128)
+    return bwd_tc_launch<128>(q, k, v, dout, lse, delta, dq, dk, dv, B, S, nh, nkv, ldq, ldk, ldv, ldo, lddq, lddk,
+                              lddv, err, st);
+  if (hd == 64)
+    return bwd_tc_launch<64>(q, k, v, dout, lse, delta, dq, dk, dv, B, S, nh, nkv, ldq, ldk, ldv, ldo, lddq, lddk,
+                             lddv, err, st);
+  return cudaErrorInvalidValue;
+}
 
 cudaError_t attention_forward_tc(const __half* q, const __half* k, const __half* v, __half* o, float* lse, int B,
                                  int S, int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int* err,

@@ -17,10 +17,15 @@ cudaError_t attention_forward(const __half* q, const __half* k, const __half* v,
 cudaError_t attention_forward_tc(const __half* q, const __half* k, const __half* v, __half* o, float* lse, int B,
                                  int S, int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int* err,
                                  cudaStream_t st);
+// dO.O row sums into `delta`, then attention_backward_tc (dq is overwritten).
 cudaError_t attention_backward(const __half* q, const __half* k, const __half* v, const __half* o,
                                const __half* dout, const float* lse, float* delta, float* dq, float* dk, __half* dv,
                                int B, int S, int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int lddq,
-                               int lddk, int lddv, cudaStream_t st);
+                               int lddk, int lddv, int* err, cudaStream_t st);
+cudaError_t attention_backward_tc(const __half* q, const __half* k, const __half* v, const __half* dout,
+                                  const float* lse, const float* delta, float* dq, float* dk, __half* dv, int B, int S,
+                                  int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int lddq, int lddk,
+                                  int lddv, int* err, cudaStream_t st);
 
 // ---- gemm.cu
 // Column slices per GEMM tile (epilogue warps per TMEM lane quadrant); the

@@ -560,7 +560,7 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     }
     // attention
     TIMED(P_ATTN_BWD, attention_backward(a.qrope, a.krope, a.qkv + Q + KV, a.attn, ctx->dattn, a.lse, ctx->delta, ctx->dq, ctx->dk,
-                          ctx->dqkv + Q + KV, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV, QKV, Q, Q, KV, QKV, st));
+                          ctx->dqkv + Q + KV, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV, QKV, Q, Q, KV, QKV, err, st));
     TIMED(P_NORM, qknorm_rope_backward(ctx->dq, ctx->dk, a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, ctx->dqkv,
                             B, S, ctx->nh, ctx->nkv, ctx->hd, eps, st));
     // QKV projection
@@ -1299,7 +1299,7 @@ llmcu_status llmcu_attention_bwd(const void* q, const void* k, const void* v, co
       static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v),
       static_cast<const __half*>(o), static_cast<const __half*>(dout), lse, scratch_delta, dq, dk,
       static_cast<__half*>(dv), batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk, ldv, ldo, ldo,
-      n_kv_heads * head_dim, lddv, static_cast<cudaStream_t>(stream));
+      n_kv_heads * head_dim, lddv, nullptr, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LLMCU_OK : (e == cudaErrorInvalidValue ? LLMCU_ERR_UNSUPPORTED : LLMCU_ERR_CUDA);
 }
 
