@@ -23,6 +23,7 @@ enum DeviceErr : int {
   kErrWaitEpilogue = 1 << 3,  // MMA warp: accumulator never drained
   kErrTokenRange = 1 << 4,    // token / target id outside [0, vocab)
   kErrShape = 1 << 5,         // launch shape the kernel does not handle
+  kErrWaitPeer = 1 << 6,      // GEMM tail: another CTA's partial never arrived
 };
 
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;  // 4 s
@@ -93,7 +94,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // ----------------------------------------------------------------------- TMA
 // 2-D tiled load of one box into shared memory; completion is signalled as
 // transaction bytes on `bar`.  x is the innermost (contiguous) coordinate.
-// No multicast: every CTA fetches its own tiles.
+// Every CTA fetches its own tiles; no copy is shared across a cluster.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x,
                                             int y) {
   asm volatile(
@@ -160,6 +161,20 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 columns of 32-bit registers into TMEM (the store mirror of the load above).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor for a K-major tile written by TMA with
 // 128-byte swizzle: rows of 128 B, 8-row (1024 B) swizzle atoms stacked

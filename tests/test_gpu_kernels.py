@@ -21,19 +21,22 @@ def rel_l2(a, b):
     return float((a - b).norm() / b.norm().clamp_min(1e-30))
 
 
+# (4096, 2048, *) leave a partial last wave that runs split along K (the
+# tail split); every shape runs twice to check the split's counters re-arm.
 @pytest.mark.parametrize("M,N,K", [(4096, 4096, 2048), (32, 64, 256), (200, 300, 200), (128, 151936 // 8, 2048),
-                                   (1000, 2048, 6144)])
+                                   (1000, 2048, 6144), (4096, 2048, 2048), (4096, 2048, 12288), (640, 12288, 2048)])
 def test_gemm_nt_matches_torch(llmcu, cuda_device, M, N, K):
     g = torch.Generator(device="cpu").manual_seed(M * 7 + N)
     A = torch.randn(M, K, generator=g).half().to(cuda_device)
     B = torch.randn(N, K, generator=g).half().to(cuda_device)
-    C = torch.full((M, N), float("nan"), device=cuda_device, dtype=torch.float32)
-    llmcu.gemm_nt_f16(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, K, K, N,
-                      torch.cuda.current_stream().cuda_stream)
-    torch.cuda.synchronize()
     ref = A.float() @ B.float().t()
-    assert torch.isfinite(C).all()
-    assert rel_l2(C, ref) < 1e-3
+    for _ in range(2):
+        C = torch.full((M, N), float("nan"), device=cuda_device, dtype=torch.float32)
+        llmcu.gemm_nt_f16(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, K, K, N,
+                          torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert torch.isfinite(C).all()
+        assert rel_l2(C, ref) < 1e-3
 
 
 def _attn_ref(q, k, v, B, S, nh, nkv, hd):
