@@ -297,8 +297,8 @@ struct BwdLayout {
   static constexpr int kOOff = kQOff + kT;      // dO
   static constexpr int kPOff = kOOff + kT;      // P^T (later the dQ drain slabs)
   static constexpr int kSOff = kPOff + kP;      // dS^T
-  static constexpr int kLOff = kSOff + kP;      // lse*log2e [128], delta [128]
-  static constexpr int kBarOff = kLOff + 2 * 128 * 4;
+  static constexpr int kLOff = kSOff + kP;      // 2 x (lse*log2e [128], delta [128])
+  static constexpr int kBarOff = kLOff + 4 * 128 * 4;
   static constexpr int kBytes = kBarOff + 256 + 1024;
 };
 
@@ -326,7 +326,6 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* sL = reinterpret_cast<float*>(smem + L::kLOff);
-  float* sD = sL + 128;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkt = gridDim.x;
@@ -431,17 +430,29 @@ __global__ void __launch_bounds__(192, 1)
     uint8_t* sP = smem + L::kPOff;
     uint8_t* sS = smem + L::kSOff;
     bool ok = true;
+    // lse * log2(e) and delta of query row r of iteration `it`, loaded one
+    // iteration ahead into registers and published through a double buffer
+    auto stats = [&](int it, float& l2, float& dl) {
+      const int hq = kvh * G + it / per_head;
+      const int qq = (kt + it % per_head) * 128 + r;
+      const size_t idx = (static_cast<size_t>(b) * nh + hq) * S + qq;
+      l2 = qq < S ? lse[idx] * kLog2e : INFINITY;
+      dl = qq < S ? delta[idx] : 0.f;
+    };
+    float l_next = 0.f, d_next = 0.f;
+    if (n_it > 0) stats(0, l_next, d_next);
     for (int it = 0; it < n_it && ok; ++it) {
       const int hq = kvh * G + it / per_head;
       const int qt = kt + it % per_head;
       const int q0 = qt * 128;
-      {  // this query tile's lse * log2(e) and delta, shared by all key rows
-        const int qq = q0 + r;
-        const size_t idx = (static_cast<size_t>(b) * nh + hq) * S + qq;
-        sL[r] = qq < S ? lse[idx] * kLog2e : INFINITY;
-        sD[r] = qq < S ? delta[idx] : 0.f;
-      }
+      float* sLb = sL + (it & 1) * 256;  // lse of this tile's query columns
+      float* sDb = sLb + 128;            // delta
+      sLb[r] = l_next;
+      sDb[r] = d_next;
+      // one barrier per iteration: rows of sL[it & 1] were last read in
+      // iteration it - 2, which every thread finished before arriving here
       named_sync_softmax();
+      if (it + 1 < n_it) stats(it + 1, l_next, d_next);
       if (!mbar_wait(s_full, it & 1, abort_flag, err, kErrWaitAccum)) { ok = false; break; }
       tc_fence_after();
       // the previous drain's TMA reduce must have read the slabs before P^T is rewritten
@@ -461,10 +472,10 @@ __global__ void __launch_bounds__(192, 1)
           for (int e = 0; e < 2; ++e) {
             const int qc = 32 * c + t + e;
             const int qq = q0 + qc;
-            float p = fast_exp2(__uint_as_float(sv[t + e]) * scale_log2 - sL[qc]);
+            float p = fast_exp2(__uint_as_float(sv[t + e]) * scale_log2 - sLb[qc]);
             if (qq < kr || qq >= S || kr >= S) p = 0.f;
             pv[e] = p;
-            dsv[e] = p * (__uint_as_float(dv32[t + e]) - sD[qc]);
+            dsv[e] = p * (__uint_as_float(dv32[t + e]) - sDb[qc]);
           }
           pp[t / 2] = pack_half2(pv[0], pv[1]);
           dsp[t / 2] = pack_half2(dsv[0], dsv[1]);
@@ -489,16 +500,15 @@ __global__ void __launch_bounds__(192, 1)
       if (!mbar_wait(dq_full, it & 1, abort_flag, err, kErrWaitAccum)) { ok = false; break; }
       tc_fence_after();
       const bool valid = q0 + r < S;
-      const uint32_t slab = smem_u32(sP + qd * 4096);  // 32 rows x 32 fp32, inside this warp's P^T rows
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
+        // chunk c of this warp's 32 rows -> its own 4 KB slab inside the P^T /
+        // dS^T tiles (free once dQ_part is committed), so the reduce-adds of
+        // all chunks are in flight together
+        const uint32_t slab = smem_u32(sP + (c * 4 + qd) * 4096);
         uint32_t dqv[32];
         tmem_ld_32x32b_x32(t_s + lane_off + 32 * c, dqv);
         tmem_ld_wait();
-        if (c > 0) {
-          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-          __syncwarp();
-        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float f0 = valid ? __uint_as_float(dqv[4 * j]) * scale : 0.f;
@@ -522,7 +532,6 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_before();
       mbar_arrive(dq_free);
-      named_sync_softmax();  // every row done with sL / sD before the next tile overwrites them
     }
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     __syncwarp();
