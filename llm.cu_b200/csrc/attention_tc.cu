@@ -74,8 +74,10 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = gridDim.x - 1 - blockIdx.x;  // longest (causal) tiles first
-  const int h = blockIdx.y, b = blockIdx.z;
+  // blocks start in linear order (x fastest): every (head, sequence) of the
+  // longest causal query tile first, so short tiles fill the last wave
+  const int qt = gridDim.z - 1 - blockIdx.z;
+  const int h = blockIdx.x, b = blockIdx.y;
   const int kvh = h / (nh / nkv);
   const int n_kv = qt + 1;
   const int row_base = b * S;
@@ -328,9 +330,11 @@ __global__ void __launch_bounds__(192, 1)
   float* sL = reinterpret_cast<float*>(smem + L::kLOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nkt = gridDim.x;
-  const int kt = blockIdx.x;  // heavy (early) key tiles launch first
-  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int nkt = gridDim.z;
+  // blocks start in linear order (x fastest): key tile 0 (the most query
+  // tiles after it) of every (KV head, sequence) first
+  const int kt = blockIdx.z;
+  const int kvh = blockIdx.x, b = blockIdx.y;
   const int G = nh / nkv;
   const int nqt = (S + 127) / 128;
   const int per_head = nqt - kt;
@@ -636,7 +640,7 @@ cudaError_t bwd_tc_launch(const __half* q, const __half* k, const __half* v, con
   cudaError_t e = cudaMemset2DAsync(dq, static_cast<size_t>(lddq) * 4, 0, static_cast<size_t>(nh) * HD * 4,
                                     static_cast<size_t>(B) * S, st);
   if (e != cudaSuccess) return e;
-  dim3 grid((S + 127) / 128, nkv, B);
+  dim3 grid(nkv, B, (S + 127) / 128);
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));
   kern<<<grid, 192, L::kBytes, st>>>(mq, mk, mv, mo, mdq, lse, delta, dk, dv, S, nh, nkv, lddk, lddv, scale,
                                      scale * kLog2e, err);
@@ -658,7 +662,7 @@ cudaError_t fwd_tc_launch(const __half* q, const __half* k, const __half* v, __h
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  dim3 grid((S + kTq - 1) / kTq, nh, B);
+  dim3 grid(nh, B, (S + kTq - 1) / kTq);
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));
   kern<<<grid, 192, L::kBytes, st>>>(mq, mk, mv, o, lse, S, nh, nkv, ldo, scale * kLog2e, err);
   return cudaGetLastError();
