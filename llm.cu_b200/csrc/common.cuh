@@ -46,8 +46,7 @@ enum class Epi : int {
   kResidF32 = 2,
   kSwiGLU = 3,
   kSwiGLUBwd = 4,
-  kCEStats = 5,
-  kCEGrad = 6,
+  kCEProbs = 5,  // lm_head forward: slot max / sum-exp partials + slot-relative probabilities
 };
 
 struct EpiArgs {
@@ -55,6 +54,7 @@ struct EpiArgs {
   void* out = nullptr;
   int ld_out = 0;
   int accumulate = 0;
+  int ksplit = 1;  // kStoreF32 with accumulate: K slices that reduce-add into the same output
   const float* resid = nullptr;
   // SwiGLU
   __half* gu = nullptr;       // interleaved [M, 2I]
@@ -67,10 +67,6 @@ struct EpiArgs {
   float* part_max = nullptr;
   float* part_sum = nullptr;
   float* tgt_logit = nullptr;
-  const float* lse = nullptr;
-  const uint8_t* valid = nullptr;
-  int col_base = 0;
-  float gscale = 1.f;
 };
 
 // C[M,N] = A0 . B0^T (+ A1 . B1^T) with the given epilogue.  A*.rows = M,
@@ -103,6 +99,11 @@ cudaError_t qknorm_rope_backward(const float* dq, const float* dk, const __half*
                                  int S, int nh, int nkv, int hd, float eps, cudaStream_t st);
 cudaError_t rope_tables(float* cos_t, float* sin_t, int S, int hd, float theta, cudaStream_t st);
 // row_loss_and_sum: [M] per-row losses followed by their sum at [M]
+// In place: slot-relative probabilities p = exp(l - m_slot) (fp16, from the
+// kCEProbs GEMM) -> dlogits = gscale * (p * exp(m_slot - lse) - onehot) for
+// rows that count in the loss, 0 for the others (src/kernels/loss.cu:62-69).
+cudaError_t ce_dlogits(__half* p, int ldp, int M, int V, const float* part_max, int slots, const float* lse,
+                       const uint8_t* valid, const int* targets, float gscale, cudaStream_t st);
 cudaError_t ce_reduce(const float* part_max, const float* part_sum, const float* tgt_logit, const uint8_t* valid,
                       float* lse, float* row_loss_and_sum, int M, int tiles_n, cudaStream_t st);
 cudaError_t ce_valid_rows(uint8_t* valid, const int* targets, int B, int S, int all_positions, int V, int* err,

@@ -106,13 +106,13 @@ cudaError_t dispatch(Epi epi, const EpiArgs& ea, const CUtensorMap* maps, const 
       return launch<BN, EpiResidF32>(maps, sh, EpiResidF32::Params{}, err, st);
     case Epi::kSwiGLUBwd:
       return launch<BN, EpiSwiGLUBwd>(maps, sh, EpiSwiGLUBwd::Params{}, err, st);
-    case Epi::kCEStats: {
-      EpiCEStats::Params p{ea.targets, ea.part_max, ea.part_sum, ea.tgt_logit, sh.tiles_n * (epi_warps<BN>() / 4)};
-      return launch<BN, EpiCEStats>(maps, sh, p, err, st);
-    }
-    case Epi::kCEGrad: {
-      EpiCEGrad::Params p{ea.targets, ea.lse, ea.valid, ea.col_base, ea.gscale};
-      return launch<BN, EpiCEGrad>(maps, sh, p, err, st);
+    case Epi::kCEProbs: {
+      if constexpr (BN == 256) {
+        EpiCEProbs::Params p{ea.targets, ea.part_max, ea.part_sum, ea.tgt_logit, sh.tiles_n * (epi_warps<BN>() / 4)};
+        return launch<BN, EpiCEProbs>(maps, sh, p, err, st);
+      } else {
+        return cudaErrorInvalidValue;
+      }
     }
     case Epi::kSwiGLU: {
       if constexpr (BN == 256) {
@@ -140,7 +140,8 @@ cudaError_t gemm(const Operand& A0, const Operand& B0, const Operand& A1, const 
   int BN = bn_hint;
   if (BN == 0) BN = (epi == Epi::kSwiGLU) ? 256 : (N <= 64 ? 64 : (N <= 128 ? 128 : 256));
   if (epi == Epi::kSwiGLU && BN != 256) return cudaErrorInvalidValue;
-  if (epi == Epi::kCEStats && BN != 256) return cudaErrorInvalidValue;  // partial slots assume 256-wide tiles
+  if (epi == Epi::kCEProbs && BN != 256) return cudaErrorInvalidValue;  // partial slots assume 256-wide tiles
+  if (ea.ksplit > 1 && (epi != Epi::kStoreF32 || !ea.accumulate)) return cudaErrorInvalidValue;
   CUtensorMap maps[6];  // A0, B0, A1, B1, C, D
   if (!make_map(&maps[0], A0, kBlockM) || !make_map(&maps[1], B0, BN)) return cudaErrorInvalidValue;
   if (A1.k > 0) {
@@ -152,7 +153,7 @@ cudaError_t gemm(const Operand& A0, const Operand& B0, const Operand& A1, const 
   bool okc = true;
   switch (epi) {
     case Epi::kStoreF16:
-    case Epi::kCEGrad:
+    case Epi::kCEProbs:
       okc = make_io_map(&maps[4], ea.out, M, N, ea.ld_out, false);
       maps[5] = maps[4];
       break;
@@ -172,10 +173,6 @@ cudaError_t gemm(const Operand& A0, const Operand& B0, const Operand& A1, const 
       okc = make_io_map(&maps[4], ea.gu, M, 2 * N, ea.ld_gu, false) &&
             make_io_map(&maps[5], ea.gu_in, M, 2 * N, ea.ld_gu, false);
       break;
-    case Epi::kCEStats:
-      maps[4] = maps[0];
-      maps[5] = maps[0];
-      break;
   }
   if (!okc) return cudaErrorInvalidValue;
   GemmShape sh;
@@ -188,6 +185,13 @@ cudaError_t gemm(const Operand& A0, const Operand& B0, const Operand& A1, const 
   sh.num_tiles = sh.tiles_m * sh.tiles_n;
   sh.splits = 1;
   sh.kb_per_split = (A0.k + kBlockK - 1) / kBlockK + (A1.k + kBlockK - 1) / kBlockK;
+  sh.split_row_tiles = 0;
+  if (ea.ksplit > 1) {  // K slices reduce-add into the same rows
+    const int nk = sh.kb_per_split;
+    const int kbps = (nk + ea.ksplit - 1) / ea.ksplit;
+    sh.kb_per_split = kbps;
+    sh.splits = (nk + kbps - 1) / kbps;
+  }
   switch (BN) {
     case 64: return dispatch<64>(epi, ea, maps, sh, err, st);
     case 128: return dispatch<128>(epi, ea, maps, sh, err, st);
@@ -249,6 +253,7 @@ cudaError_t gemm_skinny(const Operand& A, const Operand& B, int M, int N, __half
   sh.num_tiles = tiles_m;
   sh.splits = splits;
   sh.kb_per_split = kbps;
+  sh.split_row_tiles = tiles_m;
   cudaError_t e = launch<64, EpiStoreF32>(maps, sh, EpiStoreF32::Params{0}, err, st);
   if (e != cudaSuccess) return e;
   const int pairs = M * (N / 2);

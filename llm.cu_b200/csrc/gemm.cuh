@@ -26,6 +26,8 @@
 // CTAs that run together share the weight (B) tile and stream it once.
 #pragma once
 
+#include <type_traits>
+
 #include "sm100.cuh"
 
 namespace llmcu {
@@ -34,8 +36,9 @@ struct GemmShape {
   int M, N;
   int K0, K1;      // K of segment 0 and of the optional segment 1 (0 = none)
   int tiles_m, tiles_n, num_tiles;
-  int splits;      // K splits (1 = none); split s writes rows [s * tiles_m * 128, ...)
+  int splits;      // K splits (1 = none); split s writes rows [s * split_row_tiles * 128, ...)
   int kb_per_split;
+  int split_row_tiles;  // tiles_m: one row block of partials per split; 0: splits reduce-add into the same rows
 };
 
 constexpr int kBlockM = 128;
@@ -349,10 +352,14 @@ struct EpiSwiGLUBwd {
   __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
 };
 
-// lm_head pass 1 (src/kernels/loss.cu:24-61 without the [M,V] logits tensor):
-// per row and (vocab tile, column slice), the running max and sum of exp of
-// the logits, plus the target logit when the target falls in this slice.
-struct EpiCEStats {
+// lm_head forward (src/kernels/loss.cu:24-61): per row and 128-column slot
+// (vocab tile x column slice) the slot's max logit m and sum of exp(l - m),
+// the target logit when the target falls in the slot, and the slot-relative
+// probabilities exp(l - m) as fp16 into the [M, V] buffer of mapC (later
+// turned into dlogits in place by ce_dlogits, so the backward never
+// recomputes the logits).  Takes its slice straight from TMEM: one pass for
+// the max, one for exp / sum / store.
+struct EpiCEProbs {
   struct Params {
     const int* targets;   // [M]
     float* part_max;      // [M, slots]
@@ -360,92 +367,70 @@ struct EpiCEStats {
     float* tgt_logit;     // [M]
     int slots;            // vocab tiles x column slices
   };
-  struct State { float m, s; int t; };
-  static constexpr int kChunk = 32;
-  static constexpr int kSlab = kSlabBytes;
-  static constexpr bool kPaired = false;
-  static constexpr bool kStores = false;
-  __device__ static void begin(State& st, const Params&, const EpiCtx&, int) {
-    st.m = -INFINITY;
-    st.s = 0.0f;
-    st.t = -1;
-  }
-  __device__ static bool chunk(State& st, const Params& p, EpiCtx& c, int col0, const float* v) {
-    if (c.row >= c.M || col0 >= c.N) return true;
-    if (st.t < 0) st.t = __ldg(p.targets + c.row);
-    const int nv = min(32, c.N - col0);
-    float cm = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < nv) cm = fmaxf(cm, v[j]);
-    const float mn = fmaxf(st.m, cm);
-    float s = st.s * fast_exp2((st.m - mn) * kLog2e);
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < nv) s += fast_exp2((v[j] - mn) * kLog2e);
-    st.m = mn;
-    st.s = s;
-    const int tj = st.t - col0;
-    if (tj >= 0 && tj < nv) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (j == tj) p.tgt_logit[c.row] = v[j];
-    }
-    return true;
-  }
-  __device__ static void end(State& st, const Params& p, const EpiCtx& c, int slot) {
-    if (c.row >= c.M) return;
-    p.part_max[static_cast<size_t>(c.row) * p.slots + slot] = st.m;
-    p.part_sum[static_cast<size_t>(c.row) * p.slots + slot] = st.s;
-  }
-};
-
-// lm_head pass 2: dlogits chunk = gscale * (softmax - onehot) for rows that
-// count in the loss, 0 for the others; fp16, columns relative to the vocab
-// chunk (mapC covers the chunk buffer).
-struct EpiCEGrad {
-  struct Params {
-    const int* targets;    // [M]
-    const float* lse;      // [M] natural-log LSE
-    const uint8_t* valid;  // [M] 1 if the row counts in the loss
-    int col_base;          // vocab id of the chunk's first column
-    float gscale;
-  };
-  struct State { float lse2; int t; int ok; };
-  static constexpr int kChunk = 64;
+  struct State {};
+  static constexpr int kChunk = 128;
   static constexpr int kSlab = kSlabBytes;
   static constexpr bool kPaired = false;
   static constexpr bool kStores = true;
-  __device__ static void begin(State& st, const Params& p, const EpiCtx& c, int) {
-    st.ok = 2;
-    st.t = -1;
-    st.lse2 = 0.f;
-    if (c.row < c.M) {
-      st.ok = p.valid[c.row] ? 1 : 2;
-      st.t = __ldg(p.targets + c.row);
-      st.lse2 = p.lse[c.row] * kLog2e;
-    }
-  }
-  __device__ static bool chunk(State& st, const Params& p, EpiCtx& c, int col0, const float* v) {
+  static constexpr bool kTmemDirect = true;
+  __device__ static void begin(State&, const Params&, const EpiCtx&, int) {}
+  // columns [col0, col0 + 128) of row c.row; taddr = TMEM address of column col0
+  __device__ static bool tile(State&, const Params& p, EpiCtx& c, int col0, uint32_t taddr, int slot) {
     if (col0 >= c.N) return true;
-    const int tl = st.t - p.col_base - col0;  // target column relative to this chunk
-    slab_wait_read(c);
+    const int nv = min(128, c.N - col0);
+    const bool live = c.row < c.M;
+    const int t = live ? __ldg(p.targets + c.row) - col0 : -1;
+    float m = -INFINITY;
+#pragma unroll 1
+    for (int q = 0; q < 4; ++q) {
+      float v[32];
+      tmem_ld_32x32b_x32(taddr + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v));
+      tmem_ld_wait();
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float d[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        float pr = fast_exp2(v[8 * j + t] * kLog2e - st.lse2);
-        if (8 * j + t == tl) pr -= 1.0f;
-        d[t] = (st.ok == 1) ? pr * p.gscale : 0.0f;
+      for (int j = 0; j < 32; ++j) {
+        if (32 * q + j < nv) m = fmaxf(m, v[j]);
+        if (32 * q + j == t) p.tgt_logit[c.row] = v[j];
       }
-      slab_st(c, j, pack8(d));
     }
-    slab_store(c, c.mapC, col0, c.row0);
+    const float m2 = m * kLog2e;
+    float s = 0.f;
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {  // 64 columns = one 128-byte slab row of fp16
+      uint32_t pk[32];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        float v[32];
+        tmem_ld_32x32b_x32(taddr + 64 * h + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v));
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const int cj = 64 * h + 32 * q + j;
+          const float e0 = cj < nv ? fast_exp2(fmaf(v[j], kLog2e, -m2)) : 0.f;
+          const float e1 = cj + 1 < nv ? fast_exp2(fmaf(v[j + 1], kLog2e, -m2)) : 0.f;
+          s += e0 + e1;
+          pk[16 * q + j / 2] = pack_half2(e0, e1);
+        }
+      }
+      if (64 * h < nv) {
+        slab_wait_read(c);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) slab_st(c, j, make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]));
+        slab_store(c, c.mapC, col0 + 64 * h, c.row0);
+      }
+    }
+    if (live) {
+      p.part_max[static_cast<size_t>(c.row) * p.slots + slot] = m;
+      p.part_sum[static_cast<size_t>(c.row) * p.slots + slot] = s;
+    }
     return true;
   }
   __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
 };
+
+template <class E, class = void>
+struct epi_tmem_direct : std::false_type {};
+template <class E>
+struct epi_tmem_direct<E, std::void_t<decltype(E::kTmemDirect)>> : std::bool_constant<E::kTmemDirect> {};
 
 // ---------------------------------------------------------------- the kernel
 
@@ -585,6 +570,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     constexpr int kCols = BN / kGroups;       // accumulator columns per warp
     constexpr int kChunk = Epi::kChunk;
     static_assert(kCols % kChunk == 0 || Epi::kPaired, "column slice must hold whole chunks");
+    static_assert(!epi_tmem_direct<Epi>::value || kCols == Epi::kChunk, "direct epilogues take whole slices");
     const int ew = warp & 3;                  // TMEM lane quadrant this warp may access
     const int cgrp = (warp - 2) / 4;          // which column slice of the tile
     const uint32_t lane_off = static_cast<uint32_t>(ew * 32) << 16;
@@ -609,13 +595,15 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       const int sp = u / sh.num_tiles;
       const int tm = tile % sh.tiles_m;
       const int tn = tile / sh.tiles_m;
-      c.row0 = (sp * sh.tiles_m + tm) * kBlockM + ew * 32;  // split s -> its own row block of partials
+      c.row0 = (sp * sh.split_row_tiles + tm) * kBlockM + ew * 32;  // split s -> its row block of partials
       c.row = c.row0 + lane;
       const uint32_t tbase = tmem_base + lane_off + acc * BN;
       typename Epi::State st;
       const int slot = tn * kGroups + cgrp;  // per-(tile, column slice) id for row-state epilogues
       Epi::begin(st, ep, c, slot);
-      if constexpr (!Epi::kPaired) {
+      if constexpr (epi_tmem_direct<Epi>::value) {
+        ok = Epi::tile(st, ep, c, tn * BN + cgrp * kCols, tbase + cgrp * kCols, slot);
+      } else if constexpr (!Epi::kPaired) {
 #pragma unroll 1
         for (int cc = cgrp * kCols; cc < (cgrp + 1) * kCols && ok; cc += kChunk) {
           float v[kChunk];

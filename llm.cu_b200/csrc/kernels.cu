@@ -307,6 +307,44 @@ __global__ void ce_lse_kernel(const float* __restrict__ pmax, const float* __res
   }
 }
 
+// dlogits from slot-relative probabilities, 8 columns (16 bytes) per thread.
+// Slot = 128-column slice of the vocabulary (column / 128).
+__global__ void ce_dlogits_kernel(__half* __restrict__ p, int ldp, int M, int V, const float* __restrict__ pmax,
+                                  int slots, const float* __restrict__ lse, const uint8_t* __restrict__ valid,
+                                  const int* __restrict__ targets, float gscale) {
+  const int groups = (V + 7) / 8;
+  const int64_t n = static_cast<int64_t>(M) * groups;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int m = static_cast<int>(i / groups);
+    const int c0 = static_cast<int>(i % groups) * 8;
+    __half* row = p + static_cast<size_t>(m) * ldp + c0;
+    const bool ok = valid[m] != 0;
+    const float f = ok ? exp2f((pmax[static_cast<size_t>(m) * slots + c0 / 128] - lse[m]) * kLog2e) * gscale : 0.f;
+    const int t = targets[m] - c0;
+    if (c0 + 8 <= V) {
+      uint4 w = *reinterpret_cast<const uint4*>(row);
+      __half2* h = reinterpret_cast<__half2*>(&w);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float2 x = __half22float2(h[k]);
+        x.x *= f;
+        x.y *= f;
+        if (ok && t == 2 * k) x.x -= gscale;
+        if (ok && t == 2 * k + 1) x.y -= gscale;
+        h[k] = __floats2half2_rn(x.x, x.y);
+      }
+      *reinterpret_cast<uint4*>(row) = w;
+    } else {
+      for (int k = 0; c0 + k < V; ++k) {
+        float x = __half2float(row[k]) * f;
+        if (ok && t == k) x -= gscale;
+        row[k] = __float2half_rn(x);
+      }
+    }
+  }
+}
+
 // Deterministic single-CTA sum of the row losses.
 __global__ void sum_kernel(const float* __restrict__ x, int n, float* __restrict__ out) {
   __shared__ float red[32];
@@ -558,6 +596,14 @@ cudaError_t ce_reduce(const float* part_max, const float* part_sum, const float*
   ce_lse_kernel<<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(part_max, part_sum, tgt_logit, valid,
                                                                              lse, row_loss, M, tiles_n);
   sum_kernel<<<1, 1024, 0, st>>>(row_loss, M, total);
+  return cudaGetLastError();
+}
+
+cudaError_t ce_dlogits(__half* p, int ldp, int M, int V, const float* part_max, int slots, const float* lse,
+                       const uint8_t* valid, const int* targets, float gscale, cudaStream_t st) {
+  if (ldp % 8) return cudaErrorInvalidValue;
+  const int64_t n = static_cast<int64_t>(M) * ((V + 7) / 8);
+  ce_dlogits_kernel<<<grid_for(n, 256), 256, 0, st>>>(p, ldp, M, V, part_max, slots, lse, valid, targets, gscale);
   return cudaGetLastError();
 }
 

@@ -10,7 +10,7 @@
 //     -> resid_mid = resid + [o|h_o][W_o|2B_o]^T
 //     -> rmsnorm(ffn) -> gate/up GEMM with SwiGLU -> resid_out = resid_mid + act W_d^T
 //   final rmsnorm -> lm_head pass 1 (per-tile max / sum-exp) -> LSE + loss
-//   -> per vocab chunk: lm_head pass 2 (dlogits chunk) + d_xf += dl E_chunk
+//   (+ slot-relative probabilities) -> dlogits in place -> d_xf = dl E (split-K)
 //   -> final-norm backward -> for each layer, reversed:
 //     down dX + SwiGLU bwd -> gate/up dX -> ffn-norm bwd -> dh_o -> o dX (+LoRA)
 //     -> LoRA grads (o) -> attention bwd -> RoPE/QK-norm bwd -> dh_qkv
@@ -39,7 +39,7 @@ using namespace llmcu;
 namespace {
 
 constexpr float kGradScale = 64.0f;   // dlogits are scaled by this power of two (fp16 range)
-constexpr int kVocabChunk = 8192;     // lm_head backward processes the vocabulary in chunks
+constexpr int kLmSplitK = 4;          // K (vocabulary) slices of the lm_head dX GEMM
 
 struct LayerW {
   __half *wqkv, *wqkvT, *wo, *woT, *wgu, *wguT, *wd, *wdT;
@@ -94,6 +94,7 @@ struct llmcu_ctx {
   float *part_max = nullptr, *part_sum = nullptr, *tgt_logit = nullptr, *lse_ce = nullptr, *row_loss = nullptr;
   uint8_t* valid = nullptr;
   __half* dl = nullptr;
+  int ld_dl = 0;
   float* d_xf = nullptr;
   int ce_tiles = 0;
   // backward scratch
@@ -275,8 +276,8 @@ void carve(llmcu_ctx* c, Carver& cv) {
   c->lse_ce = cv.take<float>(M);
   c->row_loss = cv.take<float>(M + 1);
   c->valid = cv.take<uint8_t>(M);
-  const size_t vc = std::min<size_t>(V, kVocabChunk);
-  c->dl = cv.take<__half>(M * vc);
+  c->ld_dl = static_cast<int>((V + 7) / 8 * 8);
+  c->dl = cv.take<__half>(M * c->ld_dl);  // probabilities, then dlogits, [M, V] fp16
   c->d_xf = cv.take<float>(M * H);
   c->dres = cv.take<float>(M * H);
   c->dres16 = cv.take<__half>(M * H);
@@ -496,28 +497,23 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     ea.part_max = ctx->part_max;
     ea.part_sum = ctx->part_sum;
     ea.tgt_logit = ctx->tgt_logit;
-    TIMED(P_GEMM, gemm(op(ctx->xf, M, H, H), op(E, V, H, H), kNone, kNone, M, V, Epi::kCEStats, ea, err, st, 256));
+    ea.out = ctx->dl;
+    ea.ld_out = ctx->ld_dl;
+    TIMED(P_GEMM, gemm(op(ctx->xf, M, H, H), op(E, V, H, H), kNone, kNone, M, V, Epi::kCEProbs, ea, err, st, 256));
   }
   TIMED(P_CE, ce_reduce(ctx->part_max, ctx->part_sum, ctx->tgt_logit, ctx->valid, ctx->lse_ce, ctx->row_loss, M,
                ctx->ce_tiles, st));
-  const int vc = std::min(V, kVocabChunk);
-  for (int c0 = 0, ci = 0; c0 < V; c0 += vc, ++ci) {
-    const int n = std::min(vc, V - c0);
-    EpiArgs ea;
-    ea.targets = ctx->tgt;
-    ea.lse = ctx->lse_ce;
-    ea.valid = ctx->valid;
-    ea.out = ctx->dl;
-    ea.ld_out = vc;
-    ea.col_base = c0;
-    ea.gscale = kGradScale;
-    TIMED(P_GEMM, gemm(op(ctx->xf, M, H, H), op(E + static_cast<size_t>(c0) * H, n, H, H), kNone, kNone, M, n, Epi::kCEGrad, ea,
-            err, st));
+  TIMED(P_CE, ce_dlogits(ctx->dl, ctx->ld_dl, M, V, ctx->part_max, ctx->ce_tiles, ctx->lse_ce, ctx->valid, ctx->tgt,
+                         kGradScale, st));
+  {
+    CK(cudaMemsetAsync(ctx->d_xf, 0, static_cast<size_t>(M) * H * sizeof(float), st));
     EpiArgs eb;
     eb.out = ctx->d_xf;
     eb.ld_out = H;
-    eb.accumulate = ci > 0;
-    TIMED(P_GEMM, gemm(op(ctx->dl, M, n, vc), op(ctx->ET + c0, H, n, V), kNone, kNone, M, H, Epi::kStoreF32, eb, err, st));
+    eb.accumulate = 1;
+    eb.ksplit = kLmSplitK;
+    TIMED(P_GEMM, gemm(op(ctx->dl, M, V, ctx->ld_dl), op(ctx->ET, H, V, V), kNone, kNone, M, H, Epi::kStoreF32, eb,
+                       err, st));
   }
   TIMED(P_NORM, rmsnorm_backward(ctx->d_xf, xfinal, ctx->final_norm, ctx->dres, ctx->dres16, M, H, eps, 0, st));
 
