@@ -233,6 +233,11 @@ llmcu_status llmcu_profile_read(llmcu_ctx* ctx, char* buf, size_t len, int reset
  * (src/kernels/matmul.cu:8-51) on the tcgen05 path. */
 llmcu_status llmcu_gemm_nt_f16(const void* A, const void* B, float* C, int M, int N, int K,
                                int lda, int ldb, int ldc, void* stream);
+/* C[M,N] (fp32) = A[M,K] . B[K,N], B row-major [K, N] (ldb elements between
+ * rows) -- the NN product of matmul_nn_forward (src/kernels/matmul.cu:55-98),
+ * the input-gradient GEMMs' form (B read MN-major, no transposed copy). */
+llmcu_status llmcu_gemm_nn_f16(const void* A, const void* B, float* C, int M, int N, int K,
+                               int lda, int ldb, int ldc, void* stream);
 /* Causal GQA attention forward: q [B*S, nh*hd], k/v [B*S, nkv*hd] fp16 with
  * row strides ldq/ldk/ldv; o [B*S, nh*hd] fp16, lse [B, nh, S] fp32
  * (replaces naive_attn_kernel, src/kernels/lora_forward.cu:48-135). */

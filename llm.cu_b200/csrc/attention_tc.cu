@@ -42,15 +42,7 @@ struct FwdLayout {
 // MN-major (column-contiguous) 128-byte-swizzled operand: 64-element rows of
 // 128 B, 8-row atoms of 1 KB stacked along K (stride byte offset 1 KB), the
 // next 64 columns one 16 KB box further (leading byte offset).
-__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t smem_addr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
-  d |= static_cast<uint64_t>(kBox >> 4) << 16;      // leading byte offset: next 64 columns
-  d |= static_cast<uint64_t>(1024 >> 4) << 32;      // stride byte offset: next 8 K rows
-  d |= static_cast<uint64_t>(1) << 46;
-  d |= static_cast<uint64_t>(2) << 61;
-  return d;
-}
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t smem_addr) { return sw128_mn_desc(smem_addr, kBox); }
 
 
 template <int HD>

@@ -33,11 +33,16 @@ cudaError_t attention_backward_tc(const __half* q, const __half* k, const __half
 constexpr int kGemmEpiGroups = 2;
 // Tensor operand for the GEMM: fp16, K-major rows (K contiguous), `ld`
 // elements between rows; `rows` x `k` valid extent.
+// Tensor operand for the GEMM, fp16.  K-major (mn == false): `rows` rows of
+// `k` contiguous elements, `ld` elements between rows.  MN-major (mn == true,
+// B only): the [k, rows] matrix stored row-major -- k rows of `rows`
+// contiguous elements -- e.g. a weight [out, in] used as B of dY . W.
 struct Operand {
   const __half* ptr;
   int rows;
   int k;
   int ld;
+  bool mn = false;
 };
 
 enum class Epi : int {
@@ -55,6 +60,10 @@ struct EpiArgs {
   int ld_out = 0;
   int accumulate = 0;
   int ksplit = 1;  // kStoreF32 with accumulate: K slices that reduce-add into the same output
+  // side output (kStoreF16, kResidF32): columns [n_main, N) as fp16 [M, N - n_main]
+  int n_main = 0;  // 0: no side output
+  __half* side = nullptr;
+  int ld_side = 0;
   const float* resid = nullptr;
   // SwiGLU
   __half* gu = nullptr;       // interleaved [M, 2I]
@@ -69,18 +78,11 @@ struct EpiArgs {
   float* tgt_logit = nullptr;
 };
 
-// C[M,N] = A0 . B0^T (+ A1 . B1^T) with the given epilogue.  A*.rows = M,
-// B*.rows = N; A0.k == B0.k == K0; A1/B1 may have k == 0 (absent).
-cudaError_t gemm(const Operand& A0, const Operand& B0, const Operand& A1, const Operand& B1, int M, int N, Epi epi,
-                 const EpiArgs& ea, int* err, cudaStream_t st, int bn_hint = 0);
+// C[M,N] = A . B^T (B K-major) or A . B (B MN-major) with the given
+// epilogue.  A.rows = M, B.rows = N, A.k == B.k == K.
+cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, const EpiArgs& ea, int* err,
+                 cudaStream_t st, int bn_hint = 0);
 int gemm_num_sms();
-// Skinny GEMM (N <= 64, e.g. the LoRA h = x A^T products): split over K into
-// (tile, split) units spread across the SMs, fp32 partials in `ws`, then a
-// fixed-order reduction to fp16 `out` -- deterministic.
-constexpr int kSkinnyMaxSplits = 16;
-size_t gemm_skinny_ws_floats(int M, int N);
-cudaError_t gemm_skinny(const Operand& A, const Operand& B, int M, int N, __half* out, int ld_out, float* ws,
-                        int* err, cudaStream_t st);
 
 // ---- kernels.cu
 cudaError_t embed_forward(const int* tokens, const __half* E, float* out, int M, int H, int V, int* err,

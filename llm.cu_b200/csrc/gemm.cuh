@@ -1,12 +1,15 @@
 // gemm.cuh -- persistent, warp-specialised tcgen05 GEMM for sm_100a.
 //
-//   C[M, N] = A0[M, K0] . B0[N, K0]^T  (+ A1[M, K1] . B1[N, K1]^T)
+//   C[M, N] = A[M, K] . B[N, K]^T
 //
-// fp16 operands, both K-major (rows contiguous along K), fp32 accumulation in
-// TMEM, and a fused epilogue chosen at compile time.  The optional second
-// K-segment (A1, B1) carries the LoRA term: appending [h | 2B] to [x | W] turns
-// y = xW^T + 2(xA^T)B^T into one accumulation, so the adapter update costs one
-// extra 64-wide K block instead of a separate GEMM and an add pass.
+// fp16 operands, fp32 accumulation in TMEM, and a fused epilogue chosen at
+// compile time.  A is K-major (rows contiguous along K).  B is K-major
+// ([N, K] rows) or, with BMN, MN-major: the [K, N] matrix itself, read in
+// 64 x 64 boxes, so a weight stored [out, in] serves both the forward
+// (x W^T, K-major) and the input gradient (dY W, MN-major) without a
+// transposed copy.  Columns at and past `n_main` are a side output: the
+// LoRA projections h = x A^T / dh = dY B ride along as extra rows (columns)
+// of the merged weight and leave through plain fp16 stores.
 //
 // Roles (64 + 32*EW threads, one CTA per SM):
 //   warp 0        TMA producer -- fills a STAGES-deep ring of (A, B) smem tiles
@@ -34,16 +37,20 @@ namespace llmcu {
 
 struct GemmShape {
   int M, N;
-  int K0, K1;      // K of segment 0 and of the optional segment 1 (0 = none)
+  int K;
   int tiles_m, tiles_n, num_tiles;
   int splits;      // K splits (1 = none); split s writes rows [s * split_row_tiles * 128, ...)
   int kb_per_split;
   int split_row_tiles;  // tiles_m: one row block of partials per split; 0: splits reduce-add into the same rows
+  int n_main;           // columns [n_main, N) go to the side output
+  __half* side;         // [M, N - n_main] fp16, row stride ld_side
+  int ld_side;
 };
 
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 64;
 constexpr int kSlabBytes = 32 * 128;  // one 32-row x 128-byte box
+constexpr int kMnBox = 64 * 128;      // MN-major B box: 64 K rows x 64 columns of fp16
 
 template <int BN, int STAGES, int EW, int SLAB = kSlabBytes>
 struct GemmSmem {
@@ -71,7 +78,26 @@ struct EpiCtx {
   int* err;
   const CUtensorMap* mapC;  // primary output
   const CUtensorMap* mapD;  // secondary input or output (epilogue specific)
+  int n_main;               // first side-output column
+  __half* side;
+  int ld_side;
 };
+
+// Side-output columns [col0, col0 + n) of this thread's row as fp16 (plain
+// 16-byte stores; the side output is a few columns wide).
+__device__ __forceinline__ void side_store(const EpiCtx& c, int col0, const float* v, int n) {
+  if (c.row >= c.M) return;
+  __half* dst = c.side + static_cast<size_t>(c.row) * c.ld_side + (col0 - c.n_main);
+  for (int j = 0; j < n / 8; ++j) {
+    if (col0 + 8 * j >= c.N) break;
+    uint4 w;
+    w.x = pack_half2(v[8 * j], v[8 * j + 1]);
+    w.y = pack_half2(v[8 * j + 2], v[8 * j + 3]);
+    w.z = pack_half2(v[8 * j + 4], v[8 * j + 5]);
+    w.w = pack_half2(v[8 * j + 6], v[8 * j + 7]);
+    *reinterpret_cast<uint4*>(dst + 8 * j) = w;
+  }
+}
 
 // byte offset of 16-byte chunk j (0..7) of the thread's 128-byte slab row,
 // 128-byte swizzle (chunk ^ row % 8), as TMA lays the box out
@@ -193,6 +219,10 @@ struct EpiStoreF16 {
   __device__ static void begin(State&, const Params&, const EpiCtx&, int) {}
   __device__ static bool chunk(State&, const Params&, EpiCtx& c, int col0, const float* v) {
     if (col0 >= c.N) return true;
+    if (col0 >= c.n_main) {
+      side_store(c, col0, v, kChunk);
+      return true;
+    }
     slab_wait_read(c);
 #pragma unroll
     for (int j = 0; j < 8; ++j) slab_st(c, j, pack8(v + 8 * j));
@@ -244,6 +274,10 @@ struct EpiResidF32 {
   __device__ static void begin(State&, const Params&, const EpiCtx&, int) {}
   __device__ static bool chunk(State&, const Params&, EpiCtx& c, int col0, const float* v) {
     if (col0 >= c.N) return true;
+    if (col0 >= c.n_main) {
+      side_store(c, col0, v, kChunk);
+      return true;
+    }
     slab_wait_read(c);
     if (!slab_load(c, c.mapD, col0, c.row0)) return false;
 #pragma unroll
@@ -434,10 +468,9 @@ struct epi_tmem_direct<E, std::void_t<decltype(E::kTmemDirect)>> : std::bool_con
 
 // ---------------------------------------------------------------- the kernel
 
-template <int BN, int STAGES, int EW, class Epi>
+template <int BN, int STAGES, int EW, class Epi, bool BMN>
 __global__ void __launch_bounds__(64 + 32 * EW, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmB0,
-                   const __grid_constant__ CUtensorMap tmA1, const __grid_constant__ CUtensorMap tmB1,
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
                    const GemmShape sh, const typename Epi::Params ep, int* err) {
   using L = GemmSmem<BN, STAGES, EW, Epi::kSlab>;
@@ -469,12 +502,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmA0);
-    tma_prefetch_desc(&tmB0);
-    if (sh.K1 > 0) {
-      tma_prefetch_desc(&tmA1);
-      tma_prefetch_desc(&tmB1);
-    }
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, L::kTmemCols);
@@ -485,9 +514,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int nk0 = (sh.K0 + kBlockK - 1) / kBlockK;
-  const int nk1 = (sh.K1 + kBlockK - 1) / kBlockK;
-  const int nk = nk0 + nk1;
+  const int nk = (sh.K + kBlockK - 1) / kBlockK;
   const int num_units = sh.num_tiles * sh.splits;  // (tile, K split) work units
 
   if (warp == 0) {
@@ -508,13 +535,14 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
           uint8_t* sa = smem + s * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes;
           mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-          if (kb < nk0) {
-            tma_load_2d(sa, &tmA0, &full[s], kb * kBlockK, tm * kBlockM);
-            tma_load_2d(sb, &tmB0, &full[s], kb * kBlockK, tn * BN);
+          tma_load_2d(sa, &tmA, &full[s], kb * kBlockK, tm * kBlockM);
+          if constexpr (!BMN) {
+            tma_load_2d(sb, &tmB, &full[s], kb * kBlockK, tn * BN);
           } else {
-            const int k = (kb - nk0) * kBlockK;
-            tma_load_2d(sa, &tmA1, &full[s], k, tm * kBlockM);
-            tma_load_2d(sb, &tmB1, &full[s], k, tn * BN);
+            // [64 K rows x 64 N columns] boxes side by side along N
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + j * kMnBox, &tmB, &full[s], tn * BN + 64 * j, kb * kBlockK);
           }
         }
       }
@@ -533,7 +561,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------- MMA issuer
-      constexpr uint32_t idesc = idesc_f16_f32(kBlockM, BN);
+      constexpr uint32_t idesc = idesc_f16_f32(kBlockM, BN) | (BMN ? (1u << 16) : 0u);
       int it = 0;
       int i = 0;
       bool ok = true;
@@ -552,11 +580,13 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
           const uint32_t sa = smem_u32(smem + s * L::kStageBytes);
           const uint32_t sb = sa + L::kABytes;
           const uint64_t adesc = sw128_kmajor_desc(sa);
-          const uint64_t bdesc = sw128_kmajor_desc(sb);
+          const uint64_t bdesc = BMN ? sw128_mn_desc(sb, kMnBox) : sw128_kmajor_desc(sb);
 #pragma unroll
           for (int k = 0; k < kBlockK / 16; ++k) {
-            // +32 bytes per 16-element K step inside the 128-byte swizzle row
-            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb != kb_begin || k != 0) ? 1u : 0u);
+            // K-major: +32 bytes per 16-element K step inside the 128-byte
+            // swizzle row; MN-major: +16 rows of 128 bytes
+            const uint64_t bk = BMN ? bdesc + (16 * 128 >> 4) * k : bdesc + 2 * k;
+            umma_f16(d_tmem, adesc + 2 * k, bk, idesc, (kb != kb_begin || k != 0) ? 1u : 0u);
           }
           umma_commit(&empty[s]);
         }
@@ -585,6 +615,9 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     c.err = err;
     c.mapC = &tmC;
     c.mapD = &tmD;
+    c.n_main = sh.n_main;
+    c.side = sh.side;
+    c.ld_side = sh.ld_side;
     int i = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++i) {

@@ -3,7 +3,7 @@
 //
 // Step schedule on the compute stream (reference order, src/train.cu:251-291,
 // restated for fused kernels; M = batch * seq rows):
-//   lora_prep                          fp16 operands from the fp32 adapters
+//   lora_merge                         merged q/k/v/o weights W + s B A (+ A, s B pads)
 //   embed -> for each layer:
 //     rmsnorm(attn) -> h = xn A_cat^T -> qkv = [xn|h][W_qkv|2B]^T
 //     -> QK-norm+RoPE -> flash attention -> h_o = o A_o^T
@@ -42,12 +42,13 @@ constexpr float kGradScale = 64.0f;   // dlogits are scaled by this power of two
 constexpr int kLmSplitK = 4;          // K (vocabulary) slices of the lm_head dX GEMM
 
 struct LayerW {
-  __half *wqkv, *wqkvT, *wo, *woT, *wgu, *wguT, *wd, *wdT;
+  __half *wqkv, *wo, *wgu, *wd;  // fp16 base, [out, in] (also read MN-major by the dX GEMMs)
   float *attn_norm, *ffn_norm, *q_norm, *k_norm;
-  // INT8 base: q [out, in] per fused weight + per-row scales; transposed copies
+  // INT8 base: q [out, in] per fused weight + per-row scales
   int8_t *q_qkv, *q_o, *q_gu, *q_d;
-  int8_t *qT_qkv, *qT_o, *qT_gu, *qT_d;
   float *s_qkv, *s_o, *s_gu, *s_d;
+  // merged base + LoRA weights of this step (lora_merge)
+  __half *mqkv, *mo;
 };
 
 struct LayerA {  // forward stash
@@ -72,20 +73,20 @@ struct llmcu_ctx {
   size_t arena_bytes = 0;
 
   // base
-  __half *E = nullptr, *ET = nullptr;
+  __half* E = nullptr;
   float* final_norm = nullptr;
   int8_t *qE = nullptr;
   float* sE = nullptr;
   std::vector<LayerW> lw;
-  // int8 dequant scratch (one layer's fp16 weights, forward and transposed)
-  __half *dq_w = nullptr, *dq_wT = nullptr;
+  // int8 dequant scratch (one layer's fp16 weight) and a row-scale temporary
+  __half* dq_w = nullptr;
+  float* q_scale_tmp = nullptr;
+  MergeWeights mw;  // all layers' q/k/v and o base weights, for lora_merge
 
   // lora
   float *lp = nullptr, *lg = nullptr, *lm = nullptr, *lv = nullptr;
-  __half* lderived = nullptr;
   float* lpart = nullptr;
   int lpart_amax = 0;
-  float* skinny_ws = nullptr;  // split-K partials of the N = 64 LoRA GEMMs
 
   // activations
   std::vector<float*> resid;  // L + 1 buffers
@@ -149,7 +150,7 @@ enum ProfClass : int {
   P_GEMM = 0, P_ATTN_FWD, P_ATTN_BWD, P_NORM, P_LORA_GRAD, P_LORA_PREP, P_CE, P_EMBED, P_ADAMW, P_DEQUANT, P_COUNT
 };
 const char* kProfNames[P_COUNT] = {"gemm_tc", "attention_fwd", "attention_bwd", "norm_rope", "lora_grad",
-                                   "lora_prep", "ce_reduce", "embed", "adamw", "int8_dequant"};
+                                   "lora_merge", "ce_reduce", "embed", "adamw", "int8_dequant"};
 const int kProfLaunches[P_COUNT] = {1, 1, 3, 1, 2, 1, 2, 1, 1, 1};  // kernels per call
 
 void prof_mark(llmcu_ctx* c, int cls) {
@@ -173,7 +174,6 @@ void prof_mark(llmcu_ctx* c, int cls) {
   } while (0)
 
 Operand op(const __half* p, int rows, int k, int ld) { return Operand{p, rows, k, ld}; }
-const Operand kNone{nullptr, 0, 0, 0};
 
 // ------------------------------------------------------------------ arena
 struct Carver {
@@ -194,51 +194,75 @@ void carve(llmcu_ctx* c, Carver& cv) {
   c->lw.assign(L, LayerW{});
   c->la.assign(L, LayerA{});
   c->resid.assign(L + 1, nullptr);
-  // base weights
-  if (!int8) {
-    c->E = cv.take<__half>(V * H);
-    c->ET = cv.take<__half>(H * V);
-  } else {
+  // base weights: each kind for all layers in one array (lora_merge indexes layers by stride)
+  c->E = cv.take<__half>(V * H);  // INT8: the dequantised table (gather + lm_head)
+  if (int8) {
     c->qE = cv.take<int8_t>(V * H);
     c->sE = cv.take<float>(V);
-    c->E = cv.take<__half>(V * H);   // dequantised copies of the tied head (gather + lm_head)
-    c->ET = cv.take<__half>(H * V);
   }
   c->final_norm = cv.take<float>(H);
+  c->mw = MergeWeights{};
+  if (!int8) {
+    __half* wqkv = cv.take<__half>(L * QKV * H);
+    __half* wo = cv.take<__half>(L * H * Q);
+    __half* wgu = cv.take<__half>(L * 2 * I * H);
+    __half* wd = cv.take<__half>(L * H * I);
+    for (size_t l = 0; l < L; ++l) {
+      LayerW& w = c->lw[l];
+      w.wqkv = wqkv ? wqkv + l * QKV * H : nullptr;
+      w.wo = wo ? wo + l * H * Q : nullptr;
+      w.wgu = wgu ? wgu + l * 2 * I * H : nullptr;
+      w.wd = wd ? wd + l * H * I : nullptr;
+    }
+    c->mw.wqkv = wqkv;
+    c->mw.wo = wo;
+  } else {
+    int8_t* q_qkv = cv.take<int8_t>(L * QKV * H);
+    int8_t* q_o = cv.take<int8_t>(L * H * Q);
+    int8_t* q_gu = cv.take<int8_t>(L * 2 * I * H);
+    int8_t* q_d = cv.take<int8_t>(L * H * I);
+    float* s_qkv = cv.take<float>(L * QKV);
+    float* s_o = cv.take<float>(L * H);
+    float* s_gu = cv.take<float>(L * 2 * I);
+    float* s_d = cv.take<float>(L * H);
+    for (size_t l = 0; l < L; ++l) {
+      LayerW& w = c->lw[l];
+      w.q_qkv = q_qkv ? q_qkv + l * QKV * H : nullptr;
+      w.q_o = q_o ? q_o + l * H * Q : nullptr;
+      w.q_gu = q_gu ? q_gu + l * 2 * I * H : nullptr;
+      w.q_d = q_d ? q_d + l * H * I : nullptr;
+      w.s_qkv = s_qkv ? s_qkv + l * QKV : nullptr;
+      w.s_o = s_o ? s_o + l * H : nullptr;
+      w.s_gu = s_gu ? s_gu + l * 2 * I : nullptr;
+      w.s_d = s_d ? s_d + l * H : nullptr;
+    }
+    c->mw.q_qkv = q_qkv;
+    c->mw.q_o = q_o;
+    c->mw.s_qkv = s_qkv;
+    c->mw.s_o = s_o;
+    c->mw.s_layer_qkv = static_cast<int64_t>(QKV);
+    c->mw.s_layer_o = static_cast<int64_t>(H);
+    const size_t wmax = std::max({QKV * H, H * Q, 2 * I * H, H * I});
+    c->dq_w = cv.take<__half>(wmax);
+    c->q_scale_tmp = cv.take<float>(std::max({QKV, H, 2 * I}));
+  }
+  c->mw.w_layer_qkv = static_cast<int64_t>(QKV * H);
+  c->mw.w_layer_o = static_cast<int64_t>(H * Q);
+  {
+    const int64_t nq = merged_qkv_elems(c->ld), no = merged_o_elems(c->ld);
+    __half* mqkv = cv.take<__half>(L * nq);
+    __half* mo = cv.take<__half>(L * no);
+    for (size_t l = 0; l < L; ++l) {
+      c->lw[l].mqkv = mqkv ? mqkv + l * nq : nullptr;
+      c->lw[l].mo = mo ? mo + l * no : nullptr;
+    }
+  }
   for (size_t l = 0; l < L; ++l) {
     LayerW& w = c->lw[l];
-    if (!int8) {
-      w.wqkv = cv.take<__half>(QKV * H);
-      w.wqkvT = cv.take<__half>(H * QKV);
-      w.wo = cv.take<__half>(H * Q);
-      w.woT = cv.take<__half>(Q * H);
-      w.wgu = cv.take<__half>(2 * I * H);
-      w.wguT = cv.take<__half>(H * 2 * I);
-      w.wd = cv.take<__half>(H * I);
-      w.wdT = cv.take<__half>(I * H);
-    } else {
-      w.q_qkv = cv.take<int8_t>(QKV * H);
-      w.qT_qkv = cv.take<int8_t>(H * QKV);
-      w.s_qkv = cv.take<float>(QKV);
-      w.q_o = cv.take<int8_t>(H * Q);
-      w.qT_o = cv.take<int8_t>(Q * H);
-      w.s_o = cv.take<float>(H);
-      w.q_gu = cv.take<int8_t>(2 * I * H);
-      w.qT_gu = cv.take<int8_t>(H * 2 * I);
-      w.s_gu = cv.take<float>(2 * I);
-      w.q_d = cv.take<int8_t>(H * I);
-      w.qT_d = cv.take<int8_t>(I * H);
-      w.s_d = cv.take<float>(H);
-    }
     w.attn_norm = cv.take<float>(H);
     w.ffn_norm = cv.take<float>(H);
     w.q_norm = cv.take<float>(c->hd);
     w.k_norm = cv.take<float>(c->hd);
-  }
-  if (int8) {
-    const size_t wmax = std::max({QKV * H, H * Q, 2 * I * H, H * I});
-    c->dq_w = cv.take<__half>(wmax);
-    c->dq_wT = cv.take<__half>(wmax);
   }
   // lora
   const size_t n = static_cast<size_t>(c->n_lora);
@@ -246,10 +270,8 @@ void carve(llmcu_ctx* c, Carver& cv) {
   c->lg = cv.take<float>(n);
   c->lm = cv.take<float>(n);
   c->lv = cv.take<float>(n);
-  c->lderived = cv.take<__half>(static_cast<size_t>(c->ld.derived_per_layer) * L);
   c->lpart_amax = static_cast<int>((std::max({H, Q, KV}) + 63) / 64 * 64);
   c->lpart = cv.take<float>(static_cast<size_t>(kLoraMaxSplits) * kLoraMaxProbs * c->lpart_amax * 64);
-  c->skinny_ws = cv.take<float>(gemm_skinny_ws_floats(static_cast<int>(M), 64));
   // activations
   for (size_t l = 0; l <= L; ++l) c->resid[l] = cv.take<float>(M * H);
   const size_t lse_n = static_cast<size_t>(c->rc.max_batch) * c->nh * c->rc.max_seq;
@@ -368,56 +390,21 @@ llmcu_status wait_event(llmcu_ctx* ctx, cudaEvent_t ev) {
 }
 
 // ------------------------------------------------------------- INT8 base
-// Dequantise one layer's weight (or its transposed copy) into fp16 scratch.
-// Forward copy: W[o, i] = q[o, i] * s[o].  Transposed copy: WT[i, o] = qT[i, o] * s[o].
-__global__ void dequant_cols_kernel(const int8_t* __restrict__ q, const float* __restrict__ s, int rows, int cols,
-                                    __half* __restrict__ out) {
-  const int64_t n = static_cast<int64_t>(rows) * cols;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    out[i] = __float2half_rn(static_cast<float>(q[i]) * s[i % cols]);
-}
-
-__global__ void transpose_i8_kernel(const int8_t* __restrict__ src, int rows, int cols, int8_t* __restrict__ dst) {
-  __shared__ int8_t tile[32][33];
-  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  for (int i = ty; i < 32; i += 8) {
-    const int r = r0 + i, c = c0 + tx;
-    tile[i][tx] = (r < rows && c < cols) ? src[static_cast<size_t>(r) * cols + c] : 0;
-  }
-  __syncthreads();
-  for (int i = ty; i < 32; i += 8) {
-    const int c = c0 + i, r = r0 + tx;
-    if (r < rows && c < cols) dst[static_cast<size_t>(c) * rows + r] = tile[tx][i];
-  }
-}
-
 __global__ void scale_loss_kernel(const float* total, float inv_n, float* out) { out[0] = total[0] * inv_n; }
 
-int grid_n(int64_t n) {
-  int64_t g = (n + 255) / 256;
-  return static_cast<int>(std::min<int64_t>(std::max<int64_t>(g, 1), 148 * 16));
-}
 
-const __half* fwd_weight(llmcu_ctx* c, const __half* w16, const int8_t* q, const float* s, int rows, int cols,
-                         cudaError_t* e) {
+// fp16 [rows, cols] view of one base weight: the fp16 copy, or the INT8 rows
+// dequantised into scratch (src/kernels/quantize.cu:55-78 applies the same
+// per-row scale).  The forward reads it K-major, the input gradient MN-major.
+const __half* base_weight(llmcu_ctx* c, const __half* w16, const int8_t* q, const float* s, int rows, int cols,
+                          cudaError_t* e) {
   if (c->rc.base_dtype != LLMCU_BASE_INT8) return w16;
   prof_mark(c, P_DEQUANT);
   *e = dequant_rows_f16(q, s, rows, cols, c->dq_w, c->st);
   prof_mark(c, P_DEQUANT);
   return c->dq_w;
 }
-const __half* bwd_weight(llmcu_ctx* c, const __half* wT16, const int8_t* qT, const float* s, int rows_t, int cols_t,
-                         cudaError_t* e) {
-  if (c->rc.base_dtype != LLMCU_BASE_INT8) return wT16;
-  prof_mark(c, P_DEQUANT);
-  dequant_cols_kernel<<<grid_n(static_cast<int64_t>(rows_t) * cols_t), 256, 0, c->st>>>(qT, s, rows_t, cols_t,
-                                                                                        c->dq_wT);
-  prof_mark(c, P_DEQUANT);
-  *e = cudaGetLastError();
-  return c->dq_wT;
-}
+Operand op_mn(const __half* p, int k_rows, int n_cols, int ld) { return Operand{p, n_cols, k_rows, ld, true}; }
 
 // ----------------------------------------------------------------- step
 llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
@@ -434,7 +421,8 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   const float unscale = static_cast<float>(1.0 / (kGradScale * n_valid_total));
   cudaError_t e = cudaSuccess;
 
-  TIMED(P_LORA_PREP, lora_prep(ctx->lp, d, ctx->L, ctx->lderived, st));
+  // merged q/k/v/o weights of this step's adapters, every layer
+  TIMED(P_LORA_PREP, lora_merge(ctx->lp, d, ctx->L, ctx->mw, ctx->lw[0].mqkv, ctx->lw[0].mo, st));
   TIMED(P_CE, ce_valid_rows(ctx->valid, ctx->tgt, B, S, ctx->rc.loss_all_positions, V, err, st));
   const __half* E = ctx->E;
   TIMED(P_EMBED, embed_forward(ctx->tok, E, ctx->resid[0], M, H, V, err, st));
@@ -443,31 +431,33 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   for (int l = 0; l < ctx->L; ++l) {
     LayerW& w = ctx->lw[l];
     LayerA& a = ctx->la[l];
-    const __half* D = ctx->lderived + d.derived_per_layer * l;
     const float* x = ctx->resid[l];
     TIMED(P_NORM, rmsnorm_forward(x, w.attn_norm, a.xn, M, H, eps, st));
-    TIMED(P_GEMM, gemm_skinny(op(a.xn, M, H, H), op(D + d.d_acat, 64, H, H), M, 64, a.hq, 64, ctx->skinny_ws, err, st));
-    const __half* wqkv = fwd_weight(ctx, w.wqkv, w.q_qkv, w.s_qkv, QKV, H, &e);
-    CK(e);
-    TIMED(P_GEMM, gemm(op(a.xn, M, H, H), op(wqkv, QKV, H, H), op(a.hq, M, 64, 64), op(D + d.d_bblk, QKV, 64, 64), M, QKV,
-            Epi::kStoreF16, EpiArgs{a.qkv, QKV}, err, st));
+    {  // [q | k | v | h] = xn . mqkv^T
+      EpiArgs ea;
+      ea.out = a.qkv;
+      ea.ld_out = QKV;
+      ea.n_main = QKV;
+      ea.side = a.hq;
+      ea.ld_side = 64;
+      TIMED(P_GEMM, gemm(op(a.xn, M, H, H), op(w.mqkv, QKV + 64, H, H + 64), M, QKV + 64, Epi::kStoreF16, ea, err, st));
+    }
     TIMED(P_NORM, qknorm_rope_forward(a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, a.qrope, a.krope, B, S,
                            ctx->nh, ctx->nkv, ctx->hd, eps, st));
     TIMED(P_ATTN_FWD, attention_forward(a.qrope, a.krope, a.qkv + Q + KV, a.attn, a.lse, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV,
                          QKV, Q, err, st));
-    TIMED(P_GEMM, gemm_skinny(op(a.attn, M, Q, Q), op(D + d.d_ao, 64, Q, Q), M, 64, a.ho, 64, ctx->skinny_ws, err, st));
-    const __half* wo = fwd_weight(ctx, w.wo, w.q_o, w.s_o, H, Q, &e);
-    CK(e);
-    {
+    {  // [resid_mid | h_o] = [resid + attn . mo^T | attn . Ao^T]
       EpiArgs ea;
       ea.out = a.resid_mid;
       ea.ld_out = H;
       ea.resid = x;
-      TIMED(P_GEMM, gemm(op(a.attn, M, Q, Q), op(wo, H, Q, Q), op(a.ho, M, 64, 64), op(D + d.d_bo, H, 64, 64), M, H,
-              Epi::kResidF32, ea, err, st));
+      ea.n_main = H;
+      ea.side = a.ho;
+      ea.ld_side = 64;
+      TIMED(P_GEMM, gemm(op(a.attn, M, Q, Q), op(w.mo, H + 64, Q, Q + 64), M, H + 64, Epi::kResidF32, ea, err, st));
     }
     TIMED(P_NORM, rmsnorm_forward(a.resid_mid, w.ffn_norm, a.xn2, M, H, eps, st));
-    const __half* wgu = fwd_weight(ctx, w.wgu, w.q_gu, w.s_gu, 2 * I, H, &e);
+    const __half* wgu = base_weight(ctx, w.wgu, w.q_gu, w.s_gu, 2 * I, H, &e);
     CK(e);
     {
       EpiArgs ea;
@@ -475,16 +465,16 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       ea.ld_gu = 2 * I;
       ea.act = a.act;
       ea.ld_act = I;
-      TIMED(P_GEMM, gemm(op(a.xn2, M, H, H), op(wgu, 2 * I, H, H), kNone, kNone, M, 2 * I, Epi::kSwiGLU, ea, err, st, 256));
+      TIMED(P_GEMM, gemm(op(a.xn2, M, H, H), op(wgu, 2 * I, H, H), M, 2 * I, Epi::kSwiGLU, ea, err, st, 256));
     }
-    const __half* wd = fwd_weight(ctx, w.wd, w.q_d, w.s_d, H, I, &e);
+    const __half* wd = base_weight(ctx, w.wd, w.q_d, w.s_d, H, I, &e);
     CK(e);
     {
       EpiArgs ea;
       ea.out = ctx->resid[l + 1];
       ea.ld_out = H;
       ea.resid = a.resid_mid;
-      TIMED(P_GEMM, gemm(op(a.act, M, I, I), op(wd, H, I, I), kNone, kNone, M, H, Epi::kResidF32, ea, err, st));
+      TIMED(P_GEMM, gemm(op(a.act, M, I, I), op(wd, H, I, I), M, H, Epi::kResidF32, ea, err, st));
     }
   }
 
@@ -499,7 +489,7 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     ea.tgt_logit = ctx->tgt_logit;
     ea.out = ctx->dl;
     ea.ld_out = ctx->ld_dl;
-    TIMED(P_GEMM, gemm(op(ctx->xf, M, H, H), op(E, V, H, H), kNone, kNone, M, V, Epi::kCEProbs, ea, err, st, 256));
+    TIMED(P_GEMM, gemm(op(ctx->xf, M, H, H), op(E, V, H, H), M, V, Epi::kCEProbs, ea, err, st, 256));
   }
   TIMED(P_CE, ce_reduce(ctx->part_max, ctx->part_sum, ctx->tgt_logit, ctx->valid, ctx->lse_ce, ctx->row_loss, M,
                ctx->ce_tiles, st));
@@ -512,8 +502,8 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     eb.ld_out = H;
     eb.accumulate = 1;
     eb.ksplit = kLmSplitK;
-    TIMED(P_GEMM, gemm(op(ctx->dl, M, V, ctx->ld_dl), op(ctx->ET, H, V, V), kNone, kNone, M, H, Epi::kStoreF32, eb,
-                       err, st));
+    // d_xf = dlogits . E  (E [V, H] read MN-major)
+    TIMED(P_GEMM, gemm(op(ctx->dl, M, V, ctx->ld_dl), op_mn(E, V, H, H), M, H, Epi::kStoreF32, eb, err, st));
   }
   TIMED(P_NORM, rmsnorm_backward(ctx->d_xf, xfinal, ctx->final_norm, ctx->dres, ctx->dres16, M, H, eps, 0, st));
 
@@ -521,29 +511,34 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   for (int l = ctx->L - 1; l >= 0; --l) {
     LayerW& w = ctx->lw[l];
     LayerA& a = ctx->la[l];
-    const __half* D = ctx->lderived + d.derived_per_layer * l;
     float* G = ctx->lg + d.per_layer * l;
-    // MLP
-    const __half* wdT = bwd_weight(ctx, w.wdT, w.qT_d, w.s_d, I, H, &e);
+    // MLP: d_act = dres . W_down (MN-major), SwiGLU backward fused
+    const __half* wd = base_weight(ctx, w.wd, w.q_d, w.s_d, H, I, &e);
     CK(e);
     {
       EpiArgs ea;
       ea.gu_in = a.gu;
       ea.gu = ctx->dgu;
       ea.ld_gu = 2 * I;
-      TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op(wdT, I, H, H), kNone, kNone, M, I, Epi::kSwiGLUBwd, ea, err, st, 256));
+      TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op_mn(wd, H, I, I), M, I, Epi::kSwiGLUBwd, ea, err, st, 256));
     }
-    const __half* wguT = bwd_weight(ctx, w.wguT, w.qT_gu, w.s_gu, H, 2 * I, &e);
+    // dxn2 = dgu . W_gate/up (MN-major)
+    const __half* wgu = base_weight(ctx, w.wgu, w.q_gu, w.s_gu, 2 * I, H, &e);
     CK(e);
-    TIMED(P_GEMM, gemm(op(ctx->dgu, M, 2 * I, 2 * I), op(wguT, H, 2 * I, 2 * I), kNone, kNone, M, H, Epi::kStoreF16,
-            EpiArgs{ctx->dxn, H}, err, st));
+    TIMED(P_GEMM, gemm(op(ctx->dgu, M, 2 * I, 2 * I), op_mn(wgu, 2 * I, H, H), M, H, Epi::kStoreF16,
+                       EpiArgs{ctx->dxn, H}, err, st));
     TIMED(P_NORM, rmsnorm_backward(ctx->dxn, a.resid_mid, w.ffn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
     // O projection
-    TIMED(P_GEMM, gemm_skinny(op(ctx->dres16, M, H, H), op(D + d.d_boT, 64, H, H), M, 64, ctx->dho, 64, ctx->skinny_ws, err, st));
-    const __half* woT = bwd_weight(ctx, w.woT, w.qT_o, w.s_o, Q, H, &e);
-    CK(e);
-    TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op(woT, Q, H, H), op(ctx->dho, M, 64, 64), op(D + d.d_aoT, Q, 64, 64), M, Q,
-            Epi::kStoreF16, EpiArgs{ctx->dattn, Q}, err, st));
+    {  // [dattn | dh_o] = dres . mo (MN-major): dres W'_o and dres s B_o
+      EpiArgs ea;
+      ea.out = ctx->dattn;
+      ea.ld_out = Q;
+      ea.n_main = Q;
+      ea.side = ctx->dho;
+      ea.ld_side = 64;
+      TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op_mn(w.mo, H, Q + 64, Q + 64), M, Q + 64, Epi::kStoreF16, ea, err,
+                         st));
+    }
     {
       LoraGradBatch gb{};
       gb.n = 2;
@@ -560,11 +555,16 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     TIMED(P_NORM, qknorm_rope_backward(ctx->dq, ctx->dk, a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, ctx->dqkv,
                             B, S, ctx->nh, ctx->nkv, ctx->hd, eps, st));
     // QKV projection
-    TIMED(P_GEMM, gemm_skinny(op(ctx->dqkv, M, QKV, QKV), op(D + d.d_bblkT, 64, QKV, QKV), M, 64, ctx->dhq, 64, ctx->skinny_ws, err, st));
-    const __half* wqkvT = bwd_weight(ctx, w.wqkvT, w.qT_qkv, w.s_qkv, H, QKV, &e);
-    CK(e);
-    TIMED(P_GEMM, gemm(op(ctx->dqkv, M, QKV, QKV), op(wqkvT, H, QKV, QKV), op(ctx->dhq, M, 64, 64), op(D + d.d_acatT, H, 64, 64),
-            M, H, Epi::kStoreF16, EpiArgs{ctx->dxn, H}, err, st));
+    {  // [dxn | dh_qkv] = dqkv . mqkv (MN-major)
+      EpiArgs ea;
+      ea.out = ctx->dxn;
+      ea.ld_out = H;
+      ea.n_main = H;
+      ea.side = ctx->dhq;
+      ea.ld_side = 64;
+      TIMED(P_GEMM, gemm(op(ctx->dqkv, M, QKV, QKV), op_mn(w.mqkv, QKV, H + 64, H + 64), M, H + 64, Epi::kStoreF16, ea,
+                         err, st));
+    }
     {
       LoraGradBatch gb{};
       gb.n = 4;
@@ -756,20 +756,18 @@ static llmcu_status upload_stage(llmcu_ctx* ctx, const float* host, size_t n) {
 }
 
 // Places one fp32 [rows, cols] weight (already in ctx->stage) into the fused
-// fp16 layout (row offset / gate-up interleave) and its transposed copy, or
-// into the INT8 layout (per-row quantiser + transposed int8 copy).
-static llmcu_status place_linear(llmcu_ctx* ctx, int rows, int cols, __half* w, __half* wT, int ld_t, int row_off,
-                                 int interleave, int8_t* q, int8_t* qT, float* s) {
+// fp16 layout (row offset / gate-up interleave), or into the INT8 layout
+// (per-row quantiser, src/kernels/quantize.cu:8-50).
+static llmcu_status place_linear(llmcu_ctx* ctx, int rows, int cols, __half* w, int row_off, int interleave,
+                                 int8_t* q, float* s) {
   if (ctx->rc.base_dtype != LLMCU_BASE_INT8) {
-    CK(convert_weight(ctx->stage, rows, cols, w, cols, row_off, interleave, wT, ld_t, 0, ctx->st));
+    CK(convert_weight(ctx->stage, rows, cols, w, cols, row_off, interleave, nullptr, 0, 0, ctx->st));
     return LLMCU_OK;
   }
-  // INT8: quantise rows of this tensor in place of the fused block
-  const int fused_row = interleave ? 0 : row_off;
   if (interleave) {
-    // quantise into a temporary block then scatter rows to the interleaved slots
+    // quantise into a temporary block then scatter 128-row blocks to the interleaved slots
     int8_t* tmp = reinterpret_cast<int8_t*>(ctx->dq_w);
-    float* stmp = reinterpret_cast<float*>(ctx->dq_wT);
+    float* stmp = ctx->q_scale_tmp;
     CK(quantize_rows_int8(ctx->stage, rows, cols, tmp, stmp, ctx->st));
     for (int r0 = 0; r0 < rows; r0 += 128) {
       const int dst_row = (r0 >> 7) * 256 + (interleave == 2 ? 128 : 0);
@@ -779,23 +777,7 @@ static llmcu_status place_linear(llmcu_ctx* ctx, int rows, int cols, __half* w, 
       CK(cudaMemcpyAsync(s + dst_row, stmp + r0, n * sizeof(float), cudaMemcpyDeviceToDevice, ctx->st));
     }
   } else {
-    CK(quantize_rows_int8(ctx->stage, rows, cols, q + static_cast<size_t>(fused_row) * cols, s + fused_row, ctx->st));
-  }
-  (void)qT;
-  (void)wT;
-  (void)ld_t;
-  return LLMCU_OK;
-}
-
-static llmcu_status finish_int8_transposes(llmcu_ctx* ctx, int layer) {
-  LayerW& w = ctx->lw[layer];
-  const int H = ctx->H, Q = ctx->Q, QKV = ctx->QKV, I = ctx->I;
-  struct T { const int8_t* q; int8_t* qT; int rows, cols; } ts[4] = {
-      {w.q_qkv, w.qT_qkv, QKV, H}, {w.q_o, w.qT_o, H, Q}, {w.q_gu, w.qT_gu, 2 * I, H}, {w.q_d, w.qT_d, H, I}};
-  for (auto& t : ts) {
-    dim3 grid((t.cols + 31) / 32, (t.rows + 31) / 32);
-    transpose_i8_kernel<<<grid, 256, 0, ctx->st>>>(t.q, t.rows, t.cols, t.qT);
-    CK(cudaGetLastError());
+    CK(quantize_rows_int8(ctx->stage, rows, cols, q + static_cast<size_t>(row_off) * cols, s + row_off, ctx->st));
   }
   return LLMCU_OK;
 }
@@ -803,7 +785,7 @@ static llmcu_status finish_int8_transposes(llmcu_ctx* ctx, int layer) {
 llmcu_status llmcu_set_base_tensor(llmcu_ctx* ctx, int id, int layer, const float* host) {
   if (!ctx || !host) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null argument");
   CK(cudaSetDevice(ctx->device));
-  const int H = ctx->H, Q = ctx->Q, KV = ctx->KV, QKV = ctx->QKV, I = ctx->I, V = ctx->V, hd = ctx->hd;
+  const int H = ctx->H, Q = ctx->Q, KV = ctx->KV, I = ctx->I, V = ctx->V, hd = ctx->hd;
   const bool per_layer = id >= LLMCU_T_ATTN_NORM && id < LLMCU_T_COUNT;
   if (per_layer && (layer < 0 || layer >= ctx->L)) return fail(ctx, LLMCU_ERR_INVALID_ARG, "layer %d out of range", layer);
   const bool int8 = ctx->rc.base_dtype == LLMCU_BASE_INT8;
@@ -811,11 +793,10 @@ llmcu_status llmcu_set_base_tensor(llmcu_ctx* ctx, int id, int layer, const floa
     case LLMCU_T_EMBED: {
       CKS(upload_stage(ctx, host, static_cast<size_t>(V) * H));
       if (!int8) {
-        CK(convert_weight(ctx->stage, V, H, ctx->E, H, 0, 0, ctx->ET, V, 0, ctx->st));
+        CK(convert_weight(ctx->stage, V, H, ctx->E, H, 0, 0, nullptr, 0, 0, ctx->st));
       } else {
         CK(quantize_rows_int8(ctx->stage, V, H, ctx->qE, ctx->sE, ctx->st));
         CK(dequant_rows_f16(ctx->qE, ctx->sE, V, H, ctx->E, ctx->st));
-        CK(transpose_f16(ctx->E, V, H, H, ctx->ET, V, ctx->st));
       }
       break;
     }
@@ -841,23 +822,13 @@ llmcu_status llmcu_set_base_tensor(llmcu_ctx* ctx, int id, int layer, const floa
       const int rows = id == LLMCU_T_WQ ? Q : KV;
       const int off = id == LLMCU_T_WQ ? 0 : (id == LLMCU_T_WK ? Q : Q + KV);
       CKS(upload_stage(ctx, host, static_cast<size_t>(rows) * H));
-      if (!int8) {
-        CK(convert_weight(ctx->stage, rows, H, w.wqkv, H, off, 0, w.wqkvT, QKV, off, ctx->st));
-      } else {
-        CKS(place_linear(ctx, rows, H, nullptr, nullptr, 0, off, 0, w.q_qkv, w.qT_qkv, w.s_qkv));
-        CKS(finish_int8_transposes(ctx, layer));
-      }
+      CKS(place_linear(ctx, rows, H, w.wqkv, off, 0, w.q_qkv, w.s_qkv));
       break;
     }
     case LLMCU_T_WO: {
       LayerW& w = ctx->lw[layer];
       CKS(upload_stage(ctx, host, static_cast<size_t>(H) * Q));
-      if (!int8) {
-        CK(convert_weight(ctx->stage, H, Q, w.wo, Q, 0, 0, w.woT, H, 0, ctx->st));
-      } else {
-        CKS(place_linear(ctx, H, Q, nullptr, nullptr, 0, 0, 0, w.q_o, w.qT_o, w.s_o));
-        CKS(finish_int8_transposes(ctx, layer));
-      }
+      CKS(place_linear(ctx, H, Q, w.wo, 0, 0, w.q_o, w.s_o));
       break;
     }
     case LLMCU_T_W_GATE:
@@ -865,23 +836,13 @@ llmcu_status llmcu_set_base_tensor(llmcu_ctx* ctx, int id, int layer, const floa
       LayerW& w = ctx->lw[layer];
       const int il = id == LLMCU_T_W_GATE ? 1 : 2;
       CKS(upload_stage(ctx, host, static_cast<size_t>(I) * H));
-      if (!int8) {
-        CK(convert_weight(ctx->stage, I, H, w.wgu, H, 0, il, w.wguT, 2 * I, 0, ctx->st));
-      } else {
-        CKS(place_linear(ctx, I, H, nullptr, nullptr, 0, 0, il, w.q_gu, w.qT_gu, w.s_gu));
-        CKS(finish_int8_transposes(ctx, layer));
-      }
+      CKS(place_linear(ctx, I, H, w.wgu, 0, il, w.q_gu, w.s_gu));
       break;
     }
     case LLMCU_T_W_DOWN: {
       LayerW& w = ctx->lw[layer];
       CKS(upload_stage(ctx, host, static_cast<size_t>(H) * I));
-      if (!int8) {
-        CK(convert_weight(ctx->stage, H, I, w.wd, I, 0, 0, w.wdT, H, 0, ctx->st));
-      } else {
-        CKS(place_linear(ctx, H, I, nullptr, nullptr, 0, 0, 0, w.q_d, w.qT_d, w.s_d));
-        CKS(finish_int8_transposes(ctx, layer));
-      }
+      CKS(place_linear(ctx, H, I, w.wd, 0, 0, w.q_d, w.s_d));
       break;
     }
     default:
@@ -940,36 +901,28 @@ llmcu_status llmcu_init_base_synthetic(llmcu_ctx* ctx, uint64_t seed, float stdd
   const int64_t H = ctx->H, Q = ctx->Q, QKV = ctx->QKV, I = ctx->I, V = ctx->V;
   cudaStream_t st = ctx->st;
   uint64_t k = seed * 1000003ull + 17;
-  auto lin = [&](int rows, int cols, __half* w, __half* wT, int8_t* q, int8_t* qT, float* s) -> llmcu_status {
+  auto lin = [&](int rows, int cols, __half* w, int8_t* q, float* s) -> llmcu_status {
     const int64_t n = static_cast<int64_t>(rows) * cols;
     if (ctx->rc.base_dtype != LLMCU_BASE_INT8) {
       CK(fill_normal_f16(w, n, k++, stddev, st));
-      CK(transpose_f16(w, rows, cols, cols, wT, rows, st));
     } else {
       CK(fill_normal_f32(ctx->stage, n, k++, stddev, st));
       CK(quantize_rows_int8(ctx->stage, rows, cols, q, s, st));
-      dim3 grid((cols + 31) / 32, (rows + 31) / 32);
-      transpose_i8_kernel<<<grid, 256, 0, st>>>(q, rows, cols, qT);
-      CK(cudaGetLastError());
     }
     return LLMCU_OK;
   };
   if (ctx->rc.base_dtype != LLMCU_BASE_INT8) {
     CK(fill_normal_f16(ctx->E, V * H, k++, stddev, st));
-    CK(transpose_f16(ctx->E, static_cast<int>(V), static_cast<int>(H), static_cast<int>(H), ctx->ET,
-                     static_cast<int>(V), st));
   } else {
     CK(fill_normal_f32(ctx->stage, V * H, k++, stddev, st));
     CK(quantize_rows_int8(ctx->stage, static_cast<int>(V), static_cast<int>(H), ctx->qE, ctx->sE, st));
     CK(dequant_rows_f16(ctx->qE, ctx->sE, static_cast<int>(V), static_cast<int>(H), ctx->E, st));
-    CK(transpose_f16(ctx->E, static_cast<int>(V), static_cast<int>(H), static_cast<int>(H), ctx->ET,
-                     static_cast<int>(V), st));
   }
   for (auto& w : ctx->lw) {
-    CKS(lin(static_cast<int>(QKV), static_cast<int>(H), w.wqkv, w.wqkvT, w.q_qkv, w.qT_qkv, w.s_qkv));
-    CKS(lin(static_cast<int>(H), static_cast<int>(Q), w.wo, w.woT, w.q_o, w.qT_o, w.s_o));
-    CKS(lin(static_cast<int>(2 * I), static_cast<int>(H), w.wgu, w.wguT, w.q_gu, w.qT_gu, w.s_gu));
-    CKS(lin(static_cast<int>(H), static_cast<int>(I), w.wd, w.wdT, w.q_d, w.qT_d, w.s_d));
+    CKS(lin(static_cast<int>(QKV), static_cast<int>(H), w.wqkv, w.q_qkv, w.s_qkv));
+    CKS(lin(static_cast<int>(H), static_cast<int>(Q), w.wo, w.q_o, w.s_o));
+    CKS(lin(static_cast<int>(2 * I), static_cast<int>(H), w.wgu, w.q_gu, w.s_gu));
+    CKS(lin(static_cast<int>(H), static_cast<int>(I), w.wd, w.q_d, w.s_d));
   }
   CK(cudaStreamSynchronize(st));
   return LLMCU_OK;
@@ -1266,9 +1219,25 @@ llmcu_status llmcu_gemm_nt_f16(const void* A, const void* B, float* C, int M, in
   EpiArgs ea;
   ea.out = C;
   ea.ld_out = ldc;
-  cudaError_t e = gemm(op(static_cast<const __half*>(A), M, K, lda), op(static_cast<const __half*>(B), N, K, ldb), kNone,
-                       kNone, M, N, Epi::kStoreF32, ea, d_err, static_cast<cudaStream_t>(stream));
+  cudaError_t e = gemm(op(static_cast<const __half*>(A), M, K, lda), op(static_cast<const __half*>(B), N, K, ldb), M,
+                       N, Epi::kStoreF32, ea, d_err, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? LLMCU_OK : LLMCU_ERR_CUDA;
+}
+
+llmcu_status llmcu_gemm_nn_f16(const void* A, const void* B, float* C, int M, int N, int K, int lda, int ldb, int ldc,
+                               void* stream) {
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0) return LLMCU_ERR_INVALID_ARG;
+  static int* d_err = nullptr;
+  if (!d_err) {
+    if (cudaMalloc(&d_err, sizeof(int)) != cudaSuccess) return LLMCU_ERR_CUDA;
+    cudaMemset(d_err, 0, sizeof(int));
+  }
+  EpiArgs ea;
+  ea.out = C;
+  ea.ld_out = ldc;
+  cudaError_t e = gemm(op(static_cast<const __half*>(A), M, K, lda), op_mn(static_cast<const __half*>(B), K, N, ldb),
+                       M, N, Epi::kStoreF32, ea, d_err, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? LLMCU_OK : (e == cudaErrorInvalidValue ? LLMCU_ERR_UNSUPPORTED : LLMCU_ERR_CUDA);
 }
 
 llmcu_status llmcu_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int batch, int seq,

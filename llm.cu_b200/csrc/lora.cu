@@ -4,15 +4,18 @@
 // A [r, d_in], B [d_out, r] as include/lora.h:13-20 of the reference), so
 // AdamW and the data-parallel allreduce each touch one contiguous range.
 //
-// lora_prep builds, per layer and per step, the fp16 operands the tcgen05
-// GEMMs consume as their 64-wide second K-segment (rank padded to 64):
-//   acat  [64, H]   rows 0.. = Aq, 16.. = Ak, 32.. = Av (r rows each) (and acatT)
-//   bblk  [QKV, 64] block-diagonal s*Bq | s*Bk | s*Bv, same columns  (and bblkT)
-// (each rank segment starts on a 16-column boundary so every operand view
-// h + 16*i stays 32-byte aligned for the 16-byte async copies)
-//   ao    [64, Q]   rows 0..r-1 = Ao                               (and aoT)
-//   bo    [H, 64]   cols 0..r-1 = s*Bo                             (and boT)
-// with s = alpha / r folded into B (src/kernels/lora.cu:190-198).
+// lora_merge builds, per layer and per step, the merged fp16 weights the
+// tcgen05 GEMMs use in place of the reference's separate LoRA products
+// (src/kernels/lora.cu:181-202: y += s (x A^T) B^T, s = alpha / r):
+//   mqkv [QKV + 64, H + 64]  rows < QKV:   W_qkv + s B_p A_p (p = q, k, v by row)
+//                            cols H + seg(p) + j:   s B_p[:, j]
+//                            rows QKV + seg(p) + j: A_p[j, :]
+//   mo   [H + 64, Q + 64]    rows < H: W_o + s B_o A_o; cols Q + j: s B_o[:, j];
+//                            rows H + j: A_o[j, :]
+// seg(q, k, v) = 0, 16, 32 (kSegK, kSegV); everything else in the pads is 0.
+// The forward GEMM x . mqkv^T (K-major, N = QKV + 64) then yields q, k, v and,
+// in its last 64 columns, h = x [Aq | Ak | Av]^T; the input-gradient GEMM
+// dY . mqkv (MN-major, N = H + 64) yields dx and dh = dY [s Bq | s Bk | s Bv].
 //
 // lora_grad computes C[a, b] = scale * sum_m U[m, a] * W[m, b] (b < 16) for a
 // batch of problems -- the reference's matmul_tn + scale_add
@@ -27,60 +30,167 @@ namespace llmcu {
 
 namespace {
 
-__global__ void lora_prep_kernel(const float* __restrict__ flat, LoraDims d, __half* __restrict__ derived) {
+// Main block of one merged weight: rows [o0, o0 + 32), columns
+// [c0, c0 + 256) of W + s B A for one adapter (A [r, d_in], B [rows_p, r]).
+// Base W is fp16 (w) or INT8 rows (q) times the per-row scale (sc), as the
+// reference's quantiser lays them out (src/kernels/quantize.cu:8-50).
+struct MergeSrc {
+  const __half* w;
+  const int8_t* q;
+  const float* sc;
+  int64_t w_layer;   // elements between layers of w / q
+  int64_t sc_layer;  // elements between layers of sc
+};
+constexpr int kMrgRows = 64;
+constexpr int kMrgCols = 256;
+
+// 256 threads; thread (rg = t / 32, cg = t % 32) owns rows rg*8.. and
+// columns cg*8.. of the 64 x 256 tile: 64 accumulators start from W and take
+// 16 rank-1 updates, each from two 8-float smem vectors (A[j, cols] and
+// s*B[rows, j]), so a warp's global rows are 512 contiguous bytes.
+__global__ void __launch_bounds__(256)
+    lora_merge_main_kernel(const float* __restrict__ flat, LoraDims d, MergeSrc src, int out_rows, int d_in,
+                           int which, __half* __restrict__ merged, int64_t merged_layer, int ldm) {
+  __shared__ __align__(16) float As[16][kMrgCols];
+  __shared__ __align__(16) float Bs[16][kMrgRows];  // s * B, transposed: [j][row]
+  const int l = blockIdx.z;
+  const int o0 = blockIdx.y * kMrgRows, c0 = blockIdx.x * kMrgCols;
+  const float* P = flat + static_cast<int64_t>(l) * d.per_layer;
+  // adapter owning rows [o0, o0 + 64): which = 0 -> q/k/v by row, 1 -> o
+  int proj, row_base;
+  if (which == 1) {
+    proj = 3;
+    row_base = 0;
+  } else if (o0 < d.Q) {
+    proj = 0;
+    row_base = 0;
+  } else if (o0 < d.Q + d.KV) {
+    proj = 1;
+    row_base = d.Q;
+  } else {
+    proj = 2;
+    row_base = d.Q + d.KV;
+  }
+  const float* A = P + d.offA(proj);
+  const float* Bm = P + d.offB(proj);
+  const int r = d.r;
+  for (int i = threadIdx.x; i < 16 * kMrgCols; i += 256) {
+    const int j = i / kMrgCols, c = i % kMrgCols;
+    As[j][c] = (j < r && c0 + c < d_in) ? A[static_cast<int64_t>(j) * d_in + c0 + c] : 0.f;
+  }
+  for (int i = threadIdx.x; i < 16 * kMrgRows; i += 256) {
+    const int rr = i / 16, j = i % 16;
+    const int o = o0 + rr;
+    Bs[j][rr] = (j < r && o < out_rows) ? d.scale * Bm[static_cast<int64_t>(o - row_base) * r + j] : 0.f;
+  }
+  __syncthreads();
+  const int rg = threadIdx.x >> 5, cg = threadIdx.x & 31;
+  const int c = c0 + 8 * cg;
+  if (c >= d_in) return;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int o = o0 + 8 * rg + i;
+    if (o >= out_rows) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
+      continue;
+    }
+    if (src.q) {
+      const int8_t* qr = src.q + static_cast<int64_t>(l) * src.w_layer + static_cast<int64_t>(o) * d_in + c;
+      const float sc = src.sc[static_cast<int64_t>(l) * src.sc_layer + o];
+      const int2 raw = *reinterpret_cast<const int2*>(qr);
+      const int8_t* qb = reinterpret_cast<const int8_t*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[i][e] = static_cast<float>(qb[e]) * sc;
+    } else {
+      const uint4 raw = *reinterpret_cast<const uint4*>(src.w + static_cast<int64_t>(l) * src.w_layer +
+                                                        static_cast<int64_t>(o) * d_in + c);
+      const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(h[e]);
+        acc[i][2 * e] = f.x;
+        acc[i][2 * e + 1] = f.y;
+      }
+    }
+  }
+#pragma unroll 4
+  for (int j = 0; j < 16; ++j) {
+    const float4 a0 = *reinterpret_cast<const float4*>(&As[j][8 * cg]);
+    const float4 a1 = *reinterpret_cast<const float4*>(&As[j][8 * cg + 4]);
+    const float4 b0 = *reinterpret_cast<const float4*>(&Bs[j][8 * rg]);
+    const float4 b1 = *reinterpret_cast<const float4*>(&Bs[j][8 * rg + 4]);
+    const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[i][e] = fmaf(b[i], a[e], acc[i][e]);
+  }
+  __half* out = merged + static_cast<int64_t>(l) * merged_layer;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int o = o0 + 8 * rg + i;
+    if (o >= out_rows) break;
+    uint4 w;
+    w.x = pack_half2(acc[i][0], acc[i][1]);
+    w.y = pack_half2(acc[i][2], acc[i][3]);
+    w.z = pack_half2(acc[i][4], acc[i][5]);
+    w.w = pack_half2(acc[i][6], acc[i][7]);
+    *reinterpret_cast<uint4*>(out + static_cast<int64_t>(o) * ldm + c) = w;
+  }
+}
+
+// The pads of both merged weights: the 64 extra columns (s B) of the rows
+// < out_rows and the 64 extra rows (A) of the columns < d_in.
+__global__ void lora_merge_pad_kernel(const float* __restrict__ flat, LoraDims d, __half* __restrict__ mqkv,
+                                      int64_t mqkv_layer, __half* __restrict__ mo, int64_t mo_layer) {
   const int l = blockIdx.y;
   const float* P = flat + static_cast<int64_t>(l) * d.per_layer;
-  __half* D = derived + static_cast<int64_t>(l) * d.derived_per_layer;
   const int r = d.r, H = d.H, Q = d.Q, KV = d.KV, QKV = Q + 2 * KV;
-  const float s = d.scale;
-  const int64_t n_acat = 64LL * H, n_bblk = 64LL * QKV, n_ao = 64LL * Q, n_bo = 64LL * H;
-  const int64_t total = n_acat + n_bblk + n_ao + n_bo;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    int64_t k = i;
-    if (k < n_acat) {  // acat[j, c]
-      const int j = static_cast<int>(k / H), c = static_cast<int>(k % H);
-      float v = 0.f;
-      if (j < r) v = P[d.oAq + j * H + c];
-      else if (j >= kSegK && j < kSegK + r) v = P[d.oAk + (j - kSegK) * H + c];
-      else if (j >= kSegV && j < kSegV + r) v = P[d.oAv + (j - kSegV) * H + c];
-      const __half hv = __float2half_rn(v);
-      D[d.d_acat + k] = hv;
-      D[d.d_acatT + static_cast<int64_t>(c) * 64 + j] = hv;
-      continue;
-    }
-    k -= n_acat;
-    if (k < n_bblk) {  // bblk[n, j]
-      const int n = static_cast<int>(k / 64), j = static_cast<int>(k % 64);
+  const int n_cq = 64 * QKV, n_rq = 64 * H, n_co = 64 * H, n_ro = 64 * Q;
+  const int total = n_cq + n_rq + n_co + n_ro;
+  __half* Mq = mqkv + static_cast<int64_t>(l) * mqkv_layer;
+  __half* Mo = mo + static_cast<int64_t>(l) * mo_layer;
+  const int ldq = H + 64, ldo = Q + 64;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    int k = i;
+    if (k < n_cq) {  // mqkv[n, H + j] = s * B_p[n', j - seg(p)]
+      const int n = k >> 6, j = k & 63;
       float v = 0.f;
       if (n < Q) {
-        if (j < r) v = s * P[d.oBq + n * r + j];
+        if (j < r) v = d.scale * P[d.oBq + static_cast<int64_t>(n) * r + j];
       } else if (n < Q + KV) {
-        if (j >= kSegK && j < kSegK + r) v = s * P[d.oBk + (n - Q) * r + (j - kSegK)];
+        if (j >= kSegK && j < kSegK + r) v = d.scale * P[d.oBk + static_cast<int64_t>(n - Q) * r + (j - kSegK)];
       } else {
-        if (j >= kSegV && j < kSegV + r) v = s * P[d.oBv + (n - Q - KV) * r + (j - kSegV)];
+        if (j >= kSegV && j < kSegV + r) v = d.scale * P[d.oBv + static_cast<int64_t>(n - Q - KV) * r + (j - kSegV)];
       }
-      const __half hv = __float2half_rn(v);
-      D[d.d_bblk + k] = hv;
-      D[d.d_bblkT + static_cast<int64_t>(j) * QKV + n] = hv;
+      Mq[static_cast<int64_t>(n) * ldq + H + j] = __float2half_rn(v);
       continue;
     }
-    k -= n_bblk;
-    if (k < n_ao) {  // ao[j, c]
-      const int j = static_cast<int>(k / Q), c = static_cast<int>(k % Q);
-      const float v = j < r ? P[d.oAo + j * Q + c] : 0.f;
-      const __half hv = __float2half_rn(v);
-      D[d.d_ao + k] = hv;
-      D[d.d_aoT + static_cast<int64_t>(c) * 64 + j] = hv;
+    k -= n_cq;
+    if (k < n_rq) {  // mqkv[QKV + j, c] = A_p[j - seg(p), c]
+      const int j = k / H, c = k % H;
+      float v = 0.f;
+      if (j < r) v = P[d.oAq + static_cast<int64_t>(j) * H + c];
+      else if (j >= kSegK && j < kSegK + r) v = P[d.oAk + static_cast<int64_t>(j - kSegK) * H + c];
+      else if (j >= kSegV && j < kSegV + r) v = P[d.oAv + static_cast<int64_t>(j - kSegV) * H + c];
+      Mq[static_cast<int64_t>(QKV + j) * ldq + c] = __float2half_rn(v);
       continue;
     }
-    k -= n_ao;
-    {  // bo[h, j]
-      const int h = static_cast<int>(k / 64), j = static_cast<int>(k % 64);
-      const float v = j < r ? s * P[d.oBo + h * r + j] : 0.f;
-      const __half hv = __float2half_rn(v);
-      D[d.d_bo + k] = hv;
-      D[d.d_boT + static_cast<int64_t>(j) * H + h] = hv;
+    k -= n_rq;
+    if (k < n_co) {  // mo[n, Q + j] = s * Bo[n, j]
+      const int n = k >> 6, j = k & 63;
+      const float v = j < r ? d.scale * P[d.oBo + static_cast<int64_t>(n) * r + j] : 0.f;
+      Mo[static_cast<int64_t>(n) * ldo + Q + j] = __float2half_rn(v);
+      continue;
+    }
+    k -= n_co;
+    {  // mo[H + j, c] = Ao[j, c]
+      const int j = k / Q, c = k % Q;
+      const float v = j < r ? P[d.oAo + static_cast<int64_t>(j) * Q + c] : 0.f;
+      Mo[static_cast<int64_t>(H + j) * ldo + c] = __float2half_rn(v);
     }
   }
 }
@@ -185,12 +295,20 @@ __global__ void lora_grad_reduce_kernel(const LoraGradBatch batch, int splits, c
 
 }  // namespace
 
-cudaError_t lora_prep(const float* flat, const LoraDims& d, int n_layers, __half* derived, cudaStream_t st) {
-  const int64_t total = 64LL * (2 * d.H + d.Q + 2 * d.KV + d.Q);
-  int gx = static_cast<int>((total + 255) / 256);
-  if (gx > 512) gx = 512;
-  dim3 grid(gx, n_layers);
-  lora_prep_kernel<<<grid, 256, 0, st>>>(flat, d, derived);
+cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const MergeWeights& base, __half* mqkv,
+                       __half* mo, cudaStream_t st) {
+  const int H = d.H, Q = d.Q, KV = d.KV, QKV = Q + 2 * KV;
+  if (d.r > 16 || Q % kMrgRows || KV % kMrgRows || H % kMrgRows || H % 8 || Q % 8) return cudaErrorInvalidValue;
+  if (64LL * (QKV + 2 * H + Q) >= (1LL << 31)) return cudaErrorInvalidValue;
+  const int64_t mqkv_layer = merged_qkv_elems(d), mo_layer = merged_o_elems(d);
+  MergeSrc sq{base.wqkv, base.q_qkv, base.s_qkv, base.w_layer_qkv, base.s_layer_qkv};
+  MergeSrc so{base.wo, base.q_o, base.s_o, base.w_layer_o, base.s_layer_o};
+  dim3 gq((H + kMrgCols - 1) / kMrgCols, QKV / kMrgRows, n_layers);
+  lora_merge_main_kernel<<<gq, 256, 0, st>>>(flat, d, sq, QKV, H, 0, mqkv, mqkv_layer, H + 64);
+  dim3 go((Q + kMrgCols - 1) / kMrgCols, H / kMrgRows, n_layers);
+  lora_merge_main_kernel<<<go, 256, 0, st>>>(flat, d, so, H, Q, 1, mo, mo_layer, Q + 64);
+  dim3 gp(128, n_layers);
+  lora_merge_pad_kernel<<<gp, 256, 0, st>>>(flat, d, mqkv, mqkv_layer, mo, mo_layer);
   return cudaGetLastError();
 }
 

@@ -8,13 +8,11 @@
 namespace llmcu {
 
 // Offsets (in floats) of each adapter inside one layer of the flat fp32
-// buffer, and of each derived fp16 operand inside one layer of the derived
 // buffer.  A [r, d_in], B [d_out, r] row-major.
 struct LoraDims {
   int r, H, Q, KV;
   float scale;  // alpha / r
   int64_t oAq, oBq, oAk, oBk, oAv, oBv, oAo, oBo, per_layer;
-  int64_t d_acat, d_acatT, d_bblk, d_bblkT, d_ao, d_aoT, d_bo, d_boT, derived_per_layer;
 
   static LoraDims make(int r, int H, int Q, int KV, float scale) {
     LoraDims d{};
@@ -29,25 +27,28 @@ struct LoraDims {
     d.oAo = o; o += static_cast<int64_t>(r) * Q;
     d.oBo = o; o += static_cast<int64_t>(H) * r;
     d.per_layer = o;
-    const int64_t QKV = Q + 2 * KV;
-    int64_t e = 0;
-    auto al = [](int64_t x) { return (x + 127) / 128 * 128; };  // keep every operand 256-byte aligned
-    d.d_acat = e; e = al(e + 64LL * H);
-    d.d_acatT = e; e = al(e + 64LL * H);
-    d.d_bblk = e; e = al(e + 64LL * QKV);
-    d.d_bblkT = e; e = al(e + 64LL * QKV);
-    d.d_ao = e; e = al(e + 64LL * Q);
-    d.d_aoT = e; e = al(e + 64LL * Q);
-    d.d_bo = e; e = al(e + 64LL * H);
-    d.d_boT = e; e = al(e + 64LL * H);
-    d.derived_per_layer = e;
     return d;
   }
   // adapter (proj 0..3 = q, k, v, o) offsets and dims
-  int64_t offA(int proj) const { return proj == 0 ? oAq : proj == 1 ? oAk : proj == 2 ? oAv : oAo; }
-  int64_t offB(int proj) const { return proj == 0 ? oBq : proj == 1 ? oBk : proj == 2 ? oBv : oBo; }
-  int d_in(int proj) const { return proj == 3 ? Q : H; }
-  int d_out(int proj) const { return proj == 0 ? Q : proj == 3 ? H : KV; }
+  __host__ __device__ int64_t offA(int proj) const { return proj == 0 ? oAq : proj == 1 ? oAk : proj == 2 ? oAv : oAo; }
+  __host__ __device__ int64_t offB(int proj) const { return proj == 0 ? oBq : proj == 1 ? oBk : proj == 2 ? oBv : oBo; }
+  __host__ __device__ int d_in(int proj) const { return proj == 3 ? Q : H; }
+  __host__ __device__ int d_out(int proj) const { return proj == 0 ? Q : proj == 3 ? H : KV; }
+};
+
+// Merged weights of one layer (see lora.cu): [QKV + 64, H + 64] and [H + 64, Q + 64].
+inline int64_t merged_qkv_elems(const LoraDims& d) {
+  return (static_cast<int64_t>(d.Q + 2 * d.KV) + 64) * (d.H + 64);
+}
+inline int64_t merged_o_elems(const LoraDims& d) { return (static_cast<int64_t>(d.H) + 64) * (d.Q + 64); }
+
+// Base q/k/v and o weights of every layer: fp16 (w*) or INT8 rows (q*) with
+// per-row scales (s*); *_layer = elements between consecutive layers.
+struct MergeWeights {
+  const __half *wqkv = nullptr, *wo = nullptr;
+  const int8_t *q_qkv = nullptr, *q_o = nullptr;
+  const float *s_qkv = nullptr, *s_o = nullptr;
+  int64_t w_layer_qkv = 0, w_layer_o = 0, s_layer_qkv = 0, s_layer_o = 0;
 };
 
 constexpr int kLoraMaxProbs = 8;
@@ -77,7 +78,8 @@ struct LoraGradBatch {
   int a_max;  // multiple of 64, >= every A
 };
 
-cudaError_t lora_prep(const float* flat, const LoraDims& d, int n_layers, __half* derived, cudaStream_t st);
+cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const MergeWeights& base, __half* mqkv,
+                       __half* mo, cudaStream_t st);
 cudaError_t lora_grad(const LoraGradBatch& batch, int M, float* part, cudaStream_t st);
 int lora_grad_splits(int M, int a_max, int n);
 

@@ -140,6 +140,8 @@ _SIGS = {
     "llmcu_profile_read": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.c_int]),
     "llmcu_gemm_nt_f16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                     C.c_int, C.c_int, C.c_void_p]),
+    "llmcu_gemm_nn_f16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                    C.c_int, C.c_int, C.c_void_p]),
     "llmcu_attention_fwd": (C.c_int, [C.c_void_p] * 5 + [C.c_int] * 8 + [C.c_void_p]),
     "llmcu_attention_bwd": (C.c_int, [C.c_void_p] * 10 + [C.c_int] * 9 + [C.c_void_p]),
     "llmcu_attention_bwd_noalloc": (C.c_int, [C.c_void_p] * 9 + [C.c_int] * 9 + [C.c_void_p]),
@@ -379,6 +381,10 @@ def _chk(st, what):
 
 def gemm_nt_f16(A_ptr, B_ptr, C_ptr, M, N, K, lda, ldb, ldc, stream=0):
     _chk(lib().llmcu_gemm_nt_f16(A_ptr, B_ptr, C_ptr, M, N, K, lda, ldb, ldc, stream), "gemm_nt_f16")
+
+
+def gemm_nn_f16(A_ptr, B_ptr, C_ptr, M, N, K, lda, ldb, ldc, stream=0):
+    _chk(lib().llmcu_gemm_nn_f16(A_ptr, B_ptr, C_ptr, M, N, K, lda, ldb, ldc, stream), "gemm_nn_f16")
 
 
 def attention_fwd(q, k, v, o, lse, batch, seq, nh, nkv, hd, ldq, ldk, ldv, stream=0):

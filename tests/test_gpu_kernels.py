@@ -39,6 +39,23 @@ def test_gemm_nt_matches_torch(llmcu, cuda_device, M, N, K):
         assert rel_l2(C, ref) < 1e-3
 
 
+@pytest.mark.parametrize("M,N,K", [(4096, 2048, 2048), (32, 64, 256), (200, 296, 200), (4096, 6144, 2048),
+                                   (1000, 2112, 4096)])
+def test_gemm_nn_matches_torch(llmcu, cuda_device, M, N, K):
+    """B read MN-major ([K, N] row-major), the input-gradient GEMMs' operand.
+    Row strides must be multiples of 16 bytes (TMA), so N is a multiple of 8."""
+    g = torch.Generator(device="cpu").manual_seed(M * 5 + N)
+    A = torch.randn(M, K, generator=g).half().to(cuda_device)
+    B = torch.randn(K, N, generator=g).half().to(cuda_device)
+    ref = A.float() @ B.float()
+    C = torch.full((M, N), float("nan"), device=cuda_device, dtype=torch.float32)
+    llmcu.gemm_nn_f16(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, K, N, N,
+                      torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert torch.isfinite(C).all()
+    assert rel_l2(C, ref) < 1e-3
+
+
 def _attn_ref(q, k, v, B, S, nh, nkv, hd):
     qh = q.view(B, S, nh, hd).transpose(1, 2)
     kh = k.view(B, S, nkv, hd).repeat_interleave(nh // nkv, dim=2).transpose(1, 2)
