@@ -107,7 +107,7 @@ cudaError_t dispatch(Epi epi, const EpiArgs& ea, const CUtensorMap* maps, const 
       return launch<BN, EpiResidF32, BMN>(maps, sh, EpiResidF32::Params{}, err, st);
     case Epi::kSwiGLUBwd:
       if constexpr (BN == 256) {
-        return launch<BN, EpiSwiGLUBwd, BMN>(maps, sh, EpiSwiGLUBwd::Params{}, err, st);
+        return launch<BN, EpiSwiGLUBwd, BMN>(maps, sh, EpiSwiGLUBwd::Params{ea.gu_in, ea.ld_gu}, err, st);
       } else {
         return cudaErrorInvalidValue;
       }
@@ -172,9 +172,10 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
       okc = make_io_map(&maps[2], ea.gu, M, N, ea.ld_gu, false) &&
             make_io_map(&maps[3], ea.act, M, N / 2, ea.ld_act, false);
       break;
-    case Epi::kSwiGLUBwd:  // C = dgu [M, 2N] out, D = gu [M, 2N] in
-      okc = make_io_map(&maps[2], ea.gu, M, 2 * N, ea.ld_gu, false) &&
-            make_io_map(&maps[3], ea.gu_in, M, 2 * N, ea.ld_gu, false);
+    case Epi::kSwiGLUBwd:  // C = dgu [M, 2N] out; gu [M, 2N] is read with plain loads
+      okc = make_io_map(&maps[2], ea.gu, M, 2 * N, ea.ld_gu, false) && ea.gu_in &&
+            reinterpret_cast<uintptr_t>(ea.gu_in) % 16 == 0 && ea.ld_gu % 8 == 0;
+      maps[3] = maps[2];
       break;
   }
   if (!okc) return cudaErrorInvalidValue;

@@ -333,30 +333,40 @@ struct EpiSwiGLU {
 };
 
 // Down-projection dX with the SwiGLU backward fused (src/kernels/activation.cu:26-38):
-// acc = d_act[row, i]; reads g, u from the interleaved stash (mapD) and writes
-// dg, du into the same interleaved layout of dgu (mapC), the A operand of the
-// gate/up dX GEMM.
+// acc = d_act[row, i]; reads g, u from the interleaved stash and writes dg, du
+// into the same interleaved layout of dgu (mapC), the A operand of the
+// gate/up dX GEMM.  g and u arrive by plain 16-byte loads (each thread its
+// row's 128 contiguous bytes of each), so the epilogue needs only the output
+// slab and the mainloop keeps four pipeline stages.
 struct EpiSwiGLUBwd {
-  struct Params {};
+  struct Params {
+    const __half* gu_in;  // [M, 2N] interleaved pre-activations
+    int ld;
+  };
   struct State {};
   static constexpr int kChunk = 64;
-  static constexpr int kSlab = 2 * kSlabBytes;  // g and u boxes side by side
+  static constexpr int kSlab = kSlabBytes;
   static constexpr bool kPaired = false;
   static constexpr bool kStores = true;
   __device__ static void begin(State&, const Params&, const EpiCtx&, int) {}
-  __device__ static bool chunk(State&, const Params&, EpiCtx& c, int col0, const float* v) {
+  __device__ static bool chunk(State&, const Params& p, EpiCtx& c, int col0, const float* v) {
     if (col0 >= c.N) return true;
     // col0 is a multiple of 64: the 64 columns share one 128-column block
     const int gcol = (col0 >> 7) * 256 + (col0 & 127);
     uint32_t gp[32], up[32];  // g and u as packed half2, later dg and du
-    slab_wait_read(c);
-    if (!slab_load2(c, c.mapD, gcol, gcol + 128, c.row0)) return false;
+    if (c.row < c.M) {
+      const uint4* gsrc = reinterpret_cast<const uint4*>(p.gu_in + static_cast<size_t>(c.row) * p.ld + gcol);
+      const uint4* usrc = gsrc + 128 / 8;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint4 w = slab_ld(c, j, 0);
-      gp[4 * j] = w.x; gp[4 * j + 1] = w.y; gp[4 * j + 2] = w.z; gp[4 * j + 3] = w.w;
-      const uint4 x = slab_ld(c, j, 1);
-      up[4 * j] = x.x; up[4 * j + 1] = x.y; up[4 * j + 2] = x.z; up[4 * j + 3] = x.w;
+      for (int j = 0; j < 8; ++j) {
+        const uint4 w = __ldg(gsrc + j);
+        gp[4 * j] = w.x; gp[4 * j + 1] = w.y; gp[4 * j + 2] = w.z; gp[4 * j + 3] = w.w;
+        const uint4 x = __ldg(usrc + j);
+        up[4 * j] = x.x; up[4 * j + 1] = x.y; up[4 * j + 2] = x.z; up[4 * j + 3] = x.w;
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 32; ++t) gp[t] = up[t] = 0u;
     }
 #pragma unroll
     for (int t = 0; t < 32; ++t) {
@@ -367,20 +377,14 @@ struct EpiSwiGLUBwd {
       gp[t] = pack_half2(d0 * u2.x * s0 * (1.0f + g2.x * (1.0f - s0)), d1 * u2.y * s1 * (1.0f + g2.y * (1.0f - s1)));
       up[t] = pack_half2(d0 * g2.x * s0, d1 * g2.y * s1);
     }
-    __syncwarp();
+    slab_wait_read(c);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      slab_st(c, j, make_uint4(gp[4 * j], gp[4 * j + 1], gp[4 * j + 2], gp[4 * j + 3]), 0);
-      slab_st(c, j, make_uint4(up[4 * j], up[4 * j + 1], up[4 * j + 2], up[4 * j + 3]), 1);
-    }
-    slab_store(c, c.mapC, gcol, c.row0, 0);
-    if (c.lane == 0) {
-      asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                       reinterpret_cast<uint64_t>(c.mapC)),
-                   "r"(c.slab + kSlabBytes), "r"(gcol + 128), "r"(c.row0)
-                   : "memory");
-      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-    }
+    for (int j = 0; j < 8; ++j) slab_st(c, j, make_uint4(gp[4 * j], gp[4 * j + 1], gp[4 * j + 2], gp[4 * j + 3]));
+    slab_store(c, c.mapC, gcol, c.row0);
+    slab_wait_read(c);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) slab_st(c, j, make_uint4(up[4 * j], up[4 * j + 1], up[4 * j + 2], up[4 * j + 3]));
+    slab_store(c, c.mapC, gcol + 128, c.row0);
     return true;
   }
   __device__ static void end(State&, const Params&, const EpiCtx&, int) {}

@@ -41,104 +41,128 @@ struct MergeSrc {
   int64_t w_layer;   // elements between layers of w / q
   int64_t sc_layer;  // elements between layers of sc
 };
-constexpr int kMrgRows = 64;
-constexpr int kMrgCols = 256;
+constexpr int kMrgRows = 64;   // rows of one row tile
+constexpr int kMrgCols = 256;  // columns of a block
+constexpr int kMrgTiles = 4;   // row tiles per block (fewer when an adapter has fewer rows)
 
-// 256 threads; thread (rg = t / 32, cg = t % 32) owns rows rg*8.. and
-// columns cg*8.. of the 64 x 256 tile: 64 accumulators start from W and take
-// 16 rank-1 updates, each from two 8-float smem vectors (A[j, cols] and
-// s*B[rows, j]), so a warp's global rows are 512 contiguous bytes.
-__global__ void __launch_bounds__(256)
+// Base weight row o, columns [c, c + 8): fp16 bits, or INT8 codes + row scale.
+struct MergeRaw {
+  uint4 bits;  // 8 fp16, or 8 int8 in the low 8 bytes
+  float sc;
+};
+__device__ __forceinline__ MergeRaw merge_load(const MergeSrc& src, int l, int o, int d_in, int c) {
+  MergeRaw m;
+  const int64_t off = static_cast<int64_t>(l) * src.w_layer + static_cast<int64_t>(o) * d_in + c;
+  if (src.q) {
+    const int2 raw = *reinterpret_cast<const int2*>(src.q + off);
+    m.bits = make_uint4(static_cast<uint32_t>(raw.x), static_cast<uint32_t>(raw.y), 0u, 0u);
+    m.sc = src.sc[static_cast<int64_t>(l) * src.sc_layer + o];
+  } else {
+    m.bits = *reinterpret_cast<const uint4*>(src.w + off);
+    m.sc = 1.f;
+  }
+  return m;
+}
+__device__ __forceinline__ void merge_unpack(const MergeRaw& m, bool int8, float (&v)[8]) {
+  if (int8) {
+    const int8_t* qb = reinterpret_cast<const int8_t*>(&m.bits);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = static_cast<float>(qb[e]) * m.sc;
+  } else {
+    const __half2* h = reinterpret_cast<const __half2*>(&m.bits);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      v[2 * e] = f.x;
+      v[2 * e + 1] = f.y;
+    }
+  }
+}
+
+// 256 threads; a block covers `tiles` row tiles of 64 rows (one adapter) and
+// 256 columns.  Thread (rg = t / 32, cg = t % 32) owns rows rg*8.. and
+// columns cg*8.. of each row tile: 64 accumulators start from W and take 16
+// rank-1 updates from two 8-float smem vectors (A[j, cols] and s*B[rows, j]);
+// a warp's global rows are 512 contiguous bytes.  The next tile's W rows are
+// loaded while the current tile is computed.
+__global__ void __launch_bounds__(256, 1)
     lora_merge_main_kernel(const float* __restrict__ flat, LoraDims d, MergeSrc src, int out_rows, int d_in,
-                           int which, __half* __restrict__ merged, int64_t merged_layer, int ldm) {
+                           int which, int tiles, __half* __restrict__ merged, int64_t merged_layer, int ldm) {
   __shared__ __align__(16) float As[16][kMrgCols];
-  __shared__ __align__(16) float Bs[16][kMrgRows];  // s * B, transposed: [j][row]
+  __shared__ __align__(16) float Bs[kMrgTiles][16][kMrgRows];  // s * B, transposed: [tile][j][row]
   const int l = blockIdx.z;
-  const int o0 = blockIdx.y * kMrgRows, c0 = blockIdx.x * kMrgCols;
+  const int ob = blockIdx.y * kMrgRows * tiles, c0 = blockIdx.x * kMrgCols;
   const float* P = flat + static_cast<int64_t>(l) * d.per_layer;
-  // adapter owning rows [o0, o0 + 64): which = 0 -> q/k/v by row, 1 -> o
+  // adapter owning rows [ob, ob + 64 * tiles): which = 0 -> q/k/v by row, 1 -> o
   int proj, row_base;
   if (which == 1) {
     proj = 3;
     row_base = 0;
-  } else if (o0 < d.Q) {
+  } else if (ob < d.Q) {
     proj = 0;
     row_base = 0;
-  } else if (o0 < d.Q + d.KV) {
+  } else if (ob < d.Q + d.KV) {
     proj = 1;
     row_base = d.Q;
   } else {
     proj = 2;
     row_base = d.Q + d.KV;
   }
+  const int rg = threadIdx.x >> 5, cg = threadIdx.x & 31;
+  const int c = c0 + 8 * cg;
+  const bool col_ok = c < d_in;
+  const bool int8 = src.q != nullptr;
+  MergeRaw raw[8];
+  if (col_ok) {  // first tile's W rows, in flight while the adapters are staged
+#pragma unroll
+    for (int i = 0; i < 8; ++i) raw[i] = merge_load(src, l, ob + 8 * rg + i, d_in, c);
+  }
   const float* A = P + d.offA(proj);
   const float* Bm = P + d.offB(proj);
   const int r = d.r;
   for (int i = threadIdx.x; i < 16 * kMrgCols; i += 256) {
-    const int j = i / kMrgCols, c = i % kMrgCols;
-    As[j][c] = (j < r && c0 + c < d_in) ? A[static_cast<int64_t>(j) * d_in + c0 + c] : 0.f;
+    const int j = i / kMrgCols, cc = i % kMrgCols;
+    As[j][cc] = (j < r && c0 + cc < d_in) ? A[static_cast<int64_t>(j) * d_in + c0 + cc] : 0.f;
   }
-  for (int i = threadIdx.x; i < 16 * kMrgRows; i += 256) {
-    const int rr = i / 16, j = i % 16;
-    const int o = o0 + rr;
-    Bs[j][rr] = (j < r && o < out_rows) ? d.scale * Bm[static_cast<int64_t>(o - row_base) * r + j] : 0.f;
+  for (int i = threadIdx.x; i < tiles * 16 * kMrgRows; i += 256) {
+    const int t = i / (16 * kMrgRows), rr = (i / 16) % kMrgRows, j = i % 16;
+    const int o = ob + t * kMrgRows + rr;
+    Bs[t][j][rr] = j < r ? d.scale * Bm[static_cast<int64_t>(o - row_base) * r + j] : 0.f;
   }
   __syncthreads();
-  const int rg = threadIdx.x >> 5, cg = threadIdx.x & 31;
-  const int c = c0 + 8 * cg;
-  if (c >= d_in) return;
-  float acc[8][8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int o = o0 + 8 * rg + i;
-    if (o >= out_rows) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
-      continue;
-    }
-    if (src.q) {
-      const int8_t* qr = src.q + static_cast<int64_t>(l) * src.w_layer + static_cast<int64_t>(o) * d_in + c;
-      const float sc = src.sc[static_cast<int64_t>(l) * src.sc_layer + o];
-      const int2 raw = *reinterpret_cast<const int2*>(qr);
-      const int8_t* qb = reinterpret_cast<const int8_t*>(&raw);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[i][e] = static_cast<float>(qb[e]) * sc;
-    } else {
-      const uint4 raw = *reinterpret_cast<const uint4*>(src.w + static_cast<int64_t>(l) * src.w_layer +
-                                                        static_cast<int64_t>(o) * d_in + c);
-      const __half2* h = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(h[e]);
-        acc[i][2 * e] = f.x;
-        acc[i][2 * e + 1] = f.y;
-      }
-    }
-  }
-#pragma unroll 4
-  for (int j = 0; j < 16; ++j) {
-    const float4 a0 = *reinterpret_cast<const float4*>(&As[j][8 * cg]);
-    const float4 a1 = *reinterpret_cast<const float4*>(&As[j][8 * cg + 4]);
-    const float4 b0 = *reinterpret_cast<const float4*>(&Bs[j][8 * rg]);
-    const float4 b1 = *reinterpret_cast<const float4*>(&Bs[j][8 * rg + 4]);
-    const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-    const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[i][e] = fmaf(b[i], a[e], acc[i][e]);
-  }
+  if (!col_ok) return;
   __half* out = merged + static_cast<int64_t>(l) * merged_layer;
+  for (int t = 0; t < tiles; ++t) {
+    const int o0 = ob + t * kMrgRows + 8 * rg;
+    float acc[8][8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int o = o0 + 8 * rg + i;
-    if (o >= out_rows) break;
-    uint4 w;
-    w.x = pack_half2(acc[i][0], acc[i][1]);
-    w.y = pack_half2(acc[i][2], acc[i][3]);
-    w.z = pack_half2(acc[i][4], acc[i][5]);
-    w.w = pack_half2(acc[i][6], acc[i][7]);
-    *reinterpret_cast<uint4*>(out + static_cast<int64_t>(o) * ldm + c) = w;
+    for (int i = 0; i < 8; ++i) merge_unpack(raw[i], int8, acc[i]);
+    if (t + 1 < tiles) {  // next tile's rows load during this tile's updates
+#pragma unroll
+      for (int i = 0; i < 8; ++i) raw[i] = merge_load(src, l, o0 + kMrgRows + i, d_in, c);
+    }
+#pragma unroll 4
+    for (int j = 0; j < 16; ++j) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[j][8 * cg]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[j][8 * cg + 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[t][j][8 * rg]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[t][j][8 * rg + 4]);
+      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[i][e] = fmaf(b[i], a[e], acc[i][e]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      uint4 w;
+      w.x = pack_half2(acc[i][0], acc[i][1]);
+      w.y = pack_half2(acc[i][2], acc[i][3]);
+      w.z = pack_half2(acc[i][4], acc[i][5]);
+      w.w = pack_half2(acc[i][6], acc[i][7]);
+      *reinterpret_cast<uint4*>(out + static_cast<int64_t>(o0 + i) * ldm + c) = w;
+    }
   }
 }
 
@@ -303,10 +327,17 @@ cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const
   const int64_t mqkv_layer = merged_qkv_elems(d), mo_layer = merged_o_elems(d);
   MergeSrc sq{base.wqkv, base.q_qkv, base.s_qkv, base.w_layer_qkv, base.s_layer_qkv};
   MergeSrc so{base.wo, base.q_o, base.s_o, base.w_layer_o, base.s_layer_o};
-  dim3 gq((H + kMrgCols - 1) / kMrgCols, QKV / kMrgRows, n_layers);
-  lora_merge_main_kernel<<<gq, 256, 0, st>>>(flat, d, sq, QKV, H, 0, mqkv, mqkv_layer, H + 64);
-  dim3 go((Q + kMrgCols - 1) / kMrgCols, H / kMrgRows, n_layers);
-  lora_merge_main_kernel<<<go, 256, 0, st>>>(flat, d, so, H, Q, 1, mo, mo_layer, Q + 64);
+  // row tiles per block: a divisor of every adapter's row-tile count
+  auto tiles_for = [](int a, int b) {
+    int t = kMrgTiles;
+    while (t > 1 && ((a / kMrgRows) % t || (b / kMrgRows) % t)) t /= 2;
+    return t;
+  };
+  const int tq = tiles_for(Q, KV), to = tiles_for(H, H);
+  dim3 gq((H + kMrgCols - 1) / kMrgCols, QKV / (kMrgRows * tq), n_layers);
+  lora_merge_main_kernel<<<gq, 256, 0, st>>>(flat, d, sq, QKV, H, 0, tq, mqkv, mqkv_layer, H + 64);
+  dim3 go((Q + kMrgCols - 1) / kMrgCols, H / (kMrgRows * to), n_layers);
+  lora_merge_main_kernel<<<go, 256, 0, st>>>(flat, d, so, H, Q, 1, to, mo, mo_layer, Q + 64);
   dim3 gp(128, n_layers);
   lora_merge_pad_kernel<<<gp, 256, 0, st>>>(flat, d, mqkv, mqkv_layer, mo, mo_layer);
   return cudaGetLastError();

@@ -61,10 +61,15 @@ def test_tiny_step_matches_golden(llmcu, cuda_device, batch, seq):
     G.adamw(same, gpu_grads, G.zeros_like_lora(lora), G.zeros_like_lora(lora), **kw)
     for k in same:
         assert np.max(np.abs(got[k] - same[k])) <= 1e-6 * max(1.0, float(np.max(np.abs(same[k])))), k
-    # (3) the update direction: Adam's first step is ~lr*sign(g), so elements
-    # with |g| near 0 may flip; the update still has to point the same way
+    # (3) the update direction: Adam's first step is ~lr*sign(g), which is
+    # ill-conditioned where |g| sits at the fp16 noise floor (the sign there
+    # is noise, and the reduction order of the GPU's dQ is not fixed), so
+    # compare it on the elements whose golden gradient is above 1% of the
+    # tensor's RMS gradient
     for k in upd:
-        d_got, d_ref = got[k] - lora[k], upd[k] - lora[k]
+        g = ref.grads[k]
+        keep = np.abs(g) >= 1e-2 * np.sqrt(np.mean(g.astype(np.float64) ** 2))
+        d_got, d_ref = (got[k] - lora[k])[keep], (upd[k] - lora[k])[keep]
         assert G.cosine(d_got, d_ref) >= 0.99, k
     ctx.close()
 
