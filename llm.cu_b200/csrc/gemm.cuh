@@ -162,27 +162,6 @@ __device__ __forceinline__ bool slab_load(EpiCtx& c, const CUtensorMap* map, int
   c.phase ^= 1u;
   return ok;
 }
-// TMA-load two boxes, (x0, y) into box 0 and (x1, y) into box 1, and wait for both.
-__device__ __forceinline__ bool slab_load2(EpiCtx& c, const CUtensorMap* map, int x0, int x1, int y) {
-  if (c.lane == 0) {
-    mbar_arrive_expect_tx(c.bar, 2 * kSlabBytes);
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4}], [%2];" ::"r"(c.slab),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(c.bar)), "r"(x0), "r"(y)
-        : "memory");
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4}], [%2];" ::"r"(c.slab + kSlabBytes),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(c.bar)), "r"(x1), "r"(y)
-        : "memory");
-  }
-  __syncwarp();
-  const bool ok = mbar_wait(c.bar, c.phase, c.abort_flag, c.err, kErrWaitAccum);
-  c.phase ^= 1u;
-  return ok;
-}
-
 __device__ __forceinline__ uint4 pack8(const float* v) {
   uint4 w;
   w.x = pack_half2(v[0], v[1]);
@@ -201,7 +180,6 @@ __device__ __forceinline__ void unpack8(uint4 w, float* v) {
   }
 }
 
-__device__ __forceinline__ float silu_f(float g) { return g * (1.0f / (1.0f + __expf(-g))); }
 
 // ----------------------------------------------------------------- epilogues
 // Interface: kChunk accumulator columns per call (one 128-byte slab row per
@@ -298,8 +276,10 @@ struct EpiResidF32 {
 // Gate/up GEMM with SwiGLU (src/kernels/activation.cu:5-11).  The fused
 // weight interleaves 128-row blocks of W_gate and W_up, so a 256-wide tile
 // holds gate columns [0,128) and the matching up columns [128,256).  Writes
-// the pre-activations (kept for the backward) and act = silu(g) * u.
-// mapC = gu [M, 2I] (fp16), mapD = act [M, I] (fp16).
+// act = silu(g) * u and, for the backward, the two factors it needs
+// (src/kernels/activation.cu:26-38): at the gate slot  u * silu'(g)  =
+// u * s * (1 + g * (1 - s)), at the up slot  silu(g) = g * s  (s = sigmoid(g)).
+// mapC = stash [M, 2I] (fp16, interleaved like the weight), mapD = act [M, I].
 struct EpiSwiGLU {
   struct Params {};
   struct State {};
@@ -310,22 +290,35 @@ struct EpiSwiGLU {
   __device__ static void begin(State&, const Params&, const EpiCtx&, int) {}
   // g: gate columns [cc, cc+64) of tile tn, u: the matching up columns
   __device__ static bool pair(State&, const Params&, EpiCtx& c, int tile_n, int cc, const float* g, const float* u) {
+    uint32_t dgp[32], sp[32], ap[32];  // u silu'(g), silu(g), act as packed half2
+#pragma unroll
+    for (int t = 0; t < 32; ++t) {
+      float r0[3], r1[3];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float gv = g[2 * t + e], uv = u[2 * t + e];
+        const float sg = 1.0f / (1.0f + __expf(-gv));
+        const float si = gv * sg;
+        float* r = e ? r1 : r0;
+        r[0] = uv * sg * (1.0f + gv * (1.0f - sg));
+        r[1] = si;
+        r[2] = si * uv;
+      }
+      dgp[t] = pack_half2(r0[0], r1[0]);
+      sp[t] = pack_half2(r0[1], r1[1]);
+      ap[t] = pack_half2(r0[2], r1[2]);
+    }
     slab_wait_read(c);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) slab_st(c, j, pack8(g + 8 * j));
+    for (int j = 0; j < 8; ++j) slab_st(c, j, make_uint4(dgp[4 * j], dgp[4 * j + 1], dgp[4 * j + 2], dgp[4 * j + 3]));
     slab_store(c, c.mapC, tile_n * 256 + cc, c.row0);
     slab_wait_read(c);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) slab_st(c, j, pack8(u + 8 * j));
+    for (int j = 0; j < 8; ++j) slab_st(c, j, make_uint4(sp[4 * j], sp[4 * j + 1], sp[4 * j + 2], sp[4 * j + 3]));
     slab_store(c, c.mapC, tile_n * 256 + 128 + cc, c.row0);
     slab_wait_read(c);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float a[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) a[t] = silu_f(g[8 * j + t]) * u[8 * j + t];
-      slab_st(c, j, pack8(a));
-    }
+    for (int j = 0; j < 8; ++j) slab_st(c, j, make_uint4(ap[4 * j], ap[4 * j + 1], ap[4 * j + 2], ap[4 * j + 3]));
     slab_store(c, c.mapD, tile_n * 128 + cc, c.row0);
     return true;
   }
@@ -333,58 +326,85 @@ struct EpiSwiGLU {
 };
 
 // Down-projection dX with the SwiGLU backward fused (src/kernels/activation.cu:26-38):
-// acc = d_act[row, i]; reads g, u from the interleaved stash and writes dg, du
-// into the same interleaved layout of dgu (mapC), the A operand of the
-// gate/up dX GEMM.  g and u arrive by plain 16-byte loads (each thread its
-// row's 128 contiguous bytes of each), so the epilogue needs only the output
-// slab and the mainloop keeps four pipeline stages.
+// acc = d_act[row, i] for the tile's 128-column slice; with the factors the
+// forward stashed, dg = d_act * u silu'(g) and du = d_act * silu(g), written
+// into the interleaved dgu (mapC), the A operand of the gate/up dX GEMM.  The
+// factors arrive by plain 16-byte loads (each thread its row's 64 contiguous
+// bytes per 32 columns), one 32-column step ahead, the first issued before
+// the accumulator is ready; outputs leave through the 4-KB slab.
 struct EpiSwiGLUBwd {
   struct Params {
-    const __half* gu_in;  // [M, 2N] interleaved pre-activations
+    const __half* gu_in;  // [M, 2N] interleaved stash
     int ld;
   };
-  struct State {};
-  static constexpr int kChunk = 64;
+  struct State {
+    uint4 f[2][4];  // factors of the next 32 columns: [0] u silu'(g), [1] silu(g)
+  };
+  static constexpr int kChunk = 128;
   static constexpr int kSlab = kSlabBytes;
   static constexpr bool kPaired = false;
   static constexpr bool kStores = true;
-  __device__ static void begin(State&, const Params&, const EpiCtx&, int) {}
-  __device__ static bool chunk(State&, const Params& p, EpiCtx& c, int col0, const float* v) {
-    if (col0 >= c.N) return true;
-    // col0 is a multiple of 64: the 64 columns share one 128-column block
-    const int gcol = (col0 >> 7) * 256 + (col0 & 127);
-    uint32_t gp[32], up[32];  // g and u as packed half2, later dg and du
-    if (c.row < c.M) {
-      const uint4* gsrc = reinterpret_cast<const uint4*>(p.gu_in + static_cast<size_t>(c.row) * p.ld + gcol);
-      const uint4* usrc = gsrc + 128 / 8;
+  static constexpr bool kTmemDirect = true;
+  // 32-column step q of the slice starting at column col0 (a multiple of 128)
+  __device__ static void fetch(State& st, const Params& p, const EpiCtx& c, int col0, int q) {
+    if (c.row < c.M && col0 < c.N) {
+      const uint4* src =
+          reinterpret_cast<const uint4*>(p.gu_in + static_cast<size_t>(c.row) * p.ld + (col0 >> 7) * 256 + 32 * q);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint4 w = __ldg(gsrc + j);
-        gp[4 * j] = w.x; gp[4 * j + 1] = w.y; gp[4 * j + 2] = w.z; gp[4 * j + 3] = w.w;
-        const uint4 x = __ldg(usrc + j);
-        up[4 * j] = x.x; up[4 * j + 1] = x.y; up[4 * j + 2] = x.z; up[4 * j + 3] = x.w;
+      for (int j = 0; j < 4; ++j) {
+        st.f[0][j] = __ldg(src + j);
+        st.f[1][j] = __ldg(src + 128 / 8 + j);
       }
     } else {
 #pragma unroll
-      for (int t = 0; t < 32; ++t) gp[t] = up[t] = 0u;
+      for (int j = 0; j < 4; ++j) st.f[0][j] = st.f[1][j] = make_uint4(0u, 0u, 0u, 0u);
     }
+  }
+  __device__ static void begin(State& st, const Params& p, const EpiCtx& c, int, int col0) { fetch(st, p, c, col0, 0); }
+  __device__ static bool tile(State& st, const Params& p, EpiCtx& c, int col0, uint32_t taddr, int) {
+    if (col0 >= c.N) return true;
+    const int gcol = (col0 >> 7) * 256;
+    uint32_t du_keep[16];
+#pragma unroll 1
+    for (int q = 0; q < 4; ++q) {
+      uint32_t f0[16], f1[16];
 #pragma unroll
-    for (int t = 0; t < 32; ++t) {
-      const float2 g2 = __half22float2(*reinterpret_cast<const __half2*>(&gp[t]));
-      const float2 u2 = __half22float2(*reinterpret_cast<const __half2*>(&up[t]));
-      const float s0 = 1.0f / (1.0f + __expf(-g2.x)), s1 = 1.0f / (1.0f + __expf(-g2.y));
-      const float d0 = v[2 * t], d1 = v[2 * t + 1];
-      gp[t] = pack_half2(d0 * u2.x * s0 * (1.0f + g2.x * (1.0f - s0)), d1 * u2.y * s1 * (1.0f + g2.y * (1.0f - s1)));
-      up[t] = pack_half2(d0 * g2.x * s0, d1 * g2.y * s1);
+      for (int j = 0; j < 4; ++j) {
+        f0[4 * j] = st.f[0][j].x; f0[4 * j + 1] = st.f[0][j].y; f0[4 * j + 2] = st.f[0][j].z; f0[4 * j + 3] = st.f[0][j].w;
+        f1[4 * j] = st.f[1][j].x; f1[4 * j + 1] = st.f[1][j].y; f1[4 * j + 2] = st.f[1][j].z; f1[4 * j + 3] = st.f[1][j].w;
+      }
+      if (q < 3) fetch(st, p, c, col0, q + 1);
+      float v[32];
+      tmem_ld_32x32b_x32(taddr + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v));
+      tmem_ld_wait();
+      uint32_t dg[16], du[16];
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&f0[t]));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&f1[t]));
+        dg[t] = pack_half2(v[2 * t] * a.x, v[2 * t + 1] * a.y);
+        du[t] = pack_half2(v[2 * t] * b.x, v[2 * t + 1] * b.y);
+      }
+      // slab rows hold 64 columns: steps 0/2 fill chunks 0-3, steps 1/3 chunks 4-7
+      const int h = (q & 1) * 4;
+      if ((q & 1) == 0) slab_wait_read(c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) slab_st(c, h + j, make_uint4(dg[4 * j], dg[4 * j + 1], dg[4 * j + 2], dg[4 * j + 3]));
+      if ((q & 1) == 0) {
+#pragma unroll
+        for (int t = 0; t < 16; ++t) du_keep[t] = du[t];
+        continue;
+      }
+      const int gc = gcol + 32 * (q - 1);  // first column of these 64 gate columns
+      slab_store(c, c.mapC, gc, c.row0);
+      slab_wait_read(c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        slab_st(c, j, make_uint4(du_keep[4 * j], du_keep[4 * j + 1], du_keep[4 * j + 2], du_keep[4 * j + 3]));
+        slab_st(c, 4 + j, make_uint4(du[4 * j], du[4 * j + 1], du[4 * j + 2], du[4 * j + 3]));
+      }
+      slab_store(c, c.mapC, gc + 128, c.row0);
     }
-    slab_wait_read(c);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) slab_st(c, j, make_uint4(gp[4 * j], gp[4 * j + 1], gp[4 * j + 2], gp[4 * j + 3]));
-    slab_store(c, c.mapC, gcol, c.row0);
-    slab_wait_read(c);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) slab_st(c, j, make_uint4(up[4 * j], up[4 * j + 1], up[4 * j + 2], up[4 * j + 3]));
-    slab_store(c, c.mapC, gcol + 128, c.row0);
     return true;
   }
   __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
@@ -464,6 +484,13 @@ struct EpiCEProbs {
   }
   __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
 };
+
+// begin(st, p, c, slot, col0): the epilogue takes its slice's first column
+template <class E, class = void>
+struct epi_begin_col : std::false_type {};
+template <class E>
+struct epi_begin_col<E, std::void_t<decltype(E::begin(std::declval<typename E::State&>(), std::declval<const typename E::Params&>(),
+                                                      std::declval<const EpiCtx&>(), 0, 0))>> : std::true_type {};
 
 template <class E, class = void>
 struct epi_tmem_direct : std::false_type {};
@@ -626,8 +653,6 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     bool ok = true;
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++i) {
       const int acc = i & 1;
-      if (!mbar_wait(&acc_full[acc], (i >> 1) & 1, abort_flag, err, kErrWaitAccum)) break;
-      tc_fence_after();
       const int tile = u % sh.num_tiles;
       const int sp = u / sh.num_tiles;
       const int tm = tile % sh.tiles_m;
@@ -637,7 +662,14 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       const uint32_t tbase = tmem_base + lane_off + acc * BN;
       typename Epi::State st;
       const int slot = tn * kGroups + cgrp;  // per-(tile, column slice) id for row-state epilogues
-      Epi::begin(st, ep, c, slot);
+      // begin() runs before the accumulator is ready: epilogues that read
+      // global inputs start fetching them here
+      if constexpr (epi_begin_col<Epi>::value)
+        Epi::begin(st, ep, c, slot, tn * BN + cgrp * kCols);
+      else
+        Epi::begin(st, ep, c, slot);
+      if (!mbar_wait(&acc_full[acc], (i >> 1) & 1, abort_flag, err, kErrWaitAccum)) break;
+      tc_fence_after();
       if constexpr (epi_tmem_direct<Epi>::value) {
         ok = Epi::tile(st, ep, c, tn * BN + cgrp * kCols, tbase + cgrp * kCols, slot);
       } else if constexpr (!Epi::kPaired) {
