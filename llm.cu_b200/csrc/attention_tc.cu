@@ -1,16 +1,19 @@
 // attention_tc.cu -- causal GQA flash attention on tcgen05 / TMEM (forward and backward).
 //
-// One CTA per (128-row query tile, query head, sequence), 192 threads:
-//   warp 0     TMA producer: Q once, then (K_j, V_j) 128-row tiles in a 2-deep ring
-//   warp 1     MMA issuer:   S_j = Q K_j^T into one of two TMEM buffers, then
-//                            O += P_{j-1} V_{j-1} (O accumulates in TMEM)
-//   warps 2-5  softmax:      thread r owns query row r: reads S_j from TMEM,
-//                            masks, keeps the running max / sum in registers,
-//                            writes P_j (fp16) to shared memory, and rescales
-//                            its O row in TMEM only when the max grew by more
-//                            than 2^8 (P stays < 256, exact in fp16)
-// Shared memory (hd 128): Q 32 KB, K 2x32 KB, V 2x32 KB, P 32 KB.  TMEM:
-// S0 [0,128), S1 [128,256), O [256, 256+hd).  P V uses V as an MN-major
+// Forward: one CTA per (128-row query tile, query head, sequence), 192
+// threads, two CTAs per SM (96 KB of shared memory and 256 TMEM columns
+// each), so one CTA's softmax overlaps the other's MMAs:
+//   warp 0     TMA producer: Q once, then K_j and V_j, each single-buffered
+//              and refilled as soon as the MMA that reads it completes
+//   warp 1     MMA issuer:   S_j = Q K_j^T (SS form), then O += P_j V_j with P
+//                            read from tensor memory (TS form)
+//   warps 2-5  softmax:      thread r owns query row r: one pass over S_j in
+//                            TMEM for the row max, one for exp / sum, writing
+//                            P_j (fp16 pairs) back over the consumed S columns;
+//                            keeps the running max / sum in registers and
+//                            rescales its O row in TMEM only when the max grew
+//                            by more than 2^8 (P stays < 256, exact in fp16)
+// TMEM: S_j / P_j [0,128), O [128, 128+hd).  P V uses V as an MN-major
 // operand (head_dim contiguous), so no transposed copy of V is made.
 // Writes O (fp16) and the per-row log-sum-exp; P never leaves the SM.
 // Replaces naive_attn_kernel (src/kernels/lora_forward.cu:48-135).
@@ -30,13 +33,12 @@ template <int HD>
 struct FwdLayout {
   static constexpr int kQ = kTq * HD * 2;
   static constexpr int kKV = kTk * HD * 2;
-  static constexpr int kP = kTq * kTk * 2;
   static constexpr int kQOff = 0;
-  static constexpr int kKOff = kQOff + kQ;        // 2 stages
-  static constexpr int kVOff = kKOff + 2 * kKV;   // 2 stages
-  static constexpr int kPOff = kVOff + 2 * kKV;
-  static constexpr int kBarOff = kPOff + kP;
-  static constexpr int kBytes = kBarOff + 256 + 1024;
+  static constexpr int kKOff = kQOff + kQ;
+  static constexpr int kVOff = kKOff + kKV;
+  static constexpr int kBarOff = kVOff + kKV;
+  static constexpr int kBytes = kBarOff + 128 + 1024;
+  static constexpr int kTmemCols = 256;  // S / P 128 + O hd
 };
 
 // MN-major (column-contiguous) 128-byte-swizzled operand: 64-element rows of
@@ -44,9 +46,8 @@ struct FwdLayout {
 // next 64 columns one 16 KB box further (leading byte offset).
 __device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t smem_addr) { return sw128_mn_desc(smem_addr, kBox); }
 
-
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, 2)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, __half* __restrict__ o, float* __restrict__ lse,
                        int S, int nh, int nkv, int ldo, float scale_log2, int* err) {
@@ -56,13 +57,14 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_free = bars + 7;    // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* pv_done = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 2;
+  uint64_t* v_full = bars + 3;
+  uint64_t* v_empty = bars + 4;
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* pv_done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -76,26 +78,25 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
-    }
+    mbar_init(k_full, 1);
+    mbar_init(k_empty, 1);
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
+    mbar_init(s_full, 1);
     mbar_init(p_full, 128);
     mbar_init(pv_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, L::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s0 = tmem, t_o = tmem + 256;
+  const uint32_t t_s = tmem, t_o = tmem + 128;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -106,16 +107,17 @@ __global__ void __launch_bounds__(192, 1)
       mbar_arrive_expect_tx(q_full, L::kQ);
       for (int i = 0; i < kDBoxes; ++i)
         tma_load_2d(smem + L::kQOff + i * kBox, &tmQ, q_full, h * HD + 64 * i, row_base + qt * kTq);
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j & 1;
-        if (j >= 2 && !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, abort_flag, err, kErrWaitConsumer)) break;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * L::kKV);
-        for (int i = 0; i < kDBoxes; ++i) {
-          tma_load_2d(smem + L::kKOff + s * L::kKV + i * kBox, &tmK, &kv_full[s], kvh * HD + 64 * i,
-                      row_base + j * kTk);
-          tma_load_2d(smem + L::kVOff + s * L::kKV + i * kBox, &tmV, &kv_full[s], kvh * HD + 64 * i,
-                      row_base + j * kTk);
-        }
+      bool ok = true;
+      for (int j = 0; j < n_kv && ok; ++j) {
+        // K_j once S_{j-1} has read K_{j-1}; V_j once P_{j-1} V_{j-1} has read V_{j-1}
+        if (j >= 1 && !mbar_wait(k_empty, (j - 1) & 1, abort_flag, err, kErrWaitConsumer)) { ok = false; break; }
+        mbar_arrive_expect_tx(k_full, L::kKV);
+        for (int i = 0; i < kDBoxes; ++i)
+          tma_load_2d(smem + L::kKOff + i * kBox, &tmK, k_full, kvh * HD + 64 * i, row_base + j * kTk);
+        if (j >= 1 && !mbar_wait(v_empty, (j - 1) & 1, abort_flag, err, kErrWaitConsumer)) { ok = false; break; }
+        mbar_arrive_expect_tx(v_full, L::kKV);
+        for (int i = 0; i < kDBoxes; ++i)
+          tma_load_2d(smem + L::kVOff + i * kBox, &tmV, v_full, kvh * HD + 64 * i, row_base + j * kTk);
       }
     }
   } else if (warp == 1) {
@@ -124,41 +126,33 @@ __global__ void __launch_bounds__(192, 1)
       constexpr uint32_t idesc_s = idesc_f16_f32(kTq, kTk);
       constexpr uint32_t idesc_pv = idesc_f16_f32(kTq, HD) | (1u << 16);  // B (V) MN-major
       const uint32_t sq = smem_u32(smem + L::kQOff);
-      const uint32_t sp = smem_u32(smem + L::kPOff);
-      auto issue_pv = [&](int j) -> bool {
-        if (!mbar_wait(p_full, j & 1, abort_flag, err, kErrWaitProducer)) return false;
-        tc_fence_after();
-        const uint32_t sv = smem_u32(smem + L::kVOff + (j & 1) * L::kKV);
-#pragma unroll
-        for (int k = 0; k < kTk / 16; ++k) {
-          const uint64_t adesc = sw128_kmajor_desc(sp + (k >> 2) * kBox + (k & 3) * 32);
-          const uint64_t bdesc = sw128_mnmajor_desc(sv + k * 16 * 128);
-          umma_f16(t_o, adesc, bdesc, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
-        }
-        umma_commit(pv_done);
-        umma_commit(&kv_empty[j & 1]);
-        return true;
-      };
+      const uint32_t sk = smem_u32(smem + L::kKOff);
+      const uint32_t sv = smem_u32(smem + L::kVOff);
       bool ok = mbar_wait(q_full, 0, abort_flag, err, kErrWaitProducer);
       for (int j = 0; j < n_kv && ok; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort_flag, err, kErrWaitProducer)) { ok = false; break; }
-        if (j >= 2 && !mbar_wait(&s_free[s], ((j >> 1) - 1) & 1, abort_flag, err, kErrWaitEpilogue)) {
-          ok = false;
-          break;
-        }
+        // S_j overwrites P_{j-1}, which the P V MMA issued before it has read (in order)
+        if (!mbar_wait(k_full, j & 1, abort_flag, err, kErrWaitProducer)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sk = smem_u32(smem + L::kKOff + s * L::kKV);
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
           const uint64_t adesc = sw128_kmajor_desc(sq + (k >> 2) * kBox + (k & 3) * 32);
           const uint64_t bdesc = sw128_kmajor_desc(sk + (k >> 2) * kBox + (k & 3) * 32);
-          umma_f16(t_s0 + s * kTk, adesc, bdesc, idesc_s, k > 0 ? 1u : 0u);
+          umma_f16(t_s, adesc, bdesc, idesc_s, k > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[s]);
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        umma_commit(s_full);
+        umma_commit(k_empty);
+        if (!mbar_wait(p_full, j & 1, abort_flag, err, kErrWaitAccum)) { ok = false; break; }
+        if (!mbar_wait(v_full, j & 1, abort_flag, err, kErrWaitProducer)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kTk / 16; ++k) {
+          // P columns [16k, 16k + 16) are 32-bit TMEM columns [8k, 8k + 8)
+          const uint64_t bdesc = sw128_mnmajor_desc(sv + k * 16 * 128);
+          umma_f16_ts(t_o, t_s + 8 * k, bdesc, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(pv_done);
+        umma_commit(v_empty);
       }
-      if (ok) issue_pv(n_kv - 1);
     }
   } else {
     // ------------------------------------------------------------- softmax
@@ -166,42 +160,48 @@ __global__ void __launch_bounds__(192, 1)
     const int r = qd * 32 + lane;            // query row within the tile
     const int q = qt * kTq + r;              // query position in the sequence
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
-    uint8_t* sP = smem + L::kPOff;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv && ok; ++j) {
-      const int s = j & 1;
-      if (!mbar_wait(&s_full[s], (j >> 1) & 1, abort_flag, err, kErrWaitAccum)) { ok = false; break; }
+      if (!mbar_wait(s_full, j & 1, abort_flag, err, kErrWaitAccum)) { ok = false; break; }
       tc_fence_after();
-      float sv[kTk];
-#pragma unroll
-      for (int c = 0; c < kTk / 32; ++c)
-        tmem_ld_32x32b_x32(t_s0 + s * kTk + lane_off + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(sv + 32 * c));
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&s_free[s]);
+      const int kv0 = j * kTk;
+      // pass 1: row max of the scaled, masked scores
       float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < kTk / 32; ++c) {
+        float sv[32];
+        tmem_ld_32x32b_x32(t_s + lane_off + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(sv));
+        tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < kTk; ++i) {
-        const int kv = j * kTk + i;
-        float x = sv[i] * scale_log2;
-        if (kv > q || kv >= S) x = -INFINITY;
-        sv[i] = x;
-        mx = fmaxf(mx, x);
+        for (int i = 0; i < 32; ++i) {
+          const int kv = kv0 + 32 * c + i;
+          if (kv <= q && kv < S) mx = fmaxf(mx, sv[i] * scale_log2);
+        }
       }
       const float m_new = fmaxf(m_used, mx);
       const bool resc = (j > 0) && (m_new > m_used + 8.0f);
       const float m_next = (j == 0 || resc) ? m_new : m_used;
       const float corr = resc ? fast_exp2(m_used - m_next) : 1.0f;
-      uint32_t pk[kTk / 2];
+      // pass 2: P = exp2(s - m) as fp16 pairs over the S columns already read
+      // (chunk c of 32 scores -> P columns [16c, 16c + 16), below 32c)
       float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kTk / 32; ++c) {
+        float sv[32];
+        tmem_ld_32x32b_x32(t_s + lane_off + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(sv));
+        tmem_ld_wait();
+        uint32_t pk[16];
 #pragma unroll
-      for (int i = 0; i < kTk / 2; ++i) {
-        float p0 = fast_exp2(sv[2 * i] - m_next);
-        float p1 = fast_exp2(sv[2 * i + 1] - m_next);
-        if (m_next == -INFINITY) p0 = p1 = 0.f;
-        rs += p0 + p1;
-        pk[i] = pack_half2(p0, p1);
+        for (int i = 0; i < 16; ++i) {
+          const int kv = kv0 + 32 * c + 2 * i;
+          float p0 = (kv <= q && kv < S) ? fast_exp2(fmaf(sv[2 * i], scale_log2, -m_next)) : 0.f;
+          float p1 = (kv + 1 <= q && kv + 1 < S) ? fast_exp2(fmaf(sv[2 * i + 1], scale_log2, -m_next)) : 0.f;
+          if (m_next == -INFINITY) p0 = p1 = 0.f;
+          rs += p0 + p1;
+          pk[i] = pack_half2(p0, p1);
+        }
+        tmem_st_32x32b_x16(t_s + lane_off + 16 * c, pk);
       }
       l = l * corr + rs;
       m_used = m_next;
@@ -210,7 +210,7 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
       }
       if (__any_sync(0xffffffffu, resc)) {
-#pragma unroll
+#pragma unroll 1
         for (int c = 0; c < HD / 32; ++c) {
           uint32_t ov[32];
           tmem_ld_32x32b_x32(t_o + lane_off + 32 * c, ov);
@@ -219,18 +219,8 @@ __global__ void __launch_bounds__(192, 1)
           for (int t = 0; t < 32; ++t) ov[t] = __float_as_uint(__uint_as_float(ov[t]) * corr);
           tmem_st_32x32b_x32(t_o + lane_off + 32 * c, ov);
         }
-        tmem_st_wait();
       }
-      // P row r: columns [64*bx, 64*bx + 64) in box bx, 16-byte chunk c swizzled by r % 8
-#pragma unroll
-      for (int c = 0; c < kTk / 8; ++c) {
-        const int bx = c >> 3, cc = c & 7;
-        const uint32_t addr = smem_u32(sP + bx * kBox + r * 128 + ((cc ^ (r & 7)) << 4));
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * c]), "r"(pk[4 * c + 1]),
-                     "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
-                     : "memory");
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full);
     }
@@ -238,7 +228,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       __half* orow = o + static_cast<size_t>(row_base + q) * ldo + h * HD;
-#pragma unroll
+#pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t ov[32];
         tmem_ld_32x32b_x32(t_o + lane_off + 32 * c, ov);
@@ -264,7 +254,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, L::kTmemCols);
   }
 }
 
@@ -651,6 +641,9 @@ cudaError_t fwd_tc_launch(const __half* q, const __half* k, const __half* v, __h
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    if (e != cudaSuccess) return e;
+    // two CTAs per SM need the whole shared-memory carveout
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     attr = true;
   }
