@@ -52,6 +52,7 @@ enum class Epi : int {
   kSwiGLU = 3,
   kSwiGLUBwd = 4,
   kCEProbs = 5,  // lm_head forward: slot max / sum-exp partials + slot-relative probabilities
+  kStoreF16Delta = 6,  // fp16 dO + the attention backward's per-(row, head) dO.O sums
 };
 
 struct EpiArgs {
@@ -60,7 +61,12 @@ struct EpiArgs {
   int ld_out = 0;
   int accumulate = 0;
   int ksplit = 1;  // kStoreF32 with accumulate: K slices that reduce-add into the same output
-  // side output (kStoreF16, kResidF32): columns [n_main, N) as fp16 [M, N - n_main]
+  // kStoreF16Delta: O [M, n_main] (row stride ld_o) and the delta output [B, n_heads, seq]
+  const __half* attn_o = nullptr;
+  int ld_o = 0;
+  float* delta = nullptr;
+  int seq = 0, n_heads = 0, head_dim = 0;
+  // side output (kStoreF16, kStoreF16Delta, kResidF32): columns [n_main, N) as fp16 [M, N - n_main]
   int n_main = 0;  // 0: no side output
   __half* side = nullptr;
   int ld_side = 0;

@@ -111,6 +111,13 @@ cudaError_t dispatch(Epi epi, const EpiArgs& ea, const CUtensorMap* maps, const 
       } else {
         return cudaErrorInvalidValue;
       }
+    case Epi::kStoreF16Delta:
+      if constexpr (BN == 256) {
+        EpiStoreF16Delta::Params p{ea.attn_o, ea.ld_o, ea.delta, ea.seq, ea.n_heads, ea.head_dim};
+        return launch<BN, EpiStoreF16Delta, BMN>(maps, sh, p, err, st);
+      } else {
+        return cudaErrorInvalidValue;
+      }
     case Epi::kCEProbs:
       if constexpr (BN == 256 && !BMN) {
         EpiCEProbs::Params p{ea.targets, ea.part_max, ea.part_sum, ea.tgt_logit, sh.tiles_n * (epi_warps<BN>() / 4)};
@@ -142,12 +149,19 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
   if (M <= 0 || N <= 0 || A.k <= 0 || A.k != B.k || A.mn) return cudaErrorInvalidValue;
   int BN = bn_hint;
   if (BN == 0) BN = (epi == Epi::kSwiGLU || epi == Epi::kSwiGLUBwd) ? 256 : (N <= 64 ? 64 : (N <= 128 ? 128 : 256));
+  if (epi == Epi::kStoreF16Delta) {
+    BN = 256;
+    if (!ea.attn_o || !ea.delta || ea.seq <= 0 || (ea.head_dim != 64 && ea.head_dim != 128) || ea.ld_o % 8 ||
+        reinterpret_cast<uintptr_t>(ea.attn_o) % 16)
+      return cudaErrorInvalidValue;
+  }
   if ((epi == Epi::kSwiGLU || epi == Epi::kSwiGLUBwd || epi == Epi::kCEProbs) && BN != 256)
     return cudaErrorInvalidValue;  // paired columns / partial slots assume 256-wide tiles
   if (ea.ksplit > 1 && (epi != Epi::kStoreF32 || !ea.accumulate)) return cudaErrorInvalidValue;
   const int n_main = ea.n_main > 0 ? ea.n_main : N;
   if (n_main < N) {  // side output: only for the plain stores, from a tile boundary
-    if ((epi != Epi::kStoreF16 && epi != Epi::kResidF32) || n_main % BN || (N - n_main) % 8 || !ea.side ||
+    if ((epi != Epi::kStoreF16 && epi != Epi::kStoreF16Delta && epi != Epi::kResidF32) || n_main % BN ||
+        (N - n_main) % 8 || !ea.side ||
         ea.ld_side % 8 || reinterpret_cast<uintptr_t>(ea.side) % 16)
       return cudaErrorInvalidValue;
   }
@@ -156,6 +170,7 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
   bool okc = true;
   switch (epi) {
     case Epi::kStoreF16:
+    case Epi::kStoreF16Delta:
     case Epi::kCEProbs:
       okc = make_io_map(&maps[2], ea.out, M, n_main, ea.ld_out, false);
       maps[3] = maps[2];

@@ -210,6 +210,95 @@ struct EpiStoreF16 {
   __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
 };
 
+// Output-projection dX with the attention backward's row sums fused:
+// C (fp16) = dO = acc for the main columns, and per (row, head) of the slice
+// delta = sum_d dO[row, d] * O[row, d] over the fp16-rounded dO (the value the
+// attention backward reads) -- what FlashAttention's backward calls D
+// (replaces a separate pass over dO and O).  O arrives by plain 16-byte
+// loads one 32-column step ahead; the side columns (dh of the LoRA rows)
+// leave as fp16 like EpiStoreF16's.
+struct EpiStoreF16Delta {
+  struct Params {
+    const __half* o;  // attention output [M, n_main], row stride ldo
+    int ldo;
+    float* delta;     // [B, n_heads, S]
+    int S, n_heads, head_dim;
+  };
+  struct State {
+    uint4 f[4];  // O of the next 32 columns
+  };
+  static constexpr int kChunk = 128;
+  static constexpr int kSlab = kSlabBytes;
+  static constexpr bool kPaired = false;
+  static constexpr bool kStores = true;
+  static constexpr bool kTmemDirect = true;
+  __device__ static void fetch(State& st, const Params& p, const EpiCtx& c, int col0, int q) {
+    if (c.row < c.M && col0 < c.n_main) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.o + static_cast<size_t>(c.row) * p.ldo + col0 + 32 * q);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) st.f[j] = __ldg(src + j);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) st.f[j] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  __device__ static void begin(State& st, const Params& p, const EpiCtx& c, int, int col0) { fetch(st, p, c, col0, 0); }
+  __device__ static bool tile(State& st, const Params& p, EpiCtx& c, int col0, uint32_t taddr, int) {
+    if (col0 >= c.N) return true;
+    if (col0 >= c.n_main) {
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {
+        float v[32];
+        tmem_ld_32x32b_x32(taddr + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v));
+        tmem_ld_wait();
+        side_store(c, col0 + 32 * q, v, 32);
+      }
+      return true;
+    }
+    float dsum[2] = {0.f, 0.f};  // one or two heads per 128-column slice
+#pragma unroll 1
+    for (int q = 0; q < 4; ++q) {
+      uint32_t of[16];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        of[4 * j] = st.f[j].x; of[4 * j + 1] = st.f[j].y; of[4 * j + 2] = st.f[j].z; of[4 * j + 3] = st.f[j].w;
+      }
+      if (q < 3) fetch(st, p, c, col0, q + 1);
+      float v[32];
+      tmem_ld_32x32b_x32(taddr + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v));
+      tmem_ld_wait();
+      uint32_t pk[16];
+      float d = 0.f;
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        pk[t] = pack_half2(v[2 * t], v[2 * t + 1]);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&pk[t]));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&of[t]));
+        d = fmaf(a.x, b.x, fmaf(a.y, b.y, d));
+      }
+      if ((32 * q) / p.head_dim == 0)
+        dsum[0] += d;
+      else
+        dsum[1] += d;
+      const int h = (q & 1) * 4;
+      if ((q & 1) == 0) slab_wait_read(c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) slab_st(c, h + j, make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]));
+      if (q & 1) slab_store(c, c.mapC, col0 + 32 * (q - 1), c.row0);
+    }
+    if (c.row < c.M) {
+      const int b = c.row / p.S, s = c.row % p.S;
+      const int nh_slice = 128 / p.head_dim;
+      for (int k = 0; k < nh_slice; ++k) {
+        const int head = col0 / p.head_dim + k;
+        p.delta[(static_cast<size_t>(b) * p.n_heads + head) * p.S + s] = dsum[k];
+      }
+    }
+    return true;
+  }
+  __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
+};
+
 // C (fp32) = acc, or C += acc (TMA reduce-add) when accumulate != 0.
 struct EpiStoreF32 {
   struct Params { int accumulate; };

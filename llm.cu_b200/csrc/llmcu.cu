@@ -529,15 +529,21 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
                        EpiArgs{ctx->dxn, H}, err, st));
     TIMED(P_NORM, rmsnorm_backward(ctx->dxn, a.resid_mid, w.ffn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
     // O projection
-    {  // [dattn | dh_o] = dres . mo (MN-major): dres W'_o and dres s B_o
+    {  // [dattn | dh_o] = dres . mo (MN-major): dres W'_o and dres s B_o, plus delta = rowsum(dO * O) per head
       EpiArgs ea;
       ea.out = ctx->dattn;
       ea.ld_out = Q;
       ea.n_main = Q;
       ea.side = ctx->dho;
       ea.ld_side = 64;
-      TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op_mn(w.mo, H, Q + 64, Q + 64), M, Q + 64, Epi::kStoreF16, ea, err,
-                         st));
+      ea.attn_o = a.attn;
+      ea.ld_o = Q;
+      ea.delta = ctx->delta;
+      ea.seq = S;
+      ea.n_heads = ctx->nh;
+      ea.head_dim = ctx->hd;
+      TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op_mn(w.mo, H, Q + 64, Q + 64), M, Q + 64, Epi::kStoreF16Delta, ea,
+                         err, st));
     }
     {
       LoraGradBatch gb{};
@@ -550,8 +556,10 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       TIMED(P_LORA_GRAD, lora_grad(gb, M, ctx->lpart, st));
     }
     // attention
-    TIMED(P_ATTN_BWD, attention_backward(a.qrope, a.krope, a.qkv + Q + KV, a.attn, ctx->dattn, a.lse, ctx->delta, ctx->dq, ctx->dk,
-                          ctx->dqkv + Q + KV, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV, QKV, Q, Q, KV, QKV, err, st));
+    // (delta came with the O-projection dX GEMM)
+    TIMED(P_ATTN_BWD, attention_backward_tc(a.qrope, a.krope, a.qkv + Q + KV, ctx->dattn, a.lse, ctx->delta, ctx->dq,
+                                            ctx->dk, ctx->dqkv + Q + KV, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV, QKV, Q,
+                                            Q, KV, QKV, err, st));
     TIMED(P_NORM, qknorm_rope_backward(ctx->dq, ctx->dk, a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, ctx->dqkv,
                             B, S, ctx->nh, ctx->nkv, ctx->hd, eps, st));
     // QKV projection
