@@ -83,6 +83,33 @@ __device__ __forceinline__ float4 ld4(const __half* p) {
   return make_float4(a.x, a.y, b.x, b.y);
 }
 
+// Same with the row in registers (H = 128 * NV): all loads issued up front.
+template <int NV>
+__global__ void __launch_bounds__(128) rmsnorm_fwd_row_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                              __half* __restrict__ out, int M, float eps) {
+  constexpr int H = 128 * NV;
+  const int m = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (m >= M) return;
+  const size_t base = static_cast<size_t>(m) * H + lane * 4;
+  float4 v[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) v[i] = *reinterpret_cast<const float4*>(x + base + 128 * i);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / static_cast<float>(H) + eps);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float4 g = *reinterpret_cast<const float4*>(w + lane * 4 + 128 * i);
+    uint2 u;
+    u.x = pack_half2(v[i].x * r * g.x, v[i].y * r * g.y);
+    u.y = pack_half2(v[i].z * r * g.z, v[i].w * r * g.w);
+    *reinterpret_cast<uint2*>(out + base + 128 * i) = u;
+  }
+}
+
 template <class DY>
 __global__ void rmsnorm_bwd_kernel(const DY* __restrict__ dy, const float* __restrict__ x,
                                    const float* __restrict__ w, float* __restrict__ dres,
@@ -118,6 +145,61 @@ __global__ void rmsnorm_bwd_kernel(const DY* __restrict__ dy, const float* __res
     u.x = pack_half2(o.x, o.y);
     u.y = pack_half2(o.z, o.w);
     *reinterpret_cast<uint2*>(dres16 + base + c) = u;
+  }
+}
+
+// Same computation with the whole row in registers (H = 128 * NV): every
+// load of the row (x, dy, and the running dres) is issued before the first
+// reduction, so a warp keeps ~NV * 40 bytes per lane in flight instead of
+// one loop iteration's worth.
+template <class DY, int NV>
+__global__ void __launch_bounds__(128) rmsnorm_bwd_row_kernel(const DY* __restrict__ dy, const float* __restrict__ x,
+                                                              const float* __restrict__ w, float* __restrict__ dres,
+                                                              __half* __restrict__ dres16, int M, float eps,
+                                                              int accumulate) {
+  constexpr int H = 128 * NV;
+  const int m = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (m >= M) return;
+  const size_t base = static_cast<size_t>(m) * H + lane * 4;
+  float4 xv[NV], dv[NV], pv[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    xv[i] = ld4(x + base + 128 * i);
+    dv[i] = ld4(dy + base + 128 * i);
+  }
+  if (accumulate) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) pv[i] = *reinterpret_cast<const float4*>(dres + base + 128 * i);
+  } else {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) pv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float ss = 0.f, dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float4 g = ld4(w + lane * 4 + 128 * i);
+    ss += xv[i].x * xv[i].x + xv[i].y * xv[i].y + xv[i].z * xv[i].z + xv[i].w * xv[i].w;
+    dot += dv[i].x * g.x * xv[i].x + dv[i].y * g.y * xv[i].y + dv[i].z * g.z * xv[i].z + dv[i].w * g.w * xv[i].w;
+  }
+  ss = warp_sum(ss);
+  dot = warp_sum(dot);
+  const float r = rsqrtf(ss / static_cast<float>(H) + eps);
+  const float cc = r * r / static_cast<float>(H) * dot;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float4 g = ld4(w + lane * 4 + 128 * i);
+    float4 o = make_float4(r * (dv[i].x * g.x - cc * xv[i].x), r * (dv[i].y * g.y - cc * xv[i].y),
+                           r * (dv[i].z * g.z - cc * xv[i].z), r * (dv[i].w * g.w - cc * xv[i].w));
+    o.x += pv[i].x;
+    o.y += pv[i].y;
+    o.z += pv[i].z;
+    o.w += pv[i].w;
+    *reinterpret_cast<float4*>(dres + base + 128 * i) = o;
+    uint2 u;
+    u.x = pack_half2(o.x, o.y);
+    u.y = pack_half2(o.z, o.w);
+    *reinterpret_cast<uint2*>(dres16 + base + 128 * i) = u;
   }
 }
 
@@ -522,6 +604,14 @@ cudaError_t embed_forward(const int* tokens, const __half* E, float* out, int M,
 
 cudaError_t rmsnorm_forward(const float* x, const float* w, __half* out, int M, int H, float eps, cudaStream_t st) {
   if (H % 4) return cudaErrorInvalidValue;
+  if (H == 2048) {
+    rmsnorm_fwd_row_kernel<16><<<(M + 3) / 4, 128, 0, st>>>(x, w, out, M, eps);
+    return cudaGetLastError();
+  }
+  if (H == 256) {
+    rmsnorm_fwd_row_kernel<2><<<(M + 3) / 4, 128, 0, st>>>(x, w, out, M, eps);
+    return cudaGetLastError();
+  }
   rmsnorm_fwd_kernel<<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(x, w, out, M, H, eps);
   return cudaGetLastError();
 }
@@ -529,6 +619,14 @@ cudaError_t rmsnorm_forward(const float* x, const float* w, __half* out, int M, 
 cudaError_t rmsnorm_backward(const float* dy, const float* x, const float* w, float* dres, __half* dres16, int M,
                              int H, float eps, int accumulate, cudaStream_t st) {
   if (H % 4) return cudaErrorInvalidValue;
+  if (H == 2048 || H == 256) {
+    const int grid = (M + 3) / 4;
+    if (H == 2048)
+      rmsnorm_bwd_row_kernel<float, 16><<<grid, 128, 0, st>>>(dy, x, w, dres, dres16, M, eps, accumulate);
+    else
+      rmsnorm_bwd_row_kernel<float, 2><<<grid, 128, 0, st>>>(dy, x, w, dres, dres16, M, eps, accumulate);
+    return cudaGetLastError();
+  }
   rmsnorm_bwd_kernel<float><<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(dy, x, w, dres, dres16, M, H,
                                                                                          eps, accumulate);
   return cudaGetLastError();
@@ -537,6 +635,14 @@ cudaError_t rmsnorm_backward(const float* dy, const float* x, const float* w, fl
 cudaError_t rmsnorm_backward(const __half* dy, const float* x, const float* w, float* dres, __half* dres16, int M,
                              int H, float eps, int accumulate, cudaStream_t st) {
   if (H % 4) return cudaErrorInvalidValue;
+  if (H == 2048 || H == 256) {
+    const int grid = (M + 3) / 4;
+    if (H == 2048)
+      rmsnorm_bwd_row_kernel<__half, 16><<<grid, 128, 0, st>>>(dy, x, w, dres, dres16, M, eps, accumulate);
+    else
+      rmsnorm_bwd_row_kernel<__half, 2><<<grid, 128, 0, st>>>(dy, x, w, dres, dres16, M, eps, accumulate);
+    return cudaGetLastError();
+  }
   rmsnorm_bwd_kernel<__half><<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(dy, x, w, dres, dres16, M,
                                                                                           H, eps, accumulate);
   return cudaGetLastError();

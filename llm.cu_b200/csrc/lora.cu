@@ -30,7 +30,7 @@ namespace llmcu {
 
 namespace {
 
-// Main block of one merged weight: rows [o0, o0 + 32), columns
+// Main block of one merged weight: `tiles` row tiles of 64 rows, columns
 // [c0, c0 + 256) of W + s B A for one adapter (A [r, d_in], B [rows_p, r]).
 // Base W is fp16 (w) or INT8 rows (q) times the per-row scale (sc), as the
 // reference's quantiser lays them out (src/kernels/quantize.cu:8-50).
