@@ -217,141 +217,157 @@ __global__ void rope_table_kernel(float* cos_t, float* sin_t, int S, int hd, flo
   sin_t[i] = sinf(ang);
 }
 
-// One warp per (token, head).  q heads then k heads.  Per-head RMSNorm with
-// the q_norm / k_norm gain, then the half-split rotation of pairs (d, d+hd/2)
-// (src/kernels/lora_forward.cu:233-237, src/kernels/rope.cu:26-35).  Lane l
-// owns the kV consecutive elements d = kV*l .. of each half (kV = hd/64).
+// Qwen3's per-head RMSNorm of q and k with the q_norm / k_norm gain, then the
+// half-split rotation of pairs (d, d + hd/2) (src/kernels/lora_forward.cu:233-237,
+// src/kernels/rope.cu:26-35); the backward applies the inverse rotation
+// (src/kernels/rope.cu:57-83) then the RMSNorm backward at the raw q / k
+// (src/kernels/rmsnorm.cu:53-90).  q heads, then k heads.
+// LPH = hd/16 lanes per (token, head), each lane 8 consecutive elements of
+// each half, so every global access is 16 or 32 bytes and the head
+// reductions are log2(LPH) shuffles; 32/LPH heads per warp.
 template <int HD>
-struct QkVec {
+struct QkLanes {
+  static constexpr int kLph = HD / 16;     // lanes per head
+  static constexpr int kHpw = 32 / kLph;   // heads per warp
   static constexpr int kHalf = HD / 2;
-  static constexpr int kV = HD / 64;  // consecutive elements per lane per half
 };
+__device__ __forceinline__ void ld8h(const __half* p, float (&x)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void ld8f(const float* p, float (&x)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+__device__ __forceinline__ void st8h(__half* p, const float (&x)[8]) {
+  uint4 u;
+  u.x = pack_half2(x[0], x[1]);
+  u.y = pack_half2(x[2], x[3]);
+  u.z = pack_half2(x[4], x[5]);
+  u.w = pack_half2(x[6], x[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+template <int LPH>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = LPH / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
 
 template <int HD>
-__device__ __forceinline__ void ld_h(const __half* p, float (&x)[HD / 64]) {
-  if constexpr (HD / 64 == 2) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(p));
-    x[0] = f.x;
-    x[1] = f.y;
-  } else {
-    x[0] = __half2float(*p);
-  }
-}
-template <int HD>
-__device__ __forceinline__ void st_h(__half* p, const float (&x)[HD / 64]) {
-  if constexpr (HD / 64 == 2) {
-    *reinterpret_cast<__half2*>(p) = __floats2half2_rn(x[0], x[1]);
-  } else {
-    *p = __float2half_rn(x[0]);
-  }
-}
-template <int HD>
-__device__ __forceinline__ void ld_f(const float* p, float (&x)[HD / 64]) {
-  if constexpr (HD / 64 == 2) {
-    const float2 f = *reinterpret_cast<const float2*>(p);
-    x[0] = f.x;
-    x[1] = f.y;
-  } else {
-    x[0] = *p;
-  }
-}
-
-template <int HD>
-__global__ void qknorm_rope_fwd_kernel(const __half* __restrict__ qkv, int ld, const float* __restrict__ qn_w,
-                                       const float* __restrict__ kn_w, const float* __restrict__ cos_t,
-                                       const float* __restrict__ sin_t, __half* __restrict__ q_out,
-                                       __half* __restrict__ k_out, int M, int S, int nh, int nkv, float eps) {
-  constexpr int kHalf = QkVec<HD>::kHalf, kV = QkVec<HD>::kV;
+__global__ void qknorm_rope_fwd_vec_kernel(const __half* __restrict__ qkv, int ld, const float* __restrict__ qn_w,
+                                           const float* __restrict__ kn_w, const float* __restrict__ cos_t,
+                                           const float* __restrict__ sin_t, __half* __restrict__ q_out,
+                                           __half* __restrict__ k_out, int M, int S, int nh, int nkv, float eps) {
+  using C = QkLanes<HD>;
   const int w = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int nhead = nh + nkv;
-  if (w >= M * nhead) return;
-  const int m = w / nhead, hh = w % nhead;
+  const int wpt = (nhead + C::kHpw - 1) / C::kHpw;  // warps per token
+  const int m = w / wpt;
+  const int hh = (w % wpt) * C::kHpw + lane / C::kLph;
+  if (m >= M) return;  // whole warp (m is warp-uniform)
+  const bool live = hh < nhead;
   const bool isq = hh < nh;
-  const __half* src = qkv + static_cast<size_t>(m) * ld + (isq ? hh * HD : nh * HD + (hh - nh) * HD);
-  const float* gw = isq ? qn_w : kn_w;
-  const int d = lane * kV;
-  float x0[kV], x1[kV];
-  ld_h<HD>(src + d, x0);
-  ld_h<HD>(src + d + kHalf, x1);
+  const int d = (lane % C::kLph) * 8;
+  float x0[8] = {}, x1[8] = {};
+  const int col = isq ? hh * HD : nh * HD + (hh - nh) * HD;
+  if (live) {
+    ld8h(qkv + static_cast<size_t>(m) * ld + col + d, x0);
+    ld8h(qkv + static_cast<size_t>(m) * ld + col + d + C::kHalf, x1);
+  }
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < kV; ++i) ss += x0[i] * x0[i] + x1[i] * x1[i];
-  ss = warp_sum(ss);
+  for (int i = 0; i < 8; ++i) ss += x0[i] * x0[i] + x1[i] * x1[i];
+  ss = group_sum<C::kLph>(ss);
+  if (!live) return;
   const float r = rsqrtf(ss / static_cast<float>(HD) + eps);
   const int pos = m % S;
-  float c[kV], s[kV], w0[kV], w1[kV], y0[kV], y1[kV];
-  ld_f<HD>(cos_t + pos * kHalf + d, c);
-  ld_f<HD>(sin_t + pos * kHalf + d, s);
-  ld_f<HD>(gw + d, w0);
-  ld_f<HD>(gw + d + kHalf, w1);
+  const float* gw = isq ? qn_w : kn_w;
+  float c[8], sn[8], w0[8], w1[8], y0[8], y1[8];
+  ld8f(cos_t + pos * C::kHalf + d, c);
+  ld8f(sin_t + pos * C::kHalf + d, sn);
+  ld8f(gw + d, w0);
+  ld8f(gw + d + C::kHalf, w1);
 #pragma unroll
-  for (int i = 0; i < kV; ++i) {
+  for (int i = 0; i < 8; ++i) {
     const float a = x0[i] * r * w0[i];
     const float b = x1[i] * r * w1[i];
-    y0[i] = a * c[i] - b * s[i];
-    y1[i] = b * c[i] + a * s[i];
+    y0[i] = a * c[i] - b * sn[i];
+    y1[i] = b * c[i] + a * sn[i];
   }
   __half* dst = isq ? q_out + static_cast<size_t>(m) * nh * HD + hh * HD
                     : k_out + static_cast<size_t>(m) * nkv * HD + (hh - nh) * HD;
-  st_h<HD>(dst + d, y0);
-  st_h<HD>(dst + d + kHalf, y1);
+  st8h(dst + d, y0);
+  st8h(dst + d + C::kHalf, y1);
 }
 
-// Inverse rotation (src/kernels/rope.cu:57-83) then the per-head RMSNorm
-// backward at the raw q / k (src/kernels/rmsnorm.cu:53-90); writes fp16 into
-// the q / k columns of dqkv.
 template <int HD>
-__global__ void qknorm_rope_bwd_kernel(const float* __restrict__ dq, const float* __restrict__ dk,
-                                       const __half* __restrict__ qkv, int ld, const float* __restrict__ qn_w,
-                                       const float* __restrict__ kn_w, const float* __restrict__ cos_t,
-                                       const float* __restrict__ sin_t, __half* __restrict__ dqkv, int M, int S,
-                                       int nh, int nkv, float eps) {
-  constexpr int kHalf = QkVec<HD>::kHalf, kV = QkVec<HD>::kV;
+__global__ void qknorm_rope_bwd_vec_kernel(const float* __restrict__ dq, const float* __restrict__ dk,
+                                           const __half* __restrict__ qkv, int ld, const float* __restrict__ qn_w,
+                                           const float* __restrict__ kn_w, const float* __restrict__ cos_t,
+                                           const float* __restrict__ sin_t, __half* __restrict__ dqkv, int M, int S,
+                                           int nh, int nkv, float eps) {
+  using C = QkLanes<HD>;
   const int w = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int nhead = nh + nkv;
-  if (w >= M * nhead) return;
-  const int m = w / nhead, hh = w % nhead;
+  const int wpt = (nhead + C::kHpw - 1) / C::kHpw;
+  const int m = w / wpt;
+  const int hh = (w % wpt) * C::kHpw + lane / C::kLph;
+  if (m >= M) return;
+  const bool live = hh < nhead;
   const bool isq = hh < nh;
+  const int d = (lane % C::kLph) * 8;
   const int col = isq ? hh * HD : nh * HD + (hh - nh) * HD;
-  const __half* xs = qkv + static_cast<size_t>(m) * ld + col;
-  const float* g = isq ? dq + static_cast<size_t>(m) * nh * HD + hh * HD
-                       : dk + static_cast<size_t>(m) * nkv * HD + (hh - nh) * HD;
-  const float* gw = isq ? qn_w : kn_w;
   const int pos = m % S;
-  const int d = lane * kV;
-  float x0[kV], x1[kV], g0[kV], g1[kV], c[kV], s[kV], w0[kV], w1[kV], d0[kV], d1[kV];
-  ld_h<HD>(xs + d, x0);
-  ld_h<HD>(xs + d + kHalf, x1);
-  ld_f<HD>(g + d, g0);
-  ld_f<HD>(g + d + kHalf, g1);
-  ld_f<HD>(cos_t + pos * kHalf + d, c);
-  ld_f<HD>(sin_t + pos * kHalf + d, s);
-  ld_f<HD>(gw + d, w0);
-  ld_f<HD>(gw + d + kHalf, w1);
+  float x0[8] = {}, x1[8] = {}, g0[8] = {}, g1[8] = {}, c[8] = {}, sn[8] = {}, w0[8] = {}, w1[8] = {};
+  if (live) {
+    const float* g = isq ? dq + static_cast<size_t>(m) * nh * HD + hh * HD
+                         : dk + static_cast<size_t>(m) * nkv * HD + (hh - nh) * HD;
+    const float* gw = isq ? qn_w : kn_w;
+    ld8h(qkv + static_cast<size_t>(m) * ld + col + d, x0);
+    ld8h(qkv + static_cast<size_t>(m) * ld + col + d + C::kHalf, x1);
+    ld8f(g + d, g0);
+    ld8f(g + d + C::kHalf, g1);
+    ld8f(cos_t + pos * C::kHalf + d, c);
+    ld8f(sin_t + pos * C::kHalf + d, sn);
+    ld8f(gw + d, w0);
+    ld8f(gw + d + C::kHalf, w1);
+  }
+  float d0[8], d1[8];
   float ss = 0.f, dot = 0.f;
 #pragma unroll
-  for (int i = 0; i < kV; ++i) {
-    d0[i] = (g0[i] * c[i] + g1[i] * s[i]) * w0[i];  // d(normed) * w
-    d1[i] = (g1[i] * c[i] - g0[i] * s[i]) * w1[i];
+  for (int i = 0; i < 8; ++i) {
+    d0[i] = (g0[i] * c[i] + g1[i] * sn[i]) * w0[i];  // d(normed) * w
+    d1[i] = (g1[i] * c[i] - g0[i] * sn[i]) * w1[i];
     ss += x0[i] * x0[i] + x1[i] * x1[i];
     dot += d0[i] * x0[i] + d1[i] * x1[i];
   }
-  ss = warp_sum(ss);
-  dot = warp_sum(dot);
+  ss = group_sum<C::kLph>(ss);
+  dot = group_sum<C::kLph>(dot);
+  if (!live) return;
   const float r = rsqrtf(ss / static_cast<float>(HD) + eps);
   const float cc = r * r / static_cast<float>(HD) * dot;
-  float y0[kV], y1[kV];
+  float y0[8], y1[8];
 #pragma unroll
-  for (int i = 0; i < kV; ++i) {
+  for (int i = 0; i < 8; ++i) {
     y0[i] = r * (d0[i] - cc * x0[i]);
     y1[i] = r * (d1[i] - cc * x1[i]);
   }
   __half* dst = dqkv + static_cast<size_t>(m) * ld + col;
-  st_h<HD>(dst + d, y0);
-  st_h<HD>(dst + d + kHalf, y1);
+  st8h(dst + d, y0);
+  st8h(dst + d + C::kHalf, y1);
 }
+
+
 
 // ------------------------------------------------------- cross-entropy
 // valid[m] = 1 if row m contributes to the loss; checks target ids.
@@ -658,16 +674,18 @@ cudaError_t qknorm_rope_forward(const __half* qkv, int ld_qkv, const float* qn_w
                                 const float* cos_t, const float* sin_t, __half* q_out, __half* k_out, int B, int S,
                                 int nh, int nkv, int hd, float eps, cudaStream_t st) {
   const int M = B * S;
-  const int warps = M * (nh + nkv);
-  const int grid = (warps + kRowWarps - 1) / kRowWarps;
-  if (hd == 128)
-    qknorm_rope_fwd_kernel<128><<<grid, kRowWarps * 32, 0, st>>>(qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, q_out, k_out,
-                                                                  M, S, nh, nkv, eps);
-  else if (hd == 64)
-    qknorm_rope_fwd_kernel<64><<<grid, kRowWarps * 32, 0, st>>>(qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, q_out, k_out,
-                                                                 M, S, nh, nkv, eps);
-  else
+  if (ld_qkv % 8) return cudaErrorInvalidValue;
+  if (hd == 128) {
+    const int warps = M * ((nh + nkv + QkLanes<128>::kHpw - 1) / QkLanes<128>::kHpw);
+    qknorm_rope_fwd_vec_kernel<128><<<(warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(
+        qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, q_out, k_out, M, S, nh, nkv, eps);
+  } else if (hd == 64) {
+    const int warps = M * ((nh + nkv + QkLanes<64>::kHpw - 1) / QkLanes<64>::kHpw);
+    qknorm_rope_fwd_vec_kernel<64><<<(warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(
+        qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, q_out, k_out, M, S, nh, nkv, eps);
+  } else {
     return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 
@@ -675,16 +693,18 @@ cudaError_t qknorm_rope_backward(const float* dq, const float* dk, const __half*
                                  const float* kn_w, const float* cos_t, const float* sin_t, __half* dqkv, int B,
                                  int S, int nh, int nkv, int hd, float eps, cudaStream_t st) {
   const int M = B * S;
-  const int warps = M * (nh + nkv);
-  const int grid = (warps + kRowWarps - 1) / kRowWarps;
-  if (hd == 128)
-    qknorm_rope_bwd_kernel<128><<<grid, kRowWarps * 32, 0, st>>>(dq, dk, qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, dqkv,
-                                                                  M, S, nh, nkv, eps);
-  else if (hd == 64)
-    qknorm_rope_bwd_kernel<64><<<grid, kRowWarps * 32, 0, st>>>(dq, dk, qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, dqkv,
-                                                                 M, S, nh, nkv, eps);
-  else
+  if (ld_qkv % 8) return cudaErrorInvalidValue;
+  if (hd == 128) {
+    const int warps = M * ((nh + nkv + QkLanes<128>::kHpw - 1) / QkLanes<128>::kHpw);
+    qknorm_rope_bwd_vec_kernel<128><<<(warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(
+        dq, dk, qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, dqkv, M, S, nh, nkv, eps);
+  } else if (hd == 64) {
+    const int warps = M * ((nh + nkv + QkLanes<64>::kHpw - 1) / QkLanes<64>::kHpw);
+    qknorm_rope_bwd_vec_kernel<64><<<(warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(
+        dq, dk, qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, dqkv, M, S, nh, nkv, eps);
+  } else {
     return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 
