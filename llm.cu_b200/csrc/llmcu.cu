@@ -85,7 +85,6 @@ struct llmcu_ctx {
 
   // lora
   float *lp = nullptr, *lg = nullptr, *lm = nullptr, *lv = nullptr;
-  float* lpart = nullptr;
   int lpart_amax = 0;
 
   // activations
@@ -271,7 +270,7 @@ void carve(llmcu_ctx* c, Carver& cv) {
   c->lm = cv.take<float>(n);
   c->lv = cv.take<float>(n);
   c->lpart_amax = static_cast<int>((std::max({H, Q, KV}) + 63) / 64 * 64);
-  c->lpart = cv.take<float>(static_cast<size_t>(kLoraMaxSplits) * kLoraMaxProbs * c->lpart_amax * 64);
+
   // activations
   for (size_t l = 0; l <= L; ++l) c->resid[l] = cv.take<float>(M * H);
   const size_t lse_n = static_cast<size_t>(c->rc.max_batch) * c->nh * c->rc.max_seq;
@@ -421,6 +420,8 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   const float unscale = static_cast<float>(1.0 / (kGradScale * n_valid_total));
   cudaError_t e = cudaSuccess;
 
+  // gradients accumulate (lora_grad adds each split's share)
+  CK(cudaMemsetAsync(ctx->lg, 0, static_cast<size_t>(ctx->n_lora) * sizeof(float), st));
   // merged q/k/v/o weights of this step's adapters, every layer
   TIMED(P_LORA_PREP, lora_merge(ctx->lp, d, ctx->L, ctx->mw, ctx->lw[0].mqkv, ctx->lw[0].mo, st));
   TIMED(P_CE, ce_valid_rows(ctx->valid, ctx->tgt, B, S, ctx->rc.loss_all_positions, V, err, st));
@@ -545,16 +546,6 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op_mn(w.mo, H, Q + 64, Q + 64), M, Q + 64, Epi::kStoreF16Delta, ea,
                          err, st));
     }
-    {
-      LoraGradBatch gb{};
-      gb.n = 2;
-      gb.a_max = ctx->lpart_amax;
-      // dBo[h, j] = s * sum_m dres[m, h] ho[m, j]
-      gb.p[0] = LoraGradProb{ctx->dres16, H, a.ho, 64, {G + d.oBo}, 1, r, 1, H, r, d.scale * unscale};
-      // dAo[j, q] = sum_m dho[m, j] attn[m, q]
-      gb.p[1] = LoraGradProb{a.attn, Q, ctx->dho, 64, {G + d.oAo}, 1, 1, Q, Q, r, unscale};
-      TIMED(P_LORA_GRAD, lora_grad(gb, M, ctx->lpart, st));
-    }
     // attention
     // (delta came with the O-projection dX GEMM)
     TIMED(P_ATTN_BWD, attention_backward_tc(a.qrope, a.krope, a.qkv + Q + KV, ctx->dattn, a.lse, ctx->delta, ctx->dq,
@@ -574,16 +565,22 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
                          err, st));
     }
     {
+      // all six adapter gradients of the layer in one launch (the O
+      // projection's inputs -- dres16, attn, h_o, dh_o -- are still intact here)
       LoraGradBatch gb{};
-      gb.n = 4;
+      gb.n = 6;
       gb.a_max = ctx->lpart_amax;
       const float sb = d.scale * unscale;
+      // dBo[h, j] = s * sum_m dres[m, h] ho[m, j]
+      gb.p[4] = LoraGradProb{ctx->dres16, H, a.ho, 64, {G + d.oBo}, 1, r, 1, H, r, d.scale * unscale};
+      // dAo[j, q] = sum_m dho[m, j] attn[m, q]
+      gb.p[5] = LoraGradProb{a.attn, Q, ctx->dho, 64, {G + d.oAo}, 1, 1, Q, Q, r, unscale};
       gb.p[0] = LoraGradProb{ctx->dqkv, QKV, a.hq, 64, {G + d.oBq}, 1, r, 1, Q, r, sb};
       gb.p[1] = LoraGradProb{ctx->dqkv + Q, QKV, a.hq + kSegK, 64, {G + d.oBk}, 1, r, 1, KV, r, sb};
       gb.p[2] = LoraGradProb{ctx->dqkv + Q + KV, QKV, a.hq + kSegV, 64, {G + d.oBv}, 1, r, 1, KV, r, sb};
       // dA_q, dA_k, dA_v in one pass over the normed input (column groups 0 / 16 / 32 of dh)
       gb.p[3] = LoraGradProb{a.xn, H, ctx->dhq, 64, {G + d.oAq, G + d.oAk, G + d.oAv}, 3, 1, H, H, r, unscale};
-      TIMED(P_LORA_GRAD, lora_grad(gb, M, ctx->lpart, st));
+      TIMED(P_LORA_GRAD, lora_grad(gb, M, st));
     }
     TIMED(P_NORM, rmsnorm_backward(ctx->dxn, ctx->resid[l], w.attn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
     if (ctx->nccl) {

@@ -22,7 +22,8 @@
 // (src/kernels/lora_backward.cu:50-90, src/kernels/matmul.cu:102-139):
 //   dB = s * dY^T h     (a over d_out, b over r)
 //   dA = dh^T x         (computed as (x^T dh)^T: a over d_in, b over r)
-// split over m, mma.sync m16n8k16, partials reduced in a fixed order.
+// split over m, mma.sync m16n8k16; each split adds its share into the
+// zeroed gradients with fp32 atomics.
 #include "common.cuh"
 #include "lora.cuh"
 
@@ -227,8 +228,7 @@ __device__ __forceinline__ uint32_t uoff(int m, int c) {  // [64 m][64 cols] til
   return static_cast<uint32_t>((m * 8 + (c ^ (m & 7))) * 16);
 }
 
-__global__ void __launch_bounds__(kLgThreads) lora_grad_kernel(const LoraGradBatch batch, int M, int splits,
-                                                              float* __restrict__ part) {
+__global__ void __launch_bounds__(kLgThreads) lora_grad_kernel(const LoraGradBatch batch, int M, int splits) {
   __shared__ __align__(128) uint8_t su[2][kLgM * kLgA * 2];
   __shared__ __align__(128) uint8_t sw[2][kLgM * 64 * 2];
   const LoraGradProb& pb = batch.p[blockIdx.y];
@@ -290,32 +290,25 @@ __global__ void __launch_bounds__(kLgThreads) lora_grad_kernel(const LoraGradBat
   }
   cp_async_wait<0>();
 
-  // partial tile [64 a][64 b] for (split, problem, a-block)
+  // this split's share, scaled, added straight into the gradients (zeroed
+  // before the layer's first split lands; the order of the additions across
+  // splits is not fixed)
   const int gq = lane >> 2, t = lane & 3;
-  float* pp = part + ((static_cast<size_t>(split) * batch.n + blockIdx.y) * batch.a_max + a0) * 64;
 #pragma unroll
   for (int n = 0; n < 8; ++n) {
     if (n < 2 * ng) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int a = warp * 16 + gq + (e >> 1) * 8;
-        const int b = n * 8 + 2 * t + (e & 1);
-        pp[a * 64 + b] = acc[n][e];
+        const int a = a0 + warp * 16 + gq + (e >> 1) * 8;
+        const int gb = n * 8 + 2 * t + (e & 1);
+        const int g = gb >> 4, b = gb & 15;
+        if (a < pb.A && b < pb.Bn)
+          atomicAdd(pb.out[g] + static_cast<size_t>(a) * pb.sa + static_cast<size_t>(b) * pb.sb, acc[n][e] * pb.scale);
       }
     }
   }
 }
 
-__global__ void lora_grad_reduce_kernel(const LoraGradBatch batch, int splits, const float* __restrict__ part) {
-  const LoraGradProb& pb = batch.p[blockIdx.y];
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;  // a * 64 + (16 g + b)
-  const int a = idx >> 6, gb = idx & 63, g = gb >> 4, b = gb & 15;
-  if (a >= pb.A || g >= pb.groups || b >= pb.Bn) return;
-  float s = 0.f;
-  for (int sp = 0; sp < splits; ++sp)
-    s += part[((static_cast<size_t>(sp) * batch.n + blockIdx.y) * batch.a_max + a) * 64 + gb];
-  pb.out[g][static_cast<size_t>(a) * pb.sa + static_cast<size_t>(b) * pb.sb] = s * pb.scale;
-}
 
 }  // namespace
 
@@ -345,7 +338,7 @@ cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const
 
 int lora_grad_splits(int M, int a_max, int n) {
   const int tiles = (a_max + kLgA - 1) / kLgA * n;
-  int s = (2 * gemm_num_sms() + tiles - 1) / tiles;
+  int s = (6 * gemm_num_sms() + tiles - 1) / tiles;  // ~6 CTAs per SM
   const int max_s = (M + 255) / 256;
   if (s > max_s) s = max_s;
   if (s > kLoraMaxSplits) s = kLoraMaxSplits;
@@ -353,13 +346,11 @@ int lora_grad_splits(int M, int a_max, int n) {
   return s;
 }
 
-cudaError_t lora_grad(const LoraGradBatch& batch, int M, float* part, cudaStream_t st) {
+cudaError_t lora_grad(const LoraGradBatch& batch, int M, cudaStream_t st) {
   if (batch.n <= 0 || batch.n > kLoraMaxProbs) return cudaErrorInvalidValue;
   const int splits = lora_grad_splits(M, batch.a_max, batch.n);
   dim3 grid((batch.a_max + kLgA - 1) / kLgA, batch.n, splits);
-  lora_grad_kernel<<<grid, kLgThreads, 0, st>>>(batch, M, splits, part);
-  dim3 g2((batch.a_max * 64 + 255) / 256, batch.n);
-  lora_grad_reduce_kernel<<<g2, 256, 0, st>>>(batch, splits, part);
+  lora_grad_kernel<<<grid, kLgThreads, 0, st>>>(batch, M, splits);
   return cudaGetLastError();
 }
 

@@ -80,7 +80,8 @@ struct LoraGradBatch {
 
 cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const MergeWeights& base, __half* mqkv,
                        __half* mo, cudaStream_t st);
-cudaError_t lora_grad(const LoraGradBatch& batch, int M, float* part, cudaStream_t st);
+// Adds into out[] (which the caller zeroes first).
+cudaError_t lora_grad(const LoraGradBatch& batch, int M, cudaStream_t st);
 int lora_grad_splits(int M, int a_max, int n);
 
 }  // namespace llmcu
