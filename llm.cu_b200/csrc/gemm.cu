@@ -62,9 +62,9 @@ bool make_io_map(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, 
 }
 
 // As many pipeline stages as fit beside the epilogue slabs (at most 8).
-template <int BN, int EW, int SLAB>
+template <int BN, int EW, int SLAB, int CG>
 constexpr int stages_for() {
-  constexpr int stage = kBlockM * kBlockK * 2 + BN * kBlockK * 2;
+  constexpr int stage = kBlockM * kBlockK * 2 + BN / CG * kBlockK * 2;
   constexpr int s = (232448 - 1536 - EW * SLAB) / stage;
   return s > 8 ? 8 : s;
 }
@@ -75,14 +75,14 @@ constexpr int epi_warps() {
   return BN >= 128 ? 4 * kGemmEpiGroups : 4;
 }
 
-template <int BN, class E, bool BMN>
+template <int BN, class E, bool BMN, int CG>
 cudaError_t launch(const CUtensorMap* maps, const GemmShape& sh, const typename E::Params& p, int* err,
                    cudaStream_t st) {
   constexpr int kEpiWarps = epi_warps<BN>();
-  constexpr int S = stages_for<BN, kEpiWarps, E::kSlab>();
-  using L = GemmSmem<BN, S, kEpiWarps, E::kSlab>;
+  constexpr int S = stages_for<BN, kEpiWarps, E::kSlab, CG>();
+  using L = GemmSmem<BN, S, kEpiWarps, E::kSlab, CG>;
   static_assert(L::kBytes <= 232448, "shared memory budget");
-  auto kern = gemm_tc_kernel<BN, S, kEpiWarps, E, BMN>;
+  auto kern = gemm_tc_kernel<BN, S, kEpiWarps, E, BMN, CG>;
   static bool attr_done = false;  // set once per instantiation
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
@@ -90,44 +90,63 @@ cudaError_t launch(const CUtensorMap* maps, const GemmShape& sh, const typename 
     attr_done = true;
   }
   const int units = sh.num_tiles * sh.splits;
-  int grid = units < g_num_sms ? units : g_num_sms;
-  kern<<<grid, 64 + 32 * kEpiWarps, L::kBytes, st>>>(maps[0], maps[1], maps[2], maps[3], sh, p, err);
+  if constexpr (CG == 1) {
+    const int grid = units < g_num_sms ? units : g_num_sms;
+    kern<<<grid, 64 + 32 * kEpiWarps, L::kBytes, st>>>(maps[0], maps[1], maps[2], maps[3], sh, p, err);
+  } else {
+    // one CTA pair per unit, at most one CTA per SM
+    const int pairs = std::min(units, g_num_sms / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(64 + 32 * kEpiWarps);
+    cfg.dynamicSmemBytes = L::kBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], sh, p, err);
+    if (e != cudaSuccess) return e;
+  }
   return cudaGetLastError();
 }
 
-template <int BN, bool BMN>
+template <int BN, bool BMN, int CG>
 cudaError_t dispatch(Epi epi, const EpiArgs& ea, const CUtensorMap* maps, const GemmShape& sh, int* err,
                      cudaStream_t st) {
   switch (epi) {
     case Epi::kStoreF16:
-      return launch<BN, EpiStoreF16, BMN>(maps, sh, EpiStoreF16::Params{}, err, st);
+      return launch<BN, EpiStoreF16, BMN, CG>(maps, sh, EpiStoreF16::Params{}, err, st);
     case Epi::kStoreF32:
-      return launch<BN, EpiStoreF32, BMN>(maps, sh, EpiStoreF32::Params{ea.accumulate}, err, st);
+      return launch<BN, EpiStoreF32, BMN, CG>(maps, sh, EpiStoreF32::Params{ea.accumulate}, err, st);
     case Epi::kResidF32:
-      return launch<BN, EpiResidF32, BMN>(maps, sh, EpiResidF32::Params{}, err, st);
+      return launch<BN, EpiResidF32, BMN, CG>(maps, sh, EpiResidF32::Params{}, err, st);
     case Epi::kSwiGLUBwd:
       if constexpr (BN == 256) {
-        return launch<BN, EpiSwiGLUBwd, BMN>(maps, sh, EpiSwiGLUBwd::Params{ea.gu_in, ea.ld_gu}, err, st);
+        return launch<BN, EpiSwiGLUBwd, BMN, CG>(maps, sh, EpiSwiGLUBwd::Params{ea.gu_in, ea.ld_gu}, err, st);
       } else {
         return cudaErrorInvalidValue;
       }
     case Epi::kStoreF16Delta:
       if constexpr (BN == 256) {
         EpiStoreF16Delta::Params p{ea.attn_o, ea.ld_o, ea.delta, ea.seq, ea.n_heads, ea.head_dim};
-        return launch<BN, EpiStoreF16Delta, BMN>(maps, sh, p, err, st);
+        return launch<BN, EpiStoreF16Delta, BMN, CG>(maps, sh, p, err, st);
       } else {
         return cudaErrorInvalidValue;
       }
     case Epi::kCEProbs:
       if constexpr (BN == 256 && !BMN) {
         EpiCEProbs::Params p{ea.targets, ea.part_max, ea.part_sum, ea.tgt_logit, sh.tiles_n * (epi_warps<BN>() / 4)};
-        return launch<BN, EpiCEProbs, BMN>(maps, sh, p, err, st);
+        return launch<BN, EpiCEProbs, BMN, CG>(maps, sh, p, err, st);
       } else {
         return cudaErrorInvalidValue;
       }
     case Epi::kSwiGLU:
       if constexpr (BN == 256 && !BMN) {
-        return launch<BN, EpiSwiGLU, BMN>(maps, sh, EpiSwiGLU::Params{}, err, st);
+        return launch<BN, EpiSwiGLU, BMN, CG>(maps, sh, EpiSwiGLU::Params{}, err, st);
       } else {
         return cudaErrorInvalidValue;
       }
@@ -165,8 +184,11 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
         ea.ld_side % 8 || reinterpret_cast<uintptr_t>(ea.side) % 16)
       return cudaErrorInvalidValue;
   }
+  // CTA pairs (cta_group::2) for the 256-wide tiles of matrices with more
+  // than one 128-row block: each pair shares a 256 x 256 tile
+  const int CG = (BN == 256 && M > kBlockM) ? 2 : 1;
   CUtensorMap maps[4];  // A, B, C, D
-  if (!make_map(&maps[0], A, kBlockM) || !make_map(&maps[1], B, BN)) return cudaErrorInvalidValue;
+  if (!make_map(&maps[0], A, kBlockM) || !make_map(&maps[1], B, BN / CG)) return cudaErrorInvalidValue;
   bool okc = true;
   switch (epi) {
     case Epi::kStoreF16:
@@ -198,7 +220,7 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
   sh.M = M;
   sh.N = N;
   sh.K = A.k;
-  sh.tiles_m = (M + kBlockM - 1) / kBlockM;
+  sh.tiles_m = (M + kBlockM * CG - 1) / (kBlockM * CG);
   sh.tiles_n = (N + BN - 1) / BN;
   sh.num_tiles = sh.tiles_m * sh.tiles_n;
   sh.splits = 1;
@@ -213,18 +235,22 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
     sh.kb_per_split = kbps;
     sh.splits = (nk + kbps - 1) / kbps;
   }
+  if (CG == 2) {
+    if (B.mn) return dispatch<256, true, 2>(epi, ea, maps, sh, err, st);
+    return dispatch<256, false, 2>(epi, ea, maps, sh, err, st);
+  }
   if (B.mn) {
     switch (BN) {
-      case 64: return dispatch<64, true>(epi, ea, maps, sh, err, st);
-      case 128: return dispatch<128, true>(epi, ea, maps, sh, err, st);
-      case 256: return dispatch<256, true>(epi, ea, maps, sh, err, st);
+      case 64: return dispatch<64, true, 1>(epi, ea, maps, sh, err, st);
+      case 128: return dispatch<128, true, 1>(epi, ea, maps, sh, err, st);
+      case 256: return dispatch<256, true, 1>(epi, ea, maps, sh, err, st);
       default: return cudaErrorInvalidValue;
     }
   }
   switch (BN) {
-    case 64: return dispatch<64, false>(epi, ea, maps, sh, err, st);
-    case 128: return dispatch<128, false>(epi, ea, maps, sh, err, st);
-    case 256: return dispatch<256, false>(epi, ea, maps, sh, err, st);
+    case 64: return dispatch<64, false, 1>(epi, ea, maps, sh, err, st);
+    case 128: return dispatch<128, false, 1>(epi, ea, maps, sh, err, st);
+    case 256: return dispatch<256, false, 1>(epi, ea, maps, sh, err, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -52,10 +52,12 @@ constexpr int kBlockK = 64;
 constexpr int kSlabBytes = 32 * 128;  // one 32-row x 128-byte box
 constexpr int kMnBox = 64 * 128;      // MN-major B box: 64 K rows x 64 columns of fp16
 
-template <int BN, int STAGES, int EW, int SLAB = kSlabBytes>
+// CG = 2: a CTA pair shares each 256 x BN tile; every CTA holds 128 rows
+// of A and BN/2 rows of B per stage.
+template <int BN, int STAGES, int EW, int SLAB = kSlabBytes, int CG = 1>
 struct GemmSmem {
   static constexpr int kABytes = kBlockM * kBlockK * 2;       // 16 KB
-  static constexpr int kBBytes = BN * kBlockK * 2;            // 8/16/32 KB
+  static constexpr int kBBytes = BN / CG * kBlockK * 2;       // 8/16/32 KB
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;  // two accumulators
   static constexpr int kSlabOffset = STAGES * kStageBytes;
@@ -588,12 +590,20 @@ struct epi_tmem_direct<E, std::void_t<decltype(E::kTmemDirect)>> : std::bool_con
 
 // ---------------------------------------------------------------- the kernel
 
-template <int BN, int STAGES, int EW, class Epi, bool BMN>
+// CG = 2: launched as clusters of two CTAs.  The even CTA's MMA warp issues
+// tcgen05.mma.cta_group::2 (M = 256) for both; both CTAs' TMA loads count
+// on the even CTA's `full` barriers, its commits arrive on both CTAs'
+// `empty` / `acc_full` barriers, and both CTAs' epilogues drain their own
+// TMEM rows and arrive on the even CTA's `acc_empty`.
+template <int BN, int STAGES, int EW, class Epi, bool BMN, int CG>
 __global__ void __launch_bounds__(64 + 32 * EW, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
                    const GemmShape sh, const typename Epi::Params ep, int* err) {
-  using L = GemmSmem<BN, STAGES, EW, Epi::kSlab>;
+  static_assert(CG == 1 || (CG == 2 && BN == 256), "CTA pairs use 256-wide tiles");
+  using L = GemmSmem<BN, STAGES, EW, Epi::kSlab, CG>;
+  constexpr int kRowsPerTile = kBlockM * CG;  // tile rows (both CTAs of a pair)
+  constexpr int kBRows = BN / CG;             // B rows (N) this CTA loads
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
@@ -607,6 +617,9 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+  const int unit0 = CG == 2 ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
+  const int ustep = CG == 2 ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -615,7 +628,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 32 * EW);
+      mbar_init(&acc_empty[a], 32 * EW * CG);
     }
     for (int w = 0; w < EW; ++w) mbar_init(&slab_bar[w], 1);
     *abort_flag = 0;
@@ -626,11 +639,19 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, L::kTmemCols);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(tmem_slot, L::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, L::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2)
+    cluster_sync_all();  // barriers initialised in both CTAs before any remote arrive
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -642,32 +663,48 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       // ------------------------------------------------------------ producer
       int it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      for (int u = unit0; u < num_units && ok; u += ustep) {
         const int tile = u % sh.num_tiles;
         const int sp = u / sh.num_tiles;
         const int tm = tile % sh.tiles_m;
         const int tn = tile / sh.tiles_m;
         const int kb_end = min(nk, (sp + 1) * sh.kb_per_split);
+        const int arow = tm * kRowsPerTile + static_cast<int>(rank) * kBlockM;
+        const int brow = tn * BN + static_cast<int>(rank) * kBRows;
         for (int kb = sp * sh.kb_per_split; kb < kb_end; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t par = ((it / STAGES) & 1) ^ 1;
           if (!mbar_wait(&empty[s], par, abort_flag, err, kErrWaitConsumer)) { ok = false; break; }
           uint8_t* sa = smem + s * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes;
-          mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-          tma_load_2d(sa, &tmA, &full[s], kb * kBlockK, tm * kBlockM);
-          if constexpr (!BMN) {
-            tma_load_2d(sb, &tmB, &full[s], kb * kBlockK, tn * BN);
-          } else {
-            // [64 K rows x 64 N columns] boxes side by side along N
+          if constexpr (CG == 2) {
+            // both CTAs' bytes count on the even CTA's barrier
+            const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
+            tma_load_2d_pair(sa, &tmA, fb, kb * kBlockK, arow);
+            if constexpr (!BMN) {
+              tma_load_2d_pair(sb, &tmB, fb, kb * kBlockK, brow);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(sb + j * kMnBox, &tmB, &full[s], tn * BN + 64 * j, kb * kBlockK);
+              for (int j = 0; j < kBRows / 64; ++j) tma_load_2d_pair(sb + j * kMnBox, &tmB, fb, brow + 64 * j, kb * kBlockK);
+            }
+          } else {
+            mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+            tma_load_2d(sa, &tmA, &full[s], kb * kBlockK, arow);
+            if constexpr (!BMN) {
+              tma_load_2d(sb, &tmB, &full[s], kb * kBlockK, brow);
+            } else {
+              // [64 K rows x 64 N columns] boxes side by side along N
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_2d(sb + j * kMnBox, &tmB, &full[s], brow + 64 * j, kb * kBlockK);
+            }
           }
         }
       }
-      if (!ok) {
-        // Let the copies already issued land before the CTA can exit.
+      if (!ok && CG == 1) {
+        // Let the copies already issued land before the CTA can exit (a CTA
+        // pair waits for the peer at the final cluster barrier instead).
         for (int j = 0; j < STAGES; ++j) {
           const int i2 = it - 1 - j;
           if (i2 < 0) break;
@@ -679,13 +716,13 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       // ---------------------------------------------------------- MMA issuer
-      constexpr uint32_t idesc = idesc_f16_f32(kBlockM, BN) | (BMN ? (1u << 16) : 0u);
+      constexpr uint32_t idesc = idesc_f16_f32(kRowsPerTile, BN) | (BMN ? (1u << 16) : 0u);
       int it = 0;
       int i = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++i) {
+      for (int u = unit0; u < num_units && ok; u += ustep, ++i) {
         const int acc = i & 1;
         if (!mbar_wait(&acc_empty[acc], ((i >> 1) & 1) ^ 1, abort_flag, err, kErrWaitEpilogue)) break;
         tc_fence_after();
@@ -706,11 +743,26 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
             // K-major: +32 bytes per 16-element K step inside the 128-byte
             // swizzle row; MN-major: +16 rows of 128 bytes
             const uint64_t bk = BMN ? bdesc + (16 * 128 >> 4) * k : bdesc + 2 * k;
-            umma_f16(d_tmem, adesc + 2 * k, bk, idesc, (kb != kb_begin || k != 0) ? 1u : 0u);
+            if constexpr (CG == 2)
+              umma_f16_pair(d_tmem, adesc + 2 * k, bk, idesc, (kb != kb_begin || k != 0) ? 1u : 0u);
+            else
+              umma_f16(d_tmem, adesc + 2 * k, bk, idesc, (kb != kb_begin || k != 0) ? 1u : 0u);
           }
-          umma_commit(&empty[s]);
+          if constexpr (CG == 2) {
+            umma_commit_pair(smem_u32(&empty[s]));
+            umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1));
+          } else {
+            umma_commit(&empty[s]);
+          }
         }
-        if (ok) umma_commit(&acc_full[acc]);
+        if (ok) {
+          if constexpr (CG == 2) {
+            umma_commit_pair(smem_u32(&acc_full[acc]));
+            umma_commit_pair(mapa_shared(smem_u32(&acc_full[acc]), 1));
+          } else {
+            umma_commit(&acc_full[acc]);
+          }
+        }
       }
     }
   } else {
@@ -740,13 +792,14 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     c.ld_side = sh.ld_side;
     int i = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++i) {
+    for (int u = unit0; u < num_units && ok; u += ustep, ++i) {
       const int acc = i & 1;
       const int tile = u % sh.num_tiles;
       const int sp = u / sh.num_tiles;
       const int tm = tile % sh.tiles_m;
       const int tn = tile / sh.tiles_m;
-      c.row0 = (sp * sh.split_row_tiles + tm) * kBlockM + ew * 32;  // split s -> its row block of partials
+      // split s -> its row block of partials; the odd CTA of a pair owns rows 128..255
+      c.row0 = (sp * sh.split_row_tiles + tm) * kRowsPerTile + static_cast<int>(rank) * kBlockM + ew * 32;
       c.row = c.row0 + lane;
       const uint32_t tbase = tmem_base + lane_off + acc * BN;
       typename Epi::State st;
@@ -788,18 +841,27 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       }
       Epi::end(st, ep, c, slot);
       tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
+      if constexpr (CG == 2)
+        mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
+      else
+        mbar_arrive(&acc_empty[acc]);
     }
     if (Epi::kStores && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     __syncwarp();
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2)
+    cluster_sync_all();  // the peer's MMAs, barriers and TMEM stay live until both CTAs are done
+  else
+    __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, L::kTmemCols);
+    if constexpr (CG == 2)
+      tmem_dealloc_pair(tmem_base, L::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, L::kTmemCols);
   }
 }
 
