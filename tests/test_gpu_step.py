@@ -103,3 +103,53 @@ def test_qwen3_shape_slice_matches_golden(llmcu, cuda_device):
     assert abs(loss - ref.loss) <= LOSS_RTOL * abs(ref.loss), (loss, ref.loss)
     _check_dicts(G, ctx.grads_dict(), ref.grads, "grad")
     ctx.close()
+
+
+def _int8_view(base):
+    """The base weights the INT8 path computes with: every linear weight (and
+    the tied embedding) quantised per output row (src/kernels/quantize.cu:8-50)
+    and dequantised in fp32; norm gains unchanged."""
+    from oracle import quant
+    out = {}
+    for k, w in base.items():
+        if w.ndim == 2:
+            q, s = quant.quantize_rows(w)
+            out[k] = (q.astype(np.float32) * s[:, None]).astype(np.float32)
+        else:
+            out[k] = w
+    return out
+
+
+@pytest.mark.parametrize("batch,seq", [(2, 64)])
+def test_int8_base_step_matches_golden(llmcu, cuda_device, batch, seq):
+    """INT8 base: the library quantises the uploaded fp32 weights
+    itself; the golden runs on the same quantise-dequantise weights."""
+    from oracle import golden as G
+    cfg = G.CFG_TINY
+    base = G.make_base_weights(cfg, 41, round_fp16=True)
+    lora = G.make_lora(cfg, 42)
+    tok, tgt = G.make_tokens(cfg, batch, seq, 43, dist="zipf")
+    model = llmcu.Model(cfg.hidden, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab,
+                        cfg.rope_theta, cfg.rms_eps)
+    ctx = llmcu.Context(model, llmcu.Lora(cfg.lora_rank, cfg.lora_alpha),
+                        llmcu.Run(batch, seq, base_dtype=llmcu.BASE_INT8))
+    ctx.set_base(base)
+    ctx.set_lora_dict(lora)
+    ref = G.forward_backward(cfg, _int8_view(base), lora, tok, tgt)
+    loss = ctx.forward_backward(tok, tgt)
+    assert abs(loss - ref.loss) <= LOSS_RTOL * abs(ref.loss), (loss, ref.loss)
+    _check_dicts(G, ctx.grads_dict(), ref.grads, "int8 grad")
+    ctx.close()
+
+
+def test_long_sequence_step_matches_golden(llmcu, cuda_device):
+    """configs[3]'s long sequence at the tiny dims: batch 1 x seq 2048, uniform
+    tokens (16 query tiles per head in the causal attention)."""
+    from oracle import golden as G
+    cfg = G.CFG_TINY
+    G, base, lora, tok, tgt, ctx = _setup(llmcu, cfg, 1, 2048, seed=51, dist="uniform")
+    ref = G.forward_backward(cfg, base, lora, tok, tgt, threads=8)
+    loss = ctx.forward_backward(tok, tgt)
+    assert abs(loss - ref.loss) <= LOSS_RTOL * abs(ref.loss), (loss, ref.loss)
+    _check_dicts(G, ctx.grads_dict(), ref.grads, "grad")
+    ctx.close()
