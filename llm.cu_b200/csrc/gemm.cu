@@ -226,6 +226,8 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
   sh.splits = 1;
   sh.kb_per_split = (A.k + kBlockK - 1) / kBlockK;
   sh.split_row_tiles = 0;
+  // walk N first when A outweighs B, so the CTAs that run together share A's rows
+  sh.n_fastest = static_cast<int64_t>(M) * A.k > static_cast<int64_t>(N) * B.k ? 1 : 0;
   sh.n_main = n_main;
   sh.side = ea.side;
   sh.ld_side = ea.ld_side;

@@ -26,7 +26,9 @@
 // pre-activations) arrive the same way through TMA loads.
 // Tiles: BLOCK_M = 128 rows, BLOCK_N = BN (64/128/256), BLOCK_K = 64 (one
 // 128-byte swizzle row of fp16).  Tile t -> (t % tiles_m, t / tiles_m), so
-// CTAs that run together share the weight (B) tile and stream it once.
+// CTAs that run together share the weight (B) tile and stream it once -- or,
+// when A is the larger operand (the lm_head dX reads [M, V] dlogits), the
+// transposed order, so concurrent CTAs share A's rows instead.
 #pragma once
 
 #include <type_traits>
@@ -42,6 +44,7 @@ struct GemmShape {
   int splits;      // K splits (1 = none); split s writes rows [s * split_row_tiles * 128, ...)
   int kb_per_split;
   int split_row_tiles;  // tiles_m: one row block of partials per split; 0: splits reduce-add into the same rows
+  int n_fastest;        // tile order: 1 = consecutive units walk N (share A rows), 0 = walk M (share B)
   int n_main;           // columns [n_main, N) go to the side output
   __half* side;         // [M, N - n_main] fp16, row stride ld_side
   int ld_side;
@@ -666,8 +669,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       for (int u = unit0; u < num_units && ok; u += ustep) {
         const int tile = u % sh.num_tiles;
         const int sp = u / sh.num_tiles;
-        const int tm = tile % sh.tiles_m;
-        const int tn = tile / sh.tiles_m;
+        const int tm = sh.n_fastest ? tile / sh.tiles_n : tile % sh.tiles_m;
+        const int tn = sh.n_fastest ? tile % sh.tiles_n : tile / sh.tiles_m;
         const int kb_end = min(nk, (sp + 1) * sh.kb_per_split);
         const int arow = tm * kRowsPerTile + static_cast<int>(rank) * kBlockM;
         const int brow = tn * BN + static_cast<int>(rank) * kBRows;
@@ -796,8 +799,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       const int acc = i & 1;
       const int tile = u % sh.num_tiles;
       const int sp = u / sh.num_tiles;
-      const int tm = tile % sh.tiles_m;
-      const int tn = tile / sh.tiles_m;
+      const int tm = sh.n_fastest ? tile / sh.tiles_n : tile % sh.tiles_m;
+      const int tn = sh.n_fastest ? tile % sh.tiles_n : tile / sh.tiles_m;
       // split s -> its row block of partials; the odd CTA of a pair owns rows 128..255
       c.row0 = (sp * sh.split_row_tiles + tm) * kRowsPerTile + static_cast<int>(rank) * kBlockM + ew * 32;
       c.row = c.row0 + lane;
