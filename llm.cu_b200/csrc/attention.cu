@@ -19,6 +19,8 @@ namespace {
 template <int HD>
 __global__ void attn_delta_kernel(const __half* __restrict__ o, const __half* __restrict__ dout,
                                   float* __restrict__ delta, int B, int S, int nh, int ld) {
+  pdl_trigger();
+  pdl_wait();
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= B * S * nh) return;
@@ -43,7 +45,7 @@ template <int HD>
 void attn_delta_launch(const __half* o, const __half* dout, float* delta, int B, int S, int nh, int ldo,
                        cudaStream_t st) {
   const int warps = B * S * nh;
-  attn_delta_kernel<HD><<<(warps + 7) / 8, 256, 0, st>>>(o, dout, delta, B, S, nh, ldo);
+  launch_pdl(attn_delta_kernel<HD>, (warps + 7) / 8, 256, 0, st, o, dout, delta, B, S, nh, ldo);
 }
 
 }  // namespace

@@ -53,6 +53,7 @@ __global__ void __launch_bounds__(192, 2)
                        int S, int nh, int nkv, int ldo, float scale_log2, int* err) {
   using L = FwdLayout<HD>;
   constexpr int kDBoxes = HD / 64;  // 64-wide boxes along head_dim
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
@@ -96,6 +97,7 @@ __global__ void __launch_bounds__(192, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // the prologue above overlapped the previous kernel's tail
   const uint32_t t_s = tmem, t_o = tmem + 128;
 
   if (warp == 0) {
@@ -297,6 +299,7 @@ __global__ void __launch_bounds__(192, 1)
                        int nh, int nkv, int lddk, int lddv, float scale, float scale_log2, int* err) {
   using L = BwdLayout<HD>;
   constexpr int kDBoxes = HD / 64;
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
@@ -343,6 +346,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // the prologue above overlapped the previous kernel's tail
   const uint32_t t_s = tmem, t_dp = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 256 + HD;
 
   if (warp == 0) {
@@ -619,13 +623,12 @@ cudaError_t bwd_tc_launch(const __half* q, const __half* k, const __half* v, con
     attr = true;
   }
   // dQ accumulates partial products of every key tile
-  cudaError_t e = cudaMemset2DAsync(dq, static_cast<size_t>(lddq) * 4, 0, static_cast<size_t>(nh) * HD * 4,
-                                    static_cast<size_t>(B) * S, st);
+  cudaError_t e = fill_f32_2d(dq, lddq, B * S, nh * HD, 0.f, st);
   if (e != cudaSuccess) return e;
   dim3 grid(nkv, B, (S + 127) / 128);
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));
-  kern<<<grid, 192, L::kBytes, st>>>(mq, mk, mv, mo, mdq, lse, delta, dk, dv, S, nh, nkv, lddk, lddv, scale,
-                                     scale * kLog2e, err);
+  launch_pdl(kern, grid, 192, L::kBytes, st, mq, mk, mv, mo, mdq, lse, delta, dk, dv, S, nh, nkv, lddk, lddv, scale,
+             scale * kLog2e, err);
   return cudaGetLastError();
 }
 
@@ -649,7 +652,7 @@ cudaError_t fwd_tc_launch(const __half* q, const __half* k, const __half* v, __h
   }
   dim3 grid(nh, B, (S + kTq - 1) / kTq);
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));
-  kern<<<grid, 192, L::kBytes, st>>>(mq, mk, mv, o, lse, S, nh, nkv, ldo, scale * kLog2e, err);
+  launch_pdl(kern, grid, 192, L::kBytes, st, mq, mk, mv, o, lse, S, nh, nkv, ldo, scale * kLog2e, err);
   return cudaGetLastError();
 }
 

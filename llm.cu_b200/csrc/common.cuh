@@ -10,6 +10,31 @@
 
 namespace llmcu {
 
+// Programmatic dependent launch for the calling host thread: on while a
+// training step issues its chain of kernels (each awaits its predecessor in
+// pdl_wait), off otherwise, so a kernel that follows a copy, a memset, an
+// event wait or another library's work is launched normally.
+bool pdl_enabled();
+void set_pdl(bool on);
+
+// Launch `kern`, with programmatic stream serialization when pdl_enabled().
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+
 // ---- attention.cu
 cudaError_t attention_forward(const __half* q, const __half* k, const __half* v, __half* o, float* lse, int B, int S,
                               int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int* err, cudaStream_t st);
@@ -118,6 +143,7 @@ cudaError_t ce_valid_rows(uint8_t* valid, const int* targets, int B, int S, int 
                           cudaStream_t st);
 cudaError_t adamw_flat(float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1, float b2,
                        float eps, float wd, float bc1, float bc2, float gscale, cudaStream_t st);
+cudaError_t fill_f32_2d(float* p, int ld, int rows, int cols, float v, cudaStream_t st);
 cudaError_t fill_f32(float* p, int64_t n, float v, cudaStream_t st);
 cudaError_t fill_normal_f16(__half* p, int64_t n, uint64_t seed, float stddev, cudaStream_t st);
 cudaError_t fill_normal_f32(float* p, int64_t n, uint64_t seed, float stddev, cudaStream_t st);

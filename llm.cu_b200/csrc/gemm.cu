@@ -92,7 +92,9 @@ cudaError_t launch(const CUtensorMap* maps, const GemmShape& sh, const typename 
   const int units = sh.num_tiles * sh.splits;
   if constexpr (CG == 1) {
     const int grid = units < g_num_sms ? units : g_num_sms;
-    kern<<<grid, 64 + 32 * kEpiWarps, L::kBytes, st>>>(maps[0], maps[1], maps[2], maps[3], sh, p, err);
+    cudaError_t e = launch_pdl(kern, grid, 64 + 32 * kEpiWarps, L::kBytes, st, maps[0], maps[1], maps[2], maps[3], sh,
+                               p, err);
+    if (e != cudaSuccess) return e;
   } else {
     // one CTA pair per unit, at most one CTA per SM
     const int pairs = std::min(units, g_num_sms / 2);
@@ -101,13 +103,15 @@ cudaError_t launch(const CUtensorMap* maps, const GemmShape& sh, const typename 
     cfg.blockDim = dim3(64 + 32 * kEpiWarps);
     cfg.dynamicSmemBytes = L::kBytes;
     cfg.stream = st;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = 2;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], sh, p, err);
     if (e != cudaSuccess) return e;
   }

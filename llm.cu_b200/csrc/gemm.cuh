@@ -618,6 +618,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(slab_bar + EW);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+  pdl_trigger();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
@@ -657,6 +658,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the prologue above overlapped the previous kernel's tail
 
   const int nk = (sh.K + kBlockK - 1) / kBlockK;
   const int num_units = sh.num_tiles * sh.splits;  // (tile, K split) work units

@@ -11,6 +11,13 @@
 namespace llmcu {
 
 namespace {
+thread_local bool t_pdl = false;
+}
+bool pdl_enabled() { return t_pdl; }
+void set_pdl(bool on) { t_pdl = on; }
+
+
+namespace {
 
 constexpr int kRowWarps = 8;  // warps per CTA for row kernels
 
@@ -29,6 +36,8 @@ __device__ __forceinline__ void load8h(const __half* p, float (&f)[8]) {
 // out[m, :] = E[tok[m], :]   (src/kernels/embed.cu:6-14), fp16 table -> fp32
 __global__ void embed_kernel(const int* __restrict__ tok, const __half* __restrict__ E, float* __restrict__ out,
                              int M, int H, int V, int* err) {
+  pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
@@ -51,6 +60,8 @@ __global__ void embed_kernel(const int* __restrict__ tok, const __half* __restri
 // y = x * rsqrt(mean(x^2) + eps) * w   (src/kernels/rmsnorm.cu:6-34)
 __global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                    __half* __restrict__ out, int M, int H, float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
@@ -87,6 +98,8 @@ __device__ __forceinline__ float4 ld4(const __half* p) {
 template <int NV>
 __global__ void __launch_bounds__(128) rmsnorm_fwd_row_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                               __half* __restrict__ out, int M, float eps) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int H = 128 * NV;
   const int m = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -114,6 +127,8 @@ template <class DY>
 __global__ void rmsnorm_bwd_kernel(const DY* __restrict__ dy, const float* __restrict__ x,
                                    const float* __restrict__ w, float* __restrict__ dres,
                                    __half* __restrict__ dres16, int M, int H, float eps, int accumulate) {
+  pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
@@ -157,6 +172,8 @@ __global__ void __launch_bounds__(128) rmsnorm_bwd_row_kernel(const DY* __restri
                                                               const float* __restrict__ w, float* __restrict__ dres,
                                                               __half* __restrict__ dres16, int M, float eps,
                                                               int accumulate) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int H = 128 * NV;
   const int m = blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -266,6 +283,8 @@ __global__ void qknorm_rope_fwd_vec_kernel(const __half* __restrict__ qkv, int l
                                            const float* __restrict__ kn_w, const float* __restrict__ cos_t,
                                            const float* __restrict__ sin_t, __half* __restrict__ q_out,
                                            __half* __restrict__ k_out, int M, int S, int nh, int nkv, float eps) {
+  pdl_trigger();
+  pdl_wait();
   using C = QkLanes<HD>;
   const int w = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -315,6 +334,8 @@ __global__ void qknorm_rope_bwd_vec_kernel(const float* __restrict__ dq, const f
                                            const float* __restrict__ kn_w, const float* __restrict__ cos_t,
                                            const float* __restrict__ sin_t, __half* __restrict__ dqkv, int M, int S,
                                            int nh, int nkv, float eps) {
+  pdl_trigger();
+  pdl_wait();
   using C = QkLanes<HD>;
   const int w = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -373,6 +394,8 @@ __global__ void qknorm_rope_bwd_vec_kernel(const float* __restrict__ dq, const f
 // valid[m] = 1 if row m contributes to the loss; checks target ids.
 __global__ void ce_valid_kernel(uint8_t* valid, const int* targets, int B, int S, int all_positions, int V,
                                 int* err) {
+  pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   if (m >= B * S) return;
   const int s = m % S;
@@ -387,6 +410,8 @@ __global__ void ce_valid_kernel(uint8_t* valid, const int* targets, int B, int S
 __global__ void ce_lse_kernel(const float* __restrict__ pmax, const float* __restrict__ psum,
                               const float* __restrict__ tgt, const uint8_t* __restrict__ valid,
                               float* __restrict__ lse, float* __restrict__ row_loss, int M, int T) {
+  pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
@@ -410,6 +435,8 @@ __global__ void ce_lse_kernel(const float* __restrict__ pmax, const float* __res
 __global__ void ce_dlogits_kernel(__half* __restrict__ p, int ldp, int M, int V, const float* __restrict__ pmax,
                                   int slots, const float* __restrict__ lse, const uint8_t* __restrict__ valid,
                                   const int* __restrict__ targets, float gscale) {
+  pdl_trigger();
+  pdl_wait();
   const int groups = (V + 7) / 8;
   const int64_t n = static_cast<int64_t>(M) * groups;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
@@ -445,6 +472,8 @@ __global__ void ce_dlogits_kernel(__half* __restrict__ p, int ldp, int M, int V,
 
 // Deterministic single-CTA sum of the row losses.
 __global__ void sum_kernel(const float* __restrict__ x, int n, float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   float s = 0.f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
@@ -465,6 +494,8 @@ __global__ void sum_kernel(const float* __restrict__ x, int n, float* __restrict
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, int64_t n, float lr, float b1, float b2, float eps, float wd,
                              float bc1, float bc2, float gscale) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const float gi = g[i] * gscale;
@@ -496,10 +527,22 @@ __device__ __forceinline__ float normal_at(uint64_t seed, int64_t i) {
 }
 
 __global__ void fill_f32_kernel(float* p, int64_t n, float v) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     p[i] = v;
 }
+// rows x cols of a row-major fp32 matrix (row stride ld) set to v.
+__global__ void fill_f32_2d_kernel(float* p, int ld, int rows, int cols, float v) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t n = static_cast<int64_t>(rows) * cols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p[(i / cols) * ld + i % cols] = v;
+}
+
 __global__ void fill_normal_f16_kernel(__half* p, int64_t n, uint64_t seed, float sd) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
@@ -596,6 +639,8 @@ __global__ void quantize_rows_kernel(const float* __restrict__ w, int cols, int8
 
 __global__ void dequant_rows_kernel(const int8_t* __restrict__ q, const float* __restrict__ scale, int rows,
                                     int cols, __half* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t n = static_cast<int64_t>(rows) * cols;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
@@ -614,21 +659,21 @@ int grid_for(int64_t n, int threads) {
 cudaError_t embed_forward(const int* tokens, const __half* E, float* out, int M, int H, int V, int* err,
                           cudaStream_t st) {
   if (H % 8) return cudaErrorInvalidValue;
-  embed_kernel<<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(tokens, E, out, M, H, V, err);
+  launch_pdl(embed_kernel, (M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, tokens, E, out, M, H, V, err);
   return cudaGetLastError();
 }
 
 cudaError_t rmsnorm_forward(const float* x, const float* w, __half* out, int M, int H, float eps, cudaStream_t st) {
   if (H % 4) return cudaErrorInvalidValue;
   if (H == 2048) {
-    rmsnorm_fwd_row_kernel<16><<<(M + 3) / 4, 128, 0, st>>>(x, w, out, M, eps);
+    launch_pdl(rmsnorm_fwd_row_kernel<16>, (M + 3) / 4, 128, 0, st, x, w, out, M, eps);
     return cudaGetLastError();
   }
   if (H == 256) {
-    rmsnorm_fwd_row_kernel<2><<<(M + 3) / 4, 128, 0, st>>>(x, w, out, M, eps);
+    launch_pdl(rmsnorm_fwd_row_kernel<2>, (M + 3) / 4, 128, 0, st, x, w, out, M, eps);
     return cudaGetLastError();
   }
-  rmsnorm_fwd_kernel<<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(x, w, out, M, H, eps);
+  launch_pdl(rmsnorm_fwd_kernel, (M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, x, w, out, M, H, eps);
   return cudaGetLastError();
 }
 
@@ -638,12 +683,12 @@ cudaError_t rmsnorm_backward(const float* dy, const float* x, const float* w, fl
   if (H == 2048 || H == 256) {
     const int grid = (M + 3) / 4;
     if (H == 2048)
-      rmsnorm_bwd_row_kernel<float, 16><<<grid, 128, 0, st>>>(dy, x, w, dres, dres16, M, eps, accumulate);
+      launch_pdl(rmsnorm_bwd_row_kernel<float, 16>, grid, 128, 0, st, dy, x, w, dres, dres16, M, eps, accumulate);
     else
-      rmsnorm_bwd_row_kernel<float, 2><<<grid, 128, 0, st>>>(dy, x, w, dres, dres16, M, eps, accumulate);
+      launch_pdl(rmsnorm_bwd_row_kernel<float, 2>, grid, 128, 0, st, dy, x, w, dres, dres16, M, eps, accumulate);
     return cudaGetLastError();
   }
-  rmsnorm_bwd_kernel<float><<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(dy, x, w, dres, dres16, M, H,
+  launch_pdl(rmsnorm_bwd_kernel<float>, (M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, dy, x, w, dres, dres16, M, H,
                                                                                          eps, accumulate);
   return cudaGetLastError();
 }
@@ -654,19 +699,19 @@ cudaError_t rmsnorm_backward(const __half* dy, const float* x, const float* w, f
   if (H == 2048 || H == 256) {
     const int grid = (M + 3) / 4;
     if (H == 2048)
-      rmsnorm_bwd_row_kernel<__half, 16><<<grid, 128, 0, st>>>(dy, x, w, dres, dres16, M, eps, accumulate);
+      launch_pdl(rmsnorm_bwd_row_kernel<__half, 16>, grid, 128, 0, st, dy, x, w, dres, dres16, M, eps, accumulate);
     else
-      rmsnorm_bwd_row_kernel<__half, 2><<<grid, 128, 0, st>>>(dy, x, w, dres, dres16, M, eps, accumulate);
+      launch_pdl(rmsnorm_bwd_row_kernel<__half, 2>, grid, 128, 0, st, dy, x, w, dres, dres16, M, eps, accumulate);
     return cudaGetLastError();
   }
-  rmsnorm_bwd_kernel<__half><<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(dy, x, w, dres, dres16, M,
+  launch_pdl(rmsnorm_bwd_kernel<__half>, (M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, dy, x, w, dres, dres16, M,
                                                                                           H, eps, accumulate);
   return cudaGetLastError();
 }
 
 cudaError_t rope_tables(float* cos_t, float* sin_t, int S, int hd, float theta, cudaStream_t st) {
   const int n = S * (hd / 2);
-  rope_table_kernel<<<(n + 255) / 256, 256, 0, st>>>(cos_t, sin_t, S, hd, theta);
+  launch_pdl(rope_table_kernel, (n + 255) / 256, 256, 0, st, cos_t, sin_t, S, hd, theta);
   return cudaGetLastError();
 }
 
@@ -677,11 +722,11 @@ cudaError_t qknorm_rope_forward(const __half* qkv, int ld_qkv, const float* qn_w
   if (ld_qkv % 8) return cudaErrorInvalidValue;
   if (hd == 128) {
     const int warps = M * ((nh + nkv + QkLanes<128>::kHpw - 1) / QkLanes<128>::kHpw);
-    qknorm_rope_fwd_vec_kernel<128><<<(warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(
+    launch_pdl(qknorm_rope_fwd_vec_kernel<128>, (warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, 
         qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, q_out, k_out, M, S, nh, nkv, eps);
   } else if (hd == 64) {
     const int warps = M * ((nh + nkv + QkLanes<64>::kHpw - 1) / QkLanes<64>::kHpw);
-    qknorm_rope_fwd_vec_kernel<64><<<(warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(
+    launch_pdl(qknorm_rope_fwd_vec_kernel<64>, (warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, 
         qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, q_out, k_out, M, S, nh, nkv, eps);
   } else {
     return cudaErrorInvalidValue;
@@ -696,11 +741,11 @@ cudaError_t qknorm_rope_backward(const float* dq, const float* dk, const __half*
   if (ld_qkv % 8) return cudaErrorInvalidValue;
   if (hd == 128) {
     const int warps = M * ((nh + nkv + QkLanes<128>::kHpw - 1) / QkLanes<128>::kHpw);
-    qknorm_rope_bwd_vec_kernel<128><<<(warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(
+    launch_pdl(qknorm_rope_bwd_vec_kernel<128>, (warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, 
         dq, dk, qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, dqkv, M, S, nh, nkv, eps);
   } else if (hd == 64) {
     const int warps = M * ((nh + nkv + QkLanes<64>::kHpw - 1) / QkLanes<64>::kHpw);
-    qknorm_rope_bwd_vec_kernel<64><<<(warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(
+    launch_pdl(qknorm_rope_bwd_vec_kernel<64>, (warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, 
         dq, dk, qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, dqkv, M, S, nh, nkv, eps);
   } else {
     return cudaErrorInvalidValue;
@@ -711,7 +756,7 @@ cudaError_t qknorm_rope_backward(const float* dq, const float* dk, const __half*
 cudaError_t ce_valid_rows(uint8_t* valid, const int* targets, int B, int S, int all_positions, int V, int* err,
                           cudaStream_t st) {
   const int M = B * S;
-  ce_valid_kernel<<<(M + 255) / 256, 256, 0, st>>>(valid, targets, B, S, all_positions, V, err);
+  launch_pdl(ce_valid_kernel, (M + 255) / 256, 256, 0, st, valid, targets, B, S, all_positions, V, err);
   return cudaGetLastError();
 }
 
@@ -719,9 +764,9 @@ cudaError_t ce_reduce(const float* part_max, const float* part_sum, const float*
                       float* lse, float* row_loss_and_sum, int M, int tiles_n, cudaStream_t st) {
   float* row_loss = row_loss_and_sum;
   float* total = row_loss_and_sum + M;
-  ce_lse_kernel<<<(M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st>>>(part_max, part_sum, tgt_logit, valid,
+  launch_pdl(ce_lse_kernel, (M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, part_max, part_sum, tgt_logit, valid,
                                                                              lse, row_loss, M, tiles_n);
-  sum_kernel<<<1, 1024, 0, st>>>(row_loss, M, total);
+  launch_pdl(sum_kernel, 1, 1024, 0, st, row_loss, M, total);
   return cudaGetLastError();
 }
 
@@ -729,37 +774,42 @@ cudaError_t ce_dlogits(__half* p, int ldp, int M, int V, const float* part_max, 
                        const uint8_t* valid, const int* targets, float gscale, cudaStream_t st) {
   if (ldp % 8) return cudaErrorInvalidValue;
   const int64_t n = static_cast<int64_t>(M) * ((V + 7) / 8);
-  ce_dlogits_kernel<<<grid_for(n, 256), 256, 0, st>>>(p, ldp, M, V, part_max, slots, lse, valid, targets, gscale);
+  launch_pdl(ce_dlogits_kernel, grid_for(n, 256), 256, 0, st, p, ldp, M, V, part_max, slots, lse, valid, targets, gscale);
   return cudaGetLastError();
 }
 
 cudaError_t adamw_flat(float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1, float b2,
                        float eps, float wd, float bc1, float bc2, float gscale, cudaStream_t st) {
-  adamw_kernel<<<grid_for(n, 256), 256, 0, st>>>(p, g, m, v, n, lr, b1, b2, eps, wd, bc1, bc2, gscale);
+  launch_pdl(adamw_kernel, grid_for(n, 256), 256, 0, st, p, g, m, v, n, lr, b1, b2, eps, wd, bc1, bc2, gscale);
   return cudaGetLastError();
 }
 
 cudaError_t fill_f32(float* p, int64_t n, float v, cudaStream_t st) {
-  fill_f32_kernel<<<grid_for(n, 256), 256, 0, st>>>(p, n, v);
+  launch_pdl(fill_f32_kernel, grid_for(n, 256), 256, 0, st, p, n, v);
+  return cudaGetLastError();
+}
+cudaError_t fill_f32_2d(float* p, int ld, int rows, int cols, float v, cudaStream_t st) {
+  const int64_t n = static_cast<int64_t>(rows) * cols;
+  launch_pdl(fill_f32_2d_kernel, grid_for(n, 256), 256, 0, st, p, ld, rows, cols, v);
   return cudaGetLastError();
 }
 cudaError_t fill_normal_f16(__half* p, int64_t n, uint64_t seed, float sd, cudaStream_t st) {
-  fill_normal_f16_kernel<<<grid_for(n, 256), 256, 0, st>>>(p, n, seed, sd);
+  launch_pdl(fill_normal_f16_kernel, grid_for(n, 256), 256, 0, st, p, n, seed, sd);
   return cudaGetLastError();
 }
 cudaError_t fill_normal_f32(float* p, int64_t n, uint64_t seed, float sd, cudaStream_t st) {
-  fill_normal_f32_kernel<<<grid_for(n, 256), 256, 0, st>>>(p, n, seed, sd);
+  launch_pdl(fill_normal_f32_kernel, grid_for(n, 256), 256, 0, st, p, n, seed, sd);
   return cudaGetLastError();
 }
 cudaError_t fill_uniform_f32(float* p, int64_t n, uint64_t seed, float lo, float hi, cudaStream_t st) {
-  fill_uniform_f32_kernel<<<grid_for(n, 256), 256, 0, st>>>(p, n, seed, lo, hi);
+  launch_pdl(fill_uniform_f32_kernel, grid_for(n, 256), 256, 0, st, p, n, seed, lo, hi);
   return cudaGetLastError();
 }
 
 cudaError_t convert_weight(const float* src, int rows, int cols, __half* dst, int ld_dst, int row_off,
                            int interleave, __half* dst_t, int ld_t, int col_off_t, cudaStream_t st) {
   dim3 grid((cols + 31) / 32, (rows + 31) / 32);
-  convert_weight_kernel<<<grid, 256, 0, st>>>(src, rows, cols, dst, ld_dst, row_off, interleave, dst_t, ld_t,
+  launch_pdl(convert_weight_kernel, grid, 256, 0, st, src, rows, cols, dst, ld_dst, row_off, interleave, dst_t, ld_t,
                                               col_off_t);
   return cudaGetLastError();
 }
@@ -767,19 +817,19 @@ cudaError_t convert_weight(const float* src, int rows, int cols, __half* dst, in
 cudaError_t transpose_f16(const __half* src, int rows, int cols, int ld_src, __half* dst, int ld_dst,
                           cudaStream_t st) {
   dim3 grid((cols + 31) / 32, (rows + 31) / 32);
-  transpose_f16_kernel<<<grid, 256, 0, st>>>(src, rows, cols, ld_src, dst, ld_dst);
+  launch_pdl(transpose_f16_kernel, grid, 256, 0, st, src, rows, cols, ld_src, dst, ld_dst);
   return cudaGetLastError();
 }
 
 cudaError_t quantize_rows_int8(const float* w, int rows, int cols, int8_t* q, float* scale, cudaStream_t st) {
   if (rows <= 0 || cols <= 0) return cudaErrorInvalidValue;
-  quantize_rows_kernel<<<rows, 256, 0, st>>>(w, cols, q, scale);
+  launch_pdl(quantize_rows_kernel, rows, 256, 0, st, w, cols, q, scale);
   return cudaGetLastError();
 }
 
 cudaError_t dequant_rows_f16(const int8_t* q, const float* scale, int rows, int cols, __half* out, cudaStream_t st) {
   const int64_t n = static_cast<int64_t>(rows) * cols;
-  dequant_rows_kernel<<<grid_for(n, 256), 256, 0, st>>>(q, scale, rows, cols, out);
+  launch_pdl(dequant_rows_kernel, grid_for(n, 256), 256, 0, st, q, scale, rows, cols, out);
   return cudaGetLastError();
 }
 

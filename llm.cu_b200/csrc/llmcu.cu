@@ -389,7 +389,7 @@ llmcu_status wait_event(llmcu_ctx* ctx, cudaEvent_t ev) {
 }
 
 // ------------------------------------------------------------- INT8 base
-__global__ void scale_loss_kernel(const float* total, float inv_n, float* out) { out[0] = total[0] * inv_n; }
+__global__ void scale_loss_kernel(const float* total, float inv_n, float* out) { pdl_trigger(); pdl_wait(); out[0] = total[0] * inv_n; }
 
 
 // fp16 [rows, cols] view of one base weight: the fp16 copy, or the INT8 rows
@@ -420,8 +420,15 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   const float unscale = static_cast<float>(1.0 / (kGradScale * n_valid_total));
   cudaError_t e = cudaSuccess;
 
-  // gradients accumulate (lora_grad adds each split's share)
-  CK(cudaMemsetAsync(ctx->lg, 0, static_cast<size_t>(ctx->n_lora) * sizeof(float), st));
+  // gradients accumulate (lora_grad adds each split's share); this first
+  // kernel follows the host's token upload, so it is launched normally and the
+  // rest of the step's kernels chain by programmatic dependent launch
+  struct PdlScope {
+    ~PdlScope() { set_pdl(false); }
+  } pdl_scope;
+  set_pdl(false);
+  CK(fill_f32(ctx->lg, ctx->n_lora, 0.f, st));
+  set_pdl(true);
   // merged q/k/v/o weights of this step's adapters, every layer
   TIMED(P_LORA_PREP, lora_merge(ctx->lp, d, ctx->L, ctx->mw, ctx->lw[0].mqkv, ctx->lw[0].mo, st));
   TIMED(P_CE, ce_valid_rows(ctx->valid, ctx->tgt, B, S, ctx->rc.loss_all_positions, V, err, st));
@@ -497,7 +504,7 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   TIMED(P_CE, ce_dlogits(ctx->dl, ctx->ld_dl, M, V, ctx->part_max, ctx->ce_tiles, ctx->lse_ce, ctx->valid, ctx->tgt,
                          kGradScale, st));
   {
-    CK(cudaMemsetAsync(ctx->d_xf, 0, static_cast<size_t>(M) * H * sizeof(float), st));
+    CK(fill_f32(ctx->d_xf, static_cast<int64_t>(M) * H, 0.f, st));
     EpiArgs eb;
     eb.out = ctx->d_xf;
     eb.ld_out = H;
@@ -591,7 +598,9 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
                     "allreduce of layer gradients"));
     }
   }
-  // loss: sum over valid rows (over all ranks) / number of valid rows
+  // loss: sum over valid rows (over all ranks) / number of valid rows; the
+  // final kernel may follow an event wait, so it is launched normally
+  set_pdl(false);
   float* total = ctx->row_loss + M;
   if (ctx->nccl) {
     CK(cudaEventRecord(ctx->ev_layer[0], st));

@@ -89,6 +89,8 @@ __device__ __forceinline__ void merge_unpack(const MergeRaw& m, bool int8, float
 __global__ void __launch_bounds__(256, 1)
     lora_merge_main_kernel(const float* __restrict__ flat, LoraDims d, MergeSrc src, int out_rows, int d_in,
                            int which, int tiles, __half* __restrict__ merged, int64_t merged_layer, int ldm) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ __align__(16) float As[16][kMrgCols];
   __shared__ __align__(16) float Bs[kMrgTiles][16][kMrgRows];  // s * B, transposed: [tile][j][row]
   const int l = blockIdx.z;
@@ -171,6 +173,8 @@ __global__ void __launch_bounds__(256, 1)
 // < out_rows and the 64 extra rows (A) of the columns < d_in.
 __global__ void lora_merge_pad_kernel(const float* __restrict__ flat, LoraDims d, __half* __restrict__ mqkv,
                                       int64_t mqkv_layer, __half* __restrict__ mo, int64_t mo_layer) {
+  pdl_trigger();
+  pdl_wait();
   const int l = blockIdx.y;
   const float* P = flat + static_cast<int64_t>(l) * d.per_layer;
   const int r = d.r, H = d.H, Q = d.Q, KV = d.KV, QKV = Q + 2 * KV;
@@ -229,6 +233,8 @@ __device__ __forceinline__ uint32_t uoff(int m, int c) {  // [64 m][64 cols] til
 }
 
 __global__ void __launch_bounds__(kLgThreads) lora_grad_kernel(const LoraGradBatch batch, int M, int splits) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ __align__(128) uint8_t su[2][kLgM * kLgA * 2];
   __shared__ __align__(128) uint8_t sw[2][kLgM * 64 * 2];
   const LoraGradProb& pb = batch.p[blockIdx.y];
@@ -328,11 +334,11 @@ cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const
   };
   const int tq = tiles_for(Q, KV), to = tiles_for(H, H);
   dim3 gq((H + kMrgCols - 1) / kMrgCols, QKV / (kMrgRows * tq), n_layers);
-  lora_merge_main_kernel<<<gq, 256, 0, st>>>(flat, d, sq, QKV, H, 0, tq, mqkv, mqkv_layer, H + 64);
+  launch_pdl(lora_merge_main_kernel, gq, 256, 0, st, flat, d, sq, QKV, H, 0, tq, mqkv, mqkv_layer, H + 64);
   dim3 go((Q + kMrgCols - 1) / kMrgCols, H / (kMrgRows * to), n_layers);
-  lora_merge_main_kernel<<<go, 256, 0, st>>>(flat, d, so, H, Q, 1, to, mo, mo_layer, Q + 64);
+  launch_pdl(lora_merge_main_kernel, go, 256, 0, st, flat, d, so, H, Q, 1, to, mo, mo_layer, Q + 64);
   dim3 gp(128, n_layers);
-  lora_merge_pad_kernel<<<gp, 256, 0, st>>>(flat, d, mqkv, mqkv_layer, mo, mo_layer);
+  launch_pdl(lora_merge_pad_kernel, gp, 256, 0, st, flat, d, mqkv, mqkv_layer, mo, mo_layer);
   return cudaGetLastError();
 }
 
@@ -350,7 +356,7 @@ cudaError_t lora_grad(const LoraGradBatch& batch, int M, cudaStream_t st) {
   if (batch.n <= 0 || batch.n > kLoraMaxProbs) return cudaErrorInvalidValue;
   const int splits = lora_grad_splits(M, batch.a_max, batch.n);
   dim3 grid((batch.a_max + kLgA - 1) / kLgA, batch.n, splits);
-  lora_grad_kernel<<<grid, kLgThreads, 0, st>>>(batch, M, splits);
+  launch_pdl(lora_grad_kernel, grid, kLgThreads, 0, st, batch, M, splits);
   return cudaGetLastError();
 }
 

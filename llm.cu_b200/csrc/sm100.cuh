@@ -151,6 +151,16 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// ------------------------------------------ programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel in the stream drains.  pdl_trigger lets the next kernel
+// start (once every CTA of this one has triggered or exited); pdl_wait blocks
+// until the previous kernel has completed and its writes are visible.  Every
+// step kernel calls pdl_wait before it reads or writes global memory; both
+// are no-ops for launches that did not opt in.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ------------------------------------------------- CTA pairs (cta_group::2)
 // Two CTAs of a cluster share one MMA: the even CTA issues
 // tcgen05.mma.cta_group::2 with M = 256; each CTA holds 128 rows of A, half
