@@ -4,6 +4,7 @@
 //
 // All row kernels put one warp on one row and move 16 bytes per lane per
 // access; reductions are warp shuffles (no shared-memory trees).
+#include <algorithm>
 #include <cmath>
 
 #include "common.cuh"
@@ -470,6 +471,56 @@ __global__ void ce_dlogits_kernel(__half* __restrict__ p, int ldp, int M, int V,
   }
 }
 
+// The same for one row per blockIdx.y: the row's lse / target / validity are
+// read once, no per-element index division, U 16-byte loads in flight per
+// thread before the first store.
+template <int U>
+__global__ void ce_dlogits_row_kernel(__half* __restrict__ p, int ldp, int V, const float* __restrict__ pmax,
+                                      int slots, const float* __restrict__ lse, const uint8_t* __restrict__ valid,
+                                      const int* __restrict__ targets, float gscale) {
+  pdl_trigger();
+  pdl_wait();
+  const int m = blockIdx.y;
+  const bool ok = valid[m] != 0;
+  const float lm = lse[m];
+  const int tgt = targets[m];
+  __half* row = p + static_cast<size_t>(m) * ldp;
+  const float* pm = pmax + static_cast<size_t>(m) * slots;
+  const int base = blockIdx.x * (blockDim.x * 8 * U);
+  uint4 w[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int c0 = base + (u * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x)) * 8;
+    if (c0 + 8 <= V) w[u] = *reinterpret_cast<const uint4*>(row + c0);
+  }
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int c0 = base + (u * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x)) * 8;
+    if (c0 >= V) continue;
+    const float f = ok ? exp2f((pm[c0 / 128] - lm) * kLog2e) * gscale : 0.f;
+    const int t = tgt - c0;
+    if (c0 + 8 <= V) {
+      __half2* h = reinterpret_cast<__half2*>(&w[u]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float2 x = __half22float2(h[k]);
+        x.x *= f;
+        x.y *= f;
+        if (ok && t == 2 * k) x.x -= gscale;
+        if (ok && t == 2 * k + 1) x.y -= gscale;
+        h[k] = __floats2half2_rn(x.x, x.y);
+      }
+      *reinterpret_cast<uint4*>(row + c0) = w[u];
+    } else {
+      for (int k = 0; c0 + k < V; ++k) {
+        float x = __half2float(row[c0 + k]) * f;
+        if (ok && t == k) x -= gscale;
+        row[c0 + k] = __float2half_rn(x);
+      }
+    }
+  }
+}
+
 // Deterministic single-CTA sum of the row losses.
 __global__ void sum_kernel(const float* __restrict__ x, int n, float* __restrict__ out) {
   pdl_trigger();
@@ -533,6 +584,14 @@ __global__ void fill_f32_kernel(float* p, int64_t n, float v) {
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     p[i] = v;
 }
+__global__ void fill_f32x4_kernel(float4* p, int64_t n4, float v) {
+  pdl_trigger();
+  pdl_wait();
+  const float4 q = make_float4(v, v, v, v);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p[i] = q;
+}
 // rows x cols of a row-major fp32 matrix (row stride ld) set to v.
 __global__ void fill_f32_2d_kernel(float* p, int ld, int rows, int cols, float v) {
   pdl_trigger();
@@ -541,6 +600,17 @@ __global__ void fill_f32_2d_kernel(float* p, int ld, int rows, int cols, float v
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     p[(i / cols) * ld + i % cols] = v;
+}
+// The same with 16-byte stores, one block per row at a time (p 16-byte
+// aligned, ld and cols multiples of 4).
+__global__ void fill_f32_2d_vec_kernel(float* p, int ld, int rows, int cols4, float v) {
+  pdl_trigger();
+  pdl_wait();
+  const float4 q = make_float4(v, v, v, v);
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    float4* row = reinterpret_cast<float4*>(p + static_cast<int64_t>(r) * ld);
+    for (int c = threadIdx.x; c < cols4; c += blockDim.x) row[c] = q;
+  }
 }
 
 __global__ void fill_normal_f16_kernel(__half* p, int64_t n, uint64_t seed, float sd) {
@@ -773,6 +843,12 @@ cudaError_t ce_reduce(const float* part_max, const float* part_sum, const float*
 cudaError_t ce_dlogits(__half* p, int ldp, int M, int V, const float* part_max, int slots, const float* lse,
                        const uint8_t* valid, const int* targets, float gscale, cudaStream_t st) {
   if (ldp % 8) return cudaErrorInvalidValue;
+  if (M <= 65535 && reinterpret_cast<uintptr_t>(p) % 16 == 0) {
+    constexpr int kU = 4;
+    const dim3 grid((V + 256 * 8 * kU - 1) / (256 * 8 * kU), M);
+    launch_pdl(ce_dlogits_row_kernel<kU>, grid, 256, 0, st, p, ldp, V, part_max, slots, lse, valid, targets, gscale);
+    return cudaGetLastError();
+  }
   const int64_t n = static_cast<int64_t>(M) * ((V + 7) / 8);
   launch_pdl(ce_dlogits_kernel, grid_for(n, 256), 256, 0, st, p, ldp, M, V, part_max, slots, lse, valid, targets, gscale);
   return cudaGetLastError();
@@ -785,10 +861,21 @@ cudaError_t adamw_flat(float* p, const float* g, float* m, float* v, int64_t n, 
 }
 
 cudaError_t fill_f32(float* p, int64_t n, float v, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  if (reinterpret_cast<uintptr_t>(p) % 16 == 0 && n % 4 == 0) {
+    launch_pdl(fill_f32x4_kernel, grid_for(n / 4, 256), 256, 0, st, reinterpret_cast<float4*>(p), n / 4, v);
+    return cudaGetLastError();
+  }
   launch_pdl(fill_f32_kernel, grid_for(n, 256), 256, 0, st, p, n, v);
   return cudaGetLastError();
 }
 cudaError_t fill_f32_2d(float* p, int ld, int rows, int cols, float v, cudaStream_t st) {
+  if (rows <= 0 || cols <= 0) return cudaSuccess;
+  if (reinterpret_cast<uintptr_t>(p) % 16 == 0 && ld % 4 == 0 && cols % 4 == 0) {
+    const int threads = cols / 4 >= 256 ? 256 : ((cols / 4 + 31) / 32) * 32;
+    launch_pdl(fill_f32_2d_vec_kernel, std::min(rows, 8 * gemm_num_sms()), threads, 0, st, p, ld, rows, cols / 4, v);
+    return cudaGetLastError();
+  }
   const int64_t n = static_cast<int64_t>(rows) * cols;
   launch_pdl(fill_f32_2d_kernel, grid_for(n, 256), 256, 0, st, p, ld, rows, cols, v);
   return cudaGetLastError();

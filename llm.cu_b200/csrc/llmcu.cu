@@ -113,6 +113,7 @@ struct llmcu_ctx {
   bool prof_on = false;
   std::vector<cudaEvent_t> prof_ev;
   std::vector<int> prof_cls;  // class of each recorded (begin, end) event pair
+  std::vector<int> prof_k;    // kernels launched between each (begin, end) pair
   int prof_n = 0;             // events used
   double prof_ms[16] = {0};
   int64_t prof_cnt[16] = {0};
@@ -146,16 +147,20 @@ llmcu_status fail(llmcu_ctx* c, llmcu_status s, const char* fmt, ...) {
   } while (0)
 
 enum ProfClass : int {
-  P_GEMM = 0, P_ATTN_FWD, P_ATTN_BWD, P_NORM, P_LORA_GRAD, P_LORA_PREP, P_CE, P_EMBED, P_ADAMW, P_DEQUANT, P_COUNT
+  P_GEMM = 0, P_ATTN_FWD, P_ATTN_BWD, P_NORM, P_LORA_GRAD, P_LORA_PREP, P_CE, P_EMBED, P_ADAMW, P_DEQUANT, P_FILL,
+  P_COUNT
 };
 const char* kProfNames[P_COUNT] = {"gemm_tc", "attention_fwd", "attention_bwd", "norm_rope", "lora_grad",
-                                   "lora_merge", "ce_reduce", "embed", "adamw", "int8_dequant"};
-const int kProfLaunches[P_COUNT] = {1, 1, 3, 1, 2, 1, 2, 1, 1, 1};  // kernels per call
+                                   "lora_merge", "ce_reduce", "embed", "adamw", "int8_dequant", "fill_and_loss"};
 
-void prof_mark(llmcu_ctx* c, int cls) {
+// Records one event of a (begin, end) pair around `kernels` launches of class `cls`.
+void prof_mark(llmcu_ctx* c, int cls, int kernels = 1) {
   if (!c->prof_on || c->prof_n + 1 > static_cast<int>(c->prof_ev.size())) return;
   cudaEventRecord(c->prof_ev[c->prof_n], c->st);
-  if ((c->prof_n & 1) == 0) c->prof_cls.push_back(cls);
+  if ((c->prof_n & 1) == 0) {
+    c->prof_cls.push_back(cls);
+    c->prof_k.push_back(kernels);
+  }
   ++c->prof_n;
 }
 
@@ -165,12 +170,14 @@ void prof_mark(llmcu_ctx* c, int cls) {
     if (s_ != LLMCU_OK) return s_;                 \
   } while (0)
 
-#define TIMED(cls, expr)        \
+// `expr` launches `n` kernels of class `cls`
+#define TIMEDN(cls, n, expr)    \
   do {                          \
-    prof_mark(ctx, cls);        \
+    prof_mark(ctx, cls, n);     \
     CK(expr);                   \
-    prof_mark(ctx, cls);        \
+    prof_mark(ctx, cls, n);     \
   } while (0)
+#define TIMED(cls, expr) TIMEDN(cls, 1, expr)
 
 Operand op(const __half* p, int rows, int k, int ld) { return Operand{p, rows, k, ld}; }
 
@@ -427,10 +434,10 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     ~PdlScope() { set_pdl(false); }
   } pdl_scope;
   set_pdl(false);
-  CK(fill_f32(ctx->lg, ctx->n_lora, 0.f, st));
+  TIMED(P_FILL, fill_f32(ctx->lg, ctx->n_lora, 0.f, st));
   set_pdl(true);
   // merged q/k/v/o weights of this step's adapters, every layer
-  TIMED(P_LORA_PREP, lora_merge(ctx->lp, d, ctx->L, ctx->mw, ctx->lw[0].mqkv, ctx->lw[0].mo, st));
+  TIMEDN(P_LORA_PREP, 3, lora_merge(ctx->lp, d, ctx->L, ctx->mw, ctx->lw[0].mqkv, ctx->lw[0].mo, st));
   TIMED(P_CE, ce_valid_rows(ctx->valid, ctx->tgt, B, S, ctx->rc.loss_all_positions, V, err, st));
   const __half* E = ctx->E;
   TIMED(P_EMBED, embed_forward(ctx->tok, E, ctx->resid[0], M, H, V, err, st));
@@ -499,12 +506,12 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     ea.ld_out = ctx->ld_dl;
     TIMED(P_GEMM, gemm(op(ctx->xf, M, H, H), op(E, V, H, H), M, V, Epi::kCEProbs, ea, err, st, 256));
   }
-  TIMED(P_CE, ce_reduce(ctx->part_max, ctx->part_sum, ctx->tgt_logit, ctx->valid, ctx->lse_ce, ctx->row_loss, M,
+  TIMEDN(P_CE, 2, ce_reduce(ctx->part_max, ctx->part_sum, ctx->tgt_logit, ctx->valid, ctx->lse_ce, ctx->row_loss, M,
                ctx->ce_tiles, st));
   TIMED(P_CE, ce_dlogits(ctx->dl, ctx->ld_dl, M, V, ctx->part_max, ctx->ce_tiles, ctx->lse_ce, ctx->valid, ctx->tgt,
                          kGradScale, st));
   {
-    CK(fill_f32(ctx->d_xf, static_cast<int64_t>(M) * H, 0.f, st));
+    TIMED(P_FILL, fill_f32(ctx->d_xf, static_cast<int64_t>(M) * H, 0.f, st));
     EpiArgs eb;
     eb.out = ctx->d_xf;
     eb.ld_out = H;
@@ -555,7 +562,7 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     }
     // attention
     // (delta came with the O-projection dX GEMM)
-    TIMED(P_ATTN_BWD, attention_backward_tc(a.qrope, a.krope, a.qkv + Q + KV, ctx->dattn, a.lse, ctx->delta, ctx->dq,
+    TIMEDN(P_ATTN_BWD, 2, attention_backward_tc(a.qrope, a.krope, a.qkv + Q + KV, ctx->dattn, a.lse, ctx->delta, ctx->dq,
                                             ctx->dk, ctx->dqkv + Q + KV, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV, QKV, Q,
                                             Q, KV, QKV, err, st));
     TIMED(P_NORM, qknorm_rope_backward(ctx->dq, ctx->dk, a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, ctx->dqkv,
@@ -609,8 +616,10 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     CK(cudaEventRecord(ctx->ev_comm_done, ctx->comm));
     CK(cudaStreamWaitEvent(st, ctx->ev_comm_done, 0));
   }
+  prof_mark(ctx, P_FILL);
   scale_loss_kernel<<<1, 1, 0, st>>>(total, static_cast<float>(1.0 / n_valid_total), ctx->loss_dev);
   CK(cudaGetLastError());
+  prof_mark(ctx, P_FILL);
   return LLMCU_OK;
 }
 
@@ -1178,11 +1187,12 @@ static void prof_collect(llmcu_ctx* ctx) {
     if (cudaEventElapsedTime(&ms, ctx->prof_ev[i], ctx->prof_ev[i + 1]) == cudaSuccess) {
       const int c = ctx->prof_cls[i / 2];
       ctx->prof_ms[c] += ms;
-      ctx->prof_cnt[c] += kProfLaunches[c];
+      ctx->prof_cnt[c] += ctx->prof_k[i / 2];
     }
   }
   ctx->prof_n = 0;
   ctx->prof_cls.clear();
+  ctx->prof_k.clear();
 }
 
 llmcu_status llmcu_profile_enable(llmcu_ctx* ctx, int on) {

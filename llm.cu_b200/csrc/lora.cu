@@ -169,6 +169,92 @@ __global__ void __launch_bounds__(256, 1)
   }
 }
 
+// Tensor-core form of the main block for fp16 base weights: a block merges
+// 64 rows x 128 columns of one adapter.  The W tile is staged in shared
+// memory (16-byte cp.async, issued before the wait on the previous kernel:
+// the base weights are constant), s*B [64 x 16] and A^T [128 x 16] are
+// rounded to fp16 there, and each warp adds s*B*A to its 16 rows with one
+// m16n8k16 MMA per 8 columns, the accumulator starting from W.  The merged
+// tile is written back in place and stored with 16-byte coalesced stores.
+constexpr int kMtRows = 64;
+constexpr int kMtCols = 128;
+constexpr int kMtPad = 8;  // halves of row padding: conflict-free fragment access
+__global__ void __launch_bounds__(128)
+    lora_merge_tc_kernel(const float* __restrict__ flat, LoraDims d, const __half* __restrict__ w, int64_t w_layer,
+                         int d_in, int which, __half* __restrict__ merged, int64_t merged_layer, int ldm) {
+  pdl_trigger();
+  __shared__ __align__(16) __half sW[kMtRows][kMtCols + kMtPad];
+  __shared__ __align__(16) __half sB[kMtRows][16 + kMtPad];
+  __shared__ __align__(16) __half sAT[kMtCols][16 + kMtPad];
+  const int l = blockIdx.z, o0 = blockIdx.y * kMtRows, c0 = blockIdx.x * kMtCols;
+  const __half* wl = w + static_cast<int64_t>(l) * w_layer;
+  for (int i = threadIdx.x; i < kMtRows * (kMtCols / 8); i += blockDim.x) {
+    const int rr = i / (kMtCols / 8), ch = i % (kMtCols / 8);
+    const int c = c0 + ch * 8;
+    const bool ok = c < d_in;
+    cp_async_16(smem_u32(&sW[rr][ch * 8]), wl + static_cast<int64_t>(o0 + rr) * d_in + (ok ? c : 0), ok ? 16 : 0);
+  }
+  cp_async_commit();
+  pdl_wait();  // the adapters are written by the previous step's optimizer
+  const float* P = flat + static_cast<int64_t>(l) * d.per_layer;
+  int proj, row_base;
+  if (which == 1) {
+    proj = 3;
+    row_base = 0;
+  } else if (o0 < d.Q) {
+    proj = 0;
+    row_base = 0;
+  } else if (o0 < d.Q + d.KV) {
+    proj = 1;
+    row_base = d.Q;
+  } else {
+    proj = 2;
+    row_base = d.Q + d.KV;
+  }
+  const float* A = P + d.offA(proj);
+  const float* Bm = P + d.offB(proj);
+  const int r = d.r;
+  for (int i = threadIdx.x; i < kMtRows * 16; i += blockDim.x) {
+    const int rr = i / 16, j = i % 16;
+    sB[rr][j] = __float2half_rn(j < r ? d.scale * Bm[static_cast<int64_t>(o0 + rr - row_base) * r + j] : 0.f);
+  }
+  for (int i = threadIdx.x; i < 16 * kMtCols; i += blockDim.x) {
+    const int j = i / kMtCols, c = i % kMtCols;
+    sAT[c][j] = __float2half_rn((j < r && c0 + c < d_in) ? A[static_cast<int64_t>(j) * d_in + c0 + c] : 0.f);
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int wr = warp * 16;
+  uint32_t a[4];
+  a[0] = *reinterpret_cast<const uint32_t*>(&sB[wr + g][2 * t]);
+  a[1] = *reinterpret_cast<const uint32_t*>(&sB[wr + g + 8][2 * t]);
+  a[2] = *reinterpret_cast<const uint32_t*>(&sB[wr + g][8 + 2 * t]);
+  a[3] = *reinterpret_cast<const uint32_t*>(&sB[wr + g + 8][8 + 2 * t]);
+#pragma unroll
+  for (int nb = 0; nb < kMtCols / 8; ++nb) {
+    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&sAT[nb * 8 + g][2 * t]);
+    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&sAT[nb * 8 + g][8 + 2 * t]);
+    __half2* p0 = reinterpret_cast<__half2*>(&sW[wr + g][nb * 8 + 2 * t]);
+    __half2* p1 = reinterpret_cast<__half2*>(&sW[wr + g + 8][nb * 8 + 2 * t]);
+    const float2 w0 = __half22float2(*p0), w1 = __half22float2(*p1);
+    float acc[4] = {w0.x, w0.y, w1.x, w1.y};
+    mma_16816(acc, a, b0, b1);
+    *p0 = __floats2half2_rn(acc[0], acc[1]);
+    *p1 = __floats2half2_rn(acc[2], acc[3]);
+  }
+  __syncwarp();
+  __half* out = merged + static_cast<int64_t>(l) * merged_layer;
+  for (int i = lane; i < 16 * (kMtCols / 8); i += 32) {
+    const int rr = i / (kMtCols / 8), ch = i % (kMtCols / 8);
+    const int c = c0 + ch * 8;
+    if (c < d_in)
+      *reinterpret_cast<uint4*>(out + static_cast<int64_t>(o0 + wr + rr) * ldm + c) =
+          *reinterpret_cast<const uint4*>(&sW[wr + rr][ch * 8]);
+  }
+}
+
 // The pads of both merged weights: the 64 extra columns (s B) of the rows
 // < out_rows and the 64 extra rows (A) of the columns < d_in.
 __global__ void lora_merge_pad_kernel(const float* __restrict__ flat, LoraDims d, __half* __restrict__ mqkv,
@@ -332,11 +418,19 @@ cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const
     while (t > 1 && ((a / kMrgRows) % t || (b / kMrgRows) % t)) t /= 2;
     return t;
   };
-  const int tq = tiles_for(Q, KV), to = tiles_for(H, H);
-  dim3 gq((H + kMrgCols - 1) / kMrgCols, QKV / (kMrgRows * tq), n_layers);
-  launch_pdl(lora_merge_main_kernel, gq, 256, 0, st, flat, d, sq, QKV, H, 0, tq, mqkv, mqkv_layer, H + 64);
-  dim3 go((Q + kMrgCols - 1) / kMrgCols, H / (kMrgRows * to), n_layers);
-  launch_pdl(lora_merge_main_kernel, go, 256, 0, st, flat, d, so, H, Q, 1, to, mo, mo_layer, Q + 64);
+  if (!base.q_qkv && !base.q_o) {  // fp16 base: tensor-core rank-r update
+    dim3 gq((H + kMtCols - 1) / kMtCols, QKV / kMtRows, n_layers);
+    launch_pdl(lora_merge_tc_kernel, gq, 128, 0, st, flat, d, base.wqkv, base.w_layer_qkv, H, 0, mqkv, mqkv_layer,
+               H + 64);
+    dim3 go((Q + kMtCols - 1) / kMtCols, H / kMtRows, n_layers);
+    launch_pdl(lora_merge_tc_kernel, go, 128, 0, st, flat, d, base.wo, base.w_layer_o, Q, 1, mo, mo_layer, Q + 64);
+  } else {
+    const int tq = tiles_for(Q, KV), to = tiles_for(H, H);
+    dim3 gq((H + kMrgCols - 1) / kMrgCols, QKV / (kMrgRows * tq), n_layers);
+    launch_pdl(lora_merge_main_kernel, gq, 256, 0, st, flat, d, sq, QKV, H, 0, tq, mqkv, mqkv_layer, H + 64);
+    dim3 go((Q + kMrgCols - 1) / kMrgCols, H / (kMrgRows * to), n_layers);
+    launch_pdl(lora_merge_main_kernel, go, 256, 0, st, flat, d, so, H, Q, 1, to, mo, mo_layer, Q + 64);
+  }
   dim3 gp(128, n_layers);
   launch_pdl(lora_merge_pad_kernel, gp, 256, 0, st, flat, d, mqkv, mqkv_layer, mo, mo_layer);
   return cudaGetLastError();
