@@ -114,6 +114,9 @@ struct EpiArgs {
 cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, const EpiArgs& ea, int* err,
                  cudaStream_t st, int bn_hint = 0);
 int gemm_num_sms();
+// fp16 [rows, cols] row-major (row stride ld elements), 128-byte swizzle,
+// box 64 columns x box_rows rows.
+bool encode_tma_2d_f16(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, int box_rows);
 
 // ---- kernels.cu
 cudaError_t embed_forward(const int* tokens, const __half* E, float* out, int M, int H, int V, int* err,

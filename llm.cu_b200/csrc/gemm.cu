@@ -165,6 +165,12 @@ int gemm_num_sms() {
   return g_num_sms;
 }
 
+bool encode_tma_2d_f16(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, int box_rows) {
+  std::call_once(g_once, init_once);
+  Operand op{static_cast<const __half*>(ptr), rows, cols, ld, false};
+  return make_map(map, op, box_rows);
+}
+
 cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, const EpiArgs& ea, int* err,
                  cudaStream_t st, int bn_hint) {
   std::call_once(g_once, init_once);

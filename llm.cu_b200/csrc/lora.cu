@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(256, 1)
 // Tensor-core form of the main block for fp16 base weights: a block merges
 // 64 rows x 128 columns of one adapter.  The W tile is staged in shared
 // memory (16-byte cp.async, issued before the wait on the previous kernel:
-// the base weights are constant), s*B [64 x 16] and A^T [128 x 16] are
+// the base weights are constant), s*B [64 x 16] and A [16 x 128] are
 // rounded to fp16 there, and each warp adds s*B*A to its 16 rows with one
 // m16n8k16 MMA per 8 columns, the accumulator starting from W.  The merged
 // tile is written back in place and stored with 16-byte coalesced stores.
@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(128)
   pdl_trigger();
   __shared__ __align__(16) __half sW[kMtRows][kMtCols + kMtPad];
   __shared__ __align__(16) __half sB[kMtRows][16 + kMtPad];
-  __shared__ __align__(16) __half sAT[kMtCols][16 + kMtPad];
+  __shared__ __align__(16) __half sA[16][kMtCols + kMtPad];
   const int l = blockIdx.z, o0 = blockIdx.y * kMtRows, c0 = blockIdx.x * kMtCols;
   const __half* wl = w + static_cast<int64_t>(l) * w_layer;
   for (int i = threadIdx.x; i < kMtRows * (kMtCols / 8); i += blockDim.x) {
@@ -214,13 +214,47 @@ __global__ void __launch_bounds__(128)
   const float* A = P + d.offA(proj);
   const float* Bm = P + d.offB(proj);
   const int r = d.r;
-  for (int i = threadIdx.x; i < kMtRows * 16; i += blockDim.x) {
-    const int rr = i / 16, j = i % 16;
-    sB[rr][j] = __float2half_rn(j < r ? d.scale * Bm[static_cast<int64_t>(o0 + rr - row_base) * r + j] : 0.f);
-  }
-  for (int i = threadIdx.x; i < 16 * kMtCols; i += blockDim.x) {
-    const int j = i / kMtCols, c = i % kMtCols;
-    sAT[c][j] = __float2half_rn((j < r && c0 + c < d_in) ? A[static_cast<int64_t>(j) * d_in + c0 + c] : 0.f);
+  if (r == 16 && d_in % 4 == 0) {
+    // every adapter load of the thread in flight at once (16-byte loads):
+    // A rows [16 x 128] are 512 float4, B rows [64 x 16] are 256
+    static_assert(kMtCols == 128 && kMtRows == 64, "staging below assumes a 64 x 128 block of 128 threads");
+    float4 av[4], bv[2];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = threadIdx.x + k * 128;
+      const int j = i >> 5, c = (i & 31) * 4;
+      av[k] = c0 + c < d_in ? *reinterpret_cast<const float4*>(A + static_cast<int64_t>(j) * d_in + c0 + c)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = threadIdx.x + k * 128;
+      const int rr = i >> 2, j = (i & 3) * 4;
+      bv[k] = *reinterpret_cast<const float4*>(Bm + static_cast<int64_t>(o0 + rr - row_base) * 16 + j);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = threadIdx.x + k * 128;
+      const int j = i >> 5, c = (i & 31) * 4;
+      *reinterpret_cast<__half2*>(&sA[j][c]) = __floats2half2_rn(av[k].x, av[k].y);
+      *reinterpret_cast<__half2*>(&sA[j][c + 2]) = __floats2half2_rn(av[k].z, av[k].w);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = threadIdx.x + k * 128;
+      const int rr = i >> 2, j = (i & 3) * 4;
+      *reinterpret_cast<__half2*>(&sB[rr][j]) = __floats2half2_rn(d.scale * bv[k].x, d.scale * bv[k].y);
+      *reinterpret_cast<__half2*>(&sB[rr][j + 2]) = __floats2half2_rn(d.scale * bv[k].z, d.scale * bv[k].w);
+    }
+  } else {
+    for (int i = threadIdx.x; i < kMtRows * 16; i += blockDim.x) {
+      const int rr = i / 16, j = i % 16;
+      sB[rr][j] = __float2half_rn(j < r ? d.scale * Bm[static_cast<int64_t>(o0 + rr - row_base) * r + j] : 0.f);
+    }
+    for (int i = threadIdx.x; i < 16 * kMtCols; i += blockDim.x) {
+      const int j = i / kMtCols, c = i % kMtCols;
+      sA[j][c] = __float2half_rn((j < r && c0 + c < d_in) ? A[static_cast<int64_t>(j) * d_in + c0 + c] : 0.f);
+    }
   }
   cp_async_wait<0>();
   __syncthreads();
@@ -232,17 +266,23 @@ __global__ void __launch_bounds__(128)
   a[1] = *reinterpret_cast<const uint32_t*>(&sB[wr + g + 8][2 * t]);
   a[2] = *reinterpret_cast<const uint32_t*>(&sB[wr + g][8 + 2 * t]);
   a[3] = *reinterpret_cast<const uint32_t*>(&sB[wr + g + 8][8 + 2 * t]);
+  // B operand (k = rank, n = column) straight from the row-major A tile:
+  // one transposed ldmatrix.x4 yields the fragments of two 8-column blocks
+  const int lrow = (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
-  for (int nb = 0; nb < kMtCols / 8; ++nb) {
-    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&sAT[nb * 8 + g][2 * t]);
-    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&sAT[nb * 8 + g][8 + 2 * t]);
-    __half2* p0 = reinterpret_cast<__half2*>(&sW[wr + g][nb * 8 + 2 * t]);
-    __half2* p1 = reinterpret_cast<__half2*>(&sW[wr + g + 8][nb * 8 + 2 * t]);
-    const float2 w0 = __half22float2(*p0), w1 = __half22float2(*p1);
-    float acc[4] = {w0.x, w0.y, w1.x, w1.y};
-    mma_16816(acc, a, b0, b1);
-    *p0 = __floats2half2_rn(acc[0], acc[1]);
-    *p1 = __floats2half2_rn(acc[2], acc[3]);
+  for (int nb = 0; nb < kMtCols / 8; nb += 2) {
+    uint32_t bf[4];
+    ldmatrix_x4_trans(smem_u32(&sA[lrow][nb * 8 + (lane >> 4) * 8]), bf[0], bf[1], bf[2], bf[3]);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      __half2* p0 = reinterpret_cast<__half2*>(&sW[wr + g][(nb + h) * 8 + 2 * t]);
+      __half2* p1 = reinterpret_cast<__half2*>(&sW[wr + g + 8][(nb + h) * 8 + 2 * t]);
+      const float2 w0 = __half22float2(*p0), w1 = __half22float2(*p1);
+      float acc[4] = {w0.x, w0.y, w1.x, w1.y};
+      mma_16816(acc, a, bf[2 * h], bf[2 * h + 1]);
+      *p0 = __floats2half2_rn(acc[0], acc[1]);
+      *p1 = __floats2half2_rn(acc[2], acc[3]);
+    }
   }
   __syncwarp();
   __half* out = merged + static_cast<int64_t>(l) * merged_layer;
@@ -310,97 +350,170 @@ __global__ void lora_merge_pad_kernel(const float* __restrict__ flat, LoraDims d
   }
 }
 
-constexpr int kLgThreads = 128;
-constexpr int kLgA = 64;   // a-rows per CTA (4 warps x 16)
-constexpr int kLgM = 64;   // m per smem stage
+constexpr int kLgThreads = 128;  // warp 0 lane 0: TMA, warp 1 lane 0: MMA; all four drain TMEM
+constexpr int kLgA = 128;         // a-rows per CTA: the UMMA M
+constexpr int kLgM = 64;          // m per stage: four K = 16 UMMA steps
+constexpr int kLgStages = 4;
+constexpr int kLgUBytes = kLgM * kLgA * 2;  // 16 KB: two [64 m][64 a] TMA boxes
+constexpr int kLgWBytes = kLgM * 64 * 2;    // 8 KB: one [64 m][64 b] TMA box
+constexpr int kLgSmem = kLgStages * (kLgUBytes + kLgWBytes) + 1024 + 256;
 
-__device__ __forceinline__ uint32_t uoff(int m, int c) {  // [64 m][64 cols] tile, 8 chunks per row
-  return static_cast<uint32_t>((m * 8 + (c ^ (m & 7))) * 16);
-}
+// U and W of every problem as TMA tensors ([M, A] and [M, 16 * groups]),
+// 64 x 64 boxes, 128-byte swizzle
+struct LoraGradMaps {
+  CUtensorMap u[kLoraMaxProbs];
+  CUtensorMap w[kLoraMaxProbs];
+};
 
-__global__ void __launch_bounds__(kLgThreads) lora_grad_kernel(const LoraGradBatch batch, int M, int splits) {
+// One CTA: a-rows [a0, a0 + 128) of one problem over its split's m range,
+// D[a, b] = sum_m U[m, a] W[m, b] on the tensor cores: U^T is the A operand
+// and W the B operand, both read MN-major (a and b are the contiguous
+// dimensions of the [m, *] row-major inputs), D in 64 TMEM columns.  TMA
+// keeps kLgStages stages in flight; the epilogue adds the scaled sums into
+// the gradients.
+__global__ void __launch_bounds__(kLgThreads, 2)
+    lora_grad_kernel(const __grid_constant__ LoraGradMaps maps, const LoraGradBatch batch, int M, int splits) {
   pdl_trigger();
-  pdl_wait();
-  __shared__ __align__(128) uint8_t su[2][kLgM * kLgA * 2];
-  __shared__ __align__(128) uint8_t sw[2][kLgM * 64 * 2];
+  extern __shared__ uint8_t lg_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(lg_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kLgStages * (kLgUBytes + kLgWBytes));
+  uint64_t* empty = full + kLgStages;
+  uint64_t* acc_full = empty + kLgStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const LoraGradProb& pb = batch.p[blockIdx.y];
   const int a0 = blockIdx.x * kLgA;
-  if (a0 >= pb.A) return;
+  if (a0 >= pb.A) return;  // whole CTA
   const int split = blockIdx.z;
   const int m_per = ((M + splits - 1) / splits + kLgM - 1) / kLgM * kLgM;
   const int m_begin = split * m_per;
   const int m_end = min(M, m_begin + m_per);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ng = pb.groups;
-
-  auto load = [&](int buf, int m0) {
-    const uint32_t su_b = smem_u32(su[buf]);
-    const uint32_t sw_b = smem_u32(sw[buf]);
-    for (int i = threadIdx.x; i < kLgM * 8; i += kLgThreads) {
-      const int mm = i >> 3, c = i & 7;
-      const int m = m0 + mm;
-      const bool ok = m < m_end && (a0 + c * 8) < pb.A;
-      const __half* src = pb.U + static_cast<size_t>(ok ? m : m_begin) * pb.ldu + (ok ? a0 + c * 8 : 0);
-      cp_async_16(su_b + uoff(mm, c), src, ok ? 16 : 0);
-      const bool okw = m < m_end && c < 2 * ng;
-      const __half* srcw = pb.W + static_cast<size_t>(okw ? m : m_begin) * pb.ldw + (okw ? c * 8 : 0);
-      cp_async_16(sw_b + uoff(mm, c), srcw, okw ? 16 : 0);
-    }
-  };
-
-  float acc[8][4];
-#pragma unroll
-  for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  // splits end on 64-row boundaries or at M (where the boxes read zeros), so
+  // no box reaches into the next split's rows
   const int nsteps = m_end > m_begin ? (m_end - m_begin + kLgM - 1) / kLgM : 0;
-  if (nsteps > 0) load(0, m_begin);
-  cp_async_commit();
-  for (int s = 0; s < nsteps; ++s) {
-    const int buf = s & 1;
-    if (s + 1 < nsteps) load(buf ^ 1, m_begin + (s + 1) * kLgM);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    const uint32_t su_b = smem_u32(su[buf]);
-    const uint32_t sw_b = smem_u32(sw[buf]);
-#pragma unroll
-    for (int kk = 0; kk < kLgM / 16; ++kk) {
-      const int mi = lane >> 3;
-      uint32_t a[4];
-      ldmatrix_x4_trans(su_b + uoff(kk * 16 + (mi >> 1) * 8 + (lane & 7), warp * 2 + (mi & 1)), a[0], a[1], a[2],
-                        a[3]);
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        if (g < ng) {
-          uint32_t b0, b1, b2, b3;
-          ldmatrix_x4_trans(sw_b + uoff(kk * 16 + (mi & 1) * 8 + (lane & 7), 2 * g + (mi >> 1)), b0, b1, b2, b3);
-          mma_16816(acc[2 * g], a, b0, b1);
-          mma_16816(acc[2 * g + 1], a, b2, b3);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const CUtensorMap* umap = &maps.u[blockIdx.y];
+  const CUtensorMap* wmap = &maps.w[blockIdx.y];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kLgStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(umap);
+    tma_prefetch_desc(wmap);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 64);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    int issued = 0;
+    bool ok = true;
+    for (int s = 0; s < nsteps; ++s) {
+      const int buf = s % kLgStages;
+      if (!mbar_wait(&empty[buf], ((s / kLgStages) & 1) ^ 1, abort_flag, nullptr, 0)) {
+        ok = false;
+        break;
+      }
+      uint8_t* su = smem + buf * kLgUBytes;
+      uint8_t* sw = smem + kLgStages * kLgUBytes + buf * kLgWBytes;
+      const int m0 = m_begin + s * kLgM;
+      mbar_arrive_expect_tx(&full[buf], kLgUBytes + kLgWBytes);
+      tma_load_2d(su, umap, &full[buf], a0, m0);
+      tma_load_2d(su + kLgUBytes / 2, umap, &full[buf], a0 + 64, m0);
+      tma_load_2d(sw, wmap, &full[buf], 0, m0);
+      ++issued;
+    }
+    if (!ok) {  // let the copies already issued land before the CTA can exit
+      for (int j = max(0, issued - kLgStages); j < issued; ++j) {
+        const uint32_t bar = smem_u32(&full[j % kLgStages]);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(bar, (j / kLgStages) & 1) && globaltimer_ns() - t0 < 100000000ull) {
         }
       }
     }
-    __syncthreads();
+  } else if (warp == 1 && lane == 0) {
+    // ---------------------------------------------------------- MMA issuer
+    constexpr uint32_t idesc = idesc_f16_f32(kLgA, 64) | (1u << 15) | (1u << 16);  // A, B MN-major
+    bool ok = true;
+    for (int s = 0; s < nsteps && ok; ++s) {
+      const int buf = s % kLgStages;
+      if (!mbar_wait(&full[buf], (s / kLgStages) & 1, abort_flag, nullptr, 0)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t su = smem_u32(smem + buf * kLgUBytes);
+      const uint32_t sw = smem_u32(smem + kLgStages * kLgUBytes + buf * kLgWBytes);
+      const uint64_t adesc = sw128_mn_desc(su, kLgUBytes / 2);
+      const uint64_t bdesc = sw128_mn_desc(sw, kLgWBytes);
+#pragma unroll
+      for (int k = 0; k < kLgM / 16; ++k)  // +16 m rows of 128 bytes per K step
+        umma_f16(tmem, adesc + (16 * 128 >> 4) * k, bdesc + (16 * 128 >> 4) * k, idesc, (s > 0 || k > 0) ? 1u : 0u);
+      umma_commit(&empty[buf]);
+    }
+    if (ok && nsteps > 0) umma_commit(acc_full);
   }
-  cp_async_wait<0>();
+  __syncwarp();
 
-  // this split's share, scaled, added straight into the gradients (zeroed
-  // before the layer's first split lands; the order of the additions across
-  // splits is not fixed)
-  const int gq = lane >> 2, t = lane & 3;
+  // ------------------------------------------------------------ epilogue
+  // warp w owns TMEM lanes 32w.. = a-rows a0 + 32w + lane; column b = 16 g + j
+  const bool got = nsteps > 0 && mbar_wait(acc_full, 0, abort_flag, nullptr, 0);
+  if (__syncthreads_and(got)) {  // CTA-uniform: the staged path below synchronises
+    tc_fence_after();
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const int ar = warp * 32 + lane;  // a-row within the tile
+    const int a = a0 + ar;
+    const int ng = pb.groups;
+    // [a][b] row-major gradients (dB: sa = 16, sb = 1) are staged through
+    // shared memory so that the additions leave as contiguous runs; the
+    // [b][a] ones (dA: sa = 1) are already contiguous across the lanes
+    const bool staged = pb.sb == 1 && pb.sa == 16 && pb.Bn == 16 && ng == 1 && a0 + kLgA <= pb.A;
+    float* stage = reinterpret_cast<float*>(smem);  // [128][17], the stage buffers are idle now
+    uint32_t v[32];
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      if (32 * half < 16 * ng) {  // warp-uniform
+        tmem_ld_32x32b_x32(taddr + 32 * half, v);
+        tmem_ld_wait();
+        if (staged) {
 #pragma unroll
-  for (int n = 0; n < 8; ++n) {
-    if (n < 2 * ng) {
+          for (int j = 0; j < 16; ++j) stage[ar * 17 + j] = __uint_as_float(v[j]) * pb.scale;
+        } else if (a < pb.A) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int a = a0 + warp * 16 + gq + (e >> 1) * 8;
-        const int gb = n * 8 + 2 * t + (e & 1);
-        const int g = gb >> 4, b = gb & 15;
-        if (a < pb.A && b < pb.Bn)
-          atomicAdd(pb.out[g] + static_cast<size_t>(a) * pb.sa + static_cast<size_t>(b) * pb.sb, acc[n][e] * pb.scale);
+          for (int j = 0; j < 32; ++j) {
+            const int bcol = 32 * half + j;
+            const int g = bcol >> 4, b = bcol & 15;
+            if (g < ng && b < pb.Bn)
+              atomicAdd(pb.out[g] + static_cast<size_t>(a) * pb.sa + static_cast<size_t>(b) * pb.sb,
+                        __uint_as_float(v[j]) * pb.scale);
+          }
+        }
       }
     }
+    if (staged) {
+      __syncthreads();
+      float* dst = pb.out[0] + static_cast<size_t>(a0) * 16;
+      for (int i = threadIdx.x; i < kLgA * 16; i += kLgThreads) atomicAdd(dst + i, stage[(i >> 4) * 17 + (i & 15)]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
   }
 }
-
 
 }  // namespace
 
@@ -438,7 +551,7 @@ cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const
 
 int lora_grad_splits(int M, int a_max, int n) {
   const int tiles = (a_max + kLgA - 1) / kLgA * n;
-  int s = (6 * gemm_num_sms() + tiles - 1) / tiles;  // ~6 CTAs per SM
+  int s = 2 * gemm_num_sms() / tiles;  // about two CTAs per SM, one wave
   const int max_s = (M + 255) / 256;
   if (s > max_s) s = max_s;
   if (s > kLoraMaxSplits) s = kLoraMaxSplits;
@@ -449,8 +562,22 @@ int lora_grad_splits(int M, int a_max, int n) {
 cudaError_t lora_grad(const LoraGradBatch& batch, int M, cudaStream_t st) {
   if (batch.n <= 0 || batch.n > kLoraMaxProbs) return cudaErrorInvalidValue;
   const int splits = lora_grad_splits(M, batch.a_max, batch.n);
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(lora_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kLgSmem);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  LoraGradMaps maps;
+  for (int i = 0; i < batch.n; ++i) {
+    const LoraGradProb& p = batch.p[i];
+    if (p.groups < 1 || p.groups > 4) return cudaErrorInvalidValue;
+    if (!encode_tma_2d_f16(&maps.u[i], p.U, M, p.A, p.ldu, kLgM) ||
+        !encode_tma_2d_f16(&maps.w[i], p.W, M, 16 * p.groups, p.ldw, kLgM))
+      return cudaErrorInvalidValue;
+  }
   dim3 grid((batch.a_max + kLgA - 1) / kLgA, batch.n, splits);
-  launch_pdl(lora_grad_kernel, grid, kLgThreads, 0, st, batch, M, splits);
+  launch_pdl(lora_grad_kernel, grid, kLgThreads, kLgSmem, st, maps, batch, M, splits);
   return cudaGetLastError();
 }
 

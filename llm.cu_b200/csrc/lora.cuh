@@ -75,7 +75,7 @@ struct LoraGradProb {
 struct LoraGradBatch {
   LoraGradProb p[kLoraMaxProbs];
   int n;
-  int a_max;  // multiple of 64, >= every A
+  int a_max;  // >= every A
 };
 
 cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const MergeWeights& base, __half* mqkv,
