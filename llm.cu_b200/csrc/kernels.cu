@@ -297,11 +297,17 @@ __global__ void qknorm_rope_fwd_vec_kernel(const __half* __restrict__ qkv, int l
   const bool live = hh < nhead;
   const bool isq = hh < nh;
   const int d = (lane % C::kLph) * 8;
-  float x0[8] = {}, x1[8] = {};
+  const int pos = m % S;
+  float x0[8] = {}, x1[8] = {}, c[8] = {}, sn[8] = {}, w0[8] = {}, w1[8] = {};
   const int col = isq ? hh * HD : nh * HD + (hh - nh) * HD;
-  if (live) {
+  if (live) {  // every load of the lane in flight together (the tables do not wait for the norm)
+    const float* gw = isq ? qn_w : kn_w;
     ld8h(qkv + static_cast<size_t>(m) * ld + col + d, x0);
     ld8h(qkv + static_cast<size_t>(m) * ld + col + d + C::kHalf, x1);
+    ld8f(cos_t + pos * C::kHalf + d, c);
+    ld8f(sin_t + pos * C::kHalf + d, sn);
+    ld8f(gw + d, w0);
+    ld8f(gw + d + C::kHalf, w1);
   }
   float ss = 0.f;
 #pragma unroll
@@ -309,13 +315,7 @@ __global__ void qknorm_rope_fwd_vec_kernel(const __half* __restrict__ qkv, int l
   ss = group_sum<C::kLph>(ss);
   if (!live) return;
   const float r = rsqrtf(ss / static_cast<float>(HD) + eps);
-  const int pos = m % S;
-  const float* gw = isq ? qn_w : kn_w;
-  float c[8], sn[8], w0[8], w1[8], y0[8], y1[8];
-  ld8f(cos_t + pos * C::kHalf + d, c);
-  ld8f(sin_t + pos * C::kHalf + d, sn);
-  ld8f(gw + d, w0);
-  ld8f(gw + d + C::kHalf, w1);
+  float y0[8], y1[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const float a = x0[i] * r * w0[i];
