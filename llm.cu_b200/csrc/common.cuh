@@ -78,6 +78,7 @@ enum class Epi : int {
   kSwiGLUBwd = 4,
   kCEProbs = 5,  // lm_head forward: slot max / sum-exp partials + slot-relative probabilities
   kStoreF16Delta = 6,  // fp16 dO + the attention backward's per-(row, head) dO.O sums
+  kQKNormRope = 7,     // fp16 q/k/v + (head_dim 128) per-head RMSNorm and RoPE of q and k into rope_out
 };
 
 struct EpiArgs {
@@ -102,6 +103,17 @@ struct EpiArgs {
   int ld_gu = 0;
   __half* act = nullptr;      // [M, I]
   int ld_act = 0;
+  // kQKNormRope: q heads are columns [0, n_q_cols), k heads [n_q_cols,
+  // n_qk_cols); their normed, rotated copies go to rope_out (same columns,
+  // row stride ld_rope); cos/sin tables [seq, 64]
+  __half* rope_out = nullptr;
+  int ld_rope = 0;
+  const float* q_norm_w = nullptr;
+  const float* k_norm_w = nullptr;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+  int n_q_cols = 0, n_qk_cols = 0;
+  float eps = 0.f;
   // cross-entropy
   const int* targets = nullptr;
   float* part_max = nullptr;
@@ -127,7 +139,7 @@ cudaError_t rmsnorm_backward(const float* dy, const float* x, const float* w, fl
                              int H, float eps, int accumulate, cudaStream_t st);
 cudaError_t rmsnorm_backward(const __half* dy, const float* x, const float* w, float* dres, __half* dres16, int M,
                              int H, float eps, int accumulate, cudaStream_t st);
-cudaError_t qknorm_rope_forward(const __half* qkv, int ld_qkv, const float* qn_w, const float* kn_w,
+cudaError_t qknorm_rope_forward(const __half* qkv, int ld_qkv, const float* qn_w, const float* kn_w, int ld_out,
                                 const float* cos_t, const float* sin_t, __half* q_out, __half* k_out, int B, int S,
                                 int nh, int nkv, int hd, float eps, cudaStream_t st);
 cudaError_t qknorm_rope_backward(const float* dq, const float* dk, const __half* qkv, int ld_qkv, const float* qn_w,

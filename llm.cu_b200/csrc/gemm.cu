@@ -141,6 +141,14 @@ cudaError_t dispatch(Epi epi, const EpiArgs& ea, const CUtensorMap* maps, const 
       } else {
         return cudaErrorInvalidValue;
       }
+    case Epi::kQKNormRope:
+      if constexpr (BN == 256 && !BMN) {
+        EpiQKNormRope::Params p{ea.q_norm_w, ea.k_norm_w, ea.rope_cos, ea.rope_sin, ea.seq, ea.n_q_cols,
+                                ea.n_qk_cols, ea.eps};
+        return launch<BN, EpiQKNormRope, BMN, CG>(maps, sh, p, err, st);
+      } else {
+        return cudaErrorInvalidValue;
+      }
     case Epi::kCEProbs:
       if constexpr (BN == 256 && !BMN) {
         EpiCEProbs::Params p{ea.targets, ea.part_max, ea.part_sum, ea.tgt_logit, sh.tiles_n * (epi_warps<BN>() / 4)};
@@ -178,6 +186,15 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
   if (M <= 0 || N <= 0 || A.k <= 0 || A.k != B.k || A.mn) return cudaErrorInvalidValue;
   int BN = bn_hint;
   if (BN == 0) BN = (epi == Epi::kSwiGLU || epi == Epi::kSwiGLUBwd) ? 256 : (N <= 64 ? 64 : (N <= 128 ? 128 : 256));
+  if (epi == Epi::kQKNormRope) {
+    BN = 256;
+    // 128-wide heads that start on slice boundaries; tables [seq, 64]
+    if (!ea.rope_out || !ea.q_norm_w || !ea.k_norm_w || !ea.rope_cos || !ea.rope_sin || ea.seq <= 0 ||
+        ea.n_q_cols % 128 || ea.n_qk_cols % 128 || ea.n_qk_cols < ea.n_q_cols || ea.ld_rope % 8 ||
+        reinterpret_cast<uintptr_t>(ea.q_norm_w) % 16 || reinterpret_cast<uintptr_t>(ea.k_norm_w) % 16 ||
+        reinterpret_cast<uintptr_t>(ea.rope_cos) % 16 || reinterpret_cast<uintptr_t>(ea.rope_sin) % 16)
+      return cudaErrorInvalidValue;
+  }
   if (epi == Epi::kStoreF16Delta) {
     BN = 256;
     if (!ea.attn_o || !ea.delta || ea.seq <= 0 || (ea.head_dim != 64 && ea.head_dim != 128) || ea.ld_o % 8 ||
@@ -189,7 +206,9 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
   if (ea.ksplit > 1 && (epi != Epi::kStoreF32 || !ea.accumulate)) return cudaErrorInvalidValue;
   const int n_main = ea.n_main > 0 ? ea.n_main : N;
   if (n_main < N) {  // side output: only for the plain stores, from a tile boundary
-    if ((epi != Epi::kStoreF16 && epi != Epi::kStoreF16Delta && epi != Epi::kResidF32) || n_main % BN ||
+    if ((epi != Epi::kStoreF16 && epi != Epi::kStoreF16Delta && epi != Epi::kResidF32 &&
+         epi != Epi::kQKNormRope) ||
+        n_main % BN ||
         (N - n_main) % 8 || !ea.side ||
         ea.ld_side % 8 || reinterpret_cast<uintptr_t>(ea.side) % 16)
       return cudaErrorInvalidValue;
@@ -206,6 +225,10 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
     case Epi::kCEProbs:
       okc = make_io_map(&maps[2], ea.out, M, n_main, ea.ld_out, false);
       maps[3] = maps[2];
+      break;
+    case Epi::kQKNormRope:  // C = q/k/v [M, n_main], D = normed, rotated q/k [M, n_qk_cols]
+      okc = make_io_map(&maps[2], ea.out, M, n_main, ea.ld_out, false) &&
+            make_io_map(&maps[3], ea.rope_out, M, ea.n_qk_cols, ea.ld_rope, false);
       break;
     case Epi::kStoreF32:
       okc = make_io_map(&maps[2], ea.out, M, N, ea.ld_out, true);

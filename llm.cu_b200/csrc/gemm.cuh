@@ -304,6 +304,102 @@ struct EpiStoreF16Delta {
   __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
 };
 
+// q/k/v projection with Qwen3's per-head q/k RMSNorm and the rotary
+// embedding fused (head_dim 128: one warp's 128-column slice is one head of
+// its 32 rows).  Every main column leaves as fp16 through mapC (the raw
+// q/k/v the backward re-normalises); for q and k heads the warp then forms
+// the head's sum of squares from the fp32 accumulator, and writes
+// rot(x * rstd * gain) -- pairs (d, d + 64) rotated by the position's angle
+// (src/kernels/rope.cu:26-35 after src/kernels/lora_forward.cu:233-237) --
+// through mapD into the same columns of the rope output.  Side columns (h
+// of the LoRA rows) leave as fp16 like EpiStoreF16's.  Replaces the
+// separate QK-norm + RoPE pass over q and k.
+struct EpiQKNormRope {
+  struct Params {
+    const float* qw;     // q_norm gain [128]
+    const float* kw;     // k_norm gain [128]
+    const float* cos_t;  // [S, 64]
+    const float* sin_t;
+    int S, n_q_cols, n_qk_cols;
+    float eps;
+  };
+  struct State {};
+  static constexpr int kChunk = 128;
+  static constexpr int kSlab = 2 * kSlabBytes;  // both 64-column halves of the head at once
+  static constexpr bool kPaired = false;
+  static constexpr bool kStores = true;
+  static constexpr bool kTmemDirect = true;
+  __device__ static void begin(State&, const Params&, const EpiCtx&, int, int) {}
+  __device__ static bool tile(State&, const Params& p, EpiCtx& c, int col0, uint32_t taddr, int) {
+    if (col0 >= c.N) return true;
+    if (col0 >= c.n_main) {
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {
+        float v[32];
+        tmem_ld_32x32b_x32(taddr + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v));
+        tmem_ld_wait();
+        side_store(c, col0 + 32 * q, v, 32);
+      }
+      return true;
+    }
+    const bool qk = col0 < p.n_qk_cols;
+    // raw fp16 values (box hb = columns [64 hb, 64 hb + 64)) and the head's sum of squares
+    float ss = 0.f;
+    slab_wait_read(c);
+#pragma unroll 1
+    for (int q = 0; q < 4; ++q) {
+      float v[32];
+      tmem_ld_32x32b_x32(taddr + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v));
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) ss = fmaf(v[i], v[i], ss);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) slab_st(c, 4 * (q & 1) + j, pack8(v + 8 * j), q >> 1);
+    }
+    slab_store(c, c.mapC, col0, c.row0, 0);
+    slab_store(c, c.mapC, col0 + 64, c.row0, 1);
+    if (!qk) return true;
+    const float* gw = col0 < p.n_q_cols ? p.qw : p.kw;
+    const float r = rsqrtf(ss * (1.0f / 128.0f) + p.eps);
+    const int pos = (c.row < c.M ? c.row : 0) % p.S;
+    const float* cs = p.cos_t + static_cast<size_t>(pos) * 64;
+    const float* sn = p.sin_t + static_cast<size_t>(pos) * 64;
+    slab_wait_read(c);
+#pragma unroll 1
+    for (int d0 = 0; d0 < 64; d0 += 16) {
+      // pairs (d, d + 64), d = d0 .. d0 + 15: y0 -> box 0, y1 -> box 1
+      uint32_t a[16], b[16];
+      tmem_ld_32x32b_x16(taddr + d0, a);
+      tmem_ld_32x32b_x16(taddr + 64 + d0, b);
+      float cv[16], sv[16], wa[16], wb[16];
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        *reinterpret_cast<float4*>(cv + i) = *reinterpret_cast<const float4*>(cs + d0 + i);
+        *reinterpret_cast<float4*>(sv + i) = *reinterpret_cast<const float4*>(sn + d0 + i);
+        *reinterpret_cast<float4*>(wa + i) = __ldg(reinterpret_cast<const float4*>(gw + d0 + i));
+        *reinterpret_cast<float4*>(wb + i) = __ldg(reinterpret_cast<const float4*>(gw + 64 + d0 + i));
+      }
+      tmem_ld_wait();
+      uint32_t p0[8], p1[8];
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) {
+        const float xa0 = __uint_as_float(a[i]) * r * wa[i], xb0 = __uint_as_float(b[i]) * r * wb[i];
+        const float xa1 = __uint_as_float(a[i + 1]) * r * wa[i + 1], xb1 = __uint_as_float(b[i + 1]) * r * wb[i + 1];
+        p0[i / 2] = pack_half2(xa0 * cv[i] - xb0 * sv[i], xa1 * cv[i + 1] - xb1 * sv[i + 1]);
+        p1[i / 2] = pack_half2(xb0 * cv[i] + xa0 * sv[i], xb1 * cv[i + 1] + xa1 * sv[i + 1]);
+      }
+      slab_st(c, d0 / 8, make_uint4(p0[0], p0[1], p0[2], p0[3]), 0);
+      slab_st(c, d0 / 8 + 1, make_uint4(p0[4], p0[5], p0[6], p0[7]), 0);
+      slab_st(c, d0 / 8, make_uint4(p1[0], p1[1], p1[2], p1[3]), 1);
+      slab_st(c, d0 / 8 + 1, make_uint4(p1[4], p1[5], p1[6], p1[7]), 1);
+    }
+    slab_store(c, c.mapD, col0, c.row0, 0);
+    slab_store(c, c.mapD, col0 + 64, c.row0, 1);
+    return true;
+  }
+  __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
+};
+
 // C (fp32) = acc, or C += acc (TMA reduce-add) when accumulate != 0.
 struct EpiStoreF32 {
   struct Params { int accumulate; };

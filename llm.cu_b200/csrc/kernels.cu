@@ -283,7 +283,8 @@ template <int HD>
 __global__ void qknorm_rope_fwd_vec_kernel(const __half* __restrict__ qkv, int ld, const float* __restrict__ qn_w,
                                            const float* __restrict__ kn_w, const float* __restrict__ cos_t,
                                            const float* __restrict__ sin_t, __half* __restrict__ q_out,
-                                           __half* __restrict__ k_out, int M, int S, int nh, int nkv, float eps) {
+                                           __half* __restrict__ k_out, int ldo, int M, int S, int nh, int nkv,
+                                           float eps) {
   pdl_trigger();
   pdl_wait();
   using C = QkLanes<HD>;
@@ -323,8 +324,8 @@ __global__ void qknorm_rope_fwd_vec_kernel(const __half* __restrict__ qkv, int l
     y0[i] = a * c[i] - b * sn[i];
     y1[i] = b * c[i] + a * sn[i];
   }
-  __half* dst = isq ? q_out + static_cast<size_t>(m) * nh * HD + hh * HD
-                    : k_out + static_cast<size_t>(m) * nkv * HD + (hh - nh) * HD;
+  __half* dst = isq ? q_out + static_cast<size_t>(m) * ldo + hh * HD
+                    : k_out + static_cast<size_t>(m) * ldo + (hh - nh) * HD;
   st8h(dst + d, y0);
   st8h(dst + d + C::kHalf, y1);
 }
@@ -785,19 +786,19 @@ cudaError_t rope_tables(float* cos_t, float* sin_t, int S, int hd, float theta, 
   return cudaGetLastError();
 }
 
-cudaError_t qknorm_rope_forward(const __half* qkv, int ld_qkv, const float* qn_w, const float* kn_w,
+cudaError_t qknorm_rope_forward(const __half* qkv, int ld_qkv, const float* qn_w, const float* kn_w, int ld_out,
                                 const float* cos_t, const float* sin_t, __half* q_out, __half* k_out, int B, int S,
                                 int nh, int nkv, int hd, float eps, cudaStream_t st) {
   const int M = B * S;
-  if (ld_qkv % 8) return cudaErrorInvalidValue;
+  if (ld_qkv % 8 || ld_out % 8) return cudaErrorInvalidValue;
   if (hd == 128) {
     const int warps = M * ((nh + nkv + QkLanes<128>::kHpw - 1) / QkLanes<128>::kHpw);
     launch_pdl(qknorm_rope_fwd_vec_kernel<128>, (warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, 
-        qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, q_out, k_out, M, S, nh, nkv, eps);
+        qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, q_out, k_out, ld_out, M, S, nh, nkv, eps);
   } else if (hd == 64) {
     const int warps = M * ((nh + nkv + QkLanes<64>::kHpw - 1) / QkLanes<64>::kHpw);
     launch_pdl(qknorm_rope_fwd_vec_kernel<64>, (warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, 
-        qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, q_out, k_out, M, S, nh, nkv, eps);
+        qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, q_out, k_out, ld_out, M, S, nh, nkv, eps);
   } else {
     return cudaErrorInvalidValue;
   }

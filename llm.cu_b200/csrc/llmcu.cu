@@ -53,7 +53,7 @@ struct LayerW {
 
 struct LayerA {  // forward stash
   float *resid_mid;
-  __half *xn, *hq, *qkv, *qrope, *krope, *attn, *ho, *xn2, *gu, *act;
+  __half *xn, *hq, *qkv, *qkr, *attn, *ho, *xn2, *gu, *act;  // qkr: normed, rotated q | k [M, Q + KV]
   float* lse;
 };
 
@@ -287,8 +287,7 @@ void carve(llmcu_ctx* c, Carver& cv) {
     a.xn = cv.take<__half>(M * H);
     a.hq = cv.take<__half>(M * 64);
     a.qkv = cv.take<__half>(M * QKV);
-    a.qrope = cv.take<__half>(M * Q);
-    a.krope = cv.take<__half>(M * KV);
+    a.qkr = cv.take<__half>(M * (Q + KV));
     a.attn = cv.take<__half>(M * Q);
     a.ho = cv.take<__half>(M * 64);
     a.xn2 = cv.take<__half>(M * H);
@@ -448,19 +447,35 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     LayerA& a = ctx->la[l];
     const float* x = ctx->resid[l];
     TIMED(P_NORM, rmsnorm_forward(x, w.attn_norm, a.xn, M, H, eps, st));
-    {  // [q | k | v | h] = xn . mqkv^T
+    {  // [q | k | v | h] = xn . mqkv^T; q, k normed and rotated into qkr
       EpiArgs ea;
       ea.out = a.qkv;
       ea.ld_out = QKV;
       ea.n_main = QKV;
       ea.side = a.hq;
       ea.ld_side = 64;
-      TIMED(P_GEMM, gemm(op(a.xn, M, H, H), op(w.mqkv, QKV + 64, H, H + 64), M, QKV + 64, Epi::kStoreF16, ea, err, st));
+      if (ctx->hd == 128) {  // QK-norm + RoPE in the GEMM epilogue
+        ea.rope_out = a.qkr;
+        ea.ld_rope = Q + KV;
+        ea.q_norm_w = w.q_norm;
+        ea.k_norm_w = w.k_norm;
+        ea.rope_cos = ctx->rope_cos;
+        ea.rope_sin = ctx->rope_sin;
+        ea.seq = S;
+        ea.n_q_cols = Q;
+        ea.n_qk_cols = Q + KV;
+        ea.eps = eps;
+        TIMED(P_GEMM, gemm(op(a.xn, M, H, H), op(w.mqkv, QKV + 64, H, H + 64), M, QKV + 64, Epi::kQKNormRope, ea, err,
+                           st));
+      } else {
+        TIMED(P_GEMM, gemm(op(a.xn, M, H, H), op(w.mqkv, QKV + 64, H, H + 64), M, QKV + 64, Epi::kStoreF16, ea, err,
+                           st));
+        TIMED(P_NORM, qknorm_rope_forward(a.qkv, QKV, w.q_norm, w.k_norm, Q + KV, ctx->rope_cos, ctx->rope_sin, a.qkr,
+                                          a.qkr + Q, B, S, ctx->nh, ctx->nkv, ctx->hd, eps, st));
+      }
     }
-    TIMED(P_NORM, qknorm_rope_forward(a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, a.qrope, a.krope, B, S,
-                           ctx->nh, ctx->nkv, ctx->hd, eps, st));
-    TIMED(P_ATTN_FWD, attention_forward(a.qrope, a.krope, a.qkv + Q + KV, a.attn, a.lse, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV,
-                         QKV, Q, err, st));
+    TIMED(P_ATTN_FWD, attention_forward(a.qkr, a.qkr + Q, a.qkv + Q + KV, a.attn, a.lse, B, S, ctx->nh, ctx->nkv, ctx->hd,
+                                        Q + KV, Q + KV, QKV, Q, err, st));
     {  // [resid_mid | h_o] = [resid + attn . mo^T | attn . Ao^T]
       EpiArgs ea;
       ea.out = a.resid_mid;
@@ -562,9 +577,9 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     }
     // attention
     // (delta came with the O-projection dX GEMM)
-    TIMEDN(P_ATTN_BWD, 2, attention_backward_tc(a.qrope, a.krope, a.qkv + Q + KV, ctx->dattn, a.lse, ctx->delta, ctx->dq,
-                                            ctx->dk, ctx->dqkv + Q + KV, B, S, ctx->nh, ctx->nkv, ctx->hd, Q, KV, QKV, Q,
-                                            Q, KV, QKV, err, st));
+    TIMEDN(P_ATTN_BWD, 2, attention_backward_tc(a.qkr, a.qkr + Q, a.qkv + Q + KV, ctx->dattn, a.lse, ctx->delta, ctx->dq,
+                                            ctx->dk, ctx->dqkv + Q + KV, B, S, ctx->nh, ctx->nkv, ctx->hd, Q + KV, Q + KV,
+                                            QKV, Q, Q, KV, QKV, err, st));
     TIMED(P_NORM, qknorm_rope_backward(ctx->dq, ctx->dk, a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, ctx->dqkv,
                             B, S, ctx->nh, ctx->nkv, ctx->hd, eps, st));
     // QKV projection
