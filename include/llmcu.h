@@ -189,6 +189,17 @@ llmcu_status llmcu_save_lora(llmcu_ctx* ctx, const char* dir, int step);
 /* Reads the same files back (e.g. those written by save_lora.py --from-hf). */
 llmcu_status llmcu_load_lora(llmcu_ctx* ctx, const char* dir, int step);
 
+/* Optimizer sidecar for resuming (no reference counterpart: the reference
+ * saves A / B only, src/train.cu:146-170): dir/lora_step{step}_adamw.bin holds
+ * a 64-byte header ("LLMCUADW", version 1, step, layers, rank, hidden, q and
+ * kv dims, parameter count) and the AdamW first and second moments, fp32, in
+ * the flat adapter layout.  Together with llmcu_save_lora's A / B files of the
+ * same step, llmcu_load_lora + llmcu_load_adamw_state restore the training
+ * state; the next llmcu_train_step then takes step + 1.  Loading checks every
+ * header field against the context (LLMCU_ERR_INVALID_ARG on a mismatch). */
+llmcu_status llmcu_save_adamw_state(llmcu_ctx* ctx, const char* dir, int step);
+llmcu_status llmcu_load_adamw_state(llmcu_ctx* ctx, const char* dir, int step);
+
 /* --------------------------------------------------------------- INT8 */
 
 /* Per-row symmetric quantiser, bit-exact with quantize_kernel

@@ -1141,6 +1141,86 @@ llmcu_status llmcu_load_lora(llmcu_ctx* ctx, const char* dir, int step) {
   return LLMCU_OK;
 }
 
+// ----------------------------------------------------- optimizer sidecar
+// dir/lora_step{N}_adamw.bin: a 64-byte header, then the AdamW first and
+// second moments of every adapter in the flat layout (per layer Aq Bq Ak Bk
+// Av Bv Ao Bo; A [r, in], B [out, r]), fp32.  The reference saves A and B
+// only (src/train.cu:146-170) and cannot resume; with this file and the
+// A / B files of the same step a run continues where it stopped.
+namespace {
+struct AdamwHeader {
+  char magic[8];  // "LLMCUADW"
+  int32_t version, step, n_layers, rank, hidden, q_dim, kv_dim, reserved;
+  int64_t n_params;
+  int64_t reserved2[2];
+};
+static_assert(sizeof(AdamwHeader) == 64, "sidecar header is 64 bytes");
+constexpr char kAdamwMagic[8] = {'L', 'L', 'M', 'C', 'U', 'A', 'D', 'W'};
+
+void adamw_path(char* path, size_t n, const char* dir, int step) {
+  snprintf(path, n, "%s/lora_step%d_adamw.bin", dir, step);
+}
+}  // namespace
+
+llmcu_status llmcu_save_adamw_state(llmcu_ctx* ctx, const char* dir, int step) {
+  if (!ctx || !dir || step < 0) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null argument or negative step");
+  const size_t n = static_cast<size_t>(ctx->n_lora);
+  std::vector<float> m(n), v(n);
+  CK(cudaMemcpyAsync(m.data(), ctx->lm, n * sizeof(float), cudaMemcpyDeviceToHost, ctx->st));
+  CK(cudaMemcpyAsync(v.data(), ctx->lv, n * sizeof(float), cudaMemcpyDeviceToHost, ctx->st));
+  CK(cudaStreamSynchronize(ctx->st));
+  AdamwHeader h{};
+  memcpy(h.magic, kAdamwMagic, 8);
+  h.version = 1;
+  h.step = step;
+  h.n_layers = ctx->L;
+  h.rank = ctx->ld.r;
+  h.hidden = ctx->H;
+  h.q_dim = ctx->Q;
+  h.kv_dim = ctx->KV;
+  h.n_params = ctx->n_lora;
+  char path[1024];
+  adamw_path(path, sizeof(path), dir, step);
+  FILE* f = fopen(path, "wb");
+  if (!f) return fail(ctx, LLMCU_ERR_IO, "cannot write %s", path);
+  const bool ok = fwrite(&h, sizeof(h), 1, f) == 1 && fwrite(m.data(), sizeof(float), n, f) == n &&
+                  fwrite(v.data(), sizeof(float), n, f) == n;
+  const bool closed = fclose(f) == 0;
+  if (!ok || !closed) return fail(ctx, LLMCU_ERR_IO, "short write %s", path);
+  return LLMCU_OK;
+}
+
+llmcu_status llmcu_load_adamw_state(llmcu_ctx* ctx, const char* dir, int step) {
+  if (!ctx || !dir || step < 0) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null argument or negative step");
+  char path[1024];
+  adamw_path(path, sizeof(path), dir, step);
+  FILE* f = fopen(path, "rb");
+  if (!f) return fail(ctx, LLMCU_ERR_IO, "cannot open %s", path);
+  AdamwHeader h{};
+  if (fread(&h, sizeof(h), 1, f) != 1 || memcmp(h.magic, kAdamwMagic, 8) != 0 || h.version != 1) {
+    fclose(f);
+    return fail(ctx, LLMCU_ERR_IO, "%s is not an AdamW state file", path);
+  }
+  if (h.step != step || h.n_layers != ctx->L || h.rank != ctx->ld.r || h.hidden != ctx->H || h.q_dim != ctx->Q ||
+      h.kv_dim != ctx->KV || h.n_params != ctx->n_lora) {
+    fclose(f);
+    return fail(ctx, LLMCU_ERR_INVALID_ARG,
+                "%s holds step %d, %d layers, rank %d, dims %d/%d/%d (%lld params); this context has %d layers, "
+                "rank %d, dims %d/%d/%d (%lld params)",
+                path, h.step, h.n_layers, h.rank, h.hidden, h.q_dim, h.kv_dim, static_cast<long long>(h.n_params),
+                ctx->L, ctx->ld.r, ctx->H, ctx->Q, ctx->KV, static_cast<long long>(ctx->n_lora));
+  }
+  const size_t n = static_cast<size_t>(ctx->n_lora);
+  std::vector<float> m(n), v(n);
+  const bool ok = fread(m.data(), sizeof(float), n, f) == n && fread(v.data(), sizeof(float), n, f) == n;
+  fclose(f);
+  if (!ok) return fail(ctx, LLMCU_ERR_IO, "short read %s", path);
+  CK(cudaMemcpyAsync(ctx->lm, m.data(), n * sizeof(float), cudaMemcpyHostToDevice, ctx->st));
+  CK(cudaMemcpyAsync(ctx->lv, v.data(), n * sizeof(float), cudaMemcpyHostToDevice, ctx->st));
+  CK(cudaStreamSynchronize(ctx->st));
+  return LLMCU_OK;
+}
+
 // ------------------------------------------------------------------- INT8
 
 llmcu_status llmcu_quantize_int8_rows(const float* w, int rows, int cols, int8_t* q, float* scale, void* stream) {

@@ -11,7 +11,9 @@
 //
 // Additions: --batch B (sequences per step and GPU), --config tiny|1.7b,
 // --synthetic (device-generated N(0,0.02) base and adapters, uniform tokens),
-// --int8 (INT8 per-row base), --weights DIR, --data FILE, --out DIR, --seed.
+// --int8 (INT8 per-row base), --weights DIR, --data FILE, --out DIR, --seed,
+// --resume N (continue after step N from the adapter and AdamW files in --out;
+// every save also writes the AdamW sidecar lora_step{N}_adamw.bin).
 // Data parallel: when WORLD_SIZE > 1 (e.g. under torchrun) each process
 // drives GPU LOCAL_RANK, rank 0 writes the NCCL id to --dp-id-file and the
 // others read it; rank r takes sequences r, r+W, ... of every step window.
@@ -46,7 +48,7 @@ void die(llmcu_ctx* ctx, llmcu_status s, const char* what) {
 
 int main(int argc, char** argv) {
   float lr = 3e-4f;
-  int steps = 1000, seq_len = 512, save_every = 100, log_every = 10, batch = 1;
+  int steps = 1000, seq_len = 512, save_every = 100, log_every = 10, batch = 1, resume = 0;
   const float beta1 = 0.9f, beta2 = 0.999f, eps_adam = 1e-8f, wd = 0.01f;
   std::string config = "1.7b", weights = "weights", data = "data/train_tokens.bin", out = "weights";
   std::string id_file = "/tmp/llmcu_nccl_id";
@@ -71,12 +73,13 @@ int main(int argc, char** argv) {
     else if ((v = next("--out"))) out = v;
     else if ((v = next("--seed"))) seed = strtoull(v, nullptr, 10);
     else if ((v = next("--dp-id-file"))) id_file = v;
+    else if ((v = next("--resume"))) resume = atoi(v);
     else if (!strcmp(argv[i], "--synthetic")) synthetic = true;
     else if (!strcmp(argv[i], "--int8")) int8 = true;
     else if (!strcmp(argv[i], "--help") || !strcmp(argv[i], "-h")) {
       printf("usage: llm_train [--lr F] [--steps N] [--seq-len S] [--save-every N] [--log-every N]\n"
              "                 [--batch B] [--config tiny|1.7b] [--synthetic] [--int8] [--weights DIR]\n"
-             "                 [--data FILE] [--out DIR] [--seed N] [--dp-id-file PATH]\n");
+             "                 [--data FILE] [--out DIR] [--seed N] [--dp-id-file PATH] [--resume N]\n");
       return 0;
     }
   }
@@ -164,6 +167,11 @@ int main(int argc, char** argv) {
   }
   // adapters as BASELINE configs: A ~ U(+-1/sqrt(in)), B ~ N(0, 0.01); identical on every rank
   if ((s = llmcu_init_lora_synthetic(ctx, seed + 1, 0.01f)) != LLMCU_OK) die(ctx, s, "llmcu_init_lora_synthetic");
+  if (resume > 0) {  // adapters and AdamW moments of step `resume` from --out; continue at resume + 1
+    if ((s = llmcu_load_lora(ctx, out.c_str(), resume)) != LLMCU_OK) die(ctx, s, "llmcu_load_lora");
+    if ((s = llmcu_load_adamw_state(ctx, out.c_str(), resume)) != LLMCU_OK) die(ctx, s, "llmcu_load_adamw_state");
+    if (rank == 0) printf("Resumed from step %d (%s)\n", resume, out.c_str());
+  }
   if (rank == 0)
     printf("LoRA adapters initialized (rank=%d, alpha=%.0f, scale=%.1f, %lld params)\n", lc.rank, lc.alpha,
            lc.alpha / lc.rank, static_cast<long long>(llmcu_lora_param_count(ctx)));
@@ -171,12 +179,14 @@ int main(int argc, char** argv) {
   const int M = batch * seq_len;
   std::vector<int32_t> tok(M), tgt(M);
   std::mt19937_64 rng(seed * 31 + rank);
+  // the synthetic stream draws seq_len + 1 ids per sequence: skip the steps already taken
+  if (synthetic && resume > 0) rng.discard(static_cast<unsigned long long>(resume) * batch * (seq_len + 1));
   const llmcu_adamw_cfg opt = {lr, beta1, beta2, eps_adam, wd};
   if (rank == 0) printf("\n=== Training ===\n");
   float running = 0.f;
   int count = 0;
   auto t_log = std::chrono::steady_clock::now();
-  for (int step = 1; step <= steps; ++step) {
+  for (int step = resume + 1; step <= steps; ++step) {
     for (int b = 0; b < batch; ++b) {
       if (synthetic) {
         for (int i = 0; i < seq_len; ++i) {
@@ -211,11 +221,13 @@ int main(int argc, char** argv) {
     }
     if (step % save_every == 0 && rank == 0) {
       if ((s = llmcu_save_lora(ctx, out.c_str(), step)) != LLMCU_OK) die(ctx, s, "llmcu_save_lora");
+      if ((s = llmcu_save_adamw_state(ctx, out.c_str(), step)) != LLMCU_OK) die(ctx, s, "llmcu_save_adamw_state");
       printf("Saved LoRA weights at step %d\n", step);
     }
   }
   if (rank == 0) {
     if ((s = llmcu_save_lora(ctx, out.c_str(), steps)) != LLMCU_OK) die(ctx, s, "llmcu_save_lora");
+    if ((s = llmcu_save_adamw_state(ctx, out.c_str(), steps)) != LLMCU_OK) die(ctx, s, "llmcu_save_adamw_state");
     printf("Saved LoRA weights at step %d\n\nTraining complete.\n", steps);
   }
   llmcu_ctx_destroy(ctx);

@@ -132,6 +132,8 @@ _SIGS = {
     "llmcu_adamw": (C.c_int, [C.c_void_p, C.POINTER(_AdamWCfg), C.c_int]),
     "llmcu_save_lora": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),
     "llmcu_load_lora": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),
+    "llmcu_save_adamw_state": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),
+    "llmcu_load_adamw_state": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),
     "llmcu_quantize_int8_rows": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "llmcu_dp_get_unique_id": (C.c_int, [C.c_void_p]),
     "llmcu_dp_init": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
@@ -345,6 +347,13 @@ class Context:
 
     def load_lora(self, directory: str, step: int):
         self._check(lib().llmcu_load_lora(self._h, directory.encode(), step), "load_lora")
+
+    def save_adamw_state(self, directory: str, step: int):
+        """AdamW moments of every adapter to directory/lora_step{step}_adamw.bin."""
+        self._check(lib().llmcu_save_adamw_state(self._h, directory.encode(), step), "save_adamw_state")
+
+    def load_adamw_state(self, directory: str, step: int):
+        self._check(lib().llmcu_load_adamw_state(self._h, directory.encode(), step), "load_adamw_state")
 
     # -- profiling
     def profile_enable(self, on: bool = True):
