@@ -203,6 +203,55 @@ def run_reference(args, workload):
     return 0
 
 
+def run_decode(args):
+    """`--decode N`: greedy KV-cache decoding of N tokens after a 128-token
+    prompt on one GPU (llmcu_generate: batched prefill, then one CUDA-graph
+    replay per token), Qwen3-1.7B shape, synthetic fp16 (or --int8) base.  Its
+    own JSON line; not the training benchmark."""
+    import torch
+    torch.cuda.set_device(0)
+    m = load_binding()
+    model = m.Model.qwen3_1p7b(n_layers=args.layers)
+    n_prompt, n_new = 128, args.decode
+    base = m.BASE_INT8 if args.int8 else m.BASE_FP16
+    ctx = m.Context(model, m.Lora(16, 32.0), m.Run(1, n_prompt + n_new, base), device=0)
+    ctx.init_base_synthetic(seed=1, std=0.02)
+    ctx.init_lora_synthetic(seed=2, b_std=0.01)
+    prompt, _ = make_tokens(model.vocab, 1, n_prompt, 7, "zipf")
+    ctx.generate(prompt[0], 8)  # warm-up: captures the decode graph
+    runs = []
+    for _ in range(max(1, args.steps)):
+        _, _, ms = ctx.generate(prompt[0], n_new)
+        runs.append(ms)
+    ms = float(np.median(runs))
+    # bytes every decoded token must read: all linear weights once (merged
+    # q/k/v/o in fp16; MLP and lm_head fp16 or INT8 rows + scales) and the cache
+    H, Q, KV, I, V, L = model.hidden, model.n_heads * model.head_dim, model.n_kv_heads * model.head_dim, \
+        model.ffn, model.vocab, model.n_layers
+    attn = (Q + 2 * KV) * H + H * Q
+    mlp_el = 3 * I * H
+    wbytes = L * (2 * attn + mlp_el * (1 if args.int8 else 2)) + V * H * (1 if args.int8 else 2)
+    if args.int8:
+        wbytes += L * (2 * I + H) * 4 + V * 4  # row scales
+    avg_ctx = n_prompt + n_new / 2
+    kv_bytes = L * 2 * avg_ctx * KV * 2
+    bpt = wbytes + kv_bytes
+    pk = peaks()
+    achieved = bpt / (ms / 1e3) / 1e9
+    line = {"metric": "greedy decode tokens/s, batch 1, Qwen3-1.7B shape", "value": round(1e3 / ms, 2),
+            "unit": "tokens/s", "n_gpus": 1, "ms_per_token": round(ms, 4), "higher_is_better": True,
+            "dtype": "int8 MLP/lm_head rows, fp16 q/k/v/o" if args.int8 else "f16",
+            "data": "synthetic (device-generated base, seeded Zipf prompt)",
+            "config": {"workload": "decode", "prompt": n_prompt, "new_tokens": n_new, "layers": L,
+                       "base": "int8" if args.int8 else "fp16"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / pk["hbm_gbs"], 4), "bytes_per_token": int(bpt),
+                         "peak_src": pk.get("src", "MEASURED_PEAKS.json")},
+            "published_reference": "llm_engine 26.4 tok/s fp16, 33.8 tok/s int8 (RTX A5000, its README)"}
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -213,7 +262,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=28,
                     help="fewer layers for small ncu captures only; the benchmark line uses 28")
+    ap.add_argument("--decode", type=int, default=0,
+                    help="instead of the training step: greedy decode of N tokens after a 128-token prompt")
+    ap.add_argument("--int8", action="store_true", help="with --decode: INT8 base")
     args = ap.parse_args()
+    if args.decode:
+        return run_decode(args)
     if args.impl == "reference":
         return run_reference(args, args.workload)
 

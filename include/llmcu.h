@@ -189,6 +189,20 @@ llmcu_status llmcu_save_lora(llmcu_ctx* ctx, const char* dir, int step);
 /* Reads the same files back (e.g. those written by save_lora.py --from-hf). */
 llmcu_status llmcu_load_lora(llmcu_ctx* ctx, const char* dir, int step);
 
+/* Greedy generation with a KV cache (llm_engine --generate, src/main.cu:340-385,
+ * on the training context's weights and current adapters): the prompt (one
+ * sequence of n_prompt host ids) runs through the batched forward and fills the
+ * cache, then n_new tokens are chosen by argmax (the lowest id on ties).  The
+ * decode steps replay one CUDA graph per token.  n_prompt + n_new <= max_seq.
+ * out_tokens[n_new] receives every chosen id; *n_out (nullable) the count
+ * before Qwen3's end ids 151643 / 151645 (as llm_engine stops there; n_new
+ * when the vocabulary has no such ids).  step_logits (nullable, host
+ * [n_new, vocab] fp32): the logits each token was chosen from (then the steps
+ * run without the graph).  decode_ms (nullable): device time per decoded token
+ * after the first. */
+llmcu_status llmcu_generate(llmcu_ctx* ctx, const int32_t* prompt, int n_prompt, int n_new,
+                            int32_t* out_tokens, int* n_out, float* step_logits, float* decode_ms);
+
 /* Optimizer sidecar for resuming (no reference counterpart: the reference
  * saves A / B only, src/train.cu:146-170): dir/lora_step{step}_adamw.bin holds
  * a 64-byte header ("LLMCUADW", version 1, step, layers, rank, hidden, q and

@@ -130,6 +130,21 @@ int gemm_num_sms();
 // box 64 columns x box_rows rows.
 bool encode_tma_2d_f16(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, int box_rows);
 
+// ---- decode.cu (single-sequence KV-cache decoding; the position is read from
+// counters[0] on the device so a decode step can be replayed as a CUDA graph)
+int decode_attn_splits(int max_ctx);
+cudaError_t decode_gemv(const void* W, const float* scale, bool int8, int ldw, const __half* x, int N, int K,
+                        const float* resid, float* out32, __half* out16, cudaStream_t st);
+cudaError_t decode_qk_rope(const __half* qkv, const float* qn_w, const float* kn_w, const float* cos_t,
+                           const float* sin_t, const int* d_pos, __half* q_out, __half* k_cache, __half* v_cache,
+                           int nh, int nkv, int hd, float eps, cudaStream_t st);
+cudaError_t decode_attention(const __half* q, const __half* k_cache, const __half* v_cache, const int* d_pos,
+                             float* part, __half* out, int nh, int nkv, int hd, int max_ctx, cudaStream_t st);
+cudaError_t decode_swiglu(const __half* gu, __half* act, int I, cudaStream_t st);
+// counters: [0] position of the next input token, [1] tokens chosen so far, [2] the next input token
+cudaError_t decode_argmax(const float* logits, int V, int* counters, int* tokens, float* step_logits,
+                          cudaStream_t st);
+
 // ---- kernels.cu
 cudaError_t embed_forward(const int* tokens, const __half* E, float* out, int M, int H, int V, int* err,
                           cudaStream_t st);

@@ -42,7 +42,7 @@ __global__ void embed_kernel(const int* __restrict__ tok, const __half* __restri
   const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
-  int t = tok[m];
+  int t = __ldcg(tok + m);  // decode feeds ids written by the previous kernel chain
   if (t < 0 || t >= V) {
     if (lane == 0) atomicOr(err, kErrTokenRange);
     t = 0;

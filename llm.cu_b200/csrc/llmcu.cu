@@ -108,6 +108,14 @@ struct llmcu_ctx {
   float* stage = nullptr;      // fp32 staging for host uploads
   size_t stage_elems = 0;
   int last_n_valid = 0;
+  // decoding (llmcu_generate): K / V cache [L][max_seq][KV] (roped k, v), one
+  // position's vectors, split-attention partials, counters and chosen tokens
+  __half *kc = nullptr, *vc = nullptr;
+  float *dec_x = nullptr, *dec_xmid = nullptr, *dec_logits = nullptr, *dec_part = nullptr;
+  __half *dec_xn = nullptr, *dec_qkv = nullptr, *dec_q = nullptr, *dec_attn = nullptr, *dec_gu = nullptr,
+         *dec_act = nullptr;
+  int *dec_cnt = nullptr, *dec_tok = nullptr;
+  cudaGraphExec_t dec_graph = nullptr;  // one decode step, captured on first use
 
   // per-kernel-class timing (llmcu_profile_enable)
   bool prof_on = false;
@@ -325,6 +333,21 @@ void carve(llmcu_ctx* c, Carver& cv) {
   c->rope_sin = cv.take<float>(static_cast<size_t>(c->rc.max_seq) * (c->hd / 2));
   c->stage_elems = std::max({V * H, 2 * I * H, QKV * H});
   c->stage = cv.take<float>(c->stage_elems);
+  const size_t ctxlen = static_cast<size_t>(c->rc.max_seq);
+  c->kc = cv.take<__half>(L * ctxlen * KV);
+  c->vc = cv.take<__half>(L * ctxlen * KV);
+  c->dec_x = cv.take<float>(H);
+  c->dec_xmid = cv.take<float>(H);
+  c->dec_logits = cv.take<float>(V);
+  c->dec_part = cv.take<float>(static_cast<size_t>(c->nh) * decode_attn_splits(c->rc.max_seq) * (c->hd + 2));
+  c->dec_xn = cv.take<__half>(H);
+  c->dec_qkv = cv.take<__half>(QKV);
+  c->dec_q = cv.take<__half>(Q);
+  c->dec_attn = cv.take<__half>(Q);
+  c->dec_gu = cv.take<__half>(2 * I);
+  c->dec_act = cv.take<__half>(I);
+  c->dec_cnt = cv.take<int>(4);
+  c->dec_tok = cv.take<int>(ctxlen);
 }
 
 llmcu_status check_dev_err(llmcu_ctx* ctx) {
@@ -412,32 +435,16 @@ const __half* base_weight(llmcu_ctx* c, const __half* w16, const int8_t* q, cons
 Operand op_mn(const __half* p, int k_rows, int n_cols, int ld) { return Operand{p, n_cols, k_rows, ld, true}; }
 
 // ----------------------------------------------------------------- step
-llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
+// Embedding and every layer's forward over ctx->tok ([B, S] ids on the device),
+// leaving each layer's stash and ctx->resid[L] (the pre-final-norm hidden).
+// Expects the merged q/k/v/o weights of the current adapters.
+llmcu_status forward_layers(llmcu_ctx* ctx, int B, int S) {
   const int M = B * S;
   const int H = ctx->H, Q = ctx->Q, KV = ctx->KV, QKV = ctx->QKV, I = ctx->I, V = ctx->V;
   const float eps = ctx->m.rms_eps;
   cudaStream_t st = ctx->st;
   int* err = ctx->derr;
-  const LoraDims& d = ctx->ld;
-  const int r = ctx->lc.rank;
-  const int n_valid_local = ctx->rc.loss_all_positions ? M : B * (S - 1);
-  const double n_valid_total = static_cast<double>(n_valid_local) * ctx->world;
-  ctx->last_n_valid = n_valid_local;
-  const float unscale = static_cast<float>(1.0 / (kGradScale * n_valid_total));
   cudaError_t e = cudaSuccess;
-
-  // gradients accumulate (lora_grad adds each split's share); this first
-  // kernel follows the host's token upload, so it is launched normally and the
-  // rest of the step's kernels chain by programmatic dependent launch
-  struct PdlScope {
-    ~PdlScope() { set_pdl(false); }
-  } pdl_scope;
-  set_pdl(false);
-  TIMED(P_FILL, fill_f32(ctx->lg, ctx->n_lora, 0.f, st));
-  set_pdl(true);
-  // merged q/k/v/o weights of this step's adapters, every layer
-  TIMEDN(P_LORA_PREP, 3, lora_merge(ctx->lp, d, ctx->L, ctx->mw, ctx->lw[0].mqkv, ctx->lw[0].mo, st));
-  TIMED(P_CE, ce_valid_rows(ctx->valid, ctx->tgt, B, S, ctx->rc.loss_all_positions, V, err, st));
   const __half* E = ctx->E;
   TIMED(P_EMBED, embed_forward(ctx->tok, E, ctx->resid[0], M, H, V, err, st));
 
@@ -507,6 +514,38 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       TIMED(P_GEMM, gemm(op(a.act, M, I, I), op(wd, H, I, I), M, H, Epi::kResidF32, ea, err, st));
     }
   }
+
+  return LLMCU_OK;
+}
+
+llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
+  const int M = B * S;
+  const int H = ctx->H, Q = ctx->Q, KV = ctx->KV, QKV = ctx->QKV, I = ctx->I, V = ctx->V;
+  const float eps = ctx->m.rms_eps;
+  cudaStream_t st = ctx->st;
+  int* err = ctx->derr;
+  const LoraDims& d = ctx->ld;
+  const int r = ctx->lc.rank;
+  const int n_valid_local = ctx->rc.loss_all_positions ? M : B * (S - 1);
+  const double n_valid_total = static_cast<double>(n_valid_local) * ctx->world;
+  ctx->last_n_valid = n_valid_local;
+  const float unscale = static_cast<float>(1.0 / (kGradScale * n_valid_total));
+  cudaError_t e = cudaSuccess;
+
+  // gradients accumulate (lora_grad adds each split's share); this first
+  // kernel follows the host's token upload, so it is launched normally and the
+  // rest of the step's kernels chain by programmatic dependent launch
+  struct PdlScope {
+    ~PdlScope() { set_pdl(false); }
+  } pdl_scope;
+  set_pdl(false);
+  TIMED(P_FILL, fill_f32(ctx->lg, ctx->n_lora, 0.f, st));
+  set_pdl(true);
+  // merged q/k/v/o weights of this step's adapters, every layer
+  TIMEDN(P_LORA_PREP, 3, lora_merge(ctx->lp, d, ctx->L, ctx->mw, ctx->lw[0].mqkv, ctx->lw[0].mo, st));
+  TIMED(P_CE, ce_valid_rows(ctx->valid, ctx->tgt, B, S, ctx->rc.loss_all_positions, V, err, st));
+  CKS(forward_layers(ctx, B, S));
+  const __half* E = ctx->E;
 
   // ------------------------------------------------------- lm_head + CE
   float* xfinal = ctx->resid[ctx->L];
@@ -771,6 +810,7 @@ void llmcu_ctx_destroy(llmcu_ctx* ctx) {
     if (ev) cudaEventDestroy(ev);
   if (ctx->ev_comm_done) cudaEventDestroy(ctx->ev_comm_done);
   if (ctx->ev_step_done) cudaEventDestroy(ctx->ev_step_done);
+  if (ctx->dec_graph) cudaGraphExecDestroy(ctx->dec_graph);
   if (ctx->arena) cudaFree(ctx->arena);
   if (ctx->st) cudaStreamDestroy(ctx->st);
   if (ctx->comm) cudaStreamDestroy(ctx->comm);
@@ -1137,6 +1177,160 @@ llmcu_status llmcu_load_lora(llmcu_ctx* ctx, const char* dir, int step) {
       }
       CKS(llmcu_set_lora(ctx, l, p, A.data(), B.data()));
     }
+  }
+  return LLMCU_OK;
+}
+
+// ------------------------------------------------------------- generation
+namespace {
+
+// One decode step (llm_engine's transformer_decode, src/kernels/forward.cu:340-394)
+// for the token dec_cnt[2] at position dec_cnt[0], both read on the device:
+// GEMVs over the merged q/k/v/o weights and the base MLP / lm_head rows (INT8
+// rows with their scales for an INT8 base), the cache append inside the
+// QK-norm/RoPE kernel, split attention over the cache and the argmax that
+// chooses the next token.
+llmcu_status decode_step(llmcu_ctx* ctx, float* step_logits) {
+  const int H = ctx->H, Q = ctx->Q, KV = ctx->KV, QKV = ctx->QKV, I = ctx->I, V = ctx->V;
+  const float eps = ctx->m.rms_eps;
+  cudaStream_t st = ctx->st;
+  const bool int8 = ctx->rc.base_dtype == LLMCU_BASE_INT8;
+  const size_t ctxlen = static_cast<size_t>(ctx->rc.max_seq);
+  CK(embed_forward(ctx->dec_cnt + 2, ctx->E, ctx->dec_x, 1, H, V, ctx->derr, st));
+  for (int l = 0; l < ctx->L; ++l) {
+    LayerW& w = ctx->lw[l];
+    __half* kc = ctx->kc + l * ctxlen * KV;
+    __half* vc = ctx->vc + l * ctxlen * KV;
+    CK(rmsnorm_forward(ctx->dec_x, w.attn_norm, ctx->dec_xn, 1, H, eps, st));
+    CK(decode_gemv(w.mqkv, nullptr, false, H + 64, ctx->dec_xn, QKV, H, nullptr, nullptr, ctx->dec_qkv, st));
+    CK(decode_qk_rope(ctx->dec_qkv, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, ctx->dec_cnt, ctx->dec_q, kc,
+                      vc, ctx->nh, ctx->nkv, ctx->hd, eps, st));
+    CK(decode_attention(ctx->dec_q, kc, vc, ctx->dec_cnt, ctx->dec_part, ctx->dec_attn, ctx->nh, ctx->nkv, ctx->hd,
+                        ctx->rc.max_seq, st));
+    CK(decode_gemv(w.mo, nullptr, false, Q + 64, ctx->dec_attn, H, Q, ctx->dec_x, ctx->dec_xmid, nullptr, st));
+    CK(rmsnorm_forward(ctx->dec_xmid, w.ffn_norm, ctx->dec_xn, 1, H, eps, st));
+    if (int8)
+      CK(decode_gemv(w.q_gu, w.s_gu, true, H, ctx->dec_xn, 2 * I, H, nullptr, nullptr, ctx->dec_gu, st));
+    else
+      CK(decode_gemv(w.wgu, nullptr, false, H, ctx->dec_xn, 2 * I, H, nullptr, nullptr, ctx->dec_gu, st));
+    CK(decode_swiglu(ctx->dec_gu, ctx->dec_act, I, st));
+    if (int8)
+      CK(decode_gemv(w.q_d, w.s_d, true, I, ctx->dec_act, H, I, ctx->dec_xmid, ctx->dec_x, nullptr, st));
+    else
+      CK(decode_gemv(w.wd, nullptr, false, I, ctx->dec_act, H, I, ctx->dec_xmid, ctx->dec_x, nullptr, st));
+  }
+  CK(rmsnorm_forward(ctx->dec_x, ctx->final_norm, ctx->dec_xn, 1, H, eps, st));
+  if (int8)
+    CK(decode_gemv(ctx->qE, ctx->sE, true, H, ctx->dec_xn, V, H, nullptr, ctx->dec_logits, nullptr, st));
+  else
+    CK(decode_gemv(ctx->E, nullptr, false, H, ctx->dec_xn, V, H, nullptr, ctx->dec_logits, nullptr, st));
+  CK(decode_argmax(ctx->dec_logits, V, ctx->dec_cnt, ctx->dec_tok, step_logits, st));
+  return LLMCU_OK;
+}
+
+// The decode step as a CUDA graph (its kernels read the position on the
+// device, so one capture serves every token of every generate call).
+llmcu_status decode_graph(llmcu_ctx* ctx) {
+  if (ctx->dec_graph) return LLMCU_OK;
+  CK(cudaStreamBeginCapture(ctx->st, cudaStreamCaptureModeThreadLocal));
+  const llmcu_status s = decode_step(ctx, nullptr);
+  cudaGraph_t g = nullptr;
+  const cudaError_t e = cudaStreamEndCapture(ctx->st, &g);
+  if (s != LLMCU_OK) {
+    if (g) cudaGraphDestroy(g);
+    return s;
+  }
+  CK(e);
+  const cudaError_t ei = cudaGraphInstantiate(&ctx->dec_graph, g, 0);
+  cudaGraphDestroy(g);
+  CK(ei);
+  return LLMCU_OK;
+}
+
+constexpr int kQwenEos[2] = {151643, 151645};  // the ids llm_engine stops at (src/main.cu:368)
+
+}  // namespace
+
+llmcu_status llmcu_generate(llmcu_ctx* ctx, const int32_t* prompt, int n_prompt, int n_new, int32_t* out_tokens,
+                            int* n_out, float* step_logits, float* decode_ms) {
+  if (!ctx || !prompt || !out_tokens || n_prompt < 1 || n_new < 1)
+    return fail(ctx, LLMCU_ERR_INVALID_ARG, "generate: null pointer or empty prompt / request");
+  if (n_prompt + n_new > ctx->rc.max_seq)
+    return fail(ctx, LLMCU_ERR_INVALID_ARG, "generate: %d prompt + %d new tokens exceed max_seq %d", n_prompt, n_new,
+                ctx->rc.max_seq);
+  CK(cudaSetDevice(ctx->device));
+  const int H = ctx->H, Q = ctx->Q, KV = ctx->KV, QKV = ctx->QKV, V = ctx->V, L = ctx->L;
+  const size_t ctxlen = static_cast<size_t>(ctx->rc.max_seq);
+  cudaStream_t st = ctx->st;
+  const float eps = ctx->m.rms_eps;
+  CK(cudaMemcpyAsync(ctx->tok, prompt, sizeof(int32_t) * n_prompt, cudaMemcpyHostToDevice, st));
+  float* dlog = nullptr;  // logits history, only when the caller asks for it
+  if (step_logits) CK(cudaMalloc(&dlog, sizeof(float) * static_cast<size_t>(n_new) * V));
+  struct Cleanup {
+    float* p;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    ~Cleanup() {
+      set_pdl(false);
+      if (p) cudaFree(p);
+      if (e0) cudaEventDestroy(e0);
+      if (e1) cudaEventDestroy(e1);
+    }
+  } cleanup{dlog};
+  CK(cudaEventCreate(&cleanup.e0));
+  CK(cudaEventCreate(&cleanup.e1));
+  // merged weights of the current adapters, then the prompt through the batched forward
+  set_pdl(false);
+  CK(lora_merge(ctx->lp, ctx->ld, L, ctx->mw, ctx->lw[0].mqkv, ctx->lw[0].mo, st));
+  set_pdl(true);
+  CKS(forward_layers(ctx, 1, n_prompt));
+  set_pdl(false);
+  for (int l = 0; l < L; ++l) {  // cache rows 0 .. n_prompt - 1: rotated k, raw v
+    const LayerA& a = ctx->la[l];
+    CK(cudaMemcpy2DAsync(ctx->kc + l * ctxlen * KV, sizeof(__half) * KV, a.qkr + Q, sizeof(__half) * (Q + KV),
+                         sizeof(__half) * KV, n_prompt, cudaMemcpyDeviceToDevice, st));
+    CK(cudaMemcpy2DAsync(ctx->vc + l * ctxlen * KV, sizeof(__half) * KV, a.qkv + Q + KV, sizeof(__half) * QKV,
+                         sizeof(__half) * KV, n_prompt, cudaMemcpyDeviceToDevice, st));
+  }
+  const int init[4] = {n_prompt - 1, 0, 0, 0};  // the argmax advances the position to n_prompt
+  CK(cudaMemcpyAsync(ctx->dec_cnt, init, sizeof(init), cudaMemcpyHostToDevice, st));
+  // first token: final norm + lm_head of the prompt's last position
+  CK(rmsnorm_forward(ctx->resid[L] + static_cast<size_t>(n_prompt - 1) * H, ctx->final_norm, ctx->dec_xn, 1, H, eps,
+                     st));
+  if (ctx->rc.base_dtype == LLMCU_BASE_INT8)
+    CK(decode_gemv(ctx->qE, ctx->sE, true, H, ctx->dec_xn, V, H, nullptr, ctx->dec_logits, nullptr, st));
+  else
+    CK(decode_gemv(ctx->E, nullptr, false, H, ctx->dec_xn, V, H, nullptr, ctx->dec_logits, nullptr, st));
+  CK(decode_argmax(ctx->dec_logits, V, ctx->dec_cnt, ctx->dec_tok, dlog, st));
+  if (!dlog && n_new > 1) CKS(decode_graph(ctx));
+  CK(cudaEventRecord(cleanup.e0, st));
+  set_pdl(true);
+  for (int t = 1; t < n_new; ++t) {
+    if (dlog)
+      CKS(decode_step(ctx, dlog));
+    else
+      CK(cudaGraphLaunch(ctx->dec_graph, st));
+  }
+  set_pdl(false);
+  CK(cudaEventRecord(cleanup.e1, st));
+  CK(cudaEventSynchronize(cleanup.e1));
+  CKS(check_dev_err(ctx));
+  std::vector<int32_t> toks(n_new);
+  CK(cudaMemcpy(toks.data(), ctx->dec_tok, sizeof(int32_t) * n_new, cudaMemcpyDeviceToHost));
+  int n = n_new;
+  if (V > kQwenEos[1])
+    for (int i = 0; i < n_new; ++i)
+      if (toks[i] == kQwenEos[0] || toks[i] == kQwenEos[1]) {
+        n = i;
+        break;
+      }
+  memcpy(out_tokens, toks.data(), sizeof(int32_t) * n_new);
+  if (n_out) *n_out = n;
+  if (step_logits) CK(cudaMemcpy(step_logits, dlog, sizeof(float) * static_cast<size_t>(n_new) * V,
+                                 cudaMemcpyDeviceToHost));
+  if (decode_ms) {
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, cleanup.e0, cleanup.e1));
+    *decode_ms = n_new > 1 ? ms / static_cast<float>(n_new - 1) : 0.f;
   }
   return LLMCU_OK;
 }

@@ -133,6 +133,8 @@ _SIGS = {
     "llmcu_save_lora": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),
     "llmcu_load_lora": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),
     "llmcu_save_adamw_state": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),
+    "llmcu_generate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_int),
+                                 C.c_void_p, C.POINTER(C.c_float)]),
     "llmcu_load_adamw_state": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),
     "llmcu_quantize_int8_rows": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "llmcu_dp_get_unique_id": (C.c_int, [C.c_void_p]),
@@ -347,6 +349,18 @@ class Context:
 
     def load_lora(self, directory: str, step: int):
         self._check(lib().llmcu_load_lora(self._h, directory.encode(), step), "load_lora")
+
+    def generate(self, prompt, n_new: int, want_logits: bool = False):
+        """Greedy continuation of one prompt: (tokens [n], logits [n_new, V] or None,
+        decode ms per token).  n excludes Qwen3's end ids and what follows."""
+        p = np.ascontiguousarray(np.asarray(prompt, dtype=np.int32).reshape(-1))
+        toks = np.zeros(n_new, dtype=np.int32)
+        n_out = C.c_int(0)
+        ms = C.c_float(0.0)
+        logits = np.zeros((n_new, self.model.vocab), dtype=np.float32) if want_logits else None
+        self._check(lib().llmcu_generate(self._h, _ptr(p), p.size, n_new, _ptr(toks), C.byref(n_out),
+                                         _ptr(logits) if want_logits else None, C.byref(ms)), "generate")
+        return toks[: n_out.value], logits, float(ms.value)
 
     def save_adamw_state(self, directory: str, step: int):
         """AdamW moments of every adapter to directory/lora_step{step}_adamw.bin."""

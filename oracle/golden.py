@@ -295,6 +295,68 @@ def causal_gqa_attention(q, k, v, scale):
 # one step
 # ----------------------------------------------------------------------------
 
+def _layers(cfg: ModelCfg, W: Dict[str, torch.Tensor], lora_add, tokens: np.ndarray, cos, sin,
+            ref_bugs: bool = False):
+    """Embedding and every layer (src/kernels/lora_forward.cu:194-304): the
+    pre-final-norm hidden [B, S, H] and the last layer's post-attention hidden."""
+    B, S = tokens.shape
+    H, hd, nq, nkv = cfg.hidden, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
+    eps = cfg.rms_eps
+    x = W["embed"][torch.from_numpy(tokens.astype(np.int64))]   # [B,S,H]
+    post_attn_last = None
+    for l in range(cfg.n_layers):
+        p = f"L{l}."
+        xn = rmsnorm(x, W[p + "attn_norm"], eps)
+        q = xn @ W[p + "wq"].t() + lora_add(xn, p + "wq")
+        k = xn @ W[p + "wk"].t() + lora_add(xn, p + "wk")
+        v = xn @ W[p + "wv"].t() + lora_add(xn, p + "wv")
+        q = rmsnorm(q.view(B, S, nq, hd), W[p + "q_norm"], eps)
+        k = rmsnorm(k.view(B, S, nkv, hd), W[p + "k_norm"], eps)
+        q = apply_rope(q, cos, sin)
+        k = apply_rope(k, cos, sin)
+        o = causal_gqa_attention(q, k, v.view(B, S, nkv, hd), 1.0 / math.sqrt(hd))
+        o = o.reshape(B, S, nq * hd)
+        x = x + o @ W[p + "wo"].t() + lora_add(o, p + "wo")
+        post_attn_last = x
+        xn2 = rmsnorm(x, W[p + "ffn_norm"], eps)
+        g = xn2 @ W[p + "w_gate"].t()
+        u = xn2 @ W[p + "w_up"].t()
+        act = _SwiGLURefBug.apply(g, u) if ref_bugs else torch.nn.functional.silu(g) * u
+        x = x + act @ W[p + "w_down"].t()
+    return x, post_attn_last
+
+
+def forward_logits(cfg: ModelCfg, base: Dict[str, np.ndarray], lora: Dict[str, np.ndarray],
+                   tokens: np.ndarray) -> np.ndarray:
+    """Logits [B, S, V] of the forward (fp32, no gradient) -- what the
+    reference's inference path computes position by position
+    (src/kernels/forward.cu:340-394)."""
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    W = {k: T(v) for k, v in base.items()}
+    A = {k: T(v) for k, v in lora.items()}
+    s_lora = cfg.lora_scale
+    lora_add = lambda x, name: ((x @ A[name + ".A"].t()) @ A[name + ".B"].t()) * s_lora
+    cos, sin = rope_tables(cfg, tokens.shape[1])
+    with torch.no_grad():
+        x, _ = _layers(cfg, W, lora_add, tokens, cos, sin)
+        return (rmsnorm(x, W["final_norm"], cfg.rms_eps) @ W["embed"].t()).numpy()
+
+
+def generate_greedy(cfg: ModelCfg, base, lora, prompt: np.ndarray, n_new: int):
+    """Greedy continuation (first maximum on ties, as llm_engine's host loop,
+    src/main.cu:362-366): (tokens [n_new], logits [n_new, V]), each step
+    re-running the forward over the whole prefix."""
+    seq = [int(t) for t in np.asarray(prompt).reshape(-1)]
+    toks, logits = [], []
+    for _ in range(n_new):
+        lg = forward_logits(cfg, base, lora, np.array([seq], dtype=np.int32))[0, -1]
+        t = int(np.argmax(lg))
+        toks.append(t)
+        logits.append(lg)
+        seq.append(t)
+    return np.array(toks, dtype=np.int32), np.stack(logits)
+
+
 @dataclasses.dataclass
 class StepResult:
     loss: float
@@ -329,28 +391,8 @@ def forward_backward(cfg: ModelCfg, base: Dict[str, np.ndarray], lora: Dict[str,
         h = _LoraDownRefBug.apply(x, A) if ref_bugs else x @ A.t()
         return (h @ Bm.t()) * s_lora
 
-    x = E[torch.from_numpy(tokens.astype(np.int64))]          # [B,S,H]
-    post_attn_last = None
     with torch.enable_grad():
-        for l in range(cfg.n_layers):
-            p = f"L{l}."
-            xn = rmsnorm(x, W[p + "attn_norm"], eps)
-            q = xn @ W[p + "wq"].t() + lora_add(xn, p + "wq")
-            k = xn @ W[p + "wk"].t() + lora_add(xn, p + "wk")
-            v = xn @ W[p + "wv"].t() + lora_add(xn, p + "wv")
-            q = rmsnorm(q.view(B, S, nq, hd), W[p + "q_norm"], eps)
-            k = rmsnorm(k.view(B, S, nkv, hd), W[p + "k_norm"], eps)
-            q = apply_rope(q, cos, sin)
-            k = apply_rope(k, cos, sin)
-            o = causal_gqa_attention(q, k, v.view(B, S, nkv, hd), 1.0 / math.sqrt(hd))
-            o = o.reshape(B, S, nq * hd)
-            x = x + o @ W[p + "wo"].t() + lora_add(o, p + "wo")
-            post_attn_last = x
-            xn2 = rmsnorm(x, W[p + "ffn_norm"], eps)
-            g = xn2 @ W[p + "w_gate"].t()
-            u = xn2 @ W[p + "w_up"].t()
-            act = _SwiGLURefBug.apply(g, u) if ref_bugs else torch.nn.functional.silu(g) * u
-            x = x + act @ W[p + "w_down"].t()
+        x, post_attn_last = _layers(cfg, W, lora_add, tokens, cos, sin, ref_bugs)
         if ref_bugs:
             xf = _FinalNormRefBug.apply(x, post_attn_last.detach(), W["final_norm"], eps)
         else:
