@@ -133,16 +133,22 @@ bool encode_tma_2d_f16(CUtensorMap* map, const void* ptr, int rows, int cols, in
 // ---- decode.cu (single-sequence KV-cache decoding; the position is read from
 // counters[0] on the device so a decode step can be replayed as a CUDA graph)
 int decode_attn_splits(int max_ctx);
-cudaError_t decode_gemv(const void* W, const float* scale, bool int8, int ldw, const __half* x, int N, int K,
-                        const float* resid, float* out32, __half* out16, cudaStream_t st);
-cudaError_t decode_qk_rope(const __half* qkv, const float* qn_w, const float* kn_w, const float* cos_t,
-                           const float* sin_t, const int* d_pos, __half* q_out, __half* k_cache, __half* v_cache,
-                           int nh, int nkv, int hd, float eps, cudaStream_t st);
-cudaError_t decode_attention(const __half* q, const __half* k_cache, const __half* v_cache, const int* d_pos,
-                             float* part, __half* out, int nh, int nkv, int hd, int max_ctx, cudaStream_t st);
-cudaError_t decode_swiglu(const __half* gu, __half* act, int I, cudaStream_t st);
-// counters: [0] position of the next input token, [1] tokens chosen so far, [2] the next input token
-cudaError_t decode_argmax(const float* logits, int V, int* counters, int* tokens, float* step_logits,
+// x: xmode 0 = fp16 [K]; 1 = fp32 row [K] RMSNorm'd with `gain` / eps on the
+// way in; 2 = fp16 gate/up row [2K] (128-row interleave), SwiGLU on the way in
+cudaError_t decode_gemv(const void* W, const float* scale, bool int8, int ldw, const void* x, int xmode,
+                        const float* gain, float eps, int N, int K, const float* resid, float* out32, __half* out16,
+                        cudaStream_t st);
+// raw q/k/v row -> QK-norm + RoPE, cache append at *d_pos, attention over
+// rows [0, *d_pos], fp16 output [nh, hd]; part: nh * decode_attn_splits(max_ctx)
+// * (hd + 2) floats; tickets: nh ints, zero between calls
+cudaError_t decode_attention(const __half* qkv, const float* qn_w, const float* kn_w, const float* cos_t,
+                             const float* sin_t, const int* d_pos, __half* k_cache, __half* v_cache, float* part,
+                             int* tickets, __half* out, int nh, int nkv, int hd, float eps, int max_ctx,
+                             cudaStream_t st);
+// counters: [0] position of the next input token, [1] tokens chosen so far, [2] the next input token,
+// [3] the argmax blocks' ticket (0 between steps); scratch: decode_argmax_scratch() floats
+int decode_argmax_scratch();
+cudaError_t decode_argmax(const float* logits, int V, int* counters, int* tokens, float* step_logits, float* scratch,
                           cudaStream_t st);
 
 // ---- kernels.cu

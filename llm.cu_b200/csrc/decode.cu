@@ -4,10 +4,10 @@
 //   * GEMV for every projection, fp16 rows or INT8 rows with per-row scales
 //     (one warp per output row, 16-byte coalesced row reads, the input vector
 //     staged once per block in shared memory; optional residual add);
-//   * QK-norm + RoPE of one position, writing K and V into the cache;
-//   * attention of one query over the cache, split over key ranges (each
-//     split a partial max / sum / output, then one combine per head);
-//   * SwiGLU of one row (gate/up interleaved in 128-row groups, as stored);
+//   * one kernel from the raw q/k/v row to the attention output: QK-norm +
+//     RoPE of the position, the K / V cache append, attention split over key
+//     ranges (partial max / sum / output each) and the merge of the splits;
+//   * the RMSNorms and the SwiGLU folded into the GEMVs' input staging;
 //   * greedy argmax (lowest id on ties, as the reference's host loop).
 // The position being decoded lives in device memory (`d_pos`) and every
 // kernel reads it there, so one decode step is captured once into a CUDA
@@ -20,19 +20,91 @@ namespace {
 
 constexpr int kGemvThreads = 256;  // 8 warps; a warp owns one output row at a time
 
+// How a GEMV forms its fp16 input vector in shared memory:
+enum : int {
+  kXHalf = 0,    // x is the fp16 vector itself
+  kXNorm = 1,    // x is an fp32 row: RMSNorm with gain g (each block forms the row's rstd)
+  kXSwiGLU = 2,  // x is the fp16 gate/up row [2K], interleaved in 128-row groups: silu(g) * u
+};
+
 // y[n] = s[n] * sum_k W[n, k] x[k] for W fp16 (s = 1) or INT8 [N, K] (row
-// stride ldw); x fp16 [K].  out32 (nullable) = resid[n] (nullable: 0) + y;
-// out16 (nullable) = fp16(y).
-template <bool kInt8>
+// stride ldw), x as kX says.  out32 (nullable) = resid[n] (nullable: 0) + y;
+// out16 (nullable) = fp16(y).  The fused input forms repeat the separate
+// kernels' arithmetic (rmsnorm_fwd_row_kernel, the SwiGLU of one row), so a
+// norm or activation costs no launch of its own.
+template <bool kInt8, int kX>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const void* __restrict__ W, const float* __restrict__ scale,
-                                                            int ldw, const __half* __restrict__ x, int N, int K,
+                                                            int ldw, const void* __restrict__ xin,
+                                                            const float* __restrict__ gain, float eps, int N, int K,
                                                             const float* __restrict__ resid, float* __restrict__ out32,
                                                             __half* __restrict__ out16) {
   pdl_trigger();
   extern __shared__ __align__(16) __half gv_x[];
+  __shared__ float gv_red[kGemvThreads / 32];
   pdl_wait();
-  for (int i = threadIdx.x * 8; i < K; i += blockDim.x * 8)
-    *reinterpret_cast<uint4*>(gv_x + i) = *reinterpret_cast<const uint4*>(x + i);
+  if constexpr (kX == kXHalf) {
+    const __half* x = static_cast<const __half*>(xin);
+    for (int i = threadIdx.x * 8; i < K; i += blockDim.x * 8)
+      *reinterpret_cast<uint4*>(gv_x + i) = *reinterpret_cast<const uint4*>(x + i);
+  } else if constexpr (kX == kXNorm) {
+    // the thread's share of x and the gain, all loads issued before any use
+    // (K <= 4 * 4 * blockDim.x: at most four float4 per thread)
+    const float* x = static_cast<const float*>(xin);
+    float4 v[4], g[4];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = (threadIdx.x + j * blockDim.x) * 4;
+      v[j] = i < K ? *reinterpret_cast<const float4*>(x + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      g[j] = i < K ? *reinterpret_cast<const float4*>(gain + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) gv_red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    ss = 0.f;
+#pragma unroll
+    for (int w = 0; w < kGemvThreads / 32; ++w) ss += gv_red[w];
+    const float r = rsqrtf(ss / static_cast<float>(K) + eps);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = (threadIdx.x + j * blockDim.x) * 4;
+      if (i < K) {
+        uint2 u;
+        u.x = pack_half2(v[j].x * r * g[j].x, v[j].y * r * g[j].y);
+        u.y = pack_half2(v[j].z * r * g[j].z, v[j].w * r * g[j].w);
+        *reinterpret_cast<uint2*>(gv_x + i) = u;
+      }
+    }
+  } else {
+    // eight activations per chunk from 16-byte gate and up loads, every
+    // chunk's loads issued first (K <= 4 * 8 * blockDim.x)
+    const __half* gu = static_cast<const __half*>(xin);
+    uint4 gq[4], uq[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = (threadIdx.x + j * blockDim.x) * 8;
+      const int grp = i >> 7, jj = i & 127;
+      gq[j] = i < K ? *reinterpret_cast<const uint4*>(gu + grp * 256 + jj) : make_uint4(0u, 0u, 0u, 0u);
+      uq[j] = i < K ? *reinterpret_cast<const uint4*>(gu + grp * 256 + 128 + jj) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = (threadIdx.x + j * blockDim.x) * 8;
+      if (i < K) {
+        const __half2* hg = reinterpret_cast<const __half2*>(&gq[j]);
+        const __half2* hu = reinterpret_cast<const __half2*>(&uq[j]);
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 fg = __half22float2(hg[e]), fu = __half22float2(hu[e]);
+          o[e] = pack_half2(fg.x / (1.0f + __expf(-fg.x)) * fu.x, fg.y / (1.0f + __expf(-fg.y)) * fu.y);
+        }
+        *reinterpret_cast<uint4*>(gv_x + i) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int warps = gridDim.x * (blockDim.x >> 5);
@@ -82,32 +154,14 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const void* __restri
   }
 }
 
-// One warp per head of [q heads | k heads | v heads] of the position *d_pos:
-// q and k get the per-head RMSNorm (gain q_norm / k_norm) and the rotation of
-// pairs (d, d + hd/2) -- the arithmetic of qknorm_rope_fwd_vec_kernel -- q
-// into q_out, k into the K cache row; v is copied into the V cache row.
+// Per-head RMSNorm (gain g) and rotation of pairs (d, d + HD/2) at position
+// pos for the warp's head row src -- the arithmetic of
+// qknorm_rope_fwd_vec_kernel -- rounded to fp16; lane holds pairs
+// d = lane + 32 p, in y0 (d) and y1 (d + HD/2).
 template <int HD>
-__global__ void decode_qk_rope_kernel(const __half* __restrict__ qkv, const float* __restrict__ qn_w,
-                                      const float* __restrict__ kn_w, const float* __restrict__ cos_t,
-                                      const float* __restrict__ sin_t, const int* __restrict__ d_pos,
-                                      __half* __restrict__ q_out, __half* __restrict__ k_cache,
-                                      __half* __restrict__ v_cache, int nh, int nkv, float eps) {
-  pdl_trigger();
-  pdl_wait();
-  constexpr int kHalf = HD / 2, kP = kHalf / 32;  // rotation pairs per lane
-  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (w >= nh + 2 * nkv) return;  // whole warp
-  const int pos = __ldcg(d_pos);  // written by the previous step's argmax: read through L2
-  if (w >= nh + nkv) {  // v head
-    const int vh = w - nh - nkv;
-    const __half* src = qkv + static_cast<size_t>(nh + nkv) * HD + vh * HD;
-    __half* dst = v_cache + static_cast<size_t>(pos) * nkv * HD + vh * HD;
-    for (int d = lane; d < HD; d += 32) dst[d] = src[d];
-    return;
-  }
-  const bool isq = w < nh;
-  const __half* src = qkv + static_cast<size_t>(w) * HD;  // q heads, then k heads
+__device__ __forceinline__ void rope_head(const __half* src, const float* g, const float* cos_t, const float* sin_t,
+                                          int pos, float eps, int lane, __half (&y0)[HD / 64], __half (&y1)[HD / 64]) {
+  constexpr int kHalf = HD / 2, kP = HD / 64;
   float a[kP], b[kP];
   float ss = 0.f;
 #pragma unroll
@@ -118,184 +172,222 @@ __global__ void decode_qk_rope_kernel(const __half* __restrict__ qkv, const floa
   }
   ss = warp_sum(ss);
   const float r = rsqrtf(ss / static_cast<float>(HD) + eps);
-  const float* gw = isq ? qn_w : kn_w;
-  __half* dst = isq ? q_out + static_cast<size_t>(w) * HD
-                    : k_cache + static_cast<size_t>(pos) * nkv * HD + (w - nh) * HD;
 #pragma unroll
   for (int p = 0; p < kP; ++p) {
     const int d = lane + 32 * p;
     const float c = cos_t[pos * kHalf + d], s = sin_t[pos * kHalf + d];
-    const float x = a[p] * r * gw[d], y = b[p] * r * gw[d + kHalf];
-    dst[d] = __float2half_rn(x * c - y * s);
-    dst[d + kHalf] = __float2half_rn(y * c + x * s);
+    const float x = a[p] * r * g[d], y = b[p] * r * g[d + kHalf];
+    y0[p] = __float2half_rn(x * c - y * s);
+    y1[p] = __float2half_rn(y * c + x * s);
   }
 }
 
-// Attention of the query heads over cache rows [0, *d_pos]: block (h, sp)
-// takes the kDecT keys [sp * kDecT, ...), stages their K and V rows in shared
-// memory with 16-byte loads (all in flight at once), and leaves its partial
-// output, max and sum (log2 domain) in part[h][sp] = {o[HD], m, l}.
+// Attention of one position over the cache, everything between the q/k/v
+// GEMV and the o-projection in one launch.  Block (h, sp) takes the kDecT
+// keys [sp * kDecT, ...) of the cache rows [0, pos] (pos = *d_pos):
+//   * warp 0 forms the head's q (QK-norm + RoPE) from the raw q/k/v row;
+//   * the block whose range holds pos forms that position's k (QK-norm +
+//     RoPE) and v, appends them to the cache (both query heads of a KV group
+//     write the same bytes) and uses them directly; older rows are staged
+//     from the cache with 16-byte loads through L2, all in flight at once;
+//   * scores, max, exp2 and the partial output {o[HD], m, l} (log2 domain)
+//     go to part[h][sp]; the last block of the head to finish (a ticket per
+//     head) merges the splits into the fp16 output row.
 constexpr int kDecT = 32;
 template <int HD>
-__global__ void __launch_bounds__(128) decode_attn_kernel(const __half* __restrict__ q,
-                                                          const __half* __restrict__ k_cache,
-                                                          const __half* __restrict__ v_cache,
-                                                          const int* __restrict__ d_pos, float* __restrict__ part,
-                                                          int nh, int nkv, float scale_log2) {
+__global__ void __launch_bounds__(128) decode_attn_kernel(const __half* __restrict__ qkv, const float* __restrict__ qn_w,
+                                                          const float* __restrict__ kn_w,
+                                                          const float* __restrict__ cos_t,
+                                                          const float* __restrict__ sin_t,
+                                                          const int* __restrict__ d_pos, __half* __restrict__ k_cache,
+                                                          __half* __restrict__ v_cache, float* __restrict__ part,
+                                                          int* __restrict__ tickets, __half* __restrict__ out, int nh,
+                                                          int nkv, float eps, float scale_log2) {
   pdl_trigger();
   __shared__ __align__(16) __half ks[kDecT][HD + 8];
   __shared__ __align__(16) __half vs[kDecT][HD + 8];
   __shared__ float qs[HD];
   __shared__ float ps[kDecT];
   __shared__ float stat[2];
+  __shared__ int last;
   pdl_wait();
+  constexpr int kHalf = HD / 2, kP = HD / 64;
   const int h = blockIdx.x, sp = blockIdx.y, splits = gridDim.y;
   const int kvh = h / (nh / nkv);
-  const int L = __ldcg(d_pos) + 1;
-  const int t0 = sp * kDecT;
-  float* dst = part + (static_cast<size_t>(h) * splits + sp) * (HD + 2);
-  if (t0 >= L) {  // whole block: no keys here
-    for (int d = threadIdx.x; d < HD; d += blockDim.x) dst[d] = 0.f;
-    if (threadIdx.x == 0) {
-      dst[HD] = -INFINITY;
-      dst[HD + 1] = 0.f;
-    }
-    return;
-  }
-  const int n = min(kDecT, L - t0);
-  const size_t kv_stride = static_cast<size_t>(nkv) * HD;
-  constexpr int kC = HD / 8;  // 16-byte chunks per row
-  for (int i = threadIdx.x; i < n * kC; i += blockDim.x) {
-    const int r = i / kC, c = i % kC;
-    const size_t off = static_cast<size_t>(t0 + r) * kv_stride + kvh * HD + c * 8;
-    *reinterpret_cast<uint4*>(&ks[r][c * 8]) = __ldg(reinterpret_cast<const uint4*>(k_cache + off));
-    *reinterpret_cast<uint4*>(&vs[r][c * 8]) = __ldg(reinterpret_cast<const uint4*>(v_cache + off));
-  }
-  for (int d = threadIdx.x; d < HD; d += blockDim.x) qs[d] = __half2float(q[static_cast<size_t>(h) * HD + d]) * scale_log2;
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos = __ldcg(d_pos);  // written by the previous step's argmax: read through L2
+  const int L = pos + 1;
+  const int t0 = sp * kDecT;
+  const size_t kv_stride = static_cast<size_t>(nkv) * HD;
+  float* dst = part + (static_cast<size_t>(h) * splits + sp) * (HD + 2);
+  if (t0 < L) {  // block-uniform
+    const int n = min(kDecT, L - t0);
+    const bool mine = pos < t0 + kDecT;  // this block holds the new row pos - t0
+    constexpr int kC = HD / 8;           // 16-byte chunks per row
+    for (int i = threadIdx.x; i < n * kC; i += blockDim.x) {
+      const int r = i / kC, c = i % kC;
+      if (t0 + r == pos) continue;
+      const size_t off = static_cast<size_t>(t0 + r) * kv_stride + kvh * HD + c * 8;
+      *reinterpret_cast<uint4*>(&ks[r][c * 8]) = __ldcg(reinterpret_cast<const uint4*>(k_cache + off));
+      *reinterpret_cast<uint4*>(&vs[r][c * 8]) = __ldcg(reinterpret_cast<const uint4*>(v_cache + off));
+    }
+    if (warp == 0) {
+      __half y0[kP], y1[kP];
+      rope_head<HD>(qkv + static_cast<size_t>(h) * HD, qn_w, cos_t, sin_t, pos, eps, lane, y0, y1);
 #pragma unroll
-  for (int j = 0; j < kDecT / 4; ++j) {  // warp w: keys 8w .. 8w + 7
-    const int r = warp * (kDecT / 4) + j;
-    if (r < n) {
-      float s = 0.f;
+      for (int p = 0; p < kP; ++p) {
+        qs[lane + 32 * p] = __half2float(y0[p]) * scale_log2;
+        qs[lane + 32 * p + kHalf] = __half2float(y1[p]) * scale_log2;
+      }
+    } else if (mine && warp == 1) {
+      __half y0[kP], y1[kP];
+      rope_head<HD>(qkv + static_cast<size_t>(nh + kvh) * HD, kn_w, cos_t, sin_t, pos, eps, lane, y0, y1);
+      __half* kc = k_cache + static_cast<size_t>(pos) * kv_stride + kvh * HD;
 #pragma unroll
-      for (int d = lane; d < HD; d += 32) s = fmaf(qs[d], __half2float(ks[r][d]), s);
-      s = warp_sum(s);
-      if (lane == 0) ps[r] = s;
+      for (int p = 0; p < kP; ++p) {
+        const int d = lane + 32 * p;
+        ks[pos - t0][d] = y0[p];
+        ks[pos - t0][d + kHalf] = y1[p];
+        kc[d] = y0[p];
+        kc[d + kHalf] = y1[p];
+      }
+    } else if (mine && warp == 2) {
+      const __half* src = qkv + static_cast<size_t>(nh + nkv + kvh) * HD;
+      __half* vc = v_cache + static_cast<size_t>(pos) * kv_stride + kvh * HD;
+      for (int d = lane; d < HD; d += 32) {
+        vs[pos - t0][d] = src[d];
+        vc[d] = src[d];
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kDecT / 4; ++j) {  // warp w: keys 8w .. 8w + 7
+      const int r = warp * (kDecT / 4) + j;
+      if (r < n) {
+        float sc = 0.f;
+#pragma unroll
+        for (int d = lane; d < HD; d += 32) sc = fmaf(qs[d], __half2float(ks[r][d]), sc);
+        sc = warp_sum(sc);
+        if (lane == 0) ps[r] = sc;
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const float v = lane < n ? ps[lane] : -INFINITY;
+      const float m = warp_max(v);
+      const float p = lane < n ? exp2f(v - m) : 0.f;
+      const float l = warp_sum(p);
+      if (lane < n) ps[lane] = p;
+      if (lane == 0) {
+        stat[0] = m;
+        stat[1] = l;
+      }
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+      float o = 0.f;
+      for (int r = 0; r < n; ++r) o = fmaf(ps[r], __half2float(vs[r][d]), o);
+      __stcg(dst + d, o);
+    }
+    if (threadIdx.x == 0) {
+      __stcg(dst + HD, stat[0]);
+      __stcg(dst + HD + 1, stat[1]);
+    }
+  } else {  // no keys here
+    for (int d = threadIdx.x; d < HD; d += blockDim.x) __stcg(dst + d, 0.f);
+    if (threadIdx.x == 0) {
+      __stcg(dst + HD, -INFINITY);
+      __stcg(dst + HD + 1, 0.f);
     }
   }
+  // the head's last block merges: out[h][d] = sum 2^(m - M) o[d] / sum 2^(m - M) l
+  __threadfence();
   __syncthreads();
-  if (warp == 0) {
-    const float v = lane < n ? ps[lane] : -INFINITY;
-    const float m = warp_max(v);
-    const float p = lane < n ? exp2f(v - m) : 0.f;
-    const float l = warp_sum(p);
-    if (lane < n) ps[lane] = p;
-    if (lane == 0) {
-      stat[0] = m;
-      stat[1] = l;
-    }
-  }
+  if (threadIdx.x == 0) last = atomicAdd(tickets + h, 1) == splits - 1;
   __syncthreads();
-  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-    float o = 0.f;
-    for (int r = 0; r < n; ++r) o = fmaf(ps[r], __half2float(vs[r][d]), o);
-    dst[d] = o;
-  }
-  if (threadIdx.x == 0) {
-    dst[HD] = stat[0];
-    dst[HD + 1] = stat[1];
-  }
-}
-
-// out[h][d] = sum_sp 2^(m_sp - M) o_sp[d] / sum_sp 2^(m_sp - M) l_sp (fp16)
-template <int HD>
-__global__ void decode_attn_combine_kernel(const float* __restrict__ part, __half* __restrict__ out, int splits) {
-  pdl_trigger();
-  pdl_wait();
-  const int h = blockIdx.x, d = threadIdx.x;
+  if (!last) return;
+  __threadfence();
   const float* ph = part + static_cast<size_t>(h) * splits * (HD + 2);
   float M = -INFINITY;
-  for (int sp = 0; sp < splits; ++sp) M = fmaxf(M, ph[sp * (HD + 2) + HD]);
-  float num = 0.f, den = 0.f;
-  for (int sp = 0; sp < splits; ++sp) {
-    const float m = ph[sp * (HD + 2) + HD];
-    if (m == -INFINITY) continue;
-    const float f = exp2f(m - M);
-    num = fmaf(f, ph[sp * (HD + 2) + d], num);
-    den = fmaf(f, ph[sp * (HD + 2) + HD + 1], den);
+  for (int s2 = 0; s2 < splits; ++s2) M = fmaxf(M, __ldcg(ph + s2 * (HD + 2) + HD));
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+    float num = 0.f, den = 0.f;
+    for (int s2 = 0; s2 < splits; ++s2) {
+      const float m = __ldcg(ph + s2 * (HD + 2) + HD);
+      if (m == -INFINITY) continue;
+      const float f = exp2f(m - M);
+      num = fmaf(f, __ldcg(ph + s2 * (HD + 2) + d), num);
+      den = fmaf(f, __ldcg(ph + s2 * (HD + 2) + HD + 1), den);
+    }
+    out[static_cast<size_t>(h) * HD + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
   }
-  out[static_cast<size_t>(h) * HD + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
+  if (threadIdx.x == 0) __stcg(tickets + h, 0);  // for the next step
 }
 
-// act[i] = silu(g) * u for the gate/up rows stored interleaved in 128-row
-// groups (row group j: gate rows j*128.., then the matching up rows)
-__global__ void decode_swiglu_kernel(const __half* __restrict__ gu, __half* __restrict__ act, int I) {
-  pdl_trigger();
-  pdl_wait();
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= I) return;
-  const int grp = i >> 7, j = i & 127;
-  const float g = __half2float(gu[grp * 256 + j]), u = __half2float(gu[grp * 256 + 128 + j]);
-  act[i] = __float2half_rn(g / (1.0f + __expf(-g)) * u);
+// (value, id) pair order of the greedy choice: larger value, then lower id
+__device__ __forceinline__ void amax_merge(float& best, int& idx, float v2, int i2) {
+  if (v2 > best || (v2 == best && i2 < idx)) {
+    best = v2;
+    idx = i2;
+  }
+}
+__device__ __forceinline__ void amax_warp(float& best, int& idx) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    amax_merge(best, idx, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, idx, o));
 }
 
 // Greedy choice over logits [V] (the first maximum, as the reference's host
-// loop): tokens[*d_step] = next = argmax; step_logits (nullable) row *d_step
-// receives the logits; then the step and the position advance.
-__global__ void __launch_bounds__(1024) decode_argmax_kernel(const float* __restrict__ logits, int V,
-                                                             int* __restrict__ counters, int* __restrict__ tokens,
-                                                             float* __restrict__ step_logits) {
+// loop), spread over kAmaxBlocks blocks: each leaves its chunk's best in
+// (pval, pidx); the last block to finish (a ticket in counters[3]) picks the
+// overall best: tokens[step] = next = argmax, then the step and the position
+// advance.  step_logits (nullable) row `step` receives the logits.
+constexpr int kAmaxBlocks = 128;
+__global__ void __launch_bounds__(256) decode_argmax_kernel(const float* __restrict__ logits, int V,
+                                                            int* __restrict__ counters, int* __restrict__ tokens,
+                                                            float* __restrict__ step_logits, float* __restrict__ pval,
+                                                            int* __restrict__ pidx) {
   pdl_trigger();
   pdl_wait();
-  __shared__ float bv[32];
-  __shared__ int bi[32];
+  __shared__ float bv[8];
+  __shared__ int bi[8];
+  __shared__ int last;
   const int step = __ldcg(counters + 1);  // the counters change every step: L2 only
   float best = -INFINITY;
   int idx = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) {
     const float v = logits[i];
-    if (v > best || (v == best && i < idx)) {
-      best = v;
-      idx = i;
-    }
+    amax_merge(best, idx, v, i);
     if (step_logits) step_logits[static_cast<size_t>(step) * V + i] = v;
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
-    const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (v2 > best || (v2 == best && i2 < idx)) {
-      best = v2;
-      idx = i2;
-    }
-  }
+  amax_warp(best, idx);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) {
     bv[warp] = best;
     bi[warp] = idx;
   }
   __syncthreads();
-  if (warp == 0) {
-    best = lane < (blockDim.x >> 5) ? bv[lane] : -INFINITY;
-    idx = lane < (blockDim.x >> 5) ? bi[lane] : 0x7fffffff;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
-      const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
-      if (v2 > best || (v2 == best && i2 < idx)) {
-        best = v2;
-        idx = i2;
-      }
-    }
-    if (lane == 0) {
-      if (idx == 0x7fffffff) idx = 0;  // every logit NaN
-      tokens[step] = idx;
-      __stcg(counters + 2, idx);  // the next step's input token
-      __stcg(counters + 1, step + 1);
-      __stcg(counters, __ldcg(counters) + 1);  // its position
-    }
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) amax_merge(best, idx, bv[w], bi[w]);
+    __stcg(pval + blockIdx.x, best);
+    __stcg(pidx + blockIdx.x, idx);
+    __threadfence();
+    last = atomicAdd(counters + 3, 1) == static_cast<int>(gridDim.x) - 1;
+  }
+  __syncthreads();
+  if (!last || warp != 0) return;
+  __threadfence();
+  best = -INFINITY;
+  idx = 0x7fffffff;
+  for (int b = lane; b < static_cast<int>(gridDim.x); b += 32) amax_merge(best, idx, __ldcg(pval + b), __ldcg(pidx + b));
+  amax_warp(best, idx);
+  if (lane == 0) {
+    if (idx == 0x7fffffff) idx = 0;  // every logit NaN
+    tokens[step] = idx;
+    __stcg(counters + 2, idx);  // the next step's input token
+    __stcg(counters + 1, step + 1);
+    __stcg(counters, __ldcg(counters) + 1);  // its position
+    __stcg(counters + 3, 0);                 // ticket for the next step
   }
 }
 
@@ -303,66 +395,59 @@ __global__ void __launch_bounds__(1024) decode_argmax_kernel(const float* __rest
 
 int decode_attn_splits(int max_ctx) { return max_ctx < 1 ? 1 : (max_ctx + kDecT - 1) / kDecT; }
 
-cudaError_t decode_gemv(const void* W, const float* scale, bool int8, int ldw, const __half* x, int N, int K,
-                        const float* resid, float* out32, __half* out16, cudaStream_t st) {
+cudaError_t decode_gemv(const void* W, const float* scale, bool int8, int ldw, const void* x, int xmode,
+                        const float* gain, float eps, int N, int K, const float* resid, float* out32, __half* out16,
+                        cudaStream_t st) {
   if (K % (int8 ? 16 : 8) || ldw % (int8 ? 16 : 8) || reinterpret_cast<uintptr_t>(W) % 16 ||
-      reinterpret_cast<uintptr_t>(x) % 16 || (int8 && !scale))
+      reinterpret_cast<uintptr_t>(x) % 16 || (int8 && !scale) || (xmode == kXNorm && !gain) ||
+      (xmode == kXSwiGLU && K % 128) || xmode < 0 || xmode > 2 ||
+      (xmode == kXNorm && (K > 16 * kGemvThreads || K % 4)) || (xmode == kXSwiGLU && K > 32 * kGemvThreads))
     return cudaErrorInvalidValue;
   const int rows_per_block = kGemvThreads / 32;
   int blocks = (N + rows_per_block - 1) / rows_per_block;
   const int cap = 8 * gemm_num_sms();
   if (blocks > cap) blocks = cap;
   const size_t smem = static_cast<size_t>(K) * sizeof(__half);
-  if (int8)
-    launch_pdl(gemv_kernel<true>, blocks, kGemvThreads, smem, st, W, scale, ldw, x, N, K, resid, out32, out16);
-  else
-    launch_pdl(gemv_kernel<false>, blocks, kGemvThreads, smem, st, W, scale, ldw, x, N, K, resid, out32, out16);
-  return cudaGetLastError();
-}
-
-cudaError_t decode_qk_rope(const __half* qkv, const float* qn_w, const float* kn_w, const float* cos_t,
-                           const float* sin_t, const int* d_pos, __half* q_out, __half* k_cache, __half* v_cache,
-                           int nh, int nkv, int hd, float eps, cudaStream_t st) {
-  const int warps = nh + 2 * nkv;
-  const int blocks = (warps + 3) / 4;
-  if (hd == 128)
-    launch_pdl(decode_qk_rope_kernel<128>, blocks, 128, 0, st, qkv, qn_w, kn_w, cos_t, sin_t, d_pos, q_out, k_cache,
-               v_cache, nh, nkv, eps);
-  else if (hd == 64)
-    launch_pdl(decode_qk_rope_kernel<64>, blocks, 128, 0, st, qkv, qn_w, kn_w, cos_t, sin_t, d_pos, q_out, k_cache,
-               v_cache, nh, nkv, eps);
-  else
-    return cudaErrorInvalidValue;
-  return cudaGetLastError();
-}
-
-cudaError_t decode_attention(const __half* q, const __half* k_cache, const __half* v_cache, const int* d_pos,
-                             float* part, __half* out, int nh, int nkv, int hd, int max_ctx, cudaStream_t st) {
-  if (nkv <= 0 || nh % nkv) return cudaErrorInvalidValue;
-  const int splits = decode_attn_splits(max_ctx);
-  const float scale_log2 = kLog2e / sqrtf(static_cast<float>(hd));
-  const dim3 grid(nh, splits);
-  if (hd == 128) {
-    launch_pdl(decode_attn_kernel<128>, grid, 128, 0, st, q, k_cache, v_cache, d_pos, part, nh, nkv, scale_log2);
-    launch_pdl(decode_attn_combine_kernel<128>, nh, 128, 0, st, part, out, splits);
-  } else if (hd == 64) {
-    launch_pdl(decode_attn_kernel<64>, grid, 128, 0, st, q, k_cache, v_cache, d_pos, part, nh, nkv, scale_log2);
-    launch_pdl(decode_attn_combine_kernel<64>, nh, 64, 0, st, part, out, splits);
+#define LLMCU_GEMV(I8, XM)                                                                                     \
+  launch_pdl(gemv_kernel<I8, XM>, blocks, kGemvThreads, smem, st, W, scale, ldw, x, gain, eps, N, K, resid, out32, \
+             out16)
+  if (int8) {
+    if (xmode == kXHalf) LLMCU_GEMV(true, kXHalf);
+    else if (xmode == kXNorm) LLMCU_GEMV(true, kXNorm);
+    else LLMCU_GEMV(true, kXSwiGLU);
   } else {
-    return cudaErrorInvalidValue;
+    if (xmode == kXHalf) LLMCU_GEMV(false, kXHalf);
+    else if (xmode == kXNorm) LLMCU_GEMV(false, kXNorm);
+    else LLMCU_GEMV(false, kXSwiGLU);
   }
+#undef LLMCU_GEMV
   return cudaGetLastError();
 }
 
-cudaError_t decode_swiglu(const __half* gu, __half* act, int I, cudaStream_t st) {
-  if (I % 128) return cudaErrorInvalidValue;
-  launch_pdl(decode_swiglu_kernel, (I + 255) / 256, 256, 0, st, gu, act, I);
+cudaError_t decode_attention(const __half* qkv, const float* qn_w, const float* kn_w, const float* cos_t,
+                             const float* sin_t, const int* d_pos, __half* k_cache, __half* v_cache, float* part,
+                             int* tickets, __half* out, int nh, int nkv, int hd, float eps, int max_ctx,
+                             cudaStream_t st) {
+  if (nkv <= 0 || nh % nkv) return cudaErrorInvalidValue;
+  const dim3 grid(nh, decode_attn_splits(max_ctx));
+  const float scale_log2 = kLog2e / sqrtf(static_cast<float>(hd));
+  if (hd == 128)
+    launch_pdl(decode_attn_kernel<128>, grid, 128, 0, st, qkv, qn_w, kn_w, cos_t, sin_t, d_pos, k_cache, v_cache,
+               part, tickets, out, nh, nkv, eps, scale_log2);
+  else if (hd == 64)
+    launch_pdl(decode_attn_kernel<64>, grid, 128, 0, st, qkv, qn_w, kn_w, cos_t, sin_t, d_pos, k_cache, v_cache, part,
+               tickets, out, nh, nkv, eps, scale_log2);
+  else
+    return cudaErrorInvalidValue;
   return cudaGetLastError();
 }
 
-cudaError_t decode_argmax(const float* logits, int V, int* counters, int* tokens, float* step_logits,
+int decode_argmax_scratch() { return 2 * kAmaxBlocks; }
+
+cudaError_t decode_argmax(const float* logits, int V, int* counters, int* tokens, float* step_logits, float* scratch,
                           cudaStream_t st) {
-  launch_pdl(decode_argmax_kernel, 1, 1024, 0, st, logits, V, counters, tokens, step_logits);
+  launch_pdl(decode_argmax_kernel, kAmaxBlocks, 256, 0, st, logits, V, counters, tokens, step_logits, scratch,
+             reinterpret_cast<int*>(scratch + kAmaxBlocks));
   return cudaGetLastError();
 }
 

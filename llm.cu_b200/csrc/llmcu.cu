@@ -111,10 +111,9 @@ struct llmcu_ctx {
   // decoding (llmcu_generate): K / V cache [L][max_seq][KV] (roped k, v), one
   // position's vectors, split-attention partials, counters and chosen tokens
   __half *kc = nullptr, *vc = nullptr;
-  float *dec_x = nullptr, *dec_xmid = nullptr, *dec_logits = nullptr, *dec_part = nullptr;
-  __half *dec_xn = nullptr, *dec_qkv = nullptr, *dec_q = nullptr, *dec_attn = nullptr, *dec_gu = nullptr,
-         *dec_act = nullptr;
-  int *dec_cnt = nullptr, *dec_tok = nullptr;
+  float *dec_x = nullptr, *dec_xmid = nullptr, *dec_logits = nullptr, *dec_part = nullptr, *dec_amax = nullptr;
+  __half *dec_qkv = nullptr, *dec_attn = nullptr, *dec_gu = nullptr;
+  int *dec_cnt = nullptr, *dec_tok = nullptr, *dec_tickets = nullptr;
   cudaGraphExec_t dec_graph = nullptr;  // one decode step, captured on first use
 
   // per-kernel-class timing (llmcu_profile_enable)
@@ -340,13 +339,12 @@ void carve(llmcu_ctx* c, Carver& cv) {
   c->dec_xmid = cv.take<float>(H);
   c->dec_logits = cv.take<float>(V);
   c->dec_part = cv.take<float>(static_cast<size_t>(c->nh) * decode_attn_splits(c->rc.max_seq) * (c->hd + 2));
-  c->dec_xn = cv.take<__half>(H);
   c->dec_qkv = cv.take<__half>(QKV);
-  c->dec_q = cv.take<__half>(Q);
   c->dec_attn = cv.take<__half>(Q);
   c->dec_gu = cv.take<__half>(2 * I);
-  c->dec_act = cv.take<__half>(I);
   c->dec_cnt = cv.take<int>(4);
+  c->dec_tickets = cv.take<int>(c->nh);
+  c->dec_amax = cv.take<float>(decode_argmax_scratch());
   c->dec_tok = cv.take<int>(ctxlen);
 }
 
@@ -1201,30 +1199,34 @@ llmcu_status decode_step(llmcu_ctx* ctx, float* step_logits) {
     LayerW& w = ctx->lw[l];
     __half* kc = ctx->kc + l * ctxlen * KV;
     __half* vc = ctx->vc + l * ctxlen * KV;
-    CK(rmsnorm_forward(ctx->dec_x, w.attn_norm, ctx->dec_xn, 1, H, eps, st));
-    CK(decode_gemv(w.mqkv, nullptr, false, H + 64, ctx->dec_xn, QKV, H, nullptr, nullptr, ctx->dec_qkv, st));
-    CK(decode_qk_rope(ctx->dec_qkv, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, ctx->dec_cnt, ctx->dec_q, kc,
-                      vc, ctx->nh, ctx->nkv, ctx->hd, eps, st));
-    CK(decode_attention(ctx->dec_q, kc, vc, ctx->dec_cnt, ctx->dec_part, ctx->dec_attn, ctx->nh, ctx->nkv, ctx->hd,
-                        ctx->rc.max_seq, st));
-    CK(decode_gemv(w.mo, nullptr, false, Q + 64, ctx->dec_attn, H, Q, ctx->dec_x, ctx->dec_xmid, nullptr, st));
-    CK(rmsnorm_forward(ctx->dec_xmid, w.ffn_norm, ctx->dec_xn, 1, H, eps, st));
+    CK(decode_gemv(w.mqkv, nullptr, false, H + 64, ctx->dec_x, 1, w.attn_norm, eps, QKV, H, nullptr, nullptr,
+                   ctx->dec_qkv, st));
+    CK(decode_attention(ctx->dec_qkv, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, ctx->dec_cnt, kc, vc,
+                        ctx->dec_part, ctx->dec_tickets, ctx->dec_attn, ctx->nh, ctx->nkv, ctx->hd, eps, ctx->rc.max_seq,
+                        st));
+    CK(decode_gemv(w.mo, nullptr, false, Q + 64, ctx->dec_attn, 0, nullptr, 0.f, H, Q, ctx->dec_x, ctx->dec_xmid,
+                   nullptr, st));
+    // ffn norm folded into the gate/up GEMV, SwiGLU into the down GEMV
     if (int8)
-      CK(decode_gemv(w.q_gu, w.s_gu, true, H, ctx->dec_xn, 2 * I, H, nullptr, nullptr, ctx->dec_gu, st));
+      CK(decode_gemv(w.q_gu, w.s_gu, true, H, ctx->dec_xmid, 1, w.ffn_norm, eps, 2 * I, H, nullptr, nullptr,
+                     ctx->dec_gu, st));
     else
-      CK(decode_gemv(w.wgu, nullptr, false, H, ctx->dec_xn, 2 * I, H, nullptr, nullptr, ctx->dec_gu, st));
-    CK(decode_swiglu(ctx->dec_gu, ctx->dec_act, I, st));
+      CK(decode_gemv(w.wgu, nullptr, false, H, ctx->dec_xmid, 1, w.ffn_norm, eps, 2 * I, H, nullptr, nullptr,
+                     ctx->dec_gu, st));
     if (int8)
-      CK(decode_gemv(w.q_d, w.s_d, true, I, ctx->dec_act, H, I, ctx->dec_xmid, ctx->dec_x, nullptr, st));
+      CK(decode_gemv(w.q_d, w.s_d, true, I, ctx->dec_gu, 2, nullptr, 0.f, H, I, ctx->dec_xmid, ctx->dec_x, nullptr,
+                     st));
     else
-      CK(decode_gemv(w.wd, nullptr, false, I, ctx->dec_act, H, I, ctx->dec_xmid, ctx->dec_x, nullptr, st));
+      CK(decode_gemv(w.wd, nullptr, false, I, ctx->dec_gu, 2, nullptr, 0.f, H, I, ctx->dec_xmid, ctx->dec_x, nullptr,
+                     st));
   }
-  CK(rmsnorm_forward(ctx->dec_x, ctx->final_norm, ctx->dec_xn, 1, H, eps, st));
   if (int8)
-    CK(decode_gemv(ctx->qE, ctx->sE, true, H, ctx->dec_xn, V, H, nullptr, ctx->dec_logits, nullptr, st));
+    CK(decode_gemv(ctx->qE, ctx->sE, true, H, ctx->dec_x, 1, ctx->final_norm, eps, V, H, nullptr, ctx->dec_logits,
+                   nullptr, st));
   else
-    CK(decode_gemv(ctx->E, nullptr, false, H, ctx->dec_xn, V, H, nullptr, ctx->dec_logits, nullptr, st));
-  CK(decode_argmax(ctx->dec_logits, V, ctx->dec_cnt, ctx->dec_tok, step_logits, st));
+    CK(decode_gemv(ctx->E, nullptr, false, H, ctx->dec_x, 1, ctx->final_norm, eps, V, H, nullptr, ctx->dec_logits,
+                   nullptr, st));
+  CK(decode_argmax(ctx->dec_logits, V, ctx->dec_cnt, ctx->dec_tok, step_logits, ctx->dec_amax, st));
   return LLMCU_OK;
 }
 
@@ -1294,13 +1296,14 @@ llmcu_status llmcu_generate(llmcu_ctx* ctx, const int32_t* prompt, int n_prompt,
   const int init[4] = {n_prompt - 1, 0, 0, 0};  // the argmax advances the position to n_prompt
   CK(cudaMemcpyAsync(ctx->dec_cnt, init, sizeof(init), cudaMemcpyHostToDevice, st));
   // first token: final norm + lm_head of the prompt's last position
-  CK(rmsnorm_forward(ctx->resid[L] + static_cast<size_t>(n_prompt - 1) * H, ctx->final_norm, ctx->dec_xn, 1, H, eps,
-                     st));
+  const float* xlast = ctx->resid[L] + static_cast<size_t>(n_prompt - 1) * H;
   if (ctx->rc.base_dtype == LLMCU_BASE_INT8)
-    CK(decode_gemv(ctx->qE, ctx->sE, true, H, ctx->dec_xn, V, H, nullptr, ctx->dec_logits, nullptr, st));
+    CK(decode_gemv(ctx->qE, ctx->sE, true, H, xlast, 1, ctx->final_norm, eps, V, H, nullptr, ctx->dec_logits,
+                   nullptr, st));
   else
-    CK(decode_gemv(ctx->E, nullptr, false, H, ctx->dec_xn, V, H, nullptr, ctx->dec_logits, nullptr, st));
-  CK(decode_argmax(ctx->dec_logits, V, ctx->dec_cnt, ctx->dec_tok, dlog, st));
+    CK(decode_gemv(ctx->E, nullptr, false, H, xlast, 1, ctx->final_norm, eps, V, H, nullptr, ctx->dec_logits, nullptr,
+                   st));
+  CK(decode_argmax(ctx->dec_logits, V, ctx->dec_cnt, ctx->dec_tok, dlog, ctx->dec_amax, st));
   if (!dlog && n_new > 1) CKS(decode_graph(ctx));
   CK(cudaEventRecord(cleanup.e0, st));
   set_pdl(true);
