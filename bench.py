@@ -115,14 +115,36 @@ class ClockSampler:
 
 
 def algorithmic_gemm_flops_per_token(m) -> float:
-    """Forward + dX of every frozen linear (tied lm_head once) + LoRA fwd/dX."""
+    """Forward + dX of every frozen linear (tied lm_head once)."""
     H, Q, KV, I, V, L = m.hidden, m.n_heads * m.head_dim, m.n_kv_heads * m.head_dim, m.ffn, m.vocab, m.n_layers
     n_lin = L * (Q * H + 2 * KV * H + H * Q + 3 * I * H) + V * H
     return float(4 * n_lin)
 
 
+def algorithmic_flops_per_token(m, seq, n_lora) -> float:
+    """The step's algorithmic work per token: 4 N_lin (forward + dX of the
+    frozen linears) + 3 (2 S hd nq L) (causal attention forward and backward)
+    + 6 n_lora (adapter forward, dX and gradients)."""
+    attn = 3 * (2 * seq * m.head_dim * m.n_heads * m.n_layers)
+    return algorithmic_gemm_flops_per_token(m) + attn + 6.0 * n_lora
+
+
+ALL_PROJS = ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down")
+
+
+def parse_targets(arg: str):
+    """Adapter names of a --lora-targets value."""
+    named = {"attn": ALL_PROJS[:4], "mlp": ALL_PROJS[4:], "all": ALL_PROJS}
+    if arg in named:
+        return tuple(named[arg])
+    out = tuple(x.strip() for x in arg.split(",") if x.strip())
+    bad = [x for x in out if x not in ALL_PROJS]
+    if bad or not out:
+        raise SystemExit(f"unknown --lora-targets entries: {bad or arg}")
+    return tuple(p for p in ALL_PROJS if p in out)
+
+
 def make_tokens(vocab, batch, seq, seed, dist):
-    from oracle.golden import ModelCfg  # noqa: F401  (generator only)
     rng = np.random.Generator(np.random.PCG64(seed))
     n = batch * (seq + 1)
     if dist == "uniform":
@@ -265,6 +287,9 @@ def main():
     ap.add_argument("--decode", type=int, default=0,
                     help="instead of the training step: greedy decode of N tokens after a 128-token prompt")
     ap.add_argument("--int8", action="store_true", help="with --decode: INT8 base")
+    ap.add_argument("--lora-targets", default="attn",
+                    help="adapted projections: attn (the reference's q/k/v/o), mlp, all, or a comma list of "
+                         "wq,wk,wv,wo,w_gate,w_up,w_down")
     args = ap.parse_args()
     if args.decode:
         return run_decode(args)
@@ -297,7 +322,8 @@ def main():
 
     m = load_binding()
     model = m.Model.qwen3_1p7b(n_layers=args.layers)
-    ctx = m.Context(model, m.Lora(16, 32.0), m.Run(B, S, base_dtype), device=local)
+    projs = parse_targets(args.lora_targets)
+    ctx = m.Context(model, m.Lora(16, 32.0, m.targets_mask(projs)), m.Run(B, S, base_dtype), device=local)
     if world > 1:
         obj = [m.Context.dp_unique_id() if rank == 0 else None]
         dist_.broadcast_object_list(obj, src=0)
@@ -402,8 +428,7 @@ def main():
             cpu = {"value": None, "unit": UNIT, "error": str(exc)[:200]}
 
     if rank == 0:
-        from oracle.golden import CFG_QWEN3_1P7B, algorithmic_flops_per_token
-        step_alg = algorithmic_flops_per_token(CFG_QWEN3_1P7B, S) * tokens_per_step
+        step_alg = algorithmic_flops_per_token(model, S, ctx.lora_param_count()) * tokens_per_step
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
@@ -412,7 +437,7 @@ def main():
             "config": {"workload": args.workload, "description": desc,
                        "model": "qwen3-1.7b-shape" + ("" if args.layers == 28 else f" ({args.layers} layers)"),
                        "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world}",
-                       "lora": "rank 16 alpha 32 on q/k/v/o", "l2": "inputs larger than L2 (6.9 GB of weights "
+                       "lora": "rank 16 alpha 32 on " + "/".join(projs), "l2": "inputs larger than L2 (6.9 GB of weights "
                        "and ~9 GB of activations stream per step); no flush"},
             "step_roofline": {"alg_tflop_per_step": round(step_alg / 1e12, 3),
                               "achieved_tflops": round(step_alg / (ms / 1e3) / 1e12 / world, 2),

@@ -65,6 +65,9 @@ typedef struct {
 typedef struct {
     int32_t rank;          /* LORA_RANK   16 (1..16 supported) */
     float   alpha;         /* LORA_ALPHA  32 -> scale alpha/rank */
+    int32_t targets;       /* adapted projections: bit p set = llmcu_proj p has
+                              an adapter; 0 = LLMCU_TARGETS_ATTN, the reference's
+                              fixed set (include/lora.h:22-27)                 */
 } llmcu_lora_cfg;
 
 typedef enum { LLMCU_BASE_FP16 = 0, LLMCU_BASE_INT8 = 1 } llmcu_base_dtype;
@@ -101,8 +104,19 @@ typedef enum {
     LLMCU_T_COUNT = 13
 } llmcu_tensor_id;
 
-/* LoRA projection ids, in the order of include/lora.h:22-27. */
-typedef enum { LLMCU_P_Q = 0, LLMCU_P_K = 1, LLMCU_P_V = 2, LLMCU_P_O = 3 } llmcu_proj;
+/* LoRA projection ids: q/k/v/o in the order of include/lora.h:22-27, then
+ * the MLP projections (gate_proj, up_proj, down_proj), which the reference
+ * does not adapt.  Adapter shapes: A [rank, d_in], B [d_out, rank] with
+ * (d_out, d_in) = q (nh*hd, H), k / v (nkv*hd, H), o (H, nh*hd),
+ * gate / up (I, H), down (H, I). */
+typedef enum {
+    LLMCU_P_Q = 0, LLMCU_P_K = 1, LLMCU_P_V = 2, LLMCU_P_O = 3,
+    LLMCU_P_GATE = 4, LLMCU_P_UP = 5, LLMCU_P_DOWN = 6,
+    LLMCU_P_COUNT = 7
+} llmcu_proj;
+#define LLMCU_TARGETS_ATTN 0x0F   /* q, k, v, o (the reference)      */
+#define LLMCU_TARGETS_MLP  0x70   /* gate, up, down                  */
+#define LLMCU_TARGETS_ALL  0x7F
 
 typedef struct llmcu_ctx llmcu_ctx;
 
@@ -144,7 +158,8 @@ llmcu_status llmcu_init_base_synthetic(llmcu_ctx* ctx, uint64_t seed, float std)
 /* ------------------------------------------------------------------ LoRA */
 
 /* A is [rank, d_in] and B is [d_out, rank], fp32 row-major, host memory --
- * the layout of include/lora.h:13-20 and of the lora_step files. */
+ * the layout of include/lora.h:13-20 and of the lora_step files.  `proj`
+ * must be one of the context's targets (LLMCU_ERR_INVALID_ARG otherwise). */
 llmcu_status llmcu_set_lora(llmcu_ctx* ctx, int layer, int proj, const float* A, const float* B);
 llmcu_status llmcu_get_lora(llmcu_ctx* ctx, int layer, int proj, float* A, float* B);
 /* Gradients of the last llmcu_forward_backward / llmcu_train_step. */
@@ -155,6 +170,8 @@ llmcu_status llmcu_init_lora_synthetic(llmcu_ctx* ctx, uint64_t seed, float b_st
 llmcu_status llmcu_reset_optimizer(llmcu_ctx* ctx);
 /* Total LoRA parameter count (A and B of every adapter). */
 int64_t llmcu_lora_param_count(const llmcu_ctx* ctx);
+/* The context's target mask (llmcu_lora_cfg.targets with 0 resolved). */
+int32_t llmcu_lora_targets(const llmcu_ctx* ctx);
 
 /* ------------------------------------------------------------------ steps */
 
@@ -184,7 +201,9 @@ llmcu_status llmcu_adamw(llmcu_ctx* ctx, const llmcu_adamw_cfg* opt, int step);
 
 /* Replaces save_lora (src/train.cu:146-170): writes
  * dir/lora_step{step}_layer{l}_{wq,wk,wv,wo}_{A,B}.bin, raw fp32, A [r, d_in],
- * B [d_out, r], no header -- the files python/save_lora.py reads. */
+ * B [d_out, r], no header -- the files python/save_lora.py reads.  The MLP
+ * targets, when enabled, add ..._{w_gate,w_up,w_down}_{A,B}.bin the same way
+ * (names of the base weights they adapt). */
 llmcu_status llmcu_save_lora(llmcu_ctx* ctx, const char* dir, int step);
 /* Reads the same files back (e.g. those written by save_lora.py --from-hf). */
 llmcu_status llmcu_load_lora(llmcu_ctx* ctx, const char* dir, int step);

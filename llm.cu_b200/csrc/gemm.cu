@@ -207,7 +207,7 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
   const int n_main = ea.n_main > 0 ? ea.n_main : N;
   if (n_main < N) {  // side output: only for the plain stores, from a tile boundary
     if ((epi != Epi::kStoreF16 && epi != Epi::kStoreF16Delta && epi != Epi::kResidF32 &&
-         epi != Epi::kQKNormRope) ||
+         epi != Epi::kQKNormRope && epi != Epi::kSwiGLU && epi != Epi::kSwiGLUBwd) ||
         n_main % BN ||
         (N - n_main) % 8 || !ea.side ||
         ea.ld_side % 8 || reinterpret_cast<uintptr_t>(ea.side) % 16)
@@ -238,12 +238,12 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
       okc = make_io_map(&maps[2], ea.out, M, n_main, ea.ld_out, true) &&
             make_io_map(&maps[3], ea.resid, M, n_main, ea.ld_out, true);
       break;
-    case Epi::kSwiGLU:  // C = gate/up pre-activations [M, N], D = act [M, N/2]
-      okc = make_io_map(&maps[2], ea.gu, M, N, ea.ld_gu, false) &&
-            make_io_map(&maps[3], ea.act, M, N / 2, ea.ld_act, false);
+    case Epi::kSwiGLU:  // C = gate/up pre-activations [M, n_main], D = act [M, n_main/2]
+      okc = make_io_map(&maps[2], ea.gu, M, n_main, ea.ld_gu, false) &&
+            make_io_map(&maps[3], ea.act, M, n_main / 2, ea.ld_act, false);
       break;
-    case Epi::kSwiGLUBwd:  // C = dgu [M, 2N] out; gu [M, 2N] is read with plain loads
-      okc = make_io_map(&maps[2], ea.gu, M, 2 * N, ea.ld_gu, false) && ea.gu_in &&
+    case Epi::kSwiGLUBwd:  // C = dgu [M, 2 n_main] out; gu [M, 2 n_main] is read with plain loads
+      okc = make_io_map(&maps[2], ea.gu, M, 2 * n_main, ea.ld_gu, false) && ea.gu_in &&
             reinterpret_cast<uintptr_t>(ea.gu_in) % 16 == 0 && ea.ld_gu % 8 == 0;
       maps[3] = maps[2];
       break;

@@ -478,8 +478,14 @@ struct EpiSwiGLU {
   static constexpr bool kPaired = true;  // requires BN == 256
   static constexpr bool kStores = true;
   __device__ static void begin(State&, const Params&, const EpiCtx&, int) {}
-  // g: gate columns [cc, cc+64) of tile tn, u: the matching up columns
+  // g: gate columns [cc, cc+64) of tile tn, u: the matching up columns.
+  // A tile past n_main holds the side output (h of the gate/up adapters) in
+  // its first 64 columns.
   __device__ static bool pair(State&, const Params&, EpiCtx& c, int tile_n, int cc, const float* g, const float* u) {
+    if (tile_n * 256 >= c.n_main) {
+      side_store(c, tile_n * 256 + cc, g, kChunk);
+      return true;
+    }
     uint32_t dgp[32], sp[32], ap[32];  // u silu'(g), silu(g), act as packed half2
 #pragma unroll
     for (int t = 0; t < 32; ++t) {
@@ -537,7 +543,7 @@ struct EpiSwiGLUBwd {
   static constexpr bool kTmemDirect = true;
   // 32-column step q of the slice starting at column col0 (a multiple of 128)
   __device__ static void fetch(State& st, const Params& p, const EpiCtx& c, int col0, int q) {
-    if (c.row < c.M && col0 < c.N) {
+    if (c.row < c.M && col0 < c.n_main) {
       const uint4* src =
           reinterpret_cast<const uint4*>(p.gu_in + static_cast<size_t>(c.row) * p.ld + (col0 >> 7) * 256 + 32 * q);
 #pragma unroll
@@ -553,6 +559,16 @@ struct EpiSwiGLUBwd {
   __device__ static void begin(State& st, const Params& p, const EpiCtx& c, int, int col0) { fetch(st, p, c, col0, 0); }
   __device__ static bool tile(State& st, const Params& p, EpiCtx& c, int col0, uint32_t taddr, int) {
     if (col0 >= c.N) return true;
+    if (col0 >= c.n_main) {  // dh of the down adapter (s B_down columns)
+#pragma unroll 1
+      for (int q = 0; q < 4 && col0 + 32 * q < c.N; ++q) {
+        float v[32];
+        tmem_ld_32x32b_x32(taddr + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v));
+        tmem_ld_wait();
+        side_store(c, col0 + 32 * q, v, 32);
+      }
+      return true;
+    }
     const int gcol = (col0 >> 7) * 256;
     uint32_t du_keep[16];
 #pragma unroll 1

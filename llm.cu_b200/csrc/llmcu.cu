@@ -47,13 +47,15 @@ struct LayerW {
   // INT8 base: q [out, in] per fused weight + per-row scales
   int8_t *q_qkv, *q_o, *q_gu, *q_d;
   float *s_qkv, *s_o, *s_gu, *s_d;
-  // merged base + LoRA weights of this step (lora_merge)
-  __half *mqkv, *mo;
+  // merged base + LoRA weights of this step (lora_merge); mgu / md only
+  // with MLP targets
+  __half *mqkv, *mo, *mgu, *md;
 };
 
 struct LayerA {  // forward stash
   float *resid_mid;
   __half *xn, *hq, *qkv, *qkr, *attn, *ho, *xn2, *gu, *act;  // qkr: normed, rotated q | k [M, Q + KV]
+  __half *hgu, *hd;  // MLP targets: x A^T of gate | up (segments 0 / 16) and of down, [M, 64]
   float* lse;
 };
 
@@ -81,7 +83,7 @@ struct llmcu_ctx {
   // int8 dequant scratch (one layer's fp16 weight) and a row-scale temporary
   __half* dq_w = nullptr;
   float* q_scale_tmp = nullptr;
-  MergeWeights mw;  // all layers' q/k/v and o base weights, for lora_merge
+  MergeWeights mw;  // all layers' base weights, for lora_merge
 
   // lora
   float *lp = nullptr, *lg = nullptr, *lm = nullptr, *lv = nullptr;
@@ -101,6 +103,7 @@ struct llmcu_ctx {
   float *dres = nullptr, *dq = nullptr, *dk = nullptr, *delta = nullptr;
   __half* dxn = nullptr;  // dX of the normed inputs (fp16, feeds the RMSNorm backward)
   __half *dres16 = nullptr, *dgu = nullptr, *dho = nullptr, *dattn = nullptr, *dqkv = nullptr, *dhq = nullptr;
+  __half *dhgu = nullptr, *dhd = nullptr;  // MLP targets: dY s B of gate | up and of down, [M, 64]
   // io
   int *tok = nullptr, *tgt = nullptr, *derr = nullptr;
   float* loss_dev = nullptr;   // [0] = mean loss of the last step
@@ -227,8 +230,10 @@ void carve(llmcu_ctx* c, Carver& cv) {
       w.wgu = wgu ? wgu + l * 2 * I * H : nullptr;
       w.wd = wd ? wd + l * H * I : nullptr;
     }
-    c->mw.wqkv = wqkv;
-    c->mw.wo = wo;
+    c->mw.qkv.w = wqkv;
+    c->mw.o.w = wo;
+    c->mw.gu.w = wgu;
+    c->mw.d.w = wd;
   } else {
     int8_t* q_qkv = cv.take<int8_t>(L * QKV * H);
     int8_t* q_o = cv.take<int8_t>(L * H * Q);
@@ -249,25 +254,39 @@ void carve(llmcu_ctx* c, Carver& cv) {
       w.s_gu = s_gu ? s_gu + l * 2 * I : nullptr;
       w.s_d = s_d ? s_d + l * H : nullptr;
     }
-    c->mw.q_qkv = q_qkv;
-    c->mw.q_o = q_o;
-    c->mw.s_qkv = s_qkv;
-    c->mw.s_o = s_o;
-    c->mw.s_layer_qkv = static_cast<int64_t>(QKV);
-    c->mw.s_layer_o = static_cast<int64_t>(H);
+    c->mw.qkv.q = q_qkv;
+    c->mw.o.q = q_o;
+    c->mw.gu.q = q_gu;
+    c->mw.d.q = q_d;
+    c->mw.qkv.s = s_qkv;
+    c->mw.o.s = s_o;
+    c->mw.gu.s = s_gu;
+    c->mw.d.s = s_d;
+    c->mw.qkv.s_layer = static_cast<int64_t>(QKV);
+    c->mw.o.s_layer = static_cast<int64_t>(H);
+    c->mw.gu.s_layer = static_cast<int64_t>(2 * I);
+    c->mw.d.s_layer = static_cast<int64_t>(H);
     const size_t wmax = std::max({QKV * H, H * Q, 2 * I * H, H * I});
     c->dq_w = cv.take<__half>(wmax);
     c->q_scale_tmp = cv.take<float>(std::max({QKV, H, 2 * I}));
   }
-  c->mw.w_layer_qkv = static_cast<int64_t>(QKV * H);
-  c->mw.w_layer_o = static_cast<int64_t>(H * Q);
+  c->mw.qkv.w_layer = static_cast<int64_t>(QKV * H);
+  c->mw.o.w_layer = static_cast<int64_t>(H * Q);
+  c->mw.gu.w_layer = static_cast<int64_t>(2 * I * H);
+  c->mw.d.w_layer = static_cast<int64_t>(H * I);
+  const bool mlp = c->ld.has_mlp();
   {
     const int64_t nq = merged_qkv_elems(c->ld), no = merged_o_elems(c->ld);
+    const int64_t ng = merged_gu_elems(c->ld), nd = merged_d_elems(c->ld);
     __half* mqkv = cv.take<__half>(L * nq);
     __half* mo = cv.take<__half>(L * no);
+    __half* mgu = mlp ? cv.take<__half>(L * ng) : nullptr;
+    __half* md = mlp ? cv.take<__half>(L * nd) : nullptr;
     for (size_t l = 0; l < L; ++l) {
       c->lw[l].mqkv = mqkv ? mqkv + l * nq : nullptr;
       c->lw[l].mo = mo ? mo + l * no : nullptr;
+      c->lw[l].mgu = mgu ? mgu + l * ng : nullptr;
+      c->lw[l].md = md ? md + l * nd : nullptr;
     }
   }
   for (size_t l = 0; l < L; ++l) {
@@ -300,6 +319,8 @@ void carve(llmcu_ctx* c, Carver& cv) {
     a.xn2 = cv.take<__half>(M * H);
     a.gu = cv.take<__half>(M * 2 * I);
     a.act = cv.take<__half>(M * I);
+    a.hgu = mlp ? cv.take<__half>(M * 64) : nullptr;
+    a.hd = mlp ? cv.take<__half>(M * 64) : nullptr;
     a.lse = cv.take<float>(lse_n);
   }
   c->xf = cv.take<__half>(M * H);
@@ -324,6 +345,8 @@ void carve(llmcu_ctx* c, Carver& cv) {
   c->delta = cv.take<float>(lse_n);
   c->dqkv = cv.take<__half>(M * QKV);
   c->dhq = cv.take<__half>(M * 64);
+  c->dhgu = mlp ? cv.take<__half>(M * 64) : nullptr;
+  c->dhd = mlp ? cv.take<__half>(M * 64) : nullptr;
   c->tok = cv.take<int>(M);
   c->tgt = cv.take<int>(M);
   c->derr = cv.take<int>(4);
@@ -432,10 +455,20 @@ const __half* base_weight(llmcu_ctx* c, const __half* w16, const int8_t* q, cons
 }
 Operand op_mn(const __half* p, int k_rows, int n_cols, int ld) { return Operand{p, n_cols, k_rows, ld, true}; }
 
+// Merged weights of the current adapters, every layer (lora_merge).
+cudaError_t merge_adapters(llmcu_ctx* ctx) {
+  MergedOut mo;
+  mo.qkv = ctx->lw[0].mqkv;
+  mo.o = ctx->lw[0].mo;
+  mo.gu = ctx->lw[0].mgu;
+  mo.d = ctx->lw[0].md;
+  return lora_merge(ctx->lp, ctx->ld, ctx->L, ctx->mw, mo, ctx->st);
+}
+
 // ----------------------------------------------------------------- step
 // Embedding and every layer's forward over ctx->tok ([B, S] ids on the device),
 // leaving each layer's stash and ctx->resid[L] (the pre-final-norm hidden).
-// Expects the merged q/k/v/o weights of the current adapters.
+// Expects the merged weights of the current adapters (merge_adapters).
 llmcu_status forward_layers(llmcu_ctx* ctx, int B, int S) {
   const int M = B * S;
   const int H = ctx->H, Q = ctx->Q, KV = ctx->KV, QKV = ctx->QKV, I = ctx->I, V = ctx->V;
@@ -492,6 +525,31 @@ llmcu_status forward_layers(llmcu_ctx* ctx, int B, int S) {
       TIMED(P_GEMM, gemm(op(a.attn, M, Q, Q), op(w.mo, H + 64, Q, Q + 64), M, H + 64, Epi::kResidF32, ea, err, st));
     }
     TIMED(P_NORM, rmsnorm_forward(a.resid_mid, w.ffn_norm, a.xn2, M, H, eps, st));
+    if (ctx->ld.has_mlp()) {
+      {  // [gu | act | h_gu] = xn2 . mgu^T: SwiGLU over the merged rows, h of gate / up in the side tile
+        EpiArgs ea;
+        ea.gu = a.gu;
+        ea.ld_gu = 2 * I;
+        ea.act = a.act;
+        ea.ld_act = I;
+        ea.n_main = 2 * I;
+        ea.side = a.hgu;
+        ea.ld_side = 64;
+        TIMED(P_GEMM, gemm(op(a.xn2, M, H, H), op(w.mgu, 2 * I + 64, H, H + 64), M, 2 * I + 64, Epi::kSwiGLU, ea, err,
+                           st, 256));
+      }
+      {  // [resid' | h_d] = [resid_mid + act . md^T | act . Ad^T]
+        EpiArgs ea;
+        ea.out = ctx->resid[l + 1];
+        ea.ld_out = H;
+        ea.resid = a.resid_mid;
+        ea.n_main = H;
+        ea.side = a.hd;
+        ea.ld_side = 64;
+        TIMED(P_GEMM, gemm(op(a.act, M, I, I), op(w.md, H + 64, I, I + 64), M, H + 64, Epi::kResidF32, ea, err, st));
+      }
+      continue;
+    }
     const __half* wgu = base_weight(ctx, w.wgu, w.q_gu, w.s_gu, 2 * I, H, &e);
     CK(e);
     {
@@ -540,7 +598,7 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   TIMED(P_FILL, fill_f32(ctx->lg, ctx->n_lora, 0.f, st));
   set_pdl(true);
   // merged q/k/v/o weights of this step's adapters, every layer
-  TIMEDN(P_LORA_PREP, 3, lora_merge(ctx->lp, d, ctx->L, ctx->mw, ctx->lw[0].mqkv, ctx->lw[0].mo, st));
+  TIMEDN(P_LORA_PREP, d.has_mlp() ? 6 : 3, merge_adapters(ctx));
   TIMED(P_CE, ce_valid_rows(ctx->valid, ctx->tgt, B, S, ctx->rc.loss_all_positions, V, err, st));
   CKS(forward_layers(ctx, B, S));
   const __half* E = ctx->E;
@@ -579,21 +637,65 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     LayerW& w = ctx->lw[l];
     LayerA& a = ctx->la[l];
     float* G = ctx->lg + d.per_layer * l;
-    // MLP: d_act = dres . W_down (MN-major), SwiGLU backward fused
-    const __half* wd = base_weight(ctx, w.wd, w.q_d, w.s_d, H, I, &e);
-    CK(e);
-    {
-      EpiArgs ea;
-      ea.gu_in = a.gu;
-      ea.gu = ctx->dgu;
-      ea.ld_gu = 2 * I;
-      TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op_mn(wd, H, I, I), M, I, Epi::kSwiGLUBwd, ea, err, st, 256));
+    if (d.has_mlp()) {
+      {  // [d_act | dh_d] = dres . md (MN-major), SwiGLU backward fused into dgu
+        EpiArgs ea;
+        ea.gu_in = a.gu;
+        ea.gu = ctx->dgu;
+        ea.ld_gu = 2 * I;
+        ea.n_main = I;
+        ea.side = ctx->dhd;
+        ea.ld_side = 64;
+        TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op_mn(w.md, H, I + 64, I + 64), M, I + 64, Epi::kSwiGLUBwd, ea,
+                           err, st, 256));
+      }
+      {  // [dxn2 | dh_gu] = dgu . mgu (MN-major)
+        EpiArgs ea;
+        ea.out = ctx->dxn;
+        ea.ld_out = H;
+        ea.n_main = H;
+        ea.side = ctx->dhgu;
+        ea.ld_side = 64;
+        TIMED(P_GEMM, gemm(op(ctx->dgu, M, 2 * I, 2 * I), op_mn(w.mgu, 2 * I, H + 64, H + 64), M, H + 64,
+                           Epi::kStoreF16, ea, err, st));
+      }
+      // the MLP adapters' gradients while dres16 still holds the layer-output gradient
+      LoraGradBatch gb{};
+      const float sb = d.scale * unscale;
+      auto gp = [&](int p, bool b_side) { return d.has(p) ? G + (b_side ? d.offB(p) : d.offA(p)) : nullptr; };
+      // dB_d[h, j] = s sum_m dres[m, h] h_d[m, j];  dA_d[j, i] = sum_m dh_d[m, j] act[m, i]
+      if (d.has(kPDown)) {
+        gb.p[gb.n++] = LoraGradProb{ctx->dres16, H, a.hd, 64, {gp(kPDown, true)}, 1, r, 1, H, r, sb, 0};
+        gb.p[gb.n++] = LoraGradProb{a.act, I, ctx->dhd, 64, {gp(kPDown, false)}, 1, 1, I, I, r, unscale, 0};
+      }
+      if (d.has(kPGate) || d.has(kPUp)) {
+        // dB_gate / dB_up from the interleaved dgu columns against h_gu's segments 0 / 16
+        gb.p[gb.n++] = LoraGradProb{ctx->dgu, 2 * I, a.hgu, 64, {gp(kPGate, true), gp(kPUp, true)}, 2, r, 1, 2 * I,
+                                    r, sb, 1};
+        // dA_gate, dA_up in one pass over the normed input
+        gb.p[gb.n++] = LoraGradProb{a.xn2, H, ctx->dhgu, 64, {gp(kPGate, false), gp(kPUp, false)}, 2, 1, H, H, r,
+                                    unscale, 0};
+      }
+      gb.a_max = 0;
+      for (int i = 0; i < gb.n; ++i) gb.a_max = std::max(gb.a_max, gb.p[i].A);
+      TIMED(P_LORA_GRAD, lora_grad(gb, M, st));
+    } else {
+      // MLP: d_act = dres . W_down (MN-major), SwiGLU backward fused
+      const __half* wd = base_weight(ctx, w.wd, w.q_d, w.s_d, H, I, &e);
+      CK(e);
+      {
+        EpiArgs ea;
+        ea.gu_in = a.gu;
+        ea.gu = ctx->dgu;
+        ea.ld_gu = 2 * I;
+        TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op_mn(wd, H, I, I), M, I, Epi::kSwiGLUBwd, ea, err, st, 256));
+      }
+      // dxn2 = dgu . W_gate/up (MN-major)
+      const __half* wgu = base_weight(ctx, w.wgu, w.q_gu, w.s_gu, 2 * I, H, &e);
+      CK(e);
+      TIMED(P_GEMM, gemm(op(ctx->dgu, M, 2 * I, 2 * I), op_mn(wgu, 2 * I, H, H), M, H, Epi::kStoreF16,
+                         EpiArgs{ctx->dxn, H}, err, st));
     }
-    // dxn2 = dgu . W_gate/up (MN-major)
-    const __half* wgu = base_weight(ctx, w.wgu, w.q_gu, w.s_gu, 2 * I, H, &e);
-    CK(e);
-    TIMED(P_GEMM, gemm(op(ctx->dgu, M, 2 * I, 2 * I), op_mn(wgu, 2 * I, H, H), M, H, Epi::kStoreF16,
-                       EpiArgs{ctx->dxn, H}, err, st));
     TIMED(P_NORM, rmsnorm_backward(ctx->dxn, a.resid_mid, w.ffn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
     // O projection
     {  // [dattn | dh_o] = dres . mo (MN-major): dres W'_o and dres s B_o, plus delta = rowsum(dO * O) per head
@@ -634,19 +736,25 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       // all six adapter gradients of the layer in one launch (the O
       // projection's inputs -- dres16, attn, h_o, dh_o -- are still intact here)
       LoraGradBatch gb{};
-      gb.n = 6;
       gb.a_max = ctx->lpart_amax;
       const float sb = d.scale * unscale;
-      // dBo[h, j] = s * sum_m dres[m, h] ho[m, j]
-      gb.p[4] = LoraGradProb{ctx->dres16, H, a.ho, 64, {G + d.oBo}, 1, r, 1, H, r, d.scale * unscale};
-      // dAo[j, q] = sum_m dho[m, j] attn[m, q]
-      gb.p[5] = LoraGradProb{a.attn, Q, ctx->dho, 64, {G + d.oAo}, 1, 1, Q, Q, r, unscale};
-      gb.p[0] = LoraGradProb{ctx->dqkv, QKV, a.hq, 64, {G + d.oBq}, 1, r, 1, Q, r, sb};
-      gb.p[1] = LoraGradProb{ctx->dqkv + Q, QKV, a.hq + kSegK, 64, {G + d.oBk}, 1, r, 1, KV, r, sb};
-      gb.p[2] = LoraGradProb{ctx->dqkv + Q + KV, QKV, a.hq + kSegV, 64, {G + d.oBv}, 1, r, 1, KV, r, sb};
+      auto gp = [&](int p, bool b_side) { return d.has(p) ? G + (b_side ? d.offB(p) : d.offA(p)) : nullptr; };
+      if (d.has(kPQ)) gb.p[gb.n++] = LoraGradProb{ctx->dqkv, QKV, a.hq, 64, {gp(kPQ, true)}, 1, r, 1, Q, r, sb, 0};
+      if (d.has(kPK))
+        gb.p[gb.n++] = LoraGradProb{ctx->dqkv + Q, QKV, a.hq + kSegK, 64, {gp(kPK, true)}, 1, r, 1, KV, r, sb, 0};
+      if (d.has(kPV))
+        gb.p[gb.n++] = LoraGradProb{ctx->dqkv + Q + KV, QKV, a.hq + kSegV, 64, {gp(kPV, true)}, 1, r, 1, KV, r, sb, 0};
       // dA_q, dA_k, dA_v in one pass over the normed input (column groups 0 / 16 / 32 of dh)
-      gb.p[3] = LoraGradProb{a.xn, H, ctx->dhq, 64, {G + d.oAq, G + d.oAk, G + d.oAv}, 3, 1, H, H, r, unscale};
-      TIMED(P_LORA_GRAD, lora_grad(gb, M, st));
+      if (d.has(kPQ) || d.has(kPK) || d.has(kPV))
+        gb.p[gb.n++] = LoraGradProb{a.xn, H, ctx->dhq, 64, {gp(kPQ, false), gp(kPK, false), gp(kPV, false)}, 3, 1, H,
+                                    H, r, unscale, 0};
+      if (d.has(kPO)) {
+        // dBo[h, j] = s * sum_m dres[m, h] ho[m, j]
+        gb.p[gb.n++] = LoraGradProb{ctx->dres16, H, a.ho, 64, {gp(kPO, true)}, 1, r, 1, H, r, sb, 0};
+        // dAo[j, q] = sum_m dho[m, j] attn[m, q]
+        gb.p[gb.n++] = LoraGradProb{a.attn, Q, ctx->dho, 64, {gp(kPO, false)}, 1, 1, Q, Q, r, unscale, 0};
+      }
+      if (gb.n) TIMED(P_LORA_GRAD, lora_grad(gb, M, st));
     }
     TIMED(P_NORM, rmsnorm_backward(ctx->dxn, ctx->resid[l], w.attn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
     if (ctx->nccl) {
@@ -724,6 +832,8 @@ void* llmcu_stream(const llmcu_ctx* ctx) { return ctx ? static_cast<void*>(ctx->
 
 int64_t llmcu_lora_param_count(const llmcu_ctx* ctx) { return ctx ? ctx->n_lora : 0; }
 
+int32_t llmcu_lora_targets(const llmcu_ctx* ctx) { return ctx ? static_cast<int32_t>(ctx->ld.targets) : 0; }
+
 llmcu_status llmcu_ctx_create(const llmcu_model_cfg* model, const llmcu_lora_cfg* lora, const llmcu_run_cfg* run,
                               int device, llmcu_ctx** out) {
   if (!model || !lora || !run || !out) return LLMCU_ERR_INVALID_ARG;
@@ -735,12 +845,17 @@ llmcu_status llmcu_ctx_create(const llmcu_model_cfg* model, const llmcu_lora_cfg
   if (m.n_heads % m.n_kv_heads) return LLMCU_ERR_INVALID_ARG;
   if (m.hidden % 64 || m.ffn % 128 || m.vocab % 8) return LLMCU_ERR_UNSUPPORTED;
   if (lora->rank < 1 || lora->rank > 16) return LLMCU_ERR_UNSUPPORTED;
+  const uint32_t targets = lora->targets ? static_cast<uint32_t>(lora->targets) : kTargetsAttn;
+  if (targets & ~(kTargetsAttn | kTargetsMlp)) return LLMCU_ERR_INVALID_ARG;
+  // the MLP's merged weights put their side columns on 256-column tile boundaries
+  if ((targets & kTargetsMlp) && m.ffn % 256) return LLMCU_ERR_UNSUPPORTED;
   if (run->max_batch < 1 || run->max_seq < 2) return LLMCU_ERR_INVALID_ARG;
   if (run->base_dtype != LLMCU_BASE_FP16 && run->base_dtype != LLMCU_BASE_INT8) return LLMCU_ERR_INVALID_ARG;
 
   llmcu_ctx* ctx = new llmcu_ctx();
   ctx->m = m;
   ctx->lc = *lora;
+  ctx->lc.targets = static_cast<int32_t>(targets);
   ctx->rc = *run;
   ctx->device = device;
   ctx->H = m.hidden;
@@ -754,7 +869,8 @@ llmcu_status llmcu_ctx_create(const llmcu_model_cfg* model, const llmcu_lora_cfg
   ctx->I = m.ffn;
   ctx->V = m.vocab;
   ctx->Mmax = run->max_batch * run->max_seq;
-  ctx->ld = LoraDims::make(lora->rank, ctx->H, ctx->Q, ctx->KV, lora->alpha / static_cast<float>(lora->rank));
+  ctx->ld = LoraDims::make(lora->rank, ctx->H, ctx->Q, ctx->KV, ctx->I, lora->alpha / static_cast<float>(lora->rank),
+                           targets);
   ctx->n_lora = ctx->ld.per_layer * ctx->L;
 
   auto bail = [&](llmcu_status s) {
@@ -1007,8 +1123,10 @@ llmcu_status llmcu_init_base_synthetic(llmcu_ctx* ctx, uint64_t seed, float stdd
 // ------------------------------------------------------------------- LoRA
 
 static llmcu_status check_proj(llmcu_ctx* ctx, int layer, int proj) {
-  if (layer < 0 || layer >= ctx->L || proj < 0 || proj > 3)
+  if (layer < 0 || layer >= ctx->L || proj < 0 || proj >= kNumProj)
     return fail(ctx, LLMCU_ERR_INVALID_ARG, "layer %d / proj %d out of range", layer, proj);
+  if (!ctx->ld.has(proj))
+    return fail(ctx, LLMCU_ERR_INVALID_ARG, "proj %d is not among the targets 0x%x", proj, ctx->ld.targets);
   return LLMCU_OK;
 }
 
@@ -1054,7 +1172,8 @@ llmcu_status llmcu_init_lora_synthetic(llmcu_ctx* ctx, uint64_t seed, float b_st
   uint64_t k = seed * 7919ull + 3;
   for (int l = 0; l < ctx->L; ++l) {
     float* base = ctx->lp + d.per_layer * l;
-    for (int p = 0; p < 4; ++p) {
+    for (int p = 0; p < kNumProj; ++p) {
+      if (!d.has(p)) continue;
       const float bound = 1.0f / sqrtf(static_cast<float>(d.d_in(p)));
       CK(fill_uniform_f32(base + d.offA(p), static_cast<int64_t>(d.r) * d.d_in(p), k++, -bound, bound, ctx->st));
       CK(fill_normal_f32(base + d.offB(p), static_cast<int64_t>(d.d_out(p)) * d.r, k++, b_std, ctx->st));
@@ -1127,14 +1246,17 @@ llmcu_status llmcu_read_loss(llmcu_ctx* ctx, float* loss_out) {
 
 // ---------------------------------------------------------- checkpointing
 
-static const char* kProjNames[4] = {"wq", "wk", "wv", "wo"};
+// file-name parts of the adapters (the reference's four, then the MLP's, named
+// like the base weights they adapt)
+static const char* kProjNames[kNumProj] = {"wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"};
 
 llmcu_status llmcu_save_lora(llmcu_ctx* ctx, const char* dir, int step) {
   if (!ctx || !dir) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null argument");
   const LoraDims& d = ctx->ld;
   std::vector<float> A, B;
   for (int l = 0; l < ctx->L; ++l) {
-    for (int p = 0; p < 4; ++p) {
+    for (int p = 0; p < kNumProj; ++p) {
+      if (!d.has(p)) continue;
       A.resize(static_cast<size_t>(d.r) * d.d_in(p));
       B.resize(static_cast<size_t>(d.d_out(p)) * d.r);
       CKS(llmcu_get_lora(ctx, l, p, A.data(), B.data()));
@@ -1159,7 +1281,8 @@ llmcu_status llmcu_load_lora(llmcu_ctx* ctx, const char* dir, int step) {
   const LoraDims& d = ctx->ld;
   std::vector<float> A, B;
   for (int l = 0; l < ctx->L; ++l) {
-    for (int p = 0; p < 4; ++p) {
+    for (int p = 0; p < kNumProj; ++p) {
+      if (!d.has(p)) continue;
       A.resize(static_cast<size_t>(d.r) * d.d_in(p));
       B.resize(static_cast<size_t>(d.d_out(p)) * d.r);
       std::vector<float>* parts[2] = {&A, &B};
@@ -1184,8 +1307,9 @@ namespace {
 
 // One decode step (llm_engine's transformer_decode, src/kernels/forward.cu:340-394)
 // for the token dec_cnt[2] at position dec_cnt[0], both read on the device:
-// GEMVs over the merged q/k/v/o weights and the base MLP / lm_head rows (INT8
-// rows with their scales for an INT8 base), the cache append inside the
+// GEMVs over the merged q/k/v/o weights and the base (or, with MLP targets,
+// merged) MLP and lm_head rows (INT8 rows with their scales for an INT8
+// base), the cache append inside the
 // QK-norm/RoPE kernel, split attention over the cache and the argmax that
 // chooses the next token.
 llmcu_status decode_step(llmcu_ctx* ctx, float* step_logits) {
@@ -1206,7 +1330,15 @@ llmcu_status decode_step(llmcu_ctx* ctx, float* step_logits) {
                         st));
     CK(decode_gemv(w.mo, nullptr, false, Q + 64, ctx->dec_attn, 0, nullptr, 0.f, H, Q, ctx->dec_x, ctx->dec_xmid,
                    nullptr, st));
-    // ffn norm folded into the gate/up GEMV, SwiGLU into the down GEMV
+    // ffn norm folded into the gate/up GEMV, SwiGLU into the down GEMV; with
+    // MLP targets both read the merged fp16 rows (their pads are skipped)
+    if (w.mgu) {
+      CK(decode_gemv(w.mgu, nullptr, false, H + 64, ctx->dec_xmid, 1, w.ffn_norm, eps, 2 * I, H, nullptr, nullptr,
+                     ctx->dec_gu, st));
+      CK(decode_gemv(w.md, nullptr, false, I + 64, ctx->dec_gu, 2, nullptr, 0.f, H, I, ctx->dec_xmid, ctx->dec_x,
+                     nullptr, st));
+      continue;
+    }
     if (int8)
       CK(decode_gemv(w.q_gu, w.s_gu, true, H, ctx->dec_xmid, 1, w.ffn_norm, eps, 2 * I, H, nullptr, nullptr,
                      ctx->dec_gu, st));
@@ -1282,7 +1414,7 @@ llmcu_status llmcu_generate(llmcu_ctx* ctx, const int32_t* prompt, int n_prompt,
   CK(cudaEventCreate(&cleanup.e1));
   // merged weights of the current adapters, then the prompt through the batched forward
   set_pdl(false);
-  CK(lora_merge(ctx->lp, ctx->ld, L, ctx->mw, ctx->lw[0].mqkv, ctx->lw[0].mo, st));
+  CK(merge_adapters(ctx));
   set_pdl(true);
   CKS(forward_layers(ctx, 1, n_prompt));
   set_pdl(false);
@@ -1347,7 +1479,8 @@ llmcu_status llmcu_generate(llmcu_ctx* ctx, const int32_t* prompt, int n_prompt,
 namespace {
 struct AdamwHeader {
   char magic[8];  // "LLMCUADW"
-  int32_t version, step, n_layers, rank, hidden, q_dim, kv_dim, reserved;
+  int32_t version, step, n_layers, rank, hidden, q_dim, kv_dim;
+  int32_t targets;  // adapter mask; 0 reads as q/k/v/o
   int64_t n_params;
   int64_t reserved2[2];
 };
@@ -1375,6 +1508,7 @@ llmcu_status llmcu_save_adamw_state(llmcu_ctx* ctx, const char* dir, int step) {
   h.hidden = ctx->H;
   h.q_dim = ctx->Q;
   h.kv_dim = ctx->KV;
+  h.targets = static_cast<int32_t>(ctx->ld.targets);
   h.n_params = ctx->n_lora;
   char path[1024];
   adamw_path(path, sizeof(path), dir, step);
@@ -1398,14 +1532,16 @@ llmcu_status llmcu_load_adamw_state(llmcu_ctx* ctx, const char* dir, int step) {
     fclose(f);
     return fail(ctx, LLMCU_ERR_IO, "%s is not an AdamW state file", path);
   }
+  const uint32_t file_targets = h.targets ? static_cast<uint32_t>(h.targets) : kTargetsAttn;
   if (h.step != step || h.n_layers != ctx->L || h.rank != ctx->ld.r || h.hidden != ctx->H || h.q_dim != ctx->Q ||
-      h.kv_dim != ctx->KV || h.n_params != ctx->n_lora) {
+      h.kv_dim != ctx->KV || h.n_params != ctx->n_lora || file_targets != ctx->ld.targets) {
     fclose(f);
     return fail(ctx, LLMCU_ERR_INVALID_ARG,
-                "%s holds step %d, %d layers, rank %d, dims %d/%d/%d (%lld params); this context has %d layers, "
-                "rank %d, dims %d/%d/%d (%lld params)",
-                path, h.step, h.n_layers, h.rank, h.hidden, h.q_dim, h.kv_dim, static_cast<long long>(h.n_params),
-                ctx->L, ctx->ld.r, ctx->H, ctx->Q, ctx->KV, static_cast<long long>(ctx->n_lora));
+                "%s holds step %d, %d layers, rank %d, dims %d/%d/%d, targets 0x%x (%lld params); this context has "
+                "%d layers, rank %d, dims %d/%d/%d, targets 0x%x (%lld params)",
+                path, h.step, h.n_layers, h.rank, h.hidden, h.q_dim, h.kv_dim, file_targets,
+                static_cast<long long>(h.n_params), ctx->L, ctx->ld.r, ctx->H, ctx->Q, ctx->KV, ctx->ld.targets,
+                static_cast<long long>(ctx->n_lora));
   }
   const size_t n = static_cast<size_t>(ctx->n_lora);
   std::vector<float> m(n), v(n);

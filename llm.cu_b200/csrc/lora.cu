@@ -1,8 +1,9 @@
 // lora.cu -- LoRA operand preparation and the adapter-gradient kernel.
 //
-// Adapters live in one flat fp32 buffer (per layer: Aq Bq Ak Bk Av Bv Ao Bo,
-// A [r, d_in], B [d_out, r] as include/lora.h:13-20 of the reference), so
-// AdamW and the data-parallel allreduce each touch one contiguous range.
+// Adapters live in one flat fp32 buffer (per layer: the enabled ones of
+// Aq Bq Ak Bk Av Bv Ao Bo Agate Bgate Aup Bup Adown Bdown, A [r, d_in],
+// B [d_out, r] as include/lora.h:13-20 of the reference), so AdamW and the
+// data-parallel allreduce each touch one contiguous range.
 //
 // lora_merge builds, per layer and per step, the merged fp16 weights the
 // tcgen05 GEMMs use in place of the reference's separate LoRA products
@@ -12,7 +13,14 @@
 //                            rows QKV + seg(p) + j: A_p[j, :]
 //   mo   [H + 64, Q + 64]    rows < H: W_o + s B_o A_o; cols Q + j: s B_o[:, j];
 //                            rows H + j: A_o[j, :]
-// seg(q, k, v) = 0, 16, 32 (kSegK, kSegV); everything else in the pads is 0.
+//   mgu  [2I + 64, H + 64]   (MLP targets) the 128-row gate/up interleave of
+//                            the base: gate rows W_g + s B_g A_g, cols H + j:
+//                            s B_g; up rows likewise with seg 16; rows 2I +
+//                            seg + j: A_g / A_u
+//   md   [H + 64, I + 64]    (MLP targets) as mo for the down projection
+// seg(q, k, v) = 0, 16, 32 (kSegK, kSegV), seg(gate, up) = 0, 16; everything
+// else in the pads is 0, and so is the s B A of an adapter that is not
+// trained (its rows are the base weight).
 // The forward GEMM x . mqkv^T (K-major, N = QKV + 64) then yields q, k, v and,
 // in its last 64 columns, h = x [Aq | Ak | Av]^T; the input-gradient GEMM
 // dY . mqkv (MN-major, N = H + 64) yields dx and dh = dY [s Bq | s Bk | s Bv].
@@ -22,7 +30,7 @@
 // (src/kernels/lora_backward.cu:50-90, src/kernels/matmul.cu:102-139):
 //   dB = s * dY^T h     (a over d_out, b over r)
 //   dA = dh^T x         (computed as (x^T dh)^T: a over d_in, b over r)
-// split over m, mma.sync m16n8k16; each split adds its share into the
+// on the tensor cores, split over m; each split adds its share into the
 // zeroed gradients with fp32 atomics.
 #include "common.cuh"
 #include "lora.cuh"
@@ -33,15 +41,31 @@ namespace {
 
 // Main block of one merged weight: `tiles` row tiles of 64 rows, columns
 // [c0, c0 + 256) of W + s B A for one adapter (A [r, d_in], B [rows_p, r]).
-// Base W is fp16 (w) or INT8 rows (q) times the per-row scale (sc), as the
+// Base W is fp16 (w) or INT8 rows (q) times the per-row scale (s), as the
 // reference's quantiser lays them out (src/kernels/quantize.cu:8-50).
-struct MergeSrc {
-  const __half* w;
-  const int8_t* q;
-  const float* sc;
-  int64_t w_layer;   // elements between layers of w / q
-  int64_t sc_layer;  // elements between layers of sc
-};
+using MergeSrc = MergeBase;
+
+// Which adapter owns merged main-block row o, and its row in that adapter's
+// B: which = 0 q/k/v (stacked), 1 o, 2 gate/up (128-row interleave, gate
+// first), 3 down.
+__device__ __forceinline__ void merge_row(const LoraDims& d, int which, int o, int& proj, int& arow) {
+  if (which == 0) {
+    if (o < d.Q) {
+      proj = kPQ; arow = o;
+    } else if (o < d.Q + d.KV) {
+      proj = kPK; arow = o - d.Q;
+    } else {
+      proj = kPV; arow = o - d.Q - d.KV;
+    }
+  } else if (which == 1) {
+    proj = kPO; arow = o;
+  } else if (which == 2) {
+    proj = ((o >> 7) & 1) ? kPUp : kPGate;
+    arow = ((o >> 8) << 7) + (o & 127);
+  } else {
+    proj = kPDown; arow = o;
+  }
+}
 constexpr int kMrgRows = 64;   // rows of one row tile
 constexpr int kMrgCols = 256;  // columns of a block
 constexpr int kMrgTiles = 4;   // row tiles per block (fewer when an adapter has fewer rows)
@@ -57,7 +81,7 @@ __device__ __forceinline__ MergeRaw merge_load(const MergeSrc& src, int l, int o
   if (src.q) {
     const int2 raw = *reinterpret_cast<const int2*>(src.q + off);
     m.bits = make_uint4(static_cast<uint32_t>(raw.x), static_cast<uint32_t>(raw.y), 0u, 0u);
-    m.sc = src.sc[static_cast<int64_t>(l) * src.sc_layer + o];
+    m.sc = src.s[static_cast<int64_t>(l) * src.s_layer + o];
   } else {
     m.bits = *reinterpret_cast<const uint4*>(src.w + off);
     m.sc = 1.f;
@@ -87,8 +111,8 @@ __device__ __forceinline__ void merge_unpack(const MergeRaw& m, bool int8, float
 // a warp's global rows are 512 contiguous bytes.  The next tile's W rows are
 // loaded while the current tile is computed.
 __global__ void __launch_bounds__(256, 1)
-    lora_merge_main_kernel(const float* __restrict__ flat, LoraDims d, MergeSrc src, int out_rows, int d_in,
-                           int which, int tiles, __half* __restrict__ merged, int64_t merged_layer, int ldm) {
+    lora_merge_main_kernel(const float* __restrict__ flat, LoraDims d, MergeSrc src, int d_in, int which, int tiles,
+                           __half* __restrict__ merged, int64_t merged_layer, int ldm) {
   pdl_trigger();
   pdl_wait();
   __shared__ __align__(16) float As[16][kMrgCols];
@@ -96,21 +120,10 @@ __global__ void __launch_bounds__(256, 1)
   const int l = blockIdx.z;
   const int ob = blockIdx.y * kMrgRows * tiles, c0 = blockIdx.x * kMrgCols;
   const float* P = flat + static_cast<int64_t>(l) * d.per_layer;
-  // adapter owning rows [ob, ob + 64 * tiles): which = 0 -> q/k/v by row, 1 -> o
-  int proj, row_base;
-  if (which == 1) {
-    proj = 3;
-    row_base = 0;
-  } else if (ob < d.Q) {
-    proj = 0;
-    row_base = 0;
-  } else if (ob < d.Q + d.KV) {
-    proj = 1;
-    row_base = d.Q;
-  } else {
-    proj = 2;
-    row_base = d.Q + d.KV;
-  }
+  // adapter owning rows [ob, ob + 64 * tiles) (a block never straddles two)
+  int proj, arow0;
+  merge_row(d, which, ob, proj, arow0);
+  const bool on = d.has(proj);  // off: the rows are the base weight
   const int rg = threadIdx.x >> 5, cg = threadIdx.x & 31;
   const int c = c0 + 8 * cg;
   const bool col_ok = c < d_in;
@@ -120,17 +133,17 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
     for (int i = 0; i < 8; ++i) raw[i] = merge_load(src, l, ob + 8 * rg + i, d_in, c);
   }
-  const float* A = P + d.offA(proj);
-  const float* Bm = P + d.offB(proj);
-  const int r = d.r;
+  const float* A = P + (on ? d.offA(proj) : 0);
+  const float* Bm = P + (on ? d.offB(proj) : 0);
+  const int r = on ? d.r : 0;
   for (int i = threadIdx.x; i < 16 * kMrgCols; i += 256) {
     const int j = i / kMrgCols, cc = i % kMrgCols;
     As[j][cc] = (j < r && c0 + cc < d_in) ? A[static_cast<int64_t>(j) * d_in + c0 + cc] : 0.f;
   }
   for (int i = threadIdx.x; i < tiles * 16 * kMrgRows; i += 256) {
     const int t = i / (16 * kMrgRows), rr = (i / 16) % kMrgRows, j = i % 16;
-    const int o = ob + t * kMrgRows + rr;
-    Bs[t][j][rr] = j < r ? d.scale * Bm[static_cast<int64_t>(o - row_base) * r + j] : 0.f;
+    const int ar = arow0 + t * kMrgRows + rr;
+    Bs[t][j][rr] = j < r ? d.scale * Bm[static_cast<int64_t>(ar) * r + j] : 0.f;
   }
   __syncthreads();
   if (!col_ok) return;
@@ -197,23 +210,12 @@ __global__ void __launch_bounds__(128)
   cp_async_commit();
   pdl_wait();  // the adapters are written by the previous step's optimizer
   const float* P = flat + static_cast<int64_t>(l) * d.per_layer;
-  int proj, row_base;
-  if (which == 1) {
-    proj = 3;
-    row_base = 0;
-  } else if (o0 < d.Q) {
-    proj = 0;
-    row_base = 0;
-  } else if (o0 < d.Q + d.KV) {
-    proj = 1;
-    row_base = d.Q;
-  } else {
-    proj = 2;
-    row_base = d.Q + d.KV;
-  }
-  const float* A = P + d.offA(proj);
-  const float* Bm = P + d.offB(proj);
-  const int r = d.r;
+  int proj, arow0;
+  merge_row(d, which, o0, proj, arow0);
+  const bool on = d.has(proj);  // off: the rows are the base weight (s B A = 0)
+  const float* A = P + (on ? d.offA(proj) : 0);
+  const float* Bm = P + (on ? d.offB(proj) : 0);
+  const int r = on ? d.r : 0;
   if (r == 16 && d_in % 4 == 0) {
     // every adapter load of the thread in flight at once (16-byte loads):
     // A rows [16 x 128] are 512 float4, B rows [64 x 16] are 256
@@ -230,7 +232,7 @@ __global__ void __launch_bounds__(128)
     for (int k = 0; k < 2; ++k) {
       const int i = threadIdx.x + k * 128;
       const int rr = i >> 2, j = (i & 3) * 4;
-      bv[k] = *reinterpret_cast<const float4*>(Bm + static_cast<int64_t>(o0 + rr - row_base) * 16 + j);
+      bv[k] = *reinterpret_cast<const float4*>(Bm + static_cast<int64_t>(arow0 + rr) * 16 + j);
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -249,7 +251,7 @@ __global__ void __launch_bounds__(128)
   } else {
     for (int i = threadIdx.x; i < kMtRows * 16; i += blockDim.x) {
       const int rr = i / 16, j = i % 16;
-      sB[rr][j] = __float2half_rn(j < r ? d.scale * Bm[static_cast<int64_t>(o0 + rr - row_base) * r + j] : 0.f);
+      sB[rr][j] = __float2half_rn(j < r ? d.scale * Bm[static_cast<int64_t>(arow0 + rr) * r + j] : 0.f);
     }
     for (int i = threadIdx.x; i < 16 * kMtCols; i += blockDim.x) {
       const int j = i / kMtCols, c = i % kMtCols;
@@ -295,15 +297,23 @@ __global__ void __launch_bounds__(128)
   }
 }
 
-// The pads of both merged weights: the 64 extra columns (s B) of the rows
-// < out_rows and the 64 extra rows (A) of the columns < d_in.
+// s * B_p[n, j] and A_p[j, c] of an adapter, 0 when p is not trained or j >= r
+__device__ __forceinline__ float pad_sb(const LoraDims& d, const float* P, int p, int n, int j) {
+  return (d.has(p) && j >= 0 && j < d.r) ? d.scale * P[d.offB(p) + static_cast<int64_t>(n) * d.r + j] : 0.f;
+}
+__device__ __forceinline__ float pad_a(const LoraDims& d, const float* P, int p, int j, int c) {
+  return (d.has(p) && j >= 0 && j < d.r) ? P[d.offA(p) + static_cast<int64_t>(j) * d.d_in(p) + c] : 0.f;
+}
+
+// The pads of the attention's merged weights: the 64 extra columns (s B) of
+// the rows < out_rows and the 64 extra rows (A) of the columns < d_in.
 __global__ void lora_merge_pad_kernel(const float* __restrict__ flat, LoraDims d, __half* __restrict__ mqkv,
                                       int64_t mqkv_layer, __half* __restrict__ mo, int64_t mo_layer) {
   pdl_trigger();
   pdl_wait();
   const int l = blockIdx.y;
   const float* P = flat + static_cast<int64_t>(l) * d.per_layer;
-  const int r = d.r, H = d.H, Q = d.Q, KV = d.KV, QKV = Q + 2 * KV;
+  const int H = d.H, Q = d.Q, KV = d.KV, QKV = Q + 2 * KV;
   const int n_cq = 64 * QKV, n_rq = 64 * H, n_co = 64 * H, n_ro = 64 * Q;
   const int total = n_cq + n_rq + n_co + n_ro;
   __half* Mq = mqkv + static_cast<int64_t>(l) * mqkv_layer;
@@ -313,39 +323,75 @@ __global__ void lora_merge_pad_kernel(const float* __restrict__ flat, LoraDims d
     int k = i;
     if (k < n_cq) {  // mqkv[n, H + j] = s * B_p[n', j - seg(p)]
       const int n = k >> 6, j = k & 63;
-      float v = 0.f;
-      if (n < Q) {
-        if (j < r) v = d.scale * P[d.oBq + static_cast<int64_t>(n) * r + j];
-      } else if (n < Q + KV) {
-        if (j >= kSegK && j < kSegK + r) v = d.scale * P[d.oBk + static_cast<int64_t>(n - Q) * r + (j - kSegK)];
-      } else {
-        if (j >= kSegV && j < kSegV + r) v = d.scale * P[d.oBv + static_cast<int64_t>(n - Q - KV) * r + (j - kSegV)];
-      }
+      const float v = n < Q         ? pad_sb(d, P, kPQ, n, j)
+                      : n < Q + KV  ? pad_sb(d, P, kPK, n - Q, j - kSegK)
+                                    : pad_sb(d, P, kPV, n - Q - KV, j - kSegV);
       Mq[static_cast<int64_t>(n) * ldq + H + j] = __float2half_rn(v);
       continue;
     }
     k -= n_cq;
     if (k < n_rq) {  // mqkv[QKV + j, c] = A_p[j - seg(p), c]
       const int j = k / H, c = k % H;
-      float v = 0.f;
-      if (j < r) v = P[d.oAq + static_cast<int64_t>(j) * H + c];
-      else if (j >= kSegK && j < kSegK + r) v = P[d.oAk + static_cast<int64_t>(j - kSegK) * H + c];
-      else if (j >= kSegV && j < kSegV + r) v = P[d.oAv + static_cast<int64_t>(j - kSegV) * H + c];
+      const float v = j < kSegK ? pad_a(d, P, kPQ, j, c) : j < kSegV ? pad_a(d, P, kPK, j - kSegK, c)
+                                                                     : pad_a(d, P, kPV, j - kSegV, c);
       Mq[static_cast<int64_t>(QKV + j) * ldq + c] = __float2half_rn(v);
       continue;
     }
     k -= n_rq;
     if (k < n_co) {  // mo[n, Q + j] = s * Bo[n, j]
       const int n = k >> 6, j = k & 63;
-      const float v = j < r ? d.scale * P[d.oBo + static_cast<int64_t>(n) * r + j] : 0.f;
-      Mo[static_cast<int64_t>(n) * ldo + Q + j] = __float2half_rn(v);
+      Mo[static_cast<int64_t>(n) * ldo + Q + j] = __float2half_rn(pad_sb(d, P, kPO, n, j));
       continue;
     }
     k -= n_co;
     {  // mo[H + j, c] = Ao[j, c]
       const int j = k / Q, c = k % Q;
-      const float v = j < r ? P[d.oAo + static_cast<int64_t>(j) * Q + c] : 0.f;
-      Mo[static_cast<int64_t>(H + j) * ldo + c] = __float2half_rn(v);
+      Mo[static_cast<int64_t>(H + j) * ldo + c] = __float2half_rn(pad_a(d, P, kPO, j, c));
+    }
+  }
+}
+
+// The pads of the MLP's merged weights: mgu columns H + j (s B_gate at seg 0,
+// s B_up at seg 16, by the row's place in the interleave) and rows 2I + j
+// (A_gate, A_up); md columns I + j (s B_down) and rows H + j (A_down).
+__global__ void lora_merge_pad_mlp_kernel(const float* __restrict__ flat, LoraDims d, __half* __restrict__ mgu,
+                                          int64_t mgu_layer, __half* __restrict__ md, int64_t md_layer) {
+  pdl_trigger();
+  pdl_wait();
+  const int l = blockIdx.y;
+  const float* P = flat + static_cast<int64_t>(l) * d.per_layer;
+  const int H = d.H, I = d.I;
+  const int n_cg = 64 * 2 * I, n_rg = 64 * H, n_cd = 64 * H, n_rd = 64 * I;
+  const int total = n_cg + n_rg + n_cd + n_rd;
+  __half* Mg = mgu + static_cast<int64_t>(l) * mgu_layer;
+  __half* Md = md + static_cast<int64_t>(l) * md_layer;
+  const int ldg = H + 64, ldd = I + 64;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    int k = i;
+    if (k < n_cg) {
+      const int n = k >> 6, j = k & 63;
+      const int ar = ((n >> 8) << 7) + (n & 127);
+      const float v = ((n >> 7) & 1) ? pad_sb(d, P, kPUp, ar, j - 16) : pad_sb(d, P, kPGate, ar, j);
+      Mg[static_cast<int64_t>(n) * ldg + H + j] = __float2half_rn(v);
+      continue;
+    }
+    k -= n_cg;
+    if (k < n_rg) {
+      const int j = k / H, c = k % H;
+      const float v = j < 16 ? pad_a(d, P, kPGate, j, c) : pad_a(d, P, kPUp, j - 16, c);
+      Mg[static_cast<int64_t>(2 * I + j) * ldg + c] = __float2half_rn(v);
+      continue;
+    }
+    k -= n_rg;
+    if (k < n_cd) {
+      const int n = k >> 6, j = k & 63;
+      Md[static_cast<int64_t>(n) * ldd + I + j] = __float2half_rn(pad_sb(d, P, kPDown, n, j));
+      continue;
+    }
+    k -= n_cd;
+    {
+      const int j = k / I, c = k % I;
+      Md[static_cast<int64_t>(H + j) * ldd + c] = __float2half_rn(pad_a(d, P, kPDown, j, c));
     }
   }
 }
@@ -384,6 +430,9 @@ __global__ void __launch_bounds__(kLgThreads, 2)
   const LoraGradProb& pb = batch.p[blockIdx.y];
   const int a0 = blockIdx.x * kLgA;
   if (a0 >= pb.A) return;  // whole CTA
+  // interleaved U: the tile's 128 columns are all gate or all up
+  const int sel = pb.ilv ? (a0 >> 7) & 1 : 0;
+  if (!pb.out[sel] && (pb.ilv || pb.groups == 1)) return;  // that adapter is not trained
   const int split = blockIdx.z;
   const int m_per = ((M + splits - 1) / splits + kLgM - 1) / kLgM * kLgM;
   const int m_begin = split * m_per;
@@ -478,32 +527,38 @@ __global__ void __launch_bounds__(kLgThreads, 2)
     // [a][b] row-major gradients (dB: sa = 16, sb = 1) are staged through
     // shared memory so that the additions leave as contiguous runs; the
     // [b][a] ones (dA: sa = 1) are already contiguous across the lanes
-    const bool staged = pb.sb == 1 && pb.sa == 16 && pb.Bn == 16 && ng == 1 && a0 + kLgA <= pb.A;
+    const bool staged = pb.sb == 1 && pb.sa == 16 && pb.Bn == 16 && (ng == 1 || pb.ilv) && a0 + kLgA <= pb.A;
     float* stage = reinterpret_cast<float*>(smem);  // [128][17], the stage buffers are idle now
     uint32_t v[32];
+    if (staged) {  // group sel's 16 columns lie in the first 32
+      tmem_ld_32x32b_x32(taddr, v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) stage[ar * 17 + j] = __uint_as_float(v[16 * sel + j]) * pb.scale;
+    } else {
+      // gradient row of this lane's a (the interleave maps a to its adapter row)
+      const int orow = pb.ilv ? ((a0 >> 8) << 7) + ar : a;
 #pragma unroll 1
-    for (int half = 0; half < 2; ++half) {
-      if (32 * half < 16 * ng) {  // warp-uniform
-        tmem_ld_32x32b_x32(taddr + 32 * half, v);
-        tmem_ld_wait();
-        if (staged) {
+      for (int half = 0; half < 2; ++half) {
+        if (32 * half < 16 * ng) {  // warp-uniform
+          tmem_ld_32x32b_x32(taddr + 32 * half, v);
+          tmem_ld_wait();
+          if (a < pb.A) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) stage[ar * 17 + j] = __uint_as_float(v[j]) * pb.scale;
-        } else if (a < pb.A) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int bcol = 32 * half + j;
-            const int g = bcol >> 4, b = bcol & 15;
-            if (g < ng && b < pb.Bn)
-              atomicAdd(pb.out[g] + static_cast<size_t>(a) * pb.sa + static_cast<size_t>(b) * pb.sb,
-                        __uint_as_float(v[j]) * pb.scale);
+            for (int j = 0; j < 32; ++j) {
+              const int bcol = 32 * half + j;
+              const int g = bcol >> 4, b = bcol & 15;
+              if (g < ng && b < pb.Bn && pb.out[g] && (!pb.ilv || g == sel))
+                atomicAdd(pb.out[g] + static_cast<size_t>(orow) * pb.sa + static_cast<size_t>(b) * pb.sb,
+                          __uint_as_float(v[j]) * pb.scale);
+            }
           }
         }
       }
     }
     if (staged) {
       __syncthreads();
-      float* dst = pb.out[0] + static_cast<size_t>(a0) * 16;
+      float* dst = pb.out[sel] + static_cast<size_t>(pb.ilv ? ((a0 >> 8) << 7) : a0) * 16;
       for (int i = threadIdx.x; i < kLgA * 16; i += kLgThreads) atomicAdd(dst + i, stage[(i >> 4) * 17 + (i & 15)]);
     }
   }
@@ -517,41 +572,58 @@ __global__ void __launch_bounds__(kLgThreads, 2)
 
 }  // namespace
 
-cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const MergeWeights& base, __half* mqkv,
-                       __half* mo, cudaStream_t st) {
-  const int H = d.H, Q = d.Q, KV = d.KV, QKV = Q + 2 * KV;
+cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const MergeWeights& base,
+                       const MergedOut& out, cudaStream_t st) {
+  const int H = d.H, Q = d.Q, KV = d.KV, I = d.I, QKV = Q + 2 * KV;
+  const bool mlp = d.has_mlp();
   if (d.r > 16 || Q % kMrgRows || KV % kMrgRows || H % kMrgRows || H % 8 || Q % 8) return cudaErrorInvalidValue;
   if (64LL * (QKV + 2 * H + Q) >= (1LL << 31)) return cudaErrorInvalidValue;
+  if (mlp && (I % 128 || !out.gu || !out.d || 64LL * (2 * I + 2 * H + I) >= (1LL << 31)))
+    return cudaErrorInvalidValue;
   const int64_t mqkv_layer = merged_qkv_elems(d), mo_layer = merged_o_elems(d);
-  MergeSrc sq{base.wqkv, base.q_qkv, base.s_qkv, base.w_layer_qkv, base.s_layer_qkv};
-  MergeSrc so{base.wo, base.q_o, base.s_o, base.w_layer_o, base.s_layer_o};
+  const int64_t mgu_layer = merged_gu_elems(d), md_layer = merged_d_elems(d);
   // row tiles per block: a divisor of every adapter's row-tile count
   auto tiles_for = [](int a, int b) {
     int t = kMrgTiles;
     while (t > 1 && ((a / kMrgRows) % t || (b / kMrgRows) % t)) t /= 2;
     return t;
   };
-  if (!base.q_qkv && !base.q_o) {  // fp16 base: tensor-core rank-r update
-    dim3 gq((H + kMtCols - 1) / kMtCols, QKV / kMtRows, n_layers);
-    launch_pdl(lora_merge_tc_kernel, gq, 128, 0, st, flat, d, base.wqkv, base.w_layer_qkv, H, 0, mqkv, mqkv_layer,
-               H + 64);
-    dim3 go((Q + kMtCols - 1) / kMtCols, H / kMtRows, n_layers);
-    launch_pdl(lora_merge_tc_kernel, go, 128, 0, st, flat, d, base.wo, base.w_layer_o, Q, 1, mo, mo_layer, Q + 64);
-  } else {
-    const int tq = tiles_for(Q, KV), to = tiles_for(H, H);
-    dim3 gq((H + kMrgCols - 1) / kMrgCols, QKV / (kMrgRows * tq), n_layers);
-    launch_pdl(lora_merge_main_kernel, gq, 256, 0, st, flat, d, sq, QKV, H, 0, tq, mqkv, mqkv_layer, H + 64);
-    dim3 go((Q + kMrgCols - 1) / kMrgCols, H / (kMrgRows * to), n_layers);
-    launch_pdl(lora_merge_main_kernel, go, 256, 0, st, flat, d, so, H, Q, 1, to, mo, mo_layer, Q + 64);
+  // one merged weight: rows [0, rows) of W (d_in columns) plus s B A
+  auto main_block = [&](const MergeBase& src, int rows, int d_in, int which, int tiles, __half* dst, int64_t layer) {
+    if (!src.q) {  // fp16 base: tensor-core rank-r update
+      dim3 g((d_in + kMtCols - 1) / kMtCols, rows / kMtRows, n_layers);
+      launch_pdl(lora_merge_tc_kernel, g, 128, 0, st, flat, d, src.w, src.w_layer, d_in, which, dst, layer, d_in + 64);
+    } else {
+      dim3 g((d_in + kMrgCols - 1) / kMrgCols, rows / (kMrgRows * tiles), n_layers);
+      launch_pdl(lora_merge_main_kernel, g, 256, 0, st, flat, d, src, d_in, which, tiles, dst, layer, d_in + 64);
+    }
+  };
+  main_block(base.qkv, QKV, H, 0, tiles_for(Q, KV), out.qkv, mqkv_layer);
+  main_block(base.o, H, Q, 1, tiles_for(H, H), out.o, mo_layer);
+  if (mlp) {
+    // gate/up: blocks of at most 128 rows stay inside one half of the interleave
+    main_block(base.gu, 2 * I, H, 2, 2, out.gu, mgu_layer);
+    main_block(base.d, H, I, 3, tiles_for(H, H), out.d, md_layer);
   }
   dim3 gp(128, n_layers);
-  launch_pdl(lora_merge_pad_kernel, gp, 256, 0, st, flat, d, mqkv, mqkv_layer, mo, mo_layer);
+  launch_pdl(lora_merge_pad_kernel, gp, 256, 0, st, flat, d, out.qkv, mqkv_layer, out.o, mo_layer);
+  if (mlp) {
+    dim3 gm(256, n_layers);
+    launch_pdl(lora_merge_pad_mlp_kernel, gm, 256, 0, st, flat, d, out.gu, mgu_layer, out.d, md_layer);
+  }
   return cudaGetLastError();
 }
 
-int lora_grad_splits(int M, int a_max, int n) {
-  const int tiles = (a_max + kLgA - 1) / kLgA * n;
-  int s = 2 * gemm_num_sms() / tiles;  // about two CTAs per SM, one wave
+// CTAs per SM the m-splits aim for (two are resident at a time)
+#ifndef LLMCU_LG_CTAS_PER_SM
+#define LLMCU_LG_CTAS_PER_SM 2
+#endif
+
+int lora_grad_splits(int M, const LoraGradBatch& batch) {
+  int tiles = 0;  // CTAs with work in one split
+  for (int i = 0; i < batch.n; ++i) tiles += (batch.p[i].A + kLgA - 1) / kLgA;
+  if (tiles < 1) tiles = 1;
+  int s = (LLMCU_LG_CTAS_PER_SM * gemm_num_sms() + tiles - 1) / tiles;
   const int max_s = (M + 255) / 256;
   if (s > max_s) s = max_s;
   if (s > kLoraMaxSplits) s = kLoraMaxSplits;
@@ -561,7 +633,7 @@ int lora_grad_splits(int M, int a_max, int n) {
 
 cudaError_t lora_grad(const LoraGradBatch& batch, int M, cudaStream_t st) {
   if (batch.n <= 0 || batch.n > kLoraMaxProbs) return cudaErrorInvalidValue;
-  const int splits = lora_grad_splits(M, batch.a_max, batch.n);
+  const int splits = lora_grad_splits(M, batch);
   static bool attr_done = false;
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(lora_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kLgSmem);
@@ -572,6 +644,7 @@ cudaError_t lora_grad(const LoraGradBatch& batch, int M, cudaStream_t st) {
   for (int i = 0; i < batch.n; ++i) {
     const LoraGradProb& p = batch.p[i];
     if (p.groups < 1 || p.groups > 4) return cudaErrorInvalidValue;
+    if (p.ilv && (p.groups != 2 || p.A % 256)) return cudaErrorInvalidValue;
     if (!encode_tma_2d_f16(&maps.u[i], p.U, M, p.A, p.ldu, kLgM) ||
         !encode_tma_2d_f16(&maps.w[i], p.W, M, 16 * p.groups, p.ldw, kLgM))
       return cudaErrorInvalidValue;

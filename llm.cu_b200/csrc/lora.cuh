@@ -7,48 +7,71 @@
 
 namespace llmcu {
 
-// Offsets (in floats) of each adapter inside one layer of the flat fp32
-// buffer.  A [r, d_in], B [d_out, r] row-major.
-struct LoraDims {
-  int r, H, Q, KV;
-  float scale;  // alpha / r
-  int64_t oAq, oBq, oAk, oBk, oAv, oBv, oAo, oBo, per_layer;
+// Adapter ids: q, k, v, o (the reference's four, include/lora.h:22-27),
+// then the MLP's gate, up and down projections.
+enum LoraProj : int { kPQ = 0, kPK = 1, kPV = 2, kPO = 3, kPGate = 4, kPUp = 5, kPDown = 6, kNumProj = 7 };
+constexpr uint32_t kTargetsAttn = 0x0Fu;
+constexpr uint32_t kTargetsMlp = 0x70u;
 
-  static LoraDims make(int r, int H, int Q, int KV, float scale) {
+// Offsets (in floats) of each adapter inside one layer of the flat fp32
+// buffer.  A [r, d_in], B [d_out, r] row-major; the enabled adapters follow
+// one another in id order (A then B), a disabled one has offsets -1.
+struct LoraDims {
+  int r, H, Q, KV, I;
+  float scale;        // alpha / r
+  uint32_t targets;   // bit p: adapter p is trained
+  int64_t oA[kNumProj], oB[kNumProj], per_layer;
+
+  static LoraDims make(int r, int H, int Q, int KV, int I, float scale, uint32_t targets) {
     LoraDims d{};
-    d.r = r; d.H = H; d.Q = Q; d.KV = KV; d.scale = scale;
+    d.r = r; d.H = H; d.Q = Q; d.KV = KV; d.I = I; d.scale = scale; d.targets = targets;
     int64_t o = 0;
-    d.oAq = o; o += static_cast<int64_t>(r) * H;
-    d.oBq = o; o += static_cast<int64_t>(Q) * r;
-    d.oAk = o; o += static_cast<int64_t>(r) * H;
-    d.oBk = o; o += static_cast<int64_t>(KV) * r;
-    d.oAv = o; o += static_cast<int64_t>(r) * H;
-    d.oBv = o; o += static_cast<int64_t>(KV) * r;
-    d.oAo = o; o += static_cast<int64_t>(r) * Q;
-    d.oBo = o; o += static_cast<int64_t>(H) * r;
+    for (int p = 0; p < kNumProj; ++p) {
+      d.oA[p] = d.oB[p] = -1;
+      if (!d.has(p)) continue;
+      d.oA[p] = o; o += static_cast<int64_t>(r) * d.d_in(p);
+      d.oB[p] = o; o += static_cast<int64_t>(d.d_out(p)) * r;
+    }
     d.per_layer = o;
     return d;
   }
-  // adapter (proj 0..3 = q, k, v, o) offsets and dims
-  __host__ __device__ int64_t offA(int proj) const { return proj == 0 ? oAq : proj == 1 ? oAk : proj == 2 ? oAv : oAo; }
-  __host__ __device__ int64_t offB(int proj) const { return proj == 0 ? oBq : proj == 1 ? oBk : proj == 2 ? oBv : oBo; }
-  __host__ __device__ int d_in(int proj) const { return proj == 3 ? Q : H; }
-  __host__ __device__ int d_out(int proj) const { return proj == 0 ? Q : proj == 3 ? H : KV; }
+  __host__ __device__ bool has(int p) const { return (targets >> p) & 1u; }
+  __host__ __device__ bool has_mlp() const { return (targets & kTargetsMlp) != 0u; }
+  __host__ __device__ int64_t offA(int p) const { return oA[p]; }
+  __host__ __device__ int64_t offB(int p) const { return oB[p]; }
+  __host__ __device__ int d_in(int p) const { return p == kPO ? Q : p == kPDown ? I : H; }
+  __host__ __device__ int d_out(int p) const {
+    return p == kPQ ? Q : (p == kPK || p == kPV) ? KV : (p == kPGate || p == kPUp) ? I : H;
+  }
 };
 
-// Merged weights of one layer (see lora.cu): [QKV + 64, H + 64] and [H + 64, Q + 64].
+// Merged weights of one layer (see lora.cu): q/k/v [QKV + 64, H + 64],
+// o [H + 64, Q + 64], gate/up (128-row interleaved) [2I + 64, H + 64] and
+// down [H + 64, I + 64].
 inline int64_t merged_qkv_elems(const LoraDims& d) {
   return (static_cast<int64_t>(d.Q + 2 * d.KV) + 64) * (d.H + 64);
 }
 inline int64_t merged_o_elems(const LoraDims& d) { return (static_cast<int64_t>(d.H) + 64) * (d.Q + 64); }
+inline int64_t merged_gu_elems(const LoraDims& d) { return (2 * static_cast<int64_t>(d.I) + 64) * (d.H + 64); }
+inline int64_t merged_d_elems(const LoraDims& d) { return (static_cast<int64_t>(d.H) + 64) * (d.I + 64); }
 
-// Base q/k/v and o weights of every layer: fp16 (w*) or INT8 rows (q*) with
-// per-row scales (s*); *_layer = elements between consecutive layers.
+// One fused base weight of every layer: fp16 (w) or INT8 rows (q) with
+// per-row scales (s); *_layer = elements between consecutive layers.
+struct MergeBase {
+  const __half* w = nullptr;
+  const int8_t* q = nullptr;
+  const float* s = nullptr;
+  int64_t w_layer = 0, s_layer = 0;
+};
+// The base weights lora_merge reads: q/k/v, o and (for the MLP targets)
+// gate/up (interleaved) and down.
 struct MergeWeights {
-  const __half *wqkv = nullptr, *wo = nullptr;
-  const int8_t *q_qkv = nullptr, *q_o = nullptr;
-  const float *s_qkv = nullptr, *s_o = nullptr;
-  int64_t w_layer_qkv = 0, w_layer_o = 0, s_layer_qkv = 0, s_layer_o = 0;
+  MergeBase qkv, o, gu, d;
+};
+// Where lora_merge writes: layer 0 of each merged weight, consecutive layers
+// merged_*_elems apart (gu / d are null without MLP targets).
+struct MergedOut {
+  __half *qkv = nullptr, *o = nullptr, *gu = nullptr, *d = nullptr;
 };
 
 constexpr int kLoraMaxProbs = 8;
@@ -61,6 +84,10 @@ constexpr int kLoraMaxSplits = 16;
 // g < groups (<= 4), b < Bn (<= 16); group g is stored at
 // out[g][a * sa + b * sb].  One pass over U serves every group, so the three
 // dA of q/k/v (which share the normed input) read it once.
+// A null out[g] skips group g (an adapter that is not trained).  With ilv
+// set, U's columns are the gate/up interleave (128-column blocks, gate
+// first): a column a belongs to group sel = (a >> 7) & 1 alone, and lands
+// in out[sel] at row ((a >> 8) << 7) + (a & 127).
 struct LoraGradProb {
   const __half* U;
   int ldu;
@@ -71,6 +98,7 @@ struct LoraGradProb {
   int sa, sb;
   int A, Bn;
   float scale;
+  int ilv;
 };
 struct LoraGradBatch {
   LoraGradProb p[kLoraMaxProbs];
@@ -78,10 +106,10 @@ struct LoraGradBatch {
   int a_max;  // >= every A
 };
 
-cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const MergeWeights& base, __half* mqkv,
-                       __half* mo, cudaStream_t st);
+cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const MergeWeights& base,
+                       const MergedOut& out, cudaStream_t st);
 // Adds into out[] (which the caller zeroes first).
 cudaError_t lora_grad(const LoraGradBatch& batch, int M, cudaStream_t st);
-int lora_grad_splits(int M, int a_max, int n);
+int lora_grad_splits(int M, const LoraGradBatch& batch);
 
 }  // namespace llmcu

@@ -13,7 +13,10 @@
 // --synthetic (device-generated N(0,0.02) base and adapters, uniform tokens),
 // --int8 (INT8 per-row base), --weights DIR, --data FILE, --out DIR, --seed,
 // --resume N (continue after step N from the adapter and AdamW files in --out;
-// every save also writes the AdamW sidecar lora_step{N}_adamw.bin).
+// every save also writes the AdamW sidecar lora_step{N}_adamw.bin),
+// --rank R / --alpha A (LoRA rank 1..16 and alpha; default the config's),
+// --lora-targets LIST (comma-separated wq,wk,wv,wo,w_gate,w_up,w_down, or
+// "attn" = the reference's q/k/v/o, "mlp", "all"; default attn).
 // Data parallel: when WORLD_SIZE > 1 (e.g. under torchrun) each process
 // drives GPU LOCAL_RANK, rank 0 writes the NCCL id to --dp-id-file and the
 // others read it; rank r takes sequences r, r+W, ... of every step window.
@@ -54,6 +57,9 @@ int main(int argc, char** argv) {
   std::string id_file = "/tmp/llmcu_nccl_id";
   bool synthetic = false, int8 = false;
   unsigned long long seed = 1234;
+  int lora_rank = 0;
+  float lora_alpha = 0.f;
+  std::string targets_arg = "attn";
 
   for (int i = 1; i < argc; i++) {
     auto next = [&](const char* flag) -> const char* {
@@ -74,12 +80,16 @@ int main(int argc, char** argv) {
     else if ((v = next("--seed"))) seed = strtoull(v, nullptr, 10);
     else if ((v = next("--dp-id-file"))) id_file = v;
     else if ((v = next("--resume"))) resume = atoi(v);
+    else if ((v = next("--rank"))) lora_rank = atoi(v);
+    else if ((v = next("--alpha"))) lora_alpha = static_cast<float>(atof(v));
+    else if ((v = next("--lora-targets"))) targets_arg = v;
     else if (!strcmp(argv[i], "--synthetic")) synthetic = true;
     else if (!strcmp(argv[i], "--int8")) int8 = true;
     else if (!strcmp(argv[i], "--help") || !strcmp(argv[i], "-h")) {
       printf("usage: llm_train [--lr F] [--steps N] [--seq-len S] [--save-every N] [--log-every N]\n"
              "                 [--batch B] [--config tiny|1.7b] [--synthetic] [--int8] [--weights DIR]\n"
-             "                 [--data FILE] [--out DIR] [--seed N] [--dp-id-file PATH] [--resume N]\n");
+             "                 [--data FILE] [--out DIR] [--seed N] [--dp-id-file PATH] [--resume N]\n"
+             "                 [--rank R] [--alpha A] [--lora-targets attn|mlp|all|wq,wk,...,w_down]\n");
       return 0;
     }
   }
@@ -92,15 +102,42 @@ int main(int argc, char** argv) {
   llmcu_lora_cfg lc;
   if (config == "tiny") {
     mc = {256, 2, 4, 2, 64, 768, 4096, 1.0e6f, 1.0e-6f};
-    lc = {4, 8.0f};
+    lc = {4, 8.0f, LLMCU_TARGETS_ATTN};
   } else {
     mc = {2048, 28, 16, 8, 128, 6144, 151936, 1.0e6f, 1.0e-6f};
-    lc = {16, 32.0f};
+    lc = {16, 32.0f, LLMCU_TARGETS_ATTN};
+  }
+  if (lora_rank > 0) lc.rank = lora_rank;
+  if (lora_alpha > 0.f) lc.alpha = lora_alpha;
+  {
+    static const char* kNames[LLMCU_P_COUNT] = {"wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"};
+    int mask = 0;
+    if (targets_arg == "attn") mask = LLMCU_TARGETS_ATTN;
+    else if (targets_arg == "mlp") mask = LLMCU_TARGETS_MLP;
+    else if (targets_arg == "all") mask = LLMCU_TARGETS_ALL;
+    else {
+      size_t pos = 0;
+      while (pos <= targets_arg.size()) {
+        const size_t comma = targets_arg.find(',', pos);
+        const std::string name = targets_arg.substr(pos, comma == std::string::npos ? std::string::npos : comma - pos);
+        int p = 0;
+        while (p < LLMCU_P_COUNT && name != kNames[p]) ++p;
+        if (p == LLMCU_P_COUNT) {
+          fprintf(stderr, "ERROR: unknown --lora-targets entry '%s'\n", name.c_str());
+          return 1;
+        }
+        mask |= 1 << p;
+        if (comma == std::string::npos) break;
+        pos = comma + 1;
+      }
+    }
+    lc.targets = mask;
   }
   llmcu_run_cfg rc = {batch, seq_len, int8 ? LLMCU_BASE_INT8 : LLMCU_BASE_FP16, 0};
   if (rank == 0)
-    printf("Training config: lr=%.2e steps=%d seq_len=%d batch=%d world=%d model=%s base=%s\n", lr, steps, seq_len,
-           batch, world, config.c_str(), int8 ? "int8" : "fp16");
+    printf("Training config: lr=%.2e steps=%d seq_len=%d batch=%d world=%d model=%s base=%s lora rank=%d "
+           "alpha=%g targets=0x%x\n",
+           lr, steps, seq_len, batch, world, config.c_str(), int8 ? "int8" : "fp16", lc.rank, lc.alpha, lc.targets);
 
   // training data (src/train.cu:195-214): int32 count + ids
   std::vector<int32_t> train;

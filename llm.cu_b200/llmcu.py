@@ -28,7 +28,19 @@ STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OOM", 4: "IO", 5: "NCCL", 6:
 
 T_EMBED, T_FINAL_NORM, T_ATTN_NORM, T_FFN_NORM, T_WQ, T_WK, T_WV, T_WO, T_Q_NORM, T_K_NORM, \
     T_W_GATE, T_W_UP, T_W_DOWN = range(13)
-P_Q, P_K, P_V, P_O = range(4)
+P_Q, P_K, P_V, P_O, P_GATE, P_UP, P_DOWN = range(7)
+TARGETS_ATTN, TARGETS_MLP, TARGETS_ALL = 0x0F, 0x70, 0x7F
+# adapter names (golden dict keys and lora_step file names), by projection id
+PROJ_NAMES = {P_Q: "wq", P_K: "wk", P_V: "wv", P_O: "wo", P_GATE: "w_gate", P_UP: "w_up", P_DOWN: "w_down"}
+
+
+def targets_mask(names) -> int:
+    """Target mask of an iterable of adapter names ("wq", ..., "w_down")."""
+    ids = {n: p for p, n in PROJ_NAMES.items()}
+    m = 0
+    for n in names:
+        m |= 1 << ids[n]
+    return m
 BASE_FP16, BASE_INT8 = 0, 1
 
 
@@ -45,7 +57,7 @@ class _ModelCfg(C.Structure):
 
 
 class _LoraCfg(C.Structure):
-    _fields_ = [("rank", C.c_int32), ("alpha", C.c_float)]
+    _fields_ = [("rank", C.c_int32), ("alpha", C.c_float), ("targets", C.c_int32)]
 
 
 class _RunCfg(C.Structure):
@@ -83,6 +95,10 @@ class Model:
 class Lora:
     rank: int = 16
     alpha: float = 32.0
+    targets: int = TARGETS_ATTN  # llmcu_lora_cfg.targets: bit p = projection p has an adapter
+
+    def projs(self):
+        return [p for p in PROJ_NAMES if (self.targets >> p) & 1]
 
 
 @dataclass(frozen=True)
@@ -110,6 +126,7 @@ _SIGS = {
     "llmcu_device_bytes": (C.c_size_t, [C.c_void_p]),
     "llmcu_stream": (C.c_void_p, [C.c_void_p]),
     "llmcu_lora_param_count": (C.c_int64, [C.c_void_p]),
+    "llmcu_lora_targets": (C.c_int32, [C.c_void_p]),
     "llmcu_ctx_create": (C.c_int, [C.POINTER(_ModelCfg), C.POINTER(_LoraCfg), C.POINTER(_RunCfg), C.c_int,
                                    C.POINTER(C.c_void_p)]),
     "llmcu_ctx_destroy": (None, [C.c_void_p]),
@@ -183,7 +200,7 @@ class Context:
         self.model, self.lora, self.run = model, lora, run
         mc = _ModelCfg(model.hidden, model.n_layers, model.n_heads, model.n_kv_heads, model.head_dim,
                        model.ffn, model.vocab, model.rope_theta, model.rms_eps)
-        lc = _LoraCfg(lora.rank, lora.alpha)
+        lc = _LoraCfg(lora.rank, lora.alpha, lora.targets)
         rc = _RunCfg(run.max_batch, run.max_seq, run.base_dtype, int(run.loss_all_positions))
         h = C.c_void_p()
         st = L.llmcu_ctx_create(C.byref(mc), C.byref(lc), C.byref(rc), device, C.byref(h))
@@ -226,6 +243,9 @@ class Context:
     def lora_param_count(self) -> int:
         return int(lib().llmcu_lora_param_count(self._h))
 
+    def lora_targets(self) -> int:
+        return int(lib().llmcu_lora_targets(self._h))
+
     def synchronize(self):
         self._check(lib().llmcu_synchronize(self._h), "synchronize")
 
@@ -256,8 +276,8 @@ class Context:
     def _dims(self, proj: int):
         m = self.model
         q, kv = m.n_heads * m.head_dim, m.n_kv_heads * m.head_dim
-        d_out = {P_Q: q, P_K: kv, P_V: kv, P_O: m.hidden}[proj]
-        d_in = q if proj == P_O else m.hidden
+        d_out = {P_Q: q, P_K: kv, P_V: kv, P_O: m.hidden, P_GATE: m.ffn, P_UP: m.ffn, P_DOWN: m.hidden}[proj]
+        d_in = {P_O: q, P_DOWN: m.ffn}.get(proj, m.hidden)
         return d_out, d_in
 
     def set_lora(self, layer: int, proj: int, A: np.ndarray, B: np.ndarray):
@@ -268,9 +288,9 @@ class Context:
         self._check(lib().llmcu_set_lora(self._h, layer, proj, _ptr(a), _ptr(b)), "set_lora")
 
     def set_lora_dict(self, lora: dict):
-        pid = {"wq": P_Q, "wk": P_K, "wv": P_V, "wo": P_O}
         for l in range(self.model.n_layers):
-            for p, i in pid.items():
+            for i in self.lora.projs():
+                p = PROJ_NAMES[i]
                 self.set_lora(l, i, lora[f"L{l}.{p}.A"], lora[f"L{l}.{p}.B"])
 
     def _get_pair(self, fn, layer, proj):
@@ -287,10 +307,10 @@ class Context:
         return self._get_pair(lib().llmcu_get_lora_grads, layer, proj)
 
     def _dict(self, getter):
-        names = {P_Q: "wq", P_K: "wk", P_V: "wv", P_O: "wo"}
         out = {}
         for l in range(self.model.n_layers):
-            for p, n in names.items():
+            for p in self.lora.projs():
+                n = PROJ_NAMES[p]
                 a, b = getter(l, p)
                 out[f"L{l}.{n}.A"], out[f"L{l}.{n}.B"] = a, b
         return out

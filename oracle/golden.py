@@ -16,6 +16,9 @@ It restates, in torch fp32 autograd on the CPU, the step that llm.cu's
 * causal GQA attention, scale 1/sqrt(hd) .. src/kernels/lora_forward.cu:60-118
 * SwiGLU  silu(g)*u ....................... src/kernels/activation.cu:9
 * LoRA    y += (alpha/r) * (x A^T) B^T .... src/kernels/lora.cu:190-198
+  (the reference adapts q/k/v/o only, include/lora.h:22-27; the same
+  formula on gate_proj / up_proj / down_proj when ``make_lora(projs=...)``
+  includes them -- a projection without adapter keys gets no LoRA term)
 * cross-entropy over positions 0..S-2 of
   each sequence (last position skipped) .. src/kernels/loss.cu:18-69
 * AdamW (decoupled weight decay) .......... src/kernels/lora.cu:212-219
@@ -55,6 +58,10 @@ import numpy as np
 import torch
 
 PROJS = ("wq", "wk", "wv", "wo")
+# MLP adapters: not in the reference (include/lora.h:22-27 fixes q/k/v/o); the
+# same y += s (x A^T) B^T on gate_proj, up_proj and down_proj.
+MLP_PROJS = ("w_gate", "w_up", "w_down")
+ALL_PROJS = PROJS + MLP_PROJS
 
 
 @dataclasses.dataclass(frozen=True)
@@ -90,11 +97,14 @@ class ModelCfg:
             "wk": (self.kv_dim, self.hidden),
             "wv": (self.kv_dim, self.hidden),
             "wo": (self.hidden, self.q_dim),
+            "w_gate": (self.ffn, self.hidden),
+            "w_up": (self.ffn, self.hidden),
+            "w_down": (self.hidden, self.ffn),
         }[proj]
 
-    def n_lora_params(self) -> int:
+    def n_lora_params(self, projs=PROJS) -> int:
         n = 0
-        for p in PROJS:
+        for p in projs:
             d_out, d_in = self.adapter_dims(p)
             n += self.lora_rank * (d_in + d_out)
         return n * self.n_layers
@@ -151,13 +161,14 @@ def make_base_weights(cfg: ModelCfg, seed: int, std: float = 0.02,
     return w
 
 
-def make_lora(cfg: ModelCfg, seed: int, b_std: float = 0.01) -> Dict[str, np.ndarray]:
-    """LoRA adapters: A ~ U(+-1/sqrt(in)) [r, in], B ~ N(0, b_std) [out, r]."""
+def make_lora(cfg: ModelCfg, seed: int, b_std: float = 0.01, projs=PROJS) -> Dict[str, np.ndarray]:
+    """LoRA adapters: A ~ U(+-1/sqrt(in)) [r, in], B ~ N(0, b_std) [out, r],
+    for the projections ``projs`` (default: the reference's q/k/v/o)."""
     rng = np.random.Generator(np.random.PCG64(seed))
     out: Dict[str, np.ndarray] = {}
     r = cfg.lora_rank
     for l in range(cfg.n_layers):
-        for p in PROJS:
+        for p in projs:
             d_out, d_in = cfg.adapter_dims(p)
             bound = 1.0 / math.sqrt(d_in)
             out[f"L{l}.{p}.A"] = rng.uniform(-bound, bound, size=(r, d_in)).astype(np.float32)
@@ -319,10 +330,10 @@ def _layers(cfg: ModelCfg, W: Dict[str, torch.Tensor], lora_add, tokens: np.ndar
         x = x + o @ W[p + "wo"].t() + lora_add(o, p + "wo")
         post_attn_last = x
         xn2 = rmsnorm(x, W[p + "ffn_norm"], eps)
-        g = xn2 @ W[p + "w_gate"].t()
-        u = xn2 @ W[p + "w_up"].t()
+        g = xn2 @ W[p + "w_gate"].t() + lora_add(xn2, p + "w_gate")
+        u = xn2 @ W[p + "w_up"].t() + lora_add(xn2, p + "w_up")
         act = _SwiGLURefBug.apply(g, u) if ref_bugs else torch.nn.functional.silu(g) * u
-        x = x + act @ W[p + "w_down"].t()
+        x = x + act @ W[p + "w_down"].t() + lora_add(act, p + "w_down")
     return x, post_attn_last
 
 
@@ -335,7 +346,10 @@ def forward_logits(cfg: ModelCfg, base: Dict[str, np.ndarray], lora: Dict[str, n
     W = {k: T(v) for k, v in base.items()}
     A = {k: T(v) for k, v in lora.items()}
     s_lora = cfg.lora_scale
-    lora_add = lambda x, name: ((x @ A[name + ".A"].t()) @ A[name + ".B"].t()) * s_lora
+    def lora_add(x, name):  # 0 for a projection without an adapter
+        if name + ".A" not in A:
+            return 0.0
+        return ((x @ A[name + ".A"].t()) @ A[name + ".B"].t()) * s_lora
     cos, sin = rope_tables(cfg, tokens.shape[1])
     with torch.no_grad():
         x, _ = _layers(cfg, W, lora_add, tokens, cos, sin)
@@ -387,6 +401,8 @@ def forward_backward(cfg: ModelCfg, base: Dict[str, np.ndarray], lora: Dict[str,
     cos, sin = rope_tables(cfg, S)
 
     def lora_add(x, name):
+        if name + ".A" not in params:  # a projection without an adapter
+            return 0.0
         A, Bm = params[name + ".A"], params[name + ".B"]
         h = _LoraDownRefBug.apply(x, A) if ref_bugs else x @ A.t()
         return (h @ Bm.t()) * s_lora
@@ -440,13 +456,13 @@ def zeros_like_lora(lora: Dict[str, np.ndarray]) -> Dict[str, np.ndarray]:
     return {k: np.zeros_like(a) for k, a in lora.items()}
 
 
-def algorithmic_flops_per_token(cfg: ModelCfg, seq: int) -> float:
+def algorithmic_flops_per_token(cfg: ModelCfg, seq: int, projs=PROJS) -> float:
     """4*N_lin + 3*(2*S*hd*nq*L) + 6*n_lora (forward + dX, causal attention, LoRA)."""
     per_layer = (cfg.q_dim * cfg.hidden + 2 * cfg.kv_dim * cfg.hidden + cfg.hidden * cfg.q_dim
                  + 3 * cfg.ffn * cfg.hidden)
     n_lin = cfg.n_layers * per_layer + cfg.vocab * cfg.hidden
     attn = 3 * (2 * seq * cfg.head_dim * cfg.n_heads * cfg.n_layers)
-    return float(4 * n_lin + attn + 6 * cfg.n_lora_params())
+    return float(4 * n_lin + attn + 6 * cfg.n_lora_params(projs))
 
 
 def rel_l2(a: np.ndarray, b: np.ndarray) -> float:

@@ -54,6 +54,9 @@ def test_ctx_create_rejects_unsupported_configs(llmcu):
         (llmcu.Model(256, 2, 4, 2, 64, 768, 4096), llmcu.Lora(32, 8.0), llmcu.Run(1, 32), 8),  # rank 32
         (llmcu.Model(256, 2, 4, 2, 64, 700, 4096), llmcu.Lora(4, 8.0), llmcu.Run(1, 32), 8),   # ffn % 128
         (llmcu.Model(256, 2, 4, 2, 64, 768, 4096), llmcu.Lora(4, 8.0), llmcu.Run(0, 32), 1),   # batch 0
+        (llmcu.Model(256, 2, 4, 2, 64, 768, 4096), llmcu.Lora(4, 8.0, 0x80), llmcu.Run(1, 32), 1),  # target bit 7
+        # MLP targets put their side columns on 256-column tile boundaries
+        (llmcu.Model(256, 2, 4, 2, 64, 640, 4096), llmcu.Lora(4, 8.0, llmcu.TARGETS_ALL), llmcu.Run(1, 32), 8),
     ]
     for model, lora, run, want in cases:
         with pytest.raises(llmcu.LlmcuError) as ei:

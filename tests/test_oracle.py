@@ -167,3 +167,45 @@ def test_dequant_gemm_restatement():
     c = dequant_gemm_nt(a, q, s)
     ref = a.astype(np.float64) @ (q.astype(np.float64) * s[:, None].astype(np.float64)).T
     np.testing.assert_allclose(c, ref, rtol=1e-5, atol=1e-5)
+
+
+def test_golden_mlp_adapters_equal_merged_base():
+    """The golden's LoRA terms on gate/up/down are the rank-r update of the
+    base weight: forward logits with adapters equal those of the base with
+    W + s B A folded in and no adapters on those projections."""
+    cfg = G.CFG_TINY
+    base = G.make_base_weights(cfg, 3)
+    lora = G.make_lora(cfg, 4, projs=G.ALL_PROJS, b_std=0.05)
+    tok, _ = G.make_tokens(cfg, 2, 24, 5)
+    got = G.forward_logits(cfg, base, lora, tok)
+    merged = {k: v.copy() for k, v in base.items()}
+    attn_only = {}
+    for k, v in lora.items():
+        l, p, ab = k.split(".")
+        if p in G.MLP_PROJS:
+            if ab == "A":
+                w = f"{l}.{p}"
+                merged[w] = merged[w] + cfg.lora_scale * (lora[f"{l}.{p}.B"] @ lora[f"{l}.{p}.A"])
+        else:
+            attn_only[k] = v
+    ref = G.forward_logits(cfg, merged, attn_only, tok)
+    assert G.rel_l2(got, ref) < 1e-5
+    # and the MLP terms are not empty
+    plain = G.forward_logits(cfg, base, attn_only, tok)
+    assert G.rel_l2(got, plain) > 1e-3
+
+
+def test_golden_target_subsets():
+    cfg = G.CFG_QWEN3_1P7B
+    assert cfg.n_lora_params() == 6_422_528                      # the reference's q/k/v/o
+    assert cfg.n_lora_params(G.MLP_PROJS) == 28 * 3 * 16 * (2048 + 6144)
+    tiny = G.CFG_TINY
+    lora = G.make_lora(tiny, 1, projs=("wk", "w_down"))
+    assert sorted({k.split(".")[1] for k in lora}) == ["w_down", "wk"]
+    assert lora["L0.w_down.A"].shape == (4, 768) and lora["L0.w_down.B"].shape == (256, 4)
+    # gradients exist exactly for the adapters present
+    base = G.make_base_weights(tiny, 2)
+    tok, tgt = G.make_tokens(tiny, 1, 16, 3)
+    res = G.forward_backward(tiny, base, lora, tok, tgt)
+    assert set(res.grads) == set(lora)
+    assert all(np.abs(g).sum() > 0 for g in res.grads.values())
