@@ -24,20 +24,22 @@ def main():
     ap.add_argument("--batch", type=int, default=2, help="sequences per rank")
     ap.add_argument("--seq", type=int, default=48)
     ap.add_argument("--seed", type=int, default=31)
+    ap.add_argument("--targets", default="wq,wk,wv,wo", help="adapted projections (comma list)")
     a = ap.parse_args()
+    projs = tuple(a.targets.split(","))
 
     from conftest import load_binding
     from oracle import golden as G
     llmcu = load_binding()
     cfg = G.CFG_TINY
     base = G.make_base_weights(cfg, a.seed, round_fp16=True)
-    lora = G.make_lora(cfg, a.seed + 1)
+    lora = G.make_lora(cfg, a.seed + 1, projs=projs)
     tok, tgt = G.make_tokens(cfg, a.batch * a.world, a.seq, a.seed + 2)
     rows = slice(a.rank * a.batch, (a.rank + 1) * a.batch)
     model = llmcu.Model(cfg.hidden, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab,
                         cfg.rope_theta, cfg.rms_eps)
-    ctx = llmcu.Context(model, llmcu.Lora(cfg.lora_rank, cfg.lora_alpha), llmcu.Run(a.batch, a.seq),
-                        device=a.rank)
+    ctx = llmcu.Context(model, llmcu.Lora(cfg.lora_rank, cfg.lora_alpha, llmcu.targets_mask(projs)),
+                        llmcu.Run(a.batch, a.seq), device=a.rank)
     ctx.set_base(base)
     ctx.set_lora_dict(lora)
     if a.rank == 0:

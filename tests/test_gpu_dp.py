@@ -23,8 +23,9 @@ def _n_gpus():
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-@pytest.mark.parametrize("world", [2])
-def test_dp_ranks_match_golden(llmcu, cuda_device, tmp_path, world):
+@pytest.mark.parametrize("world,projs", [(2, ("wq", "wk", "wv", "wo")),
+                                         (2, ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"))])
+def test_dp_ranks_match_golden(llmcu, cuda_device, tmp_path, world, projs):
     if _n_gpus() < world:
         pytest.skip(f"needs {world} GPUs")
     from oracle import golden as G
@@ -33,7 +34,8 @@ def test_dp_ranks_match_golden(llmcu, cuda_device, tmp_path, world):
     idfile = str(tmp_path / "nccl.id")
     procs = [subprocess.Popen([sys.executable, os.path.join(ROOT, "tests", "dp_rank.py"), "--rank", str(r),
                                "--world", str(world), "--idfile", idfile, "--out", str(tmp_path / f"r{r}.npz"),
-                               "--batch", str(batch), "--seq", str(seq), "--seed", str(seed)], env=env)
+                               "--batch", str(batch), "--seq", str(seq), "--seed", str(seed),
+                               "--targets", ",".join(projs)], env=env)
              for r in range(world)]
     for p in procs:
         assert p.wait(timeout=600) == 0
@@ -41,7 +43,7 @@ def test_dp_ranks_match_golden(llmcu, cuda_device, tmp_path, world):
 
     cfg = G.CFG_TINY
     base = G.make_base_weights(cfg, seed, round_fp16=True)
-    lora = G.make_lora(cfg, seed + 1)
+    lora = G.make_lora(cfg, seed + 1, projs=projs)
     tok, tgt = G.make_tokens(cfg, batch * world, seq, seed + 2)
     ref = G.forward_backward(cfg, base, lora, tok, tgt)
     upd = {k: a.copy() for k, a in lora.items()}
