@@ -71,6 +71,7 @@ struct llmcu_ctx {
   int64_t n_lora = 0;
   std::string err;
   cudaStream_t st = nullptr, comm = nullptr;
+  cudaStream_t side = nullptr;  // adapter-gradient launches, overlapped with the backward's main chain
   char* arena = nullptr;
   size_t arena_bytes = 0;
 
@@ -103,6 +104,7 @@ struct llmcu_ctx {
   float *dres = nullptr, *dq = nullptr, *dk = nullptr, *delta = nullptr;
   __half* dxn = nullptr;  // dX of the normed inputs (fp16, feeds the RMSNorm backward)
   __half *dres16 = nullptr, *dgu = nullptr, *dho = nullptr, *dattn = nullptr, *dqkv = nullptr, *dhq = nullptr;
+  __half* dres16m = nullptr;  // fp16 gradient at the attention block's output (the FFN norm backward's)
   __half *dhgu = nullptr, *dhd = nullptr;  // MLP targets: dY s B of gate | up and of down, [M, 64]
   // io
   int *tok = nullptr, *tgt = nullptr, *derr = nullptr;
@@ -134,6 +136,9 @@ struct llmcu_ctx {
   int timeout_ms = 60000;
   std::vector<cudaEvent_t> ev_layer;
   cudaEvent_t ev_comm_done = nullptr, ev_step_done = nullptr;
+  // per layer: main -> side before the MLP and attention adapter gradients,
+  // side -> main after each
+  std::vector<cudaEvent_t> ev_side;
 };
 
 namespace {
@@ -336,6 +341,7 @@ void carve(llmcu_ctx* c, Carver& cv) {
   c->d_xf = cv.take<float>(M * H);
   c->dres = cv.take<float>(M * H);
   c->dres16 = cv.take<__half>(M * H);
+  c->dres16m = cv.take<__half>(M * H);
   c->dxn = cv.take<__half>(M * H);
   c->dgu = cv.take<__half>(M * 2 * I);
   c->dho = cv.take<__half>(M * 64);
@@ -633,10 +639,42 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   TIMED(P_NORM, rmsnorm_backward(ctx->d_xf, xfinal, ctx->final_norm, ctx->dres, ctx->dres16, M, H, eps, 0, st));
 
   // ----------------------------------------------------------- backward
+  // The adapter gradients of a layer run on ctx->side, beside the main chain:
+  // the main stream hands its inputs over with an event, and waits for the
+  // side's event only before it overwrites what they read (the MLP batch reads
+  // dres16, rewritten by the layer's attention-norm backward; the attention
+  // batch reads dres16m, dho, dqkv and dhq, rewritten from the next layer's
+  // FFN-norm backward on).  A kernel that follows an event wait is launched
+  // without programmatic dependence.  With profiling on, everything stays on
+  // the main stream so that the per-class times stay separable.
+  cudaStream_t gs = ctx->prof_on ? st : ctx->side;
+  const bool split = gs != st;
+  auto ev_side = [&](int l, int k) { return ctx->ev_side[4 * l + k]; };  // 0/1 MLP in/out, 2/3 attention in/out
+  auto side_grad = [&](int l, int k, const LoraGradBatch& gb) -> llmcu_status {
+    if (split) {
+      CK(cudaEventRecord(ev_side(l, k), st));
+      CK(cudaStreamWaitEvent(gs, ev_side(l, k), 0));
+    }
+    set_pdl(!split);
+    TIMED(P_LORA_GRAD, lora_grad(gb, M, gs));
+    set_pdl(true);
+    if (split) CK(cudaEventRecord(ev_side(l, k + 1), gs));
+    return LLMCU_OK;
+  };
+  // true when the next main-stream kernel follows an event wait
+  auto wait_side = [&](int l, int k) -> llmcu_status {
+    if (split) {
+      CK(cudaStreamWaitEvent(st, ev_side(l, k), 0));
+      set_pdl(false);
+    }
+    return LLMCU_OK;
+  };
   for (int l = ctx->L - 1; l >= 0; --l) {
     LayerW& w = ctx->lw[l];
     LayerA& a = ctx->la[l];
     float* G = ctx->lg + d.per_layer * l;
+    auto gp = [&](int p, bool b_side) { return d.has(p) ? G + (b_side ? d.offB(p) : d.offA(p)) : nullptr; };
+    const float sb = d.scale * unscale;
     if (d.has_mlp()) {
       {  // [d_act | dh_d] = dres . md (MN-major), SwiGLU backward fused into dgu
         EpiArgs ea;
@@ -659,10 +697,8 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
         TIMED(P_GEMM, gemm(op(ctx->dgu, M, 2 * I, 2 * I), op_mn(w.mgu, 2 * I, H + 64, H + 64), M, H + 64,
                            Epi::kStoreF16, ea, err, st));
       }
-      // the MLP adapters' gradients while dres16 still holds the layer-output gradient
+      // the MLP adapters' gradients; dres16 holds the layer-output gradient
       LoraGradBatch gb{};
-      const float sb = d.scale * unscale;
-      auto gp = [&](int p, bool b_side) { return d.has(p) ? G + (b_side ? d.offB(p) : d.offA(p)) : nullptr; };
       // dB_d[h, j] = s sum_m dres[m, h] h_d[m, j];  dA_d[j, i] = sum_m dh_d[m, j] act[m, i]
       if (d.has(kPDown)) {
         gb.p[gb.n++] = LoraGradProb{ctx->dres16, H, a.hd, 64, {gp(kPDown, true)}, 1, r, 1, H, r, sb, 0};
@@ -678,7 +714,7 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       }
       gb.a_max = 0;
       for (int i = 0; i < gb.n; ++i) gb.a_max = std::max(gb.a_max, gb.p[i].A);
-      TIMED(P_LORA_GRAD, lora_grad(gb, M, st));
+      CKS(side_grad(l, 0, gb));
     } else {
       // MLP: d_act = dres . W_down (MN-major), SwiGLU backward fused
       const __half* wd = base_weight(ctx, w.wd, w.q_d, w.s_d, H, I, &e);
@@ -696,7 +732,10 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       TIMED(P_GEMM, gemm(op(ctx->dgu, M, 2 * I, 2 * I), op_mn(wgu, 2 * I, H, H), M, H, Epi::kStoreF16,
                          EpiArgs{ctx->dxn, H}, err, st));
     }
-    TIMED(P_NORM, rmsnorm_backward(ctx->dxn, a.resid_mid, w.ffn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
+    // the layer above's attention-adapter gradients read dres16m, dho, dqkv, dhq
+    if (l + 1 < ctx->L) CKS(wait_side(l + 1, 3));
+    TIMED(P_NORM, rmsnorm_backward(ctx->dxn, a.resid_mid, w.ffn_norm, ctx->dres, ctx->dres16m, M, H, eps, 1, st));
+    set_pdl(true);
     // O projection
     {  // [dattn | dh_o] = dres . mo (MN-major): dres W'_o and dres s B_o, plus delta = rowsum(dO * O) per head
       EpiArgs ea;
@@ -711,8 +750,8 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       ea.seq = S;
       ea.n_heads = ctx->nh;
       ea.head_dim = ctx->hd;
-      TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op_mn(w.mo, H, Q + 64, Q + 64), M, Q + 64, Epi::kStoreF16Delta, ea,
-                         err, st));
+      TIMED(P_GEMM, gemm(op(ctx->dres16m, M, H, H), op_mn(w.mo, H, Q + 64, Q + 64), M, Q + 64, Epi::kStoreF16Delta,
+                         ea, err, st));
     }
     // attention
     // (delta came with the O-projection dX GEMM)
@@ -733,12 +772,9 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
                          err, st));
     }
     {
-      // all six adapter gradients of the layer in one launch (the O
-      // projection's inputs -- dres16, attn, h_o, dh_o -- are still intact here)
+      // the attention adapters' gradients of the layer in one launch
       LoraGradBatch gb{};
       gb.a_max = ctx->lpart_amax;
-      const float sb = d.scale * unscale;
-      auto gp = [&](int p, bool b_side) { return d.has(p) ? G + (b_side ? d.offB(p) : d.offA(p)) : nullptr; };
       if (d.has(kPQ)) gb.p[gb.n++] = LoraGradProb{ctx->dqkv, QKV, a.hq, 64, {gp(kPQ, true)}, 1, r, 1, Q, r, sb, 0};
       if (d.has(kPK))
         gb.p[gb.n++] = LoraGradProb{ctx->dqkv + Q, QKV, a.hq + kSegK, 64, {gp(kPK, true)}, 1, r, 1, KV, r, sb, 0};
@@ -749,22 +785,38 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
         gb.p[gb.n++] = LoraGradProb{a.xn, H, ctx->dhq, 64, {gp(kPQ, false), gp(kPK, false), gp(kPV, false)}, 3, 1, H,
                                     H, r, unscale, 0};
       if (d.has(kPO)) {
-        // dBo[h, j] = s * sum_m dres[m, h] ho[m, j]
-        gb.p[gb.n++] = LoraGradProb{ctx->dres16, H, a.ho, 64, {gp(kPO, true)}, 1, r, 1, H, r, sb, 0};
+        // dBo[h, j] = s * sum_m dres[m, h] ho[m, j] (dres at the attention block's output)
+        gb.p[gb.n++] = LoraGradProb{ctx->dres16m, H, a.ho, 64, {gp(kPO, true)}, 1, r, 1, H, r, sb, 0};
         // dAo[j, q] = sum_m dho[m, j] attn[m, q]
         gb.p[gb.n++] = LoraGradProb{a.attn, Q, ctx->dho, 64, {gp(kPO, false)}, 1, 1, Q, Q, r, unscale, 0};
       }
-      if (gb.n) TIMED(P_LORA_GRAD, lora_grad(gb, M, st));
+      if (gb.n) {
+        CKS(side_grad(l, 2, gb));
+      } else if (split) {  // keep the layer's "done" event meaningful
+        CK(cudaEventRecord(ev_side(l, 2), st));
+        CK(cudaStreamWaitEvent(gs, ev_side(l, 2), 0));
+        CK(cudaEventRecord(ev_side(l, 3), gs));
+      }
     }
+    // the MLP batch reads dres16, which the attention-norm backward rewrites
+    if (d.has_mlp()) CKS(wait_side(l, 1));
     TIMED(P_NORM, rmsnorm_backward(ctx->dxn, ctx->resid[l], w.attn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
+    set_pdl(true);
     if (ctx->nccl) {
-      CK(cudaEventRecord(ctx->ev_layer[l], st));
-      CK(cudaStreamWaitEvent(ctx->comm, ctx->ev_layer[l], 0));
+      // the layer's gradients are complete once its last side launch is
+      cudaEvent_t done = ctx->ev_layer[l];
+      if (split) {
+        done = ev_side(l, 3);
+      } else {
+        CK(cudaEventRecord(done, st));
+      }
+      CK(cudaStreamWaitEvent(ctx->comm, done, 0));
       CKS(nccl_wait(ctx, ncclAllReduce(G, G, static_cast<size_t>(d.per_layer), ncclFloat, ncclSum, ctx->nccl,
                                        ctx->comm),
                     "allreduce of layer gradients"));
     }
   }
+  if (split) CK(cudaStreamWaitEvent(st, ev_side(0, 3), 0));  // every gradient is in place before AdamW
   // loss: sum over valid rows (over all ranks) / number of valid rows; the
   // final kernel may follow an event wait, so it is launched normally
   set_pdl(false);
@@ -880,6 +932,7 @@ llmcu_status llmcu_ctx_create(const llmcu_model_cfg* model, const llmcu_lora_cfg
   if (cudaSetDevice(device) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
   if (cudaStreamCreateWithFlags(&ctx->st, cudaStreamNonBlocking) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
   if (cudaStreamCreateWithFlags(&ctx->comm, cudaStreamNonBlocking) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
+  if (cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
   Carver probe;
   carve(ctx, probe);
   ctx->arena_bytes = probe.off + 256;
@@ -893,6 +946,9 @@ llmcu_status llmcu_ctx_create(const llmcu_model_cfg* model, const llmcu_lora_cfg
   carve(ctx, cv);
   ctx->ev_layer.assign(ctx->L, nullptr);
   for (auto& ev : ctx->ev_layer)
+    if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
+  ctx->ev_side.assign(4 * ctx->L, nullptr);
+  for (auto& ev : ctx->ev_side)
     if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
   if (cudaEventCreateWithFlags(&ctx->ev_comm_done, cudaEventDisableTiming) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
   if (cudaEventCreateWithFlags(&ctx->ev_step_done, cudaEventDisableTiming) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
@@ -917,8 +973,11 @@ void llmcu_ctx_destroy(llmcu_ctx* ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->st) cudaStreamSynchronize(ctx->st);
   if (ctx->comm) cudaStreamSynchronize(ctx->comm);
+  if (ctx->side) cudaStreamSynchronize(ctx->side);
   if (ctx->nccl) ncclCommDestroy(ctx->nccl);
   for (auto ev : ctx->ev_layer)
+    if (ev) cudaEventDestroy(ev);
+  for (auto ev : ctx->ev_side)
     if (ev) cudaEventDestroy(ev);
   for (auto ev : ctx->prof_ev)
     if (ev) cudaEventDestroy(ev);
@@ -928,6 +987,7 @@ void llmcu_ctx_destroy(llmcu_ctx* ctx) {
   if (ctx->arena) cudaFree(ctx->arena);
   if (ctx->st) cudaStreamDestroy(ctx->st);
   if (ctx->comm) cudaStreamDestroy(ctx->comm);
+  if (ctx->side) cudaStreamDestroy(ctx->side);
   delete ctx;
 }
 
@@ -936,6 +996,7 @@ llmcu_status llmcu_synchronize(llmcu_ctx* ctx) {
   CK(cudaSetDevice(ctx->device));
   CK(cudaStreamSynchronize(ctx->st));
   CK(cudaStreamSynchronize(ctx->comm));
+  CK(cudaStreamSynchronize(ctx->side));
   return LLMCU_OK;
 }
 
