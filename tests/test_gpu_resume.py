@@ -6,8 +6,9 @@ fresh context from those files must take step 3 as the uninterrupted run
 does.  The step's gradient sums are not bit-reproducible (fp32 atomics and
 TMA reduce-adds in no fixed order, whose last-bit differences can flip an
 fp16 rounding downstream), so two identical runs agree to about 1e-3 in the
-gradients and AdamW moments and far closer in the adapters; the checks use
-1e-4 on adapters and 1e-2 (the gradient parity bound) on moments.  The
+gradients and AdamW moments and to about 1e-4 in the adapters (1.3e-4 was
+the worst of three identical 4-step driver runs on a B200); the checks use
+1e-3 on adapters and 1e-2 (the gradient parity bound) on moments.  The
 sidecar refuses a context of another shape, and the C++ driver's --resume
 continues a synthetic run to the same adapters."""
 import os
@@ -31,7 +32,7 @@ def _ctx(llmcu, G, cfg, batch, seq, seed, lora_seed=None):
     return ctx
 
 
-def _close(a, b, rtol=1e-4):
+def _close(a, b, rtol=1e-3):
     for k in a:
         d = np.linalg.norm(a[k] - b[k]) / max(np.linalg.norm(b[k]), 1e-30)
         assert d <= rtol, (k, d)
@@ -109,7 +110,7 @@ def test_driver_resume_matches_uninterrupted_run(cuda_device, tmp_path):
     for f in names:
         x = np.fromfile(full / f, dtype=np.float32)
         y = np.fromfile(part / f, dtype=np.float32)
-        tol = 1e-4
+        tol = 1e-3
         if f.endswith("_adamw.bin"):
             x, y = x[16:], y[16:]  # past the 64-byte header
             tol = 1e-2
