@@ -6,9 +6,12 @@ fresh context from those files must take step 3 as the uninterrupted run
 does.  The step's gradient sums are not bit-reproducible (fp32 atomics and
 TMA reduce-adds in no fixed order, whose last-bit differences can flip an
 fp16 rounding downstream), so two identical runs agree to about 1e-3 in the
-gradients and AdamW moments and to about 1e-4 in the adapters (1.3e-4 was
-the worst of three identical 4-step driver runs on a B200); the checks use
-1e-3 on adapters and 1e-2 (the gradient parity bound) on moments.  The
+gradients and AdamW moments.  In the adapters most elements agree to ~1e-4,
+but an element whose gradient sits at the noise floor can take Adam's
+~lr * sign(g) step in the other direction (2 lr apart: 1.9e-3 relative on a
+tiny-shape B once in a handful of runs).  The checks therefore use 1e-2 (the
+gradient parity bound) on adapters and on moments -- a resume that lost the
+moments would miss the first two steps' share of m (tens of percent).  The
 sidecar refuses a context of another shape, and the C++ driver's --resume
 continues a synthetic run to the same adapters."""
 import os
@@ -32,7 +35,7 @@ def _ctx(llmcu, G, cfg, batch, seq, seed, lora_seed=None):
     return ctx
 
 
-def _close(a, b, rtol=1e-3):
+def _close(a, b, rtol=1e-2):
     for k in a:
         d = np.linalg.norm(a[k] - b[k]) / max(np.linalg.norm(b[k]), 1e-30)
         assert d <= rtol, (k, d)
@@ -53,18 +56,29 @@ def test_resume_continues_the_run(llmcu, cuda_device, tmp_path):
     a.train_step(toks[2][0], toks[2][1], opt, 3)
     want = a.lora_dict()
 
+    def moments(ctx, name):  # (m, v) after step 3, through the sidecar writer
+        d = tmp_path / name
+        d.mkdir()
+        ctx.save_adamw_state(str(d), 3)
+        raw = np.fromfile(d / "lora_step3_adamw.bin", dtype=np.float32)[16:]
+        return raw[: raw.size // 2], raw[raw.size // 2:]
+
+    m_want, v_want = moments(a, "a")
     b = _ctx(llmcu, G, cfg, batch, seq, seed, lora_seed=seed + 100)  # other adapters before the load
     b.load_lora(str(tmp_path), 2)
     b.load_adamw_state(str(tmp_path), 2)
     b.train_step(toks[2][0], toks[2][1], opt, 3)
     _close(b.lora_dict(), want)
+    m_b, v_b = moments(b, "b")
+    assert G.rel_l2(m_b, m_want) <= 1e-2 and G.rel_l2(v_b, v_want) <= 1e-2
 
-    # without the moments the same step lands elsewhere
+    # without the moments the step starts Adam afresh: m lacks the first two
+    # steps' share (beta1 weights them 0.9 and 0.81)
     c = _ctx(llmcu, G, cfg, batch, seq, seed)
     c.load_lora(str(tmp_path), 2)
     c.train_step(toks[2][0], toks[2][1], opt, 3)
-    got = c.lora_dict()
-    assert any(np.linalg.norm(got[k] - want[k]) > 1e-3 * np.linalg.norm(want[k]) for k in want)
+    m_c, _ = moments(c, "c")
+    assert G.rel_l2(m_c, m_want) > 0.1
 
 
 def test_sidecar_refuses_other_shapes(llmcu, cuda_device, tmp_path):
@@ -110,7 +124,7 @@ def test_driver_resume_matches_uninterrupted_run(cuda_device, tmp_path):
     for f in names:
         x = np.fromfile(full / f, dtype=np.float32)
         y = np.fromfile(part / f, dtype=np.float32)
-        tol = 1e-3
+        tol = 1e-2
         if f.endswith("_adamw.bin"):
             x, y = x[16:], y[16:]  # past the 64-byte header
             tol = 1e-2
