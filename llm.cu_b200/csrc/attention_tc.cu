@@ -608,7 +608,7 @@ template <int HD>
 cudaError_t bwd_tc_launch(const __half* q, const __half* k, const __half* v, const __half* dout, const float* lse,
                           const float* delta, float* dq, float* dk, __half* dv, int B, int S, int nh, int nkv,
                           int ldq, int ldk, int ldv, int ldo, int lddq, int lddk, int lddv, int* err,
-                          cudaStream_t st) {
+                          cudaStream_t st, bool dq_zeroed) {
   using L = BwdLayout<HD>;
   CUtensorMap mq, mk, mv, mo, mdq;
   if (!tile_map(&mq, q, B * S, nh * HD, ldq) || !tile_map(&mk, k, B * S, nkv * HD, ldk) ||
@@ -622,9 +622,11 @@ cudaError_t bwd_tc_launch(const __half* q, const __half* k, const __half* v, con
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  // dQ accumulates partial products of every key tile
-  cudaError_t e = fill_f32_2d(dq, lddq, B * S, nh * HD, 0.f, st);
-  if (e != cudaSuccess) return e;
+  // dQ accumulates partial products of every key tile (into zeros)
+  if (!dq_zeroed) {
+    cudaError_t e = fill_f32_2d(dq, lddq, B * S, nh * HD, 0.f, st);
+    if (e != cudaSuccess) return e;
+  }
   dim3 grid(nkv, B, (S + 127) / 128);
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));
   launch_pdl(kern, grid, 192, L::kBytes, st, mq, mk, mv, mo, mdq, lse, delta, dk, dv, S, nh, nkv, lddk, lddv, scale,
@@ -661,13 +663,13 @@ cudaError_t fwd_tc_launch(const __half* q, const __half* k, const __half* v, __h
 cudaError_t attention_backward_tc(const __half* q, const __half* k, const __half* v, const __half* dout,
                                   const float* lse, const float* delta, float* dq, float* dk, __half* dv, int B, int S,
                                   int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int lddq, int lddk,
-                                  int lddv, int* err, cudaStream_t st) {
+                                  int lddv, int* err, cudaStream_t st, bool dq_zeroed) {
   if (hd == 128)
     return bwd_tc_launch<128>(q, k, v, dout, lse, delta, dq, dk, dv, B, S, nh, nkv, ldq, ldk, ldv, ldo, lddq, lddk,
-                              lddv, err, st);
+                              lddv, err, st, dq_zeroed);
   if (hd == 64)
     return bwd_tc_launch<64>(q, k, v, dout, lse, delta, dq, dk, dv, B, S, nh, nkv, ldq, ldk, ldv, ldo, lddq, lddk,
-                             lddv, err, st);
+                             lddv, err, st, dq_zeroed);
   return cudaErrorInvalidValue;
 }
 

@@ -47,10 +47,12 @@ cudaError_t attention_backward(const __half* q, const __half* k, const __half* v
                                const __half* dout, const float* lse, float* delta, float* dq, float* dk, __half* dv,
                                int B, int S, int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int lddq,
                                int lddk, int lddv, int* err, cudaStream_t st);
+// dq accumulates with reduce-adds: it is zeroed first unless the caller
+// already did (dq_zeroed).
 cudaError_t attention_backward_tc(const __half* q, const __half* k, const __half* v, const __half* dout,
                                   const float* lse, const float* delta, float* dq, float* dk, __half* dv, int B, int S,
                                   int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int lddq, int lddk,
-                                  int lddv, int* err, cudaStream_t st);
+                                  int lddv, int* err, cudaStream_t st, bool dq_zeroed = false);
 
 // ---- gemm.cu
 // Column slices per GEMM tile (epilogue warps per TMEM lane quadrant); the

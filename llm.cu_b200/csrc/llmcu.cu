@@ -136,6 +136,7 @@ struct llmcu_ctx {
   int timeout_ms = 60000;
   std::vector<cudaEvent_t> ev_layer;
   cudaEvent_t ev_comm_done = nullptr, ev_step_done = nullptr;
+  cudaEvent_t ev_dq_in = nullptr, ev_dq_done = nullptr;  // dq zeroed on the side stream
   // per layer: main -> side before the MLP and attention adapter gradients,
   // side -> main after each
   std::vector<cudaEvent_t> ev_side;
@@ -669,6 +670,19 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     }
     return LLMCU_OK;
   };
+  // dq (the attention backward's fp32 reduce-add target) is zeroed on the
+  // side stream: for the top layer while the lm_head backward runs, for each
+  // lower layer once the layer above has read it
+  auto zero_dq_side = [&]() -> llmcu_status {
+    CK(cudaEventRecord(ctx->ev_dq_in, st));
+    CK(cudaStreamWaitEvent(gs, ctx->ev_dq_in, 0));
+    set_pdl(false);
+    CK(fill_f32_2d(ctx->dq, Q, M, Q, 0.f, gs));
+    set_pdl(true);
+    CK(cudaEventRecord(ctx->ev_dq_done, gs));
+    return LLMCU_OK;
+  };
+  if (split) CKS(zero_dq_side());
   for (int l = ctx->L - 1; l >= 0; --l) {
     LayerW& w = ctx->lw[l];
     LayerA& a = ctx->la[l];
@@ -755,11 +769,18 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     }
     // attention
     // (delta came with the O-projection dX GEMM)
-    TIMEDN(P_ATTN_BWD, 2, attention_backward_tc(a.qkr, a.qkr + Q, a.qkv + Q + KV, ctx->dattn, a.lse, ctx->delta, ctx->dq,
-                                            ctx->dk, ctx->dqkv + Q + KV, B, S, ctx->nh, ctx->nkv, ctx->hd, Q + KV, Q + KV,
-                                            QKV, Q, Q, KV, QKV, err, st));
+    if (split) {  // dq was zeroed on the side stream
+      CK(cudaStreamWaitEvent(st, ctx->ev_dq_done, 0));
+      set_pdl(false);
+    }
+    TIMEDN(P_ATTN_BWD, split ? 1 : 2,
+           attention_backward_tc(a.qkr, a.qkr + Q, a.qkv + Q + KV, ctx->dattn, a.lse, ctx->delta, ctx->dq, ctx->dk,
+                                 ctx->dqkv + Q + KV, B, S, ctx->nh, ctx->nkv, ctx->hd, Q + KV, Q + KV, QKV, Q, Q, KV,
+                                 QKV, err, st, split));
+    set_pdl(true);
     TIMED(P_NORM, qknorm_rope_backward(ctx->dq, ctx->dk, a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, ctx->dqkv,
                             B, S, ctx->nh, ctx->nkv, ctx->hd, eps, st));
+    if (split && l > 0) CKS(zero_dq_side());  // for the next layer, once read
     // QKV projection
     {  // [dxn | dh_qkv] = dqkv . mqkv (MN-major)
       EpiArgs ea;
@@ -951,6 +972,8 @@ llmcu_status llmcu_ctx_create(const llmcu_model_cfg* model, const llmcu_lora_cfg
   for (auto& ev : ctx->ev_side)
     if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
   if (cudaEventCreateWithFlags(&ctx->ev_comm_done, cudaEventDisableTiming) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
+  if (cudaEventCreateWithFlags(&ctx->ev_dq_in, cudaEventDisableTiming) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
+  if (cudaEventCreateWithFlags(&ctx->ev_dq_done, cudaEventDisableTiming) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
   if (cudaEventCreateWithFlags(&ctx->ev_step_done, cudaEventDisableTiming) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
   // zero everything once (adapters A = B = 0, moments 0), norms = 1
   if (cudaMemsetAsync(ctx->arena, 0, ctx->arena_bytes, ctx->st) != cudaSuccess) return bail(LLMCU_ERR_CUDA);
@@ -982,6 +1005,8 @@ void llmcu_ctx_destroy(llmcu_ctx* ctx) {
   for (auto ev : ctx->prof_ev)
     if (ev) cudaEventDestroy(ev);
   if (ctx->ev_comm_done) cudaEventDestroy(ctx->ev_comm_done);
+  if (ctx->ev_dq_in) cudaEventDestroy(ctx->ev_dq_in);
+  if (ctx->ev_dq_done) cudaEventDestroy(ctx->ev_dq_done);
   if (ctx->ev_step_done) cudaEventDestroy(ctx->ev_step_done);
   if (ctx->dec_graph) cudaGraphExecDestroy(ctx->dec_graph);
   if (ctx->arena) cudaFree(ctx->arena);
