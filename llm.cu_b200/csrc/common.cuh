@@ -128,6 +128,11 @@ struct EpiArgs {
 cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, const EpiArgs& ea, int* err,
                  cudaStream_t st, int bn_hint = 0);
 int gemm_num_sms();
+// Split-K fix-up workspace for the calling thread's gemm() calls (null: off):
+// ws_floats fp32 partials and cnt_n counters that must be zero (the GEMMs
+// leave them zero).  GEMMs whose tiles fill under half a wave then run as K
+// splits whose last arrival per tile finishes it.
+void set_gemm_workspace(float* ws, size_t ws_floats, int* cnt, int cnt_n);
 // fp16 [rows, cols] row-major (row stride ld elements), 128-byte swizzle,
 // box 64 columns x box_rows rows.
 bool encode_tma_2d_f16(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, int box_rows);

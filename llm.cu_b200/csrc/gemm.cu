@@ -3,6 +3,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 
 #include "common.cuh"
@@ -179,6 +180,21 @@ bool encode_tma_2d_f16(CUtensorMap* map, const void* ptr, int rows, int cols, in
   return make_map(map, op, box_rows);
 }
 
+namespace {
+// split-K fix-up workspace of the calling host thread (set_gemm_workspace)
+thread_local float* t_fx_ws = nullptr;
+thread_local size_t t_fx_ws_floats = 0;
+thread_local int* t_fx_cnt = nullptr;
+thread_local int t_fx_cnt_n = 0;
+}  // namespace
+
+void set_gemm_workspace(float* ws, size_t ws_floats, int* cnt, int cnt_n) {
+  t_fx_ws = ws;
+  t_fx_ws_floats = ws_floats;
+  t_fx_cnt = cnt;
+  t_fx_cnt_n = cnt_n;
+}
+
 cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, const EpiArgs& ea, int* err,
                  cudaStream_t st, int bn_hint) {
   std::call_once(g_once, init_once);
@@ -264,11 +280,39 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
   sh.n_main = n_main;
   sh.side = ea.side;
   sh.ld_side = ea.ld_side;
+  sh.fixup = 0;
+  sh.fx_ws = nullptr;
+  sh.fx_cnt = nullptr;
   if (ea.ksplit > 1) {  // K slices reduce-add into the same rows
     const int nk = sh.kb_per_split;
     const int kbps = (nk + ea.ksplit - 1) / ea.ksplit;
     sh.kb_per_split = kbps;
     sh.splits = (nk + kbps - 1) / kbps;
+  } else if (t_fx_ws && epi != Epi::kCEProbs) {
+    // tiles that fill under half a wave: K splits with a fix-up, about one
+    // wave of units, at least two 64-deep K blocks each
+    const int slots = CG == 2 ? g_num_sms / 2 : g_num_sms;
+    const int nk = sh.kb_per_split;
+    if (2 * sh.num_tiles <= slots && nk >= 4) {
+      // the last split of a tile reads the others' 128 x BN fp32 partials
+      // (about 2.7 K blocks' worth of loads each): splits ~ sqrt(K blocks / 2.7)
+      const int balance = std::max(2, static_cast<int>(std::lround(std::sqrt(nk / 2.7))));
+      int want = std::min({slots / sh.num_tiles, nk / 2, balance, 16});
+      const int groups = (BN >= 128 ? 4 * kGemmEpiGroups : 4) / 4;
+      const size_t per_split = static_cast<size_t>(sh.num_tiles) * CG * kBlockM * BN;  // floats
+      const int cnt = sh.num_tiles * CG * 4 * groups;
+      while (want > 1 && per_split * want > t_fx_ws_floats) --want;
+      if (want > 1 && cnt <= t_fx_cnt_n) {
+        const int kbps = (nk + want - 1) / want;
+        sh.kb_per_split = kbps;
+        sh.splits = (nk + kbps - 1) / kbps;
+        if (sh.splits > 1) {
+          sh.fixup = 1;
+          sh.fx_ws = t_fx_ws;
+          sh.fx_cnt = t_fx_cnt;
+        }
+      }
+    }
   }
   if (CG == 2) {
     if (B.mn) return dispatch<256, true, 2>(epi, ea, maps, sh, err, st);

@@ -48,6 +48,14 @@ struct GemmShape {
   int n_main;           // columns [n_main, N) go to the side output
   __half* side;         // [M, N - n_main] fp16, row stride ld_side
   int ld_side;
+  // K splits with a fix-up (fixup != 0, splits > 1): every split of a tile
+  // leaves its fp32 partial of each epilogue warp's slice in fx_ws; the last
+  // split to arrive (counted in fx_cnt, one counter per slice, reset by that
+  // split) adds the others' partials into its TMEM accumulator and runs the
+  // tile's epilogue as usual -- for GEMMs whose tiles fill under half a wave
+  int fixup;
+  float* fx_ws;         // [tiles * CG * 4 * groups][splits][slice columns / 4][32] float4
+  int* fx_cnt;          // [tiles * CG * 4 * groups], zero between launches
 };
 
 constexpr int kBlockM = 128;
@@ -929,7 +937,79 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
         Epi::begin(st, ep, c, slot);
       if (!mbar_wait(&acc_full[acc], (i >> 1) & 1, abort_flag, err, kErrWaitAccum)) break;
       tc_fence_after();
-      if constexpr (epi_tmem_direct<Epi>::value) {
+      bool run = true;  // false: another K split of this tile finishes it
+      if (sh.fixup) {
+        // this warp's slice of the tile: kSliceCols accumulator columns, in
+        // 32-column chunks (the paired epilogue reads gate columns and the
+        // matching up columns 128 further)
+        constexpr int kSliceCols = BN / kGroups;
+        auto col_of = [&](int q) -> int {
+          if constexpr (Epi::kPaired) {
+            constexpr int kPairChunks = 128 / kGroups / 32;
+            return q < kPairChunks ? cgrp * (128 / kGroups) + 32 * q : 128 + cgrp * (128 / kGroups) + 32 * (q - kPairChunks);
+          } else {
+            return cgrp * kSliceCols + 32 * q;
+          }
+        };
+        const int wslot = ((tile * CG + static_cast<int>(rank)) * 4 + ew) * kGroups + cgrp;
+        // a split's partial: [chunk q][column quad][lane] float4, so that
+        // each warp access moves 512 contiguous bytes
+        float4* wsb = reinterpret_cast<float4*>(sh.fx_ws) + static_cast<size_t>(wslot) * sh.splits * (8 * kSliceCols);
+        float4* mine = wsb + static_cast<size_t>(sp) * (8 * kSliceCols);
+#pragma unroll 1
+        for (int q = 0; q < kSliceCols / 32; ++q) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tbase + col_of(q), v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            __stcg(mine + (8 * q + j) * 32 + lane, make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                                              __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])));
+        }
+        __threadfence();
+        __syncwarp();
+        int prev = 0;
+        if (lane == 0) prev = atomicAdd(sh.fx_cnt + wslot, 1);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        run = prev == sh.splits - 1;
+        if (run) {
+          __threadfence();
+#pragma unroll 1
+          for (int q = 0; q < kSliceCols / 32; ++q) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tbase + col_of(q), v);
+            float4 a[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int s2 = 0; s2 < sh.splits; ++s2) {
+              if (s2 == sp) continue;
+              const float4* o = wsb + static_cast<size_t>(s2) * (8 * kSliceCols) + 8 * q * 32 + lane;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 t = __ldcg(o + 32 * j);
+                a[j].x += t.x;
+                a[j].y += t.y;
+                a[j].z += t.z;
+                a[j].w += t.w;
+              }
+            }
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              v[4 * j] = __float_as_uint(__uint_as_float(v[4 * j]) + a[j].x);
+              v[4 * j + 1] = __float_as_uint(__uint_as_float(v[4 * j + 1]) + a[j].y);
+              v[4 * j + 2] = __float_as_uint(__uint_as_float(v[4 * j + 2]) + a[j].z);
+              v[4 * j + 3] = __float_as_uint(__uint_as_float(v[4 * j + 3]) + a[j].w);
+            }
+            tmem_st_32x32b_x32(tbase + col_of(q), v);
+          }
+          tmem_st_wait();
+          if (lane == 0) sh.fx_cnt[wslot] = 0;  // ready for the next launch
+        }
+      }
+      if (!run) {
+        // nothing to store for this unit
+      } else if constexpr (epi_tmem_direct<Epi>::value) {
         ok = Epi::tile(st, ep, c, tn * BN + cgrp * kCols, tbase + cgrp * kCols, slot);
       } else if constexpr (!Epi::kPaired) {
 #pragma unroll 1
@@ -956,7 +1036,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
           ok = Epi::pair(st, ep, c, tn, cc, g, u);
         }
       }
-      Epi::end(st, ep, c, slot);
+      if (run) Epi::end(st, ep, c, slot);
       tc_fence_before();
       if constexpr (CG == 2)
         mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));

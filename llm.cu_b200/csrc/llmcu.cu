@@ -40,6 +40,10 @@ namespace {
 
 constexpr float kGradScale = 64.0f;   // dlogits are scaled by this power of two (fp16 range)
 constexpr int kLmSplitK = 4;          // K (vocabulary) slices of the lm_head dX GEMM
+// split-K fix-up workspace of the GEMMs whose tiles fill under half a wave
+// (small batches): about one wave of 128 x 256 fp32 partial tiles
+constexpr size_t kFxWsFloats = static_cast<size_t>(160) * 128 * 256;
+constexpr int kFxCounters = 16384;
 
 struct LayerW {
   __half *wqkv, *wo, *wgu, *wd;  // fp16 base, [out, in] (also read MN-major by the dX GEMMs)
@@ -108,6 +112,8 @@ struct llmcu_ctx {
   __half *dhgu = nullptr, *dhd = nullptr;  // MLP targets: dY s B of gate | up and of down, [M, 64]
   // io
   int *tok = nullptr, *tgt = nullptr, *derr = nullptr;
+  float* fx_ws = nullptr;  // split-K fix-up partials (set_gemm_workspace)
+  int* fx_cnt = nullptr;
   float* loss_dev = nullptr;   // [0] = mean loss of the last step
   float *rope_cos = nullptr, *rope_sin = nullptr;
   float* stage = nullptr;      // fp32 staging for host uploads
@@ -354,6 +360,8 @@ void carve(llmcu_ctx* c, Carver& cv) {
   c->dhq = cv.take<__half>(M * 64);
   c->dhgu = mlp ? cv.take<__half>(M * 64) : nullptr;
   c->dhd = mlp ? cv.take<__half>(M * 64) : nullptr;
+  c->fx_ws = cv.take<float>(kFxWsFloats);
+  c->fx_cnt = cv.take<int>(kFxCounters);
   c->tok = cv.take<int>(M);
   c->tgt = cv.take<int>(M);
   c->derr = cv.take<int>(4);
@@ -461,6 +469,14 @@ const __half* base_weight(llmcu_ctx* c, const __half* w16, const int8_t* q, cons
   return c->dq_w;
 }
 Operand op_mn(const __half* p, int k_rows, int n_cols, int ld) { return Operand{p, n_cols, k_rows, ld, true}; }
+
+// The context's split-K fix-up workspace for the gemm() calls of one step
+// (or prefill) on this thread; counters re-zeroed first, in case an aborted
+// launch left some behind.
+struct GemmWorkspaceScope {
+  explicit GemmWorkspaceScope(llmcu_ctx* c) { set_gemm_workspace(c->fx_ws, kFxWsFloats, c->fx_cnt, kFxCounters); }
+  ~GemmWorkspaceScope() { set_gemm_workspace(nullptr, 0, nullptr, 0); }
+};
 
 // Merged weights of the current adapters, every layer (lora_merge).
 cudaError_t merge_adapters(llmcu_ctx* ctx) {
@@ -602,6 +618,8 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     ~PdlScope() { set_pdl(false); }
   } pdl_scope;
   set_pdl(false);
+  GemmWorkspaceScope gws(ctx);
+  CK(cudaMemsetAsync(ctx->fx_cnt, 0, sizeof(int) * kFxCounters, st));
   TIMED(P_FILL, fill_f32(ctx->lg, ctx->n_lora, 0.f, st));
   set_pdl(true);
   // merged q/k/v/o weights of this step's adapters, every layer
@@ -633,7 +651,9 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     eb.out = ctx->d_xf;
     eb.ld_out = H;
     eb.accumulate = 1;
-    eb.ksplit = kLmSplitK;
+    // K (vocabulary) slices: kLmSplitK, more when the row tiles are few
+    // (small batches), up to about one wave of CTAs
+    eb.ksplit = std::max(kLmSplitK, std::min(16, gemm_num_sms() / std::max(1, (M + 127) / 128 * ((H + 255) / 256))));
     // d_xf = dlogits . E  (E [V, H] read MN-major)
     TIMED(P_GEMM, gemm(op(ctx->dl, M, V, ctx->ld_dl), op_mn(E, V, H, H), M, H, Epi::kStoreF32, eb, err, st));
   }
@@ -1501,8 +1521,12 @@ llmcu_status llmcu_generate(llmcu_ctx* ctx, const int32_t* prompt, int n_prompt,
   // merged weights of the current adapters, then the prompt through the batched forward
   set_pdl(false);
   CK(merge_adapters(ctx));
+  CK(cudaMemsetAsync(ctx->fx_cnt, 0, sizeof(int) * kFxCounters, st));
   set_pdl(true);
-  CKS(forward_layers(ctx, 1, n_prompt));
+  {
+    GemmWorkspaceScope gws(ctx);
+    CKS(forward_layers(ctx, 1, n_prompt));
+  }
   set_pdl(false);
   for (int l = 0; l < L; ++l) {  // cache rows 0 .. n_prompt - 1: rotated k, raw v
     const LayerA& a = ctx->la[l];
