@@ -718,6 +718,26 @@ __global__ void dequant_rows_kernel(const int8_t* __restrict__ q, const float* _
     out[i] = __float2half_rn(static_cast<float>(q[i]) * scale[i / cols]);
 }
 
+// The same with 16 codes per thread (one 16-byte load, two 16-byte stores)
+// when cols % 16 == 0: a 16-code group never straddles two rows.
+__global__ void dequant_rows16_kernel(const int4* __restrict__ q, const float* __restrict__ scale, int cols16,
+                                      int64_t n16, uint4* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n16;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int4 raw = __ldg(q + i);
+    const float sc = __ldg(scale + i / cols16);
+    const int8_t* c = reinterpret_cast<const int8_t*>(&raw);
+    uint32_t h[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      h[e] = pack_half2(static_cast<float>(c[2 * e]) * sc, static_cast<float>(c[2 * e + 1]) * sc);
+    out[2 * i] = make_uint4(h[0], h[1], h[2], h[3]);
+    out[2 * i + 1] = make_uint4(h[4], h[5], h[6], h[7]);
+  }
+}
+
 int grid_for(int64_t n, int threads) {
   int64_t g = (n + threads - 1) / threads;
   if (g > 148 * 32) g = 148 * 32;
@@ -917,7 +937,13 @@ cudaError_t quantize_rows_int8(const float* w, int rows, int cols, int8_t* q, fl
 
 cudaError_t dequant_rows_f16(const int8_t* q, const float* scale, int rows, int cols, __half* out, cudaStream_t st) {
   const int64_t n = static_cast<int64_t>(rows) * cols;
-  launch_pdl(dequant_rows_kernel, grid_for(n, 256), 256, 0, st, q, scale, rows, cols, out);
+  if (cols % 16 == 0 && reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) {
+    const int64_t n16 = n / 16;
+    launch_pdl(dequant_rows16_kernel, grid_for(n16, 256), 256, 0, st, reinterpret_cast<const int4*>(q), scale,
+               cols / 16, n16, reinterpret_cast<uint4*>(out));
+  } else {
+    launch_pdl(dequant_rows_kernel, grid_for(n, 256), 256, 0, st, q, scale, rows, cols, out);
+  }
   return cudaGetLastError();
 }
 
