@@ -287,6 +287,8 @@ def main():
     ap.add_argument("--decode", type=int, default=0,
                     help="instead of the training step: greedy decode of N tokens after a 128-token prompt")
     ap.add_argument("--int8", action="store_true", help="with --decode: INT8 base")
+    ap.add_argument("--int8-in-gemm", action="store_true",
+                    help="INT8 base (c4): the GEMMs stage the INT8 codes themselves instead of one dequant pass per weight")
     ap.add_argument("--lora-targets", default="attn",
                     help="adapted projections: attn (the reference's q/k/v/o), mlp, all, or a comma list of "
                          "wq,wk,wv,wo,w_gate,w_up,w_down")
@@ -323,7 +325,8 @@ def main():
     m = load_binding()
     model = m.Model.qwen3_1p7b(n_layers=args.layers)
     projs = parse_targets(args.lora_targets)
-    ctx = m.Context(model, m.Lora(16, 32.0, m.targets_mask(projs)), m.Run(B, S, base_dtype), device=local)
+    ctx = m.Context(model, m.Lora(16, 32.0, m.targets_mask(projs)),
+                    m.Run(B, S, base_dtype, int8_in_gemm=args.int8_in_gemm), device=local)
     if world > 1:
         obj = [m.Context.dp_unique_id() if rank == 0 else None]
         dist_.broadcast_object_list(obj, src=0)
@@ -437,7 +440,9 @@ def main():
             "config": {"workload": args.workload, "description": desc,
                        "model": "qwen3-1.7b-shape" + ("" if args.layers == 28 else f" ({args.layers} layers)"),
                        "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world}",
-                       "lora": "rank 16 alpha 32 on " + "/".join(projs), "l2": "inputs larger than L2 (6.9 GB of weights "
+                       "lora": "rank 16 alpha 32 on " + "/".join(projs),
+                       "int8": ("codes staged by the GEMMs" if args.int8_in_gemm else "one dequant pass per weight")
+                       if base_dtype else None, "l2": "inputs larger than L2 (6.9 GB of weights "
                        "and ~9 GB of activations stream per step); no flush"},
             "step_roofline": {"alg_tflop_per_step": round(step_alg / 1e12, 3),
                               "achieved_tflops": round(step_alg / (ms / 1e3) / 1e12 / world, 2),

@@ -79,6 +79,13 @@ typedef struct {
     int32_t loss_all_positions; /* 0 = reference convention: positions 0..S-2
                                    of each sequence (src/kernels/loss.cu:18-21);
                                    1 = every position                           */
+    int32_t int8_in_gemm;       /* INT8 base, MLP weights: 0 = each weight
+                                   dequantised to fp16 by one vectorised pass
+                                   just before its GEMM (the faster on B200);
+                                   1 = the GEMM stages the INT8 codes itself
+                                   (converter warps expand them in shared
+                                   memory; row scales in the epilogue / folded
+                                   into the input-gradient GEMM's A operand)    */
 } llmcu_run_cfg;
 
 typedef struct {

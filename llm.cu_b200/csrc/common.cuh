@@ -70,6 +70,13 @@ struct Operand {
   int k;
   int ld;
   bool mn = false;
+  // B only: INT8 codes instead of fp16 (ptr unused), the same [rows, k] /
+  // [k, rows] layout with ld bytes between rows; the GEMM stages them as exact
+  // fp16.  K-major (x W^T): q8_scale holds the weight's per-row scales, which
+  // the epilogue applies to the output columns.  MN-major (dY W): the scales
+  // run along K, so the caller folds them into A (q8_scale unused).
+  const int8_t* q8 = nullptr;
+  const float* q8_scale = nullptr;
 };
 
 enum class Epi : int {
@@ -103,6 +110,7 @@ struct EpiArgs {
   __half* gu = nullptr;       // interleaved [M, 2I]
   const __half* gu_in = nullptr;
   int ld_gu = 0;
+  const float* gu_out_scale = nullptr;  // kSwiGLUBwd: per dgu column factors (null: none)
   __half* act = nullptr;      // [M, I]
   int ld_act = 0;
   // kQKNormRope: q heads are columns [0, n_q_cols), k heads [n_q_cols,
@@ -163,10 +171,11 @@ cudaError_t embed_forward(const int* tokens, const __half* E, float* out, int M,
                           cudaStream_t st);
 cudaError_t rmsnorm_forward(const float* x, const float* w, __half* out, int M, int H, float eps, cudaStream_t st);
 // dres (+)= rmsnorm_bwd(dy, x, w); dres16 = fp16(dres)
+// s16 (optional): per-column factors applied to the fp16 copy dres16 only.
 cudaError_t rmsnorm_backward(const float* dy, const float* x, const float* w, float* dres, __half* dres16, int M,
-                             int H, float eps, int accumulate, cudaStream_t st);
+                             int H, float eps, int accumulate, cudaStream_t st, const float* s16 = nullptr);
 cudaError_t rmsnorm_backward(const __half* dy, const float* x, const float* w, float* dres, __half* dres16, int M,
-                             int H, float eps, int accumulate, cudaStream_t st);
+                             int H, float eps, int accumulate, cudaStream_t st, const float* s16 = nullptr);
 cudaError_t qknorm_rope_forward(const __half* qkv, int ld_qkv, const float* qn_w, const float* kn_w, int ld_out,
                                 const float* cos_t, const float* sin_t, __half* q_out, __half* k_out, int B, int S,
                                 int nh, int nkv, int hd, float eps, cudaStream_t st);

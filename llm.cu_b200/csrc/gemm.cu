@@ -45,6 +45,22 @@ bool make_map(CUtensorMap* map, const Operand& op, int box_rows) {
   return r == CUDA_SUCCESS;
 }
 
+// INT8 B operand: the same dimensions as make_map's, unswizzled boxes of 64
+// codes x box rows (the converter warps read them with 16-byte loads).
+bool make_map_q8(CUtensorMap* map, const Operand& op, int box_rows) {
+  if (!g_encode || !op.q8) return false;
+  if (reinterpret_cast<uintptr_t>(op.q8) % 16 != 0 || op.ld % 16 != 0) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(op.mn ? op.rows : op.k),
+                        static_cast<cuuint64_t>(op.mn ? op.k : op.rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(op.ld)};
+  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(op.mn ? 64 : box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(op.q8), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // Output / epilogue-input map: rows x cols of fp16 or fp32, box = 128 bytes of
 // columns x 32 rows (one epilogue warp's slab), 128-byte swizzle.
 bool make_io_map(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, bool f32) {
@@ -63,9 +79,9 @@ bool make_io_map(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, 
 }
 
 // As many pipeline stages as fit beside the epilogue slabs (at most 8).
-template <int BN, int EW, int SLAB, int CG>
+template <int BN, int EW, int SLAB, int CG, bool Q8 = false>
 constexpr int stages_for() {
-  constexpr int stage = kBlockM * kBlockK * 2 + BN / CG * kBlockK * 2;
+  constexpr int stage = kBlockM * kBlockK * 2 + BN / CG * kBlockK * 2;  // INT8 codes land inside B
   constexpr int s = (232448 - 1536 - EW * SLAB) / stage;
   return s > 8 ? 8 : s;
 }
@@ -76,14 +92,15 @@ constexpr int epi_warps() {
   return BN >= 128 ? 4 * kGemmEpiGroups : 4;
 }
 
-template <int BN, class E, bool BMN, int CG>
+template <int BN, class E, bool BMN, int CG, bool Q8 = false>
 cudaError_t launch(const CUtensorMap* maps, const GemmShape& sh, const typename E::Params& p, int* err,
                    cudaStream_t st) {
   constexpr int kEpiWarps = epi_warps<BN>();
-  constexpr int S = stages_for<BN, kEpiWarps, E::kSlab, CG>();
-  using L = GemmSmem<BN, S, kEpiWarps, E::kSlab, CG>;
+  constexpr int S = stages_for<BN, kEpiWarps, E::kSlab, CG, Q8>();
+  using L = GemmSmem<BN, S, kEpiWarps, E::kSlab, CG, Q8>;
   static_assert(L::kBytes <= 232448, "shared memory budget");
-  auto kern = gemm_tc_kernel<BN, S, kEpiWarps, E, BMN, CG>;
+  constexpr int kThreads = 64 + 32 * kEpiWarps + (Q8 ? kQ8Threads : 0);
+  auto kern = gemm_tc_kernel<BN, S, kEpiWarps, E, BMN, CG, Q8>;
   static bool attr_done = false;  // set once per instantiation
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
@@ -93,15 +110,14 @@ cudaError_t launch(const CUtensorMap* maps, const GemmShape& sh, const typename 
   const int units = sh.num_tiles * sh.splits;
   if constexpr (CG == 1) {
     const int grid = units < g_num_sms ? units : g_num_sms;
-    cudaError_t e = launch_pdl(kern, grid, 64 + 32 * kEpiWarps, L::kBytes, st, maps[0], maps[1], maps[2], maps[3], sh,
-                               p, err);
+    cudaError_t e = launch_pdl(kern, grid, kThreads, L::kBytes, st, maps[0], maps[1], maps[2], maps[3], sh, p, err);
     if (e != cudaSuccess) return e;
   } else {
     // one CTA pair per unit, at most one CTA per SM
     const int pairs = std::min(units, g_num_sms / 2);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
-    cfg.blockDim = dim3(64 + 32 * kEpiWarps);
+    cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = L::kBytes;
     cfg.stream = st;
     cudaLaunchAttribute at[2];
@@ -131,7 +147,7 @@ cudaError_t dispatch(Epi epi, const EpiArgs& ea, const CUtensorMap* maps, const 
       return launch<BN, EpiResidF32, BMN, CG>(maps, sh, EpiResidF32::Params{}, err, st);
     case Epi::kSwiGLUBwd:
       if constexpr (BN == 256) {
-        return launch<BN, EpiSwiGLUBwd, BMN, CG>(maps, sh, EpiSwiGLUBwd::Params{ea.gu_in, ea.ld_gu}, err, st);
+        return launch<BN, EpiSwiGLUBwd, BMN, CG>(maps, sh, EpiSwiGLUBwd::Params{ea.gu_in, ea.ld_gu, ea.gu_out_scale}, err, st);
       } else {
         return cudaErrorInvalidValue;
       }
@@ -164,6 +180,19 @@ cudaError_t dispatch(Epi epi, const EpiArgs& ea, const CUtensorMap* maps, const 
         return cudaErrorInvalidValue;
       }
   }
+  return cudaErrorInvalidValue;
+}
+
+// INT8 B: the MLP GEMMs of an INT8 base -- gate/up + SwiGLU and down +
+// residual (B K-major), down dX + SwiGLU backward and gate/up dX (B MN-major)
+template <int CG>
+cudaError_t dispatch_q8(Epi epi, bool bmn, const EpiArgs& ea, const CUtensorMap* maps, const GemmShape& sh, int* err,
+                        cudaStream_t st) {
+  if (!bmn && epi == Epi::kSwiGLU) return launch<256, EpiSwiGLU, false, CG, true>(maps, sh, EpiSwiGLU::Params{}, err, st);
+  if (!bmn && epi == Epi::kResidF32) return launch<256, EpiResidF32, false, CG, true>(maps, sh, EpiResidF32::Params{}, err, st);
+  if (bmn && epi == Epi::kSwiGLUBwd)
+    return launch<256, EpiSwiGLUBwd, true, CG, true>(maps, sh, EpiSwiGLUBwd::Params{ea.gu_in, ea.ld_gu, ea.gu_out_scale}, err, st);
+  if (bmn && epi == Epi::kStoreF16) return launch<256, EpiStoreF16, true, CG, true>(maps, sh, EpiStoreF16::Params{}, err, st);
   return cudaErrorInvalidValue;
 }
 
@@ -231,9 +260,12 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
   }
   // CTA pairs (cta_group::2) for the 256-wide tiles of matrices with more
   // than one 128-row block: each pair shares a 256 x 256 tile
+  // INT8 B: 256-wide tiles; K-major needs the row scales (the epilogue applies them)
+  if (B.q8 && (BN != 256 || (!B.mn && !B.q8_scale) || ea.ksplit > 1)) return cudaErrorInvalidValue;
   const int CG = (BN == 256 && M > kBlockM) ? 2 : 1;
   CUtensorMap maps[4];  // A, B, C, D
-  if (!make_map(&maps[0], A, kBlockM) || !make_map(&maps[1], B, BN / CG)) return cudaErrorInvalidValue;
+  if (!make_map(&maps[0], A, kBlockM)) return cudaErrorInvalidValue;
+  if (B.q8 ? !make_map_q8(&maps[1], B, BN / CG) : !make_map(&maps[1], B, BN / CG)) return cudaErrorInvalidValue;
   bool okc = true;
   switch (epi) {
     case Epi::kStoreF16:
@@ -283,6 +315,7 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
   sh.fixup = 0;
   sh.fx_ws = nullptr;
   sh.fx_cnt = nullptr;
+  sh.b_scale = B.mn ? nullptr : B.q8_scale;
   if (ea.ksplit > 1) {  // K slices reduce-add into the same rows
     const int nk = sh.kb_per_split;
     const int kbps = (nk + ea.ksplit - 1) / ea.ksplit;
@@ -314,6 +347,7 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
       }
     }
   }
+  if (B.q8) return CG == 2 ? dispatch_q8<2>(epi, B.mn, ea, maps, sh, err, st) : dispatch_q8<1>(epi, B.mn, ea, maps, sh, err, st);
   if (CG == 2) {
     if (B.mn) return dispatch<256, true, 2>(epi, ea, maps, sh, err, st);
     return dispatch<256, false, 2>(epi, ea, maps, sh, err, st);

@@ -56,19 +56,26 @@ struct GemmShape {
   int fixup;
   float* fx_ws;         // [tiles * CG * 4 * groups][splits][slice columns / 4][32] float4
   int* fx_cnt;          // [tiles * CG * 4 * groups], zero between launches
+  // INT8 B, K-major (Q8 forward kernels): the weight's per-row fp32 scales,
+  // one per output column, applied by the epilogue
+  const float* b_scale;
 };
 
 constexpr int kBlockM = 128;
+constexpr int kQ8Threads = 64;  // converter threads of the INT8-B kernels
 constexpr int kBlockK = 64;
 constexpr int kSlabBytes = 32 * 128;  // one 32-row x 128-byte box
 constexpr int kMnBox = 64 * 128;      // MN-major B box: 64 K rows x 64 columns of fp16
 
 // CG = 2: a CTA pair shares each 256 x BN tile; every CTA holds 128 rows
 // of A and BN/2 rows of B per stage.
-template <int BN, int STAGES, int EW, int SLAB = kSlabBytes, int CG = 1>
+// Q8: B arrives as INT8 codes (kQBytes per stage) in the first half of the
+// stage's B region; converter warps expand them in place into the fp16 tile.
+template <int BN, int STAGES, int EW, int SLAB = kSlabBytes, int CG = 1, bool Q8 = false>
 struct GemmSmem {
   static constexpr int kABytes = kBlockM * kBlockK * 2;       // 16 KB
   static constexpr int kBBytes = BN / CG * kBlockK * 2;       // 8/16/32 KB
+  static constexpr int kQBytes = Q8 ? BN / CG * kBlockK : 0;  // INT8 codes of the B tile (inside B)
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;  // two accumulators
   static constexpr int kSlabOffset = STAGES * kStageBytes;
@@ -94,6 +101,7 @@ struct EpiCtx {
   int n_main;               // first side-output column
   __half* side;
   int ld_side;
+  const float* col_scale;   // INT8-B forward: the weight's row scale of each output column (null: none)
 };
 
 // Side-output columns [col0, col0 + n) of this thread's row as fp16 (plain
@@ -454,15 +462,22 @@ struct EpiResidF32 {
       side_store(c, col0, v, kChunk);
       return true;
     }
+    float f[kChunk];
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) f[j] = 1.f;
+    if (c.col_scale) {
+#pragma unroll
+      for (int j = 0; j < kChunk; j += 4) *reinterpret_cast<float4*>(f + j) = __ldg(reinterpret_cast<const float4*>(c.col_scale + col0 + j));
+    }
     slab_wait_read(c);
     if (!slab_load(c, c.mapD, col0, c.row0)) return false;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       uint4 r = slab_ld(c, j);
-      r.x = __float_as_uint(__uint_as_float(r.x) + v[4 * j]);
-      r.y = __float_as_uint(__uint_as_float(r.y) + v[4 * j + 1]);
-      r.z = __float_as_uint(__uint_as_float(r.z) + v[4 * j + 2]);
-      r.w = __float_as_uint(__uint_as_float(r.w) + v[4 * j + 3]);
+      r.x = __float_as_uint(__uint_as_float(r.x) + v[4 * j] * f[4 * j]);
+      r.y = __float_as_uint(__uint_as_float(r.y) + v[4 * j + 1] * f[4 * j + 1]);
+      r.z = __float_as_uint(__uint_as_float(r.z) + v[4 * j + 2] * f[4 * j + 2]);
+      r.w = __float_as_uint(__uint_as_float(r.w) + v[4 * j + 3] * f[4 * j + 3]);
       slab_st(c, j, r);
     }
     slab_store(c, c.mapC, col0, c.row0);
@@ -495,12 +510,21 @@ struct EpiSwiGLU {
       return true;
     }
     uint32_t dgp[32], sp[32], ap[32];  // u silu'(g), silu(g), act as packed half2
+    // INT8 weight: the row scales of these gate / up columns; lane L holds
+    // columns 2L, 2L + 1 and hands them out by shuffle
+    float2 my_g = make_float2(1.f, 1.f), my_u = make_float2(1.f, 1.f);
+    if (c.col_scale) {
+      my_g = __ldg(reinterpret_cast<const float2*>(c.col_scale + tile_n * 256 + cc) + c.lane);
+      my_u = __ldg(reinterpret_cast<const float2*>(c.col_scale + tile_n * 256 + 128 + cc) + c.lane);
+    }
 #pragma unroll
     for (int t = 0; t < 32; ++t) {
       float r0[3], r1[3];
+      const float2 sg2 = make_float2(__shfl_sync(0xffffffffu, my_g.x, t), __shfl_sync(0xffffffffu, my_g.y, t));
+      const float2 su2 = make_float2(__shfl_sync(0xffffffffu, my_u.x, t), __shfl_sync(0xffffffffu, my_u.y, t));
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const float gv = g[2 * t + e], uv = u[2 * t + e];
+        const float gv = g[2 * t + e] * (e ? sg2.y : sg2.x), uv = u[2 * t + e] * (e ? su2.y : su2.x);
         const float sg = 1.0f / (1.0f + __expf(-gv));
         const float si = gv * sg;
         float* r = e ? r1 : r0;
@@ -540,6 +564,8 @@ struct EpiSwiGLUBwd {
   struct Params {
     const __half* gu_in;  // [M, 2N] interleaved stash
     int ld;
+    const float* out_scale;  // per dgu column factors (an INT8 gate/up weight's row scales, folded into
+                             // the next GEMM's A operand), null: none
   };
   struct State {
     uint4 f[2][4];  // factors of the next 32 columns: [0] u silu'(g), [1] silu(g)
@@ -592,12 +618,21 @@ struct EpiSwiGLUBwd {
       tmem_ld_32x32b_x32(taddr + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v));
       tmem_ld_wait();
       uint32_t dg[16], du[16];
+      // per dgu column factors of these 32 gate / up columns: lane L holds
+      // gate column L and up column L (+128), handed out by shuffle
+      float my_g = 1.f, my_u = 1.f;
+      if (p.out_scale) {
+        my_g = __ldg(p.out_scale + gcol + 32 * q + c.lane);
+        my_u = __ldg(p.out_scale + gcol + 128 + 32 * q + c.lane);
+      }
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
         const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&f0[t]));
         const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&f1[t]));
-        dg[t] = pack_half2(v[2 * t] * a.x, v[2 * t + 1] * a.y);
-        du[t] = pack_half2(v[2 * t] * b.x, v[2 * t + 1] * b.y);
+        const float sg0 = __shfl_sync(0xffffffffu, my_g, 2 * t), sg1 = __shfl_sync(0xffffffffu, my_g, 2 * t + 1);
+        const float su0 = __shfl_sync(0xffffffffu, my_u, 2 * t), su1 = __shfl_sync(0xffffffffu, my_u, 2 * t + 1);
+        dg[t] = pack_half2(v[2 * t] * a.x * sg0, v[2 * t + 1] * a.y * sg1);
+        du[t] = pack_half2(v[2 * t] * b.x * su0, v[2 * t + 1] * b.y * su1);
       }
       // slab rows hold 64 columns: steps 0/2 fill chunks 0-3, steps 1/3 chunks 4-7
       const int h = (q & 1) * 4;
@@ -718,13 +753,23 @@ struct epi_tmem_direct<E, std::void_t<decltype(E::kTmemDirect)>> : std::bool_con
 // on the even CTA's `full` barriers, its commits arrive on both CTAs'
 // `empty` / `acc_full` barriers, and both CTAs' epilogues drain their own
 // TMEM rows and arrive on the even CTA's `acc_empty`.
-template <int BN, int STAGES, int EW, class Epi, bool BMN, int CG>
-__global__ void __launch_bounds__(64 + 32 * EW, 1)
+// Q8: B is INT8 codes.  The producer's TMA brings them (plain row-major
+// boxes) into the stage's Q region; the converter warps (kQ8Threads, after
+// the epilogue warps) write the codes as exact fp16 values into the stage's
+// B tile in the 128-byte-swizzled layout the MMA reads, and each CTA's
+// converters arrive once on the (even CTA's) full barrier.  The weight's
+// per-row scales act outside the MMA, as in the reference's INT8 GEMM
+// (src/kernels/quantize.cu:55-78 multiplies the sum by scale[n]): K-major
+// (forward) by the epilogue on each output column (sh.b_scale); MN-major
+// (input gradient, the scales run along K) by the caller, folded into A.
+template <int BN, int STAGES, int EW, class Epi, bool BMN, int CG, bool Q8 = false>
+__global__ void __launch_bounds__(64 + 32 * EW + (Q8 ? kQ8Threads : 0), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
                    const GemmShape sh, const typename Epi::Params ep, int* err) {
   static_assert(CG == 1 || (CG == 2 && BN == 256), "CTA pairs use 256-wide tiles");
-  using L = GemmSmem<BN, STAGES, EW, Epi::kSlab, CG>;
+  static_assert(!Q8 || BN == 256, "INT8 B only with 256-wide tiles");
+  using L = GemmSmem<BN, STAGES, EW, Epi::kSlab, CG, Q8>;
   constexpr int kRowsPerTile = kBlockM * CG;  // tile rows (both CTAs of a pair)
   constexpr int kBRows = BN / CG;             // B rows (N) this CTA loads
   extern __shared__ uint8_t smem_raw[];
@@ -735,7 +780,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
   uint64_t* acc_full = bars + 2 * STAGES;   // [2]
   uint64_t* acc_empty = acc_full + 2;       // [2]
   uint64_t* slab_bar = acc_empty + 2;       // [EW]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(slab_bar + EW);
+  uint64_t* qfull = slab_bar + EW;          // [STAGES] (Q8): the stage's INT8 codes landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qfull + (Q8 ? STAGES : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   pdl_trigger();
@@ -747,8 +793,9 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], Q8 ? 1 + CG : 1);  // Q8: + one converter arrival per CTA
       mbar_init(&empty[s], 1);
+      if constexpr (Q8) mbar_init(&qfull[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
@@ -802,21 +849,36 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
           if (!mbar_wait(&empty[s], par, abort_flag, err, kErrWaitConsumer)) { ok = false; break; }
           uint8_t* sa = smem + s * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes;
+          if constexpr (Q8) {
+            // the INT8 codes of this CTA's B rows into the B region's first half (local barrier)
+            uint8_t* sq = sb;
+            mbar_arrive_expect_tx(&qfull[s], L::kQBytes);
+            if constexpr (!BMN) {
+              tma_load_2d(sq, &tmB, &qfull[s], kb * kBlockK, brow);
+            } else {
+#pragma unroll
+              for (int j = 0; j < kBRows / 64; ++j) tma_load_2d(sq + j * 4096, &tmB, &qfull[s], brow + 64 * j, kb * kBlockK);
+            }
+          }
           if constexpr (CG == 2) {
             // both CTAs' bytes count on the even CTA's barrier
             const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
-            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], Q8 ? 2 * L::kABytes : 2 * (L::kABytes + L::kBBytes));
             tma_load_2d_pair(sa, &tmA, fb, kb * kBlockK, arow);
-            if constexpr (!BMN) {
+            if constexpr (Q8) {
+              // B comes from the converters
+            } else if constexpr (!BMN) {
               tma_load_2d_pair(sb, &tmB, fb, kb * kBlockK, brow);
             } else {
 #pragma unroll
               for (int j = 0; j < kBRows / 64; ++j) tma_load_2d_pair(sb + j * kMnBox, &tmB, fb, brow + 64 * j, kb * kBlockK);
             }
           } else {
-            mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+            mbar_arrive_expect_tx(&full[s], Q8 ? L::kABytes : L::kABytes + L::kBBytes);
             tma_load_2d(sa, &tmA, &full[s], kb * kBlockK, arow);
-            if constexpr (!BMN) {
+            if constexpr (Q8) {
+              // B comes from the converters
+            } else if constexpr (!BMN) {
               tma_load_2d(sb, &tmB, &full[s], kb * kBlockK, brow);
             } else {
               // [64 K rows x 64 N columns] boxes side by side along N
@@ -890,6 +952,81 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
         }
       }
     }
+  } else if (Q8 && warp >= 2 + EW) {
+    // ------------------------------------------------------------ converters
+    // per stage: this CTA's kBRows B rows x 64 K of INT8 codes -> fp16 in
+    // the MMA's 128-byte-swizzled layout.  K-major (forward): row r = output
+    // feature brow + r, 64 codes of K.  MN-major (input gradient): box j of
+    // 64 K rows (the weight's output features, scale per row) x 64 N columns.
+    const int ct = threadIdx.x - (64 + 32 * EW);  // 0 .. kQ8Threads - 1
+    int it = 0;
+    bool ok = true;
+    for (int u = unit0; u < num_units && ok; u += ustep) {
+      const int sp = u / sh.num_tiles;
+      const int kb_end = min(nk, (sp + 1) * sh.kb_per_split);
+      for (int kb = sp * sh.kb_per_split; kb < kb_end; ++kb, ++it) {
+        const int s = it % STAGES;
+        if (!mbar_wait(&qfull[s], (it / STAGES) & 1, abort_flag, err, kErrWaitProducer)) { ok = false; break; }
+        const uint32_t sb32 = smem_u32(smem + s * L::kStageBytes + L::kABytes);  // shared-space addresses
+        // kBRows x 64 codes = kBRows * 4 groups of 16: every group is read
+        // before any fp16 is written over the codes (they share the region)
+        constexpr int kPer = kBRows * 4 / kQ8Threads;
+        int4 raw[kPer];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int g = ct + i * kQ8Threads;
+          const int box = BMN ? g / 256 : 0;
+          const int srow = BMN ? (g >> 2) & 63 : g >> 2;
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(raw[i].x), "=r"(raw[i].y), "=r"(raw[i].z), "=r"(raw[i].w)
+                       : "r"(sb32 + box * 4096 + srow * 64 + (g & 3) * 16));
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kQ8Threads) : "memory");
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int g = ct + i * kQ8Threads;
+          // K-major: row = output feature; MN-major: box of 64 N columns, row = K
+          const int box = BMN ? g / 256 : 0;
+          const int srow = BMN ? (g >> 2) & 63 : g >> 2;
+          const int part = g & 3;  // codes [16 part, 16 part + 16) of the row
+          // exact int8 -> fp16: bias each code to 0..255, place it in the low
+          // byte of fp16 1024 (0x6400 | u = 1024 + u) and subtract 1152
+          const uint32_t w4[4] = {static_cast<uint32_t>(raw[i].x) ^ 0x80808080u,
+                                  static_cast<uint32_t>(raw[i].y) ^ 0x80808080u,
+                                  static_cast<uint32_t>(raw[i].z) ^ 0x80808080u,
+                                  static_cast<uint32_t>(raw[i].w) ^ 0x80808080u};
+          const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+          uint32_t h[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t lo = __byte_perm(w4[e], 0x64646464u, 0x4140);
+            const uint32_t hi = __byte_perm(w4[e], 0x64646464u, 0x4342);
+            const __half2 a0 = __hsub2(*reinterpret_cast<const __half2*>(&lo), bias);
+            const __half2 a1 = __hsub2(*reinterpret_cast<const __half2*>(&hi), bias);
+            h[2 * e] = *reinterpret_cast<const uint32_t*>(&a0);
+            h[2 * e + 1] = *reinterpret_cast<const uint32_t*>(&a1);
+          }
+          // 16-byte chunks 2 part, 2 part + 1 of the 128-byte row, swizzled by row % 8
+          const uint32_t rowp = sb32 + (BMN ? box * kMnBox : 0) + srow * 128;
+          const int c0 = 2 * part, c1 = 2 * part + 1;
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rowp + ((c0 ^ (srow & 7)) << 4)), "r"(h[0]),
+                       "r"(h[1]), "r"(h[2]), "r"(h[3])
+                       : "memory");
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rowp + ((c1 ^ (srow & 7)) << 4)), "r"(h[4]),
+                       "r"(h[5]), "r"(h[6]), "r"(h[7])
+                       : "memory");
+        }
+        // generic-proxy writes -> visible to the tensor cores, then one arrival per CTA
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("bar.sync 1, %0;" ::"n"(kQ8Threads) : "memory");
+        if (ct == 0) {
+          if constexpr (CG == 2)
+            mbar_arrive_cluster(mapa_shared(smem_u32(&full[s]), 0));
+          else
+            mbar_arrive(&full[s]);
+        }
+      }
+    }
   } else {
     // -------------------------------------------------------------- epilogue
     static_assert(EW == 4 || EW == 8, "4 or 8 epilogue warps");
@@ -915,6 +1052,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     c.n_main = sh.n_main;
     c.side = sh.side;
     c.ld_side = sh.ld_side;
+    c.col_scale = (Q8 && !BMN) ? sh.b_scale : nullptr;
     int i = 0;
     bool ok = true;
     for (int u = unit0; u < num_units && ok; u += ustep, ++i) {

@@ -124,10 +124,13 @@ __global__ void __launch_bounds__(128) rmsnorm_fwd_row_kernel(const float* __res
   }
 }
 
+// s16 (may be null): per-column factors of the fp16 copy only (an INT8
+// weight's row scales folded into the next input-gradient GEMM's A operand).
 template <class DY>
 __global__ void rmsnorm_bwd_kernel(const DY* __restrict__ dy, const float* __restrict__ x,
                                    const float* __restrict__ w, float* __restrict__ dres,
-                                   __half* __restrict__ dres16, int M, int H, float eps, int accumulate) {
+                                   __half* __restrict__ dres16, int M, int H, float eps, int accumulate,
+                                   const float* __restrict__ s16) {
   pdl_trigger();
   pdl_wait();
   const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
@@ -157,6 +160,10 @@ __global__ void rmsnorm_bwd_kernel(const DY* __restrict__ dy, const float* __res
       o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
     }
     *reinterpret_cast<float4*>(dres + base + c) = o;
+    if (s16) {
+      const float4 f = ld4(s16 + c);
+      o.x *= f.x; o.y *= f.y; o.z *= f.z; o.w *= f.w;
+    }
     uint2 u;
     u.x = pack_half2(o.x, o.y);
     u.y = pack_half2(o.z, o.w);
@@ -172,7 +179,7 @@ template <class DY, int NV>
 __global__ void __launch_bounds__(128) rmsnorm_bwd_row_kernel(const DY* __restrict__ dy, const float* __restrict__ x,
                                                               const float* __restrict__ w, float* __restrict__ dres,
                                                               __half* __restrict__ dres16, int M, float eps,
-                                                              int accumulate) {
+                                                              int accumulate, const float* __restrict__ s16) {
   pdl_trigger();
   pdl_wait();
   constexpr int H = 128 * NV;
@@ -214,6 +221,10 @@ __global__ void __launch_bounds__(128) rmsnorm_bwd_row_kernel(const DY* __restri
     o.z += pv[i].z;
     o.w += pv[i].w;
     *reinterpret_cast<float4*>(dres + base + 128 * i) = o;
+    if (s16) {
+      const float4 f = ld4(s16 + lane * 4 + 128 * i);
+      o.x *= f.x; o.y *= f.y; o.z *= f.z; o.w *= f.w;
+    }
     uint2 u;
     u.x = pack_half2(o.x, o.y);
     u.y = pack_half2(o.z, o.w);
@@ -769,34 +780,34 @@ cudaError_t rmsnorm_forward(const float* x, const float* w, __half* out, int M, 
 }
 
 cudaError_t rmsnorm_backward(const float* dy, const float* x, const float* w, float* dres, __half* dres16, int M,
-                             int H, float eps, int accumulate, cudaStream_t st) {
+                             int H, float eps, int accumulate, cudaStream_t st, const float* s16) {
   if (H % 4) return cudaErrorInvalidValue;
   if (H == 2048 || H == 256) {
     const int grid = (M + 3) / 4;
     if (H == 2048)
-      launch_pdl(rmsnorm_bwd_row_kernel<float, 16>, grid, 128, 0, st, dy, x, w, dres, dres16, M, eps, accumulate);
+      launch_pdl(rmsnorm_bwd_row_kernel<float, 16>, grid, 128, 0, st, dy, x, w, dres, dres16, M, eps, accumulate, s16);
     else
-      launch_pdl(rmsnorm_bwd_row_kernel<float, 2>, grid, 128, 0, st, dy, x, w, dres, dres16, M, eps, accumulate);
+      launch_pdl(rmsnorm_bwd_row_kernel<float, 2>, grid, 128, 0, st, dy, x, w, dres, dres16, M, eps, accumulate, s16);
     return cudaGetLastError();
   }
   launch_pdl(rmsnorm_bwd_kernel<float>, (M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, dy, x, w, dres, dres16, M, H,
-                                                                                         eps, accumulate);
+                                                                                         eps, accumulate, s16);
   return cudaGetLastError();
 }
 
 cudaError_t rmsnorm_backward(const __half* dy, const float* x, const float* w, float* dres, __half* dres16, int M,
-                             int H, float eps, int accumulate, cudaStream_t st) {
+                             int H, float eps, int accumulate, cudaStream_t st, const float* s16) {
   if (H % 4) return cudaErrorInvalidValue;
   if (H == 2048 || H == 256) {
     const int grid = (M + 3) / 4;
     if (H == 2048)
-      launch_pdl(rmsnorm_bwd_row_kernel<__half, 16>, grid, 128, 0, st, dy, x, w, dres, dres16, M, eps, accumulate);
+      launch_pdl(rmsnorm_bwd_row_kernel<__half, 16>, grid, 128, 0, st, dy, x, w, dres, dres16, M, eps, accumulate, s16);
     else
-      launch_pdl(rmsnorm_bwd_row_kernel<__half, 2>, grid, 128, 0, st, dy, x, w, dres, dres16, M, eps, accumulate);
+      launch_pdl(rmsnorm_bwd_row_kernel<__half, 2>, grid, 128, 0, st, dy, x, w, dres, dres16, M, eps, accumulate, s16);
     return cudaGetLastError();
   }
   launch_pdl(rmsnorm_bwd_kernel<__half>, (M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, dy, x, w, dres, dres16, M,
-                                                                                          H, eps, accumulate);
+                                                                                          H, eps, accumulate, s16);
   return cudaGetLastError();
 }
 

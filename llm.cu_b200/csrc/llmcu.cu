@@ -457,18 +457,44 @@ llmcu_status wait_event(llmcu_ctx* ctx, cudaEvent_t ev) {
 __global__ void scale_loss_kernel(const float* total, float inv_n, float* out) { pdl_trigger(); pdl_wait(); out[0] = total[0] * inv_n; }
 
 
-// fp16 [rows, cols] view of one base weight: the fp16 copy, or the INT8 rows
-// dequantised into scratch (src/kernels/quantize.cu:55-78 applies the same
-// per-row scale).  The forward reads it K-major, the input gradient MN-major.
-const __half* base_weight(llmcu_ctx* c, const __half* w16, const int8_t* q, const float* s, int rows, int cols,
-                          cudaError_t* e) {
-  if (c->rc.base_dtype != LLMCU_BASE_INT8) return w16;
-  prof_mark(c, P_DEQUANT);
-  *e = dequant_rows_f16(q, s, rows, cols, c->dq_w, c->st);
-  prof_mark(c, P_DEQUANT);
-  return c->dq_w;
-}
 Operand op_mn(const __half* p, int k_rows, int n_cols, int ld) { return Operand{p, n_cols, k_rows, ld, true}; }
+
+// B operand of one base weight W [rows, cols] ([out, in]): the fp16 copy, or
+// the INT8 rows, staged as exact fp16 by the GEMM, with the per-row scales of
+// src/kernels/quantize.cu:55-78 applied to the forward's output columns by its
+// epilogue (the reference's INT8 GEMM multiplies the sum by scale[n]); for the
+// input gradient (MN-major) the caller folds the scales into A.
+Operand base_b(const llmcu_ctx* c, const __half* w16, const int8_t* q, const float* s, int rows, int cols, bool mn) {
+  Operand o = mn ? op_mn(w16, rows, cols, cols) : op(w16, rows, cols, cols);
+  if (c->rc.base_dtype == LLMCU_BASE_INT8) {
+    o.ptr = nullptr;
+    o.q8 = q;
+    o.q8_scale = s;
+  }
+  return o;
+}
+
+// fp16 [rows, cols] copy of one base weight for the GEMM: the fp16 base
+// itself, or the INT8 rows dequantised into scratch by one vectorised pass
+// (fp16(code * scale), src/kernels/quantize.cu:55-78's per-row scale).
+Operand base_dq(llmcu_ctx* c, const __half* w16, const int8_t* q, const float* s, int rows, int cols, bool mn,
+                cudaError_t* e) {
+  const __half* w = w16;
+  if (c->rc.base_dtype == LLMCU_BASE_INT8) {
+    prof_mark(c, P_DEQUANT);
+    *e = dequant_rows_f16(q, s, rows, cols, c->dq_w, c->st);
+    prof_mark(c, P_DEQUANT);
+    w = c->dq_w;
+  }
+  return mn ? op_mn(w, rows, cols, cols) : op(w, rows, cols, cols);
+}
+
+// B operand of an MLP base weight under the context's INT8 mode.
+Operand mlp_b(llmcu_ctx* c, const __half* w16, const int8_t* q, const float* s, int rows, int cols, bool mn,
+              cudaError_t* e) {
+  if (c->rc.base_dtype == LLMCU_BASE_INT8 && c->rc.int8_in_gemm) return base_b(c, w16, q, s, rows, cols, mn);
+  return base_dq(c, w16, q, s, rows, cols, mn, e);
+}
 
 // The context's split-K fix-up workspace for the gemm() calls of one step
 // (or prefill) on this thread; counters re-zeroed first, in case an aborted
@@ -498,7 +524,6 @@ llmcu_status forward_layers(llmcu_ctx* ctx, int B, int S) {
   const float eps = ctx->m.rms_eps;
   cudaStream_t st = ctx->st;
   int* err = ctx->derr;
-  cudaError_t e = cudaSuccess;
   const __half* E = ctx->E;
   TIMED(P_EMBED, embed_forward(ctx->tok, E, ctx->resid[0], M, H, V, err, st));
 
@@ -573,24 +598,25 @@ llmcu_status forward_layers(llmcu_ctx* ctx, int B, int S) {
       }
       continue;
     }
-    const __half* wgu = base_weight(ctx, w.wgu, w.q_gu, w.s_gu, 2 * I, H, &e);
-    CK(e);
+    cudaError_t e = cudaSuccess;
     {
       EpiArgs ea;
       ea.gu = a.gu;
       ea.ld_gu = 2 * I;
       ea.act = a.act;
       ea.ld_act = I;
-      TIMED(P_GEMM, gemm(op(a.xn2, M, H, H), op(wgu, 2 * I, H, H), M, 2 * I, Epi::kSwiGLU, ea, err, st, 256));
+      const Operand bgu = mlp_b(ctx, w.wgu, w.q_gu, w.s_gu, 2 * I, H, false, &e);
+      CK(e);
+      TIMED(P_GEMM, gemm(op(a.xn2, M, H, H), bgu, M, 2 * I, Epi::kSwiGLU, ea, err, st, 256));
     }
-    const __half* wd = base_weight(ctx, w.wd, w.q_d, w.s_d, H, I, &e);
-    CK(e);
     {
       EpiArgs ea;
       ea.out = ctx->resid[l + 1];
       ea.ld_out = H;
       ea.resid = a.resid_mid;
-      TIMED(P_GEMM, gemm(op(a.act, M, I, I), op(wd, H, I, I), M, H, Epi::kResidF32, ea, err, st));
+      const Operand bd = mlp_b(ctx, w.wd, w.q_d, w.s_d, H, I, false, &e);
+      CK(e);
+      TIMED(P_GEMM, gemm(op(a.act, M, I, I), bd, M, H, Epi::kResidF32, ea, err, st));
     }
   }
 
@@ -609,7 +635,6 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   const double n_valid_total = static_cast<double>(n_valid_local) * ctx->world;
   ctx->last_n_valid = n_valid_local;
   const float unscale = static_cast<float>(1.0 / (kGradScale * n_valid_total));
-  cudaError_t e = cudaSuccess;
 
   // gradients accumulate (lora_grad adds each split's share); this first
   // kernel follows the host's token upload, so it is launched normally and the
@@ -657,7 +682,11 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     // d_xf = dlogits . E  (E [V, H] read MN-major)
     TIMED(P_GEMM, gemm(op(ctx->dl, M, V, ctx->ld_dl), op_mn(E, V, H, H), M, H, Epi::kStoreF32, eb, err, st));
   }
-  TIMED(P_NORM, rmsnorm_backward(ctx->d_xf, xfinal, ctx->final_norm, ctx->dres, ctx->dres16, M, H, eps, 0, st));
+  // an INT8 base's down-projection row scales ride in the fp16 gradient that
+  // is the next input-gradient GEMM's A operand (the GEMM stages the codes)
+  const bool q8_mlp = ctx->rc.base_dtype == LLMCU_BASE_INT8 && ctx->rc.int8_in_gemm && !d.has_mlp();
+  TIMED(P_NORM, rmsnorm_backward(ctx->d_xf, xfinal, ctx->final_norm, ctx->dres, ctx->dres16, M, H, eps, 0, st,
+                                 q8_mlp ? ctx->lw[ctx->L - 1].s_d : nullptr));
 
   // ----------------------------------------------------------- backward
   // The adapter gradients of a layer run on ctx->side, beside the main chain:
@@ -751,20 +780,22 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       CKS(side_grad(l, 0, gb));
     } else {
       // MLP: d_act = dres . W_down (MN-major), SwiGLU backward fused
-      const __half* wd = base_weight(ctx, w.wd, w.q_d, w.s_d, H, I, &e);
-      CK(e);
       {
         EpiArgs ea;
         ea.gu_in = a.gu;
         ea.gu = ctx->dgu;
         ea.ld_gu = 2 * I;
-        TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), op_mn(wd, H, I, I), M, I, Epi::kSwiGLUBwd, ea, err, st, 256));
+        ea.gu_out_scale = q8_mlp ? w.s_gu : nullptr;  // the gate/up row scales, for the next GEMM
+        cudaError_t e = cudaSuccess;
+        const Operand bd = mlp_b(ctx, w.wd, w.q_d, w.s_d, H, I, true, &e);
+        CK(e);
+        TIMED(P_GEMM, gemm(op(ctx->dres16, M, H, H), bd, M, I, Epi::kSwiGLUBwd, ea, err, st, 256));
       }
       // dxn2 = dgu . W_gate/up (MN-major)
-      const __half* wgu = base_weight(ctx, w.wgu, w.q_gu, w.s_gu, 2 * I, H, &e);
+      cudaError_t e = cudaSuccess;
+      const Operand bgu = mlp_b(ctx, w.wgu, w.q_gu, w.s_gu, 2 * I, H, true, &e);
       CK(e);
-      TIMED(P_GEMM, gemm(op(ctx->dgu, M, 2 * I, 2 * I), op_mn(wgu, 2 * I, H, H), M, H, Epi::kStoreF16,
-                         EpiArgs{ctx->dxn, H}, err, st));
+      TIMED(P_GEMM, gemm(op(ctx->dgu, M, 2 * I, 2 * I), bgu, M, H, Epi::kStoreF16, EpiArgs{ctx->dxn, H}, err, st));
     }
     // the layer above's attention-adapter gradients read dres16m, dho, dqkv, dhq
     if (l + 1 < ctx->L) CKS(wait_side(l + 1, 3));
@@ -841,7 +872,8 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     }
     // the MLP batch reads dres16, which the attention-norm backward rewrites
     if (d.has_mlp()) CKS(wait_side(l, 1));
-    TIMED(P_NORM, rmsnorm_backward(ctx->dxn, ctx->resid[l], w.attn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st));
+    TIMED(P_NORM, rmsnorm_backward(ctx->dxn, ctx->resid[l], w.attn_norm, ctx->dres, ctx->dres16, M, H, eps, 1, st,
+                                   q8_mlp && l > 0 ? ctx->lw[l - 1].s_d : nullptr));
     set_pdl(true);
     if (ctx->nccl) {
       // the layer's gradients are complete once its last side launch is

@@ -120,8 +120,9 @@ def _int8_view(base):
     return out
 
 
-@pytest.mark.parametrize("batch,seq", [(2, 64)])
-def test_int8_base_step_matches_golden(llmcu, cuda_device, batch, seq):
+@pytest.mark.parametrize("in_gemm", [False, True])  # one dequantisation pass per weight / codes staged by the GEMM
+@pytest.mark.parametrize("batch,seq", [(2, 64), (4, 64)])  # 128 rows: single CTAs; 256 rows: CTA pairs
+def test_int8_base_step_matches_golden(llmcu, cuda_device, batch, seq, in_gemm):
     """INT8 base: the library quantises the uploaded fp32 weights
     itself; the golden runs on the same quantise-dequantise weights."""
     from oracle import golden as G
@@ -132,7 +133,7 @@ def test_int8_base_step_matches_golden(llmcu, cuda_device, batch, seq):
     model = llmcu.Model(cfg.hidden, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab,
                         cfg.rope_theta, cfg.rms_eps)
     ctx = llmcu.Context(model, llmcu.Lora(cfg.lora_rank, cfg.lora_alpha),
-                        llmcu.Run(batch, seq, base_dtype=llmcu.BASE_INT8))
+                        llmcu.Run(batch, seq, base_dtype=llmcu.BASE_INT8, int8_in_gemm=in_gemm))
     ctx.set_base(base)
     ctx.set_lora_dict(lora)
     ref = G.forward_backward(cfg, _int8_view(base), lora, tok, tgt)
