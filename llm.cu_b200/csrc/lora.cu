@@ -192,20 +192,35 @@ __global__ void __launch_bounds__(256, 1)
 constexpr int kMtRows = 64;
 constexpr int kMtCols = 128;
 constexpr int kMtPad = 8;  // halves of row padding: conflict-free fragment access
+// Q8: the base rows are INT8 codes with per-row scales (src/kernels/quantize.cu:
+// 8-50); the accumulator starts from code * scale in fp32 and sW only holds
+// the merged result.
+template <bool Q8>
 __global__ void __launch_bounds__(128)
-    lora_merge_tc_kernel(const float* __restrict__ flat, LoraDims d, const __half* __restrict__ w, int64_t w_layer,
-                         int d_in, int which, __half* __restrict__ merged, int64_t merged_layer, int ldm) {
+    lora_merge_tc_kernel(const float* __restrict__ flat, LoraDims d, MergeBase src, int d_in, int which,
+                         __half* __restrict__ merged, int64_t merged_layer, int ldm) {
   pdl_trigger();
   __shared__ __align__(16) __half sW[kMtRows][kMtCols + kMtPad];
   __shared__ __align__(16) __half sB[kMtRows][16 + kMtPad];
   __shared__ __align__(16) __half sA[16][kMtCols + kMtPad];
+  __shared__ __align__(16) int8_t sQ[Q8 ? kMtRows : 1][Q8 ? kMtCols + 16 : 16];
   const int l = blockIdx.z, o0 = blockIdx.y * kMtRows, c0 = blockIdx.x * kMtCols;
-  const __half* wl = w + static_cast<int64_t>(l) * w_layer;
-  for (int i = threadIdx.x; i < kMtRows * (kMtCols / 8); i += blockDim.x) {
-    const int rr = i / (kMtCols / 8), ch = i % (kMtCols / 8);
-    const int c = c0 + ch * 8;
-    const bool ok = c < d_in;
-    cp_async_16(smem_u32(&sW[rr][ch * 8]), wl + static_cast<int64_t>(o0 + rr) * d_in + (ok ? c : 0), ok ? 16 : 0);
+  if constexpr (Q8) {
+    const int8_t* ql = src.q + static_cast<int64_t>(l) * src.w_layer;
+    for (int i = threadIdx.x; i < kMtRows * (kMtCols / 16); i += blockDim.x) {
+      const int rr = i / (kMtCols / 16), ch = i % (kMtCols / 16);
+      const int c = c0 + ch * 16;
+      const bool ok = c < d_in;
+      cp_async_16(smem_u32(&sQ[rr][ch * 16]), ql + static_cast<int64_t>(o0 + rr) * d_in + (ok ? c : 0), ok ? 16 : 0);
+    }
+  } else {
+    const __half* wl = src.w + static_cast<int64_t>(l) * src.w_layer;
+    for (int i = threadIdx.x; i < kMtRows * (kMtCols / 8); i += blockDim.x) {
+      const int rr = i / (kMtCols / 8), ch = i % (kMtCols / 8);
+      const int c = c0 + ch * 8;
+      const bool ok = c < d_in;
+      cp_async_16(smem_u32(&sW[rr][ch * 8]), wl + static_cast<int64_t>(o0 + rr) * d_in + (ok ? c : 0), ok ? 16 : 0);
+    }
   }
   cp_async_commit();
   pdl_wait();  // the adapters are written by the previous step's optimizer
@@ -263,6 +278,12 @@ __global__ void __launch_bounds__(128)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int wr = warp * 16;
+  float sc0 = 1.f, sc1 = 1.f;  // Q8: the scales of this thread's two fragment rows
+  if constexpr (Q8) {
+    const float* sl = src.s + static_cast<int64_t>(l) * src.s_layer;
+    sc0 = __ldg(sl + o0 + wr + g);
+    sc1 = __ldg(sl + o0 + wr + g + 8);
+  }
   uint32_t a[4];
   a[0] = *reinterpret_cast<const uint32_t*>(&sB[wr + g][2 * t]);
   a[1] = *reinterpret_cast<const uint32_t*>(&sB[wr + g + 8][2 * t]);
@@ -279,7 +300,15 @@ __global__ void __launch_bounds__(128)
     for (int h = 0; h < 2; ++h) {
       __half2* p0 = reinterpret_cast<__half2*>(&sW[wr + g][(nb + h) * 8 + 2 * t]);
       __half2* p1 = reinterpret_cast<__half2*>(&sW[wr + g + 8][(nb + h) * 8 + 2 * t]);
-      const float2 w0 = __half22float2(*p0), w1 = __half22float2(*p1);
+      float2 w0, w1;
+      if constexpr (Q8) {
+        const int cc = (nb + h) * 8 + 2 * t;
+        w0 = make_float2(static_cast<float>(sQ[wr + g][cc]) * sc0, static_cast<float>(sQ[wr + g][cc + 1]) * sc0);
+        w1 = make_float2(static_cast<float>(sQ[wr + g + 8][cc]) * sc1, static_cast<float>(sQ[wr + g + 8][cc + 1]) * sc1);
+      } else {
+        w0 = __half22float2(*p0);
+        w1 = __half22float2(*p1);
+      }
       float acc[4] = {w0.x, w0.y, w1.x, w1.y};
       mma_16816(acc, a, bf[2 * h], bf[2 * h + 1]);
       *p0 = __floats2half2_rn(acc[0], acc[1]);
@@ -590,12 +619,16 @@ cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const
   };
   // one merged weight: rows [0, rows) of W (d_in columns) plus s B A
   auto main_block = [&](const MergeBase& src, int rows, int d_in, int which, int tiles, __half* dst, int64_t layer) {
-    if (!src.q) {  // fp16 base: tensor-core rank-r update
-      dim3 g((d_in + kMtCols - 1) / kMtCols, rows / kMtRows, n_layers);
-      launch_pdl(lora_merge_tc_kernel, g, 128, 0, st, flat, d, src.w, src.w_layer, d_in, which, dst, layer, d_in + 64);
+    // tensor-core rank-r update over fp16 rows, or INT8 rows (16-column
+    // multiples) starting from code * scale
+    dim3 g((d_in + kMtCols - 1) / kMtCols, rows / kMtRows, n_layers);
+    if (!src.q) {
+      launch_pdl(lora_merge_tc_kernel<false>, g, 128, 0, st, flat, d, src, d_in, which, dst, layer, d_in + 64);
+    } else if (d_in % 16 == 0) {
+      launch_pdl(lora_merge_tc_kernel<true>, g, 128, 0, st, flat, d, src, d_in, which, dst, layer, d_in + 64);
     } else {
-      dim3 g((d_in + kMrgCols - 1) / kMrgCols, rows / (kMrgRows * tiles), n_layers);
-      launch_pdl(lora_merge_main_kernel, g, 256, 0, st, flat, d, src, d_in, which, tiles, dst, layer, d_in + 64);
+      dim3 gm((d_in + kMrgCols - 1) / kMrgCols, rows / (kMrgRows * tiles), n_layers);
+      launch_pdl(lora_merge_main_kernel, gm, 256, 0, st, flat, d, src, d_in, which, tiles, dst, layer, d_in + 64);
     }
   };
   main_block(base.qkv, QKV, H, 0, tiles_for(Q, KV), out.qkv, mqkv_layer);
