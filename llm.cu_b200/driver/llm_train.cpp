@@ -16,7 +16,8 @@
 // every save also writes the AdamW sidecar lora_step{N}_adamw.bin),
 // --rank R / --alpha A (LoRA rank 1..16 and alpha; default the config's),
 // --lora-targets LIST (comma-separated wq,wk,wv,wo,w_gate,w_up,w_down, or
-// "attn" = the reference's q/k/v/o, "mlp", "all"; default attn).
+// "attn" = the reference's q/k/v/o, "mlp", "all"; default attn),
+// --int8-in-gemm (with --int8: the GEMMs stage the INT8 codes themselves).
 // Data parallel: when WORLD_SIZE > 1 (e.g. under torchrun) each process
 // drives GPU LOCAL_RANK, rank 0 writes the NCCL id to --dp-id-file and the
 // others read it; rank r takes sequences r, r+W, ... of every step window.
@@ -55,7 +56,7 @@ int main(int argc, char** argv) {
   const float beta1 = 0.9f, beta2 = 0.999f, eps_adam = 1e-8f, wd = 0.01f;
   std::string config = "1.7b", weights = "weights", data = "data/train_tokens.bin", out = "weights";
   std::string id_file = "/tmp/llmcu_nccl_id";
-  bool synthetic = false, int8 = false;
+  bool synthetic = false, int8 = false, int8_in_gemm = false;
   unsigned long long seed = 1234;
   int lora_rank = 0;
   float lora_alpha = 0.f;
@@ -85,11 +86,13 @@ int main(int argc, char** argv) {
     else if ((v = next("--lora-targets"))) targets_arg = v;
     else if (!strcmp(argv[i], "--synthetic")) synthetic = true;
     else if (!strcmp(argv[i], "--int8")) int8 = true;
+    else if (!strcmp(argv[i], "--int8-in-gemm")) int8_in_gemm = true;
     else if (!strcmp(argv[i], "--help") || !strcmp(argv[i], "-h")) {
       printf("usage: llm_train [--lr F] [--steps N] [--seq-len S] [--save-every N] [--log-every N]\n"
              "                 [--batch B] [--config tiny|1.7b] [--synthetic] [--int8] [--weights DIR]\n"
              "                 [--data FILE] [--out DIR] [--seed N] [--dp-id-file PATH] [--resume N]\n"
-             "                 [--rank R] [--alpha A] [--lora-targets attn|mlp|all|wq,wk,...,w_down]\n");
+             "                 [--rank R] [--alpha A] [--lora-targets attn|mlp|all|wq,wk,...,w_down]\n"
+             "                 [--int8-in-gemm]\n");
       return 0;
     }
   }
@@ -133,7 +136,7 @@ int main(int argc, char** argv) {
     }
     lc.targets = mask;
   }
-  llmcu_run_cfg rc = {batch, seq_len, int8 ? LLMCU_BASE_INT8 : LLMCU_BASE_FP16, 0, 0};
+  llmcu_run_cfg rc = {batch, seq_len, int8 ? LLMCU_BASE_INT8 : LLMCU_BASE_FP16, 0, int8_in_gemm ? 1 : 0};
   if (rank == 0)
     printf("Training config: lr=%.2e steps=%d seq_len=%d batch=%d world=%d model=%s base=%s lora rank=%d "
            "alpha=%g targets=0x%x\n",
