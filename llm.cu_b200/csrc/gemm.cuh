@@ -783,6 +783,7 @@ __global__ void __launch_bounds__(64 + 32 * EW + (Q8 ? kQ8Threads : 0), 1)
   uint64_t* qfull = slab_bar + EW;          // [STAGES] (Q8): the stage's INT8 codes landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qfull + (Q8 ? STAGES : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* conv_ok = reinterpret_cast<volatile int*>(tmem_slot + 2);  // Q8 converters' shared verdict
 
   pdl_trigger();
   const int warp = threadIdx.x >> 5;
@@ -966,7 +967,14 @@ __global__ void __launch_bounds__(64 + 32 * EW + (Q8 ? kQ8Threads : 0), 1)
       const int kb_end = min(nk, (sp + 1) * sh.kb_per_split);
       for (int kb = sp * sh.kb_per_split; kb < kb_end; ++kb, ++it) {
         const int s = it % STAGES;
-        if (!mbar_wait(&qfull[s], (it / STAGES) & 1, abort_flag, err, kErrWaitProducer)) { ok = false; break; }
+        // one thread waits for the codes and publishes the outcome, so that
+        // every converter thread leaves together when a wait gives up
+        if (ct == 0) *conv_ok = mbar_wait(&qfull[s], (it / STAGES) & 1, abort_flag, err, kErrWaitProducer) ? 1 : 0;
+        asm volatile("bar.sync 1, %0;" ::"n"(kQ8Threads) : "memory");
+        if (!*conv_ok) {
+          ok = false;
+          break;
+        }
         const uint32_t sb32 = smem_u32(smem + s * L::kStageBytes + L::kABytes);  // shared-space addresses
         // kBRows x 64 codes = kBRows * 4 groups of 16: every group is read
         // before any fp16 is written over the codes (they share the region)
