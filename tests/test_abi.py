@@ -108,3 +108,28 @@ def test_ref_io_round_trip(tmp_path):
     assert losses.tolist() == [0.0, 1.0]
     assert grads["L0.wq.A"].shape == (4, 256) and after["L1.wo.B"].shape == (256, 4)
     assert grads["L0.wq.A"].ravel()[0] == 2.0
+
+
+def test_config_structs_match_the_header(llmcu, tmp_path):
+    """The ctypes mirrors of the config structs have the C layout: every
+    field at the offset (and the struct at the size) a C compiler gives the
+    header's definition."""
+    structs = {"llmcu_model_cfg": llmcu._ModelCfg, "llmcu_lora_cfg": llmcu._LoraCfg,
+               "llmcu_run_cfg": llmcu._RunCfg, "llmcu_adamw_cfg": llmcu._AdamWCfg}
+    lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "llmcu.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'  printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c99", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True,
+                   timeout=60)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True, timeout=30).stdout.split("\n")
+    got = {tuple(l.split()[:2]): int(l.split()[2]) for l in out if l.strip()}
+    for cname, py in structs.items():
+        assert got[(cname, "size")] == C.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert got[(cname, fname)] == getattr(py, fname).offset, (cname, fname)
