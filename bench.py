@@ -2,6 +2,7 @@
 """bench.py -- LoRA training-step throughput of the B200 build (libllmcu.so).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2|c1|c3|c4]
+                    [--lora-targets attn|mlp|all|wq,...,w_down] [--int8-in-gemm] [--decode N [--int8]]
 
 One step = forward + cross-entropy + backward + AdamW of the Qwen3-1.7B-shape
 LoRA model on one batch of synthetic tokens per GPU.
@@ -21,6 +22,12 @@ Printed JSON line keys beyond the driver contract:
              sample, rank 0 at N = 1 only
   kernels    per-class device time per step from the same event pass
   clocks     nvidia-smi samples taken during the timed region
+
+--lora-targets trains adapters on other projections than the reference's
+q/k/v/o (the MLP's too with `all`); --int8-in-gemm (c4) lets the GEMMs stage
+the INT8 codes instead of one dequantisation pass per weight; --decode N times
+greedy KV-cache generation of N tokens after a 128-token prompt instead of the
+training step.
 """
 from __future__ import annotations
 

@@ -133,3 +133,13 @@ def test_config_structs_match_the_header(llmcu, tmp_path):
         assert got[(cname, "size")] == C.sizeof(py), cname
         for fname, _ in py._fields_:
             assert got[(cname, fname)] == getattr(py, fname).offset, (cname, fname)
+
+
+def test_llm_train_rejects_unknown_lora_targets():
+    exe = os.path.join(ROOT, "llm.cu_b200", "llm_train")
+    if not os.path.exists(exe):
+        pytest.skip("llm_train not built")
+    r = subprocess.run([exe, "--config", "tiny", "--synthetic", "--lora-targets", "wq,w_bogus"], capture_output=True,
+                       text=True, timeout=30)
+    assert r.returncode == 1
+    assert "unknown --lora-targets entry 'w_bogus'" in r.stderr
