@@ -191,7 +191,8 @@ cudaError_t dispatch_q8(Epi epi, bool bmn, const EpiArgs& ea, const CUtensorMap*
   if (!bmn && epi == Epi::kSwiGLU) return launch<256, EpiSwiGLU, false, CG, true>(maps, sh, EpiSwiGLU::Params{}, err, st);
   if (!bmn && epi == Epi::kResidF32) return launch<256, EpiResidF32, false, CG, true>(maps, sh, EpiResidF32::Params{}, err, st);
   if (bmn && epi == Epi::kSwiGLUBwd)
-    return launch<256, EpiSwiGLUBwd, true, CG, true>(maps, sh, EpiSwiGLUBwd::Params{ea.gu_in, ea.ld_gu, ea.gu_out_scale}, err, st);
+    return launch<256, EpiSwiGLUBwdScaled, true, CG, true>(
+        maps, sh, EpiSwiGLUBwdScaled::Params{ea.gu_in, ea.ld_gu, ea.gu_out_scale}, err, st);
   if (bmn && epi == Epi::kStoreF16) return launch<256, EpiStoreF16, true, CG, true>(maps, sh, EpiStoreF16::Params{}, err, st);
   return cudaErrorInvalidValue;
 }

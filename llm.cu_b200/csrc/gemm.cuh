@@ -517,11 +517,15 @@ struct EpiSwiGLU {
       my_g = __ldg(reinterpret_cast<const float2*>(c.col_scale + tile_n * 256 + cc) + c.lane);
       my_u = __ldg(reinterpret_cast<const float2*>(c.col_scale + tile_n * 256 + 128 + cc) + c.lane);
     }
+    const bool scaled = c.col_scale != nullptr;  // warp-uniform
 #pragma unroll
     for (int t = 0; t < 32; ++t) {
       float r0[3], r1[3];
-      const float2 sg2 = make_float2(__shfl_sync(0xffffffffu, my_g.x, t), __shfl_sync(0xffffffffu, my_g.y, t));
-      const float2 su2 = make_float2(__shfl_sync(0xffffffffu, my_u.x, t), __shfl_sync(0xffffffffu, my_u.y, t));
+      float2 sg2 = make_float2(1.f, 1.f), su2 = make_float2(1.f, 1.f);
+      if (scaled) {
+        sg2 = make_float2(__shfl_sync(0xffffffffu, my_g.x, t), __shfl_sync(0xffffffffu, my_g.y, t));
+        su2 = make_float2(__shfl_sync(0xffffffffu, my_u.x, t), __shfl_sync(0xffffffffu, my_u.y, t));
+      }
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const float gv = g[2 * t + e] * (e ? sg2.y : sg2.x), uv = u[2 * t + e] * (e ? su2.y : su2.x);
@@ -560,7 +564,10 @@ struct EpiSwiGLU {
 // factors arrive by plain 16-byte loads (each thread its row's 64 contiguous
 // bytes per 32 columns), one 32-column step ahead, the first issued before
 // the accumulator is ready; outputs leave through the 4-KB slab.
-struct EpiSwiGLUBwd {
+// kScaled: the INT8 in-GEMM mode, whose dgu columns carry the gate/up row
+// scales (out_scale) for the next GEMM; compiled out otherwise.
+template <bool kScaled>
+struct EpiSwiGLUBwdT {
   struct Params {
     const __half* gu_in;  // [M, 2N] interleaved stash
     int ld;
@@ -621,16 +628,22 @@ struct EpiSwiGLUBwd {
       // per dgu column factors of these 32 gate / up columns: lane L holds
       // gate column L and up column L (+128), handed out by shuffle
       float my_g = 1.f, my_u = 1.f;
-      if (p.out_scale) {
+      if (kScaled && p.out_scale) {
         my_g = __ldg(p.out_scale + gcol + 32 * q + c.lane);
         my_u = __ldg(p.out_scale + gcol + 128 + 32 * q + c.lane);
       }
+      const bool scaled = kScaled && p.out_scale != nullptr;  // warp-uniform
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
         const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&f0[t]));
         const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&f1[t]));
-        const float sg0 = __shfl_sync(0xffffffffu, my_g, 2 * t), sg1 = __shfl_sync(0xffffffffu, my_g, 2 * t + 1);
-        const float su0 = __shfl_sync(0xffffffffu, my_u, 2 * t), su1 = __shfl_sync(0xffffffffu, my_u, 2 * t + 1);
+        float sg0 = 1.f, sg1 = 1.f, su0 = 1.f, su1 = 1.f;
+        if (scaled) {
+          sg0 = __shfl_sync(0xffffffffu, my_g, 2 * t);
+          sg1 = __shfl_sync(0xffffffffu, my_g, 2 * t + 1);
+          su0 = __shfl_sync(0xffffffffu, my_u, 2 * t);
+          su1 = __shfl_sync(0xffffffffu, my_u, 2 * t + 1);
+        }
         dg[t] = pack_half2(v[2 * t] * a.x * sg0, v[2 * t + 1] * a.y * sg1);
         du[t] = pack_half2(v[2 * t] * b.x * su0, v[2 * t + 1] * b.y * su1);
       }
@@ -658,6 +671,8 @@ struct EpiSwiGLUBwd {
   }
   __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
 };
+using EpiSwiGLUBwd = EpiSwiGLUBwdT<false>;
+using EpiSwiGLUBwdScaled = EpiSwiGLUBwdT<true>;
 
 // lm_head forward (src/kernels/loss.cu:24-61): per row and 128-column slot
 // (vocab tile x column slice) the slot's max logit m and sum of exp(l - m),
