@@ -1,6 +1,6 @@
-"""KV-cache generation on the GPU (the survey's next-step row "inference
-reuse": llm_engine --generate, src/main.cu:340-385, on the training context's
-weights and current adapters) against the fp32 CPU golden.
+"""KV-cache generation on the GPU (inference reuse of the training context's
+weights and current adapters, as llm_engine --generate does with its own,
+src/main.cu:340-385) against the fp32 CPU golden.
 
 Every step's logits must match the golden's logits of the same prefix to
 rel-L2 <= 1e-2 (fp16 activations against fp32), the chosen ids must be the

@@ -1,6 +1,5 @@
-"""LoRA on the MLP projections and configurable target sets (the survey's
-next-step row "LoRA on MLP projections / configurable rank and targets",
-generalising include/lora.h:22-27, which fixes q/k/v/o) on the GPU against
+"""LoRA on the MLP projections and configurable target sets (generalising
+include/lora.h:22-27, which fixes q/k/v/o) on the GPU against
 the fp32 CPU autograd golden (oracle/golden.py, same formula
 y += (alpha/r) (x A^T) B^T on gate_proj / up_proj / down_proj).
 

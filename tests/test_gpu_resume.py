@@ -1,5 +1,6 @@
-"""Checkpoint / resume on the GPU (the survey's next-step row: an optimizer
-sidecar beside the reference's adapter files, which alone cannot resume).
+"""Checkpoint / resume on the GPU: an AdamW-moment sidecar beside the
+reference's adapter files (the reference saves A and B only and cannot
+resume).
 
 A run that saves adapters + AdamW moments after step 2 and is continued in a
 fresh context from those files must take step 3 as the uninterrupted run

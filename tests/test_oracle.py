@@ -119,7 +119,7 @@ def test_loss_conventions():
     assert abs(a.loss - np.log(cfg.vocab)) < 0.5
 
 
-def test_flop_model_matches_the_survey():
+def test_flop_model_per_token_figures():
     f = G.algorithmic_flops_per_token(G.CFG_QWEN3_1P7B, 512)
     assert f / 1e9 == pytest.approx(7.097, abs=2e-3)
     assert G.algorithmic_flops_per_token(G.CFG_QWEN3_1P7B, 4096) / 1e9 == pytest.approx(8.330, abs=2e-3)
