@@ -28,14 +28,14 @@ four places where the reference's hand-written backward departs from it, so
 that the golden can be pinned against the reference's own CUDA build
 (oracle/ref_harness):
 
-* A12 the final-RMSNorm backward is evaluated at post_attn[L-1] instead of
+* the final-RMSNorm backward is evaluated at post_attn[L-1] instead of
   the real pre-norm hidden ............... src/kernels/lora_backward.cu:245-267
-* A18 the LoRA dX term reads A ([r, d_in]) as if it were [d_in, r]
+* the LoRA dX term reads A ([r, d_in]) as if it were [d_in, r]
   ........................................ src/kernels/lora_backward.cu:87
-* A11 the last position gets no dlogits row (its gradient is zero; the
+* the last position gets no dlogits row (its gradient is zero; the
   reference leaves the row uninitialised, the harness zeroes it)
   ........................................ src/kernels/loss.cu:18-21
-* A14 SwiGLU backward runs in place with d_swiglu aliased to d_gate
+* the SwiGLU backward runs in place with d_swiglu aliased to d_gate
   (src/kernels/lora_backward.cu:287 calls silu_backward(d_gate, .., d_gate,
   d_up)), so d_up is formed from the already-overwritten d_gate:
   d_up = (dy * u * silu'(g)) * silu(g) instead of dy * silu(g)
@@ -219,7 +219,7 @@ def rmsnorm_backward_at(dy: torch.Tensor, x: torch.Tensor, w: torch.Tensor, eps:
 
 
 class _FinalNormRefBug(torch.autograd.Function):
-    """Final RMSNorm whose backward is evaluated at a stand-in input (A12)."""
+    """Final RMSNorm whose backward is evaluated at a stand-in input (post_attn[L-1])."""
 
     @staticmethod
     def forward(ctx, x, x_bwd, w, eps):
@@ -234,7 +234,7 @@ class _FinalNormRefBug(torch.autograd.Function):
 
 
 class _SwiGLURefBug(torch.autograd.Function):
-    """silu(g) * u whose backward reproduces the in-place aliasing of A14."""
+    """silu(g) * u whose backward reproduces the reference's in-place d_gate / d_swiglu aliasing."""
 
     @staticmethod
     def forward(ctx, g, u):
@@ -252,7 +252,7 @@ class _SwiGLURefBug(torch.autograd.Function):
 
 
 class _LoraDownRefBug(torch.autograd.Function):
-    """h = x A^T whose dX reads A [r, d_in] with a [d_in, r] layout (A18)."""
+    """h = x A^T whose dX reads A [r, d_in] with a [d_in, r] layout (the reference's misread)."""
 
     @staticmethod
     def forward(ctx, x, A):

@@ -66,7 +66,7 @@ def test_true_gradient_golden_shares_the_reference_forward(case):
 
 
 def test_ref_bug_switches_are_the_only_difference():
-    """With B = 0 (the reference's own adapter init) the A18 dX term vanishes
+    """With B = 0 (the reference's own adapter init) the misread-A dX term vanishes
     and both goldens share the forward; dA is exactly zero in both."""
     cfg = G.CFG_TINY
     base = G.make_base_weights(cfg, 1)
