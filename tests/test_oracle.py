@@ -83,18 +83,20 @@ def test_ref_bug_switches_are_the_only_difference():
 
 def test_golden_gradient_matches_finite_differences():
     """Autograd of the golden against a central difference of its own loss on
-    a few adapter entries (float64 tiny model)."""
+    a few adapter entries of every projection kind, MLP adapters included
+    (float64 tiny model)."""
     import torch
     torch.set_default_dtype(torch.float64)
     try:
         cfg = G.ModelCfg(hidden=64, n_layers=1, n_heads=2, n_kv_heads=1, head_dim=64, ffn=128, vocab=97,
                          lora_rank=2, lora_alpha=4.0)
         base = {k: v.astype(np.float64) for k, v in G.make_base_weights(cfg, 5, std=0.2).items()}
-        lora = {k: v.astype(np.float64) for k, v in G.make_lora(cfg, 6, b_std=0.2).items()}
+        lora = {k: v.astype(np.float64) for k, v in G.make_lora(cfg, 6, b_std=0.2, projs=G.ALL_PROJS).items()}
         tok, tgt = G.make_tokens(cfg, 1, 8, 7)
         res = G.forward_backward(cfg, base, lora, tok, tgt)
         rng = np.random.default_rng(0)
-        for key in ("L0.wq.A", "L0.wv.B", "L0.wo.A", "L0.wk.B"):
+        for key in ("L0.wq.A", "L0.wv.B", "L0.wo.A", "L0.wk.B", "L0.w_gate.A", "L0.w_up.B", "L0.w_down.A",
+                    "L0.w_down.B"):
             idx = tuple(rng.integers(0, s) for s in lora[key].shape)
             h = 1e-5
             lp = {k: v.copy() for k, v in lora.items()}
