@@ -211,3 +211,26 @@ def test_golden_target_subsets():
     res = G.forward_backward(tiny, base, lora, tok, tgt)
     assert set(res.grads) == set(lora)
     assert all(np.abs(g).sum() > 0 for g in res.grads.values())
+
+
+def test_bench_flop_model_and_targets():
+    """bench.py's own FLOP model (no oracle import on its timed path) equals the
+    golden's, for the reference's targets and for all seven; its --lora-targets
+    parser keeps the projection order and rejects unknown names."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(os.path.dirname(HERE), "bench.py"))
+    b = importlib.util.module_from_spec(spec)
+    sys.modules["bench_mod"] = b
+    spec.loader.exec_module(b)
+    from conftest import load_binding
+    m = load_binding()
+    model = m.Model.qwen3_1p7b()
+    full = G.CFG_QWEN3_1P7B
+    for projs in (G.PROJS, G.ALL_PROJS):
+        got = b.algorithmic_flops_per_token(model, 512, full.n_lora_params(projs))
+        assert got == pytest.approx(G.algorithmic_flops_per_token(full, 512, projs), rel=1e-12)
+    assert b.parse_targets("attn") == G.PROJS
+    assert b.parse_targets("all") == G.ALL_PROJS
+    assert b.parse_targets("w_down,wq") == ("wq", "w_down")
+    with pytest.raises(SystemExit):
+        b.parse_targets("wq,w_bogus")
