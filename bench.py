@@ -165,6 +165,34 @@ def make_tokens(vocab, batch, seq, seed, dist):
     return np.ascontiguousarray(win[:, :seq]), np.ascontiguousarray(win[:, 1:])
 
 
+def shard_seed(rank: int) -> int:
+    """Rank r of a data-parallel run draws its own sequences with seed 1000 + r
+    (weak scaling: every rank adds one full batch of distinct tokens)."""
+    return 1000 + rank
+
+
+def rank_max(dist_, world: int, x: float) -> float:
+    """Max of a per-rank float over the host process group (gloo): the timed
+    figure of an N-GPU run is the slowest rank's."""
+    if world == 1:
+        return x
+    import torch
+    t = torch.tensor([x], dtype=torch.float64)
+    dist_.all_reduce(t, op=dist_.ReduceOp.MAX)
+    return float(t.item())
+
+
+def share_unique_id(dist_, rank: int, world: int, make_id) -> bytes:
+    """Rank 0 creates the NCCL unique id (make_id, the library's
+    llmcu_dp_get_unique_id) and every rank receives it over the host process
+    group; the other ranks never call make_id."""
+    if world == 1:
+        return make_id()
+    obj = [make_id() if rank == 0 else None]
+    dist_.broadcast_object_list(obj, src=0)
+    return obj[0]
+
+
 def cpu_baseline(seq):
     """fp32 CPU autograd golden on a bounded sample: 2 layers of the full
     shape (full vocabulary), batch 1 x seq, one warm-up + timed steps; the
@@ -323,11 +351,7 @@ def main():
             dist_.barrier()
 
     def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64)
-        dist_.all_reduce(t, op=dist_.ReduceOp.MAX)
-        return float(t.item())
+        return rank_max(dist_, world, x)
 
     m = load_binding()
     model = m.Model.qwen3_1p7b(n_layers=args.layers)
@@ -335,14 +359,13 @@ def main():
     ctx = m.Context(model, m.Lora(16, 32.0, m.targets_mask(projs)),
                     m.Run(B, S, base_dtype, int8_in_gemm=args.int8_in_gemm), device=local)
     if world > 1:
-        obj = [m.Context.dp_unique_id() if rank == 0 else None]
-        dist_.broadcast_object_list(obj, src=0)
+        uid = share_unique_id(dist_, rank, world, m.Context.dp_unique_id)
         ctx.dp_set_timeout_ms(120000)
-        ctx.dp_init(obj[0], rank, world)
+        ctx.dp_init(uid, rank, world)
     ctx.init_base_synthetic(seed=1, std=0.02)
     ctx.init_lora_synthetic(seed=2, b_std=0.01)
 
-    tok, tgt = make_tokens(model.vocab, B, S, 1000 + rank, dist)
+    tok, tgt = make_tokens(model.vocab, B, S, shard_seed(rank), dist)
     d_tok = torch.from_numpy(tok).cuda()
     d_tgt = torch.from_numpy(tgt).cuda()
     h_tok = torch.from_numpy(tok).pin_memory()
