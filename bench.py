@@ -451,7 +451,6 @@ def main():
     kernels = {k: {"ms_per_step": round(v["ms"] / n_prof, 3), "launches_per_step": v["launches"] / n_prof}
                for k, v in prof.items() if v["launches"]}
     gpu_launches = int(sum(v["launches"] for v in prof.values()) / n_prof * args.steps)
-    step_flops = algorithmic_gemm_flops_per_token(model)  # noqa: F841
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
