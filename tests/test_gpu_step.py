@@ -154,3 +154,56 @@ def test_long_sequence_step_matches_golden(llmcu, cuda_device):
     assert abs(loss - ref.loss) <= LOSS_RTOL * abs(ref.loss), (loss, ref.loss)
     _check_dicts(G, ctx.grads_dict(), ref.grads, "grad")
     ctx.close()
+
+
+def test_ragged_steps_and_refused_inputs(llmcu, cuda_device):
+    """One context sized 4 x 96 takes smaller steps (fewer sequences, lengths
+    that are no multiple of the 128-row tiles, down to two positions) and each
+    matches the golden of the same batch.  Sizes outside [1, max_batch] x
+    [2, max_seq] are refused on the host; a token or target id outside
+    [0, vocab) is caught by the embedding / cross-entropy kernels' own range
+    checks (the id is never used as an address) and reported as INVALID_ARG,
+    after which the context takes valid steps again."""
+    from oracle import golden as G
+    cfg = G.CFG_TINY
+    base = G.make_base_weights(cfg, 21, round_fp16=True)
+    lora = G.make_lora(cfg, 22)
+    model = llmcu.Model(cfg.hidden, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab,
+                        cfg.rope_theta, cfg.rms_eps)
+    ctx = llmcu.Context(model, llmcu.Lora(cfg.lora_rank, cfg.lora_alpha), llmcu.Run(4, 96))
+    ctx.set_base(base)
+    ctx.set_lora_dict(lora)
+
+    def step_matches(b, s, seed):
+        tok, tgt = G.make_tokens(cfg, b, s, seed)
+        ref = G.forward_backward(cfg, base, lora, tok, tgt)
+        loss = ctx.forward_backward(tok, tgt)
+        assert abs(loss - ref.loss) <= LOSS_RTOL * abs(ref.loss), (b, s, loss, ref.loss)
+        got = ctx.grads_dict()
+        # at seq 2 only position 0 is scored and it attends to itself alone
+        # (softmax weight exactly 1), so the q/k adapters' gradients are zero
+        # in exact arithmetic; the GPU's must sit at rounding level
+        zero = {k for k, g in ref.grads.items() if not np.any(g)}
+        assert all(k.split(".")[1] in ("wq", "wk") for k in zero) and (s == 2 or not zero), sorted(zero)
+        scale = np.median([np.linalg.norm(ref.grads[k]) for k in ref.grads if k not in zero])
+        for k in zero:
+            assert np.linalg.norm(got[k]) <= 1e-4 * scale, (k, float(np.linalg.norm(got[k])), scale)
+        _check_dicts(G, got, {k: g for k, g in ref.grads.items() if k not in zero}, f"grad {b}x{s}")
+
+    for i, (b, s) in enumerate([(3, 40), (1, 96), (4, 2), (2, 77)]):
+        step_matches(b, s, 23 + i)
+    for b, s in [(5, 32), (2, 97), (2, 1), (0, 32)]:
+        z = np.zeros((b, s), np.int32)
+        with pytest.raises(llmcu.LlmcuError) as e:
+            ctx.forward_backward(z, z)
+        assert e.value.status == 1, (b, s)
+    tok, tgt = G.make_tokens(cfg, 2, 32, 29)
+    for which, pos, bad in [("tokens", (0, 5), cfg.vocab), ("tokens", (1, 0), -1), ("targets", (1, 7), cfg.vocab),
+                            ("targets", (0, 0), -3)]:
+        t, g = tok.copy(), tgt.copy()
+        (t if which == "tokens" else g)[pos] = bad
+        with pytest.raises(llmcu.LlmcuError) as e:
+            ctx.forward_backward(t, g)
+        assert e.value.status == 1 and "vocab" in str(e.value), (which, pos, bad, str(e.value))
+    step_matches(2, 32, 29)
+    ctx.close()
