@@ -333,8 +333,17 @@ class Context:
     def _tok(a):
         return np.ascontiguousarray(a, dtype=np.int32)
 
+    @classmethod
+    def _batch(cls, tokens, targets):
+        """int32 [B, S] tokens and targets of one shape (the library copies
+        B * S ids from each host pointer)."""
+        t, g = cls._tok(tokens), cls._tok(targets)
+        if t.ndim != 2 or g.shape != t.shape:
+            raise ValueError(f"tokens {t.shape} and targets {g.shape} must be one [batch, seq] shape")
+        return t, g
+
     def forward_backward(self, tokens: np.ndarray, targets: np.ndarray) -> float:
-        t, g = self._tok(tokens), self._tok(targets)
+        t, g = self._batch(tokens, targets)
         B, S = t.shape
         loss = C.c_float()
         self._check(lib().llmcu_forward_backward(self._h, _ptr(t), _ptr(g), B, S, C.byref(loss)),
@@ -346,7 +355,7 @@ class Context:
         self._check(lib().llmcu_adamw(self._h, C.byref(o), step), "adamw")
 
     def train_step(self, tokens: np.ndarray, targets: np.ndarray, opt: AdamW, step: int) -> float:
-        t, g = self._tok(tokens), self._tok(targets)
+        t, g = self._batch(tokens, targets)
         B, S = t.shape
         o = _AdamWCfg(opt.lr, opt.beta1, opt.beta2, opt.eps, opt.weight_decay)
         loss = C.c_float()

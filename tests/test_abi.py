@@ -143,3 +143,15 @@ def test_llm_train_rejects_unknown_lora_targets():
                        text=True, timeout=30)
     assert r.returncode == 1
     assert "unknown --lora-targets entry 'w_bogus'" in r.stderr
+
+
+def test_step_inputs_must_share_one_shape(llmcu):
+    """The library copies batch * seq ids from each host pointer, so the
+    binding refuses tokens and targets of different shapes before any call."""
+    Ctx = llmcu.Context
+    t, g = Ctx._batch(np.arange(6, dtype=np.int64).reshape(2, 3), [[1, 2, 3], [4, 5, 6]])
+    assert t.dtype == np.int32 and g.dtype == np.int32 and t.flags.c_contiguous and t.shape == g.shape == (2, 3)
+    for tok, tgt in [(np.zeros((2, 3)), np.zeros((2, 2))), (np.zeros((2, 3)), np.zeros((3, 2))),
+                     (np.zeros(6), np.zeros(6)), (np.zeros((2, 3)), np.zeros((1, 3)))]:
+        with pytest.raises(ValueError):
+            Ctx._batch(tok, tgt)
