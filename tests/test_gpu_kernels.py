@@ -16,8 +16,8 @@ pytestmark = pytest.mark.gpu
 
 
 def rel_l2(a, b):
-    a = a.double().flatten()
-    b = b.double().flatten()
+    a = a.detach().double().flatten()
+    b = b.detach().double().flatten()
     return float((a - b).norm() / b.norm().clamp_min(1e-30))
 
 
