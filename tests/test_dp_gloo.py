@@ -43,3 +43,14 @@ def test_dp_host_logic_gloo(world):
                 p.wait()
     for r, (p, out) in enumerate(zip(procs, outs)):
         assert p.returncode == 0, f"rank {r} exited {p.returncode}:\n{out[-3000:]}"
+
+
+def test_reference_arm_runs_on_rank_zero_only():
+    """Under torchrun the reference arm is timed by rank 0 alone; every other
+    rank exits 0 without work or output."""
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1", CUDA_VISIBLE_DEVICES="")
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--gpus", "2",
+                        "--steps", "1", "--warmup", "3"], env=env, cwd=ROOT, capture_output=True, text=True,
+                       timeout=120)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip() == "", r.stdout
