@@ -185,7 +185,15 @@ int32_t llmcu_lora_targets(const llmcu_ctx* ctx);
 /* One full step: lora_grads_zero + transformer_forward_lora +
  * cross_entropy_forward + transformer_backward_lora + adamw_step_lora
  * (src/train.cu:251-291).  tokens/targets are HOST int32 [batch, seq];
- * *loss_out receives the mean NLL (over all ranks when data parallel). */
+ * *loss_out receives the mean NLL (over all ranks when data parallel).
+ *
+ * Argument rules of every step entry point: batch in [1, max_batch] and seq
+ * in [2, max_seq] of the context's llmcu_run_cfg, else LLMCU_ERR_INVALID_ARG
+ * before any work.  Ids are checked on the device: a token outside
+ * [0, vocab) embeds as id 0 and a target outside it scores nothing, the step
+ * runs to its end, and the call that reads the loss (this one, or
+ * llmcu_read_loss after llmcu_train_step_device) returns
+ * LLMCU_ERR_INVALID_ARG; the context stays usable. */
 llmcu_status llmcu_train_step(llmcu_ctx* ctx, const int32_t* tokens, const int32_t* targets,
                               int batch, int seq, const llmcu_adamw_cfg* opt, int step,
                               float* loss_out);
