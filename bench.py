@@ -225,7 +225,11 @@ def cpu_baseline(seq):
 
 def run_reference(args, workload):
     """The reference trainer's own CUDA code (compiled from its sources into
-    oracle/_ref by oracle/ref_harness/Makefile) on one GPU, rank 0 only."""
+    oracle/_ref by oracle/ref_harness/Makefile) on one GPU, rank 0 only: the
+    whole batch of the workload per step (the reference runs its B sequences
+    one after another, src/train.cu:251-291 per sequence, then one AdamW), on
+    the same token windows as this arm's rank 0 (make_tokens, seed
+    shard_seed(0))."""
     B, S, dist, base_dtype, desc = WORKLOADS[workload]
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -233,28 +237,40 @@ def run_reference(args, workload):
     exe = os.path.join(ROOT, "oracle", "_ref", "ref_harness_full")
     line = {"metric": METRIC, "unit": UNIT, "higher_is_better": True, "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": workload, "description": desc}}
+            "data": "synthetic", "config": {"workload": workload, "description": desc, "global_batch": B,
+                                            "seq_len": S}}
     if not os.path.exists(exe):
         line["unavailable"] = "oracle/_ref/ref_harness_full was not built (make -C oracle/ref_harness)"
         print(json.dumps(line))
         return 0
-    # bounded sample: one sequence per step (the reference runs B sequences one after another)
-    sample_b = 1
-    cmd = [exe, "bench", str(sample_b), str(S), str(args.steps), str(args.warmup)]
-    r = subprocess.run(cmd, capture_output=True, text=True, timeout=3000)
+    vocab = 151936
+    tok, tgt = make_tokens(vocab, B, S, shard_seed(0), dist)
+    windows = np.concatenate([tok, tgt[:, -1:]], axis=1).astype(np.int32)  # [B, S + 1]
+    fd, tok_path = tempfile.mkstemp(suffix=".i32")
+    os.close(fd)
+    windows.tofile(tok_path)
+    try:
+        cmd = [exe, "bench", str(B), str(S), str(args.steps), str(args.warmup), tok_path]
+        t0 = time.perf_counter()
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=3000)
+        wall = time.perf_counter() - t0
+    finally:
+        os.unlink(tok_path)
     if r.returncode != 0:
         line["unavailable"] = f"reference harness exited {r.returncode}: {r.stderr.strip()[-200:]}"
         print(json.dumps(line))
         return 0
     res = json.loads(r.stdout.strip().splitlines()[-1])
     v = res["tokens_per_s"]
-    line.update({"value": round(v, 3), "ms_per_step": round(res["ms_per_step"] * B / sample_b, 3),
+    line.update({"value": round(v, 3), "ms_per_step": round(res["ms_per_step"], 3), "loss": res.get("loss"),
+                 "wall_s": round(wall, 1),
                  "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                  "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": 1, "kind": "reference",
                                   "sample": f"reference trainer's own CUDA code (visheshnarayan/llm.cu src/kernels/"
                                             f"*.cu, compute_80 PTX JIT on the B200) via oracle/_ref/ref_harness_full,"
-                                            f" {sample_b} sequence x seq {S} per step (of batch {B}), fp32, "
-                                            f"cudaEvent timing; tokens/s = seq / step time"},
+                                            f" the whole batch of {B} x seq {S} per step (its sequences one after "
+                                            f"another, then one AdamW), {dist} token windows identical to this "
+                                            f"workload's rank 0, fp32, cudaEvent timing over {args.steps} steps"},
                  "gpu_launches": None})
     print(json.dumps(line))
     return 0
@@ -399,21 +415,24 @@ def main():
     value = tokens_per_step / (ms / 1e3)
 
     # ------------------------------------------------ e2e: host-buffer public API
-    n_e2e = max(2, min(args.steps, 5))
+    # the same number of steps as `value`, timed by the host clock: every call
+    # copies this step's tokens/targets from pinned host memory, runs the step
+    # and reads the loss back (llmcu_train_step returns after that D2H copy)
+    n_e2e = args.steps
     barrier()
     torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
+    t0 = time.perf_counter()
     for _ in range(n_e2e):
         step += 1
         ctx.train_step(h_tok.numpy(), h_tgt.numpy(), opt, step)
-    f1.record(stream)
-    f1.synchronize()
+    t1 = time.perf_counter()
     barrier()
-    ms_e2e = max_over_ranks(f0.elapsed_time(f1) / n_e2e)
+    ms_e2e = max_over_ranks((t1 - t0) * 1e3 / n_e2e)
     e2e = {"value": round(tokens_per_step / (ms_e2e / 1e3), 3), "unit": UNIT,
            "h2d_bytes_per_step": int(h_tok.numel() * 4 + h_tgt.numel() * 4), "d2h_bytes_per_step": 8,
-           "ms_per_step": round(ms_e2e, 3), "steps": n_e2e, "api": "llmcu_train_step (host int32 tokens/targets)"}
+           "ms_per_step": round(ms_e2e, 3), "steps": n_e2e, "timer": "host perf_counter, max over ranks",
+           "api": "llmcu_train_step (host int32 tokens/targets; the loss and the device error word, 4 B each, "
+                  "read back every step)"}
 
     # ------------------------------------- per-kernel-class events (roofline)
     n_prof = 2

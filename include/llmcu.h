@@ -223,6 +223,24 @@ llmcu_status llmcu_save_lora(llmcu_ctx* ctx, const char* dir, int step);
 /* Reads the same files back (e.g. those written by save_lora.py --from-hf). */
 llmcu_status llmcu_load_lora(llmcu_ctx* ctx, const char* dir, int step);
 
+/* The same adapter files on the host alone, no device or context needed (the
+ * file side of llmcu_save_lora / llmcu_load_lora, which call the same code
+ * after / before their device copy): for converters and checkpoint tools that
+ * run where there is no GPU.  `flat` is the library's adapter layout: per
+ * layer, for each target projection in llmcu_proj order, A [rank, d_in] then
+ * B [d_out, rank], fp32 -- llmcu_lora_layout_count floats in all (0 for an
+ * invalid layout).  Same file names and contents as save_lora
+ * (src/train.cu:146-170); LLMCU_ERR_IO for a missing, short or unwritable
+ * file, LLMCU_ERR_INVALID_ARG for a null pointer or invalid layout. */
+typedef struct {
+    int32_t n_layers, hidden, q_dim, kv_dim, ffn;
+    int32_t rank;     /* 1..16 */
+    int32_t targets;  /* as llmcu_lora_cfg.targets (0 = q, k, v, o) */
+} llmcu_lora_layout;
+int64_t llmcu_lora_layout_count(const llmcu_lora_layout* layout);
+llmcu_status llmcu_lora_files_write(const llmcu_lora_layout* layout, const float* flat, const char* dir, int step);
+llmcu_status llmcu_lora_files_read(const llmcu_lora_layout* layout, float* flat, const char* dir, int step);
+
 /* Greedy generation with a KV cache (llm_engine --generate, src/main.cu:340-385,
  * on the training context's weights and current adapters): the prompt (one
  * sequence of n_prompt host ids) runs through the batched forward and fills the
@@ -285,7 +303,22 @@ llmcu_status llmcu_profile_read(llmcu_ctx* ctx, char* buf, size_t len, int reset
 
 /* ------------------------------------------------------------ kernel test
  * Single-kernel entry points on DEVICE pointers, used by the kernel-level
- * parity tests.  `stream` is a cudaStream_t; results are asynchronous. */
+ * parity tests.  `stream` is a cudaStream_t; results are asynchronous.  The
+ * returned status covers the launch: LLMCU_ERR_INVALID_ARG for a null pointer
+ * or a non-positive size, LLMCU_ERR_UNSUPPORTED for a base address or row
+ * stride the TMA descriptors refuse (they need 16-byte alignment) or an
+ * unsupported head_dim, LLMCU_ERR_CUDA for a failed launch.  What the kernels
+ * find while they run (a bounded wait that gave up, leaving a partial result)
+ * is reported afterwards by llmcu_kernel_checks. */
+
+/* Device-side checks of the kernel-level entry points below: their kernels OR
+ * an error bit into one word per device, held by the library, when a bounded
+ * wait gives up (and then leave their outputs partly written).  This call
+ * synchronises `stream`, reads the current device's word, clears it, and
+ * returns LLMCU_ERR_DEVICE_CHECK if any bit was set since the last call
+ * (LLMCU_OK otherwise); *bits (nullable) receives the raw bits.  No reference
+ * counterpart: the reference's kernels have no device-side checks. */
+llmcu_status llmcu_kernel_checks(void* stream, int* bits);
 
 /* C[M,N] (fp32) = A[M,K] . B[N,K]^T, fp16 inputs, K-major rows with leading
  * dims lda/ldb/ldc in elements -- the NT product of matmul_kernel
@@ -324,14 +357,17 @@ llmcu_status llmcu_attention_bwd(const void* q, const void* k, const void* v, co
  * GPU that loads the library holds until the process exits:
  *   - batch * n_heads * seq must be <= 1,048,576, else LLMCU_ERR_UNSUPPORTED
  *     and nothing is launched;
- *   - the first call on a device looks up that device's copy of the array
- *     (make it with the intended device current);
  *   - all calls share the one array: calls that overlap on the GPU (different
  *     streams, or several host threads) race and give wrong results; calls on
  *     one stream are ordered and safe.  Every entry the kernels read is written
  *     earlier in the same call, so stale contents from a previous call are
- *     never used.
- * Same arguments, layouts and results as llmcu_attention_bwd otherwise. */
+ *     never used;
+ *   - each call looks up the current device's copy of the array (so make the
+ *     call with the intended device current);
+ *   - a bounded wait that gives up inside the kernels is reported, as for the
+ *     other kernel-level entry points, by llmcu_kernel_checks.
+ * Same arguments, layouts, statuses and results as llmcu_attention_bwd
+ * otherwise. */
 llmcu_status llmcu_attention_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
                                          const void* dout, const float* lse, float* dq, float* dk, void* dv,
                                          int batch, int seq, int n_heads, int n_kv_heads, int head_dim,

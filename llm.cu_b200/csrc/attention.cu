@@ -6,8 +6,6 @@
 // K/V gradients, src/kernels/lora_backward.cu:104-208).  The kernels are the
 // tcgen05 ones in attention_tc.cu; this file holds the dO.O row sums of the
 // backward, the dispatch, and the allocation-free backward entry point.
-#include <mutex>
-
 #include "../../include/llmcu.h"
 #include "common.cuh"
 
@@ -77,28 +75,17 @@ namespace llmcu {
 // File-scope scratch for the row-wise dO.O sums of llmcu_attention_bwd_noalloc.
 // Every device that loads this library holds it (4 MiB) until the process
 // exits.  In host code the name is only a stand-in; the device address comes
-// from cudaGetSymbolAddress, looked up once per device with that device current.
+// from cudaGetSymbolAddress with the device current, looked up on every call
+// (so it is never stale, e.g. after cudaDeviceReset reloads the module).
 namespace {
 constexpr int64_t kNoAllocDeltaFloats = 1 << 20;  // batch * n_heads * seq <= 1,048,576
 __device__ __align__(256) float g_noalloc_delta[kNoAllocDeltaFloats];
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mu;
-float* g_noalloc_ptr[kMaxDevices] = {};
 
 cudaError_t noalloc_scratch(float** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_delta);
-    if (e != cudaSuccess) return e;
-    g_noalloc_ptr[dev] = static_cast<float*>(p);
-  }
-  *out = g_noalloc_ptr[dev];
-  return cudaSuccess;
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_delta);
+  *out = static_cast<float*>(p);
+  return e;
 }
 }  // namespace
 
@@ -116,12 +103,14 @@ extern "C" llmcu_status llmcu_attention_bwd_noalloc(const void* q, const void* k
   if (static_cast<int64_t>(batch) * n_heads * seq > kNoAllocDeltaFloats) return LLMCU_ERR_UNSUPPORTED;
   if (head_dim != 64 && head_dim != 128) return LLMCU_ERR_UNSUPPORTED;
   float* delta = nullptr;
-  if (noalloc_scratch(&delta) != cudaSuccess) return LLMCU_ERR_CUDA;
+  int* err = nullptr;  // the kernel-level entry points' error word (llmcu_kernel_checks)
+  if (noalloc_scratch(&delta) != cudaSuccess || kernel_err_word(&err) != cudaSuccess) return LLMCU_ERR_CUDA;
   const int ldo = n_heads * head_dim;
   const cudaError_t e = attention_backward(
       static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v),
       static_cast<const __half*>(o), static_cast<const __half*>(dout), lse, delta, dq, dk, static_cast<__half*>(dv),
-      batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk, ldv, ldo, ldo, n_kv_heads * head_dim, lddv, nullptr,
+      batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk, ldv, ldo, ldo, n_kv_heads * head_dim, lddv, err,
       static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? LLMCU_OK : LLMCU_ERR_CUDA;
+  // as llmcu_attention_bwd: a refused pointer / stride (TMA descriptor) is UNSUPPORTED
+  return e == cudaSuccess ? LLMCU_OK : (e == cudaErrorInvalidValue ? LLMCU_ERR_UNSUPPORTED : LLMCU_ERR_CUDA);
 }

@@ -616,11 +616,12 @@ cudaError_t bwd_tc_launch(const __half* q, const __half* k, const __half* v, con
       !f32_slab_map(&mdq, dq, B * S, nh * HD, lddq))
     return cudaErrorInvalidValue;
   auto kern = attn_bwd_tc_kernel<HD>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+  static std::atomic<unsigned long long> attr_set{0};
+  {
+    cudaError_t e = once_per_device(attr_set, [&] {
+      return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    });
     if (e != cudaSuccess) return e;
-    attr = true;
   }
   // dQ accumulates partial products of every key tile (into zeros)
   if (!dq_zeroed) {
@@ -643,14 +644,15 @@ cudaError_t fwd_tc_launch(const __half* q, const __half* k, const __half* v, __h
       !tile_map(&mv, v, B * S, nkv * HD, ldv))
     return cudaErrorInvalidValue;
   auto kern = attn_fwd_tc_kernel<HD>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+  static std::atomic<unsigned long long> attr_set{0};
+  {
+    cudaError_t e = once_per_device(attr_set, [&] {
+      cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+      // two CTAs per SM need the whole shared-memory carveout
+      if (r == cudaSuccess) r = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+      return r;
+    });
     if (e != cudaSuccess) return e;
-    // two CTAs per SM need the whole shared-memory carveout
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    if (e != cudaSuccess) return e;
-    attr = true;
   }
   dim3 grid(nh, B, (S + kTq - 1) / kTq);
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));

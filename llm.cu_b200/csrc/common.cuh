@@ -4,11 +4,35 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "sm100.cuh"
 
 namespace llmcu {
+
+// Runs `set` (cudaFuncSetAttribute calls for one kernel) once on each device
+// the process launches that kernel on: function attributes apply per device,
+// so a process-wide flag would leave a second device without them.  `mask`
+// holds one bit per device ordinal (devices past 63 run `set` every time).
+template <class F>
+inline cudaError_t once_per_device(std::atomic<unsigned long long>& mask, F&& set) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return set();
+  const unsigned long long bit = 1ull << dev;
+  if (mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = set();  // two threads may both get here; setting an attribute twice is harmless
+  if (e == cudaSuccess) mask.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
+// Device error word of the kernel-level entry points (llmcu_gemm_*,
+// llmcu_attention_*): one int per device, held by the library, into which
+// their kernels OR the DeviceErr bits of bounded waits that gave up.  The
+// address belongs to the current device and is looked up on every call.
+cudaError_t kernel_err_word(int** out);
 
 // Programmatic dependent launch for the calling host thread: on while a
 // training step issues its chain of kernels (each awaits its predecessor in

@@ -101,11 +101,12 @@ cudaError_t launch(const CUtensorMap* maps, const GemmShape& sh, const typename 
   static_assert(L::kBytes <= 232448, "shared memory budget");
   constexpr int kThreads = 64 + 32 * kEpiWarps + (Q8 ? kQ8Threads : 0);
   auto kern = gemm_tc_kernel<BN, S, kEpiWarps, E, BMN, CG, Q8>;
-  static bool attr_done = false;  // set once per instantiation
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+  static std::atomic<unsigned long long> attr_set{0};  // per instantiation, one bit per device
+  {
+    cudaError_t e = once_per_device(attr_set, [&] {
+      return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    });
     if (e != cudaSuccess) return e;
-    attr_done = true;
   }
   const int units = sh.num_tiles * sh.splits;
   if constexpr (CG == 1) {

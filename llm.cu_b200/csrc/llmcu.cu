@@ -1388,55 +1388,85 @@ llmcu_status llmcu_read_loss(llmcu_ctx* ctx, float* loss_out) {
 // like the base weights they adapt)
 static const char* kProjNames[kNumProj] = {"wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"};
 
-llmcu_status llmcu_save_lora(llmcu_ctx* ctx, const char* dir, int step) {
-  if (!ctx || !dir) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null argument");
-  const LoraDims& d = ctx->ld;
-  std::vector<float> A, B;
-  for (int l = 0; l < ctx->L; ++l) {
+// The adapter files of one step (src/train.cu:146-170's names and layout:
+// dir/lora_step{step}_layer{l}_{proj}_{A,B}.bin, raw fp32, A [r, d_in],
+// B [d_out, r], no header) from / into the flat host layout of `d`.  `what`
+// receives the failing path.
+static llmcu_status lora_files_io(const LoraDims& d, int n_layers, float* flat, const char* dir, int step, bool write,
+                                  std::string* what) {
+  for (int l = 0; l < n_layers; ++l) {
+    float* base = flat + d.per_layer * l;
     for (int p = 0; p < kNumProj; ++p) {
       if (!d.has(p)) continue;
-      A.resize(static_cast<size_t>(d.r) * d.d_in(p));
-      B.resize(static_cast<size_t>(d.d_out(p)) * d.r);
-      CKS(llmcu_get_lora(ctx, l, p, A.data(), B.data()));
-      const std::vector<float>* parts[2] = {&A, &B};
+      const size_t n[2] = {static_cast<size_t>(d.r) * d.d_in(p), static_cast<size_t>(d.d_out(p)) * d.r};
+      float* part[2] = {base + d.offA(p), base + d.offB(p)};
       const char* ab[2] = {"A", "B"};
       for (int i = 0; i < 2; ++i) {
         char path[1024];
         snprintf(path, sizeof(path), "%s/lora_step%d_layer%d_%s_%s.bin", dir, step, l, kProjNames[p], ab[i]);
-        FILE* f = fopen(path, "wb");
-        if (!f) return fail(ctx, LLMCU_ERR_IO, "cannot write %s", path);
-        const size_t n = fwrite(parts[i]->data(), sizeof(float), parts[i]->size(), f);
-        fclose(f);
-        if (n != parts[i]->size()) return fail(ctx, LLMCU_ERR_IO, "short write %s", path);
+        *what = path;
+        FILE* f = fopen(path, write ? "wb" : "rb");
+        if (!f) return LLMCU_ERR_IO;
+        const size_t got = write ? fwrite(part[i], sizeof(float), n[i], f) : fread(part[i], sizeof(float), n[i], f);
+        const bool closed = fclose(f) == 0;
+        if (got != n[i] || !closed) return LLMCU_ERR_IO;
       }
     }
   }
   return LLMCU_OK;
 }
 
+static bool layout_dims(const llmcu_lora_layout* lay, LoraDims* d) {
+  if (!lay || lay->n_layers <= 0 || lay->hidden <= 0 || lay->q_dim <= 0 || lay->kv_dim <= 0 || lay->ffn <= 0 ||
+      lay->rank < 1 || lay->rank > 16)
+    return false;
+  const uint32_t t = lay->targets ? static_cast<uint32_t>(lay->targets) : kTargetsAttn;
+  if (t & ~(kTargetsAttn | kTargetsMlp)) return false;
+  *d = LoraDims::make(lay->rank, lay->hidden, lay->q_dim, lay->kv_dim, lay->ffn, 1.0f, t);
+  return true;
+}
+
+int64_t llmcu_lora_layout_count(const llmcu_lora_layout* lay) {
+  LoraDims d;
+  return layout_dims(lay, &d) ? d.per_layer * lay->n_layers : 0;
+}
+
+llmcu_status llmcu_lora_files_write(const llmcu_lora_layout* lay, const float* flat, const char* dir, int step) {
+  LoraDims d;
+  if (!flat || !dir || !layout_dims(lay, &d)) return LLMCU_ERR_INVALID_ARG;
+  std::string what;
+  return lora_files_io(d, lay->n_layers, const_cast<float*>(flat), dir, step, true, &what);
+}
+
+llmcu_status llmcu_lora_files_read(const llmcu_lora_layout* lay, float* flat, const char* dir, int step) {
+  LoraDims d;
+  if (!flat || !dir || !layout_dims(lay, &d)) return LLMCU_ERR_INVALID_ARG;
+  std::string what;
+  return lora_files_io(d, lay->n_layers, flat, dir, step, false, &what);
+}
+
+llmcu_status llmcu_save_lora(llmcu_ctx* ctx, const char* dir, int step) {
+  if (!ctx || !dir) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null argument");
+  CK(cudaSetDevice(ctx->device));
+  std::vector<float> flat(static_cast<size_t>(ctx->n_lora));
+  CK(cudaStreamSynchronize(ctx->comm));
+  CK(cudaMemcpyAsync(flat.data(), ctx->lp, flat.size() * sizeof(float), cudaMemcpyDeviceToHost, ctx->st));
+  CK(cudaStreamSynchronize(ctx->st));
+  std::string what;
+  if (lora_files_io(ctx->ld, ctx->L, flat.data(), dir, step, true, &what) != LLMCU_OK)
+    return fail(ctx, LLMCU_ERR_IO, "cannot write %s", what.c_str());
+  return LLMCU_OK;
+}
+
 llmcu_status llmcu_load_lora(llmcu_ctx* ctx, const char* dir, int step) {
   if (!ctx || !dir) return fail(ctx, LLMCU_ERR_INVALID_ARG, "null argument");
-  const LoraDims& d = ctx->ld;
-  std::vector<float> A, B;
-  for (int l = 0; l < ctx->L; ++l) {
-    for (int p = 0; p < kNumProj; ++p) {
-      if (!d.has(p)) continue;
-      A.resize(static_cast<size_t>(d.r) * d.d_in(p));
-      B.resize(static_cast<size_t>(d.d_out(p)) * d.r);
-      std::vector<float>* parts[2] = {&A, &B};
-      const char* ab[2] = {"A", "B"};
-      for (int i = 0; i < 2; ++i) {
-        char path[1024];
-        snprintf(path, sizeof(path), "%s/lora_step%d_layer%d_%s_%s.bin", dir, step, l, kProjNames[p], ab[i]);
-        FILE* f = fopen(path, "rb");
-        if (!f) return fail(ctx, LLMCU_ERR_IO, "cannot open %s", path);
-        const size_t n = fread(parts[i]->data(), sizeof(float), parts[i]->size(), f);
-        fclose(f);
-        if (n != parts[i]->size()) return fail(ctx, LLMCU_ERR_IO, "short read %s", path);
-      }
-      CKS(llmcu_set_lora(ctx, l, p, A.data(), B.data()));
-    }
-  }
+  CK(cudaSetDevice(ctx->device));
+  std::vector<float> flat(static_cast<size_t>(ctx->n_lora));
+  std::string what;
+  if (lora_files_io(ctx->ld, ctx->L, flat.data(), dir, step, false, &what) != LLMCU_OK)
+    return fail(ctx, LLMCU_ERR_IO, "cannot read %s (missing or short)", what.c_str());
+  CK(cudaMemcpyAsync(ctx->lp, flat.data(), flat.size() * sizeof(float), cudaMemcpyHostToDevice, ctx->st));
+  CK(cudaStreamSynchronize(ctx->st));
   return LLMCU_OK;
 }
 
@@ -1802,36 +1832,68 @@ llmcu_status llmcu_profile_read(llmcu_ctx* ctx, char* buf, size_t len, int reset
 
 // ------------------------------------------------------------ kernel test
 
+}  // extern "C"
+
+namespace llmcu {
+// The kernel-level entry points' device error word (one per device: every
+// device that loads the library holds its own copy).
+static __device__ int g_kernel_err;
+
+cudaError_t kernel_err_word(int** out) {
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_kernel_err);
+  *out = static_cast<int*>(p);
+  return e;
+}
+}  // namespace llmcu
+
+namespace {
+// cudaErrorInvalidValue comes from the launchers refusing a pointer, stride
+// or shape (TMA descriptors need 16-byte aligned bases and strides).
+llmcu_status kernel_status(cudaError_t e) {
+  return e == cudaSuccess ? LLMCU_OK : (e == cudaErrorInvalidValue ? LLMCU_ERR_UNSUPPORTED : LLMCU_ERR_CUDA);
+}
+}  // namespace
+
+extern "C" {
+
+llmcu_status llmcu_kernel_checks(void* stream, int* bits) {
+  int* w = nullptr;
+  if (kernel_err_word(&w) != cudaSuccess) return LLMCU_ERR_CUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int h = 0;
+  if (cudaMemcpyAsync(&h, w, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess) return LLMCU_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return LLMCU_ERR_CUDA;
+  if (h && cudaMemsetAsync(w, 0, sizeof(int), st) != cudaSuccess) return LLMCU_ERR_CUDA;
+  if (h && cudaStreamSynchronize(st) != cudaSuccess) return LLMCU_ERR_CUDA;
+  if (bits) *bits = h;
+  return h ? LLMCU_ERR_DEVICE_CHECK : LLMCU_OK;
+}
+
 llmcu_status llmcu_gemm_nt_f16(const void* A, const void* B, float* C, int M, int N, int K, int lda, int ldb, int ldc,
                                void* stream) {
   if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0) return LLMCU_ERR_INVALID_ARG;
-  static int* d_err = nullptr;
-  if (!d_err) {
-    if (cudaMalloc(&d_err, sizeof(int)) != cudaSuccess) return LLMCU_ERR_CUDA;
-    cudaMemset(d_err, 0, sizeof(int));
-  }
+  int* d_err = nullptr;
+  if (kernel_err_word(&d_err) != cudaSuccess) return LLMCU_ERR_CUDA;
   EpiArgs ea;
   ea.out = C;
   ea.ld_out = ldc;
   cudaError_t e = gemm(op(static_cast<const __half*>(A), M, K, lda), op(static_cast<const __half*>(B), N, K, ldb), M,
                        N, Epi::kStoreF32, ea, d_err, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? LLMCU_OK : LLMCU_ERR_CUDA;
+  return kernel_status(e);
 }
 
 llmcu_status llmcu_gemm_nn_f16(const void* A, const void* B, float* C, int M, int N, int K, int lda, int ldb, int ldc,
                                void* stream) {
   if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0) return LLMCU_ERR_INVALID_ARG;
-  static int* d_err = nullptr;
-  if (!d_err) {
-    if (cudaMalloc(&d_err, sizeof(int)) != cudaSuccess) return LLMCU_ERR_CUDA;
-    cudaMemset(d_err, 0, sizeof(int));
-  }
+  int* d_err = nullptr;
+  if (kernel_err_word(&d_err) != cudaSuccess) return LLMCU_ERR_CUDA;
   EpiArgs ea;
   ea.out = C;
   ea.ld_out = ldc;
   cudaError_t e = gemm(op(static_cast<const __half*>(A), M, K, lda), op_mn(static_cast<const __half*>(B), K, N, ldb),
                        M, N, Epi::kStoreF32, ea, d_err, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? LLMCU_OK : (e == cudaErrorInvalidValue ? LLMCU_ERR_UNSUPPORTED : LLMCU_ERR_CUDA);
+  return kernel_status(e);
 }
 
 llmcu_status llmcu_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int batch, int seq,
@@ -1839,11 +1901,13 @@ llmcu_status llmcu_attention_fwd(const void* q, const void* k, const void* v, vo
   if (!q || !k || !v || !o || !lse || batch <= 0 || seq <= 0 || n_heads <= 0 || n_kv_heads <= 0 ||
       n_heads % n_kv_heads)
     return LLMCU_ERR_INVALID_ARG;
+  int* d_err = nullptr;
+  if (kernel_err_word(&d_err) != cudaSuccess) return LLMCU_ERR_CUDA;
   cudaError_t e = attention_forward(static_cast<const __half*>(q), static_cast<const __half*>(k),
                                     static_cast<const __half*>(v), static_cast<__half*>(o), lse, batch, seq, n_heads,
-                                    n_kv_heads, head_dim, ldq, ldk, ldv, n_heads * head_dim, nullptr,
+                                    n_kv_heads, head_dim, ldq, ldk, ldv, n_heads * head_dim, d_err,
                                     static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? LLMCU_OK : (e == cudaErrorInvalidValue ? LLMCU_ERR_UNSUPPORTED : LLMCU_ERR_CUDA);
+  return kernel_status(e);
 }
 
 llmcu_status llmcu_attention_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
@@ -1853,13 +1917,15 @@ llmcu_status llmcu_attention_bwd(const void* q, const void* k, const void* v, co
   if (!q || !k || !v || !o || !dout || !lse || !scratch_delta || !dq || !dk || !dv || batch <= 0 || seq <= 0 ||
       n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads)
     return LLMCU_ERR_INVALID_ARG;
+  int* d_err = nullptr;
+  if (kernel_err_word(&d_err) != cudaSuccess) return LLMCU_ERR_CUDA;
   const int ldo = n_heads * head_dim;
   cudaError_t e = attention_backward(
       static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v),
       static_cast<const __half*>(o), static_cast<const __half*>(dout), lse, scratch_delta, dq, dk,
       static_cast<__half*>(dv), batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk, ldv, ldo, ldo,
-      n_kv_heads * head_dim, lddv, nullptr, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? LLMCU_OK : (e == cudaErrorInvalidValue ? LLMCU_ERR_UNSUPPORTED : LLMCU_ERR_CUDA);
+      n_kv_heads * head_dim, lddv, d_err, static_cast<cudaStream_t>(stream));
+  return kernel_status(e);
 }
 
 }  // extern "C"

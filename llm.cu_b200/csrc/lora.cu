@@ -667,11 +667,12 @@ int lora_grad_splits(int M, const LoraGradBatch& batch) {
 cudaError_t lora_grad(const LoraGradBatch& batch, int M, cudaStream_t st) {
   if (batch.n <= 0 || batch.n > kLoraMaxProbs) return cudaErrorInvalidValue;
   const int splits = lora_grad_splits(M, batch);
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(lora_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kLgSmem);
+  static std::atomic<unsigned long long> attr_set{0};
+  {
+    cudaError_t e = once_per_device(attr_set, [] {
+      return cudaFuncSetAttribute(lora_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kLgSmem);
+    });
     if (e != cudaSuccess) return e;
-    attr_done = true;
   }
   LoraGradMaps maps;
   for (int i = 0; i < batch.n; ++i) {

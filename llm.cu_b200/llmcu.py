@@ -65,6 +65,11 @@ class _RunCfg(C.Structure):
                 ("loss_all_positions", C.c_int32), ("int8_in_gemm", C.c_int32)]
 
 
+class _LoraLayout(C.Structure):
+    _fields_ = [("n_layers", C.c_int32), ("hidden", C.c_int32), ("q_dim", C.c_int32), ("kv_dim", C.c_int32),
+                ("ffn", C.c_int32), ("rank", C.c_int32), ("targets", C.c_int32)]
+
+
 class _AdamWCfg(C.Structure):
     _fields_ = [("lr", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float), ("eps", C.c_float),
                 ("weight_decay", C.c_float)]
@@ -167,6 +172,10 @@ _SIGS = {
     "llmcu_attention_fwd": (C.c_int, [C.c_void_p] * 5 + [C.c_int] * 8 + [C.c_void_p]),
     "llmcu_attention_bwd": (C.c_int, [C.c_void_p] * 10 + [C.c_int] * 9 + [C.c_void_p]),
     "llmcu_attention_bwd_noalloc": (C.c_int, [C.c_void_p] * 9 + [C.c_int] * 9 + [C.c_void_p]),
+    "llmcu_kernel_checks": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "llmcu_lora_layout_count": (C.c_int64, [C.POINTER(_LoraLayout)]),
+    "llmcu_lora_files_write": (C.c_int, [C.POINTER(_LoraLayout), C.c_void_p, C.c_char_p, C.c_int]),
+    "llmcu_lora_files_read": (C.c_int, [C.POINTER(_LoraLayout), C.c_void_p, C.c_char_p, C.c_int]),
 }
 
 
@@ -457,6 +466,68 @@ def attention_bwd_noalloc(q, k, v, o, do, lse, dq, dk, dv, batch, seq, nh, nkv, 
     check LLMCU_ERR_UNSUPPORTED for sizes above the library's fixed scratch)."""
     return lib().llmcu_attention_bwd_noalloc(q, k, v, o, do, lse, dq, dk, dv, batch, seq, nh, nkv, hd, ldq,
                                              ldk, ldv, lddv, stream)
+
+
+class LoraFiles:
+    """The adapter files of one layout on the host alone (llmcu_lora_files_*):
+    no device or context.  Adapters are given and returned as the golden's
+    dict {"L{l}.{proj}.{A,B}": array} and laid out flat as the library keeps
+    them (per layer, per target projection: A [r, d_in] then B [d_out, r])."""
+
+    def __init__(self, model: Model, lora: Lora):
+        self.model, self.lora = model, lora
+        self._lay = _LoraLayout(model.n_layers, model.hidden, model.n_heads * model.head_dim,
+                                model.n_kv_heads * model.head_dim, model.ffn, lora.rank, lora.targets)
+        self.count = int(lib().llmcu_lora_layout_count(C.byref(self._lay)))
+        if self.count <= 0:
+            raise LlmcuError(1, "invalid adapter layout")
+
+    def _dims(self, proj: int):
+        m = self.model
+        Q, KV = m.n_heads * m.head_dim, m.n_kv_heads * m.head_dim
+        return {P_Q: (Q, m.hidden), P_K: (KV, m.hidden), P_V: (KV, m.hidden), P_O: (m.hidden, Q),
+                P_GATE: (m.ffn, m.hidden), P_UP: (m.ffn, m.hidden), P_DOWN: (m.hidden, m.ffn)}[proj]
+
+    def _slots(self):
+        off = 0
+        for l in range(self.model.n_layers):
+            for p in self.lora.projs():
+                d_out, d_in = self._dims(p)
+                for mat, shape in (("A", (self.lora.rank, d_in)), ("B", (d_out, self.lora.rank))):
+                    n = shape[0] * shape[1]
+                    yield f"L{l}.{PROJ_NAMES[p]}.{mat}", off, shape
+                    off += n
+
+    def flatten(self, adapters: dict) -> np.ndarray:
+        flat = np.empty(self.count, np.float32)
+        for key, off, shape in self._slots():
+            flat[off:off + shape[0] * shape[1]] = np.asarray(adapters[key], np.float32).reshape(-1)
+        return flat
+
+    def unflatten(self, flat: np.ndarray) -> dict:
+        return {key: flat[off:off + shape[0] * shape[1]].reshape(shape).copy() for key, off, shape in self._slots()}
+
+    def write(self, adapters: dict, directory: str, step: int):
+        flat = self.flatten(adapters)
+        _chk(lib().llmcu_lora_files_write(C.byref(self._lay), _ptr(flat), directory.encode(), step),
+             f"lora_files_write {directory}")
+
+    def read(self, directory: str, step: int) -> dict:
+        flat = np.empty(self.count, np.float32)
+        _chk(lib().llmcu_lora_files_read(C.byref(self._lay), _ptr(flat), directory.encode(), step),
+             f"lora_files_read {directory}")
+        return self.unflatten(flat)
+
+
+def kernel_checks(stream=0) -> int:
+    """Synchronises `stream`, then reads and clears the current device's error
+    word of the kernel-level entry points; raises LlmcuError (DEVICE_CHECK)
+    if any of their kernels gave up a bounded wait, else returns 0."""
+    bits = C.c_int(0)
+    st = lib().llmcu_kernel_checks(stream, C.byref(bits))
+    if st != OK:
+        raise LlmcuError(st, f"kernel-level device checks failed (error bits 0x{bits.value:x})")
+    return bits.value
 
 
 def quantize_int8_rows(w_ptr, rows, cols, q_ptr, scale_ptr, stream=0):

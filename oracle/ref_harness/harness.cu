@@ -21,9 +21,11 @@
 //   harness parity IN OUT     IN: dims, batch, seq, tokens, targets, weights,
 //                             adapters, adamw config (see tests/golden/ref_io.py)
 //                             OUT: losses[B], grads, post-AdamW adapters
-//   harness bench B S STEPS WARMUP
-//                             synthetic device-filled weights; prints one JSON
-//                             line with the per-step time (cudaEvent)
+//   harness bench B S STEPS WARMUP [TOKENS]
+//                             synthetic device-filled weights; B sequences per
+//                             step (token windows from the TOKENS file when
+//                             given); prints one JSON line with the per-step
+//                             time (cudaEvent)
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -254,7 +256,7 @@ void fill(float* p, size_t n, unsigned seed, float scale) {
   CUDA_CHECK_LAST();
 }
 
-int bench(int B, int S, int steps, int warmup) {
+int bench(int B, int S, int steps, int warmup, const char* tok_file) {
   MW m;
   alloc_model(m);
   const size_t H = HIDDEN_SIZE, I = INTERMEDIATE_SIZE, V = VOCAB_SIZE;
@@ -287,9 +289,26 @@ int bench(int B, int S, int steps, int warmup) {
   int *d_tok, *d_tgt;
   CUDA_CHECK(cudaMalloc(&d_tok, (size_t)B * S * sizeof(int)));
   CUDA_CHECK(cudaMalloc(&d_tgt, (size_t)B * S * sizeof(int)));
+  // B windows of S + 1 ids (inputs = ids[0..S-1], targets = ids[1..S]): from
+  // tok_file (int32, written by bench.py with the same draw as its own arm),
+  // else an LCG over the vocabulary
   std::vector<int> tok((size_t)B * (S + 1));
-  unsigned r = 12345;
-  for (auto& t : tok) { r = r * 1664525u + 1013904223u; t = (int)(r % VOCAB_SIZE); }
+  if (tok_file) {
+    FILE* f = fopen(tok_file, "rb");
+    if (!f || fread(tok.data(), sizeof(int), tok.size(), f) != tok.size()) {
+      fprintf(stderr, "cannot read %zu token ids from %s\n", tok.size(), tok_file);
+      return 1;
+    }
+    fclose(f);
+    for (int t : tok)
+      if (t < 0 || t >= VOCAB_SIZE) {
+        fprintf(stderr, "token id %d outside [0, %d)\n", t, VOCAB_SIZE);
+        return 1;
+      }
+  } else {
+    unsigned r = 12345;
+    for (auto& t : tok) { r = r * 1664525u + 1013904223u; t = (int)(r % VOCAB_SIZE); }
+  }
   for (int b = 0; b < B; ++b) {
     CUDA_CHECK(cudaMemcpy(d_tok + b * S, tok.data() + b * (S + 1), S * 4, cudaMemcpyHostToDevice));
     CUDA_CHECK(cudaMemcpy(d_tgt + b * S, tok.data() + b * (S + 1) + 1, S * 4, cudaMemcpyHostToDevice));
@@ -319,7 +338,8 @@ int bench(int B, int S, int steps, int warmup) {
 
 int main(int argc, char** argv) {
   if (argc >= 4 && !strcmp(argv[1], "parity")) return parity(argv[2], argv[3]);
-  if (argc >= 6 && !strcmp(argv[1], "bench")) return bench(atoi(argv[2]), atoi(argv[3]), atoi(argv[4]), atoi(argv[5]));
-  fprintf(stderr, "usage: harness parity IN OUT | harness bench B S STEPS WARMUP\n");
+  if (argc >= 6 && !strcmp(argv[1], "bench"))
+    return bench(atoi(argv[2]), atoi(argv[3]), atoi(argv[4]), atoi(argv[5]), argc >= 7 ? argv[6] : nullptr);
+  fprintf(stderr, "usage: harness parity IN OUT | harness bench B S STEPS WARMUP [TOKENS]\n");
   return 2;
 }
