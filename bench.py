@@ -469,6 +469,9 @@ def main():
                 "ms_per_step": round(gemm_ms_step, 3)}
     kernels = {k: {"ms_per_step": round(v["ms"] / n_prof, 3), "launches_per_step": v["launches"] / n_prof}
                for k, v in prof.items() if v["launches"]}
+    # compute-stream wait for the allreduces the backward did not hide (events
+    # on the compute stream; the adapter gradients run on it in this pass)
+    dp_exposed_ms = round(prof.get("dp_exposed", {}).get("ms", 0.0) / n_prof, 3)
     gpu_launches = int(sum(v["launches"] for v in prof.values()) / n_prof * args.steps)
 
     cpu = None
@@ -496,7 +499,7 @@ def main():
                               "achieved_tflops": round(step_alg / (ms / 1e3) / 1e12 / world, 2),
                               "frac_of_peak_per_gpu": round(step_alg / (ms / 1e3) / 1e12 / world
                                                             / pk["bf16_tflops_sustained"], 4)},
-            "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": gpu_launches,
+            "roofline": roofline, "e2e": e2e, "dp_exposed_ms_per_step": dp_exposed_ms if world > 1 else None, "cpu_baseline": cpu, "gpu_launches": gpu_launches,
             "kernels": kernels, "clocks": clk, "loss": round(loss, 5), "warm_loss": round(warm_loss, 5),
         }
         print(json.dumps(line))

@@ -292,8 +292,11 @@ llmcu_status llmcu_dp_set_timeout_ms(llmcu_ctx* ctx, int ms);
 
 /* Per-kernel-class timing.  While enabled, every step records CUDA events on
  * the compute stream around each kernel launch (classes: gemm_tc,
- * attention_fwd, attention_bwd, norm_rope, lora_grad, lora_prep, ce_reduce,
- * embed, adamw, int8_dequant).  The reference has no counterpart (its
+ * attention_fwd, attention_bwd, norm_rope, lora_grad, lora_merge, ce_reduce,
+ * embed, adamw, int8_dequant, fill_and_loss) and, data parallel, around the
+ * compute stream's wait for the allreduces the backward did not hide
+ * (dp_exposed, no kernel); the adapter gradients then run on the compute
+ * stream.  The reference has no counterpart (its
  * per-component timers exist only in the inference bench,
  * src/kernels/forward.cu:207-335). */
 llmcu_status llmcu_profile_enable(llmcu_ctx* ctx, int on);

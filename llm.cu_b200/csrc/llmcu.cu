@@ -170,10 +170,12 @@ llmcu_status fail(llmcu_ctx* c, llmcu_status s, const char* fmt, ...) {
 
 enum ProfClass : int {
   P_GEMM = 0, P_ATTN_FWD, P_ATTN_BWD, P_NORM, P_LORA_GRAD, P_LORA_PREP, P_CE, P_EMBED, P_ADAMW, P_DEQUANT, P_FILL,
+  P_DP_WAIT,  // no kernel: the compute stream waiting for the last allreduces after the backward
   P_COUNT
 };
 const char* kProfNames[P_COUNT] = {"gemm_tc", "attention_fwd", "attention_bwd", "norm_rope", "lora_grad",
-                                   "lora_merge", "ce_reduce", "embed", "adamw", "int8_dequant", "fill_and_loss"};
+                                   "lora_merge", "ce_reduce", "embed", "adamw", "int8_dequant", "fill_and_loss",
+                                   "dp_exposed"};
 
 // Records one event of a (begin, end) pair around `kernels` launches of class `cls`.
 void prof_mark(llmcu_ctx* c, int cls, int kernels = 1) {
@@ -889,6 +891,10 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
                     "allreduce of layer gradients"));
     }
   }
+  // dp_exposed: compute-stream time from the end of the backward's last
+  // kernel until every gradient bucket and the loss are allreduced (the
+  // communication the backward did not hide)
+  prof_mark(ctx, P_DP_WAIT, 0);
   if (split) CK(cudaStreamWaitEvent(st, ev_side(0, 3), 0));  // every gradient is in place before AdamW
   // loss: sum over valid rows (over all ranks) / number of valid rows; the
   // final kernel may follow an event wait, so it is launched normally
@@ -901,6 +907,7 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     CK(cudaEventRecord(ctx->ev_comm_done, ctx->comm));
     CK(cudaStreamWaitEvent(st, ctx->ev_comm_done, 0));
   }
+  prof_mark(ctx, P_DP_WAIT, 0);
   prof_mark(ctx, P_FILL);
   scale_loss_kernel<<<1, 1, 0, st>>>(total, static_cast<float>(1.0 / n_valid_total), ctx->loss_dev);
   CK(cudaGetLastError());

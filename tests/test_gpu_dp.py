@@ -24,7 +24,9 @@ def _n_gpus():
 
 
 @pytest.mark.parametrize("world,projs", [(2, ("wq", "wk", "wv", "wo")),
-                                         (2, ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"))])
+                                         (2, ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down")),
+                                         (4, ("wq", "wk", "wv", "wo")),
+                                         (8, ("wq", "wk", "wv", "wo"))])
 def test_dp_ranks_match_golden(llmcu, cuda_device, tmp_path, world, projs):
     if _n_gpus() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -57,8 +59,9 @@ def test_dp_ranks_match_golden(llmcu, cuda_device, tmp_path, world, projs):
             assert G.rel_l2(g, ref.grads[k]) <= 1e-2 and G.cosine(g, ref.grads[k]) >= 0.999, k
             p = o["p_" + k]
             assert G.rel_l2(p, upd[k]) <= 1e-2 and G.cosine(p, upd[k]) >= 0.999, k
-    for k in outs[0]:
-        assert np.array_equal(outs[0][k], outs[1][k]), k
+    for o in outs[1:]:
+        for k in outs[0]:
+            assert np.array_equal(outs[0][k], o[k]), k
 
 
 def test_dp_missing_rank_fails_by_deadline(llmcu, cuda_device):
