@@ -121,11 +121,20 @@ class ClockSampler:
                 "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
+def layer_gemm_flops_per_token(m) -> float:
+    """Forward + dX of the frozen linears of every layer (the gemm_tc class)."""
+    H, Q, KV, I, L = m.hidden, m.n_heads * m.head_dim, m.n_kv_heads * m.head_dim, m.ffn, m.n_layers
+    return float(4 * L * (Q * H + 2 * KV * H + H * Q + 3 * I * H))
+
+
+def lm_head_flops_per_token(m) -> float:
+    """Forward + dX of the tied lm_head (the lm_head class: logits and d_xf)."""
+    return float(4 * m.vocab * m.hidden)
+
+
 def algorithmic_gemm_flops_per_token(m) -> float:
     """Forward + dX of every frozen linear (tied lm_head once)."""
-    H, Q, KV, I, V, L = m.hidden, m.n_heads * m.head_dim, m.n_kv_heads * m.head_dim, m.ffn, m.vocab, m.n_layers
-    n_lin = L * (Q * H + 2 * KV * H + H * Q + 3 * I * H) + V * H
-    return float(4 * n_lin)
+    return layer_gemm_flops_per_token(m) + lm_head_flops_per_token(m)
 
 
 def algorithmic_flops_per_token(m, seq, n_lora) -> float:
@@ -450,10 +459,19 @@ def main():
     g = prof["gemm_tc"]
     gemm_ms_step = g["ms"] / n_prof
     gemm_launches_step = g["launches"] / n_prof
-    alg_flops_step = algorithmic_gemm_flops_per_token(model) * B * S
+    alg_flops_step = layer_gemm_flops_per_token(model) * B * S
     per_launch_flops = alg_flops_step / gemm_launches_step
     per_launch_s = gemm_ms_step / gemm_launches_step / 1e3
     achieved = per_launch_flops / per_launch_s / 1e12
+    # the lm_head section: vocabulary-streamed logits + cross-entropy + d_xf
+    lh = prof.get("lm_head", {"ms": 0.0, "launches": 0})
+    lh_ms = lh["ms"] / n_prof
+    lh_flops = lm_head_flops_per_token(model) * B * S
+    lm_head = {"ms_per_step": round(lh_ms, 3), "launches_per_step": lh["launches"] / n_prof,
+               "alg_tflop_per_step": round(lh_flops / 1e12, 3),
+               "achieved_tflops": round(lh_flops / (lh_ms / 1e3) / 1e12, 2) if lh_ms > 0 else None,
+               "frac_of_sustained": round(lh_flops / (lh_ms / 1e3) / 1e12 / pk["bf16_tflops_sustained"], 4)
+               if lh_ms > 0 else None}
     traffic = None
     prof_path = os.path.join(ROOT, "profiles", "gemm_traffic_c2.txt")
     if os.path.exists(prof_path):
@@ -461,7 +479,7 @@ def main():
             tr = json.load(f).get(args.workload)
         if tr:
             traffic = tr.get("dram_bytes_per_launch")
-    roofline = {"kernel": "gemm_tc_kernel (tcgen05/TMEM, all linear layers)", "bound": "tensor",
+    roofline = {"kernel": "gemm_tc_kernel (tcgen05/TMEM, the 28 layers' linear layers)", "bound": "tensor",
                 "achieved": round(achieved, 2), "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                 "frac": round(achieved / pk["bf16_tflops_sustained"], 4), "traffic": traffic,
                 "peak_src": f"{pk['src']} sustained bf16 (kernel timed inside a long step)",
@@ -499,7 +517,7 @@ def main():
                               "achieved_tflops": round(step_alg / (ms / 1e3) / 1e12 / world, 2),
                               "frac_of_peak_per_gpu": round(step_alg / (ms / 1e3) / 1e12 / world
                                                             / pk["bf16_tflops_sustained"], 4)},
-            "roofline": roofline, "e2e": e2e, "dp_exposed_ms_per_step": dp_exposed_ms if world > 1 else None, "cpu_baseline": cpu, "gpu_launches": gpu_launches,
+            "roofline": roofline, "lm_head": lm_head, "e2e": e2e, "dp_exposed_ms_per_step": dp_exposed_ms if world > 1 else None, "cpu_baseline": cpu, "gpu_launches": gpu_launches,
             "kernels": kernels, "clocks": clk, "loss": round(loss, 5), "warm_loss": round(warm_loss, 5),
         }
         print(json.dumps(line))

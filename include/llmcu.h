@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define LLMCU_ABI_VERSION 1
+#define LLMCU_ABI_VERSION 2
 
 typedef enum {
     LLMCU_OK = 0,
@@ -86,6 +86,10 @@ typedef struct {
                                    (converter warps expand them in shared
                                    memory; row scales in the epilogue / folded
                                    into the input-gradient GEMM's A operand)    */
+    int32_t lm_head_chunk;      /* vocabulary columns per lm_head chunk (the
+                                   lm_head streams over the vocabulary; a
+                                   multiple of 256); 0 = as many as fit 64 MiB
+                                   of fp16 values at max_batch * max_seq rows */
 } llmcu_run_cfg;
 
 typedef struct {
@@ -292,8 +296,10 @@ llmcu_status llmcu_dp_set_timeout_ms(llmcu_ctx* ctx, int ms);
 
 /* Per-kernel-class timing.  While enabled, every step records CUDA events on
  * the compute stream around each kernel launch (classes: gemm_tc,
- * attention_fwd, attention_bwd, norm_rope, lora_grad, lora_merge, ce_reduce,
- * embed, adamw, int8_dequant, fill_and_loss) and, data parallel, around the
+ * attention_fwd, attention_bwd, norm_rope, lora_grad, lora_merge, lm_head
+ * (the vocabulary-streamed logits, cross-entropy and d_xf: its GEMMs are not
+ * in gemm_tc), embed, adamw, int8_dequant, fill_and_loss) and, data parallel,
+ * around the
  * compute stream's wait for the allreduces the backward did not hide
  * (dp_exposed, no kernel); the adapter gradients then run on the compute
  * stream.  The reference has no counterpart (its

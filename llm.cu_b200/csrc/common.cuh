@@ -80,7 +80,7 @@ cudaError_t attention_backward_tc(const __half* q, const __half* k, const __half
 
 // ---- gemm.cu
 // Column slices per GEMM tile (epilogue warps per TMEM lane quadrant); the
-// lm_head statistics epilogue writes one (max, sum-exp) partial per slice.
+// lm_head epilogue writes one (reference, sum) partial per 128-column slice.
 constexpr int kGemmEpiGroups = 2;
 // Tensor operand for the GEMM: fp16, K-major rows (K contiguous), `ld`
 // elements between rows; `rows` x `k` valid extent.
@@ -109,9 +109,9 @@ enum class Epi : int {
   kResidF32 = 2,
   kSwiGLU = 3,
   kSwiGLUBwd = 4,
-  kCEProbs = 5,  // lm_head forward: slot max / sum-exp partials + slot-relative probabilities
   kStoreF16Delta = 6,  // fp16 dO + the attention backward's per-(row, head) dO.O sums
   kQKNormRope = 7,     // fp16 q/k/v + (head_dim 128) per-head RMSNorm and RoPE of q and k into rope_out
+  kCEStream = 8,       // lm_head forward over one vocabulary chunk: exp(l - ref) into the chunk buffer + partials
 };
 
 struct EpiArgs {
@@ -150,9 +150,14 @@ struct EpiArgs {
   float eps = 0.f;
   // cross-entropy
   const int* targets = nullptr;
-  float* part_max = nullptr;
+  float* part_max = nullptr;   // kCEStream: the reference of each (row, 128-column slot)
   float* part_sum = nullptr;
   float* tgt_logit = nullptr;
+  // kCEStream: per-row reference ce_ref [M], vocabulary index of the chunk's
+  // first column (a multiple of 128) and slots per row in part_max / part_sum
+  const float* ce_ref = nullptr;
+  int vocab_off = 0;
+  int ce_slots = 0;
 };
 
 // C[M,N] = A . B^T (B K-major) or A . B (B MN-major) with the given
@@ -207,16 +212,25 @@ cudaError_t qknorm_rope_backward(const float* dq, const float* dk, const __half*
                                  const float* kn_w, const float* cos_t, const float* sin_t, __half* dqkv, int B,
                                  int S, int nh, int nkv, int hd, float eps, cudaStream_t st);
 cudaError_t rope_tables(float* cos_t, float* sin_t, int S, int hd, float theta, cudaStream_t st);
-// row_loss_and_sum: [M] per-row losses followed by their sum at [M]
-// In place: slot-relative probabilities p = exp(l - m_slot) (fp16, from the
-// kCEProbs GEMM) -> dlogits = gscale * (p * exp(m_slot - lse) - onehot) for
-// rows that count in the loss, 0 for the others (src/kernels/loss.cu:62-69).
-cudaError_t ce_dlogits(__half* p, int ldp, int M, int V, const float* part_max, int slots, const float* lse,
-                       const uint8_t* valid, const int* targets, float gscale, cudaStream_t st);
-cudaError_t ce_reduce(const float* part_max, const float* part_sum, const float* tgt_logit, const uint8_t* valid,
-                      float* lse, float* row_loss_and_sum, int M, int tiles_n, cudaStream_t st);
 cudaError_t ce_valid_rows(uint8_t* valid, const int* targets, int B, int S, int all_positions, int V, int* err,
                           cudaStream_t st);
+// Streamed cross-entropy over vocabulary chunks (the lm_head never holds an
+// [M, V] tensor).  After the kCEStream GEMM of the chunk [v0, v0 + n): rows
+// whose chunk brought a slot above ref + kCeSlotRange move their reference to
+// (that max - kCeRefBelowMax), rescaling the row's fp16 chunk values and its
+// fp32 d_xf accumulator (first = the first chunk: reference -inf, d_xf rows
+// set to 0).  Rows of other chunks are left alone.
+constexpr float kCeSlotRange = 11.0f;    // exp(11) < 65504: an unflagged slot's values stay fp16
+constexpr float kCeRefBelowMax = 10.0f;  // a new reference sits this far below the row's max
+cudaError_t ce_stream_rescale(__half* pc, int ldp, const float* part_ref, int slots, float* ref, float* d_xf, int M,
+                              int H, int v0, int n, int first, cudaStream_t st);
+// After the last chunk: lse and row losses (+ their sum at row_loss[M]) from
+// the slot partials; d_xf -> gscale * (exp(ref - lse) d_xf + (p_t - 1) E_t)
+// for rows in the loss, 0 for the others (src/kernels/loss.cu:62-69).
+cudaError_t ce_stream_finish(const float* part_ref, const float* part_sum, const float* tgt_logit, const float* ref,
+                             const uint8_t* valid, const int* targets, const __half* E, int M, int H, int V,
+                             int slots, float gscale, float* lse, float* row_loss_and_sum, float* d_xf,
+                             cudaStream_t st);
 cudaError_t adamw_flat(float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1, float b2,
                        float eps, float wd, float bc1, float bc2, float gscale, cudaStream_t st);
 cudaError_t fill_f32_2d(float* p, int ld, int rows, int cols, float v, cudaStream_t st);

@@ -167,16 +167,17 @@ cudaError_t dispatch(Epi epi, const EpiArgs& ea, const CUtensorMap* maps, const 
       } else {
         return cudaErrorInvalidValue;
       }
-    case Epi::kCEProbs:
-      if constexpr (BN == 256 && !BMN) {
-        EpiCEProbs::Params p{ea.targets, ea.part_max, ea.part_sum, ea.tgt_logit, sh.tiles_n * (epi_warps<BN>() / 4)};
-        return launch<BN, EpiCEProbs, BMN, CG>(maps, sh, p, err, st);
-      } else {
-        return cudaErrorInvalidValue;
-      }
     case Epi::kSwiGLU:
       if constexpr (BN == 256 && !BMN) {
         return launch<BN, EpiSwiGLU, BMN, CG>(maps, sh, EpiSwiGLU::Params{}, err, st);
+      } else {
+        return cudaErrorInvalidValue;
+      }
+    case Epi::kCEStream:
+      if constexpr (BN == 256 && !BMN) {
+        EpiCEStream::Params p{ea.targets, ea.ce_ref, ea.part_max, ea.part_sum, ea.tgt_logit, ea.ce_slots,
+                              ea.vocab_off};
+        return launch<BN, EpiCEStream, BMN, CG>(maps, sh, p, err, st);
       } else {
         return cudaErrorInvalidValue;
       }
@@ -248,8 +249,11 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
         reinterpret_cast<uintptr_t>(ea.attn_o) % 16)
       return cudaErrorInvalidValue;
   }
-  if ((epi == Epi::kSwiGLU || epi == Epi::kSwiGLUBwd || epi == Epi::kCEProbs) && BN != 256)
+  if ((epi == Epi::kSwiGLU || epi == Epi::kSwiGLUBwd || epi == Epi::kCEStream) && BN != 256)
     return cudaErrorInvalidValue;  // paired columns / partial slots assume 256-wide tiles
+  if (epi == Epi::kCEStream && (!ea.targets || !ea.ce_ref || !ea.part_max || !ea.part_sum || !ea.tgt_logit ||
+                                ea.vocab_off % 128 || ea.ce_slots < (ea.vocab_off + N + 127) / 128))
+    return cudaErrorInvalidValue;
   if (ea.ksplit > 1 && (epi != Epi::kStoreF32 || !ea.accumulate)) return cudaErrorInvalidValue;
   const int n_main = ea.n_main > 0 ? ea.n_main : N;
   if (n_main < N) {  // side output: only for the plain stores, from a tile boundary
@@ -272,7 +276,7 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
   switch (epi) {
     case Epi::kStoreF16:
     case Epi::kStoreF16Delta:
-    case Epi::kCEProbs:
+    case Epi::kCEStream:
       okc = make_io_map(&maps[2], ea.out, M, n_main, ea.ld_out, false);
       maps[3] = maps[2];
       break;
@@ -323,7 +327,7 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
     const int kbps = (nk + ea.ksplit - 1) / ea.ksplit;
     sh.kb_per_split = kbps;
     sh.splits = (nk + kbps - 1) / kbps;
-  } else if (t_fx_ws && epi != Epi::kCEProbs) {
+  } else if (t_fx_ws && epi != Epi::kCEStream) {
     // tiles that fill under half a wave: K splits with a fix-up, about one
     // wave of units, at least two 64-deep K blocks each
     const int slots = CG == 2 ? g_num_sms / 2 : g_num_sms;

@@ -27,12 +27,13 @@
 // Tiles: BLOCK_M = 128 rows, BLOCK_N = BN (64/128/256), BLOCK_K = 64 (one
 // 128-byte swizzle row of fp16).  Tile t -> (t % tiles_m, t / tiles_m), so
 // CTAs that run together share the weight (B) tile and stream it once -- or,
-// when A is the larger operand (the lm_head dX reads [M, V] dlogits), the
-// transposed order, so concurrent CTAs share A's rows instead.
+// when A is the larger operand, the transposed order, so concurrent CTAs share
+// A's rows instead.
 #pragma once
 
 #include <type_traits>
 
+#include "common.cuh"
 #include "sm100.cuh"
 
 namespace llmcu {
@@ -674,20 +675,27 @@ struct EpiSwiGLUBwdT {
 using EpiSwiGLUBwd = EpiSwiGLUBwdT<false>;
 using EpiSwiGLUBwdScaled = EpiSwiGLUBwdT<true>;
 
-// lm_head forward (src/kernels/loss.cu:24-61): per row and 128-column slot
-// (vocab tile x column slice) the slot's max logit m and sum of exp(l - m),
-// the target logit when the target falls in the slot, and the slot-relative
-// probabilities exp(l - m) as fp16 into the [M, V] buffer of mapC (later
-// turned into dlogits in place by ce_dlogits, so the backward never
-// recomputes the logits).  Takes its slice straight from TMEM: one pass for
-// the max, one for exp / sum / store.
-struct EpiCEProbs {
+// lm_head forward over one vocabulary chunk, for the streamed cross-entropy
+// (src/kernels/loss.cu:24-61 without the [M, V] logits): per row and
+// 128-column slot, exp(l - r) goes as fp16 into the chunk buffer (mapC,
+// [M, chunk width]) that the chunk's input-gradient GEMM reads next, and
+// (r, sum of exp(l - r)) into the slot's partials.  r is the row's running
+// reference (ref, kept by ce_stream_rescale) unless the slot's max lies more
+// than kCeSlotRange above it -- its values could leave fp16's range; always so
+// in the first chunk, whose reference is -inf -- and then r is the slot's own
+// max and ce_stream_rescale moves the row to a new reference before the
+// chunk's values are read.  The target's column is stored as 0 (its
+// (p - 1) E_t term is added in fp32 by ce_stream_finish) and its logit kept.
+// Straight from TMEM: one pass for the max, one for exp / sum / store.
+struct EpiCEStream {
   struct Params {
     const int* targets;   // [M]
-    float* part_max;      // [M, slots]
+    const float* ref;     // [M] running reference of each row
+    float* part_ref;      // [M, slots]
     float* part_sum;      // [M, slots]
     float* tgt_logit;     // [M]
-    int slots;            // vocab tiles x column slices
+    int slots;            // 128-column slots of the whole vocabulary
+    int vocab_off;        // vocabulary index of the chunk's column 0 (a multiple of 128)
   };
   struct State {};
   static constexpr int kChunk = 128;
@@ -696,12 +704,13 @@ struct EpiCEProbs {
   static constexpr bool kStores = true;
   static constexpr bool kTmemDirect = true;
   __device__ static void begin(State&, const Params&, const EpiCtx&, int) {}
-  // columns [col0, col0 + 128) of row c.row; taddr = TMEM address of column col0
-  __device__ static bool tile(State&, const Params& p, EpiCtx& c, int col0, uint32_t taddr, int slot) {
+  // columns [col0, col0 + 128) of the chunk for row c.row; taddr = TMEM address of column col0
+  __device__ static bool tile(State&, const Params& p, EpiCtx& c, int col0, uint32_t taddr, int) {
     if (col0 >= c.N) return true;
     const int nv = min(128, c.N - col0);
     const bool live = c.row < c.M;
-    const int t = live ? __ldg(p.targets + c.row) - col0 : -1;
+    const int t = live ? __ldg(p.targets + c.row) - (p.vocab_off + col0) : -1;
+    const float r0 = live ? p.ref[c.row] : 0.f;
     float m = -INFINITY;
 #pragma unroll 1
     for (int q = 0; q < 4; ++q) {
@@ -714,7 +723,9 @@ struct EpiCEProbs {
         if (32 * q + j == t) p.tgt_logit[c.row] = v[j];
       }
     }
-    const float m2 = m * kLog2e;
+    const bool own = !(m <= r0 + kCeSlotRange);  // -inf reference: always
+    const float r = own ? m : r0;
+    const float r2 = r * kLog2e;
     float s = 0.f;
 #pragma unroll 1
     for (int h = 0; h < 2; ++h) {  // 64 columns = one 128-byte slab row of fp16
@@ -727,10 +738,10 @@ struct EpiCEProbs {
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
           const int cj = 64 * h + 32 * q + j;
-          const float e0 = cj < nv ? fast_exp2(fmaf(v[j], kLog2e, -m2)) : 0.f;
-          const float e1 = cj + 1 < nv ? fast_exp2(fmaf(v[j + 1], kLog2e, -m2)) : 0.f;
+          const float e0 = cj < nv ? fast_exp2(fmaf(v[j], kLog2e, -r2)) : 0.f;
+          const float e1 = cj + 1 < nv ? fast_exp2(fmaf(v[j + 1], kLog2e, -r2)) : 0.f;
           s += e0 + e1;
-          pk[16 * q + j / 2] = pack_half2(e0, e1);
+          pk[16 * q + j / 2] = pack_half2(cj == t ? 0.f : e0, cj + 1 == t ? 0.f : e1);
         }
       }
       if (64 * h < nv) {
@@ -741,8 +752,9 @@ struct EpiCEProbs {
       }
     }
     if (live) {
-      p.part_max[static_cast<size_t>(c.row) * p.slots + slot] = m;
-      p.part_sum[static_cast<size_t>(c.row) * p.slots + slot] = s;
+      const size_t o = static_cast<size_t>(c.row) * p.slots + ((p.vocab_off + col0) >> 7);
+      p.part_ref[o] = r;
+      p.part_sum[o] = s;
     }
     return true;
   }

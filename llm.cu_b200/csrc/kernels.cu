@@ -418,118 +418,106 @@ __global__ void ce_valid_kernel(uint8_t* valid, const int* targets, int B, int S
   valid[m] = (in_range && (all_positions || s < S - 1)) ? 1 : 0;
 }
 
-// lse[m] = log(sum_j exp(logit)) from per-tile (max, sumexp); row loss =
-// lse - logit[target] (src/kernels/loss.cu:66-67).  One warp per row.
-__global__ void ce_lse_kernel(const float* __restrict__ pmax, const float* __restrict__ psum,
-                              const float* __restrict__ tgt, const uint8_t* __restrict__ valid,
-                              float* __restrict__ lse, float* __restrict__ row_loss, int M, int T) {
+// ------------------------------------------ streamed cross-entropy steps
+// After the kCEStream GEMM of the vocabulary chunk [v0, v0 + n): a row whose
+// chunk holds slots stored relative to their own max (EpiCEStream: above the
+// row's reference + kCeSlotRange, or the first chunk) moves to the reference
+// (chunk max - kCeRefBelowMax): its fp16 chunk values are rescaled slot by
+// slot (at most exp(kCeRefBelowMax) afterwards, inside fp16's range) and its
+// fp32 d_xf accumulator by exp(old - new) (set to 0 for the first chunk).  Rows
+// whose slots all used the reference are left alone.  One warp per row.
+__global__ void ce_stream_rescale_kernel(__half* __restrict__ pc, int ldp, const float* __restrict__ part_ref,
+                                         int slots, float* __restrict__ ref, float* __restrict__ d_xf, int M, int H,
+                                         int v0, int n, int first) {
   pdl_trigger();
   pdl_wait();
   const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
-  const float* pm = pmax + static_cast<size_t>(m) * T;
-  const float* ps = psum + static_cast<size_t>(m) * T;
-  float mx = -INFINITY;
-  for (int i = lane; i < T; i += 32) mx = fmaxf(mx, pm[i]);
+  const float r_old = first ? -INFINITY : ref[m];
+  const float* pr = part_ref + static_cast<size_t>(m) * slots + (v0 >> 7);
+  const int ns = (n + 127) >> 7;
+  float mx = r_old;
+  for (int i = lane; i < ns; i += 32) mx = fmaxf(mx, pr[i]);
   mx = warp_max(mx);
-  float s = 0.f;
-  for (int i = lane; i < T; i += 32) s += ps[i] * exp2f((pm[i] - mx) * kLog2e);
-  s = warp_sum(s);
-  const float l = mx + logf(s);
-  if (lane == 0) {
-    lse[m] = l;
-    row_loss[m] = valid[m] ? (l - tgt[m]) : 0.f;
-  }
-}
-
-// dlogits from slot-relative probabilities, 8 columns (16 bytes) per thread.
-// Slot = 128-column slice of the vocabulary (column / 128).
-__global__ void ce_dlogits_kernel(__half* __restrict__ p, int ldp, int M, int V, const float* __restrict__ pmax,
-                                  int slots, const float* __restrict__ lse, const uint8_t* __restrict__ valid,
-                                  const int* __restrict__ targets, float gscale) {
-  pdl_trigger();
-  pdl_wait();
-  const int groups = (V + 7) / 8;
-  const int64_t n = static_cast<int64_t>(M) * groups;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int m = static_cast<int>(i / groups);
-    const int c0 = static_cast<int>(i % groups) * 8;
-    __half* row = p + static_cast<size_t>(m) * ldp + c0;
-    const bool ok = valid[m] != 0;
-    const float f = ok ? exp2f((pmax[static_cast<size_t>(m) * slots + c0 / 128] - lse[m]) * kLog2e) * gscale : 0.f;
-    const int t = targets[m] - c0;
-    if (c0 + 8 <= V) {
-      uint4 w = *reinterpret_cast<const uint4*>(row);
+  if (!first && !(mx > r_old)) return;
+  const float r_new = mx - kCeRefBelowMax;
+  __half* row = pc + static_cast<size_t>(m) * ldp;
+  for (int c0 = lane * 8; c0 < n; c0 += 256) {
+    const float f = exp2f((pr[c0 >> 7] - r_new) * kLog2e);
+    if (c0 + 8 <= n) {
+      uint4 w = *reinterpret_cast<const uint4*>(row + c0);
       __half2* h = reinterpret_cast<__half2*>(&w);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        float2 x = __half22float2(h[k]);
-        x.x *= f;
-        x.y *= f;
-        if (ok && t == 2 * k) x.x -= gscale;
-        if (ok && t == 2 * k + 1) x.y -= gscale;
-        h[k] = __floats2half2_rn(x.x, x.y);
+        const float2 x = __half22float2(h[k]);
+        h[k] = __floats2half2_rn(x.x * f, x.y * f);
       }
-      *reinterpret_cast<uint4*>(row) = w;
+      *reinterpret_cast<uint4*>(row + c0) = w;
     } else {
-      for (int k = 0; c0 + k < V; ++k) {
-        float x = __half2float(row[k]) * f;
-        if (ok && t == k) x -= gscale;
-        row[k] = __float2half_rn(x);
-      }
+      for (int k = 0; c0 + k < n; ++k) row[c0 + k] = __float2half_rn(__half2float(row[c0 + k]) * f);
     }
   }
+  float* dx = d_xf + static_cast<size_t>(m) * H;
+  const float a = first ? 0.f : exp2f((r_old - r_new) * kLog2e);
+  for (int c0 = lane * 4; c0 < H; c0 += 128) {
+    float4 v = first ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(dx + c0);
+    v.x *= a;
+    v.y *= a;
+    v.z *= a;
+    v.w *= a;
+    *reinterpret_cast<float4*>(dx + c0) = v;
+  }
+  if (lane == 0) ref[m] = r_new;
 }
 
-// The same for one row per blockIdx.y: the row's lse / target / validity are
-// read once, no per-element index division, U 16-byte loads in flight per
-// thread before the first store.
-template <int U>
-__global__ void ce_dlogits_row_kernel(__half* __restrict__ p, int ldp, int V, const float* __restrict__ pmax,
-                                      int slots, const float* __restrict__ lse, const uint8_t* __restrict__ valid,
-                                      const int* __restrict__ targets, float gscale) {
+// After the last chunk, per row: lse = log sum_j exp(l_j) from the slot
+// partials (each slot's sum relative to its own reference), the row loss
+// lse - l_target (src/kernels/loss.cu:66-67), and the logits' gradient
+// applied to E in fp32: d_xf held sum_{j != t} exp(l_j - ref) E_j, so
+// dX = exp(ref - lse) d_xf + (p_t - 1) E_t (src/kernels/loss.cu:62-69 times
+// E), scaled by gscale; 0 for rows outside the loss.  One warp per row.
+__global__ void ce_stream_finish_kernel(const float* __restrict__ part_ref, const float* __restrict__ part_sum,
+                                        const float* __restrict__ tgt_logit, const float* __restrict__ ref,
+                                        const uint8_t* __restrict__ valid, const int* __restrict__ targets,
+                                        const __half* __restrict__ E, int M, int H, int V, int slots, float gscale,
+                                        float* __restrict__ lse, float* __restrict__ row_loss,
+                                        float* __restrict__ d_xf) {
   pdl_trigger();
   pdl_wait();
-  const int m = blockIdx.y;
+  const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (m >= M) return;
+  const float* pr = part_ref + static_cast<size_t>(m) * slots;
+  const float* ps = part_sum + static_cast<size_t>(m) * slots;
+  float mx = -INFINITY;
+  for (int i = lane; i < slots; i += 32) mx = fmaxf(mx, pr[i]);
+  mx = warp_max(mx);
+  float s = 0.f;
+  for (int i = lane; i < slots; i += 32) s += ps[i] * exp2f((pr[i] - mx) * kLog2e);
+  s = warp_sum(s);
+  const float l = mx + logf(s);
   const bool ok = valid[m] != 0;
-  const float lm = lse[m];
-  const int tgt = targets[m];
-  __half* row = p + static_cast<size_t>(m) * ldp;
-  const float* pm = pmax + static_cast<size_t>(m) * slots;
-  const int base = blockIdx.x * (blockDim.x * 8 * U);
-  uint4 w[U];
-#pragma unroll
-  for (int u = 0; u < U; ++u) {
-    const int c0 = base + (u * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x)) * 8;
-    if (c0 + 8 <= V) w[u] = *reinterpret_cast<const uint4*>(row + c0);
+  if (lane == 0) {
+    lse[m] = l;
+    row_loss[m] = ok ? l - tgt_logit[m] : 0.f;
   }
-#pragma unroll
-  for (int u = 0; u < U; ++u) {
-    const int c0 = base + (u * static_cast<int>(blockDim.x) + static_cast<int>(threadIdx.x)) * 8;
-    if (c0 >= V) continue;
-    const float f = ok ? exp2f((pm[c0 / 128] - lm) * kLog2e) * gscale : 0.f;
-    const int t = tgt - c0;
-    if (c0 + 8 <= V) {
-      __half2* h = reinterpret_cast<__half2*>(&w[u]);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        float2 x = __half22float2(h[k]);
-        x.x *= f;
-        x.y *= f;
-        if (ok && t == 2 * k) x.x -= gscale;
-        if (ok && t == 2 * k + 1) x.y -= gscale;
-        h[k] = __floats2half2_rn(x.x, x.y);
-      }
-      *reinterpret_cast<uint4*>(row + c0) = w[u];
-    } else {
-      for (int k = 0; c0 + k < V; ++k) {
-        float x = __half2float(row[c0 + k]) * f;
-        if (ok && t == k) x -= gscale;
-        row[c0 + k] = __float2half_rn(x);
-      }
-    }
+  float* dx = d_xf + static_cast<size_t>(m) * H;
+  const float a = ok ? exp2f((ref[m] - l) * kLog2e) * gscale : 0.f;
+  const float pt1 = ok ? (exp2f((tgt_logit[m] - l) * kLog2e) - 1.0f) * gscale : 0.f;
+  const int t = min(max(targets[m], 0), V - 1);
+  const __half* et = E + static_cast<size_t>(t) * H;
+  for (int c0 = lane * 8; c0 < H; c0 += 256) {
+    float e[8];
+    load8h(et + c0, e);
+    float4 v0 = *reinterpret_cast<const float4*>(dx + c0);
+    float4 v1 = *reinterpret_cast<const float4*>(dx + c0 + 4);
+    v0 = make_float4(fmaf(a, v0.x, pt1 * e[0]), fmaf(a, v0.y, pt1 * e[1]), fmaf(a, v0.z, pt1 * e[2]),
+                     fmaf(a, v0.w, pt1 * e[3]));
+    v1 = make_float4(fmaf(a, v1.x, pt1 * e[4]), fmaf(a, v1.y, pt1 * e[5]), fmaf(a, v1.z, pt1 * e[6]),
+                     fmaf(a, v1.w, pt1 * e[7]));
+    *reinterpret_cast<float4*>(dx + c0) = v0;
+    *reinterpret_cast<float4*>(dx + c0 + 4) = v1;
   }
 }
 
@@ -862,27 +850,25 @@ cudaError_t ce_valid_rows(uint8_t* valid, const int* targets, int B, int S, int 
   return cudaGetLastError();
 }
 
-cudaError_t ce_reduce(const float* part_max, const float* part_sum, const float* tgt_logit, const uint8_t* valid,
-                      float* lse, float* row_loss_and_sum, int M, int tiles_n, cudaStream_t st) {
-  float* row_loss = row_loss_and_sum;
-  float* total = row_loss_and_sum + M;
-  launch_pdl(ce_lse_kernel, (M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, part_max, part_sum, tgt_logit, valid,
-                                                                             lse, row_loss, M, tiles_n);
-  launch_pdl(sum_kernel, 1, 1024, 0, st, row_loss, M, total);
+cudaError_t ce_stream_rescale(__half* pc, int ldp, const float* part_ref, int slots, float* ref, float* d_xf, int M,
+                              int H, int v0, int n, int first, cudaStream_t st) {
+  if (ldp % 8 || H % 4 || v0 % 128 || reinterpret_cast<uintptr_t>(pc) % 16 || reinterpret_cast<uintptr_t>(d_xf) % 16)
+    return cudaErrorInvalidValue;
+  launch_pdl(ce_stream_rescale_kernel, (M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, pc, ldp, part_ref,
+             slots, ref, d_xf, M, H, v0, n, first);
   return cudaGetLastError();
 }
 
-cudaError_t ce_dlogits(__half* p, int ldp, int M, int V, const float* part_max, int slots, const float* lse,
-                       const uint8_t* valid, const int* targets, float gscale, cudaStream_t st) {
-  if (ldp % 8) return cudaErrorInvalidValue;
-  if (M <= 65535 && reinterpret_cast<uintptr_t>(p) % 16 == 0) {
-    constexpr int kU = 4;
-    const dim3 grid((V + 256 * 8 * kU - 1) / (256 * 8 * kU), M);
-    launch_pdl(ce_dlogits_row_kernel<kU>, grid, 256, 0, st, p, ldp, V, part_max, slots, lse, valid, targets, gscale);
-    return cudaGetLastError();
-  }
-  const int64_t n = static_cast<int64_t>(M) * ((V + 7) / 8);
-  launch_pdl(ce_dlogits_kernel, grid_for(n, 256), 256, 0, st, p, ldp, M, V, part_max, slots, lse, valid, targets, gscale);
+cudaError_t ce_stream_finish(const float* part_ref, const float* part_sum, const float* tgt_logit, const float* ref,
+                             const uint8_t* valid, const int* targets, const __half* E, int M, int H, int V,
+                             int slots, float gscale, float* lse, float* row_loss_and_sum, float* d_xf,
+                             cudaStream_t st) {
+  if (H % 8 || reinterpret_cast<uintptr_t>(d_xf) % 16 || reinterpret_cast<uintptr_t>(E) % 16)
+    return cudaErrorInvalidValue;
+  float* row_loss = row_loss_and_sum;
+  launch_pdl(ce_stream_finish_kernel, (M + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, part_ref, part_sum,
+             tgt_logit, ref, valid, targets, E, M, H, V, slots, gscale, lse, row_loss, d_xf);
+  launch_pdl(sum_kernel, 1, 1024, 0, st, row_loss, M, row_loss_and_sum + M);
   return cudaGetLastError();
 }
 

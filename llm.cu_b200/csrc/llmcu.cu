@@ -9,8 +9,10 @@
 //     -> QK-norm+RoPE -> flash attention -> h_o = o A_o^T
 //     -> resid_mid = resid + [o|h_o][W_o|2B_o]^T
 //     -> rmsnorm(ffn) -> gate/up GEMM with SwiGLU -> resid_out = resid_mid + act W_d^T
-//   final rmsnorm -> lm_head pass 1 (per-tile max / sum-exp) -> LSE + loss
-//   (+ slot-relative probabilities) -> dlogits in place -> d_xf = dl E (split-K)
+//   final rmsnorm -> lm_head streamed over vocabulary chunks: per chunk the
+//   logits GEMM leaves exp(logit - row reference) in an L2-sized chunk buffer,
+//   rows that met a new maximum are rescaled, d_xf += chunk values . E_c
+//   (split-K) -> LSE, loss, d_xf = exp(ref - lse) d_xf + (p_t - 1) E_t
 //   -> final-norm backward -> for each layer, reversed:
 //     down dX + SwiGLU bwd -> gate/up dX -> ffn-norm bwd -> dh_o -> o dX (+LoRA)
 //     -> LoRA grads (o) -> attention bwd -> RoPE/QK-norm bwd -> dh_qkv
@@ -39,7 +41,11 @@ using namespace llmcu;
 namespace {
 
 constexpr float kGradScale = 64.0f;   // dlogits are scaled by this power of two (fp16 range)
-constexpr int kLmSplitK = 4;          // K (vocabulary) slices of the lm_head dX GEMM
+constexpr int kLmSplitK = 4;          // K (vocabulary) slices of each lm_head dX GEMM
+// The lm_head streams over the vocabulary in chunks whose fp16 values
+// ([rows, chunk]) fit this many elements (64 MiB: the chunk stays in L2
+// between its two GEMMs)
+constexpr size_t kCeChunkElems = static_cast<size_t>(32) << 20;
 // split-K fix-up workspace of the GEMMs whose tiles fill under half a wave
 // (small batches): about one wave of 128 x 256 fp32 partial tiles
 constexpr size_t kFxWsFloats = static_cast<size_t>(160) * 128 * 256;
@@ -98,12 +104,15 @@ struct llmcu_ctx {
   std::vector<float*> resid;  // L + 1 buffers
   std::vector<LayerA> la;
   __half* xf = nullptr;
-  float *part_max = nullptr, *part_sum = nullptr, *tgt_logit = nullptr, *lse_ce = nullptr, *row_loss = nullptr;
+  // streamed lm_head: per (row, 128-column slot) reference and sum of
+  // exp(logit - reference); per-row running reference; one chunk of values
+  float *part_ref = nullptr, *part_sum = nullptr, *tgt_logit = nullptr, *lse_ce = nullptr, *row_loss = nullptr;
+  float* ce_ref = nullptr;
   uint8_t* valid = nullptr;
-  __half* dl = nullptr;
-  int ld_dl = 0;
+  __half* pc = nullptr;  // [rows, chunk] fp16
+  size_t pc_elems = 0;
   float* d_xf = nullptr;
-  int ce_tiles = 0;
+  int ce_slots = 0;
   // backward scratch
   float *dres = nullptr, *dq = nullptr, *dk = nullptr, *delta = nullptr;
   __half* dxn = nullptr;  // dX of the normed inputs (fp16, feeds the RMSNorm backward)
@@ -169,12 +178,12 @@ llmcu_status fail(llmcu_ctx* c, llmcu_status s, const char* fmt, ...) {
   } while (0)
 
 enum ProfClass : int {
-  P_GEMM = 0, P_ATTN_FWD, P_ATTN_BWD, P_NORM, P_LORA_GRAD, P_LORA_PREP, P_CE, P_EMBED, P_ADAMW, P_DEQUANT, P_FILL,
+  P_GEMM = 0, P_ATTN_FWD, P_ATTN_BWD, P_NORM, P_LORA_GRAD, P_LORA_PREP, P_LMHEAD, P_EMBED, P_ADAMW, P_DEQUANT, P_FILL,
   P_DP_WAIT,  // no kernel: the compute stream waiting for the last allreduces after the backward
   P_COUNT
 };
 const char* kProfNames[P_COUNT] = {"gemm_tc", "attention_fwd", "attention_bwd", "norm_rope", "lora_grad",
-                                   "lora_merge", "ce_reduce", "embed", "adamw", "int8_dequant", "fill_and_loss",
+                                   "lora_merge", "lm_head", "embed", "adamw", "int8_dequant", "fill_and_loss",
                                    "dp_exposed"};
 
 // Records one event of a (begin, end) pair around `kernels` launches of class `cls`.
@@ -338,15 +347,18 @@ void carve(llmcu_ctx* c, Carver& cv) {
     a.lse = cv.take<float>(lse_n);
   }
   c->xf = cv.take<__half>(M * H);
-  c->ce_tiles = static_cast<int>((V + 255) / 256) * kGemmEpiGroups;
-  c->part_max = cv.take<float>(M * c->ce_tiles);
-  c->part_sum = cv.take<float>(M * c->ce_tiles);
+  c->ce_slots = static_cast<int>((V + 127) / 128);
+  c->part_ref = cv.take<float>(M * c->ce_slots);
+  c->part_sum = cv.take<float>(M * c->ce_slots);
   c->tgt_logit = cv.take<float>(M);
   c->lse_ce = cv.take<float>(M);
   c->row_loss = cv.take<float>(M + 1);
+  c->ce_ref = cv.take<float>(M);
   c->valid = cv.take<uint8_t>(M);
-  c->ld_dl = static_cast<int>((V + 7) / 8 * 8);
-  c->dl = cv.take<__half>(M * c->ld_dl);  // probabilities, then dlogits, [M, V] fp16
+  const size_t v_pad = (V + 255) / 256 * 256;
+  const size_t chunk = c->rc.lm_head_chunk > 0 ? std::min<size_t>(c->rc.lm_head_chunk, v_pad) : 0;
+  c->pc_elems = chunk ? M * chunk : std::min(std::max(kCeChunkElems, M * 256), M * v_pad);
+  c->pc = cv.take<__half>(c->pc_elems);  // one vocabulary chunk of the lm_head
   c->d_xf = cv.take<float>(M * H);
   c->dres = cv.take<float>(M * H);
   c->dres16 = cv.take<__half>(M * H);
@@ -651,39 +663,57 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   set_pdl(true);
   // merged q/k/v/o weights of this step's adapters, every layer
   TIMEDN(P_LORA_PREP, d.has_mlp() ? 6 : 3, merge_adapters(ctx));
-  TIMED(P_CE, ce_valid_rows(ctx->valid, ctx->tgt, B, S, ctx->rc.loss_all_positions, V, err, st));
+  TIMED(P_FILL, ce_valid_rows(ctx->valid, ctx->tgt, B, S, ctx->rc.loss_all_positions, V, err, st));
   CKS(forward_layers(ctx, B, S));
   const __half* E = ctx->E;
 
   // ------------------------------------------------------- lm_head + CE
+  // Streamed over the vocabulary (no [M, V] tensor): per chunk of columns,
+  // logits = xf E_c^T leave as fp16 exp(logit - ref) into the chunk buffer
+  // (with per-slot partials), rows that met a new maximum move to a new
+  // reference, and d_xf += values . E_c; the last step forms the loss and
+  // dX = exp(ref - lse) d_xf + (p_t - 1) E_t (src/kernels/loss.cu:13-91,
+  // src/kernels/lora_forward.cu:304, src/kernels/lora_backward.cu:243).
   float* xfinal = ctx->resid[ctx->L];
   TIMED(P_NORM, rmsnorm_forward(xfinal, ctx->final_norm, ctx->xf, M, H, eps, st));
   {
-    EpiArgs ea;
-    ea.targets = ctx->tgt;
-    ea.part_max = ctx->part_max;
-    ea.part_sum = ctx->part_sum;
-    ea.tgt_logit = ctx->tgt_logit;
-    ea.out = ctx->dl;
-    ea.ld_out = ctx->ld_dl;
-    TIMED(P_GEMM, gemm(op(ctx->xf, M, H, H), op(E, V, H, H), M, V, Epi::kCEProbs, ea, err, st, 256));
+    // chunk width: the configured one, else as wide as the buffer holds at this step's rows
+    const int v_pad = (V + 255) / 256 * 256;
+    const int vc = ctx->rc.lm_head_chunk > 0
+                       ? std::min(v_pad, ctx->rc.lm_head_chunk)
+                       : static_cast<int>(std::min<size_t>(v_pad, ctx->pc_elems / static_cast<size_t>(M) / 256 * 256));
+    // K (vocabulary) slices of each chunk's dX GEMM: kLmSplitK, more when the
+    // row tiles are few (small batches), up to about one wave of CTAs
+    const int ksplit =
+        std::max(kLmSplitK, std::min(16, gemm_num_sms() / std::max(1, (M + 127) / 128 * ((H + 255) / 256))));
+    for (int v0 = 0; v0 < V; v0 += vc) {
+      const int n = std::min(vc, V - v0);
+      const __half* Ec = E + static_cast<size_t>(v0) * H;
+      EpiArgs ea;
+      ea.targets = ctx->tgt;
+      ea.ce_ref = ctx->ce_ref;
+      ea.part_max = ctx->part_ref;
+      ea.part_sum = ctx->part_sum;
+      ea.tgt_logit = ctx->tgt_logit;
+      ea.ce_slots = ctx->ce_slots;
+      ea.vocab_off = v0;
+      ea.out = ctx->pc;
+      ea.ld_out = vc;
+      TIMED(P_LMHEAD, gemm(op(ctx->xf, M, H, H), op(Ec, n, H, H), M, n, Epi::kCEStream, ea, err, st, 256));
+      TIMED(P_LMHEAD, ce_stream_rescale(ctx->pc, vc, ctx->part_ref, ctx->ce_slots, ctx->ce_ref, ctx->d_xf, M, H, v0, n,
+                                    v0 == 0 ? 1 : 0, st));
+      EpiArgs eb;
+      eb.out = ctx->d_xf;
+      eb.ld_out = H;
+      eb.accumulate = 1;
+      eb.ksplit = ksplit;
+      // d_xf += values . E_c  (E_c [n, H] read MN-major)
+      TIMED(P_LMHEAD, gemm(op(ctx->pc, M, n, vc), op_mn(Ec, n, H, H), M, H, Epi::kStoreF32, eb, err, st));
+    }
   }
-  TIMEDN(P_CE, 2, ce_reduce(ctx->part_max, ctx->part_sum, ctx->tgt_logit, ctx->valid, ctx->lse_ce, ctx->row_loss, M,
-               ctx->ce_tiles, st));
-  TIMED(P_CE, ce_dlogits(ctx->dl, ctx->ld_dl, M, V, ctx->part_max, ctx->ce_tiles, ctx->lse_ce, ctx->valid, ctx->tgt,
-                         kGradScale, st));
-  {
-    TIMED(P_FILL, fill_f32(ctx->d_xf, static_cast<int64_t>(M) * H, 0.f, st));
-    EpiArgs eb;
-    eb.out = ctx->d_xf;
-    eb.ld_out = H;
-    eb.accumulate = 1;
-    // K (vocabulary) slices: kLmSplitK, more when the row tiles are few
-    // (small batches), up to about one wave of CTAs
-    eb.ksplit = std::max(kLmSplitK, std::min(16, gemm_num_sms() / std::max(1, (M + 127) / 128 * ((H + 255) / 256))));
-    // d_xf = dlogits . E  (E [V, H] read MN-major)
-    TIMED(P_GEMM, gemm(op(ctx->dl, M, V, ctx->ld_dl), op_mn(E, V, H, H), M, H, Epi::kStoreF32, eb, err, st));
-  }
+  TIMEDN(P_LMHEAD, 2, ce_stream_finish(ctx->part_ref, ctx->part_sum, ctx->tgt_logit, ctx->ce_ref, ctx->valid, ctx->tgt,
+                                   E, M, H, V, ctx->ce_slots, kGradScale, ctx->lse_ce, ctx->row_loss, ctx->d_xf,
+                                   st));
   // an INT8 base's down-projection row scales ride in the fp16 gradient that
   // is the next input-gradient GEMM's A operand (the GEMM stages the codes)
   const bool q8_mlp = ctx->rc.base_dtype == LLMCU_BASE_INT8 && ctx->rc.int8_in_gemm && !d.has_mlp();
@@ -983,6 +1013,7 @@ llmcu_status llmcu_ctx_create(const llmcu_model_cfg* model, const llmcu_lora_cfg
   if ((targets & kTargetsMlp) && m.ffn % 256) return LLMCU_ERR_UNSUPPORTED;
   if (run->max_batch < 1 || run->max_seq < 2) return LLMCU_ERR_INVALID_ARG;
   if (run->base_dtype != LLMCU_BASE_FP16 && run->base_dtype != LLMCU_BASE_INT8) return LLMCU_ERR_INVALID_ARG;
+  if (run->lm_head_chunk < 0 || run->lm_head_chunk % 256) return LLMCU_ERR_INVALID_ARG;
 
   llmcu_ctx* ctx = new llmcu_ctx();
   ctx->m = m;

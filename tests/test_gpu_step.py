@@ -105,6 +105,58 @@ def test_qwen3_shape_slice_matches_golden(llmcu, cuda_device):
     ctx.close()
 
 
+@pytest.mark.parametrize("chunk", [256, 1024])
+def test_streamed_lm_head_chunks_match_golden(llmcu, cuda_device, chunk):
+    """The lm_head streams over the vocabulary: with 256- and 1024-column
+    chunks the tiny 4096-token vocabulary takes 16 / 4 chunks, each a logits
+    GEMM into the chunk buffer, a reference update and a d_xf GEMM."""
+    from oracle import golden as G
+    cfg = G.CFG_TINY
+    base = G.make_base_weights(cfg, 61, round_fp16=True)
+    lora = G.make_lora(cfg, 62)
+    tok, tgt = G.make_tokens(cfg, 3, 64, 63, dist="zipf")
+    model = llmcu.Model(cfg.hidden, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab,
+                        cfg.rope_theta, cfg.rms_eps)
+    ctx = llmcu.Context(model, llmcu.Lora(cfg.lora_rank, cfg.lora_alpha), llmcu.Run(3, 64, lm_head_chunk=chunk))
+    ctx.set_base(base)
+    ctx.set_lora_dict(lora)
+    ref = G.forward_backward(cfg, base, lora, tok, tgt)
+    loss = ctx.forward_backward(tok, tgt)
+    assert abs(loss - ref.loss) <= LOSS_RTOL * abs(ref.loss), (loss, ref.loss)
+    _check_dicts(G, ctx.grads_dict(), ref.grads, f"grad chunk {chunk}")
+    ctx.close()
+
+
+def test_streamed_lm_head_new_maxima_in_later_chunks(llmcu, cuda_device):
+    """Logits far above everything the first chunks held: three embedding rows
+    (token ids in later 256-column chunks) are scaled by 40, so many rows meet
+    their maximum late, more than exp(11) above their running reference -- the
+    chunk stores those slots relative to their own maxima and the rows move to
+    a new reference (their fp16 chunk values and fp32 d_xf rescaled).  Loss and
+    gradients still match the golden on the same weights."""
+    from oracle import golden as G
+    cfg = G.CFG_TINY
+    base = G.make_base_weights(cfg, 71, round_fp16=True)
+    big = (1500, 2600, 3900)
+    for t in big:
+        base["embed"][t] = (base["embed"][t] * 40.0).astype(np.float16).astype(np.float32)
+    lora = G.make_lora(cfg, 72)
+    tok, tgt = G.make_tokens(cfg, 2, 64, 73)
+    for t in big:  # keep the scaled rows out of the inputs (they stay possible targets)
+        tok[tok == t] = t + 1
+    model = llmcu.Model(cfg.hidden, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab,
+                        cfg.rope_theta, cfg.rms_eps)
+    ctx = llmcu.Context(model, llmcu.Lora(cfg.lora_rank, cfg.lora_alpha), llmcu.Run(2, 64, lm_head_chunk=256))
+    ctx.set_base(base)
+    ctx.set_lora_dict(lora)
+    ref = G.forward_backward(cfg, base, lora, tok, tgt)
+    loss = ctx.forward_backward(tok, tgt)
+    assert ref.loss > 10.0  # the scaled rows dominate most rows' softmax
+    assert abs(loss - ref.loss) <= LOSS_RTOL * abs(ref.loss), (loss, ref.loss)
+    _check_dicts(G, ctx.grads_dict(), ref.grads, "grad (late maxima)")
+    ctx.close()
+
+
 def _int8_view(base):
     """The base weights the INT8 path computes with: every linear weight (and
     the tied embedding) quantised per output row (src/kernels/quantize.cu:8-50)
