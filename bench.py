@@ -349,6 +349,8 @@ def main():
     ap.add_argument("--int8", action="store_true", help="with --decode: INT8 base")
     ap.add_argument("--int8-in-gemm", action="store_true",
                     help="INT8 base (c4): the GEMMs stage the INT8 codes themselves instead of one dequant pass per weight")
+    ap.add_argument("--lm-head-chunk", type=int, default=0,
+                    help="vocabulary columns per lm_head chunk (multiple of 256); 0 = the library's choice")
     ap.add_argument("--lora-targets", default="attn",
                     help="adapted projections: attn (the reference's q/k/v/o), mlp, all, or a comma list of "
                          "wq,wk,wv,wo,w_gate,w_up,w_down")
@@ -382,7 +384,8 @@ def main():
     model = m.Model.qwen3_1p7b(n_layers=args.layers)
     projs = parse_targets(args.lora_targets)
     ctx = m.Context(model, m.Lora(16, 32.0, m.targets_mask(projs)),
-                    m.Run(B, S, base_dtype, int8_in_gemm=args.int8_in_gemm), device=local)
+                    m.Run(B, S, base_dtype, int8_in_gemm=args.int8_in_gemm, lm_head_chunk=args.lm_head_chunk),
+                    device=local)
     if world > 1:
         uid = share_unique_id(dist_, rank, world, m.Context.dp_unique_id)
         ctx.dp_set_timeout_ms(120000)

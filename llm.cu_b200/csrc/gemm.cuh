@@ -710,7 +710,8 @@ struct EpiCEStream {
     const int nv = min(128, c.N - col0);
     const bool live = c.row < c.M;
     const int t = live ? __ldg(p.targets + c.row) - (p.vocab_off + col0) : -1;
-    const float r0 = live ? p.ref[c.row] : 0.f;
+    // the first chunk (column 0 of the vocabulary) starts every row at -inf
+    const float r0 = (live && p.vocab_off > 0) ? p.ref[c.row] : -INFINITY;
     float m = -INFINITY;
 #pragma unroll 1
     for (int q = 0; q < 4; ++q) {

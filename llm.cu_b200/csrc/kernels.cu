@@ -425,50 +425,69 @@ __global__ void ce_valid_kernel(uint8_t* valid, const int* targets, int B, int S
 // (chunk max - kCeRefBelowMax): its fp16 chunk values are rescaled slot by
 // slot (at most exp(kCeRefBelowMax) afterwards, inside fp16's range) and its
 // fp32 d_xf accumulator by exp(old - new) (set to 0 for the first chunk).  Rows
-// whose slots all used the reference are left alone.  One warp per row.
-__global__ void ce_stream_rescale_kernel(__half* __restrict__ pc, int ldp, const float* __restrict__ part_ref,
-                                         int slots, float* __restrict__ ref, float* __restrict__ d_xf, int M, int H,
-                                         int v0, int n, int first) {
+// whose slots all used the reference are left alone.  A block takes
+// kRowWarps rows: each warp checks one row, then the whole block rescales the
+// rows that need it one after another (16-byte accesses, all threads).
+__global__ void __launch_bounds__(kRowWarps * 32)
+    ce_stream_rescale_kernel(__half* __restrict__ pc, int ldp, const float* __restrict__ part_ref, int slots,
+                             float* __restrict__ ref, float* __restrict__ d_xf, int M, int H, int v0, int n,
+                             int first) {
   pdl_trigger();
   pdl_wait();
-  const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  __shared__ float s_old[kRowWarps], s_new[kRowWarps];
+  __shared__ int s_need[kRowWarps];
+  const int w = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (m >= M) return;
-  const float r_old = first ? -INFINITY : ref[m];
-  const float* pr = part_ref + static_cast<size_t>(m) * slots + (v0 >> 7);
+  const int m = blockIdx.x * kRowWarps + w;
   const int ns = (n + 127) >> 7;
-  float mx = r_old;
-  for (int i = lane; i < ns; i += 32) mx = fmaxf(mx, pr[i]);
-  mx = warp_max(mx);
-  if (!first && !(mx > r_old)) return;
-  const float r_new = mx - kCeRefBelowMax;
-  __half* row = pc + static_cast<size_t>(m) * ldp;
-  for (int c0 = lane * 8; c0 < n; c0 += 256) {
-    const float f = exp2f((pr[c0 >> 7] - r_new) * kLog2e);
-    if (c0 + 8 <= n) {
-      uint4 w = *reinterpret_cast<const uint4*>(row + c0);
-      __half2* h = reinterpret_cast<__half2*>(&w);
+  if (m < M) {
+    const float r_old = first ? -INFINITY : ref[m];
+    const float* pr = part_ref + static_cast<size_t>(m) * slots + (v0 >> 7);
+    float mx = r_old;
+    for (int i = lane; i < ns; i += 32) mx = fmaxf(mx, pr[i]);
+    mx = warp_max(mx);
+    if (lane == 0) {
+      s_need[w] = first || mx > r_old;
+      s_old[w] = r_old;
+      s_new[w] = mx - kCeRefBelowMax;
+    }
+  } else if (lane == 0) {
+    s_need[w] = 0;
+  }
+  __syncthreads();
+  for (int k = 0; k < kRowWarps; ++k) {
+    if (!s_need[k]) continue;
+    const int row_id = blockIdx.x * kRowWarps + k;
+    const float r_new = s_new[k];
+    const float* pr = part_ref + static_cast<size_t>(row_id) * slots + (v0 >> 7);
+    __half* row = pc + static_cast<size_t>(row_id) * ldp;
+    for (int c0 = threadIdx.x * 8; c0 < n; c0 += kRowWarps * 32 * 8) {
+      const float f = exp2f((pr[c0 >> 7] - r_new) * kLog2e);
+      if (c0 + 8 <= n) {
+        uint4 u = *reinterpret_cast<const uint4*>(row + c0);
+        __half2* h = reinterpret_cast<__half2*>(&u);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float2 x = __half22float2(h[k]);
-        h[k] = __floats2half2_rn(x.x * f, x.y * f);
+        for (int j = 0; j < 4; ++j) {
+          const float2 x = __half22float2(h[j]);
+          h[j] = __floats2half2_rn(x.x * f, x.y * f);
+        }
+        *reinterpret_cast<uint4*>(row + c0) = u;
+      } else {
+        for (int j = 0; c0 + j < n; ++j) row[c0 + j] = __float2half_rn(__half2float(row[c0 + j]) * f);
       }
-      *reinterpret_cast<uint4*>(row + c0) = w;
-    } else {
-      for (int k = 0; c0 + k < n; ++k) row[c0 + k] = __float2half_rn(__half2float(row[c0 + k]) * f);
+    }
+    float* dx = d_xf + static_cast<size_t>(row_id) * H;
+    const float a = first ? 0.f : exp2f((s_old[k] - r_new) * kLog2e);
+    for (int c0 = threadIdx.x * 4; c0 < H; c0 += kRowWarps * 32 * 4) {
+      float4 v = first ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(dx + c0);
+      v.x *= a;
+      v.y *= a;
+      v.z *= a;
+      v.w *= a;
+      *reinterpret_cast<float4*>(dx + c0) = v;
     }
   }
-  float* dx = d_xf + static_cast<size_t>(m) * H;
-  const float a = first ? 0.f : exp2f((r_old - r_new) * kLog2e);
-  for (int c0 = lane * 4; c0 < H; c0 += 128) {
-    float4 v = first ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(dx + c0);
-    v.x *= a;
-    v.y *= a;
-    v.z *= a;
-    v.w *= a;
-    *reinterpret_cast<float4*>(dx + c0) = v;
-  }
-  if (lane == 0) ref[m] = r_new;
+  if (threadIdx.x < kRowWarps && s_need[threadIdx.x]) ref[blockIdx.x * kRowWarps + threadIdx.x] = s_new[threadIdx.x];
 }
 
 // After the last chunk, per row: lse = log sum_j exp(l_j) from the slot
@@ -476,48 +495,66 @@ __global__ void ce_stream_rescale_kernel(__half* __restrict__ pc, int ldp, const
 // lse - l_target (src/kernels/loss.cu:66-67), and the logits' gradient
 // applied to E in fp32: d_xf held sum_{j != t} exp(l_j - ref) E_j, so
 // dX = exp(ref - lse) d_xf + (p_t - 1) E_t (src/kernels/loss.cu:62-69 times
-// E), scaled by gscale; 0 for rows outside the loss.  One warp per row.
-__global__ void ce_stream_finish_kernel(const float* __restrict__ part_ref, const float* __restrict__ part_sum,
-                                        const float* __restrict__ tgt_logit, const float* __restrict__ ref,
-                                        const uint8_t* __restrict__ valid, const int* __restrict__ targets,
-                                        const __half* __restrict__ E, int M, int H, int V, int slots, float gscale,
-                                        float* __restrict__ lse, float* __restrict__ row_loss,
-                                        float* __restrict__ d_xf) {
+// E), scaled by gscale; 0 for rows outside the loss.  A block takes kRowWarps
+// rows: a warp reduces one row's partials, then the whole block updates the
+// rows' d_xf.
+__global__ void __launch_bounds__(kRowWarps * 32)
+    ce_stream_finish_kernel(const float* __restrict__ part_ref, const float* __restrict__ part_sum,
+                            const float* __restrict__ tgt_logit, const float* __restrict__ ref,
+                            const uint8_t* __restrict__ valid, const int* __restrict__ targets,
+                            const __half* __restrict__ E, int M, int H, int V, int slots, float gscale,
+                            float* __restrict__ lse, float* __restrict__ row_loss, float* __restrict__ d_xf) {
   pdl_trigger();
   pdl_wait();
-  const int m = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  __shared__ float s_a[kRowWarps], s_pt1[kRowWarps];
+  __shared__ int s_t[kRowWarps], s_ok[kRowWarps];
+  const int w = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (m >= M) return;
-  const float* pr = part_ref + static_cast<size_t>(m) * slots;
-  const float* ps = part_sum + static_cast<size_t>(m) * slots;
-  float mx = -INFINITY;
-  for (int i = lane; i < slots; i += 32) mx = fmaxf(mx, pr[i]);
-  mx = warp_max(mx);
-  float s = 0.f;
-  for (int i = lane; i < slots; i += 32) s += ps[i] * exp2f((pr[i] - mx) * kLog2e);
-  s = warp_sum(s);
-  const float l = mx + logf(s);
-  const bool ok = valid[m] != 0;
-  if (lane == 0) {
-    lse[m] = l;
-    row_loss[m] = ok ? l - tgt_logit[m] : 0.f;
+  const int m = blockIdx.x * kRowWarps + w;
+  if (m < M) {
+    const float* pr = part_ref + static_cast<size_t>(m) * slots;
+    const float* ps = part_sum + static_cast<size_t>(m) * slots;
+    float mx = -INFINITY;
+    for (int i = lane; i < slots; i += 32) mx = fmaxf(mx, pr[i]);
+    mx = warp_max(mx);
+    float s = 0.f;
+    for (int i = lane; i < slots; i += 32) s += ps[i] * exp2f((pr[i] - mx) * kLog2e);
+    s = warp_sum(s);
+    const float l = mx + logf(s);
+    const bool ok = valid[m] != 0;
+    if (lane == 0) {
+      lse[m] = l;
+      row_loss[m] = ok ? l - tgt_logit[m] : 0.f;
+      s_a[w] = ok ? exp2f((ref[m] - l) * kLog2e) * gscale : 0.f;
+      s_pt1[w] = ok ? (exp2f((tgt_logit[m] - l) * kLog2e) - 1.0f) * gscale : 0.f;
+      s_t[w] = min(max(targets[m], 0), V - 1);
+      s_ok[w] = ok;
+    }
   }
-  float* dx = d_xf + static_cast<size_t>(m) * H;
-  const float a = ok ? exp2f((ref[m] - l) * kLog2e) * gscale : 0.f;
-  const float pt1 = ok ? (exp2f((tgt_logit[m] - l) * kLog2e) - 1.0f) * gscale : 0.f;
-  const int t = min(max(targets[m], 0), V - 1);
-  const __half* et = E + static_cast<size_t>(t) * H;
-  for (int c0 = lane * 8; c0 < H; c0 += 256) {
-    float e[8];
-    load8h(et + c0, e);
-    float4 v0 = *reinterpret_cast<const float4*>(dx + c0);
-    float4 v1 = *reinterpret_cast<const float4*>(dx + c0 + 4);
-    v0 = make_float4(fmaf(a, v0.x, pt1 * e[0]), fmaf(a, v0.y, pt1 * e[1]), fmaf(a, v0.z, pt1 * e[2]),
-                     fmaf(a, v0.w, pt1 * e[3]));
-    v1 = make_float4(fmaf(a, v1.x, pt1 * e[4]), fmaf(a, v1.y, pt1 * e[5]), fmaf(a, v1.z, pt1 * e[6]),
-                     fmaf(a, v1.w, pt1 * e[7]));
-    *reinterpret_cast<float4*>(dx + c0) = v0;
-    *reinterpret_cast<float4*>(dx + c0 + 4) = v1;
+  __syncthreads();
+  for (int k = 0; k < kRowWarps; ++k) {
+    const int row_id = blockIdx.x * kRowWarps + k;
+    if (row_id >= M) break;
+    const float a = s_a[k], pt1 = s_pt1[k];
+    const __half* et = E + static_cast<size_t>(s_t[k]) * H;
+    float* dx = d_xf + static_cast<size_t>(row_id) * H;
+    if (!s_ok[k]) {  // rows outside the loss: zero, whatever the accumulator held
+      for (int c0 = threadIdx.x * 4; c0 < H; c0 += kRowWarps * 32 * 4)
+        *reinterpret_cast<float4*>(dx + c0) = make_float4(0.f, 0.f, 0.f, 0.f);
+      continue;
+    }
+    for (int c0 = threadIdx.x * 8; c0 < H; c0 += kRowWarps * 32 * 8) {
+      float e[8];
+      load8h(et + c0, e);
+      float4 v0 = *reinterpret_cast<const float4*>(dx + c0);
+      float4 v1 = *reinterpret_cast<const float4*>(dx + c0 + 4);
+      v0 = make_float4(fmaf(a, v0.x, pt1 * e[0]), fmaf(a, v0.y, pt1 * e[1]), fmaf(a, v0.z, pt1 * e[2]),
+                       fmaf(a, v0.w, pt1 * e[3]));
+      v1 = make_float4(fmaf(a, v1.x, pt1 * e[4]), fmaf(a, v1.y, pt1 * e[5]), fmaf(a, v1.z, pt1 * e[6]),
+                       fmaf(a, v1.w, pt1 * e[7]));
+      *reinterpret_cast<float4*>(dx + c0) = v0;
+      *reinterpret_cast<float4*>(dx + c0 + 4) = v1;
+    }
   }
 }
 

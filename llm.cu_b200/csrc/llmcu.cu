@@ -43,9 +43,11 @@ namespace {
 constexpr float kGradScale = 64.0f;   // dlogits are scaled by this power of two (fp16 range)
 constexpr int kLmSplitK = 4;          // K (vocabulary) slices of each lm_head dX GEMM
 // The lm_head streams over the vocabulary in chunks whose fp16 values
-// ([rows, chunk]) fit this many elements (64 MiB: the chunk stays in L2
-// between its two GEMMs)
-constexpr size_t kCeChunkElems = static_cast<size_t>(32) << 20;
+// ([rows, chunk]) fit this many elements (128 MiB: 16384 columns at 4096
+// rows; measured on B200 against 8192 / 32768 columns, the shorter chain of
+// launches outweighs the part of the chunk that leaves L2)
+constexpr size_t kCeChunkElems = static_cast<size_t>(64) << 20;
+constexpr int kCeFirstChunk = 2048;  // vocabulary columns of the first chunk
 // split-K fix-up workspace of the GEMMs whose tiles fill under half a wave
 // (small batches): about one wave of 128 x 256 fp32 partial tiles
 constexpr size_t kFxWsFloats = static_cast<size_t>(160) * 128 * 256;
@@ -677,17 +679,25 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   float* xfinal = ctx->resid[ctx->L];
   TIMED(P_NORM, rmsnorm_forward(xfinal, ctx->final_norm, ctx->xf, M, H, eps, st));
   {
-    // chunk width: the configured one, else as wide as the buffer holds at this step's rows
+    // chunk width: the configured one, else as wide as the buffer holds at
+    // this step's rows; the first chunk is narrower (every row of the first
+    // chunk is rescaled once its maximum is known, so it is kept small)
     const int v_pad = (V + 255) / 256 * 256;
     const int vc = ctx->rc.lm_head_chunk > 0
                        ? std::min(v_pad, ctx->rc.lm_head_chunk)
                        : static_cast<int>(std::min<size_t>(v_pad, ctx->pc_elems / static_cast<size_t>(M) / 256 * 256));
+    const int vc0 = std::min(vc, kCeFirstChunk);
     // K (vocabulary) slices of each chunk's dX GEMM: kLmSplitK, more when the
     // row tiles are few (small batches), up to about one wave of CTAs
     const int ksplit =
         std::max(kLmSplitK, std::min(16, gemm_num_sms() / std::max(1, (M + 127) / 128 * ((H + 255) / 256))));
-    for (int v0 = 0; v0 < V; v0 += vc) {
-      const int n = std::min(vc, V - v0);
+    int launches = 2;  // + ce_stream_finish's two
+    for (int v0 = 0; v0 < V; v0 += (v0 == 0 ? vc0 : vc)) launches += 3;
+    // one event pair around the whole section (per-kernel events would break
+    // the programmatic-launch overlap of its short kernels)
+    prof_mark(ctx, P_LMHEAD, launches);
+    for (int v0 = 0; v0 < V;) {
+      const int n = std::min(v0 == 0 ? vc0 : vc, V - v0);
       const __half* Ec = E + static_cast<size_t>(v0) * H;
       EpiArgs ea;
       ea.targets = ctx->tgt;
@@ -699,21 +709,22 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
       ea.vocab_off = v0;
       ea.out = ctx->pc;
       ea.ld_out = vc;
-      TIMED(P_LMHEAD, gemm(op(ctx->xf, M, H, H), op(Ec, n, H, H), M, n, Epi::kCEStream, ea, err, st, 256));
-      TIMED(P_LMHEAD, ce_stream_rescale(ctx->pc, vc, ctx->part_ref, ctx->ce_slots, ctx->ce_ref, ctx->d_xf, M, H, v0, n,
-                                    v0 == 0 ? 1 : 0, st));
+      CK(gemm(op(ctx->xf, M, H, H), op(Ec, n, H, H), M, n, Epi::kCEStream, ea, err, st, 256));
+      CK(ce_stream_rescale(ctx->pc, vc, ctx->part_ref, ctx->ce_slots, ctx->ce_ref, ctx->d_xf, M, H, v0, n,
+                           v0 == 0 ? 1 : 0, st));
       EpiArgs eb;
       eb.out = ctx->d_xf;
       eb.ld_out = H;
       eb.accumulate = 1;
       eb.ksplit = ksplit;
       // d_xf += values . E_c  (E_c [n, H] read MN-major)
-      TIMED(P_LMHEAD, gemm(op(ctx->pc, M, n, vc), op_mn(Ec, n, H, H), M, H, Epi::kStoreF32, eb, err, st));
+      CK(gemm(op(ctx->pc, M, n, vc), op_mn(Ec, n, H, H), M, H, Epi::kStoreF32, eb, err, st));
+      v0 += n;
     }
+    CK(ce_stream_finish(ctx->part_ref, ctx->part_sum, ctx->tgt_logit, ctx->ce_ref, ctx->valid, ctx->tgt, E, M, H, V,
+                        ctx->ce_slots, kGradScale, ctx->lse_ce, ctx->row_loss, ctx->d_xf, st));
+    prof_mark(ctx, P_LMHEAD, launches);
   }
-  TIMEDN(P_LMHEAD, 2, ce_stream_finish(ctx->part_ref, ctx->part_sum, ctx->tgt_logit, ctx->ce_ref, ctx->valid, ctx->tgt,
-                                   E, M, H, V, ctx->ce_slots, kGradScale, ctx->lse_ce, ctx->row_loss, ctx->d_xf,
-                                   st));
   // an INT8 base's down-projection row scales ride in the fp16 gradient that
   // is the next input-gradient GEMM's A operand (the GEMM stages the codes)
   const bool q8_mlp = ctx->rc.base_dtype == LLMCU_BASE_INT8 && ctx->rc.int8_in_gemm && !d.has_mlp();
