@@ -88,8 +88,17 @@ typedef struct {
                                    into the input-gradient GEMM's A operand)    */
     int32_t lm_head_chunk;      /* vocabulary columns per lm_head chunk (the
                                    lm_head streams over the vocabulary; a
-                                   multiple of 256); 0 = as many as fit 64 MiB
-                                   of fp16 values at max_batch * max_seq rows */
+                                   multiple of 256); 0 = as many as fit 128 MiB
+                                   of fp16 values at the step's rows           */
+    int32_t deterministic;      /* 1 = every sum has a fixed order, so the same
+                                   step gives the same bits every time: the
+                                   attention backward stores each key tile's dQ
+                                   partial in its own slab (+ B * ceil(S/128)^2
+                                   * 128 * nh * hd floats of memory) and they
+                                   are summed in order; 0 = dQ is reduce-added
+                                   by the key tiles in no fixed order (faster).
+                                   The adapter gradients' sums are ordered
+                                   either way                                   */
 } llmcu_run_cfg;
 
 typedef struct {

@@ -296,7 +296,8 @@ __global__ void __launch_bounds__(192, 1)
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                        const __grid_constant__ CUtensorMap tmDQ, const float* __restrict__ lse,
                        const float* __restrict__ delta, float* __restrict__ dk, __half* __restrict__ dv, int S,
-                       int nh, int nkv, int lddk, int lddv, float scale, float scale_log2, int* err) {
+                       int nh, int nkv, int lddk, int lddv, float scale, float scale_log2, int dq_slab_rows,
+                       int* err) {
   using L = BwdLayout<HD>;
   constexpr int kDBoxes = HD / 64;
   pdl_trigger();
@@ -512,11 +513,22 @@ __global__ void __launch_bounds__(192, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
-          asm volatile(
-              "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                  reinterpret_cast<uint64_t>(&tmDQ)),
-              "r"(slab), "r"(hq * HD + 32 * c), "r"(row_base + q0 + qd * 32)
-              : "memory");
+          if (dq_slab_rows == 0) {
+            asm volatile(
+                "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                    reinterpret_cast<uint64_t>(&tmDQ)),
+                "r"(slab), "r"(hq * HD + 32 * c), "r"(row_base + q0 + qd * 32)
+                : "memory");
+          } else {
+            // deterministic mode: this key tile's partial into its own slab
+            // (rows padded to whole 128-row tiles per sequence), summed in key
+            // tile order by the QK-norm / RoPE backward
+            const int prow = kt * dq_slab_rows + (b * nqt + qt) * 128 + qd * 32;
+            asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                             reinterpret_cast<uint64_t>(&tmDQ)),
+                         "r"(slab), "r"(hq * HD + 32 * c), "r"(prow)
+                         : "memory");
+          }
           asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
       }
@@ -608,12 +620,15 @@ template <int HD>
 cudaError_t bwd_tc_launch(const __half* q, const __half* k, const __half* v, const __half* dout, const float* lse,
                           const float* delta, float* dq, float* dk, __half* dv, int B, int S, int nh, int nkv,
                           int ldq, int ldk, int ldv, int ldo, int lddq, int lddk, int lddv, int* err,
-                          cudaStream_t st, bool dq_zeroed) {
+                          cudaStream_t st, bool dq_zeroed, float* dq_slabs) {
   using L = BwdLayout<HD>;
   CUtensorMap mq, mk, mv, mo, mdq;
+  const int nqt = (S + 127) / 128;
+  const int slab_rows = dq_slabs ? B * nqt * 128 : 0;  // rows of one key tile's slab
   if (!tile_map(&mq, q, B * S, nh * HD, ldq) || !tile_map(&mk, k, B * S, nkv * HD, ldk) ||
       !tile_map(&mv, v, B * S, nkv * HD, ldv) || !tile_map(&mo, dout, B * S, nh * HD, ldo) ||
-      !f32_slab_map(&mdq, dq, B * S, nh * HD, lddq))
+      !(dq_slabs ? f32_slab_map(&mdq, dq_slabs, nqt * slab_rows, nh * HD, nh * HD)
+                 : f32_slab_map(&mdq, dq, B * S, nh * HD, lddq)))
     return cudaErrorInvalidValue;
   auto kern = attn_bwd_tc_kernel<HD>;
   static std::atomic<unsigned long long> attr_set{0};
@@ -623,15 +638,16 @@ cudaError_t bwd_tc_launch(const __half* q, const __half* k, const __half* v, con
     });
     if (e != cudaSuccess) return e;
   }
-  // dQ accumulates partial products of every key tile (into zeros)
-  if (!dq_zeroed) {
+  // dQ accumulates partial products of every key tile (into zeros), unless
+  // each key tile stores its own slab
+  if (!dq_zeroed && !dq_slabs) {
     cudaError_t e = fill_f32_2d(dq, lddq, B * S, nh * HD, 0.f, st);
     if (e != cudaSuccess) return e;
   }
   dim3 grid(nkv, B, (S + 127) / 128);
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));
   launch_pdl(kern, grid, 192, L::kBytes, st, mq, mk, mv, mo, mdq, lse, delta, dk, dv, S, nh, nkv, lddk, lddv, scale,
-             scale * kLog2e, err);
+             scale * kLog2e, slab_rows, err);
   return cudaGetLastError();
 }
 
@@ -665,13 +681,13 @@ cudaError_t fwd_tc_launch(const __half* q, const __half* k, const __half* v, __h
 cudaError_t attention_backward_tc(const __half* q, const __half* k, const __half* v, const __half* dout,
                                   const float* lse, const float* delta, float* dq, float* dk, __half* dv, int B, int S,
                                   int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int lddq, int lddk,
-                                  int lddv, int* err, cudaStream_t st, bool dq_zeroed) {
+                                  int lddv, int* err, cudaStream_t st, bool dq_zeroed, float* dq_slabs) {
   if (hd == 128)
     return bwd_tc_launch<128>(q, k, v, dout, lse, delta, dq, dk, dv, B, S, nh, nkv, ldq, ldk, ldv, ldo, lddq, lddk,
-                              lddv, err, st, dq_zeroed);
+                              lddv, err, st, dq_zeroed, dq_slabs);
   if (hd == 64)
     return bwd_tc_launch<64>(q, k, v, dout, lse, delta, dq, dk, dv, B, S, nh, nkv, ldq, ldk, ldv, ldo, lddq, lddk,
-                             lddv, err, st, dq_zeroed);
+                             lddv, err, st, dq_zeroed, dq_slabs);
   return cudaErrorInvalidValue;
 }
 

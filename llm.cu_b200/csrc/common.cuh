@@ -72,11 +72,15 @@ cudaError_t attention_backward(const __half* q, const __half* k, const __half* v
                                int B, int S, int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int lddq,
                                int lddk, int lddv, int* err, cudaStream_t st);
 // dq accumulates with reduce-adds: it is zeroed first unless the caller
-// already did (dq_zeroed).
+// already did (dq_zeroed).  With dq_slabs (deterministic mode) dq is not
+// touched: key tile kt stores its partial into slab kt of dq_slabs
+// [nqt][B * nqt * 128][nh * hd] fp32 (nqt = ceil(S / 128), each sequence's
+// rows padded to whole tiles), for qknorm_rope_backward to sum in order.
 cudaError_t attention_backward_tc(const __half* q, const __half* k, const __half* v, const __half* dout,
                                   const float* lse, const float* delta, float* dq, float* dk, __half* dv, int B, int S,
                                   int nh, int nkv, int hd, int ldq, int ldk, int ldv, int ldo, int lddq, int lddk,
-                                  int lddv, int* err, cudaStream_t st, bool dq_zeroed = false);
+                                  int lddv, int* err, cudaStream_t st, bool dq_zeroed = false,
+                                  float* dq_slabs = nullptr);
 
 // ---- gemm.cu
 // Column slices per GEMM tile (epilogue warps per TMEM lane quadrant); the
@@ -208,9 +212,12 @@ cudaError_t rmsnorm_backward(const __half* dy, const float* x, const float* w, f
 cudaError_t qknorm_rope_forward(const __half* qkv, int ld_qkv, const float* qn_w, const float* kn_w, int ld_out,
                                 const float* cos_t, const float* sin_t, __half* q_out, __half* k_out, int B, int S,
                                 int nh, int nkv, int hd, float eps, cudaStream_t st);
+// dq_slabs (deterministic mode): dq is read as the sum, in key-tile order, of
+// the attention backward's per-key-tile slabs (see attention_backward_tc).
 cudaError_t qknorm_rope_backward(const float* dq, const float* dk, const __half* qkv, int ld_qkv, const float* qn_w,
                                  const float* kn_w, const float* cos_t, const float* sin_t, __half* dqkv, int B,
-                                 int S, int nh, int nkv, int hd, float eps, cudaStream_t st);
+                                 int S, int nh, int nkv, int hd, float eps, cudaStream_t st,
+                                 const float* dq_slabs = nullptr);
 cudaError_t rope_tables(float* cos_t, float* sin_t, int S, int hd, float theta, cudaStream_t st);
 cudaError_t ce_valid_rows(uint8_t* valid, const int* targets, int B, int S, int all_positions, int V, int* err,
                           cudaStream_t st);

@@ -346,7 +346,7 @@ __global__ void qknorm_rope_bwd_vec_kernel(const float* __restrict__ dq, const f
                                            const __half* __restrict__ qkv, int ld, const float* __restrict__ qn_w,
                                            const float* __restrict__ kn_w, const float* __restrict__ cos_t,
                                            const float* __restrict__ sin_t, __half* __restrict__ dqkv, int M, int S,
-                                           int nh, int nkv, float eps) {
+                                           int nh, int nkv, float eps, const float* __restrict__ dq_slabs) {
   pdl_trigger();
   pdl_wait();
   using C = QkLanes<HD>;
@@ -369,8 +369,26 @@ __global__ void qknorm_rope_bwd_vec_kernel(const float* __restrict__ dq, const f
     const float* gw = isq ? qn_w : kn_w;
     ld8h(qkv + static_cast<size_t>(m) * ld + col + d, x0);
     ld8h(qkv + static_cast<size_t>(m) * ld + col + d + C::kHalf, x1);
-    ld8f(g + d, g0);
-    ld8f(g + d + C::kHalf, g1);
+    if (isq && dq_slabs) {
+      // key tiles 0 .. this query tile, in order (causal: no later one touches it)
+      const int nqt = (S + 127) / 128;
+      const int qt = pos >> 7;
+      const size_t slab = static_cast<size_t>(M / S) * nqt * 128 * nh * HD;
+      const float* p = dq_slabs + (static_cast<size_t>(m / S) * nqt * 128 + pos) * nh * HD + hh * HD;
+      for (int kt = 0; kt <= qt; ++kt) {
+        float a0[8], a1[8];
+        ld8f(p + kt * slab + d, a0);
+        ld8f(p + kt * slab + d + C::kHalf, a1);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          g0[i] += a0[i];
+          g1[i] += a1[i];
+        }
+      }
+    } else {
+      ld8f(g + d, g0);
+      ld8f(g + d + C::kHalf, g1);
+    }
     ld8f(cos_t + pos * C::kHalf + d, c);
     ld8f(sin_t + pos * C::kHalf + d, sn);
     ld8f(gw + d, w0);
@@ -863,17 +881,17 @@ cudaError_t qknorm_rope_forward(const __half* qkv, int ld_qkv, const float* qn_w
 
 cudaError_t qknorm_rope_backward(const float* dq, const float* dk, const __half* qkv, int ld_qkv, const float* qn_w,
                                  const float* kn_w, const float* cos_t, const float* sin_t, __half* dqkv, int B,
-                                 int S, int nh, int nkv, int hd, float eps, cudaStream_t st) {
+                                 int S, int nh, int nkv, int hd, float eps, cudaStream_t st, const float* dq_slabs) {
   const int M = B * S;
   if (ld_qkv % 8) return cudaErrorInvalidValue;
   if (hd == 128) {
     const int warps = M * ((nh + nkv + QkLanes<128>::kHpw - 1) / QkLanes<128>::kHpw);
-    launch_pdl(qknorm_rope_bwd_vec_kernel<128>, (warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, 
-        dq, dk, qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, dqkv, M, S, nh, nkv, eps);
+    launch_pdl(qknorm_rope_bwd_vec_kernel<128>, (warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st,
+               dq, dk, qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, dqkv, M, S, nh, nkv, eps, dq_slabs);
   } else if (hd == 64) {
     const int warps = M * ((nh + nkv + QkLanes<64>::kHpw - 1) / QkLanes<64>::kHpw);
-    launch_pdl(qknorm_rope_bwd_vec_kernel<64>, (warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st, 
-        dq, dk, qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, dqkv, M, S, nh, nkv, eps);
+    launch_pdl(qknorm_rope_bwd_vec_kernel<64>, (warps + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0, st,
+               dq, dk, qkv, ld_qkv, qn_w, kn_w, cos_t, sin_t, dqkv, M, S, nh, nkv, eps, dq_slabs);
   } else {
     return cudaErrorInvalidValue;
   }

@@ -52,6 +52,10 @@ constexpr int kCeFirstChunk = 2048;  // vocabulary columns of the first chunk
 // (small batches): about one wave of 128 x 256 fp32 partial tiles
 constexpr size_t kFxWsFloats = static_cast<size_t>(160) * 128 * 256;
 constexpr int kFxCounters = 16384;
+// adapter-gradient split partials (lora_grad): enough for the per-layer
+// batches at the split counts lora_grad_splits picks (fewer splits otherwise)
+constexpr size_t kLgWsFloats = static_cast<size_t>(8) << 20;
+constexpr int kLgCounters = 1024;
 
 struct LayerW {
   __half *wqkv, *wo, *wgu, *wd;  // fp16 base, [out, in] (also read MN-major by the dX GEMMs)
@@ -117,6 +121,7 @@ struct llmcu_ctx {
   int ce_slots = 0;
   // backward scratch
   float *dres = nullptr, *dq = nullptr, *dk = nullptr, *delta = nullptr;
+  float* dq_slabs = nullptr;  // deterministic mode: per-key-tile dQ partials
   __half* dxn = nullptr;  // dX of the normed inputs (fp16, feeds the RMSNorm backward)
   __half *dres16 = nullptr, *dgu = nullptr, *dho = nullptr, *dattn = nullptr, *dqkv = nullptr, *dhq = nullptr;
   __half* dres16m = nullptr;  // fp16 gradient at the attention block's output (the FFN norm backward's)
@@ -125,6 +130,8 @@ struct llmcu_ctx {
   int *tok = nullptr, *tgt = nullptr, *derr = nullptr;
   float* fx_ws = nullptr;  // split-K fix-up partials (set_gemm_workspace)
   int* fx_cnt = nullptr;
+  float* lg_ws = nullptr;  // adapter-gradient split partials and their counters
+  int* lg_cnt = nullptr;
   float* loss_dev = nullptr;   // [0] = mean loss of the last step
   float *rope_cos = nullptr, *rope_sin = nullptr;
   float* stage = nullptr;      // fp32 staging for host uploads
@@ -370,6 +377,10 @@ void carve(llmcu_ctx* c, Carver& cv) {
   c->dho = cv.take<__half>(M * 64);
   c->dattn = cv.take<__half>(M * Q);
   c->dq = cv.take<float>(M * Q);
+  if (c->rc.deterministic) {
+    const size_t nqt = (static_cast<size_t>(c->rc.max_seq) + 127) / 128;
+    c->dq_slabs = cv.take<float>(nqt * static_cast<size_t>(c->rc.max_batch) * nqt * 128 * Q);
+  }
   c->dk = cv.take<float>(M * KV);
   c->delta = cv.take<float>(lse_n);
   c->dqkv = cv.take<__half>(M * QKV);
@@ -378,6 +389,8 @@ void carve(llmcu_ctx* c, Carver& cv) {
   c->dhd = mlp ? cv.take<__half>(M * 64) : nullptr;
   c->fx_ws = cv.take<float>(kFxWsFloats);
   c->fx_cnt = cv.take<int>(kFxCounters);
+  c->lg_ws = cv.take<float>(kLgWsFloats);
+  c->lg_cnt = cv.take<int>(kLgCounters);
   c->tok = cv.take<int>(M);
   c->tgt = cv.take<int>(M);
   c->derr = cv.take<int>(4);
@@ -652,15 +665,17 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   ctx->last_n_valid = n_valid_local;
   const float unscale = static_cast<float>(1.0 / (kGradScale * n_valid_total));
 
-  // gradients accumulate (lora_grad adds each split's share); this first
-  // kernel follows the host's token upload, so it is launched normally and the
-  // rest of the step's kernels chain by programmatic dependent launch
+  // the gradients start at zero (lora_grad stores every adapter it trains);
+  // this first kernel follows the host's token upload, so it is launched
+  // normally and the rest of the step's kernels chain by programmatic
+  // dependent launch
   struct PdlScope {
     ~PdlScope() { set_pdl(false); }
   } pdl_scope;
   set_pdl(false);
   GemmWorkspaceScope gws(ctx);
   CK(cudaMemsetAsync(ctx->fx_cnt, 0, sizeof(int) * kFxCounters, st));
+  CK(cudaMemsetAsync(ctx->lg_cnt, 0, sizeof(int) * kLgCounters, st));
   TIMED(P_FILL, fill_f32(ctx->lg, ctx->n_lora, 0.f, st));
   set_pdl(true);
   // merged q/k/v/o weights of this step's adapters, every layer
@@ -743,11 +758,16 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   cudaStream_t gs = ctx->prof_on ? st : ctx->side;
   const bool split = gs != st;
   auto ev_side = [&](int l, int k) { return ctx->ev_side[4 * l + k]; };  // 0/1 MLP in/out, 2/3 attention in/out
-  auto side_grad = [&](int l, int k, const LoraGradBatch& gb) -> llmcu_status {
+  auto side_grad = [&](int l, int k, LoraGradBatch gb) -> llmcu_status {
     if (split) {
       CK(cudaEventRecord(ev_side(l, k), st));
       CK(cudaStreamWaitEvent(gs, ev_side(l, k), 0));
     }
+    gb.ws = ctx->lg_ws;
+    gb.ws_floats = kLgWsFloats;
+    gb.cnt = ctx->lg_cnt;
+    gb.cnt_n = kLgCounters;
+    gb.err = err;
     set_pdl(!split);
     TIMED(P_LORA_GRAD, lora_grad(gb, M, gs));
     set_pdl(true);
@@ -774,7 +794,8 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     CK(cudaEventRecord(ctx->ev_dq_done, gs));
     return LLMCU_OK;
   };
-  if (split) CKS(zero_dq_side());
+  const bool slabs = ctx->dq_slabs != nullptr;  // deterministic dQ: no zeroing, no reduce-add
+  if (split && !slabs) CKS(zero_dq_side());
   for (int l = ctx->L - 1; l >= 0; --l) {
     LayerW& w = ctx->lw[l];
     LayerA& a = ctx->la[l];
@@ -863,18 +884,18 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     }
     // attention
     // (delta came with the O-projection dX GEMM)
-    if (split) {  // dq was zeroed on the side stream
+    if (split && !slabs) {  // dq was zeroed on the side stream
       CK(cudaStreamWaitEvent(st, ctx->ev_dq_done, 0));
       set_pdl(false);
     }
-    TIMEDN(P_ATTN_BWD, split ? 1 : 2,
+    TIMEDN(P_ATTN_BWD, split || slabs ? 1 : 2,
            attention_backward_tc(a.qkr, a.qkr + Q, a.qkv + Q + KV, ctx->dattn, a.lse, ctx->delta, ctx->dq, ctx->dk,
                                  ctx->dqkv + Q + KV, B, S, ctx->nh, ctx->nkv, ctx->hd, Q + KV, Q + KV, QKV, Q, Q, KV,
-                                 QKV, err, st, split));
+                                 QKV, err, st, split, ctx->dq_slabs));
     set_pdl(true);
     TIMED(P_NORM, qknorm_rope_backward(ctx->dq, ctx->dk, a.qkv, QKV, w.q_norm, w.k_norm, ctx->rope_cos, ctx->rope_sin, ctx->dqkv,
-                            B, S, ctx->nh, ctx->nkv, ctx->hd, eps, st));
-    if (split && l > 0) CKS(zero_dq_side());  // for the next layer, once read
+                            B, S, ctx->nh, ctx->nkv, ctx->hd, eps, st, ctx->dq_slabs));
+    if (split && !slabs && l > 0) CKS(zero_dq_side());  // for the next layer, once read
     // QKV projection
     {  // [dxn | dh_qkv] = dqkv . mqkv (MN-major)
       EpiArgs ea;
@@ -1025,6 +1046,7 @@ llmcu_status llmcu_ctx_create(const llmcu_model_cfg* model, const llmcu_lora_cfg
   if (run->max_batch < 1 || run->max_seq < 2) return LLMCU_ERR_INVALID_ARG;
   if (run->base_dtype != LLMCU_BASE_FP16 && run->base_dtype != LLMCU_BASE_INT8) return LLMCU_ERR_INVALID_ARG;
   if (run->lm_head_chunk < 0 || run->lm_head_chunk % 256) return LLMCU_ERR_INVALID_ARG;
+  if (run->deterministic != 0 && run->deterministic != 1) return LLMCU_ERR_INVALID_ARG;
 
   llmcu_ctx* ctx = new llmcu_ctx();
   ctx->m = m;

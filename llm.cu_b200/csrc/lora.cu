@@ -30,8 +30,9 @@
 // (src/kernels/lora_backward.cu:50-90, src/kernels/matmul.cu:102-139):
 //   dB = s * dY^T h     (a over d_out, b over r)
 //   dA = dh^T x         (computed as (x^T dh)^T: a over d_in, b over r)
-// on the tensor cores, split over m; each split adds its share into the
-// zeroed gradients with fp32 atomics.
+// on the tensor cores, split over m; the splits' fp32 partials are summed
+// in split order by the last split to finish, so the gradients are the same
+// bits from run to run.
 #include "common.cuh"
 #include "lora.cuh"
 
@@ -546,49 +547,86 @@ __global__ void __launch_bounds__(kLgThreads, 2)
 
   // ------------------------------------------------------------ epilogue
   // warp w owns TMEM lanes 32w.. = a-rows a0 + 32w + lane; column b = 16 g + j
-  const bool got = nsteps > 0 && mbar_wait(acc_full, 0, abort_flag, nullptr, 0);
-  if (__syncthreads_and(got)) {  // CTA-uniform: the staged path below synchronises
+  const bool got = nsteps == 0 || mbar_wait(acc_full, 0, abort_flag, batch.err, kErrWaitAccum);
+  __shared__ int s_last;
+  if (__syncthreads_and(got)) {  // CTA-uniform: the reduction below synchronises
     tc_fence_after();
     const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const int ar = warp * 32 + lane;  // a-row within the tile
     const int a = a0 + ar;
     const int ng = pb.groups;
-    // [a][b] row-major gradients (dB: sa = 16, sb = 1) are staged through
-    // shared memory so that the additions leave as contiguous runs; the
-    // [b][a] ones (dA: sa = 1) are already contiguous across the lanes
-    const bool staged = pb.sb == 1 && pb.sa == 16 && pb.Bn == 16 && (ng == 1 || pb.ilv) && a0 + kLgA <= pb.A;
-    float* stage = reinterpret_cast<float*>(smem);  // [128][17], the stage buffers are idle now
-    uint32_t v[32];
-    if (staged) {  // group sel's 16 columns lie in the first 32
-      tmem_ld_32x32b_x32(taddr, v);
-      tmem_ld_wait();
+    const int ncol = 16 * ng;  // accumulator columns in use (<= 64)
+    float acc[64];
+    if (nsteps > 0) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) stage[ar * 17 + j] = __uint_as_float(v[16 * sel + j]) * pb.scale;
-    } else {
-      // gradient row of this lane's a (the interleave maps a to its adapter row)
-      const int orow = pb.ilv ? ((a0 >> 8) << 7) + ar : a;
-#pragma unroll 1
       for (int half = 0; half < 2; ++half) {
-        if (32 * half < 16 * ng) {  // warp-uniform
+        if (32 * half < ncol) {  // warp-uniform
+          uint32_t v[32];
           tmem_ld_32x32b_x32(taddr + 32 * half, v);
           tmem_ld_wait();
-          if (a < pb.A) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int bcol = 32 * half + j;
-              const int g = bcol >> 4, b = bcol & 15;
-              if (g < ng && b < pb.Bn && pb.out[g] && (!pb.ilv || g == sel))
-                atomicAdd(pb.out[g] + static_cast<size_t>(orow) * pb.sa + static_cast<size_t>(b) * pb.sb,
-                          __uint_as_float(v[j]) * pb.scale);
-            }
-          }
+          for (int j = 0; j < 32; ++j) acc[32 * half + j] = __uint_as_float(v[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[32 * half + j] = 0.f;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+    }
+    bool last = true;
+    if (splits > 1) {
+      // this split's partial [column][a-row] (each warp writes 128 contiguous bytes per column)
+      const int slot = blockIdx.y * gridDim.x + blockIdx.x;
+      float* wsb = batch.ws + static_cast<size_t>(slot) * splits * (64 * kLgA);
+      float* mine = wsb + static_cast<size_t>(split) * (64 * kLgA);
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        if (j < ncol) __stcg(mine + j * kLgA + ar, acc[j]);
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        const int prev = atomicAdd(batch.cnt + slot, 1);
+        s_last = prev == splits - 1;
+        if (s_last) batch.cnt[slot] = 0;  // ready for the next launch
+      }
+      __syncthreads();
+      last = s_last != 0;
+      if (last) {
+        __threadfence();
+        // every split's partial, in split order
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          if (j >= ncol) continue;
+          float t = 0.f;
+          for (int s2 = 0; s2 < splits; ++s2) t += __ldcg(wsb + static_cast<size_t>(s2) * (64 * kLgA) + j * kLgA + ar);
+          acc[j] = t;
         }
       }
     }
-    if (staged) {
-      __syncthreads();
-      float* dst = pb.out[sel] + static_cast<size_t>(pb.ilv ? ((a0 >> 8) << 7) : a0) * 16;
-      for (int i = threadIdx.x; i < kLgA * 16; i += kLgThreads) atomicAdd(dst + i, stage[(i >> 4) * 17 + (i & 15)]);
+    if (last) {
+      // [a][b] row-major gradients (dB: sa = 16, sb = 1) are staged through
+      // shared memory so that the stores leave as contiguous runs; the
+      // [b][a] ones (dA: sa = 1) are already contiguous across the lanes
+      const bool staged = pb.sb == 1 && pb.sa == 16 && pb.Bn == 16 && (ng == 1 || pb.ilv) && a0 + kLgA <= pb.A;
+      float* stage = reinterpret_cast<float*>(smem);  // [128][17], the stage buffers are idle now
+      if (staged) {  // group sel's 16 columns
+#pragma unroll
+        for (int j = 0; j < 16; ++j) stage[ar * 17 + j] = (sel ? acc[16 + j] : acc[j]) * pb.scale;
+        __syncthreads();
+        float* dst = pb.out[sel] + static_cast<size_t>(pb.ilv ? ((a0 >> 8) << 7) : a0) * 16;
+        for (int i = threadIdx.x; i < kLgA * 16; i += kLgThreads) dst[i] = stage[(i >> 4) * 17 + (i & 15)];
+      } else if (a < pb.A) {
+        // gradient row of this lane's a (the interleave maps a to its adapter row)
+        const int orow = pb.ilv ? ((a0 >> 8) << 7) + ar : a;
+#pragma unroll
+        for (int bcol = 0; bcol < 64; ++bcol) {
+          const int g = bcol >> 4, b = bcol & 15;
+          if (g < ng && b < pb.Bn && pb.out[g] && (!pb.ilv || g == sel))
+            pb.out[g][static_cast<size_t>(orow) * pb.sa + static_cast<size_t>(b) * pb.sb] = acc[bcol] * pb.scale;
+        }
+      }
     }
   }
   tc_fence_before();
@@ -666,7 +704,12 @@ int lora_grad_splits(int M, const LoraGradBatch& batch) {
 
 cudaError_t lora_grad(const LoraGradBatch& batch, int M, cudaStream_t st) {
   if (batch.n <= 0 || batch.n > kLoraMaxProbs) return cudaErrorInvalidValue;
-  const int splits = lora_grad_splits(M, batch);
+  int splits = lora_grad_splits(M, batch);
+  const int tiles = (batch.a_max + kLgA - 1) / kLgA;
+  // the splits' partials must fit the workspace (fewer splits otherwise)
+  const size_t per_split = static_cast<size_t>(batch.n) * tiles * 64 * kLgA;
+  if (!batch.ws || !batch.cnt || batch.cnt_n < batch.n * tiles) splits = 1;
+  while (splits > 1 && per_split * splits > batch.ws_floats) --splits;
   static std::atomic<unsigned long long> attr_set{0};
   {
     cudaError_t e = once_per_device(attr_set, [] {

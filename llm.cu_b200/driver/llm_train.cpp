@@ -136,7 +136,7 @@ int main(int argc, char** argv) {
     }
     lc.targets = mask;
   }
-  llmcu_run_cfg rc = {batch, seq_len, int8 ? LLMCU_BASE_INT8 : LLMCU_BASE_FP16, 0, int8_in_gemm ? 1 : 0, 0};
+  llmcu_run_cfg rc = {batch, seq_len, int8 ? LLMCU_BASE_INT8 : LLMCU_BASE_FP16, 0, int8_in_gemm ? 1 : 0, 0, 0};
   if (rank == 0)
     printf("Training config: lr=%.2e steps=%d seq_len=%d batch=%d world=%d model=%s base=%s lora rank=%d "
            "alpha=%g targets=0x%x\n",

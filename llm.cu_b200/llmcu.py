@@ -62,7 +62,8 @@ class _LoraCfg(C.Structure):
 
 class _RunCfg(C.Structure):
     _fields_ = [("max_batch", C.c_int32), ("max_seq", C.c_int32), ("base_dtype", C.c_int32),
-                ("loss_all_positions", C.c_int32), ("int8_in_gemm", C.c_int32), ("lm_head_chunk", C.c_int32)]
+                ("loss_all_positions", C.c_int32), ("int8_in_gemm", C.c_int32), ("lm_head_chunk", C.c_int32),
+                ("deterministic", C.c_int32)]
 
 
 class _LoraLayout(C.Structure):
@@ -114,6 +115,7 @@ class Run:
     loss_all_positions: bool = False
     int8_in_gemm: bool = False  # INT8 base: the GEMMs stage the codes themselves (else one dequant pass per weight)
     lm_head_chunk: int = 0      # vocabulary columns per lm_head chunk (multiple of 256); 0 = automatic
+    deterministic: bool = False  # fixed-order sums everywhere (dQ slabs): bit-identical repeated steps
 
 
 @dataclass(frozen=True)
@@ -213,7 +215,7 @@ class Context:
                        model.ffn, model.vocab, model.rope_theta, model.rms_eps)
         lc = _LoraCfg(lora.rank, lora.alpha, lora.targets)
         rc = _RunCfg(run.max_batch, run.max_seq, run.base_dtype, int(run.loss_all_positions), int(run.int8_in_gemm),
-                     int(run.lm_head_chunk))
+                     int(run.lm_head_chunk), int(run.deterministic))
         h = C.c_void_p()
         st = L.llmcu_ctx_create(C.byref(mc), C.byref(lc), C.byref(rc), device, C.byref(h))
         if st != OK:

@@ -157,6 +157,38 @@ def test_streamed_lm_head_new_maxima_in_later_chunks(llmcu, cuda_device):
     ctx.close()
 
 
+@pytest.mark.parametrize("shape", ["tiny", "qwen3_slice"])
+def test_deterministic_steps_repeat_bit_for_bit(llmcu, cuda_device, shape):
+    """With llmcu_run_cfg.deterministic every sum in the step has a fixed order
+    (the attention backward's dQ partials are stored per key tile and summed in
+    key-tile order; the adapter gradients' m-splits are summed in split order):
+    the same step run twice gives the same loss and gradient bits, and still
+    matches the golden.  Sequences of 300 tokens span three key tiles, the last
+    one ragged."""
+    from oracle import golden as G
+    cfg = G.CFG_TINY if shape == "tiny" else G.layer_slice(G.CFG_QWEN3_1P7B, 2, vocab=8192)
+    batch, seq = 2, 300
+    base = G.make_base_weights(cfg, 81, round_fp16=True)
+    lora = G.make_lora(cfg, 82)
+    tok, tgt = G.make_tokens(cfg, batch, seq, 83, dist="zipf")
+    model = llmcu.Model(cfg.hidden, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab,
+                        cfg.rope_theta, cfg.rms_eps)
+    ctx = llmcu.Context(model, llmcu.Lora(cfg.lora_rank, cfg.lora_alpha), llmcu.Run(batch, seq, deterministic=True))
+    ctx.set_base(base)
+    ctx.set_lora_dict(lora)
+    loss1 = ctx.forward_backward(tok, tgt)
+    g1 = ctx.grads_dict()
+    loss2 = ctx.forward_backward(tok, tgt)
+    g2 = ctx.grads_dict()
+    assert np.float32(loss1).tobytes() == np.float32(loss2).tobytes()
+    for k in g1:
+        assert np.array_equal(g1[k].view(np.uint32), g2[k].view(np.uint32)), k
+    ref = G.forward_backward(cfg, base, lora, tok, tgt, threads=8)
+    assert abs(loss1 - ref.loss) <= LOSS_RTOL * abs(ref.loss), (loss1, ref.loss)
+    _check_dicts(G, g1, ref.grads, "deterministic grad")
+    ctx.close()
+
+
 def _int8_view(base):
     """The base weights the INT8 path computes with: every linear weight (and
     the tied embedding) quantised per output row (src/kernels/quantize.cu:8-50)
