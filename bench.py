@@ -349,6 +349,8 @@ def main():
     ap.add_argument("--int8", action="store_true", help="with --decode: INT8 base")
     ap.add_argument("--int8-in-gemm", action="store_true",
                     help="INT8 base (c4): the GEMMs stage the INT8 codes themselves instead of one dequant pass per weight")
+    ap.add_argument("--deterministic", action="store_true",
+                    help="fixed-order sums everywhere (per-key-tile dQ slabs): bit-identical repeated steps")
     ap.add_argument("--lm-head-chunk", type=int, default=0,
                     help="vocabulary columns per lm_head chunk (multiple of 256); 0 = the library's choice")
     ap.add_argument("--lora-targets", default="attn",
@@ -384,7 +386,8 @@ def main():
     model = m.Model.qwen3_1p7b(n_layers=args.layers)
     projs = parse_targets(args.lora_targets)
     ctx = m.Context(model, m.Lora(16, 32.0, m.targets_mask(projs)),
-                    m.Run(B, S, base_dtype, int8_in_gemm=args.int8_in_gemm, lm_head_chunk=args.lm_head_chunk),
+                    m.Run(B, S, base_dtype, int8_in_gemm=args.int8_in_gemm, lm_head_chunk=args.lm_head_chunk,
+                          deterministic=args.deterministic),
                     device=local)
     if world > 1:
         uid = share_unique_id(dist_, rank, world, m.Context.dp_unique_id)
@@ -514,7 +517,8 @@ def main():
                        "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world}",
                        "lora": "rank 16 alpha 32 on " + "/".join(projs),
                        "int8": ("codes staged by the GEMMs" if args.int8_in_gemm else "one dequant pass per weight")
-                       if base_dtype else None, "l2": "inputs larger than L2 (6.9 GB of weights "
+                       if base_dtype else None, "deterministic": bool(args.deterministic),
+                       "l2": "inputs larger than L2 (6.9 GB of weights "
                        "and ~9 GB of activations stream per step); no flush"},
             "step_roofline": {"alg_tflop_per_step": round(step_alg / 1e12, 3),
                               "achieved_tflops": round(step_alg / (ms / 1e3) / 1e12 / world, 2),

@@ -52,8 +52,9 @@ struct GemmShape {
   // K splits with a fix-up (fixup != 0, splits > 1): every split of a tile
   // leaves its fp32 partial of each epilogue warp's slice in fx_ws; the last
   // split to arrive (counted in fx_cnt, one counter per slice, reset by that
-  // split) adds the others' partials into its TMEM accumulator and runs the
-  // tile's epilogue as usual -- for GEMMs whose tiles fill under half a wave
+  // split) sums all partials in split order into its TMEM accumulator and
+  // runs the tile's epilogue as usual -- for GEMMs whose tiles fill under
+  // half a wave
   int fixup;
   float* fx_ws;         // [tiles * CG * 4 * groups][splits][slice columns / 4][32] float4
   int* fx_cnt;          // [tiles * CG * 4 * groups], zero between launches
@@ -1148,15 +1149,14 @@ __global__ void __launch_bounds__(64 + 32 * EW + (Q8 ? kQ8Threads : 0), 1)
         run = prev == sh.splits - 1;
         if (run) {
           __threadfence();
+          // every split's partial (this one's included), summed in split
+          // order into the accumulator: the same bits whichever split is last
 #pragma unroll 1
           for (int q = 0; q < kSliceCols / 32; ++q) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(tbase + col_of(q), v);
             float4 a[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) a[j] = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int s2 = 0; s2 < sh.splits; ++s2) {
-              if (s2 == sp) continue;
               const float4* o = wsb + static_cast<size_t>(s2) * (8 * kSliceCols) + 8 * q * 32 + lane;
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
@@ -1167,13 +1167,13 @@ __global__ void __launch_bounds__(64 + 32 * EW + (Q8 ? kQ8Threads : 0), 1)
                 a[j].w += t.w;
               }
             }
-            tmem_ld_wait();
+            uint32_t v[32];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              v[4 * j] = __float_as_uint(__uint_as_float(v[4 * j]) + a[j].x);
-              v[4 * j + 1] = __float_as_uint(__uint_as_float(v[4 * j + 1]) + a[j].y);
-              v[4 * j + 2] = __float_as_uint(__uint_as_float(v[4 * j + 2]) + a[j].z);
-              v[4 * j + 3] = __float_as_uint(__uint_as_float(v[4 * j + 3]) + a[j].w);
+              v[4 * j] = __float_as_uint(a[j].x);
+              v[4 * j + 1] = __float_as_uint(a[j].y);
+              v[4 * j + 2] = __float_as_uint(a[j].z);
+              v[4 * j + 3] = __float_as_uint(a[j].w);
             }
             tmem_st_32x32b_x32(tbase + col_of(q), v);
           }

@@ -55,7 +55,6 @@ constexpr int kFxCounters = 16384;
 // adapter-gradient split partials (lora_grad): enough for the per-layer
 // batches at the split counts lora_grad_splits picks (fewer splits otherwise)
 constexpr size_t kLgWsFloats = static_cast<size_t>(8) << 20;
-constexpr int kLgCounters = 1024;
 
 struct LayerW {
   __half *wqkv, *wo, *wgu, *wd;  // fp16 base, [out, in] (also read MN-major by the dX GEMMs)
@@ -130,8 +129,7 @@ struct llmcu_ctx {
   int *tok = nullptr, *tgt = nullptr, *derr = nullptr;
   float* fx_ws = nullptr;  // split-K fix-up partials (set_gemm_workspace)
   int* fx_cnt = nullptr;
-  float* lg_ws = nullptr;  // adapter-gradient split partials and their counters
-  int* lg_cnt = nullptr;
+  float* lg_ws = nullptr;  // adapter-gradient split partials
   float* loss_dev = nullptr;   // [0] = mean loss of the last step
   float *rope_cos = nullptr, *rope_sin = nullptr;
   float* stage = nullptr;      // fp32 staging for host uploads
@@ -390,7 +388,6 @@ void carve(llmcu_ctx* c, Carver& cv) {
   c->fx_ws = cv.take<float>(kFxWsFloats);
   c->fx_cnt = cv.take<int>(kFxCounters);
   c->lg_ws = cv.take<float>(kLgWsFloats);
-  c->lg_cnt = cv.take<int>(kLgCounters);
   c->tok = cv.take<int>(M);
   c->tgt = cv.take<int>(M);
   c->derr = cv.take<int>(4);
@@ -675,7 +672,6 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
   set_pdl(false);
   GemmWorkspaceScope gws(ctx);
   CK(cudaMemsetAsync(ctx->fx_cnt, 0, sizeof(int) * kFxCounters, st));
-  CK(cudaMemsetAsync(ctx->lg_cnt, 0, sizeof(int) * kLgCounters, st));
   TIMED(P_FILL, fill_f32(ctx->lg, ctx->n_lora, 0.f, st));
   set_pdl(true);
   // merged q/k/v/o weights of this step's adapters, every layer
@@ -703,9 +699,13 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
                        : static_cast<int>(std::min<size_t>(v_pad, ctx->pc_elems / static_cast<size_t>(M) / 256 * 256));
     const int vc0 = std::min(vc, kCeFirstChunk);
     // K (vocabulary) slices of each chunk's dX GEMM: kLmSplitK, more when the
-    // row tiles are few (small batches), up to about one wave of CTAs
+    // row tiles are few (small batches), up to about one wave of CTAs; they
+    // reduce-add in no fixed order, so the deterministic mode takes none (the
+    // GEMM's own ordered split fix-up then fills small batches)
     const int ksplit =
-        std::max(kLmSplitK, std::min(16, gemm_num_sms() / std::max(1, (M + 127) / 128 * ((H + 255) / 256))));
+        ctx->rc.deterministic
+            ? 1
+            : std::max(kLmSplitK, std::min(16, gemm_num_sms() / std::max(1, (M + 127) / 128 * ((H + 255) / 256))));
     int launches = 2;  // + ce_stream_finish's two
     for (int v0 = 0; v0 < V; v0 += (v0 == 0 ? vc0 : vc)) launches += 3;
     // one event pair around the whole section (per-kernel events would break
@@ -765,11 +765,9 @@ llmcu_status run_forward_backward(llmcu_ctx* ctx, int B, int S) {
     }
     gb.ws = ctx->lg_ws;
     gb.ws_floats = kLgWsFloats;
-    gb.cnt = ctx->lg_cnt;
-    gb.cnt_n = kLgCounters;
     gb.err = err;
     set_pdl(!split);
-    TIMED(P_LORA_GRAD, lora_grad(gb, M, gs));
+    TIMEDN(P_LORA_GRAD, lora_grad_splits(M, gb) > 1 ? 2 : 1, lora_grad(gb, M, gs));
     set_pdl(true);
     if (split) CK(cudaEventRecord(ev_side(l, k + 1), gs));
     return LLMCU_OK;

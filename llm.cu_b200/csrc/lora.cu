@@ -31,8 +31,8 @@
 //   dB = s * dY^T h     (a over d_out, b over r)
 //   dA = dh^T x         (computed as (x^T dh)^T: a over d_in, b over r)
 // on the tensor cores, split over m; the splits' fp32 partials are summed
-// in split order by the last split to finish, so the gradients are the same
-// bits from run to run.
+// in split order by a second small kernel, so the gradients are the same bits
+// from run to run.
 #include "common.cuh"
 #include "lora.cuh"
 
@@ -434,6 +434,35 @@ constexpr int kLgUBytes = kLgM * kLgA * 2;  // 16 KB: two [64 m][64 a] TMA boxes
 constexpr int kLgWBytes = kLgM * 64 * 2;    // 8 KB: one [64 m][64 b] TMA box
 constexpr int kLgSmem = kLgStages * (kLgUBytes + kLgWBytes) + 1024 + 256;
 
+// Stores one a-tile's final sums into the problem's gradients: acc[16 g + b]
+// of a-row ar (of the tile at a0) times the problem's scale.  [a][b]
+// row-major gradients (dB: sa = 16, sb = 1) are staged through shared memory
+// `stage` ([128][17] floats) so that the stores leave as contiguous runs; the
+// [b][a] ones (dA: sa = 1) are already contiguous across the lanes.  The
+// staged case synchronises the CTA (its condition is CTA-uniform).
+__device__ __forceinline__ void lg_store(const LoraGradProb& pb, int a0, int sel, int ar, const float (&acc)[64],
+                                         float* stage) {
+  const int ng = pb.groups;
+  const int a = a0 + ar;
+  const bool staged = pb.sb == 1 && pb.sa == 16 && pb.Bn == 16 && (ng == 1 || pb.ilv) && a0 + 128 <= pb.A;
+  if (staged) {  // group sel's 16 columns
+#pragma unroll
+    for (int j = 0; j < 16; ++j) stage[ar * 17 + j] = (sel ? acc[16 + j] : acc[j]) * pb.scale;
+    __syncthreads();
+    float* dst = pb.out[sel] + static_cast<size_t>(pb.ilv ? ((a0 >> 8) << 7) : a0) * 16;
+    for (int i = threadIdx.x; i < 128 * 16; i += blockDim.x) dst[i] = stage[(i >> 4) * 17 + (i & 15)];
+  } else if (a < pb.A) {
+    // gradient row of this lane's a (the interleave maps a to its adapter row)
+    const int orow = pb.ilv ? ((a0 >> 8) << 7) + ar : a;
+#pragma unroll
+    for (int bcol = 0; bcol < 64; ++bcol) {
+      const int g = bcol >> 4, b = bcol & 15;
+      if (g < ng && b < pb.Bn && pb.out[g] && (!pb.ilv || g == sel))
+        pb.out[g][static_cast<size_t>(orow) * pb.sa + static_cast<size_t>(b) * pb.sb] = acc[bcol] * pb.scale;
+    }
+  }
+}
+
 // U and W of every problem as TMA tensors ([M, A] and [M, 16 * groups]),
 // 64 x 64 boxes, 128-byte swizzle
 struct LoraGradMaps {
@@ -548,85 +577,35 @@ __global__ void __launch_bounds__(kLgThreads, 2)
   // ------------------------------------------------------------ epilogue
   // warp w owns TMEM lanes 32w.. = a-rows a0 + 32w + lane; column b = 16 g + j
   const bool got = nsteps == 0 || mbar_wait(acc_full, 0, abort_flag, batch.err, kErrWaitAccum);
-  __shared__ int s_last;
-  if (__syncthreads_and(got)) {  // CTA-uniform: the reduction below synchronises
+  if (__syncthreads_and(got)) {  // CTA-uniform: the staged store below synchronises
     tc_fence_after();
     const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const int ar = warp * 32 + lane;  // a-row within the tile
-    const int a = a0 + ar;
-    const int ng = pb.groups;
-    const int ncol = 16 * ng;  // accumulator columns in use (<= 64)
+    const int ncol = 16 * pb.groups;  // accumulator columns in use (<= 64)
     float acc[64];
-    if (nsteps > 0) {
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        if (32 * half < ncol) {  // warp-uniform
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(taddr + 32 * half, v);
-          tmem_ld_wait();
+    for (int half = 0; half < 2; ++half) {
+      if (nsteps > 0 && 32 * half < ncol) {  // warp-uniform
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + 32 * half, v);
+        tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[32 * half + j] = __uint_as_float(v[j]);
-        } else {
+        for (int j = 0; j < 32; ++j) acc[32 * half + j] = __uint_as_float(v[j]);
+      } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[32 * half + j] = 0.f;
-        }
+        for (int j = 0; j < 32; ++j) acc[32 * half + j] = 0.f;
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 64; ++j) acc[j] = 0.f;
     }
-    bool last = true;
     if (splits > 1) {
-      // this split's partial [column][a-row] (each warp writes 128 contiguous bytes per column)
+      // this split's partial [column][a-row] (each warp writes 128 contiguous
+      // bytes per column); lora_grad_reduce_kernel sums the splits in order
       const int slot = blockIdx.y * gridDim.x + blockIdx.x;
-      float* wsb = batch.ws + static_cast<size_t>(slot) * splits * (64 * kLgA);
-      float* mine = wsb + static_cast<size_t>(split) * (64 * kLgA);
+      float* mine = batch.ws + (static_cast<size_t>(slot) * splits + split) * (64 * kLgA);
 #pragma unroll
       for (int j = 0; j < 64; ++j)
-        if (j < ncol) __stcg(mine + j * kLgA + ar, acc[j]);
-      __threadfence();
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        const int prev = atomicAdd(batch.cnt + slot, 1);
-        s_last = prev == splits - 1;
-        if (s_last) batch.cnt[slot] = 0;  // ready for the next launch
-      }
-      __syncthreads();
-      last = s_last != 0;
-      if (last) {
-        __threadfence();
-        // every split's partial, in split order
-#pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          if (j >= ncol) continue;
-          float t = 0.f;
-          for (int s2 = 0; s2 < splits; ++s2) t += __ldcg(wsb + static_cast<size_t>(s2) * (64 * kLgA) + j * kLgA + ar);
-          acc[j] = t;
-        }
-      }
-    }
-    if (last) {
-      // [a][b] row-major gradients (dB: sa = 16, sb = 1) are staged through
-      // shared memory so that the stores leave as contiguous runs; the
-      // [b][a] ones (dA: sa = 1) are already contiguous across the lanes
-      const bool staged = pb.sb == 1 && pb.sa == 16 && pb.Bn == 16 && (ng == 1 || pb.ilv) && a0 + kLgA <= pb.A;
-      float* stage = reinterpret_cast<float*>(smem);  // [128][17], the stage buffers are idle now
-      if (staged) {  // group sel's 16 columns
-#pragma unroll
-        for (int j = 0; j < 16; ++j) stage[ar * 17 + j] = (sel ? acc[16 + j] : acc[j]) * pb.scale;
-        __syncthreads();
-        float* dst = pb.out[sel] + static_cast<size_t>(pb.ilv ? ((a0 >> 8) << 7) : a0) * 16;
-        for (int i = threadIdx.x; i < kLgA * 16; i += kLgThreads) dst[i] = stage[(i >> 4) * 17 + (i & 15)];
-      } else if (a < pb.A) {
-        // gradient row of this lane's a (the interleave maps a to its adapter row)
-        const int orow = pb.ilv ? ((a0 >> 8) << 7) + ar : a;
-#pragma unroll
-        for (int bcol = 0; bcol < 64; ++bcol) {
-          const int g = bcol >> 4, b = bcol & 15;
-          if (g < ng && b < pb.Bn && pb.out[g] && (!pb.ilv || g == sel))
-            pb.out[g][static_cast<size_t>(orow) * pb.sa + static_cast<size_t>(b) * pb.sb] = acc[bcol] * pb.scale;
-        }
-      }
+        if (j < ncol) mine[j * kLgA + ar] = acc[j];
+    } else {
+      lg_store(pb, a0, sel, ar, acc, reinterpret_cast<float*>(smem));  // the stage buffers are idle now
     }
   }
   tc_fence_before();
@@ -635,6 +614,34 @@ __global__ void __launch_bounds__(kLgThreads, 2)
     tc_fence_after();
     tmem_dealloc(tmem, 64);
   }
+}
+
+// The m-splits' partials of lora_grad_kernel summed in split order (the same
+// bits whatever order the splits finished in) and stored as lg_store does.
+// One CTA per (a-tile, problem), thread = a-row.
+__global__ void __launch_bounds__(128) lora_grad_reduce_kernel(const LoraGradBatch batch, int splits) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float stage[128 * 17];
+  const LoraGradProb& pb = batch.p[blockIdx.y];
+  const int a0 = blockIdx.x * kLgA;
+  if (a0 >= pb.A) return;
+  const int sel = pb.ilv ? (a0 >> 7) & 1 : 0;
+  if (!pb.out[sel] && (pb.ilv || pb.groups == 1)) return;
+  const int ar = threadIdx.x;
+  const int ncol = 16 * pb.groups;
+  const float* wsb = batch.ws + static_cast<size_t>(blockIdx.y * gridDim.x + blockIdx.x) * splits * (64 * kLgA);
+  float acc[64];
+#pragma unroll
+  for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+  // split by split (in order), every column's load of a split in flight together
+  for (int s2 = 0; s2 < splits; ++s2) {
+    const float* src = wsb + static_cast<size_t>(s2) * 64 * kLgA + ar;
+#pragma unroll
+    for (int j = 0; j < 64; ++j)
+      if (j < ncol) acc[j] += src[j * kLgA];
+  }
+  lg_store(pb, a0, sel, ar, acc, stage);
 }
 
 }  // namespace
@@ -699,17 +706,17 @@ int lora_grad_splits(int M, const LoraGradBatch& batch) {
   if (s > max_s) s = max_s;
   if (s > kLoraMaxSplits) s = kLoraMaxSplits;
   if (s < 1) s = 1;
+  // the splits' partials must fit the workspace (fewer splits otherwise)
+  const size_t per_split = static_cast<size_t>(batch.n) * ((batch.a_max + kLgA - 1) / kLgA) * 64 * kLgA;
+  if (!batch.ws) s = 1;
+  while (s > 1 && per_split * s > batch.ws_floats) --s;
   return s;
 }
 
 cudaError_t lora_grad(const LoraGradBatch& batch, int M, cudaStream_t st) {
   if (batch.n <= 0 || batch.n > kLoraMaxProbs) return cudaErrorInvalidValue;
-  int splits = lora_grad_splits(M, batch);
+  const int splits = lora_grad_splits(M, batch);
   const int tiles = (batch.a_max + kLgA - 1) / kLgA;
-  // the splits' partials must fit the workspace (fewer splits otherwise)
-  const size_t per_split = static_cast<size_t>(batch.n) * tiles * 64 * kLgA;
-  if (!batch.ws || !batch.cnt || batch.cnt_n < batch.n * tiles) splits = 1;
-  while (splits > 1 && per_split * splits > batch.ws_floats) --splits;
   static std::atomic<unsigned long long> attr_set{0};
   {
     cudaError_t e = once_per_device(attr_set, [] {
@@ -726,8 +733,9 @@ cudaError_t lora_grad(const LoraGradBatch& batch, int M, cudaStream_t st) {
         !encode_tma_2d_f16(&maps.w[i], p.W, M, 16 * p.groups, p.ldw, kLgM))
       return cudaErrorInvalidValue;
   }
-  dim3 grid((batch.a_max + kLgA - 1) / kLgA, batch.n, splits);
+  dim3 grid(tiles, batch.n, splits);
   launch_pdl(lora_grad_kernel, grid, kLgThreads, kLgSmem, st, maps, batch, M, splits);
+  if (splits > 1) launch_pdl(lora_grad_reduce_kernel, dim3(tiles, batch.n), 128, 0, st, batch, splits);
   return cudaGetLastError();
 }
 

@@ -105,22 +105,21 @@ struct LoraGradBatch {
   int n;
   int a_max;  // >= every A
   // split reduction: each m-split's fp32 partial [64 columns][128 a-rows] of
-  // an (a-tile, problem) goes to ws; the last split to arrive (counted in cnt,
-  // one counter per (problem, a-tile), zero between launches) sums them in
-  // split order and stores the result -- the same sums whatever the order in
-  // which the splits finish.  err receives the bit of a bounded wait that
-  // gave up (null: none).
+  // an (a-tile, problem) goes to ws (fewer splits when it would not fit, one
+  // without ws), and a second kernel sums them in split order -- the same
+  // sums whatever the order in which the splits finish.  err receives the bit
+  // of a bounded wait that gave up (null: none).
   float* ws = nullptr;
   size_t ws_floats = 0;
-  int* cnt = nullptr;
-  int cnt_n = 0;
   int* err = nullptr;
 };
 
 cudaError_t lora_merge(const float* flat, const LoraDims& d, int n_layers, const MergeWeights& base,
                        const MergedOut& out, cudaStream_t st);
-// Stores into out[] (each element written once per launch, deterministically).
+// Stores into out[] (each element written once, in a fixed summation order);
+// two launches when the m range is split.
 cudaError_t lora_grad(const LoraGradBatch& batch, int M, cudaStream_t st);
+// m-splits of a lora_grad launch (the kernels it launches: 1, or 2 when split)
 int lora_grad_splits(int M, const LoraGradBatch& batch);
 
 }  // namespace llmcu
