@@ -617,31 +617,31 @@ __global__ void __launch_bounds__(kLgThreads, 2)
 }
 
 // The m-splits' partials of lora_grad_kernel summed in split order (the same
-// bits whatever order the splits finished in) and stored as lg_store does.
-// One CTA per (a-tile, problem), thread = a-row.
-__global__ void __launch_bounds__(128) lora_grad_reduce_kernel(const LoraGradBatch batch, int splits) {
+// bits whatever order the splits finished in), scaled and stored where
+// lg_store would put them.  One thread per (a-tile row, accumulator column):
+// grid (a-tiles, problems, 32), 256 threads.
+__global__ void __launch_bounds__(256) lora_grad_reduce_kernel(const LoraGradBatch batch, int splits) {
   pdl_trigger();
   pdl_wait();
-  __shared__ float stage[128 * 17];
   const LoraGradProb& pb = batch.p[blockIdx.y];
   const int a0 = blockIdx.x * kLgA;
   if (a0 >= pb.A) return;
   const int sel = pb.ilv ? (a0 >> 7) & 1 : 0;
   if (!pb.out[sel] && (pb.ilv || pb.groups == 1)) return;
-  const int ar = threadIdx.x;
-  const int ncol = 16 * pb.groups;
-  const float* wsb = batch.ws + static_cast<size_t>(blockIdx.y * gridDim.x + blockIdx.x) * splits * (64 * kLgA);
-  float acc[64];
-#pragma unroll
-  for (int j = 0; j < 64; ++j) acc[j] = 0.f;
-  // split by split (in order), every column's load of a split in flight together
-  for (int s2 = 0; s2 < splits; ++s2) {
-    const float* src = wsb + static_cast<size_t>(s2) * 64 * kLgA + ar;
-#pragma unroll
-    for (int j = 0; j < 64; ++j)
-      if (j < ncol) acc[j] += src[j * kLgA];
+  const int e = blockIdx.z * blockDim.x + threadIdx.x;
+  const int j = e >> 7, ar = e & (kLgA - 1);  // column, a-row (a-rows fastest: coalesced partial reads)
+  if (j >= 16 * pb.groups) return;
+  const float* src = batch.ws + static_cast<size_t>(blockIdx.y * gridDim.x + blockIdx.x) * splits * (64 * kLgA) +
+                     j * kLgA + ar;
+  float t = 0.f;
+#pragma unroll 4
+  for (int s2 = 0; s2 < splits; ++s2) t += src[static_cast<size_t>(s2) * (64 * kLgA)];
+  const int g = j >> 4, b = j & 15;
+  const int a = a0 + ar;
+  if (a < pb.A && b < pb.Bn && pb.out[g] && (!pb.ilv || g == sel)) {
+    const int orow = pb.ilv ? ((a0 >> 8) << 7) + ar : a;  // the interleave maps a to its adapter row
+    pb.out[g][static_cast<size_t>(orow) * pb.sa + static_cast<size_t>(b) * pb.sb] = t * pb.scale;
   }
-  lg_store(pb, a0, sel, ar, acc, stage);
 }
 
 }  // namespace
@@ -735,7 +735,7 @@ cudaError_t lora_grad(const LoraGradBatch& batch, int M, cudaStream_t st) {
   }
   dim3 grid(tiles, batch.n, splits);
   launch_pdl(lora_grad_kernel, grid, kLgThreads, kLgSmem, st, maps, batch, M, splits);
-  if (splits > 1) launch_pdl(lora_grad_reduce_kernel, dim3(tiles, batch.n), 128, 0, st, batch, splits);
+  if (splits > 1) launch_pdl(lora_grad_reduce_kernel, dim3(tiles, batch.n, 64 * kLgA / 256), 256, 0, st, batch, splits);
   return cudaGetLastError();
 }
 
