@@ -218,7 +218,11 @@ llmcu_status llmcu_train_step_device(llmcu_ctx* ctx, const int32_t* d_tokens,
 /* Mean loss of the last step (synchronises the compute stream). */
 llmcu_status llmcu_read_loss(llmcu_ctx* ctx, float* loss_out);
 /* Forward + loss + backward only (gradients left in place, no optimizer);
- * the split form of the step used by the parity tests. */
+ * the split form of the step used by the parity tests.  It stands in for the
+ * reference's transformer_forward_lora + cross_entropy_forward +
+ * transformer_backward_lora (src/train.cu:262-285) together: there is no
+ * forward-only or backward-only entry, because the vocabulary-streamed
+ * lm_head forms the logits' gradient in the same pass as the loss. */
 llmcu_status llmcu_forward_backward(llmcu_ctx* ctx, const int32_t* tokens, const int32_t* targets,
                                     int batch, int seq, float* loss_out);
 /* AdamW over all adapters with the gradients in place (adamw_step_lora,
