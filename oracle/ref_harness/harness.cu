@@ -21,6 +21,8 @@
 //   harness parity IN OUT     IN: dims, batch, seq, tokens, targets, weights,
 //                             adapters, adamw config (see tests/golden/ref_io.py)
 //                             OUT: losses[B], grads, post-AdamW adapters
+//   harness quantize IN OUT   the reference's quantize_weights on one matrix
+//                             (IN: rows, cols, fp32 w; OUT: int8 q, fp32 scales)
 //   harness bench B S STEPS WARMUP [TOKENS]
 //                             synthetic device-filled weights; B sequences per
 //                             step (token windows from the TOKENS file when
@@ -52,6 +54,7 @@ typedef struct {
   void* _pad[3];
 } MW;
 
+void quantize_weights(const float* weight, int8_t* q_weight, float* scales, int rows, int cols);
 void transformer_forward_lora(const int*, const MW*, const LoraWeights*, float*, float*, float*, float*, float*,
                               float*, float*, float*, float*, float*, float*, float*, LoraActs*, int);
 void transformer_backward_lora(const float*, const MW*, const LoraWeights*, const LoraActs*, LoraGrads*, float*,
@@ -336,10 +339,50 @@ int bench(int B, int S, int steps, int warmup, const char* tok_file) {
 
 }  // namespace
 
+// The reference's per-row INT8 quantiser (src/kernels/quantize.cu:8-50, its
+// own quantize_weights launch) on one weight matrix.  IN: int32 rows, int32
+// cols, float32 w[rows * cols].  OUT: int8 q[rows * cols], float32
+// scale[rows].
+int quantize(const char* in_path, const char* out_path) {
+  FILE* f = fopen(in_path, "rb");
+  int dims[2] = {0, 0};
+  if (!f || fread(dims, sizeof(int), 2, f) != 2 || dims[0] <= 0 || dims[1] <= 0) {
+    fprintf(stderr, "harness: bad quantize input %s\n", in_path);
+    return 2;
+  }
+  const size_t n = static_cast<size_t>(dims[0]) * dims[1];
+  std::vector<float> w(n);
+  if (fread(w.data(), sizeof(float), n, f) != n) {
+    fprintf(stderr, "harness: short read %s\n", in_path);
+    return 2;
+  }
+  fclose(f);
+  float *dw, *ds;
+  int8_t* dq;
+  CUDA_CHECK(cudaMalloc(&dw, n * sizeof(float)));
+  CUDA_CHECK(cudaMalloc(&dq, n));
+  CUDA_CHECK(cudaMalloc(&ds, dims[0] * sizeof(float)));
+  CUDA_CHECK(cudaMemcpy(dw, w.data(), n * sizeof(float), cudaMemcpyHostToDevice));
+  quantize_weights(dw, dq, ds, dims[0], dims[1]);
+  CUDA_CHECK(cudaDeviceSynchronize());
+  std::vector<int8_t> q(n);
+  std::vector<float> sc(dims[0]);
+  CUDA_CHECK(cudaMemcpy(q.data(), dq, n, cudaMemcpyDeviceToHost));
+  CUDA_CHECK(cudaMemcpy(sc.data(), ds, dims[0] * sizeof(float), cudaMemcpyDeviceToHost));
+  FILE* o = fopen(out_path, "wb");
+  if (!o || fwrite(q.data(), 1, n, o) != n || fwrite(sc.data(), sizeof(float), dims[0], o) != (size_t)dims[0]) {
+    fprintf(stderr, "harness: cannot write %s\n", out_path);
+    return 2;
+  }
+  fclose(o);
+  return 0;
+}
+
 int main(int argc, char** argv) {
   if (argc >= 4 && !strcmp(argv[1], "parity")) return parity(argv[2], argv[3]);
+  if (argc >= 4 && !strcmp(argv[1], "quantize")) return quantize(argv[2], argv[3]);
   if (argc >= 6 && !strcmp(argv[1], "bench"))
     return bench(atoi(argv[2]), atoi(argv[3]), atoi(argv[4]), atoi(argv[5]), argc >= 7 ? argv[6] : nullptr);
-  fprintf(stderr, "usage: harness parity IN OUT | harness bench B S STEPS WARMUP [TOKENS]\n");
+  fprintf(stderr, "usage: harness parity IN OUT | harness quantize IN OUT | harness bench B S STEPS WARMUP [TOKENS]\n");
   return 2;
 }

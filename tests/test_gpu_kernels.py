@@ -6,6 +6,7 @@ Tolerances: GEMM outputs to 1e-3 relative L2 (fp32 accumulation of exact fp16
 products; only summation order differs).  Attention to 1e-2 relative L2
 (probabilities are rounded to fp16 before the P.V and dS.K products)."""
 import math
+import os
 
 import numpy as np
 import pytest
@@ -117,5 +118,45 @@ def test_int8_quantiser_bit_exact(llmcu, cuda_device, rows, cols):
     llmcu.quantize_int8_rows(wd.data_ptr(), rows, cols, qd.data_ptr(), sd.data_ptr(),
                              torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
+    assert np.array_equal(qd.cpu().numpy(), q_ref)
+    assert np.array_equal(sd.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
+
+
+HARNESS = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref",
+                       "ref_harness_full")
+
+
+@pytest.mark.skipif(not os.path.exists(HARNESS), reason="reference harness not built (make -C oracle/ref_harness)")
+@pytest.mark.parametrize("rows,cols", [(64, 2048), (7, 13), (300, 6144)])
+def test_int8_quantiser_matches_the_reference_kernel(llmcu, cuda_device, tmp_path, rows, cols):
+    """The library's quantiser, the numpy restatement (oracle/quant.py) and the
+    reference's own quantize_kernel (src/kernels/quantize.cu:8-50, run by the
+    harness from the reference's sources) agree bit for bit on the same fp16
+    draw: codes and scales, an all-zero row and exact .5 ties included."""
+    import subprocess
+    from oracle.quant import quantize_rows
+    rng = np.random.Generator(np.random.PCG64(rows * 7 + cols))
+    w = (rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02)).astype(np.float16).astype(np.float32)
+    if rows >= 3:
+        w[1] = 0.0
+        w[2, :] = np.float32(0.25)
+        w[2, 0] = np.float32(127.0 / 2.0)  # scale 0.5: every 0.25 is a tie at 0.5 (rounds to even 0)
+    src = tmp_path / "w.bin"
+    with open(src, "wb") as f:
+        np.array([rows, cols], np.int32).tofile(f)
+        w.tofile(f)
+    out = tmp_path / "q.bin"
+    subprocess.run([HARNESS, "quantize", str(src), str(out)], check=True, timeout=300)
+    raw = np.fromfile(out, dtype=np.uint8)
+    q_ref = raw[: rows * cols].view(np.int8).reshape(rows, cols)
+    s_ref = raw[rows * cols:].view(np.float32)
+    q_np, s_np = quantize_rows(w)
+    wd = torch.from_numpy(w).to(cuda_device)
+    qd = torch.empty(rows, cols, dtype=torch.int8, device=cuda_device)
+    sd = torch.empty(rows, dtype=torch.float32, device=cuda_device)
+    llmcu.quantize_int8_rows(wd.data_ptr(), rows, cols, qd.data_ptr(), sd.data_ptr(),
+                             torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(q_ref, q_np) and np.array_equal(s_ref.view(np.uint32), s_np.view(np.uint32))
     assert np.array_equal(qd.cpu().numpy(), q_ref)
     assert np.array_equal(sd.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
