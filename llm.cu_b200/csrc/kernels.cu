@@ -479,20 +479,38 @@ __global__ void __launch_bounds__(kRowWarps * 32)
     const float r_new = s_new[k];
     const float* pr = part_ref + static_cast<size_t>(row_id) * slots + (v0 >> 7);
     __half* row = pc + static_cast<size_t>(row_id) * ldp;
-    for (int c0 = threadIdx.x * 8; c0 < n; c0 += kRowWarps * 32 * 8) {
-      const float f = exp2f((pr[c0 >> 7] - r_new) * kLog2e);
-      if (c0 + 8 <= n) {
-        uint4 u = *reinterpret_cast<const uint4*>(row + c0);
-        __half2* h = reinterpret_cast<__half2*>(&u);
+    // whole 8-column groups, four 16-byte loads per thread in flight
+    constexpr int kStep = kRowWarps * 32 * 8;
+    const int n8 = n & ~7;
+    for (int base = threadIdx.x * 8; base < n8; base += 4 * kStep) {
+      uint4 u[4];
+      float f[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 x = __half22float2(h[j]);
-          h[j] = __floats2half2_rn(x.x * f, x.y * f);
+      for (int t = 0; t < 4; ++t) {
+        const int c0 = base + t * kStep;
+        if (c0 < n8) {
+          u[t] = *reinterpret_cast<const uint4*>(row + c0);
+          f[t] = pr[c0 >> 7];
         }
-        *reinterpret_cast<uint4*>(row + c0) = u;
-      } else {
-        for (int j = 0; c0 + j < n; ++j) row[c0 + j] = __float2half_rn(__half2float(row[c0 + j]) * f);
       }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int c0 = base + t * kStep;
+        if (c0 < n8) {
+          const float g = exp2f((f[t] - r_new) * kLog2e);
+          __half2* h = reinterpret_cast<__half2*>(&u[t]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 x = __half22float2(h[j]);
+            h[j] = __floats2half2_rn(x.x * g, x.y * g);
+          }
+          *reinterpret_cast<uint4*>(row + c0) = u[t];
+        }
+      }
+    }
+    if (threadIdx.x < n - n8) {  // the last < 8 columns
+      const int c = n8 + threadIdx.x;
+      row[c] = __float2half_rn(__half2float(row[c]) * exp2f((pr[c >> 7] - r_new) * kLog2e));
     }
     float* dx = d_xf + static_cast<size_t>(row_id) * H;
     const float a = first ? 0.f : exp2f((s_old[k] - r_new) * kLog2e);
