@@ -78,6 +78,21 @@ bool make_io_map(CUtensorMap* map, const void* ptr, int rows, int cols, int ld, 
   return r == CUDA_SUCCESS;
 }
 
+// fp16 [rows, cols] with row stride ld read in [32 rows x 32 columns] boxes,
+// 64-byte swizzle (the SwiGLU backward's factor boxes).
+bool make_box32_map(CUtensorMap* map, const void* ptr, int rows, int cols, int ld) {
+  if (!g_encode || !ptr) return false;
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0 || (static_cast<int64_t>(ld) * 2) % 16 != 0) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {32u, 32u};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // As many pipeline stages as fit beside the epilogue slabs (at most 8).
 template <int BN, int EW, int SLAB, int CG, bool Q8 = false>
 constexpr int stages_for() {
@@ -296,10 +311,9 @@ cudaError_t gemm(const Operand& A, const Operand& B, int M, int N, Epi epi, cons
       okc = make_io_map(&maps[2], ea.gu, M, n_main, ea.ld_gu, false) &&
             make_io_map(&maps[3], ea.act, M, n_main / 2, ea.ld_act, false);
       break;
-    case Epi::kSwiGLUBwd:  // C = dgu [M, 2 n_main] out; gu [M, 2 n_main] is read with plain loads
+    case Epi::kSwiGLUBwd:  // C = dgu [M, 2 n_main] out; D = the stash gu [M, 2 n_main] in 32 x 32 boxes
       okc = make_io_map(&maps[2], ea.gu, M, 2 * n_main, ea.ld_gu, false) && ea.gu_in &&
-            reinterpret_cast<uintptr_t>(ea.gu_in) % 16 == 0 && ea.ld_gu % 8 == 0;
-      maps[3] = maps[2];
+            make_box32_map(&maps[3], ea.gu_in, M, 2 * n_main, ea.ld_gu);
       break;
   }
   if (!okc) return cudaErrorInvalidValue;

@@ -101,6 +101,7 @@ struct EpiCtx {
   const CUtensorMap* mapC;  // primary output
   const CUtensorMap* mapD;  // secondary input or output (epilogue specific)
   int n_main;               // first side-output column
+  int fixup;                // K splits with a fix-up: a unit may end without its epilogue
   __half* side;
   int ld_side;
   const float* col_scale;   // INT8-B forward: the weight's row scale of each output column (null: none)
@@ -563,43 +564,68 @@ struct EpiSwiGLU {
 // acc = d_act[row, i] for the tile's 128-column slice; with the factors the
 // forward stashed, dg = d_act * u silu'(g) and du = d_act * silu(g), written
 // into the interleaved dgu (mapC), the A operand of the gate/up dX GEMM.  The
-// factors arrive by plain 16-byte loads (each thread its row's 64 contiguous
-// bytes per 32 columns), one 32-column step ahead, the first issued before
-// the accumulator is ready; outputs leave through the 4-KB slab.
+// factors of each 32-column step arrive by TMA (mapD: [32 rows x 32 columns]
+// boxes, 64-byte swizzle) into the warp's second 4-KB slab, one step ahead,
+// the first issued before the accumulator is ready; outputs leave through
+// the first slab.  (One row per thread would make the loads touch 32 lines
+// per instruction; the boxes are read back from shared memory instead.)
 // kScaled: the INT8 in-GEMM mode, whose dgu columns carry the gate/up row
 // scales (out_scale) for the next GEMM; compiled out otherwise.
 template <bool kScaled>
 struct EpiSwiGLUBwdT {
   struct Params {
-    const __half* gu_in;  // [M, 2N] interleaved stash
+    const __half* gu_in;  // [M, 2N] interleaved stash (also behind mapD)
     int ld;
     const float* out_scale;  // per dgu column factors (an INT8 gate/up weight's row scales, folded into
                              // the next GEMM's A operand), null: none
   };
   struct State {
-    uint4 f[2][4];  // factors of the next 32 columns: [0] u silu'(g), [1] silu(g)
+    bool pending;  // step 0's factor boxes were issued by begin()
   };
   static constexpr int kChunk = 128;
-  static constexpr int kSlab = kSlabBytes;
+  static constexpr int kSlab = 2 * kSlabBytes;  // [0, 4 KB) output staging, [4 KB, 8 KB) factor boxes
   static constexpr bool kPaired = false;
   static constexpr bool kStores = true;
   static constexpr bool kTmemDirect = true;
-  // 32-column step q of the slice starting at column col0 (a multiple of 128)
-  __device__ static void fetch(State& st, const Params& p, const EpiCtx& c, int col0, int q) {
-    if (c.row < c.M && col0 < c.n_main) {
-      const uint4* src =
-          reinterpret_cast<const uint4*>(p.gu_in + static_cast<size_t>(c.row) * p.ld + (col0 >> 7) * 256 + 32 * q);
+  static constexpr int kFacBox = 32 * 32 * 2;  // one [32 rows x 32 fp16] box
+  // step q's boxes (gate-slot columns gcol + 32q, up-slot columns gcol + 128 + 32q)
+  __device__ static void issue(const EpiCtx& c, int gcol, int q) {
+    if (c.lane == 0) {
+      mbar_arrive_expect_tx(c.bar, 2 * kFacBox);
+      const uint32_t dst = c.slab + kSlabBytes;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        st.f[0][j] = __ldg(src + j);
-        st.f[1][j] = __ldg(src + 128 / 8 + j);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) st.f[0][j] = st.f[1][j] = make_uint4(0u, 0u, 0u, 0u);
+      for (int h = 0; h < 2; ++h)
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+            " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst + h * kFacBox),
+            "l"(reinterpret_cast<uint64_t>(c.mapD)), "r"(smem_u32(c.bar)), "r"(gcol + 128 * h + 32 * q), "r"(c.row0)
+            : "memory");
     }
   }
-  __device__ static void begin(State& st, const Params& p, const EpiCtx& c, int, int col0) { fetch(st, p, c, col0, 0); }
+  // this thread's row of box h: 16-byte chunk j sits at chunk j ^ ((row / 2) % 4) (64-byte swizzle)
+  __device__ static uint4 box_ld(const EpiCtx& c, int h, int j) {
+    uint4 v;
+    const uint32_t a =
+        c.slab + kSlabBytes + h * kFacBox + c.lane * 64 + ((j ^ ((c.lane >> 1) & 3)) << 4);
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
+    return v;
+  }
+  // before the accumulator is ready: the row's factors of this slice (128
+  // gate-slot and 128 up-slot columns, 512 contiguous bytes) into L2, and
+  // step 0's boxes (not for units that a K split may finish elsewhere)
+  __device__ static void begin(State& st, const Params& p, const EpiCtx& c, int, int col0) {
+    st.pending = false;
+    if (col0 >= c.n_main) return;
+    if (c.row < c.M) {
+      const char* f = reinterpret_cast<const char*>(p.gu_in + static_cast<size_t>(c.row) * p.ld + (col0 >> 7) * 256);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) prefetch_l2(f + 128 * j);
+    }
+    if (!c.fixup) {
+      issue(c, (col0 >> 7) * 256, 0);
+      st.pending = true;
+    }
+  }
   __device__ static bool tile(State& st, const Params& p, EpiCtx& c, int col0, uint32_t taddr, int) {
     if (col0 >= c.N) return true;
     if (col0 >= c.n_main) {  // dh of the down adapter (s B_down columns)
@@ -613,16 +639,25 @@ struct EpiSwiGLUBwdT {
       return true;
     }
     const int gcol = (col0 >> 7) * 256;
+    if (!st.pending) issue(c, gcol, 0);
+    st.pending = false;
     uint32_t du_keep[16];
 #pragma unroll 1
     for (int q = 0; q < 4; ++q) {
+      // step q's boxes landed: copy this row's 32 + 32 factors out, then
+      // (reads ordered before the async proxy's next write) issue step q + 1
+      if (!mbar_wait(c.bar, c.phase, c.abort_flag, c.err, kErrWaitAccum)) return false;
+      c.phase ^= 1u;
       uint32_t f0[16], f1[16];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        f0[4 * j] = st.f[0][j].x; f0[4 * j + 1] = st.f[0][j].y; f0[4 * j + 2] = st.f[0][j].z; f0[4 * j + 3] = st.f[0][j].w;
-        f1[4 * j] = st.f[1][j].x; f1[4 * j + 1] = st.f[1][j].y; f1[4 * j + 2] = st.f[1][j].z; f1[4 * j + 3] = st.f[1][j].w;
+        const uint4 a = box_ld(c, 0, j), b = box_ld(c, 1, j);
+        f0[4 * j] = a.x; f0[4 * j + 1] = a.y; f0[4 * j + 2] = a.z; f0[4 * j + 3] = a.w;
+        f1[4 * j] = b.x; f1[4 * j + 1] = b.y; f1[4 * j + 2] = b.z; f1[4 * j + 3] = b.w;
       }
-      if (q < 3) fetch(st, p, c, col0, q + 1);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (q < 3) issue(c, gcol, q + 1);
       float v[32];
       tmem_ld_32x32b_x32(taddr + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v));
       tmem_ld_wait();
@@ -1087,6 +1122,7 @@ __global__ void __launch_bounds__(64 + 32 * EW + (Q8 ? kQ8Threads : 0), 1)
     c.mapC = &tmC;
     c.mapD = &tmD;
     c.n_main = sh.n_main;
+    c.fixup = sh.fixup;
     c.side = sh.side;
     c.ld_side = sh.ld_side;
     c.col_scale = (Q8 && !BMN) ? sh.b_scale : nullptr;
