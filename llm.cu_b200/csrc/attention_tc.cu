@@ -168,6 +168,9 @@ __global__ void __launch_bounds__(192, 2)
       if (!mbar_wait(s_full, j & 1, abort_flag, err, kErrWaitAccum)) { ok = false; break; }
       tc_fence_after();
       const int kv0 = j * kTk;
+      // every key of the tile before every query of this CTA, all inside the
+      // sequence: no masking (and a finite row max)
+      const bool interior = j < qt && kv0 + kTk <= S;
       // pass 1: row max of the scaled, masked scores
       float mx = -INFINITY;
 #pragma unroll 1
@@ -175,10 +178,15 @@ __global__ void __launch_bounds__(192, 2)
         float sv[32];
         tmem_ld_32x32b_x32(t_s + lane_off + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(sv));
         tmem_ld_wait();
+        if (interior) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int kv = kv0 + 32 * c + i;
-          if (kv <= q && kv < S) mx = fmaxf(mx, sv[i] * scale_log2);
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sv[i] * scale_log2);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int kv = kv0 + 32 * c + i;
+            if (kv <= q && kv < S) mx = fmaxf(mx, sv[i] * scale_log2);
+          }
         }
       }
       const float m_new = fmaxf(m_used, mx);
@@ -194,14 +202,24 @@ __global__ void __launch_bounds__(192, 2)
         tmem_ld_32x32b_x32(t_s + lane_off + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(sv));
         tmem_ld_wait();
         uint32_t pk[16];
+        if (interior) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int kv = kv0 + 32 * c + 2 * i;
-          float p0 = (kv <= q && kv < S) ? fast_exp2(fmaf(sv[2 * i], scale_log2, -m_next)) : 0.f;
-          float p1 = (kv + 1 <= q && kv + 1 < S) ? fast_exp2(fmaf(sv[2 * i + 1], scale_log2, -m_next)) : 0.f;
-          if (m_next == -INFINITY) p0 = p1 = 0.f;
-          rs += p0 + p1;
-          pk[i] = pack_half2(p0, p1);
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = fast_exp2(fmaf(sv[2 * i], scale_log2, -m_next));
+            const float p1 = fast_exp2(fmaf(sv[2 * i + 1], scale_log2, -m_next));
+            rs += p0 + p1;
+            pk[i] = pack_half2(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int kv = kv0 + 32 * c + 2 * i;
+            float p0 = (kv <= q && kv < S) ? fast_exp2(fmaf(sv[2 * i], scale_log2, -m_next)) : 0.f;
+            float p1 = (kv + 1 <= q && kv + 1 < S) ? fast_exp2(fmaf(sv[2 * i + 1], scale_log2, -m_next)) : 0.f;
+            if (m_next == -INFINITY) p0 = p1 = 0.f;
+            rs += p0 + p1;
+            pk[i] = pack_half2(p0, p1);
+          }
         }
         tmem_st_32x32b_x16(t_s + lane_off + 16 * c, pk);
       }
@@ -261,18 +279,24 @@ __global__ void __launch_bounds__(192, 2)
 }
 
 // ------------------------------------------------------------- backward
-// One CTA per (128-row key tile, KV head, sequence), 192 threads:
+// One CTA per (128-row key tile, KV head, sequence), 320 threads:
 //   warp 0     TMA producer: K, V once; then per iteration one (Q, dO) tile
 //   warp 1     MMA issuer:   S^T = K Q^T and dP^T = V dO^T; then dV += P^T dO,
 //                            dK += dS^T Q and dQ_part = dS K (dS read from the
 //                            dS^T tile as an MN-major operand)
-//   warps 2-5  softmax:      thread r owns key row r: P^T = exp(S^T - LSE),
+//   warps 2-9  softmax:      two warps per TMEM lane quadrant, each taking
+//                            half of the columns (one CTA per SM: a single
+//                            warp per scheduler would leave every latency of
+//                            the exp / multiply chain exposed).  Thread r of
+//                            a half owns key row r: P^T = exp(S^T - LSE),
 //                            dS^T = P^T (dP^T - delta) into shared memory;
-//                            then, as query row r, drains dQ_part into the
-//                            global fp32 dQ with TMA reduce-add
+//                            then, as query row r, drains its half of
+//                            dQ_part's columns into the global fp32 dQ with
+//                            TMA reduce-add
 // Iterations run over the query heads of the KV group and the query tiles at
-// or after the key tile (causal).  TMEM: S^T / dQ_part [0,128), dP^T
-// [128,256), dV [256, 256+hd), dK [256+hd, 256+2hd).
+// or after the key tile (causal).  TMEM: S^T [0,128), dP^T / dQ_part
+// [128,256), dV [256, 256+hd), dK [256+hd, 256+2hd); the next S^T is issued
+// while the softmax warps drain dQ_part.
 template <int HD>
 struct BwdLayout {
   static constexpr int kT = 128 * HD * 2;       // K, V, Q or dO tile
@@ -288,10 +312,38 @@ struct BwdLayout {
   static constexpr int kBytes = kBarOff + 256 + 1024;
 };
 
-__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+constexpr int kBwdSoftmaxThreads = 256;
+
+// P^T = exp(S^T - LSE) and dS^T = P^T (dP^T - delta) for one 32-column chunk
+// (query columns 32c ..) of key row kr, packed to fp16 pairs.  kMasked: the
+// causal diagonal tile or a ragged edge, where entries past the row's last
+// query or the sequence are zero; interior tiles skip those tests.
+template <bool kMasked>
+__device__ __forceinline__ void bwd_softmax_chunk(const uint32_t (&sv)[32], const uint32_t (&dv)[32], const float* sLb,
+                                                  const float* sDb, int c, float scale_log2, int q0, int kr, int S,
+                                                  uint32_t (&pp)[16], uint32_t (&dsp)[16]) {
+#pragma unroll
+  for (int t = 0; t < 32; t += 2) {
+    float pv[2], dsv[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int qc = 32 * c + t + e;
+      float p = fast_exp2(__uint_as_float(sv[t + e]) * scale_log2 - sLb[qc]);
+      if (kMasked) {
+        const int qq = q0 + qc;
+        if (qq < kr || qq >= S || kr >= S) p = 0.f;
+      }
+      pv[e] = p;
+      dsv[e] = p * (__uint_as_float(dv[t + e]) - sDb[qc]);
+    }
+    pp[t / 2] = pack_half2(pv[0], pv[1]);
+    dsp[t / 2] = pack_half2(dsv[0], dsv[1]);
+  }
+}
+__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(64 + kBwdSoftmaxThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                        const __grid_constant__ CUtensorMap tmDQ, const float* __restrict__ lse,
@@ -333,9 +385,9 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(q_full, 1);
     mbar_init(q_free, 1);
     mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, kBwdSoftmaxThreads);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 128);
+    mbar_init(dq_free, kBwdSoftmaxThreads);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -382,15 +434,31 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t sk = smem_u32(smem + L::kKOff), sv = smem_u32(smem + L::kVOff);
       const uint32_t sq = smem_u32(smem + L::kQOff), so = smem_u32(smem + L::kOOff);
       const uint32_t sp = smem_u32(smem + L::kPOff), ss = smem_u32(smem + L::kSOff);
+      // S^T of the next iteration goes out as soon as its Q tile has landed
+      // (the softmax has read the previous S^T; P^T lives in shared memory),
+      // overlapping the drain of the previous dQ_part, which occupies the dP^T
+      // columns until dq_free
+      auto issue_st = [&]() {
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint32_t off = (k >> 2) * kBox + (k & 3) * 32;
+          umma_f16(t_s, sw128_kmajor_desc(sk + off), sw128_kmajor_desc(sq + off), idesc_s, k > 0 ? 1u : 0u);
+        }
+      };
       bool ok = mbar_wait(kv_full, 0, abort_flag, err, kErrWaitProducer);
+      if (ok && n_it > 0) {
+        ok = mbar_wait(q_full, 0, abort_flag, err, kErrWaitProducer);
+        if (ok) {
+          tc_fence_after();
+          issue_st();
+        }
+      }
       for (int it = 0; it < n_it && ok; ++it) {
-        if (!mbar_wait(q_full, it & 1, abort_flag, err, kErrWaitProducer)) { ok = false; break; }
         if (it >= 1 && !mbar_wait(dq_free, (it - 1) & 1, abort_flag, err, kErrWaitEpilogue)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
           const uint32_t off = (k >> 2) * kBox + (k & 3) * 32;
-          umma_f16(t_s, sw128_kmajor_desc(sk + off), sw128_kmajor_desc(sq + off), idesc_s, k > 0 ? 1u : 0u);
           umma_f16(t_dp, sw128_kmajor_desc(sv + off), sw128_kmajor_desc(so + off), idesc_s, k > 0 ? 1u : 0u);
         }
         umma_commit(s_full);
@@ -405,21 +473,33 @@ __global__ void __launch_bounds__(192, 1)
                    (it > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(q_free);
+        // dQ_part into the dP^T columns (read by the softmax before p_full)
 #pragma unroll
         for (int k = 0; k < 128 / 16; ++k)
-          umma_f16(t_s, sw128_mnmajor_desc(ss + k * 2048), sw128_mnmajor_desc(sk + k * 2048), idesc_dq,
+          umma_f16(t_dp, sw128_mnmajor_desc(ss + k * 2048), sw128_mnmajor_desc(sk + k * 2048), idesc_dq,
                    k > 0 ? 1u : 0u);
         umma_commit(dq_full);
+        if (it + 1 < n_it) {
+          if (!mbar_wait(q_full, (it + 1) & 1, abort_flag, err, kErrWaitProducer)) { ok = false; break; }
+          tc_fence_after();
+          issue_st();
+        }
       }
     }
   } else {
     // ------------------------------------------------------------- softmax
     const int qd = warp & 3;
+    const int hf = (warp - 2) >> 2;           // which half of the columns
     const int r = qd * 32 + lane;             // key row (phase 1) / query row (drain)
     const int kr = kt * 128 + r;              // key position
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
     uint8_t* sP = smem + L::kPOff;
     uint8_t* sS = smem + L::kSOff;
+    // this warp's rows of box hf of P^T and of dS^T -- the only bytes of those
+    // tiles it writes -- double as the staging slabs of its dQ drain, so
+    // waiting for its own reduce-adds' reads is enough before rewriting them
+    const uint32_t slab0 = smem_u32(sP + (hf * 4 + qd) * 4096);
+    const uint32_t slab1 = smem_u32(sS + (hf * 4 + qd) * 4096);
     bool ok = true;
     // lse * log2(e) and delta of query row r of iteration `it`, loaded one
     // iteration ahead into registers and published through a double buffer
@@ -436,10 +516,14 @@ __global__ void __launch_bounds__(192, 1)
       const int hq = kvh * G + it / per_head;
       const int qt = kt + it % per_head;
       const int q0 = qt * 128;
+      // every query of the tile after every key, all inside the sequence: no masking
+      const bool interior = qt > kt && q0 + 128 <= S && kt * 128 + 128 <= S;
       float* sLb = sL + (it & 1) * 256;  // lse of this tile's query columns
       float* sDb = sLb + 128;            // delta
-      sLb[r] = l_next;
-      sDb[r] = d_next;
+      if (hf == 0) {
+        sLb[r] = l_next;
+        sDb[r] = d_next;
+      }
       // one barrier per iteration: rows of sL[it & 1] were last read in
       // iteration it - 2, which every thread finished before arriving here
       named_sync_softmax();
@@ -450,27 +534,16 @@ __global__ void __launch_bounds__(192, 1)
       if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
       __syncwarp();
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {  // 32 query columns at a time
+      for (int c = 2 * hf; c < 2 * hf + 2; ++c) {  // 32 query columns at a time
         uint32_t sv[32], dv32[32];
         tmem_ld_32x32b_x32(t_s + lane_off + 32 * c, sv);
         tmem_ld_32x32b_x32(t_dp + lane_off + 32 * c, dv32);
         tmem_ld_wait();
         uint32_t pp[16], dsp[16];
-#pragma unroll
-        for (int t = 0; t < 32; t += 2) {
-          float pv[2], dsv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int qc = 32 * c + t + e;
-            const int qq = q0 + qc;
-            float p = fast_exp2(__uint_as_float(sv[t + e]) * scale_log2 - sLb[qc]);
-            if (qq < kr || qq >= S || kr >= S) p = 0.f;
-            pv[e] = p;
-            dsv[e] = p * (__uint_as_float(dv32[t + e]) - sDb[qc]);
-          }
-          pp[t / 2] = pack_half2(pv[0], pv[1]);
-          dsp[t / 2] = pack_half2(dsv[0], dsv[1]);
-        }
+        if (interior)
+          bwd_softmax_chunk<false>(sv, dv32, sLb, sDb, c, scale_log2, q0, kr, S, pp, dsp);
+        else
+          bwd_softmax_chunk<true>(sv, dv32, sLb, sDb, c, scale_log2, q0, kr, S, pp, dsp);
         // row r of P^T / dS^T: query columns 32c.. -> box c/2, 16-byte chunks 4(c%2)..
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -491,14 +564,16 @@ __global__ void __launch_bounds__(192, 1)
       if (!mbar_wait(dq_full, it & 1, abort_flag, err, kErrWaitAccum)) { ok = false; break; }
       tc_fence_after();
       const bool valid = q0 + r < S;
+      constexpr int kHalfChunks = HD / 64;  // 32-column chunks of dQ_part per half
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int i = 0; i < kHalfChunks; ++i) {
         // chunk c of this warp's 32 rows -> its own 4 KB slab inside the P^T /
         // dS^T tiles (free once dQ_part is committed), so the reduce-adds of
-        // all chunks are in flight together
-        const uint32_t slab = smem_u32(sP + (c * 4 + qd) * 4096);
+        // its chunks are in flight together
+        const int c = hf * kHalfChunks + i;
+        const uint32_t slab = i == 0 ? slab0 : slab1;
         uint32_t dqv[32];
-        tmem_ld_32x32b_x32(t_s + lane_off + 32 * c, dqv);
+        tmem_ld_32x32b_x32(t_dp + lane_off + 32 * c, dqv);
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -544,7 +619,7 @@ __global__ void __launch_bounds__(192, 1)
       float* dkrow = dk + static_cast<size_t>(row_base + kr) * lddk + kvh * HD;
       __half* dvrow = dv + static_cast<size_t>(row_base + kr) * lddv + kvh * HD;
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = hf * (HD / 64); c < (hf + 1) * (HD / 64); ++c) {
         uint32_t a[32], bvv[32];
         tmem_ld_32x32b_x32(t_dk + lane_off + 32 * c, a);
         tmem_ld_32x32b_x32(t_dv + lane_off + 32 * c, bvv);
@@ -646,7 +721,8 @@ cudaError_t bwd_tc_launch(const __half* q, const __half* k, const __half* v, con
   }
   dim3 grid(nkv, B, (S + 127) / 128);
   const float scale = 1.0f / sqrtf(static_cast<float>(HD));
-  launch_pdl(kern, grid, 192, L::kBytes, st, mq, mk, mv, mo, mdq, lse, delta, dk, dv, S, nh, nkv, lddk, lddv, scale,
+  launch_pdl(kern, grid, 64 + kBwdSoftmaxThreads, L::kBytes, st, mq, mk, mv, mo, mdq, lse, delta, dk, dv, S, nh, nkv,
+             lddk, lddv, scale,
              scale * kLog2e, slab_rows, err);
   return cudaGetLastError();
 }
