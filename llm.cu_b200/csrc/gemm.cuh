@@ -532,7 +532,8 @@ struct EpiSwiGLU {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const float gv = g[2 * t + e] * (e ? sg2.y : sg2.x), uv = u[2 * t + e] * (e ? su2.y : su2.x);
-        const float sg = 1.0f / (1.0f + __expf(-gv));
+        // fast reciprocal (2 ulp; 0 once exp overflows): far below the fp16 rounding of the outputs
+        const float sg = __fdividef(1.0f, 1.0f + __expf(-gv));
         const float si = gv * sg;
         float* r = e ? r1 : r0;
         r[0] = uv * sg * (1.0f + gv * (1.0f - sg));
@@ -748,16 +749,24 @@ struct EpiCEStream {
     const int t = live ? __ldg(p.targets + c.row) - (p.vocab_off + col0) : -1;
     // the first chunk (column 0 of the vocabulary) starts every row at -inf
     const float r0 = (live && p.vocab_off > 0) ? p.ref[c.row] : -INFINITY;
+    // a whole slot without any of the warp's targets (nearly every slot):
+    // no per-column tests
+    const bool plain = nv == 128 && !__any_sync(0xffffffffu, t >= 0 && t < 128);
     float m = -INFINITY;
 #pragma unroll 1
     for (int q = 0; q < 4; ++q) {
       float v[32];
       tmem_ld_32x32b_x32(taddr + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v));
       tmem_ld_wait();
+      if (plain) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        if (32 * q + j < nv) m = fmaxf(m, v[j]);
-        if (32 * q + j == t) p.tgt_logit[c.row] = v[j];
+        for (int j = 0; j < 32; ++j) m = fmaxf(m, v[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (32 * q + j < nv) m = fmaxf(m, v[j]);
+          if (32 * q + j == t) p.tgt_logit[c.row] = v[j];
+        }
       }
     }
     const bool own = !(m <= r0 + kCeSlotRange);  // -inf reference: always
@@ -772,13 +781,23 @@ struct EpiCEStream {
         float v[32];
         tmem_ld_32x32b_x32(taddr + 64 * h + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v));
         tmem_ld_wait();
+        if (plain) {
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const int cj = 64 * h + 32 * q + j;
-          const float e0 = cj < nv ? fast_exp2(fmaf(v[j], kLog2e, -r2)) : 0.f;
-          const float e1 = cj + 1 < nv ? fast_exp2(fmaf(v[j + 1], kLog2e, -r2)) : 0.f;
-          s += e0 + e1;
-          pk[16 * q + j / 2] = pack_half2(cj == t ? 0.f : e0, cj + 1 == t ? 0.f : e1);
+          for (int j = 0; j < 32; j += 2) {
+            const float e0 = fast_exp2(fmaf(v[j], kLog2e, -r2));
+            const float e1 = fast_exp2(fmaf(v[j + 1], kLog2e, -r2));
+            s += e0 + e1;
+            pk[16 * q + j / 2] = pack_half2(e0, e1);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const int cj = 64 * h + 32 * q + j;
+            const float e0 = cj < nv ? fast_exp2(fmaf(v[j], kLog2e, -r2)) : 0.f;
+            const float e1 = cj + 1 < nv ? fast_exp2(fmaf(v[j + 1], kLog2e, -r2)) : 0.f;
+            s += e0 + e1;
+            pk[16 * q + j / 2] = pack_half2(cj == t ? 0.f : e0, cj + 1 == t ? 0.f : e1);
+          }
         }
       }
       if (64 * h < nv) {
