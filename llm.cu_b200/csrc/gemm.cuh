@@ -909,10 +909,31 @@ __global__ void __launch_bounds__(64 + 32 * EW + (Q8 ? kQ8Threads : 0), 1)
     __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  pdl_wait();  // the prologue above overlapped the previous kernel's tail
-
   const int nk = (sh.K + kBlockK - 1) / kBlockK;
   const int num_units = sh.num_tiles * sh.splits;  // (tile, K split) work units
+  if (warp == 0 && lane == 0 && unit0 < num_units) {
+    // while the previous kernel finishes: the first unit's first stages of A
+    // and B into L2.  A prefetch only fills L2, which stays coherent with that
+    // kernel's writes; the loads into shared memory wait for it below.
+    const int tile = unit0 % sh.num_tiles;
+    const int sp = unit0 / sh.num_tiles;
+    const int tm = sh.n_fastest ? tile / sh.tiles_n : tile % sh.tiles_m;
+    const int tn = sh.n_fastest ? tile % sh.tiles_n : tile / sh.tiles_m;
+    const int arow = tm * kRowsPerTile + static_cast<int>(rank) * kBlockM;
+    const int brow = tn * BN + static_cast<int>(rank) * kBRows;
+    const int kb0 = sp * sh.kb_per_split;
+    const int kb1 = min(min(nk, kb0 + sh.kb_per_split), kb0 + STAGES);
+    for (int kb = kb0; kb < kb1; ++kb) {
+      tma_prefetch_l2_2d(&tmA, kb * kBlockK, arow);
+      if constexpr (!BMN) {
+        tma_prefetch_l2_2d(&tmB, kb * kBlockK, brow);
+      } else {
+#pragma unroll
+        for (int j = 0; j < kBRows / 64; ++j) tma_prefetch_l2_2d(&tmB, brow + 64 * j, kb * kBlockK);
+      }
+    }
+  }
+  pdl_wait();  // the prologue above overlapped the previous kernel's tail
 
   if (warp == 0) {
     if (lane == 0) {

@@ -106,6 +106,13 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
 
 // Bring the 128-byte line holding p into L2 (no register result, no wait).
 __device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+// Bring the box of map at (x, y) into L2 (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -158,8 +165,9 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 // the previous kernel in the stream drains.  pdl_trigger lets the next kernel
 // start (once every CTA of this one has triggered or exited); pdl_wait blocks
 // until the previous kernel has completed and its writes are visible.  Every
-// step kernel calls pdl_wait before it reads or writes global memory; both
-// are no-ops for launches that did not opt in.
+// step kernel calls pdl_wait before it reads or writes global memory (an L2
+// prefetch, which changes no data and leaves L2 coherent, may come earlier);
+// both are no-ops for launches that did not opt in.
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
