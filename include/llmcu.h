@@ -342,6 +342,14 @@ llmcu_status llmcu_profile_read(llmcu_ctx* ctx, char* buf, size_t len, int reset
  * counterpart: the reference's kernels have no device-side checks. */
 llmcu_status llmcu_kernel_checks(void* stream, int* bits);
 
+/* Failure-path self-test: launches one CTA on `stream` whose single wait is
+ * never satisfied, so it gives up after the kernels' bounded-wait limit
+ * (4 s), raises its abort flag and sets the same error bit a stalled pipeline
+ * would; llmcu_kernel_checks then returns LLMCU_ERR_DEVICE_CHECK, and the
+ * device stays usable.  Nothing faults, traps or hangs.  No reference
+ * counterpart. */
+llmcu_status llmcu_kernel_wait_selftest(void* stream);
+
 /* C[M,N] (fp32) = A[M,K] . B[N,K]^T, fp16 inputs, K-major rows with leading
  * dims lda/ldb/ldc in elements -- the NT product of matmul_kernel
  * (src/kernels/matmul.cu:8-51) on the tcgen05 path. */

@@ -110,16 +110,24 @@ __global__ void __launch_bounds__(192, 2)
       for (int i = 0; i < kDBoxes; ++i)
         tma_load_2d(smem + L::kQOff + i * kBox, &tmQ, q_full, h * HD + 64 * i, row_base + qt * kTq);
       bool ok = true;
+      int jk = -1, jv = -1;  // last K / V tile issued
       for (int j = 0; j < n_kv && ok; ++j) {
         // K_j once S_{j-1} has read K_{j-1}; V_j once P_{j-1} V_{j-1} has read V_{j-1}
         if (j >= 1 && !mbar_wait(k_empty, (j - 1) & 1, abort_flag, err, kErrWaitConsumer)) { ok = false; break; }
         mbar_arrive_expect_tx(k_full, L::kKV);
         for (int i = 0; i < kDBoxes; ++i)
           tma_load_2d(smem + L::kKOff + i * kBox, &tmK, k_full, kvh * HD + 64 * i, row_base + j * kTk);
+        jk = j;
         if (j >= 1 && !mbar_wait(v_empty, (j - 1) & 1, abort_flag, err, kErrWaitConsumer)) { ok = false; break; }
         mbar_arrive_expect_tx(v_full, L::kKV);
         for (int i = 0; i < kDBoxes; ++i)
           tma_load_2d(smem + L::kVOff + i * kBox, &tmV, v_full, kvh * HD + 64 * i, row_base + j * kTk);
+        jv = j;
+      }
+      if (!ok) {  // let the copies already issued land before the CTA can exit
+        mbar_drain(q_full, 0);
+        if (jk >= 0) mbar_drain(k_full, jk & 1);
+        if (jv >= 0) mbar_drain(v_full, jv & 1);
       }
     }
   } else if (warp == 1) {
@@ -417,7 +425,12 @@ __global__ void __launch_bounds__(64 + kBwdSoftmaxThreads, 1)
       for (int it = 0; it < n_it; ++it) {
         const int hq = kvh * G + it / per_head;
         const int qt = kt + it % per_head;
-        if (it >= 1 && !mbar_wait(q_free, (it - 1) & 1, abort_flag, err, kErrWaitConsumer)) break;
+        if (it >= 1 && !mbar_wait(q_free, (it - 1) & 1, abort_flag, err, kErrWaitConsumer)) {
+          // let the copies already issued land before the CTA can exit
+          mbar_drain(kv_full, 0);
+          mbar_drain(q_full, (it - 1) & 1);
+          break;
+        }
         mbar_arrive_expect_tx(q_full, 2 * L::kT);
         for (int i = 0; i < kDBoxes; ++i) {
           tma_load_2d(smem + L::kQOff + i * kBox, &tmQ, q_full, hq * HD + 64 * i, row_base + qt * 128);

@@ -251,6 +251,9 @@ cudaError_t convert_weight(const float* src, int rows, int cols, __half* dst, in
 cudaError_t transpose_f16(const __half* src, int rows, int cols, int ld_src, __half* dst, int ld_dst,
                           cudaStream_t st);
 cudaError_t quantize_rows_int8(const float* w, int rows, int cols, int8_t* q, float* scale, cudaStream_t st);
+// One CTA whose single wait is never satisfied: it gives up after the
+// kernels' bounded-wait limit and ORs kErrWaitProducer into err.
+cudaError_t wait_selftest(int* err, cudaStream_t st);
 cudaError_t dequant_rows_f16(const int8_t* q, const float* scale, int rows, int cols, __half* out, cudaStream_t st);
 
 }  // namespace llmcu

@@ -183,6 +183,7 @@ __device__ __forceinline__ bool slab_load(EpiCtx& c, const CUtensorMap* map, int
   }
   __syncwarp();
   const bool ok = mbar_wait(c.bar, c.phase, c.abort_flag, c.err, kErrWaitAccum);
+  if (!ok) mbar_drain(c.bar, c.phase);
   c.phase ^= 1u;
   return ok;
 }
@@ -614,6 +615,10 @@ struct EpiSwiGLUBwdT {
   // before the accumulator is ready: the row's factors of this slice (128
   // gate-slot and 128 up-slot columns, 512 contiguous bytes) into L2, and
   // step 0's boxes (not for units that a K split may finish elsewhere)
+  // the epilogue gave up before tile(): let step 0's boxes land first
+  __device__ static void drain(State& st, const EpiCtx& c) {
+    if (st.pending) mbar_drain(c.bar, c.phase);
+  }
   __device__ static void begin(State& st, const Params& p, const EpiCtx& c, int, int col0) {
     st.pending = false;
     if (col0 >= c.n_main) return;
@@ -647,7 +652,10 @@ struct EpiSwiGLUBwdT {
     for (int q = 0; q < 4; ++q) {
       // step q's boxes landed: copy this row's 32 + 32 factors out, then
       // (reads ordered before the async proxy's next write) issue step q + 1
-      if (!mbar_wait(c.bar, c.phase, c.abort_flag, c.err, kErrWaitAccum)) return false;
+      if (!mbar_wait(c.bar, c.phase, c.abort_flag, c.err, kErrWaitAccum)) {
+        mbar_drain(c.bar, c.phase);
+        return false;
+      }
       c.phase ^= 1u;
       uint32_t f0[16], f1[16];
 #pragma unroll
@@ -823,6 +831,12 @@ struct epi_begin_col : std::false_type {};
 template <class E>
 struct epi_begin_col<E, std::void_t<decltype(E::begin(std::declval<typename E::State&>(), std::declval<const typename E::Params&>(),
                                                       std::declval<const EpiCtx&>(), 0, 0))>> : std::true_type {};
+
+template <class E, class = void>
+struct epi_drain : std::false_type {};
+template <class E>
+struct epi_drain<E, std::void_t<decltype(E::drain(std::declval<typename E::State&>(), std::declval<const EpiCtx&>()))>>
+    : std::true_type {};
 
 template <class E, class = void>
 struct epi_tmem_direct : std::false_type {};
@@ -1186,7 +1200,10 @@ __global__ void __launch_bounds__(64 + 32 * EW + (Q8 ? kQ8Threads : 0), 1)
         Epi::begin(st, ep, c, slot, tn * BN + cgrp * kCols);
       else
         Epi::begin(st, ep, c, slot);
-      if (!mbar_wait(&acc_full[acc], (i >> 1) & 1, abort_flag, err, kErrWaitAccum)) break;
+      if (!mbar_wait(&acc_full[acc], (i >> 1) & 1, abort_flag, err, kErrWaitAccum)) {
+        if constexpr (epi_drain<Epi>::value) Epi::drain(st, c);  // copies begin() issued
+        break;
+      }
       tc_fence_after();
       bool run = true;  // false: another K split of this tile finishes it
       if (sh.fixup) {

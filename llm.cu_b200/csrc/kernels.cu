@@ -753,6 +753,23 @@ __global__ void transpose_f16_kernel(const __half* __restrict__ src, int rows, i
 // ------------------------------------------------------------------ INT8
 // Bit-exact with quantize_kernel (src/kernels/quantize.cu:8-44): every step is
 // one IEEE-rounded fp32 operation in the reference's order.
+// One mbarrier that nothing ever completes: thread 0's bounded wait gives
+// up after its limit, raises the CTA's abort flag and ORs kErrWaitProducer
+// into err -- the path every pipeline wait takes when its producer never
+// arrives, here on purpose and without any copy in flight.
+__global__ void wait_selftest_kernel(int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) (void)mbar_wait(&bar, 0, &abort_flag, err, kErrWaitProducer);
+  __syncthreads();
+}
+
 __global__ void quantize_rows_kernel(const float* __restrict__ w, int cols, int8_t* __restrict__ q,
                                      float* __restrict__ scale) {
   __shared__ float red[32];
@@ -996,6 +1013,11 @@ cudaError_t transpose_f16(const __half* src, int rows, int cols, int ld_src, __h
                           cudaStream_t st) {
   dim3 grid((cols + 31) / 32, (rows + 31) / 32);
   launch_pdl(transpose_f16_kernel, grid, 256, 0, st, src, rows, cols, ld_src, dst, ld_dst);
+  return cudaGetLastError();
+}
+
+cudaError_t wait_selftest(int* err, cudaStream_t st) {
+  wait_selftest_kernel<<<1, 32, 0, st>>>(err);
   return cudaGetLastError();
 }
 

@@ -1939,6 +1939,12 @@ llmcu_status llmcu_kernel_checks(void* stream, int* bits) {
   return h ? LLMCU_ERR_DEVICE_CHECK : LLMCU_OK;
 }
 
+llmcu_status llmcu_kernel_wait_selftest(void* stream) {
+  int* d_err = nullptr;
+  if (kernel_err_word(&d_err) != cudaSuccess) return LLMCU_ERR_CUDA;
+  return wait_selftest(d_err, static_cast<cudaStream_t>(stream)) == cudaSuccess ? LLMCU_OK : LLMCU_ERR_CUDA;
+}
+
 llmcu_status llmcu_gemm_nt_f16(const void* A, const void* B, float* C, int M, int N, int K, int lda, int ldb, int ldc,
                                void* stream) {
   if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0) return LLMCU_ERR_INVALID_ARG;

@@ -91,6 +91,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// After a wait gave up: let a copy already issued on `bar` land (at most
+// 100 ms) before the CTA can exit.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(a, parity) && globaltimer_ns() - t0 < 100000000ull) {
+  }
+}
+
 // ----------------------------------------------------------------------- TMA
 // 2-D tiled load of one box into shared memory; completion is signalled as
 // transaction bytes on `bar`.  x is the innermost (contiguous) coordinate.

@@ -176,6 +176,7 @@ _SIGS = {
     "llmcu_attention_bwd": (C.c_int, [C.c_void_p] * 10 + [C.c_int] * 9 + [C.c_void_p]),
     "llmcu_attention_bwd_noalloc": (C.c_int, [C.c_void_p] * 9 + [C.c_int] * 9 + [C.c_void_p]),
     "llmcu_kernel_checks": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "llmcu_kernel_wait_selftest": (C.c_int, [C.c_void_p]),
     "llmcu_lora_layout_count": (C.c_int64, [C.POINTER(_LoraLayout)]),
     "llmcu_lora_files_write": (C.c_int, [C.POINTER(_LoraLayout), C.c_void_p, C.c_char_p, C.c_int]),
     "llmcu_lora_files_read": (C.c_int, [C.POINTER(_LoraLayout), C.c_void_p, C.c_char_p, C.c_int]),
@@ -532,6 +533,12 @@ def kernel_checks(stream=0) -> int:
     if st != OK:
         raise LlmcuError(st, f"kernel-level device checks failed (error bits 0x{bits.value:x})")
     return bits.value
+
+
+def kernel_wait_selftest(stream=0):
+    """Launches the bounded-wait self-test (one wait that nothing satisfies;
+    it gives up after 4 s); kernel_checks afterwards raises DEVICE_CHECK."""
+    _chk(lib().llmcu_kernel_wait_selftest(stream), "kernel_wait_selftest")
 
 
 def quantize_int8_rows(w_ptr, rows, cols, q_ptr, scale_ptr, stream=0):

@@ -160,3 +160,31 @@ def test_int8_quantiser_matches_the_reference_kernel(llmcu, cuda_device, tmp_pat
     assert np.array_equal(q_ref, q_np) and np.array_equal(s_ref.view(np.uint32), s_np.view(np.uint32))
     assert np.array_equal(qd.cpu().numpy(), q_ref)
     assert np.array_equal(sd.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
+
+
+def test_bounded_wait_gives_up_and_is_reported(llmcu, cuda_device):
+    """A wait that nothing satisfies ends after the kernels' bounded-wait limit
+    with the error bit set; llmcu_kernel_checks reports it once and the device
+    keeps working (a small attention forward afterwards is clean)."""
+    import time
+    st = torch.cuda.current_stream().cuda_stream
+    assert llmcu.kernel_checks(st) == 0
+    t0 = time.time()
+    llmcu.kernel_wait_selftest(st)
+    with pytest.raises(llmcu.LlmcuError) as e:
+        llmcu.kernel_checks(st)
+    elapsed = time.time() - t0
+    assert e.value.status == 7  # LLMCU_ERR_DEVICE_CHECK
+    assert "0x1" in str(e.value)
+    assert 3.5 < elapsed < 60.0
+    assert llmcu.kernel_checks(st) == 0  # read and cleared
+    B, S, nh, nkv, hd = 1, 128, 2, 1, 128
+    q = torch.randn(B * S, nh * hd, device=cuda_device).half()
+    k = torch.randn(B * S, nkv * hd, device=cuda_device).half()
+    v = torch.randn(B * S, nkv * hd, device=cuda_device).half()
+    o = torch.empty(B * S, nh * hd, device=cuda_device, dtype=torch.float16)
+    lse = torch.empty(B, nh, S, device=cuda_device)
+    llmcu.attention_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), B, S, nh, nkv, hd,
+                        nh * hd, nkv * hd, nkv * hd, st)
+    assert llmcu.kernel_checks(st) == 0
+    assert torch.isfinite(o.float()).all()
