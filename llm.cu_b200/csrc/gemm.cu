@@ -101,16 +101,22 @@ constexpr int stages_for() {
   return s > 8 ? 8 : s;
 }
 
-// 8 epilogue warps (two per TMEM lane quadrant) for 128/256-wide tiles, 4 for 64.
-template <int BN>
+template <class E, class = void>
+struct epi_groups : std::integral_constant<int, kGemmEpiGroups> {};
+template <class E>
+struct epi_groups<E, std::void_t<decltype(E::kEpiGroups)>> : std::integral_constant<int, E::kEpiGroups> {};
+
+// 8 epilogue warps (two per TMEM lane quadrant) for 128/256-wide tiles, 4 for
+// 64 -- or as many groups of 4 as the epilogue asks for
+template <int BN, class E>
 constexpr int epi_warps() {
-  return BN >= 128 ? 4 * kGemmEpiGroups : 4;
+  return BN >= 128 ? 4 * epi_groups<E>::value : 4;
 }
 
 template <int BN, class E, bool BMN, int CG, bool Q8 = false>
 cudaError_t launch(const CUtensorMap* maps, const GemmShape& sh, const typename E::Params& p, int* err,
                    cudaStream_t st) {
-  constexpr int kEpiWarps = epi_warps<BN>();
+  constexpr int kEpiWarps = epi_warps<BN, E>();
   constexpr int S = stages_for<BN, kEpiWarps, E::kSlab, CG, Q8>();
   using L = GemmSmem<BN, S, kEpiWarps, E::kSlab, CG, Q8>;
   static_assert(L::kBytes <= 232448, "shared memory budget");

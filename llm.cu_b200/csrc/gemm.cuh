@@ -584,7 +584,12 @@ struct EpiSwiGLUBwdT {
   struct State {
     bool pending;  // step 0's factor boxes were issued by begin()
   };
-  static constexpr int kChunk = 128;
+  // one warp per TMEM lane quadrant takes the whole 256-column tile (8 steps
+  // of 32 columns): with 4 epilogue warps the two 4-KB slabs of each leave
+  // room for a sixth pipeline stage, which the main loop needs more than the
+  // epilogue needs a second warp
+  static constexpr int kEpiGroups = 1;
+  static constexpr int kChunk = 256;
   static constexpr int kSlab = 2 * kSlabBytes;  // [0, 4 KB) output staging, [4 KB, 8 KB) factor boxes
   static constexpr bool kPaired = false;
   static constexpr bool kStores = true;
@@ -612,23 +617,30 @@ struct EpiSwiGLUBwdT {
     asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
     return v;
   }
-  // before the accumulator is ready: the row's factors of this slice (128
-  // gate-slot and 128 up-slot columns, 512 contiguous bytes) into L2, and
-  // step 0's boxes (not for units that a K split may finish elsewhere)
   // the epilogue gave up before tile(): let step 0's boxes land first
   __device__ static void drain(State& st, const EpiCtx& c) {
     if (st.pending) mbar_drain(c.bar, c.phase);
   }
+  // stash column of the gate slot of step t (0..7) of the tile at col0: each
+  // 128-column half of the tile has its own 256-column block of factors
+  __device__ static int gcol_of(int col0, int t) { return ((col0 + 128 * (t >> 2)) >> 7) * 256; }
+  // before the accumulator is ready: the row's factors of this tile (2 x 512
+  // contiguous bytes) into L2, and step 0's boxes (not for units that a K
+  // split may finish elsewhere)
   __device__ static void begin(State& st, const Params& p, const EpiCtx& c, int, int col0) {
     st.pending = false;
     if (col0 >= c.n_main) return;
     if (c.row < c.M) {
-      const char* f = reinterpret_cast<const char*>(p.gu_in + static_cast<size_t>(c.row) * p.ld + (col0 >> 7) * 256);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) prefetch_l2(f + 128 * j);
+      for (int hh = 0; hh < 2; ++hh) {
+        const char* f =
+            reinterpret_cast<const char*>(p.gu_in + static_cast<size_t>(c.row) * p.ld + gcol_of(col0, 4 * hh));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) prefetch_l2(f + 128 * j);
+      }
     }
     if (!c.fixup) {
-      issue(c, (col0 >> 7) * 256, 0);
+      issue(c, gcol_of(col0, 0), 0);
       st.pending = true;
     }
   }
@@ -636,7 +648,7 @@ struct EpiSwiGLUBwdT {
     if (col0 >= c.N) return true;
     if (col0 >= c.n_main) {  // dh of the down adapter (s B_down columns)
 #pragma unroll 1
-      for (int q = 0; q < 4 && col0 + 32 * q < c.N; ++q) {
+      for (int q = 0; q < kChunk / 32 && col0 + 32 * q < c.N; ++q) {
         float v[32];
         tmem_ld_32x32b_x32(taddr + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v));
         tmem_ld_wait();
@@ -644,12 +656,13 @@ struct EpiSwiGLUBwdT {
       }
       return true;
     }
-    const int gcol = (col0 >> 7) * 256;
-    if (!st.pending) issue(c, gcol, 0);
+    if (!st.pending) issue(c, gcol_of(col0, 0), 0);
     st.pending = false;
     uint32_t du_keep[16];
 #pragma unroll 1
-    for (int q = 0; q < 4; ++q) {
+    for (int t = 0; t < kChunk / 32; ++t) {
+      const int q = t & 3;  // step within the 128-column half
+      const int gcol = gcol_of(col0, t);
       // step q's boxes landed: copy this row's 32 + 32 factors out, then
       // (reads ordered before the async proxy's next write) issue step q + 1
       if (!mbar_wait(c.bar, c.phase, c.abort_flag, c.err, kErrWaitAccum)) {
@@ -666,9 +679,9 @@ struct EpiSwiGLUBwdT {
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (q < 3) issue(c, gcol, q + 1);
+      if (t + 1 < kChunk / 32) issue(c, gcol_of(col0, t + 1), (t + 1) & 3);
       float v[32];
-      tmem_ld_32x32b_x32(taddr + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(v));
+      tmem_ld_32x32b_x32(taddr + 32 * t, *reinterpret_cast<uint32_t(*)[32]>(v));
       tmem_ld_wait();
       uint32_t dg[16], du[16];
       // per dgu column factors of these 32 gate / up columns: lane L holds
