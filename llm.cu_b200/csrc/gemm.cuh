@@ -500,8 +500,12 @@ struct EpiResidF32 {
 struct EpiSwiGLU {
   struct Params {};
   struct State {};
+  // one warp per TMEM lane quadrant (both 64-column chunks of its rows' gate
+  // columns), so that two 4-KB slabs per warp -- the gate and up slots' factors
+  // leave together -- still leave room for six pipeline stages
+  static constexpr int kEpiGroups = 1;
   static constexpr int kChunk = 64;
-  static constexpr int kSlab = kSlabBytes;
+  static constexpr int kSlab = 2 * kSlabBytes;
   static constexpr bool kPaired = true;  // requires BN == 256
   static constexpr bool kStores = true;
   __device__ static void begin(State&, const Params&, const EpiCtx&, int) {}
@@ -547,16 +551,17 @@ struct EpiSwiGLU {
     }
     slab_wait_read(c);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) slab_st(c, j, make_uint4(dgp[4 * j], dgp[4 * j + 1], dgp[4 * j + 2], dgp[4 * j + 3]));
-    slab_store(c, c.mapC, tile_n * 256 + cc, c.row0);
-    slab_wait_read(c);
+    for (int j = 0; j < 8; ++j) slab_st(c, j, make_uint4(dgp[4 * j], dgp[4 * j + 1], dgp[4 * j + 2], dgp[4 * j + 3]), 0);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) slab_st(c, j, make_uint4(sp[4 * j], sp[4 * j + 1], sp[4 * j + 2], sp[4 * j + 3]));
-    slab_store(c, c.mapC, tile_n * 256 + 128 + cc, c.row0);
-    slab_wait_read(c);
+    for (int j = 0; j < 8; ++j) slab_st(c, j, make_uint4(sp[4 * j], sp[4 * j + 1], sp[4 * j + 2], sp[4 * j + 3]), 1);
+    slab_store(c, c.mapC, tile_n * 256 + cc, c.row0, 0);
+    slab_store(c, c.mapC, tile_n * 256 + 128 + cc, c.row0, 1);
+    // the first slab again, once its store (not the second's) has read it
+    if (c.lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+    __syncwarp();
 #pragma unroll
-    for (int j = 0; j < 8; ++j) slab_st(c, j, make_uint4(ap[4 * j], ap[4 * j + 1], ap[4 * j + 2], ap[4 * j + 3]));
-    slab_store(c, c.mapD, tile_n * 128 + cc, c.row0);
+    for (int j = 0; j < 8; ++j) slab_st(c, j, make_uint4(ap[4 * j], ap[4 * j + 1], ap[4 * j + 2], ap[4 * j + 3]), 0);
+    slab_store(c, c.mapD, tile_n * 128 + cc, c.row0, 0);
     return true;
   }
   __device__ static void end(State&, const Params&, const EpiCtx&, int) {}
