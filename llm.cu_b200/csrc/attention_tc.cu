@@ -179,6 +179,9 @@ __global__ void __launch_bounds__(192, 2)
       // every key of the tile before every query of this CTA, all inside the
       // sequence: no masking (and a finite row max)
       const bool interior = j < qt && kv0 + kTk <= S;
+      // masked tiles: key kv0 + i is visible to row q iff i <= lim (causal and
+      // inside the sequence); one compare and a select per score, no branch
+      const int lim = min(q, S - 1) - kv0;
       // pass 1: row max of the scaled, masked scores
       float mx = -INFINITY;
 #pragma unroll 1
@@ -191,10 +194,7 @@ __global__ void __launch_bounds__(192, 2)
           for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sv[i] * scale_log2);
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int kv = kv0 + 32 * c + i;
-            if (kv <= q && kv < S) mx = fmaxf(mx, sv[i] * scale_log2);
-          }
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, 32 * c + i <= lim ? sv[i] * scale_log2 : -INFINITY);
         }
       }
       const float m_new = fmaxf(m_used, mx);
@@ -219,12 +219,14 @@ __global__ void __launch_bounds__(192, 2)
             pk[i] = pack_half2(p0, p1);
           }
         } else {
+          // no visible key yet (m_next = -inf): every P of the row is zero
+          const int lim_c = (m_next == -INFINITY ? -1 : lim) - 32 * c;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int kv = kv0 + 32 * c + 2 * i;
-            float p0 = (kv <= q && kv < S) ? fast_exp2(fmaf(sv[2 * i], scale_log2, -m_next)) : 0.f;
-            float p1 = (kv + 1 <= q && kv + 1 < S) ? fast_exp2(fmaf(sv[2 * i + 1], scale_log2, -m_next)) : 0.f;
-            if (m_next == -INFINITY) p0 = p1 = 0.f;
+            float p0 = fast_exp2(fmaf(sv[2 * i], scale_log2, -m_next));
+            float p1 = fast_exp2(fmaf(sv[2 * i + 1], scale_log2, -m_next));
+            p0 = 2 * i <= lim_c ? p0 : 0.f;
+            p1 = 2 * i + 1 <= lim_c ? p1 : 0.f;
             rs += p0 + p1;
             pk[i] = pack_half2(p0, p1);
           }
