@@ -333,21 +333,28 @@ __device__ __forceinline__ void bwd_softmax_chunk(const uint32_t (&sv)[32], cons
                                                   const float* sDb, int c, float scale_log2, int q0, int kr, int S,
                                                   uint32_t (&pp)[16], uint32_t (&dsp)[16]) {
 #pragma unroll
-  for (int t = 0; t < 32; t += 2) {
-    float pv[2], dsv[2];
+  for (int t = 0; t < 32; t += 4) {
+    // the column statistics four at a time (16-byte aligned: 32c + t)
+    const float4 l4 = *reinterpret_cast<const float4*>(sLb + 32 * c + t);
+    const float4 d4 = *reinterpret_cast<const float4*>(sDb + 32 * c + t);
+    const float lq[4] = {l4.x, l4.y, l4.z, l4.w};
+    const float dq[4] = {d4.x, d4.y, d4.z, d4.w};
+    float pv[4], dsv[4];
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
+    for (int e = 0; e < 4; ++e) {
       const int qc = 32 * c + t + e;
-      float p = fast_exp2(__uint_as_float(sv[t + e]) * scale_log2 - sLb[qc]);
+      float p = fast_exp2(__uint_as_float(sv[t + e]) * scale_log2 - lq[e]);
       if (kMasked) {
         const int qq = q0 + qc;
         if (qq < kr || qq >= S || kr >= S) p = 0.f;
       }
       pv[e] = p;
-      dsv[e] = p * (__uint_as_float(dv[t + e]) - sDb[qc]);
+      dsv[e] = p * (__uint_as_float(dv[t + e]) - dq[e]);
     }
     pp[t / 2] = pack_half2(pv[0], pv[1]);
+    pp[t / 2 + 1] = pack_half2(pv[2], pv[3]);
     dsp[t / 2] = pack_half2(dsv[0], dsv[1]);
+    dsp[t / 2 + 1] = pack_half2(dsv[2], dsv[3]);
   }
 }
 __device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
@@ -580,16 +587,19 @@ __global__ void __launch_bounds__(64 + kBwdSoftmaxThreads, 1)
       tc_fence_after();
       const bool valid = q0 + r < S;
       constexpr int kHalfChunks = HD / 64;  // 32-column chunks of dQ_part per half
-#pragma unroll 1
+      // this warp's chunks of dQ_part, loaded from TMEM together
+      uint32_t dq2[kHalfChunks][32];
+#pragma unroll
+      for (int i = 0; i < kHalfChunks; ++i) tmem_ld_32x32b_x32(t_dp + lane_off + 32 * (hf * kHalfChunks + i), dq2[i]);
+      tmem_ld_wait();
+#pragma unroll
       for (int i = 0; i < kHalfChunks; ++i) {
         // chunk c of this warp's 32 rows -> its own 4 KB slab inside the P^T /
         // dS^T tiles (free once dQ_part is committed), so the reduce-adds of
         // its chunks are in flight together
         const int c = hf * kHalfChunks + i;
         const uint32_t slab = i == 0 ? slab0 : slab1;
-        uint32_t dqv[32];
-        tmem_ld_32x32b_x32(t_dp + lane_off + 32 * c, dqv);
-        tmem_ld_wait();
+        const uint32_t* dqv = dq2[i];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float f0 = valid ? __uint_as_float(dqv[4 * j]) * scale : 0.f;
