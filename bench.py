@@ -103,13 +103,20 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        rows = []
         with open(self.path) as f:
-            for line in f:
-                parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
+            lines = f.readlines()
         os.unlink(self.path)
+        return self.summarise(lines)
+
+    @staticmethod
+    def summarise(lines):
+        """Median SM clock, max clock, the throttle reasons seen active and
+        the peak power of `--format=csv,noheader,nounits` rows of FIELDS."""
+        rows = []
+        for line in lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
         if not rows:
             return None
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
@@ -118,7 +125,7 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
                 "reasons": reasons, "samples": len(rows),
-                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+                "power_w_max": max((float(r[3]) for r in rows if r[3].replace(".", "").isdigit()), default=None)}
 
 
 def layer_gemm_flops_per_token(m) -> float:
