@@ -70,7 +70,9 @@ def _attn_ref(q, k, v, B, S, nh, nkv, hd):
 
 
 @pytest.mark.parametrize("B,S,nh,nkv,hd", [(2, 128, 4, 2, 64), (1, 32, 4, 2, 64), (2, 512, 16, 8, 128),
-                                           (1, 200, 16, 8, 128), (1, 1000, 4, 2, 128)])
+                                           (1, 200, 16, 8, 128), (1, 1000, 4, 2, 128),
+                                           # ragged tiles in every sequence of a batch; a KV group of four
+                                           (3, 333, 8, 4, 64), (2, 300, 8, 2, 128)])
 def test_attention_fwd_bwd_matches_torch(llmcu, cuda_device, B, S, nh, nkv, hd):
     g = torch.Generator(device="cpu").manual_seed(S + nh)
     M = B * S
