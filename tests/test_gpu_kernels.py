@@ -25,7 +25,9 @@ def rel_l2(a, b):
 # (4096, 2048, *) leave a partial last wave that runs split along K (the
 # tail split); every shape runs twice to check the split's counters re-arm.
 @pytest.mark.parametrize("M,N,K", [(4096, 4096, 2048), (32, 64, 256), (200, 300, 200), (128, 151936 // 8, 2048),
-                                   (1000, 2048, 6144), (4096, 2048, 2048), (4096, 2048, 12288), (640, 12288, 2048)])
+                                   (1000, 2048, 6144), (4096, 2048, 2048), (4096, 2048, 12288), (640, 12288, 2048),
+                                   # one row; the shortest K a 16-byte row stride allows
+                                   (1, 256, 64), (129, 520, 8)])
 def test_gemm_nt_matches_torch(llmcu, cuda_device, M, N, K):
     g = torch.Generator(device="cpu").manual_seed(M * 7 + N)
     A = torch.randn(M, K, generator=g).half().to(cuda_device)
@@ -41,7 +43,7 @@ def test_gemm_nt_matches_torch(llmcu, cuda_device, M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(4096, 2048, 2048), (32, 64, 256), (200, 296, 200), (4096, 6144, 2048),
-                                   (1000, 2112, 4096)])
+                                   (1000, 2112, 4096), (1, 64, 64), (130, 8, 72)])
 def test_gemm_nn_matches_torch(llmcu, cuda_device, M, N, K):
     """B read MN-major ([K, N] row-major), the input-gradient GEMMs' operand.
     Row strides must be multiples of 16 bytes (TMA), so N is a multiple of 8."""
